@@ -1,0 +1,213 @@
+/*
+ * whallm_b200 -- C ABI of the B200 routed-expert MoE path and the quantized
+ * KV-cache formats.
+ *
+ * Every entry point:
+ *   - takes caller-owned device pointers, plain sizes and a CUDA stream
+ *     (wm_stream_t is the same type as cudaStream_t; pass NULL for the
+ *     legacy default stream);
+ *   - is asynchronous and stream-ordered, allocates no memory and keeps no
+ *     state between calls (the tensor-core path caches a per-device tensor-map
+ *     encoder lookup behind a mutex);
+ *   - returns WM_OK (0) or a negative WM_ERR_* code; w_last_error() then
+ *     describes the failure for the calling thread.  No C++ exception crosses
+ *     this boundary.
+ *
+ * bf16 tensors are passed as uint16_t bit patterns (wm_bf16).  All matrices
+ * are row-major and densely packed.
+ *
+ * The reference (baha2046/Whallm) reaches the same operations through MLX
+ * library calls; each declaration names the reference call site it replaces.
+ * Paths are relative to the reference repository.
+ */
+#ifndef WHALLM_B200_H
+#define WHALLM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define WM_API __attribute__((visibility("default")))
+#else
+#define WM_API
+#endif
+
+typedef struct CUstream_st *wm_stream_t;
+typedef uint16_t wm_bf16;
+
+#define WM_OK 0
+#define WM_ERR_INVALID (-1)      /* bad argument, shape or alignment      */
+#define WM_ERR_UNSUPPORTED (-2)  /* valid but not implemented shape       */
+#define WM_ERR_CUDA (-3)         /* CUDA runtime error                    */
+#define WM_ERR_WORKSPACE (-4)    /* workspace too small                   */
+
+/* Output element types for dequantize calls. */
+#define WM_OUT_F32 0
+#define WM_OUT_BF16 1
+
+/* Router score functions (deepseek_v41/moe.py:60-65, qwen4_exp.py:693). */
+#define WM_SCORE_SOFTMAX 0
+#define WM_SCORE_SIGMOID 1
+#define WM_SCORE_SQRTSOFTPLUS 2
+#define WM_SCORE_NONE 3
+
+/* Order of the fused gate/up projection rows. */
+#define WM_UP_GATE 0 /* DeepSeek w13 = [w3(up); w1(gate)]  (expert_layout.py:43-60, model.py:417) */
+#define WM_GATE_UP 1 /* Qwen gate_up = [gate; up]          (qwen4_exp.py:610, Qwen.swift:440)   */
+
+/* KV-cache row formats. */
+#define WKV_FP8_F32_B64 0   /* e4m3, one fp32 scale = amax/448 per 64 values                 */
+#define WKV_FP8_UE8M0_B32 1 /* PackedRows 'fp8_ue8m0'  (deepseek_v41/packed_cache.py:24-59)   */
+#define WKV_FP4_E4M3_B16 2  /* PackedRows 'fp4_e4m3'                                          */
+#define WKV_FP4_UE8M0_B32 3 /* PackedRows 'fp4_ue8m0'                                         */
+#define WKV_MXFP8_B32 4     /* mx.quantize(mode="mxfp8") chunks (fp8_cache.py:112)             */
+#define WKV_MXFP4_B32 5     /* mx.quantize(mode="mxfp4") index copy (fp8_cache.py:116)         */
+
+/* Message for the last failing call on this thread ("" if none). */
+WM_API const char *w_last_error(void);
+/* ABI version of this library. */
+WM_API int w_abi_version(void);
+
+/* ---------------------------------------------------------------- MXFP4 --- */
+
+/* Quantize bf16 [rows, cols] (cols % 32 == 0) to MXFP4: packed e2m1 bytes
+ * [rows, cols/2] (low nibble = even column) and E8M0 scales [rows, cols/32].
+ * Replaces MXFP4.quantizeBF16 (Sources/DeepSeekRepack/MXFP4.swift:4-40); the
+ * bytes are what mx.quantize(mode="mxfp4") stores (MXFP4.swift KATs,
+ * Tests/DeepSeekRepackTests/DeepSeekRepackTests.swift:336-375). */
+WM_API int wmxfp4_quantize(const wm_bf16 *src, int64_t rows, int64_t cols, uint8_t *packed,
+                    uint8_t *scales, wm_stream_t stream);
+
+/* Dequantize MXFP4 [rows, cols] to f32 or bf16 (out_dtype WM_OUT_*), bit-exact:
+ * e2m1[code] * 2^(scale-127), code 8 -> +0.0.
+ * Replaces dequant_fp4 (runtime/deepseek_v4_ssd/deepseek_v41/dequant.py:63-66)
+ * and mx.dequantize(mode="mxfp4"). */
+WM_API int wmxfp4_dequantize(const uint8_t *packed, const uint8_t *scales, int64_t rows, int64_t cols,
+                      int out_dtype, void *out, wm_stream_t stream);
+
+/* ------------------------------------------------------ affine 4-bit ------ */
+
+/* MLX-style affine 4-bit quantize, group `group` (64 or 32) along cols:
+ * packed uint32 [rows, cols/8] (element 0 in the low nibble), bf16 scales and
+ * biases [rows, cols/group].  Replaces mx.quantize(bits=4, group_size=64)
+ * (shapes: runtime/deepseek_v4_ssd/deepseek_v41/engram.py:207-221). */
+WM_API int waffine4_quantize(const wm_bf16 *src, int64_t rows, int64_t cols, int group, uint32_t *packed,
+                      wm_bf16 *scales, wm_bf16 *biases, wm_stream_t stream);
+
+/* w = scale*q + bias (float32), to f32 or bf16.  Replaces mx.dequantize(bits=4). */
+WM_API int waffine4_dequantize(const uint32_t *packed, const wm_bf16 *scales, const wm_bf16 *biases,
+                        int64_t rows, int64_t cols, int group, int out_dtype, void *out,
+                        wm_stream_t stream);
+
+/* ------------------------------------------------------------- KV cache --- */
+
+/* Quantize bf16 rows [rows, D] into payload [rows, D*bits/8] and scales
+ * [rows, D/block] (float32 for WKV_FP8_F32_B64, one byte otherwise).
+ * Replaces PackedRows.write (deepseek_v41/packed_cache.py:24-45) and the
+ * mx.quantize calls of MXFP8PoolingCache.update (fp8_cache.py:109-117). */
+WM_API int wkv_quantize(const wm_bf16 *x, int64_t rows, int D, int fmt, uint8_t *payload, void *scales,
+                 wm_stream_t stream);
+
+/* Dequantize [rows, D] to bf16.  Replaces PackedRows.__getitem__
+ * (packed_cache.py:47-59) and mx.dequantize in MXFP8PoolingCache._fetch
+ * (fp8_cache.py:231-240). */
+WM_API int wkv_dequantize(const uint8_t *payload, const void *scales, int64_t rows, int D, int fmt,
+                   wm_bf16 *out, wm_stream_t stream);
+
+/* Gather rows row_idx[n] (clipped to [0, rows-1]) and dequantize to bf16
+ * [n, D].  Replaces the take_rows + mx.dequantize of
+ * MXFP8PoolingCache.gather (fp8_cache.py:161-190). */
+WM_API int wkv_gather_dequantize(const uint8_t *payload, const void *scales, int64_t rows,
+                          const int32_t *row_idx, int64_t n, int D, int fmt, wm_bf16 *out,
+                          wm_stream_t stream);
+
+/* --------------------------------------------------------------- router --- */
+
+/* Gate logits, scores, top-k and weights for T tokens.
+ *   logits[t,e] = x[t].wg[e] (float32, fixed order) + logit_bias[e] (if given)
+ *   score       = score_fn(logits)           (softmax over E, sigmoid, sqrt(softplus), none)
+ *   selection   = top-k of score + select_bias (bias picks, does not scale;
+ *                 deepseek_v41/moe.py:67-70), ties to the lower expert id
+ *                 (model.py:548-560); idx is in selection order
+ *   weights     = score[idx] / (sum + norm_eps) if norm_eps >= 0, times route_scale
+ *                 (deepseek_v41/moe.py:71-73: eps 1e-20, scale 1.5;
+ *                  qwen4_exp.py:696-697: eps 0, scale 1)
+ *   shared_w[t] = sigmoid(x[t].wg_shared) if wg_shared (qwen4_exp.py:699).
+ * logits [T,E] float32 is caller-provided scratch and receives the biased logits.
+ * Replaces Gate.__call__ (deepseek_v41/moe.py:58-75) and the routing half of
+ * SparseMoE.__call__ (qwen4_exp.py:692-697).  H % 8 == 0, E <= 1024, k <= 32. */
+WM_API int wmoe_router_topk(const wm_bf16 *x, const wm_bf16 *wg, const float *logit_bias,
+                     const float *select_bias, const wm_bf16 *wg_shared, int T, int H, int E, int k,
+                     int score_fn, float norm_eps, float route_scale, float *logits, int32_t *idx,
+                     float *weights, float *shared_w, wm_stream_t stream);
+
+/* The score / top-k / renormalisation half of wmoe_router_topk on caller
+ * logits [T,E] (float32).  With WM_SCORE_NONE and norm_eps < 0 this is the
+ * positional-tie top-k of _stable_topk_indices (model.py:548-560) in
+ * selection order; it also serves gates whose logits come from elsewhere
+ * (mlx-lm MoEGate, called at dspark.py:32). */
+WM_API int wmoe_topk_scores(const float *logits, const float *select_bias, int T, int E, int k,
+                            int score_fn, float norm_eps, float route_scale, int32_t *idx,
+                            float *weights, wm_stream_t stream);
+
+/* -------------------------------------------------------------- permute --- */
+
+/* Stable sort of the T*k assignments by expert (mlx-lm _gather_sort, called at
+ * model.py:404 and qwen4_exp.py:622): offsets [E+1], perm [T*k] (sorted slot
+ * -> flat assignment t*k+j), inv [T*k] (flat -> sorted slot; _scatter_unsort).
+ * The ids are checked on the device: if any is outside [0, E), offsets[E] is
+ * set to -1 and perm/inv are left unwritten. */
+WM_API int wmoe_permute(const int32_t *idx, int T, int k, int E, int32_t *offsets, int32_t *perm,
+                 int32_t *inv, wm_stream_t stream);
+
+/* ------------------------------------------------------ expert forward ---- */
+
+/* Workspace bytes for wmoe_*_experts / wmoe_*_moe_forward. */
+WM_API size_t wmoe_workspace_size(int T, int k, int H, int I, int E, int has_shared);
+
+/* Routed experts, un-reduced: out[t, j, :] = FFN_{idx[t,j]}(x[t]) in bf16 [T,k,H].
+ * Experts are stacked MXFP4: w13 [E, 2I, H/2] + s13 [E, 2I, H/32],
+ * w2 [E, H, I/2] + s2 [E, H, I/32].  FFN = down(act(split(w13 x))) with
+ * ClampedSwiGLU(limit) (limit 0: plain SwiGLU).
+ * Replaces _StreamingSwitchGLU.__call__ / _gather_qmm (model.py:283-459) and
+ * StreamingExperts.__call__ (qwen4_exp.py:613-678). */
+WM_API int wmoe_mxfp4_experts(const wm_bf16 *x, const int32_t *idx, int T, int k, int H, int I, int E,
+                       const uint8_t *w13, const uint8_t *s13, const uint8_t *w2, const uint8_t *s2,
+                       int gate_up_order, float swiglu_limit, wm_bf16 *out, void *workspace,
+                       size_t ws_bytes, wm_stream_t stream);
+
+/* Routed experts + top-k weighted combine (+ shared expert): out [T,H] bf16 =
+ *   sum_j weights[t,j] * FFN_{idx[t,j]}(x[t]) + shared_w[t] * FFN_{shared}(x[t])
+ * in float32.  shared_expert < 0: none; shared_w NULL: weight 1.
+ * Replaces _streaming_moe + _route_reduce (model.py:484-504), MoE.__call__
+ * (deepseek_v41/moe.py:105-112) and SparseMoE.__call__ (qwen4_exp.py:692-704). */
+WM_API int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const float *weights, int T, int k,
+                           int H, int I, int E, const uint8_t *w13, const uint8_t *s13,
+                           const uint8_t *w2, const uint8_t *s2, int gate_up_order,
+                           float swiglu_limit, int shared_expert, const float *shared_w,
+                           wm_bf16 *out, void *workspace, size_t ws_bytes, wm_stream_t stream);
+
+/* Affine 4-bit experts (group `group`): w13 uint32 [E, 2I, H/8] with bf16
+ * sc13/bi13 [E, 2I, H/group]; w2 uint32 [E, H, I/8] with sc2/bi2 [E, H, I/group]. */
+WM_API int wmoe_affine4_experts(const wm_bf16 *x, const int32_t *idx, int T, int k, int H, int I, int E,
+                         const uint32_t *w13, const wm_bf16 *sc13, const wm_bf16 *bi13,
+                         const uint32_t *w2, const wm_bf16 *sc2, const wm_bf16 *bi2, int group,
+                         int gate_up_order, float swiglu_limit, wm_bf16 *out, void *workspace,
+                         size_t ws_bytes, wm_stream_t stream);
+
+WM_API int wmoe_affine4_moe_forward(const wm_bf16 *x, const int32_t *idx, const float *weights, int T,
+                             int k, int H, int I, int E, const uint32_t *w13, const wm_bf16 *sc13,
+                             const wm_bf16 *bi13, const uint32_t *w2, const wm_bf16 *sc2,
+                             const wm_bf16 *bi2, int group, int gate_up_order, float swiglu_limit,
+                             int shared_expert, const float *shared_w, wm_bf16 *out,
+                             void *workspace, size_t ws_bytes, wm_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WHALLM_B200_H */

@@ -1,0 +1,86 @@
+"""The C-ABI library loads, exports every declared symbol, and rejects bad
+arguments with a status code and a message -- all without a GPU (the checks
+run before any CUDA call)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from whallm_b200 import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = []
+    inc = os.path.join(ROOT, "include")
+    for f in sorted(os.listdir(inc)):
+        if f.endswith(".h"):
+            src = open(os.path.join(inc, f)).read()
+            names += re.findall(r"^WM_API\s+[\w\s\*]+?\b(\w+)\s*\(", src, re.M)
+    return names
+
+
+def test_header_declares_the_abi():
+    names = declared_symbols()
+    assert len(names) >= 15
+    assert set(names) == set(L.SIGNATURES), "ctypes signatures and header differ"
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(L.LIB_PATH)
+    for n in declared_symbols():
+        assert hasattr(lib, n), n
+
+
+def test_version_and_empty_error():
+    assert L.lib().w_abi_version() == 1
+    assert isinstance(L.last_error(), str)
+
+
+def _expect(rc_name, *args, code=L.WM_ERR_INVALID, msg=None):
+    rc = getattr(L.lib(), rc_name)(*args)
+    assert rc == code, (rc_name, rc, L.last_error())
+    if msg:
+        assert msg in L.last_error()
+
+
+def test_mxfp4_rejects_partial_groups():
+    _expect("wmxfp4_quantize", None, 1, 33, None, None, None, msg="complete BF16 rows")
+    _expect("wmxfp4_dequantize", None, None, 1, 31, 0, None, None)
+
+
+def test_kv_rejects_bad_format_and_width():
+    _expect("wkv_quantize", None, 4, 576, 9, None, None, None, msg="unknown KV format")
+    _expect("wkv_quantize", None, 4, 600, 0, None, None, None, msg="Invalid packed cache")
+    _expect("wkv_dequantize", None, None, 4, 40, 1, None, None)
+
+
+def test_router_rejects_bad_shapes():
+    f = L.lib().wmoe_router_topk
+    assert f(None, None, None, None, None, 4, 100, 16, 2, 0, -1.0, 1.0, None, None, None, None, None) == L.WM_ERR_INVALID
+    assert "H % 8" in L.last_error()
+    assert f(None, None, None, None, None, 4, 128, 2048, 2, 0, -1.0, 1.0, None, None, None, None, None) == L.WM_ERR_INVALID
+    assert f(None, None, None, None, None, 4, 128, 16, 17, 0, -1.0, 1.0, None, None, None, None, None) == L.WM_ERR_INVALID
+    assert f(None, None, None, None, None, 4, 128, 16, 2, 9, -1.0, 1.0, None, None, None, None, None) == L.WM_ERR_INVALID
+
+
+def test_experts_reject_bad_arguments():
+    f = L.lib().wmoe_mxfp4_moe_forward
+    # gate/up order must be 0 or 1
+    rc = f(None, None, None, 1, 8, 7168, 2048, 256, None, None, None, None, 7, 0.0, -1, None, None, None, 0, None)
+    assert rc == L.WM_ERR_INVALID and "gate_up_order" in L.last_error()
+    rc = f(None, None, None, 1, 8, 7160, 2048, 256, None, None, None, None, 0, 0.0, -1, None, None, None, 0, None)
+    assert rc == L.WM_ERR_INVALID
+
+
+def test_workspace_size_is_pure_host():
+    n = L.lib().wmoe_workspace_size(16, 8, 7168, 2048, 257, 1)
+    assert n > 16 * 9 * 7168 * 4
+    assert L.lib().wmoe_workspace_size(-1, 8, 7168, 2048, 257, 1) == 0
+
+
+def test_call_raises_valueerror_on_invalid():
+    with pytest.raises(ValueError, match="complete BF16 rows"):
+        L.call("wmxfp4_quantize", None, 1, 33, None, None, None)

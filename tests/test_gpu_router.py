@@ -1,0 +1,105 @@
+"""Device router vs the CPU oracle: indices and weights bit-exact.
+
+Covers every score function, logit and selection biases, the renormalisation
+variants (V4.1 eps 1e-20 x 1.5, Qwen plain sum, none), the Qwen shared-expert
+gate, exact ties (positional rule, test_runtime.py:2530-2533), E not a
+multiple of 32, T = 0 and k = 1, and the DeepSeek-class shapes.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import whallm_b200 as W
+from oracle import formats as F
+from oracle import router as R
+
+pytestmark = pytest.mark.gpu
+GOLD = os.path.join(os.path.dirname(__file__), "golden")
+FN = {R.SCORE_SOFTMAX: "softmax", R.SCORE_SIGMOID: "sigmoid", R.SCORE_SQRTSOFTPLUS: "sqrtsoftplus", R.SCORE_NONE: "none"}
+
+
+def _bf16(bits, dev):
+    return torch.from_numpy(np.ascontiguousarray(bits).astype(np.int16)).view(torch.bfloat16).to(dev)
+
+
+def _run(dev, xb, wb, k, fn, lb=None, sb=None, eps=-1.0, scale=1.0, sg=None):
+    x = _bf16(xb, dev)
+    w = _bf16(wb, dev)
+    t = lambda a: None if a is None else torch.from_numpy(a).to(dev)
+    logits = torch.empty(xb.shape[0], wb.shape[0], dtype=torch.float32, device=dev)
+    wts, idx, sh = W.route(x, w, k, FN[fn], logit_bias=t(lb), select_bias=t(sb), norm_eps=None if eps < 0 else eps,
+                           route_scale=scale, shared_gate=None if sg is None else _bf16(sg, dev), logits_out=logits)
+    return (logits.cpu().numpy(), idx.cpu().numpy(), wts.cpu().numpy(),
+            None if sh is None else sh.reshape(-1).cpu().numpy())
+
+
+def _check(got, ref):
+    lg, idx, w, sh = got
+    rl, ri, rw, rs = ref
+    np.testing.assert_array_equal(lg.view(np.uint32), rl.view(np.uint32))
+    np.testing.assert_array_equal(idx, ri)
+    np.testing.assert_array_equal(w.view(np.uint32), rw.view(np.uint32))
+    if rs is not None:
+        np.testing.assert_array_equal(sh.view(np.uint32), rs.view(np.uint32))
+
+
+@pytest.mark.parametrize("case", range(4))
+def test_router_golden(dev, case):
+    g = np.load(os.path.join(GOLD, "golden.npz"))
+    cases = [(R.SCORE_SOFTMAX, None, "rt_logit_bias", 0.0, 1.0, "rt_shared_gate"),
+             (R.SCORE_SIGMOID, "rt_sel_bias", None, 1e-20, 2.5, None),
+             (R.SCORE_SQRTSOFTPLUS, "rt_sel_bias", "rt_logit_bias", 1e-20, 1.5, None),
+             (R.SCORE_NONE, None, None, -1.0, 1.0, None)]
+    fn, sb, lb, eps, scale, sg = cases[case]
+    got = _run(dev, g["rt_x"], g["rt_w"], 6, fn, None if lb is None else g[lb], None if sb is None else g[sb], eps,
+               scale, None if sg is None else g[sg])
+    ref = (g[f"rt{case}_logits"], g[f"rt{case}_idx"], g[f"rt{case}_w"],
+           g[f"rt{case}_shared"] if f"rt{case}_shared" in g.files else None)
+    _check(got, ref)
+
+
+@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SIGMOID, R.SCORE_SQRTSOFTPLUS])
+@pytest.mark.parametrize("shape", [(1, 7168, 256, 8), (37, 2048, 512, 10), (5, 1024, 16, 4), (9, 264, 100, 1)])
+def test_router_random_vs_oracle(dev, fn, shape):
+    T, H, E, k = shape
+    rng = np.random.default_rng(T * 131 + E + fn)
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    lb = np.log(np.arange(1, E + 1, dtype=np.float64) ** -1.0 / np.sum(np.arange(1, E + 1) ** -1.0)).astype(np.float32)
+    rng.shuffle(lb)
+    sb = rng.normal(0, 0.1, E).astype(np.float32)
+    ref = R.route(xb, wb, k, fn, logit_bias=lb, select_bias=sb, norm_eps=1e-20, route_scale=1.5)
+    _check(_run(dev, xb, wb, k, fn, lb, sb, 1e-20, 1.5), ref)
+
+
+def test_router_exact_ties_choose_lower_index(dev):
+    xb = np.zeros((3, 256), np.uint16)
+    wb = np.zeros((40, 256), np.uint16)
+    ref = R.route(xb, wb, 5, R.SCORE_SOFTMAX, norm_eps=0.0)
+    got = _run(dev, xb, wb, 5, R.SCORE_SOFTMAX, eps=0.0)
+    _check(got, ref)
+    assert got[1].tolist() == [[0, 1, 2, 3, 4]] * 3
+    s = torch.tensor([[1.0, 1.0, 1.0, 0.5]], device=dev)
+    assert W.stable_topk_indices(s, 2).cpu().tolist() == [[0, 1]]
+
+
+def test_router_empty_batch(dev):
+    x = torch.empty(0, 256, dtype=torch.bfloat16, device=dev)
+    w = torch.zeros(16, 256, dtype=torch.bfloat16, device=dev)
+    wts, idx, _ = W.route(x, w, 4)
+    assert wts.shape == (0, 4) and idx.shape == (0, 4)
+
+
+def test_gate_v41_semantics(dev):
+    rng = np.random.default_rng(77)
+    T, H, E, k = 16, 512, 64, 6
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    bias = rng.normal(0, 0.5, E).astype(np.float32)
+    gate = W.Gate(_bf16(wb, dev), k, "sqrtsoftplus", bias=torch.from_numpy(bias).to(dev), route_scale=1.5)
+    wts, idx = gate(_bf16(xb, dev))
+    _, ri, rw, _ = R.route(xb, wb, k, R.SCORE_SQRTSOFTPLUS, select_bias=bias, norm_eps=1e-20, route_scale=1.5)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_array_equal(wts.cpu().numpy().view(np.uint32), rw.view(np.uint32))

@@ -1,0 +1,460 @@
+// Number-format kernels: MXFP4 and affine-4 weights, KV-cache row formats.
+//
+// All of these are HBM-bound elementwise passes.  One thread owns one scale
+// group (16..64 values), reads it with 16-byte loads and writes its packed
+// bytes and scale; consecutive threads own consecutive groups, so warps read
+// and write contiguous spans.  Results are bit-exact against the CPU
+// restatement: only IEEE-exact float32 operations are used and this file is
+// compiled with -fmad=false.
+#include <algorithm>
+
+#include "wm_common.cuh"
+
+namespace {
+
+constexpr float kFp8MaxInv = 0x1.24924ap-9f;  // float32(1/448)  (fakequant.py:34)
+constexpr float kFp4MaxInv = 0x1.555556p-3f;  // float32(1/6)    (fakequant.py:35)
+constexpr float kFp8Floor = 0x1.a36e2ep-14f;  // float32(1e-4)   (packed_cache.py:34)
+constexpr float kFp4UeFloor = 0x1.8p-124f;    // 6 * 2^-126      (packed_cache.py:35)
+constexpr float kFp4E4Floor = 0x1.8p-7f;      // 6 * 2^-9        (packed_cache.py:29)
+
+// floor(log2 a) for positive finite a (subnormals included) == Swift Float.exponent
+__device__ __forceinline__ int floor_log2(float a) {
+  uint32_t b = __float_as_uint(a);
+  uint32_t ex = (b >> 23) & 255u;
+  if (ex != 0) return static_cast<int>(ex) - 127;
+  uint32_t m = b & 0x7fffffu;
+  return (31 - __clz(static_cast<int>(m))) - 149;
+}
+
+// 2^k as float for k in [-149, 127], exact
+__device__ __forceinline__ float pow2i(int k) {
+  if (k >= -126) return __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
+  return __uint_as_float(1u << (k + 149));
+}
+
+// ceil(log2 x) via IEEE bits for positive normal x (fakequant.py:47-52)
+__device__ __forceinline__ int ceil_log2_bits(float x) {
+  uint32_t b = __float_as_uint(x);
+  int e = static_cast<int>((b >> 23) & 255u) - 127;
+  return e + ((b & 0x7fffffu) != 0 ? 1 : 0);
+}
+
+__device__ __forceinline__ void load_bf16x32(const uint16_t *p, float *v) {
+  const uint4 *q = reinterpret_cast<const uint4 *>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = __ldg(q + i);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[8 * i + 2 * j] = wm_bf16lo(w[j]);
+      v[8 * i + 2 * j + 1] = wm_bf16hi(w[j]);
+    }
+  }
+}
+
+// Swift MXFP4.quantizeBF16 (MXFP4.swift:19-37) on 32 float32 values.
+__device__ __forceinline__ void mxfp4_group(const float *v, uint8_t *out16, uint8_t *scale) {
+  float amax = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  uint32_t words[4] = {0u, 0u, 0u, 0u};
+  if (amax == 0.0f) {
+    *scale = 0;
+  } else {
+    int e = floor_log2(amax) - 2;
+    e = max(-127, min(128, e));
+    *scale = static_cast<uint8_t>(e + 127);
+    float f = pow2i(-e);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      uint32_t c = wm_e2m1_code(v[i] * f);
+      words[i >> 3] |= c << (4 * (i & 7));
+    }
+  }
+  *reinterpret_cast<uint4 *>(out16) = make_uint4(words[0], words[1], words[2], words[3]);
+}
+
+__global__ void k_mxfp4_quantize(const uint16_t *__restrict__ src, int64_t groups,
+                                 uint8_t *__restrict__ packed, uint8_t *__restrict__ scales) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    float v[32];
+    load_bf16x32(src + g * 32, v);
+    mxfp4_group(v, packed + g * 16, scales + g);
+  }
+}
+
+template <typename OutT>
+__device__ __forceinline__ void store32(OutT *dst, const float *v);
+
+template <>
+__device__ __forceinline__ void store32<float>(float *dst, const float *v) {
+  float4 *d = reinterpret_cast<float4 *>(dst);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) d[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+}
+
+template <>
+__device__ __forceinline__ void store32<uint16_t>(uint16_t *dst, const float *v) {
+  uint4 *d = reinterpret_cast<uint4 *>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = wm_f32_to_bf16(v[8 * i + 2 * j]) | (static_cast<uint32_t>(wm_f32_to_bf16(v[8 * i + 2 * j + 1])) << 16);
+    d[i] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
+}
+
+template <typename OutT>
+__global__ void k_mxfp4_dequantize(const uint8_t *__restrict__ packed, const uint8_t *__restrict__ scales,
+                                   int64_t groups, OutT *__restrict__ out) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    uint4 u = __ldg(reinterpret_cast<const uint4 *>(packed) + g);
+    float s = wm_e8m0(scales[g]);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = wm_e2m1((w[i >> 3] >> (4 * (i & 7))) & 15u) * s;
+    store32<OutT>(out + g * 32, v);
+  }
+}
+
+// ------------------------------------------------------------ affine 4 ----
+
+__global__ void k_affine4_quantize(const uint16_t *__restrict__ src, int64_t groups, int group,
+                                   uint32_t *__restrict__ packed, uint16_t *__restrict__ scales,
+                                   uint16_t *__restrict__ biases) {
+  for (int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; g < groups;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    const uint16_t *p = src + g * group;
+    float wmax = -__int_as_float(0x7f800000), wmin = __int_as_float(0x7f800000);
+    for (int i = 0; i < group; i += 32) {
+      float v[32];
+      load_bf16x32(p + i, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) { wmax = fmaxf(wmax, v[j]); wmin = fminf(wmin, v[j]); }
+    }
+    bool mask = fabsf(wmin) > fabsf(wmax);
+    float scale = fmaxf(__fdiv_rn(wmax - wmin, 15.0f), 1e-7f);
+    scale = mask ? scale : -scale;
+    float edge = mask ? wmin : wmax;
+    float q0 = rintf(__fdiv_rn(edge, scale));
+    if (q0 != 0.0f) scale = __fdiv_rn(edge, q0);
+    float bias = q0 == 0.0f ? 0.0f : edge;
+    uint32_t *dst = packed + g * (group / 8);
+    for (int i = 0; i < group; i += 32) {
+      float v[32];
+      load_bf16x32(p + i, v);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float q = rintf(__fdiv_rn(v[8 * w + j] - bias, scale));
+          q = fminf(fmaxf(q, 0.0f), 15.0f);
+          word |= static_cast<uint32_t>(q) << (4 * j);
+        }
+        dst[i / 8 + w] = word;
+      }
+    }
+    scales[g] = wm_f32_to_bf16(scale);
+    biases[g] = wm_f32_to_bf16(bias);
+  }
+}
+
+template <typename OutT>
+__global__ void k_affine4_dequantize(const uint32_t *__restrict__ packed, const uint16_t *__restrict__ scales,
+                                     const uint16_t *__restrict__ biases, int64_t chunks, int group,
+                                     OutT *__restrict__ out) {
+  // one thread per 32 values (a quarter or half group)
+  for (int64_t c = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; c < chunks;
+       c += (int64_t)gridDim.x * blockDim.x) {
+    int64_t g = (c * 32) / group;
+    float s = wm_bf16_to_f32(scales[g]);
+    float b = wm_bf16_to_f32(biases[g]);
+    uint4 u = __ldg(reinterpret_cast<const uint4 *>(packed) + c);
+    uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = s * static_cast<float>((w[i >> 3] >> (4 * (i & 7))) & 15u) + b;
+    store32<OutT>(out + c * 32, v);
+  }
+}
+
+// ------------------------------------------------------------- KV rows ----
+
+__device__ __forceinline__ int kv_block(int fmt) {
+  return fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
+}
+__device__ __host__ __forceinline__ int kv_bits(int fmt) {
+  return (fmt == WKV_FP8_F32_B64 || fmt == WKV_FP8_UE8M0_B32 || fmt == WKV_MXFP8_B32) ? 8 : 4;
+}
+
+// e2m1 code of _e2m1_round(v) with the packed-cache sign rule:
+// sign only for a nonzero negative result (packed_cache.py:40-42).
+__device__ __forceinline__ uint32_t packed_fp4_code(float v) {
+  float m = fabsf(v);
+  uint32_t idx = (m > 0.25f) + (m > 1.25f) + (m > 2.5f) + (m > 5.0f) + (m >= 0.75f) + (m >= 1.75f) + (m >= 3.5f);
+  return idx | ((idx != 0u && v < 0.0f) ? 8u : 0u);
+}
+
+// quantize one block of `blk` values (blk = 16, 32 or 64) starting at x
+__device__ void kv_quant_block(const uint16_t *x, int blk, int fmt, uint8_t *payload, void *scales, int64_t sidx) {
+  float v[64];
+  for (int i = 0; i < blk; i += 32) {
+    if (blk == 16) {
+      const uint4 *q = reinterpret_cast<const uint4 *>(x);
+      for (int a = 0; a < 2; ++a) {
+        uint4 u = __ldg(q + a);
+        uint32_t w[4] = {u.x, u.y, u.z, u.w};
+        for (int j = 0; j < 4; ++j) { v[8 * a + 2 * j] = wm_bf16lo(w[j]); v[8 * a + 2 * j + 1] = wm_bf16hi(w[j]); }
+      }
+    } else {
+      load_bf16x32(x + i, v + i);
+    }
+  }
+  float amax = 0.0f;
+  for (int i = 0; i < blk; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  if (fmt == WKV_MXFP4_B32) {
+    uint8_t sc;
+    mxfp4_group(v, payload, &sc);
+    static_cast<uint8_t *>(scales)[sidx] = sc;
+    return;
+  }
+  if (fmt == WKV_FP8_F32_B64 || fmt == WKV_FP8_UE8M0_B32 || fmt == WKV_MXFP8_B32) {
+    float s = 0.0f, f = 1.0f;
+    bool zero = false;
+    bool mul = false;
+    if (fmt == WKV_FP8_F32_B64) {
+      s = __fdiv_rn(amax, 448.0f);
+      zero = !(s > 0.0f);
+      static_cast<float *>(scales)[sidx] = s;
+    } else if (fmt == WKV_FP8_UE8M0_B32) {
+      int e = ceil_log2_bits(fmaxf(amax, kFp8Floor) * kFp8MaxInv);
+      s = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+      static_cast<uint8_t *>(scales)[sidx] = static_cast<uint8_t>(e + 127);
+    } else {
+      zero = amax == 0.0f;
+      int e = zero ? 0 : max(-127, min(127, floor_log2(amax) - 8));
+      f = pow2i(-e);
+      mul = true;
+      static_cast<uint8_t *>(scales)[sidx] = zero ? 0 : static_cast<uint8_t>(e + 127);
+    }
+    for (int i = 0; i < blk; i += 4) {
+      uint32_t word = 0;
+      for (int j = 0; j < 4; ++j) {
+        float q = 0.0f;
+        if (!zero) {
+          q = mul ? v[i + j] * f : __fdiv_rn(v[i + j], s);
+          q = fminf(fmaxf(q, -448.0f), 448.0f);
+        }
+        uint32_t c = zero ? (__float_as_uint(v[i + j]) >> 31 ? 0u : 0u) : wm_f32_to_e4m3(q);
+        word |= c << (8 * j);
+      }
+      reinterpret_cast<uint32_t *>(payload)[i / 4] = word;
+    }
+    return;
+  }
+  // fp4 packed-cache formats
+  float s;
+  if (fmt == WKV_FP4_E4M3_B16) {
+    uint32_t enc = wm_f32_to_e4m3(__fdiv_rn(fmaxf(amax, kFp4E4Floor), 6.0f));
+    s = wm_e4m3_to_f32(enc);
+    static_cast<uint8_t *>(scales)[sidx] = static_cast<uint8_t>(enc);
+  } else {
+    int e = ceil_log2_bits(fmaxf(amax, kFp4UeFloor) * kFp4MaxInv);
+    s = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+    static_cast<uint8_t *>(scales)[sidx] = static_cast<uint8_t>(e + 127);
+  }
+  for (int i = 0; i < blk; i += 8) {
+    uint32_t word = 0;
+    for (int j = 0; j < 8; ++j) {
+      float q = fminf(fmaxf(__fdiv_rn(v[i + j], s), -6.0f), 6.0f);
+      word |= packed_fp4_code(q) << (4 * j);
+    }
+    reinterpret_cast<uint32_t *>(payload)[i / 8] = word;
+  }
+}
+
+__global__ void k_kv_quantize(const uint16_t *__restrict__ x, int64_t rows, int D, int fmt,
+                              uint8_t *__restrict__ payload, void *__restrict__ scales) {
+  const int blk = kv_block(fmt);
+  const int nb = D / blk;
+  const int bits = kv_bits(fmt);
+  const int64_t total = rows * nb;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < total;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    kv_quant_block(x + b * blk, blk, fmt, payload + b * blk * bits / 8, scales, b);
+  }
+}
+
+__device__ __forceinline__ float kv_scale(const void *scales, int64_t sidx, int fmt) {
+  if (fmt == WKV_FP8_F32_B64) return static_cast<const float *>(scales)[sidx];
+  uint32_t b = static_cast<const uint8_t *>(scales)[sidx];
+  if (fmt == WKV_FP4_E4M3_B16) return wm_e4m3_to_f32(b);
+  if (fmt == WKV_MXFP8_B32 || fmt == WKV_MXFP4_B32) return wm_e8m0(b);
+  return __uint_as_float(b << 23);  // PackedRows: (scale << 23).view(float32)
+}
+
+__device__ void kv_dequant_block(const uint8_t *payload, float s, int blk, int fmt, uint16_t *out) {
+  const int bits = kv_bits(fmt);
+  for (int i = 0; i < blk; i += 8) {
+    float v[8];
+    if (bits == 8) {
+      uint2 u = *reinterpret_cast<const uint2 *>(payload + i);
+      uint32_t w[2] = {u.x, u.y};
+      for (int j = 0; j < 8; ++j) v[j] = wm_e4m3_to_f32((w[j >> 2] >> (8 * (j & 3))) & 255u) * s;
+    } else {
+      uint32_t w = *reinterpret_cast<const uint32_t *>(payload + i / 2);
+      for (int j = 0; j < 8; ++j) {
+        uint32_t c = (w >> (4 * j)) & 15u;
+        float q = fmt == WKV_MXFP4_B32 ? wm_e2m1(c) : wm_e2m1_scaled(c) * 0x1p126f;
+        v[j] = q * s;
+      }
+    }
+    uint4 o;
+    o.x = wm_f32_to_bf16(v[0]) | (static_cast<uint32_t>(wm_f32_to_bf16(v[1])) << 16);
+    o.y = wm_f32_to_bf16(v[2]) | (static_cast<uint32_t>(wm_f32_to_bf16(v[3])) << 16);
+    o.z = wm_f32_to_bf16(v[4]) | (static_cast<uint32_t>(wm_f32_to_bf16(v[5])) << 16);
+    o.w = wm_f32_to_bf16(v[6]) | (static_cast<uint32_t>(wm_f32_to_bf16(v[7])) << 16);
+    *reinterpret_cast<uint4 *>(out + i) = o;
+  }
+}
+
+__global__ void k_kv_dequantize(const uint8_t *__restrict__ payload, const void *__restrict__ scales,
+                                int64_t rows, const int32_t *__restrict__ row_idx, int64_t n, int D, int fmt,
+                                uint16_t *__restrict__ out) {
+  const int blk = kv_block(fmt);
+  const int nb = D / blk;
+  const int bits = kv_bits(fmt);
+  const int64_t total = n * nb;
+  for (int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; b < total;
+       b += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = b / nb, j = b % nb;
+    int64_t src = r;
+    if (row_idx) {
+      int64_t q = row_idx[r];
+      src = q < 0 ? 0 : (q >= rows ? rows - 1 : q);
+    }
+    int64_t sb = src * nb + j;
+    float s = kv_scale(scales, sb, fmt);
+    kv_dequant_block(payload + sb * blk * bits / 8, s, blk, fmt, out + r * D + j * blk);
+  }
+}
+
+int grid_for(int64_t work, int threads) {
+  int64_t blocks = (work + threads - 1) / threads;
+  int64_t cap = static_cast<int64_t>(wm::sm_count()) * 16;
+  return static_cast<int>(std::max<int64_t>(1, std::min(blocks, cap)));
+}
+
+int kv_check(int64_t rows, int D, int fmt) {
+  if (fmt < 0 || fmt > 5) return wm::fail(WM_ERR_INVALID, "unknown KV format");
+  int blk = fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
+  if (rows < 0 || D <= 0 || D % blk) return wm::fail(WM_ERR_INVALID, "Invalid packed cache format or width");
+  return WM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wmxfp4_quantize(const wm_bf16 *src, int64_t rows, int64_t cols, uint8_t *packed, uint8_t *scales,
+                    wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(rows > 0 && cols > 0 && cols % 32 == 0, "MXFP4 source must contain complete BF16 rows");
+  WM_REQUIRE(wm::aligned(src, 16) && wm::aligned(packed, 16), "MXFP4 buffers must be 16-byte aligned");
+  int64_t groups = rows * (cols / 32);
+  k_mxfp4_quantize<<<grid_for(groups, 256), 256, 0, stream>>>(src, groups, packed, scales);
+  return wm::check_launch("wmxfp4_quantize");
+}
+
+int wmxfp4_dequantize(const uint8_t *packed, const uint8_t *scales, int64_t rows, int64_t cols, int out_dtype,
+                      void *out, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(rows >= 0 && cols > 0 && cols % 32 == 0, "MXFP4 dequantize needs cols % 32 == 0");
+  WM_REQUIRE(out_dtype == WM_OUT_F32 || out_dtype == WM_OUT_BF16, "out_dtype must be WM_OUT_F32 or WM_OUT_BF16");
+  WM_REQUIRE(wm::aligned(packed, 16) && wm::aligned(out, 16), "MXFP4 buffers must be 16-byte aligned");
+  int64_t groups = rows * (cols / 32);
+  if (groups == 0) return WM_OK;
+  if (out_dtype == WM_OUT_F32)
+    k_mxfp4_dequantize<float><<<grid_for(groups, 256), 256, 0, stream>>>(packed, scales, groups, static_cast<float *>(out));
+  else
+    k_mxfp4_dequantize<uint16_t><<<grid_for(groups, 256), 256, 0, stream>>>(packed, scales, groups, static_cast<uint16_t *>(out));
+  return wm::check_launch("wmxfp4_dequantize");
+}
+
+int waffine4_quantize(const wm_bf16 *src, int64_t rows, int64_t cols, int group, uint32_t *packed, wm_bf16 *scales,
+                      wm_bf16 *biases, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(group == 32 || group == 64 || group == 128, "affine4 group must be 32, 64 or 128");
+  WM_REQUIRE(rows > 0 && cols > 0 && cols % group == 0, "affine4 needs cols % group == 0");
+  WM_REQUIRE(wm::aligned(src, 16) && wm::aligned(packed, 16), "affine4 buffers must be 16-byte aligned");
+  int64_t groups = rows * (cols / group);
+  k_affine4_quantize<<<grid_for(groups, 128), 128, 0, stream>>>(src, groups, group, packed, scales, biases);
+  return wm::check_launch("waffine4_quantize");
+}
+
+int waffine4_dequantize(const uint32_t *packed, const wm_bf16 *scales, const wm_bf16 *biases, int64_t rows,
+                        int64_t cols, int group, int out_dtype, void *out, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(group == 32 || group == 64 || group == 128, "affine4 group must be 32, 64 or 128");
+  WM_REQUIRE(rows >= 0 && cols > 0 && cols % group == 0, "affine4 needs cols % group == 0");
+  WM_REQUIRE(out_dtype == WM_OUT_F32 || out_dtype == WM_OUT_BF16, "out_dtype must be WM_OUT_F32 or WM_OUT_BF16");
+  WM_REQUIRE(wm::aligned(packed, 16) && wm::aligned(out, 16), "affine4 buffers must be 16-byte aligned");
+  int64_t chunks = rows * (cols / 32);
+  if (chunks == 0) return WM_OK;
+  if (out_dtype == WM_OUT_F32)
+    k_affine4_dequantize<float><<<grid_for(chunks, 256), 256, 0, stream>>>(packed, scales, biases, chunks, group,
+                                                                            static_cast<float *>(out));
+  else
+    k_affine4_dequantize<uint16_t><<<grid_for(chunks, 256), 256, 0, stream>>>(packed, scales, biases, chunks, group,
+                                                                               static_cast<uint16_t *>(out));
+  return wm::check_launch("waffine4_dequantize");
+}
+
+int wkv_quantize(const wm_bf16 *x, int64_t rows, int D, int fmt, uint8_t *payload, void *scales, wm_stream_t stream) {
+  wm::clear_error();
+  if (int rc = kv_check(rows, D, fmt)) return rc;
+  WM_REQUIRE(wm::aligned(x, 16) && wm::aligned(payload, 16) && wm::aligned(scales, 4),
+             "KV buffers must be 16-byte aligned (scales 4-byte)");
+  int blk = fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
+  int64_t total = rows * (D / blk);
+  if (total == 0) return WM_OK;
+  k_kv_quantize<<<grid_for(total, 128), 128, 0, stream>>>(x, rows, D, fmt, payload, scales);
+  return wm::check_launch("wkv_quantize");
+}
+
+int wkv_dequantize(const uint8_t *payload, const void *scales, int64_t rows, int D, int fmt, wm_bf16 *out,
+                   wm_stream_t stream) {
+  wm::clear_error();
+  if (int rc = kv_check(rows, D, fmt)) return rc;
+  WM_REQUIRE(wm::aligned(payload, 16) && wm::aligned(out, 16) && wm::aligned(scales, 4),
+             "KV buffers must be 16-byte aligned (scales 4-byte)");
+  int blk = fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
+  int64_t total = rows * (D / blk);
+  if (total == 0) return WM_OK;
+  k_kv_dequantize<<<grid_for(total, 128), 128, 0, stream>>>(payload, scales, rows, nullptr, rows, D, fmt, out);
+  return wm::check_launch("wkv_dequantize");
+}
+
+int wkv_gather_dequantize(const uint8_t *payload, const void *scales, int64_t rows, const int32_t *row_idx,
+                          int64_t n, int D, int fmt, wm_bf16 *out, wm_stream_t stream) {
+  wm::clear_error();
+  if (int rc = kv_check(rows, D, fmt)) return rc;
+  WM_REQUIRE(rows > 0 && n >= 0 && row_idx != nullptr, "gather needs rows > 0 and an index array");
+  WM_REQUIRE(wm::aligned(payload, 16) && wm::aligned(out, 16) && wm::aligned(scales, 4),
+             "KV buffers must be 16-byte aligned (scales 4-byte)");
+  int blk = fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
+  int64_t total = n * (D / blk);
+  if (total == 0) return WM_OK;
+  k_kv_dequantize<<<grid_for(total, 128), 128, 0, stream>>>(payload, scales, rows, row_idx, n, D, fmt, out);
+  return wm::check_launch("wkv_gather_dequantize");
+}
+
+}  // extern "C"

@@ -1,0 +1,381 @@
+// Grouped expert GEMV for decode-shaped work (few tokens per expert).
+//
+// Reference: _StreamingSwitchGLU decode / _forward_with_resident / _gather_qmm
+// (model.py:283-459), _mxfp4 / _mxfp4_swiglu (model.py:462-481), Qwen
+// StreamingExperts (qwen4_exp.py:600-678), ClampedSwiGLU
+// (deepseek_v41/moe.py:30-43), _route_reduce (model.py:502-504).
+//
+// Shape of the work: weights are the bulk of the bytes (23.4 MB per
+// DeepSeek-class expert) and each is used by a handful of tokens, so the
+// kernel streams every active expert's packed rows from HBM exactly once per
+// token chunk and dequantizes them in registers.
+//
+//   * Work item = (active expert, block of rows).  A persistent grid walks the
+//     items; the list of active experts comes from the permute kernel, so
+//     idle experts cost nothing.
+//   * Each warp owns 4 weight rows.  Lane l reads 16 bytes (32 FP4 values =
+//     one scale group) of each row per step, i.e. 128-bit coalesced loads of
+//     512 contiguous bytes per row per warp instruction; the same x chunk is
+//     reused for the 4 rows.
+//   * Per-lane partial sums are reduced with a warp-shuffle butterfly.
+//   * Phase "up": rows are (up_j, gate_j, up_j+1, gate_j+1) of w13, so the
+//     fused ClampedSwiGLU runs in the epilogue and writes h (bf16) directly.
+//   * Phase "down": rows of w2 over h; outputs y (f32) in sorted-slot order.
+//   * Combine: per token, sum_j w_j * y_j (+ shared) in float32, fixed order.
+#include "wm_common.cuh"
+#include "wm_moe.cuh"
+
+namespace {
+
+constexpr int kFmtMxfp4 = 0;
+constexpr int kFmtAffine4 = 1;
+constexpr int kModeUp = 0;
+constexpr int kModeDown = 1;
+constexpr int kNT = 4;        // tokens per pass
+constexpr int kWarps = 8;     // warps per CTA
+constexpr int kRowsPerWarp = 4;
+
+struct Weights {
+  const uint8_t *w;      // packed rows, K/2 bytes per row
+  const uint8_t *s;      // mxfp4 scales [rows, K/32]
+  const uint16_t *sc;    // affine scales [rows, K/group]
+  const uint16_t *bi;    // affine biases
+  int group;             // affine group size
+  int rows;              // rows per expert
+  int K;                 // row length in elements
+};
+
+__device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
+
+template <int FMT, int MODE>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    k_expert_gemv(const uint16_t *__restrict__ in, int kk, const int32_t *__restrict__ offsets,
+                  const int32_t *__restrict__ perm, const int32_t *__restrict__ active,
+                  const int32_t *__restrict__ counters, Weights W, int I, int order, float limit,
+                  uint16_t *__restrict__ h_out, float *__restrict__ y_out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = W.K;
+  const int rows_per_item = kWarps * kRowsPerWarp;  // 32
+  // up: an item covers 16 intermediate indices (32 rows of w13); down: 32 rows of w2
+  const int items_per_expert = (MODE == kModeUp) ? (I / 16) : (W.rows / rows_per_item);
+  const int n_items = counters[0] * items_per_expert;
+  const int groups = K / 32;
+  const int64_t row_bytes = K / 2;
+  for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+    const int a = item / items_per_expert, blk = item - a * items_per_expert;
+    const int e = active[a];
+    const int p0 = offsets[e], n = offsets[e + 1] - p0;
+    int row[kRowsPerWarp];
+    int j0 = 0;
+    if (MODE == kModeUp) {
+      j0 = blk * 16 + warp * 2;
+      const int ub = order == WM_UP_GATE ? 0 : I, gb = order == WM_UP_GATE ? I : 0;
+      row[0] = ub + j0; row[1] = gb + j0; row[2] = ub + j0 + 1; row[3] = gb + j0 + 1;
+    } else {
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r) row[r] = blk * rows_per_item + warp * kRowsPerWarp + r;
+    }
+    const int64_t erow0 = static_cast<int64_t>(e) * W.rows;
+    for (int c = 0; c < n; c += kNT) {
+      const int nt = min(kNT, n - c);
+      const uint16_t *src[kNT];
+#pragma unroll
+      for (int t = 0; t < kNT; ++t) {
+        int p = p0 + c + min(t, nt - 1);
+        src[t] = (MODE == kModeUp) ? in + static_cast<int64_t>(perm[p] / kk) * K : in + static_cast<int64_t>(p) * K;
+      }
+      float acc[kRowsPerWarp][kNT];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+        for (int t = 0; t < kNT; ++t) acc[r][t] = 0.0f;
+      for (int q = lane; q < groups; q += 32) {
+        uint4 wq[kRowsPerWarp];
+        float sc[kRowsPerWarp], bi[kRowsPerWarp];
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) {
+          const int64_t gr = erow0 + row[r];
+          wq[r] = __ldg(reinterpret_cast<const uint4 *>(W.w + gr * row_bytes) + q);
+          if (FMT == kFmtMxfp4) {
+            sc[r] = wm_e8m0(W.s[gr * groups + q]);
+            bi[r] = 0.0f;
+          } else {
+            const int ng = K / W.group;
+            const int g = (q * 32) / W.group;
+            sc[r] = wm_bf16_to_f32(W.sc[gr * ng + g]);
+            bi[r] = wm_bf16_to_f32(W.bi[gr * ng + g]);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kNT; ++t) {
+          if (t < nt) {
+            const uint4 *xp = reinterpret_cast<const uint4 *>(src[t] + q * 32);
+            float xv[32];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 u = __ldg(xp + i);
+              xv[8 * i + 0] = wm_bf16lo(u.x); xv[8 * i + 1] = wm_bf16hi(u.x);
+              xv[8 * i + 2] = wm_bf16lo(u.y); xv[8 * i + 3] = wm_bf16hi(u.y);
+              xv[8 * i + 4] = wm_bf16lo(u.z); xv[8 * i + 5] = wm_bf16hi(u.z);
+              xv[8 * i + 6] = wm_bf16lo(u.w); xv[8 * i + 7] = wm_bf16hi(u.w);
+            }
+            float sx = 0.0f;
+            if (FMT == kFmtAffine4) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) sx += xv[i];
+            }
+#pragma unroll
+            for (int r = 0; r < kRowsPerWarp; ++r) {
+              const uint32_t wd[4] = {wq[r].x, wq[r].y, wq[r].z, wq[r].w};
+              float part = 0.0f;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const uint32_t nib = (wd[i >> 3] >> (4 * (i & 7))) & 15u;
+                float wv;
+                if (FMT == kFmtMxfp4) wv = wm_e2m1_scaled(nib);
+                else wv = __uint_as_float(0x4B000000u | nib) - 8388608.0f;
+                part = fmaf(xv[i], wv, part);
+              }
+              if (FMT == kFmtMxfp4) acc[r][t] = fmaf(part * 0x1p126f, sc[r], acc[r][t]);
+              else acc[r][t] = fmaf(part, sc[r], fmaf(sx, bi[r], acc[r][t]));
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+        for (int t = 0; t < kNT; ++t) {
+          float v = acc[r][t];
+#pragma unroll
+          for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+          acc[r][t] = v;
+        }
+      if (MODE == kModeUp) {
+        // lane (jj * kNT + t) finishes intermediate j0 + jj for token t
+        if (lane < 2 * kNT) {
+          const int jj = lane / kNT, t = lane % kNT;
+          if (t < nt) {
+            float up = 0.f, gate = 0.f;
+#pragma unroll
+            for (int q = 0; q < 2; ++q)
+#pragma unroll
+              for (int tt = 0; tt < kNT; ++tt)
+                if (q == jj && tt == t) { up = acc[2 * q][tt]; gate = acc[2 * q + 1][tt]; }
+            if (limit > 0.0f) {
+              up = fminf(fmaxf(up, -limit), limit);
+              gate = fminf(gate, limit);
+            }
+            h_out[static_cast<int64_t>(p0 + c + t) * I + j0 + jj] = wm_f32_to_bf16(silu_f32(gate) * up);
+          }
+        }
+      } else {
+        if (lane < kRowsPerWarp * kNT) {
+          const int r = lane / kNT, t = lane % kNT;
+          if (t < nt) {
+            float v = 0.f;
+#pragma unroll
+            for (int rr = 0; rr < kRowsPerWarp; ++rr)
+#pragma unroll
+              for (int tt = 0; tt < kNT; ++tt)
+                if (rr == r && tt == t) v = acc[rr][tt];
+            y_out[static_cast<int64_t>(p0 + c + t) * W.rows + row[r]] = v;
+          }
+        }
+      }
+    }
+  }
+}
+
+// out[t, :] = sum_j w[t,j] * y[inv[t*kk+j], :] (+ shared_w[t] * y[inv[t*kk+k], :]), fixed order
+// A set error flag (expert id out of range) yields zeros; slots are bounds-checked.
+__global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict__ inv, const float *__restrict__ w,
+                          const float *__restrict__ shared_w, const int32_t *__restrict__ err, int T, int k, int kk,
+                          int H, uint16_t *__restrict__ out) {
+  const int per_row = H / 8;
+  const int S = T * kk;
+  const bool bad = *err != 0;
+  const int64_t total = static_cast<int64_t>(T) * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = static_cast<int>(i / per_row), c8 = static_cast<int>(i % per_row) * 8;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < kk && !bad; ++j) {
+      const float wt = j < k ? w[static_cast<int64_t>(t) * k + j] : (shared_w ? shared_w[t] : 1.0f);
+      const int slot = inv[static_cast<int64_t>(t) * kk + j];
+      if (slot < 0 || slot >= S) continue;
+      const float4 *yp = reinterpret_cast<const float4 *>(y + static_cast<int64_t>(slot) * H + c8);
+      float4 a = yp[0], b = yp[1];
+      acc[0] = fmaf(wt, a.x, acc[0]); acc[1] = fmaf(wt, a.y, acc[1]);
+      acc[2] = fmaf(wt, a.z, acc[2]); acc[3] = fmaf(wt, a.w, acc[3]);
+      acc[4] = fmaf(wt, b.x, acc[4]); acc[5] = fmaf(wt, b.y, acc[5]);
+      acc[6] = fmaf(wt, b.z, acc[6]); acc[7] = fmaf(wt, b.w, acc[7]);
+    }
+    uint4 o;
+    o.x = wm_f32_to_bf16(acc[0]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16);
+    o.y = wm_f32_to_bf16(acc[2]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16);
+    o.z = wm_f32_to_bf16(acc[4]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[5])) << 16);
+    o.w = wm_f32_to_bf16(acc[6]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[7])) << 16);
+    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(t) * H + c8) = o;
+  }
+}
+
+// out[t, j, :] = bf16(y[inv[t*k+j], :])  (un-reduced switch_mlp output)
+__global__ void k_unsort(const float *__restrict__ y, const int32_t *__restrict__ inv, const int32_t *__restrict__ err,
+                         int S, int H, uint16_t *__restrict__ out) {
+  const int per_row = H / 8;
+  const bool bad = *err != 0;
+  const int64_t total = static_cast<int64_t>(S) * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int a = static_cast<int>(i / per_row), c8 = static_cast<int>(i % per_row) * 8;
+    const int slot = inv[a];
+    float4 p = make_float4(0.f, 0.f, 0.f, 0.f), q = p;
+    if (!bad && slot >= 0 && slot < S) {
+      const float4 *yp = reinterpret_cast<const float4 *>(y + static_cast<int64_t>(slot) * H + c8);
+      p = yp[0];
+      q = yp[1];
+    }
+    uint4 o;
+    o.x = wm_f32_to_bf16(p.x) | (static_cast<uint32_t>(wm_f32_to_bf16(p.y)) << 16);
+    o.y = wm_f32_to_bf16(p.z) | (static_cast<uint32_t>(wm_f32_to_bf16(p.w)) << 16);
+    o.z = wm_f32_to_bf16(q.x) | (static_cast<uint32_t>(wm_f32_to_bf16(q.y)) << 16);
+    o.w = wm_f32_to_bf16(q.z) | (static_cast<uint32_t>(wm_f32_to_bf16(q.w)) << 16);
+    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(a) * H + c8) = o;
+  }
+}
+
+struct Args {
+  const uint16_t *x;
+  const int32_t *idx;
+  const float *weights;
+  int T, k, H, I, E;
+  Weights w13, w2;
+  int order;
+  float limit;
+  int shared_expert;
+  const float *shared_w;
+  uint16_t *out;
+  bool reduce;
+  void *ws;
+  size_t ws_bytes;
+  cudaStream_t stream;
+};
+
+int check_common(const Args &a) {
+  WM_REQUIRE(a.T >= 0 && a.k >= 1 && a.E >= 1 && a.E <= 4096, "experts: need T >= 0, k >= 1, 1 <= E <= 4096");
+  WM_REQUIRE(a.H > 0 && a.H % 32 == 0 && a.I > 0 && a.I % 32 == 0, "experts: H and I must be multiples of 32");
+  WM_REQUIRE(a.I % 16 == 0 && a.H % 32 == 0, "experts: I % 16 == 0 and H % 32 == 0 required");
+  WM_REQUIRE(a.order == WM_UP_GATE || a.order == WM_GATE_UP, "experts: gate_up_order must be WM_UP_GATE or WM_GATE_UP");
+  WM_REQUIRE(a.shared_expert < a.E, "experts: shared_expert must be < E");
+  WM_REQUIRE(a.x && a.idx && a.out && a.w13.w && a.w2.w, "experts: null buffer");
+  WM_REQUIRE(!a.reduce || a.weights, "moe_forward: null weights");
+  WM_REQUIRE(wm::aligned(a.x, 16) && wm::aligned(a.out, 16) && wm::aligned(a.w13.w, 16) && wm::aligned(a.w2.w, 16),
+             "experts: x, out and packed weights must be 16-byte aligned");
+  WM_REQUIRE(wm::aligned(a.ws, 256), "experts: workspace must be 256-byte aligned");
+  return WM_OK;
+}
+
+int run(const Args &a, int fmt) {
+  if (a.T == 0) return WM_OK;
+  if (int rc = check_common(a)) return rc;
+  const int has_shared = a.shared_expert >= 0 ? 1 : 0;
+  wm::MoeWorkspace ws = wm::carve_workspace(a.ws, a.T, a.k, a.H, a.I, a.E, has_shared);
+  if (a.ws_bytes < ws.bytes) return wm::fail(WM_ERR_WORKSPACE, "experts: workspace too small");
+  if (a.T == 0) return WM_OK;
+  const int kk = a.k + has_shared;
+  const int S = a.T * kk;
+  if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
+                                  ws.counters, ws.counters + 1, a.stream))
+    return rc;
+  const int grid = wm::sm_count() * 2;
+  if (fmt == kFmtMxfp4) {
+    k_expert_gemv<kFmtMxfp4, kModeUp><<<grid, kWarps * 32, 0, a.stream>>>(a.x, kk, ws.offsets, ws.perm, ws.active,
+                                                                          ws.counters, a.w13, a.I, a.order, a.limit,
+                                                                          ws.h, nullptr);
+    k_expert_gemv<kFmtMxfp4, kModeDown><<<grid, kWarps * 32, 0, a.stream>>>(ws.h, kk, ws.offsets, ws.perm, ws.active,
+                                                                            ws.counters, a.w2, a.I, a.order, a.limit,
+                                                                            nullptr, ws.y);
+  } else {
+    k_expert_gemv<kFmtAffine4, kModeUp><<<grid, kWarps * 32, 0, a.stream>>>(a.x, kk, ws.offsets, ws.perm, ws.active,
+                                                                            ws.counters, a.w13, a.I, a.order, a.limit,
+                                                                            ws.h, nullptr);
+    k_expert_gemv<kFmtAffine4, kModeDown><<<grid, kWarps * 32, 0, a.stream>>>(ws.h, kk, ws.offsets, ws.perm, ws.active,
+                                                                              ws.counters, a.w2, a.I, a.order,
+                                                                              a.limit, nullptr, ws.y);
+  }
+  if (int rc = wm::check_launch("expert gemv")) return rc;
+  const int cgrid = wm::sm_count() * 8;
+  if (a.reduce)
+    k_combine<<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk, a.H,
+                                           a.out);
+  else
+    k_unsort<<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, ws.counters + 1, S, a.H, a.out);
+  return wm::check_launch("expert combine");
+}
+
+Weights mx_view(const uint8_t *w, const uint8_t *s, int rows, int K) {
+  Weights v{};
+  v.w = w; v.s = s; v.rows = rows; v.K = K; v.group = 32;
+  return v;
+}
+
+Weights af_view(const uint32_t *w, const uint16_t *sc, const uint16_t *bi, int group, int rows, int K) {
+  Weights v{};
+  v.w = reinterpret_cast<const uint8_t *>(w); v.sc = sc; v.bi = bi; v.group = group; v.rows = rows; v.K = K;
+  return v;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t wmoe_workspace_size(int T, int k, int H, int I, int E, int has_shared) {
+  if (T < 0 || k < 1 || H <= 0 || I <= 0 || E < 1) return 0;
+  return wm::carve_workspace(nullptr, T, k, H, I, E, has_shared).bytes;
+}
+
+int wmoe_mxfp4_experts(const wm_bf16 *x, const int32_t *idx, int T, int k, int H, int I, int E, const uint8_t *w13,
+                       const uint8_t *s13, const uint8_t *w2, const uint8_t *s2, int gate_up_order, float swiglu_limit,
+                       wm_bf16 *out, void *workspace, size_t ws_bytes, wm_stream_t stream) {
+  wm::clear_error();
+  Args a{x, idx, nullptr, T, k, H, I, E, mx_view(w13, s13, 2 * I, H), mx_view(w2, s2, H, I), gate_up_order,
+         swiglu_limit, -1, nullptr, out, false, workspace, ws_bytes, stream};
+  return run(a, kFmtMxfp4);
+}
+
+int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const float *weights, int T, int k, int H, int I,
+                           int E, const uint8_t *w13, const uint8_t *s13, const uint8_t *w2, const uint8_t *s2,
+                           int gate_up_order, float swiglu_limit, int shared_expert, const float *shared_w,
+                           wm_bf16 *out, void *workspace, size_t ws_bytes, wm_stream_t stream) {
+  wm::clear_error();
+  Args a{x, idx, weights, T, k, H, I, E, mx_view(w13, s13, 2 * I, H), mx_view(w2, s2, H, I), gate_up_order,
+         swiglu_limit, shared_expert, shared_w, out, true, workspace, ws_bytes, stream};
+  return run(a, kFmtMxfp4);
+}
+
+int wmoe_affine4_experts(const wm_bf16 *x, const int32_t *idx, int T, int k, int H, int I, int E, const uint32_t *w13,
+                         const wm_bf16 *sc13, const wm_bf16 *bi13, const uint32_t *w2, const wm_bf16 *sc2,
+                         const wm_bf16 *bi2, int group, int gate_up_order, float swiglu_limit, wm_bf16 *out,
+                         void *workspace, size_t ws_bytes, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(group == 32 || group == 64 || group == 128, "affine4 group must be 32, 64 or 128");
+  WM_REQUIRE(H % group == 0 && I % group == 0, "affine4: H and I must be multiples of the group");
+  Args a{x, idx, nullptr, T, k, H, I, E, af_view(w13, sc13, bi13, group, 2 * I, H), af_view(w2, sc2, bi2, group, H, I),
+         gate_up_order, swiglu_limit, -1, nullptr, out, false, workspace, ws_bytes, stream};
+  return run(a, kFmtAffine4);
+}
+
+int wmoe_affine4_moe_forward(const wm_bf16 *x, const int32_t *idx, const float *weights, int T, int k, int H, int I,
+                             int E, const uint32_t *w13, const wm_bf16 *sc13, const wm_bf16 *bi13, const uint32_t *w2,
+                             const wm_bf16 *sc2, const wm_bf16 *bi2, int group, int gate_up_order, float swiglu_limit,
+                             int shared_expert, const float *shared_w, wm_bf16 *out, void *workspace, size_t ws_bytes,
+                             wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(group == 32 || group == 64 || group == 128, "affine4 group must be 32, 64 or 128");
+  WM_REQUIRE(H % group == 0 && I % group == 0, "affine4: H and I must be multiples of the group");
+  Args a{x, idx, weights, T, k, H, I, E, af_view(w13, sc13, bi13, group, 2 * I, H),
+         af_view(w2, sc2, bi2, group, H, I), gate_up_order, swiglu_limit, shared_expert, shared_w, out, true,
+         workspace, ws_bytes, stream};
+  return run(a, kFmtAffine4);
+}
+
+}  // extern "C"

@@ -1,0 +1,147 @@
+// Permute: stable sort of (token, slot) assignments by expert.
+//
+// Reference: mlx-lm switch_layers._gather_sort / _scatter_unsort, called at
+// model.py:404/455 and qwen4_exp.py:622/649; the per-expert grouping by a
+// stable argsort in _forward_with_resident (model.py:371-385).
+//
+// One CTA.  The S assignments are cut into W contiguous segments, one per
+// warp.  Pass 1 builds a per-warp histogram in shared memory; a scan over
+// (expert, warp) gives every warp its starting cursor for every expert; pass
+// 2 walks each segment in order 32 assignments at a time, ranking equal
+// experts inside the 32 with __match_any_sync.  The result is the stable
+// order (ties by flat assignment index), independent of scheduling.
+//
+// Besides offsets/perm/inv the kernel emits the compact list of active
+// experts (count > 0) that the expert kernels iterate over.
+#include "wm_common.cuh"
+#include "wm_moe.cuh"
+
+namespace {
+
+__global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ idx, int T, int k, int shared_expert,
+                                                  int E, int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
+                                                  int32_t *__restrict__ inv, int32_t *__restrict__ active,
+                                                  int32_t *__restrict__ n_active, int32_t *__restrict__ error_flag) {
+  extern __shared__ int32_t sm[];
+  const int nw = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kk = k + (shared_expert >= 0 ? 1 : 0);
+  const int S = T * kk;
+  int32_t *hist = sm;                 // [nw][E]
+  int32_t *tot = sm + nw * E;         // [E+1]
+  __shared__ int32_t bad;
+  if (threadIdx.x == 0) bad = 0;
+  for (int i = threadIdx.x; i < nw * E; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int seg = (S + nw - 1) / nw;
+  const int s0 = warp * seg, s1 = min(S, s0 + seg);
+  auto expert_of = [&](int a) -> int {
+    int t = a / kk, j = a - t * kk;
+    int e = j < k ? idx[static_cast<int64_t>(t) * k + j] : shared_expert;
+    return e;
+  };
+  for (int a = s0 + lane; a < s1; a += 32) {
+    int e = expert_of(a);
+    if (e < 0 || e >= E) {
+      bad = 1;
+      continue;
+    }
+    atomicAdd(&hist[warp * E + e], 1);
+  }
+  __syncthreads();
+  if (bad) {
+    if (threadIdx.x == 0) {
+      if (error_flag) *error_flag = 1;
+      if (n_active) *n_active = 0;
+      for (int e = 0; e < E; ++e) offsets[e] = 0;
+      offsets[E] = -1;  // sentinel: an expert id was outside [0, E)
+    }
+    return;
+  }
+  // totals per expert, then exclusive scan (E <= 4096: a serial scan per thread chunk)
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int c = 0;
+    for (int w = 0; w < nw; ++w) c += hist[w * E + e];
+    tot[e] = c;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0, na = 0;
+    for (int e = 0; e < E; ++e) {
+      int c = tot[e];
+      offsets[e] = run;
+      tot[e] = run;
+      if (c > 0 && active) active[na] = e;
+      na += c > 0 ? 1 : 0;
+      run += c;
+    }
+    offsets[E] = run;
+    tot[E] = run;
+    if (n_active) *n_active = na;
+    if (error_flag) *error_flag = 0;
+  }
+  __syncthreads();
+  // per-warp cursors: base of expert e for warp w = tot[e] + sum_{w'<w} hist[w'][e]
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = tot[e];
+    for (int w = 0; w < nw; ++w) {
+      int c = hist[w * E + e];
+      hist[w * E + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int a0 = s0; a0 < s1; a0 += 32) {
+    int a = a0 + lane;
+    bool valid = a < s1;
+    int e = valid ? expert_of(a) : -1;
+    unsigned peers = __match_any_sync(0xffffffffu, e);
+    int rank = __popc(peers & lt_mask);
+    int base = valid ? hist[warp * E + e] : 0;
+    __syncwarp();
+    if (valid) {
+      int slot = base + rank;
+      perm[slot] = a;
+      inv[a] = slot;
+      // the highest lane of each peer group advances the cursor
+      if ((peers >> lane) == 1u) hist[warp * E + e] = base + __popc(peers);
+    }
+    __syncwarp();
+  }
+}
+
+}  // namespace
+
+namespace wm {
+
+size_t permute_smem_bytes(int E, int nw) { return (static_cast<size_t>(nw) * E + E + 1) * sizeof(int32_t); }
+
+int permute_warps(int E) {
+  int nw = 32;
+  while (nw > 1 && permute_smem_bytes(E, nw) > 200 * 1024) nw >>= 1;
+  return nw;
+}
+
+int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
+                   int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, cudaStream_t stream) {
+  const int nw = permute_warps(E);
+  const size_t smem = permute_smem_bytes(E, nw);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("permute smem: ") + cudaGetErrorString(e));
+  }
+  k_permute<<<1, nw * 32, smem, stream>>>(idx, T, k, shared_expert, E, offsets, perm, inv, active, n_active, error_flag);
+  return check_launch("permute");
+}
+
+}  // namespace wm
+
+extern "C" int wmoe_permute(const int32_t *idx, int T, int k, int E, int32_t *offsets, int32_t *perm, int32_t *inv,
+                            wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(T >= 0 && k >= 1 && E >= 1 && E <= 4096, "permute needs T >= 0, k >= 1, 1 <= E <= 4096");
+  WM_REQUIRE(static_cast<int64_t>(T) * k < (1LL << 30), "permute: too many assignments");
+  WM_REQUIRE(idx && offsets && perm && inv, "permute: null buffer");
+  return wm::launch_permute(idx, T, k, -1, E, offsets, perm, inv, nullptr, nullptr, nullptr, stream);
+}

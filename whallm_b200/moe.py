@@ -1,0 +1,95 @@
+"""MoE layers: router + routed experts + top-k combine (+ shared expert).
+
+Drop-in mirrors of the reference's MoE call sites:
+  * ``streaming_moe(moe, x, input_ids)`` -- ``_streaming_moe`` (model.py:484-499):
+    ``gate -> shared -> switch_mlp -> _route_reduce + shared``.
+  * ``route_reduce`` -- ``_route_reduce`` (model.py:502-504).
+  * ``MoE`` -- DeepSeek-V4.1 ``MoE.__call__`` (deepseek_v41/moe.py:96-112),
+    with the shared expert stored as one more MXFP4 expert (index E) so the
+    whole layer is two native calls (router, fused experts + combine).
+  * ``SparseMoE`` -- Qwen ``SparseMoE.__call__`` (qwen4_exp.py:680-704),
+    shared expert gated by ``sigmoid(x . w_sg)``.
+  * ``TinyMoE`` -- the affine-4 tiny configuration (softmax top-k, no shared).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import experts as X
+from .router import Gate, qwen_route
+
+
+def route_reduce(routed: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
+    """_route_reduce (model.py:502-504): sum_k routed * scores, in float32, bf16 result."""
+    return (routed.float() * scores[..., None].float()).sum(-2).to(routed.dtype)
+
+
+def streaming_moe(moe, x: torch.Tensor, input_ids=None) -> torch.Tensor:
+    """_streaming_moe (model.py:484-499) for an object with ``gate``,
+    ``shared_experts`` and ``switch_mlp`` attributes.  ``gate(x[, input_ids])``
+    returns ``(indices, scores)`` like mlx-lm's MoEGate."""
+    if getattr(moe, "sharding_group", None) is not None:
+        raise ValueError("use whallm_b200.ep for expert-parallel layers")
+    try:
+        indices, scores = moe.gate(x, input_ids)
+    except TypeError:
+        indices, scores = moe.gate(x)
+    shared = moe.shared_experts(x)
+    routed = moe.switch_mlp(x, indices)
+    return route_reduce(routed, scores) + shared
+
+
+class MoE:
+    """DeepSeek-class routed layer: V4.1 Gate semantics, ClampedSwiGLU(limit),
+    MXFP4 experts [E+1, ...] whose last expert is the always-on shared expert."""
+
+    def __init__(self, gate: Gate, experts: X.BatchedExperts, swiglu_limit: float = 0.0, has_shared: bool = True):
+        self.gate = gate
+        self.experts = experts
+        self.limit = float(swiglu_limit)
+        self.n_routed = gate.weight.shape[0]
+        self.has_shared = has_shared
+        if X._expert_count(experts) != self.n_routed + (1 if has_shared else 0):
+            raise ValueError("expert count must be routed experts (+1 shared)")
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        weights, indices = self.gate(x)
+        return X.experts_forward(x, indices, self.experts, swiglu_limit=self.limit, weights=weights,
+                                 shared_expert=self.n_routed if self.has_shared else -1)
+
+
+class SparseMoE:
+    """Qwen-class routed layer (qwen4_exp.py:680-704): softmax top-k,
+    renormalised, MXFP4 gate_up/down experts [E+1, ...] with the shared
+    expert last, scaled by sigmoid(x . shared_expert_gate)."""
+
+    def __init__(self, gate_weight: torch.Tensor, shared_expert_gate: torch.Tensor | None,
+                 experts: X.QwenBatchedExperts, top_k: int, norm_topk_prob: bool = True,
+                 logit_bias: torch.Tensor | None = None):
+        self.gate_weight = gate_weight
+        self.shared_expert_gate = shared_expert_gate
+        self.experts = experts
+        self.top_k = top_k
+        self.norm_topk_prob = norm_topk_prob
+        self.logit_bias = logit_bias
+        self.n_routed = gate_weight.shape[0]
+
+    def __call__(self, value: torch.Tensor) -> torch.Tensor:
+        scores, indices, shared_w = qwen_route(value, self.gate_weight, self.top_k, self.norm_topk_prob,
+                                               shared_gate=self.shared_expert_gate, logit_bias=self.logit_bias)
+        has_shared = X._expert_count(self.experts) > self.n_routed
+        return X.experts_forward(value, indices, self.experts, weights=scores,
+                                 shared_expert=self.n_routed if has_shared else -1, shared_w=shared_w)
+
+
+class TinyMoE:
+    """The tiny affine-4 configuration: softmax over E, top-k, renormalised, no shared expert."""
+
+    def __init__(self, gate_weight: torch.Tensor, experts: X.Affine4BatchedExperts, top_k: int):
+        self.gate_weight = gate_weight
+        self.experts = experts
+        self.top_k = top_k
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        scores, indices, _ = qwen_route(x, self.gate_weight, self.top_k, True)
+        return X.experts_forward(x, indices, self.experts, weights=scores)
