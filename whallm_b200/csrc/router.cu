@@ -10,8 +10,9 @@
 //   denominator uses the same butterfly over lane partials of experts
 //   l, l+32, l+64, ...  Compiled with -fmad=false.
 //
-// Kernel 1 (logits): one warp per (expert row, chunk of up to 8 tokens); the
-//   expert row is read once per chunk with 16-byte loads.
+// Kernel 1 (logits): one warp per (expert row, chunk of up to 8 tokens), two
+//   warps per CTA so the rows spread over all SMs; the expert row is read once
+//   per chunk with 16-byte loads, four in flight per lane.
 // Kernel 2 (top-k): one warp per token; scores live in registers
 //   (E <= 1024 -> 32 per lane); k rounds of a warp arg-max with ties to the
 //   lower expert id.
@@ -24,7 +25,7 @@ constexpr int kTokChunk = 8;
 constexpr int kMaxE = 1024;
 constexpr int kMaxK = 32;
 
-__global__ void __launch_bounds__(256) k_router_logits(const uint16_t *__restrict__ x, const uint16_t *__restrict__ wg,
+__global__ void __launch_bounds__(64) k_router_logits(const uint16_t *__restrict__ x, const uint16_t *__restrict__ wg,
                                                        const uint16_t *__restrict__ wg_shared,
                                                        const float *__restrict__ logit_bias, int T, int H, int E,
                                                        float *__restrict__ logits, float *__restrict__ shared_raw) {
@@ -40,6 +41,7 @@ __global__ void __launch_bounds__(256) k_router_logits(const uint16_t *__restric
   float acc[kTokChunk];
 #pragma unroll
   for (int t = 0; t < kTokChunk; ++t) acc[t] = 0.0f;
+#pragma unroll 4
   for (int base = 8 * lane; base < H; base += 256) {
     uint4 wu = __ldg(reinterpret_cast<const uint4 *>(w + base));
     float wv[8] = {wm_bf16lo(wu.x), wm_bf16hi(wu.x), wm_bf16lo(wu.y), wm_bf16hi(wu.y),
@@ -195,9 +197,9 @@ extern "C" int wmoe_router_topk(const wm_bf16 *x, const wm_bf16 *wg, const float
              "router inputs must be 16-byte aligned");
   const int rows = E + (wg_shared ? 1 : 0);
   const int64_t warps = static_cast<int64_t>(rows) * ((T + kTokChunk - 1) / kTokChunk);
+  k_router_logits<<<static_cast<int>((warps * 32 + 63) / 64), 64, 0, stream>>>(x, wg, wg_shared, logit_bias, T, H, E,
+                                                                             logits, shared_w);
   const int threads = 256;
-  k_router_logits<<<static_cast<int>((warps * 32 + threads - 1) / threads), threads, 0, stream>>>(
-      x, wg, wg_shared, logit_bias, T, H, E, logits, shared_w);
   if (int rc = wm::check_launch("wmoe_router_topk(logits)")) return rc;
   k_router_topk<<<(T * 32 + threads - 1) / threads, threads, 0, stream>>>(logits, select_bias, T, E, k, score_fn,
                                                                             norm_eps, route_scale, idx, weights,
