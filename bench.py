@@ -182,10 +182,12 @@ def run_ours(args, rank, world, dev):
             torch.distributed.barrier()
         torch.cuda.synchronize()
         s, e = _events(torch)
+        torch.cuda.nvtx.range_push("timed")
         s.record()
         for i in range(args.steps):
             step(i)
         e.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         ms = s.elapsed_time(e) / args.steps
         # expert-call roofline: time the expert calls alone, same stream

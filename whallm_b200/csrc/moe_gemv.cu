@@ -22,6 +22,8 @@
 //     fused ClampedSwiGLU runs in the epilogue and writes h (bf16) directly.
 //   * Phase "down": rows of w2 over h; outputs y (f32) in sorted-slot order.
 //   * Combine: per token, sum_j w_j * y_j (+ shared) in float32, fixed order.
+#include <cstdlib>
+
 #include "wm_common.cuh"
 #include "wm_moe.cuh"
 
@@ -274,6 +276,12 @@ int check_common(const Args &a) {
   return WM_OK;
 }
 
+// WM_EXPERT_PATH=simt forces the CUDA-core GEMV for MXFP4 experts (A/B checks).
+bool force_simt() {
+  const char *v = getenv("WM_EXPERT_PATH");
+  return v && v[0] == 's';
+}
+
 int run(const Args &a, int fmt) {
   if (a.T == 0) return WM_OK;
   if (int rc = check_common(a)) return rc;
@@ -283,11 +291,23 @@ int run(const Args &a, int fmt) {
   if (a.T == 0) return WM_OK;
   const int kk = a.k + has_shared;
   const int S = a.T * kk;
+  const bool tc = fmt == kFmtMxfp4 && wm::tc_supported(a.H, a.I) && !force_simt();
   if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
-                                  ws.counters, ws.counters + 1, a.stream))
+                                  ws.counters, ws.counters + 1, tc ? ws.tiles : nullptr, ws.counters + 2,
+                                  wm::kTcTileN, a.stream))
     return rc;
   const int grid = wm::sm_count() * 2;
-  if (fmt == kFmtMxfp4) {
+  if (tc) {
+    if (cudaMemsetAsync(ws.counters + 3, 0, sizeof(int32_t), a.stream) != cudaSuccess)
+      return wm::fail(WM_ERR_CUDA, "experts: memset failed");
+    if (int rc = wm::launch_gather_f16(a.x, ws.perm, S, kk, a.H, ws.x16, a.stream)) return rc;
+    if (int rc = wm::launch_tc_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x16, ws.s_pad, a.order, a.limit, ws.tiles,
+                                  ws.counters + 2, ws.h, ws.counters + 3, a.stream))
+      return rc;
+    if (int rc = wm::launch_tc_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h, ws.s_pad, ws.tiles, ws.counters + 2, ws.y,
+                                    ws.counters + 3, a.stream))
+      return rc;
+  } else if (fmt == kFmtMxfp4) {
     k_expert_gemv<kFmtMxfp4, kModeUp><<<grid, kWarps * 32, 0, a.stream>>>(a.x, kk, ws.offsets, ws.perm, ws.active,
                                                                           ws.counters, a.w13, a.I, a.order, a.limit,
                                                                           ws.h, nullptr);

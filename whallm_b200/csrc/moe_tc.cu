@@ -1,0 +1,530 @@
+// Grouped MXFP4 expert GEMM on the 5th-generation tensor cores (tcgen05).
+//
+// Reference: the MLX gather_qmm / quantized_matmul expert math
+// (model.py:393-481, qwen4_exp.py:588-678): y = x @ dequant(W)^T per routed
+// (token, expert) pair, W in MXFP4 (e2m1 + E8M0 per 32 along K).
+//
+// Orientation ("swap AB"): the MMA's M dimension is 128 weight rows, N is the
+// tokens routed to the expert (16..128 per tile), K is the reduction.  Decode
+// routes a handful of tokens to each expert, so N stays small while M spans
+// the weight matrix; prefill tiles the tokens in N = 128 chunks.
+//
+//   A (weights)  TMEM, f16.  TMA brings packed e2m1 tiles (128 rows x 64 K =
+//                4 KB) into shared memory; a dequant warpgroup converts each
+//                row with cvt.rn.f16x2.e2m1x2 and one f16x2 multiply by the
+//                block scale 2^(s-127) * 2^12, then tcgen05.st writes the
+//                32 columns (64 f16) of its TMEM lane.  A never round-trips
+//                through shared memory as f16, which keeps shared-memory
+//                traffic near 1 byte per weight element at decode rates.
+//   B (tokens)   shared memory, f16, K-major, 128-byte swizzle, loaded by TMA
+//                in 16-row boxes from a token matrix already in expert order.
+//   D            TMEM, f32, 128 lanes x N columns, double buffered.
+//
+// Scaling: A holds w * 2^12 (exact in f16 for |w| <= 12, block scales down to
+// 2^-25 kept exactly), B holds x * 2^-4, so D = 2^8 * (x . w); the epilogue
+// multiplies by 2^-8.
+//
+// Warp roles (384 threads, one CTA per SM, persistent over work items):
+//   warp 0      TMA producer              warp 1   MMA issuer (one thread)
+//   warp 2      TMEM allocator            warp 3   idle
+//   warps 4-7   dequant (TMEM lanes 0-127)
+//   warps 8-11  epilogue (TMEM lanes 0-127): fused ClampedSwiGLU for the
+//               up projection (lanes 2j / 2j+1 hold up_j / gate_j), f32 rows
+//               of y for the down projection.
+// Every mbarrier wait gives up after 2 s, records an error code and skips the
+// remaining work, so a broken invariant cannot hang the GPU.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "wm_common.cuh"
+#include "wm_moe.cuh"
+
+namespace {
+
+constexpr int kM = 128;
+constexpr int kKC = 64;                       // K per pipeline chunk
+constexpr int kStages = 6;
+constexpr int kASlots = 8;
+constexpr int kACols = 32;                    // TMEM columns per A slot (64 f16)
+constexpr int kDCol0 = 0;                     // D buffers: columns [0, 256)
+constexpr int kACol0 = 256;                   // A ring:    columns [256, 512)
+constexpr int kTmemCols = 512;
+constexpr int kBStageBytes = wm::kTcTileN * kKC * 2;  // 16 KB
+constexpr int kAStageBytes = kM * kKC / 2;            // 4 KB
+constexpr int kThreads = 384;
+constexpr unsigned long long kWaitNs = 2000000000ull;
+
+struct TcParams {
+  int mode;              // 0: up projection (+SwiGLU -> h), 1: down projection (-> y)
+  int K;                 // reduction length
+  int rows;              // weight rows per expert
+  int I;                 // intermediate size (up: row mapping; down: unused)
+  int H;                 // output row stride for y (down)
+  int order;             // WM_UP_GATE / WM_GATE_UP
+  float limit;           // ClampedSwiGLU limit (0: none)
+  int m_tiles;           // 128-row tiles per expert
+  const uint8_t *scales; // [E*rows, K/32]
+  const int4 *tiles;     // {expert, first slot, tokens, 0}
+  const int32_t *n_tiles;
+  __half *h_out;         // up: [S, I] f16, h * 2^-4
+  float *y_out;          // down: [S, H] f32
+  int32_t *err;
+};
+
+// ------------------------------------------------------------- PTX helpers
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: false (and an error code in *err) after kWaitNs.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  while (true) {
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(bar, parity)) return true;
+    if (gtimer() - t0 > kWaitNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem desc]; kind::f16, f32 accumulate
+__device__ __forceinline__ void tc_mma_ts(uint32_t d, uint32_t a, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d), "r"(a), "l"(bdesc), "r"(idesc), "r"(acc)
+      : "memory");
+}
+
+// K-major, 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B apart.
+__device__ __forceinline__ uint64_t bdesc_sw128(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (static_cast<uint64_t>(1024 >> 4) << 32) |
+         (1ull << 46) | (2ull << 61);
+}
+
+// kind::f16 instruction descriptor: f16 x f16 -> f32, K-major A and B, M = 128.
+__device__ __forceinline__ uint32_t idesc_f16(int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (static_cast<uint32_t>(kM >> 4) << 24);
+}
+
+#define WM_TMEM_ST32(taddr, r)                                                                                        \
+  asm volatile(                                                                                                       \
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "   \
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),       \
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), \
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),   \
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),   \
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])                                                                 \
+      : "memory")
+
+#define WM_TMEM_LD16(taddr, r)                                                                                       \
+  asm volatile(                                                                                                      \
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "   \
+      "%15}, [%16];"                                                                                                 \
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),            \
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])       \
+      : "r"(taddr)                                                                                                   \
+      : "memory")
+
+// Block scale 2^(s-127) * 2^12 as f16x2 (both halves); s > 128 overflows f16 -> error.
+__device__ __forceinline__ uint32_t scale_f16x2(uint32_t s, bool &bad) {
+  uint32_t h;
+  if (s > 128u) {
+    bad = true;
+    h = 0x7800u;  // 2^15: result is garbage, the error flag reports it
+  } else if (s >= 101u) {
+    h = (s - 100u) << 10;
+  } else if (s >= 91u) {
+    h = 1u << (s - 91u);
+  } else {
+    h = 0u;
+  }
+  return h | (h << 16);
+}
+
+// 16 packed bytes (32 e2m1 values) -> 16 f16x2 words scaled by `sf`
+__device__ __forceinline__ void dequant16(uint4 v, uint32_t sf, uint32_t *out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t r0, r1, r2, r3;
+    asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+        "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+        "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+        : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+        : "r"(w[i]));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(r0) : "r"(sf));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(r1) : "r"(sf));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(r2) : "r"(sf));
+    asm("mul.rn.f16x2 %0, %0, %1;" : "+r"(r3) : "r"(sf));
+    out[4 * i + 0] = r0;
+    out[4 * i + 1] = r1;
+    out[4 * i + 2] = r2;
+    out[4 * i + 3] = r3;
+  }
+}
+
+__device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_expert_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sB = smem;                                   // kStages x 16 KB
+  uint8_t *sA = smem + kStages * kBStageBytes;          // kStages x 4 KB
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sA + kStages * kAStageBytes);
+  uint64_t *full = bars;                                // [kStages]
+  uint64_t *empty = full + kStages;                     // [kStages]
+  uint64_t *afull = empty + kStages;                    // [kASlots]
+  uint64_t *aempty = afull + kASlots;                   // [kASlots]
+  uint64_t *dfull = aempty + kASlots;                   // [2]
+  uint64_t *dempty = dfull + 2;                         // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dempty + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < kASlots; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128); }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int n_items = (*p.n_tiles) * p.m_tiles;
+  const int kchunks = p.K / kKC;
+  const int ub = p.order == WM_UP_GATE ? 0 : p.I;
+  const int gb = p.order == WM_UP_GATE ? p.I : 0;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      uint32_t g = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const int4 tile = p.tiles[item / p.m_tiles];
+        const int m = item % p.m_tiles;
+        const int nb = (tile.z + 15) >> 4;
+        int r_lo, r_hi;
+        if (p.mode == 0) { r_lo = ub + m * 64; r_hi = gb + m * 64; }
+        else { r_lo = m * kM; r_hi = m * kM + 64; }
+        const int ebase = tile.x * p.rows;
+        for (int kc = 0; kc < kchunks; ++kc, ++g) {
+          const int s = g % kStages;
+          const uint32_t u = g / kStages;
+          if (!(ok = mbar_wait(&empty[s], (u & 1) ^ 1, p.err, 1))) break;
+          mbar_expect_tx(&full[s], kAStageBytes + nb * 16 * kKC * 2);
+          tma_load_2d(sA + s * kAStageBytes, &tmA, kc * (kKC / 2), ebase + r_lo, &full[s]);
+          tma_load_2d(sA + s * kAStageBytes + 64 * (kKC / 2), &tmA, kc * (kKC / 2), ebase + r_hi, &full[s]);
+          for (int j = 0; j < nb; ++j)
+            tma_load_2d(sB + s * kBStageBytes + j * 16 * 128, &tmB, kc * kKC, tile.y + 16 * j, &full[s]);
+        }
+      }
+      // drain: every issued stage has been consumed (its empty barrier completed)
+      for (uint32_t q = 0; q < kStages && q < g && ok; ++q) {
+        const uint32_t gg = g - 1 - q;
+        ok = mbar_wait(&empty[gg % kStages], (gg / kStages) & 1, p.err, 2);
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA
+    if (lane == 0) {
+      uint32_t g = 0, it = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+        const int4 tile = p.tiles[item / p.m_tiles];
+        const int n_mma = max(16, (tile.z + 15) & ~15);
+        const uint32_t idesc = idesc_f16(n_mma);
+        const int db = it & 1;
+        if (!(ok = mbar_wait(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
+        tc_fence_after();
+        const uint32_t d_addr = tmem + kDCol0 + db * wm::kTcTileN;
+        for (int kc = 0; kc < kchunks; ++kc, ++g) {
+          const int s = g % kStages;
+          const int slot = g % kASlots;
+          if (!(ok = mbar_wait(&full[s], (g / kStages) & 1, p.err, 4))) break;
+          if (!(ok = mbar_wait(&afull[slot], (g / kASlots) & 1, p.err, 5))) break;
+          tc_fence_after();
+          const uint64_t b0 = bdesc_sw128(smem_u32(sB + s * kBStageBytes));
+#pragma unroll
+          for (int kk = 0; kk < kKC / 16; ++kk) {
+            const uint32_t a_addr = tmem + kACol0 + slot * kACols + kk * 8;
+            tc_mma_ts(d_addr, a_addr, b0 + static_cast<uint64_t>(kk * 2), idesc, (kc | kk) != 0);
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&aempty[slot]);
+        }
+        if (ok) tc_commit(&dfull[db]);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ----------------------------------------------------------- dequant
+    const int t = threadIdx.x - 128;                 // TMEM lane == tile row
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    uint32_t g = 0;
+    bool ok = true, bad = false;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const int4 tile = p.tiles[item / p.m_tiles];
+      const int m = item % p.m_tiles;
+      int srow, grow;
+      if (p.mode == 0) {
+        srow = (t >> 1) + ((t & 1) ? 64 : 0);         // even lanes: up rows, odd lanes: gate rows
+        grow = ((t & 1) ? gb : ub) + m * 64 + (t >> 1);
+      } else {
+        srow = t;
+        grow = m * kM + t;
+      }
+      const uint8_t *sc = p.scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * (p.K / 32);
+      for (int kc = 0; kc < kchunks; ++kc, ++g) {
+        const int s = g % kStages;
+        const int slot = g % kASlots;
+        const uint32_t s0 = sc[2 * kc], s1 = sc[2 * kc + 1];
+        const uint32_t f0 = scale_f16x2(s0, bad), f1 = scale_f16x2(s1, bad);
+        if (!(ok = mbar_wait(&full[s], (g / kStages) & 1, p.err, 6))) break;
+        const uint4 *src = reinterpret_cast<const uint4 *>(sA + s * kAStageBytes + srow * (kKC / 2));
+        const uint4 v0 = src[0], v1 = src[1];
+        uint32_t r[32];
+        dequant16(v0, f0, r);
+        dequant16(v1, f1, r + 16);
+        if (!(ok = mbar_wait(&aempty[slot], ((g / kASlots) & 1) ^ 1, p.err, 7))) break;
+        WM_TMEM_ST32(tmem + lane_base + kACol0 + slot * kACols, r);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        tc_fence_before();
+        mbar_arrive(&afull[slot]);
+      }
+    }
+    if (bad) atomicCAS(p.err, 0, 100);
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------- epilogue
+    const int t = threadIdx.x - 256;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+      const int4 tile = p.tiles[item / p.m_tiles];
+      const int m = item % p.m_tiles;
+      const int db = it & 1;
+      if (!(ok = mbar_wait(&dfull[db], (it >> 1) & 1, p.err, 8))) break;
+      tc_fence_after();
+      const int n = tile.z;
+      for (int c0 = 0; c0 < n; c0 += 16) {
+        uint32_t r[16];
+        WM_TMEM_LD16(tmem + lane_base + kDCol0 + db * wm::kTcTileN + c0, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (p.mode == 0) {
+          const int j = m * 64 + (t >> 1);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float v = __uint_as_float(r[q]) * 0x1p-8f;
+            const float o = __shfl_xor_sync(0xffffffffu, v, 1);
+            if (!(t & 1) && c0 + q < n) {
+              float up = v, gate = o;
+              if (p.limit > 0.0f) {
+                up = fminf(fmaxf(up, -p.limit), p.limit);
+                gate = fminf(gate, p.limit);
+              }
+              p.h_out[static_cast<int64_t>(tile.y + c0 + q) * p.I + j] = __float2half_rn(silu_f32(gate) * up * 0x1p-4f);
+            }
+          }
+        } else {
+          const int row = m * kM + t;
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            if (c0 + q < n) p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = __uint_as_float(r[q]) * 0x1p-8f;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&dempty[db]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
+  }
+}
+
+// x16[p, :] = f16(x[perm[p] / kk, :] * 2^-4): the up projection's B operand in expert order
+__global__ void k_gather_f16(const uint16_t *__restrict__ x, const int32_t *__restrict__ perm, int S, int kk, int H,
+                             __half *__restrict__ x16) {
+  const int per = H / 8;
+  const int64_t total = static_cast<int64_t>(S) * per;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int pidx = static_cast<int>(i / per), c = static_cast<int>(i % per) * 8;
+    const int tok = perm[pidx] / kk;
+    const uint4 u = *reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(tok) * H + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      __half2 hv = __floats2half2_rn(wm_bf16lo(w[j]) * 0x1p-4f, wm_bf16hi(w[j]) * 0x1p-4f);
+      o[j] = *reinterpret_cast<uint32_t *>(&hv);
+    }
+    *reinterpret_cast<uint4 *>(x16 + static_cast<int64_t>(pidx) * H + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// ------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static std::mutex mu;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_t inner, uint64_t outer,
+             uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return wm::fail(WM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return wm::fail(WM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return WM_OK;
+}
+
+constexpr size_t kSmemBytes = 1024 + kStages * (kBStageBytes + kAStageBytes) + (2 * kStages + 2 * kASlots + 4) * 8 + 16;
+
+int launch_tc(int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K, const __half *bmat, int S_rows,
+              int I, int H, int order, float limit, const int4 *tiles, const int32_t *n_tiles, __half *h_out,
+              float *y_out, int32_t *err, cudaStream_t stream) {
+  CUtensorMap tmA, tmB;
+  if (int rc = make_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K / 2, static_cast<uint64_t>(E) * rows, K / 2, kKC / 2,
+                        64, CU_TENSOR_MAP_SWIZZLE_NONE))
+    return rc;
+  if (int rc = make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, bmat, K, S_rows, static_cast<uint64_t>(K) * 2, kKC, 16,
+                        CU_TENSOR_MAP_SWIZZLE_128B))
+    return rc;
+  static std::mutex mu;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(k_expert_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(kSmemBytes));
+      if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("tc smem attribute: ") + cudaGetErrorString(e));
+      attr_set[dev] = true;
+    }
+  }
+  TcParams p{};
+  p.mode = mode;
+  p.K = K;
+  p.rows = rows;
+  p.I = I;
+  p.H = H;
+  p.order = order;
+  p.limit = limit;
+  p.m_tiles = mode == 0 ? I / 64 : rows / kM;
+  p.scales = scales;
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
+  p.h_out = h_out;
+  p.y_out = y_out;
+  p.err = err;
+  k_expert_tc<<<wm::sm_count(), kThreads, kSmemBytes, stream>>>(tmA, tmB, p);
+  return wm::check_launch("expert tc");
+}
+
+}  // namespace
+
+namespace wm {
+
+bool tc_supported(int H, int I) { return H % 128 == 0 && I % 128 == 0 && H >= 128 && I >= 128; }
+
+int launch_gather_f16(const uint16_t *x, const int32_t *perm, int S, int kk, int H, void *x16, cudaStream_t stream) {
+  const int64_t work = static_cast<int64_t>(S) * (H / 8);
+  const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
+  if (grid > 0) k_gather_f16<<<grid, 256, 0, stream>>>(x, perm, S, kk, H, static_cast<__half *>(x16));
+  return check_launch("gather f16");
+}
+
+int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
+                 float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, cudaStream_t stream) {
+  return launch_tc(0, w13, s13, E, 2 * I, H, static_cast<const __half *>(x16), S_rows, I, H, order, limit, tiles,
+                   n_tiles, static_cast<__half *>(h16), nullptr, err, stream);
+}
+
+int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
+                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, cudaStream_t stream) {
+  return launch_tc(1, w2, s2, E, H, I, static_cast<const __half *>(h16), S_rows, I, H, WM_UP_GATE, 0.0f, tiles,
+                   n_tiles, nullptr, y, err, stream);
+}
+
+}  // namespace wm

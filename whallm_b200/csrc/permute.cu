@@ -21,7 +21,8 @@ namespace {
 __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ idx, int T, int k, int shared_expert,
                                                   int E, int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
                                                   int32_t *__restrict__ inv, int32_t *__restrict__ active,
-                                                  int32_t *__restrict__ n_active, int32_t *__restrict__ error_flag) {
+                                                  int32_t *__restrict__ n_active, int32_t *__restrict__ error_flag,
+                                                  int4 *__restrict__ tiles, int32_t *__restrict__ n_tiles, int tile_n) {
   extern __shared__ int32_t sm[];
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -53,6 +54,7 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
     if (threadIdx.x == 0) {
       if (error_flag) *error_flag = 1;
       if (n_active) *n_active = 0;
+      if (n_tiles) *n_tiles = 0;
       for (int e = 0; e < E; ++e) offsets[e] = 0;
       offsets[E] = -1;  // sentinel: an expert id was outside [0, E)
     }
@@ -66,15 +68,18 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int run = 0, na = 0;
+    int run = 0, na = 0, nt = 0;
     for (int e = 0; e < E; ++e) {
       int c = tot[e];
       offsets[e] = run;
       tot[e] = run;
       if (c > 0 && active) active[na] = e;
       na += c > 0 ? 1 : 0;
+      if (tiles)
+        for (int q = 0; q < c; q += tile_n) tiles[nt++] = make_int4(e, run + q, min(tile_n, c - q), 0);
       run += c;
     }
+    if (n_tiles) *n_tiles = nt;
     offsets[E] = run;
     tot[E] = run;
     if (n_active) *n_active = na;
@@ -124,14 +129,16 @@ int permute_warps(int E) {
 }
 
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
-                   int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, cudaStream_t stream) {
+                   int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
+                   int32_t *n_tiles, int tile_n, cudaStream_t stream) {
   const int nw = permute_warps(E);
   const size_t smem = permute_smem_bytes(E, nw);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("permute smem: ") + cudaGetErrorString(e));
   }
-  k_permute<<<1, nw * 32, smem, stream>>>(idx, T, k, shared_expert, E, offsets, perm, inv, active, n_active, error_flag);
+  k_permute<<<1, nw * 32, smem, stream>>>(idx, T, k, shared_expert, E, offsets, perm, inv, active, n_active, error_flag,
+                                          tiles, n_tiles, tile_n);
   return check_launch("permute");
 }
 
@@ -143,5 +150,6 @@ extern "C" int wmoe_permute(const int32_t *idx, int T, int k, int E, int32_t *of
   WM_REQUIRE(T >= 0 && k >= 1 && E >= 1 && E <= 4096, "permute needs T >= 0, k >= 1, 1 <= E <= 4096");
   WM_REQUIRE(static_cast<int64_t>(T) * k < (1LL << 30), "permute: too many assignments");
   WM_REQUIRE(idx && offsets && perm && inv, "permute: null buffer");
-  return wm::launch_permute(idx, T, k, -1, E, offsets, perm, inv, nullptr, nullptr, nullptr, stream);
+  return wm::launch_permute(idx, T, k, -1, E, offsets, perm, inv, nullptr, nullptr, nullptr, nullptr, nullptr, 0,
+                            stream);
 }

@@ -2,6 +2,7 @@
 // number-format bit manipulation.  sm_100a only.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 

@@ -8,9 +8,22 @@
 
 namespace wm {
 
-// permute.cu
+// Tokens per tensor-core tile (the MMA's N); experts with more tokens get several tiles.
+constexpr int kTcTileN = 128;
+
+// permute.cu.  With tiles != nullptr it also emits the tensor-core work list:
+// {expert, first slot, tokens (<= tile_n), 0} per tile, count in *n_tiles.
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
-                   int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, cudaStream_t stream);
+                   int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
+                   int32_t *n_tiles, int tile_n, cudaStream_t stream);
+
+// moe_tc.cu
+bool tc_supported(int H, int I);
+int launch_gather_f16(const uint16_t *x, const int32_t *perm, int S, int kk, int H, void *x16, cudaStream_t stream);
+int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
+                 float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, cudaStream_t stream);
+int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
+                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, cudaStream_t stream);
 
 // Workspace carved out of the caller's buffer for one expert-forward call.
 // S = T * (k + has_shared) assignments.
@@ -19,9 +32,12 @@ struct MoeWorkspace {
   int32_t *perm;       // [S] sorted slot -> flat assignment
   int32_t *inv;        // [S] flat assignment -> sorted slot
   int32_t *active;     // [E] active expert ids, ascending
-  int32_t *counters;   // [4]: n_active, error flag, spare
-  uint16_t *h;         // [S, I] bf16 SwiGLU output in sorted-slot order
+  int32_t *counters;   // [4]: n_active, permute error flag, n_tiles, tensor-core error code
+  int4 *tiles;         // [E + S/kTcTileN + 1] tensor-core work list
+  uint16_t *h;         // [S_pad, I] SwiGLU output in sorted-slot order (bf16 GEMV path, f16 tensor path)
+  uint16_t *x16;       // [S_pad, H] f16 tokens in sorted-slot order (tensor path)
   float *y;            // [S, H] f32 expert outputs in sorted-slot order
+  int s_pad;           // S rounded up to at least 16 rows (TMA box height)
   size_t bytes;
 };
 
@@ -41,8 +57,12 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
   size_t o_inv = take(S * sizeof(int32_t));
   size_t o_act = take(E * sizeof(int32_t));
   size_t o_cnt = take(4 * sizeof(int32_t));
-  size_t o_h = take(S * I * sizeof(uint16_t));
+  const size_t S_pad = S < 16 ? 16 : S;
+  size_t o_tiles = take((E + S / kTcTileN + 2) * sizeof(int4));
+  size_t o_h = take(S_pad * I * sizeof(uint16_t));
+  size_t o_x16 = take(S_pad * H * sizeof(uint16_t));
   size_t o_y = take(S * H * sizeof(float));
+  w.s_pad = static_cast<int>(S_pad);
   w.bytes = off;
   if (base) {
     char *b = static_cast<char *>(base);
@@ -51,7 +71,9 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
     w.inv = reinterpret_cast<int32_t *>(b + o_inv);
     w.active = reinterpret_cast<int32_t *>(b + o_act);
     w.counters = reinterpret_cast<int32_t *>(b + o_cnt);
+    w.tiles = reinterpret_cast<int4 *>(b + o_tiles);
     w.h = reinterpret_cast<uint16_t *>(b + o_h);
+    w.x16 = reinterpret_cast<uint16_t *>(b + o_x16);
     w.y = reinterpret_cast<float *>(b + o_y);
   }
   return w;
