@@ -14,9 +14,11 @@
  * The reference computes these with MLX kernels whose reduction order is not
  * specified.  To compare routing indices exactly, this oracle and the device
  * kernel agree on one order:
- *   logit[t][e]: 32 partial sums; partial l accumulates, with fmaf, the
- *     elements h = 256*i + 8*l + j (i ascending, then j = 0..7); then a
- *     butterfly over the partials with strides 16, 8, 4, 2, 1.
+ *   logit[t][e]: the 256-wide column blocks are split into 4 contiguous
+ *     segments; in each, partial l accumulates with fmaf the elements
+ *     h = 256*i + 8*l + j (i ascending, then j = 0..7); the 4 segment
+ *     partials of l are added in segment order; then a butterfly over the 32
+ *     partials with strides 16, 8, 4, 2, 1.
  *   softmax sum: partial l sums experts l, l+32, l+64, ... in order, then the
  *     same butterfly.
  *   exp / log: Cody-Waite argument reduction (ln 2 split in a high and a low
@@ -102,13 +104,26 @@ static float butterfly32(float *p) {
   return a[0];
 }
 
+/* x.w in the device order: the 256-wide column blocks i = 0..n-1 (n = ceil(H/256))
+ * are split into 4 contiguous segments [floor(s*n/4), floor((s+1)*n/4)); lane l
+ * of segment s accumulates, with fmaf, the elements 256*i + 8*l + j (i ascending,
+ * j = 0..7); the four segment partials of a lane are added in segment order;
+ * the 32 lane sums are combined by the butterfly. */
 float oracle_dot_bf16(const uint16_t *x, const uint16_t *w, int H) {
+  const int n = (H + 255) / 256;
   float part[32];
   for (int l = 0; l < 32; ++l) {
-    float acc = 0.0f;
-    for (int base = 8 * l; base < H; base += 256)
-      for (int j = 0; j < 8; ++j) acc = fmaf(bf16f(x[base + j]), bf16f(w[base + j]), acc);
-    part[l] = acc;
+    float seg[4];
+    for (int sgi = 0; sgi < 4; ++sgi) {
+      float acc = 0.0f;
+      for (int i = (sgi * n) / 4; i < ((sgi + 1) * n) / 4; ++i) {
+        const int base = 256 * i + 8 * l;
+        if (base >= H) continue;
+        for (int j = 0; j < 8; ++j) acc = fmaf(bf16f(x[base + j]), bf16f(w[base + j]), acc);
+      }
+      seg[sgi] = acc;
+    }
+    part[l] = ((seg[0] + seg[1]) + seg[2]) + seg[3];
   }
   return butterfly32(part);
 }

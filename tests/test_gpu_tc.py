@@ -45,7 +45,7 @@ def _simt(fn):
             os.environ["WM_EXPERT_PATH"] = old
 
 
-@pytest.mark.parametrize("T,E,H,I", [(300, 8, 1024, 256), (700, 4, 512, 384), (64, 4, 7168, 2048)])
+@pytest.mark.parametrize("T,E,H,I", [(300, 8, 1024, 256), (700, 4, 512, 512), (64, 4, 7168, 2048), (40, 6, 2048, 512)])
 def test_tc_many_tokens_per_expert_vs_oracle(dev, T, E, H, I):
     lay = S.make_layer("ds", dev, seed=T + H, E=E, H=H, I=I)
     x = S.make_tokens(T, H, T, dev)

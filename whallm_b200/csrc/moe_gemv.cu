@@ -292,9 +292,10 @@ int run(const Args &a, int fmt) {
   const int kk = a.k + has_shared;
   const int S = a.T * kk;
   const bool tc = fmt == kFmtMxfp4 && wm::tc_supported(a.H, a.I) && !force_simt();
+  const int tile_n = wm::tc_tile_n(a.T);
   if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
-                                  ws.counters, ws.counters + 1, tc ? ws.tiles : nullptr, ws.counters + 2,
-                                  wm::kTcTileN, a.stream))
+                                  ws.counters, ws.counters + 1, tc ? ws.tiles : nullptr, ws.counters + 2, tile_n,
+                                  a.stream))
     return rc;
   const int grid = wm::sm_count() * 2;
   if (tc) {
@@ -302,10 +303,10 @@ int run(const Args &a, int fmt) {
       return wm::fail(WM_ERR_CUDA, "experts: memset failed");
     if (int rc = wm::launch_gather_f16(a.x, ws.perm, S, kk, a.H, ws.x16, a.stream)) return rc;
     if (int rc = wm::launch_tc_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x16, ws.s_pad, a.order, a.limit, ws.tiles,
-                                  ws.counters + 2, ws.h, ws.counters + 3, a.stream))
+                                  ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream))
       return rc;
     if (int rc = wm::launch_tc_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h, ws.s_pad, ws.tiles, ws.counters + 2, ws.y,
-                                    ws.counters + 3, a.stream))
+                                    ws.counters + 3, tile_n, a.stream))
       return rc;
   } else if (fmt == kFmtMxfp4) {
     k_expert_gemv<kFmtMxfp4, kModeUp><<<grid, kWarps * 32, 0, a.stream>>>(a.x, kk, ws.offsets, ws.perm, ws.active,

@@ -24,11 +24,11 @@
 // 2^-25 kept exactly), B holds x * 2^-4, so D = 2^8 * (x . w); the epilogue
 // multiplies by 2^-8.
 //
-// Warp roles (384 threads, one CTA per SM, persistent over work items):
+// Warp roles (512 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMA producer              warp 1   MMA issuer (one thread)
 //   warp 2      TMEM allocator            warp 3   idle
-//   warps 4-7   dequant (TMEM lanes 0-127)
-//   warps 8-11  epilogue (TMEM lanes 0-127): fused ClampedSwiGLU for the
+//   warps 4-11  two dequant warpgroups on alternate A slots (TMEM lanes 0-127)
+//   warps 12-15 epilogue (TMEM lanes 0-127): fused ClampedSwiGLU for the
 //               up projection (lanes 2j / 2j+1 hold up_j / gate_j), f32 rows
 //               of y for the down projection.
 // Every mbarrier wait gives up after 2 s, records an error code and skips the
@@ -44,17 +44,37 @@
 namespace {
 
 constexpr int kM = 128;
-constexpr int kKC = 64;                       // K per pipeline chunk
-constexpr int kStages = 6;
-constexpr int kASlots = 8;
+constexpr int kSub = 64;                      // K per A slot / MMA group (4 x K16)
 constexpr int kACols = 32;                    // TMEM columns per A slot (64 f16)
-constexpr int kDCol0 = 0;                     // D buffers: columns [0, 256)
-constexpr int kACol0 = 256;                   // A ring:    columns [256, 512)
 constexpr int kTmemCols = 512;
-constexpr int kBStageBytes = wm::kTcTileN * kKC * 2;  // 16 KB
-constexpr int kAStageBytes = kM * kKC / 2;            // 4 KB
-constexpr int kThreads = 384;
+constexpr int kDqGroups = 2;                  // dequant warpgroups, alternating A slots
+constexpr int kEpiWarp0 = 4 + 4 * kDqGroups;  // first epilogue warp
+constexpr int kThreads = 32 * (kEpiWarp0 + 4);
 constexpr unsigned long long kWaitNs = 2000000000ull;
+
+// Pipeline shapes.  KC: K per TMA stage; NMAX: tokens per tile (MMA N);
+// decode streams long row segments (KC 256 = 128 B of e2m1 per row, 64 KB of
+// weights in flight per SM), prefill keeps small stages and wide N.
+template <int KC, int NMAX, int STAGES>
+struct Cfg {
+  static constexpr int kKC = KC;
+  static constexpr int kNMax = NMAX;
+  static constexpr int kStages = STAGES;
+  static constexpr int kSubs = KC / kSub;                          // A slots per stage
+  static constexpr int kAStageBytes = kM * KC / 2;
+  static constexpr int kBSubBytes = NMAX * kSub * 2;               // one 64-wide K sub-tile of B
+  static constexpr int kBStageBytes = kBSubBytes * kSubs;
+  static constexpr int kDCol0 = 0;
+  static constexpr int kACol0 = 2 * NMAX;
+  static constexpr int kASlots = (kTmemCols - 2 * NMAX) / kACols;
+  static constexpr bool kSwizzleA = (KC / 2) == 128;               // 128-byte rows: 128B swizzle
+  static constexpr size_t kSmem =
+      1024 + static_cast<size_t>(STAGES) * (kAStageBytes + kBStageBytes) + (2 * STAGES + 2 * kASlots + 4) * 8 + 16;
+  static_assert(kAStageBytes % 1024 == 0 && kBSubBytes % 1024 == 0, "stage buffers must stay 1024-aligned");
+  static_assert(kASlots >= 4, "too few A slots");
+};
+using DecodeCfg = Cfg<256, 64, 4>;
+using PrefillCfg = Cfg<64, 128, 6>;
 
 struct TcParams {
   int mode;              // 0: up projection (+SwiGLU -> h), 1: down projection (-> y)
@@ -221,25 +241,29 @@ __device__ __forceinline__ void dequant16(uint4 v, uint32_t sf, uint32_t *out) {
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
+template <class C>
 __global__ void __launch_bounds__(kThreads, 1)
     k_expert_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
+  constexpr int S = C::kStages;
+  constexpr int SUBS = C::kSubs;
+  constexpr int SLOTS = C::kASlots;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sB = smem;                                   // kStages x 16 KB
-  uint8_t *sA = smem + kStages * kBStageBytes;          // kStages x 4 KB
-  uint64_t *bars = reinterpret_cast<uint64_t *>(sA + kStages * kAStageBytes);
-  uint64_t *full = bars;                                // [kStages]
-  uint64_t *empty = full + kStages;                     // [kStages]
-  uint64_t *afull = empty + kStages;                    // [kASlots]
-  uint64_t *aempty = afull + kASlots;                   // [kASlots]
-  uint64_t *dfull = aempty + kASlots;                   // [2]
+  uint8_t *sB = smem;                                   // S x kBStageBytes
+  uint8_t *sA = smem + S * C::kBStageBytes;             // S x kAStageBytes
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sA + S * C::kAStageBytes);
+  uint64_t *full = bars;                                // [S]
+  uint64_t *empty = full + S;                           // [S]
+  uint64_t *afull = empty + S;                          // [SLOTS]
+  uint64_t *aempty = afull + SLOTS;                     // [SLOTS]
+  uint64_t *dfull = aempty + SLOTS;                     // [2]
   uint64_t *dempty = dfull + 2;                         // [2]
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dempty + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
-    for (int i = 0; i < kASlots; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
+    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < SLOTS; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -255,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int n_items = (*p.n_tiles) * p.m_tiles;
-  const int kchunks = p.K / kKC;
+  const int kstages = p.K / C::kKC;
   const int ub = p.order == WM_UP_GATE ? 0 : p.I;
   const int gb = p.order == WM_UP_GATE ? p.I : 0;
 
@@ -272,27 +296,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (p.mode == 0) { r_lo = ub + m * 64; r_hi = gb + m * 64; }
         else { r_lo = m * kM; r_hi = m * kM + 64; }
         const int ebase = tile.x * p.rows;
-        for (int kc = 0; kc < kchunks; ++kc, ++g) {
-          const int s = g % kStages;
-          const uint32_t u = g / kStages;
+        for (int kc = 0; kc < kstages; ++kc, ++g) {
+          const int s = g % S;
+          const uint32_t u = g / S;
           if (!(ok = mbar_wait(&empty[s], (u & 1) ^ 1, p.err, 1))) break;
-          mbar_expect_tx(&full[s], kAStageBytes + nb * 16 * kKC * 2);
-          tma_load_2d(sA + s * kAStageBytes, &tmA, kc * (kKC / 2), ebase + r_lo, &full[s]);
-          tma_load_2d(sA + s * kAStageBytes + 64 * (kKC / 2), &tmA, kc * (kKC / 2), ebase + r_hi, &full[s]);
-          for (int j = 0; j < nb; ++j)
-            tma_load_2d(sB + s * kBStageBytes + j * 16 * 128, &tmB, kc * kKC, tile.y + 16 * j, &full[s]);
+          mbar_expect_tx(&full[s], C::kAStageBytes + SUBS * nb * 16 * kSub * 2);
+          uint8_t *a = sA + s * C::kAStageBytes;
+          tma_load_2d(a, &tmA, kc * (C::kKC / 2), ebase + r_lo, &full[s]);
+          tma_load_2d(a + C::kAStageBytes / 2, &tmA, kc * (C::kKC / 2), ebase + r_hi, &full[s]);
+          uint8_t *b = sB + s * C::kBStageBytes;
+          for (int q = 0; q < SUBS; ++q)
+            for (int j = 0; j < nb; ++j)
+              tma_load_2d(b + q * C::kBSubBytes + j * 16 * 128, &tmB, kc * C::kKC + q * kSub, tile.y + 16 * j,
+                          &full[s]);
         }
       }
       // drain: every issued stage has been consumed (its empty barrier completed)
-      for (uint32_t q = 0; q < kStages && q < g && ok; ++q) {
+      for (uint32_t q = 0; q < S && q < g && ok; ++q) {
         const uint32_t gg = g - 1 - q;
-        ok = mbar_wait(&empty[gg % kStages], (gg / kStages) & 1, p.err, 2);
+        ok = mbar_wait(&empty[gg % S], (gg / S) & 1, p.err, 2);
       }
     }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
     if (lane == 0) {
-      uint32_t g = 0, it = 0;
+      uint32_t g = 0, h = 0, it = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
         const int4 tile = p.tiles[item / p.m_tiles];
@@ -301,31 +329,42 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int db = it & 1;
         if (!(ok = mbar_wait(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
         tc_fence_after();
-        const uint32_t d_addr = tmem + kDCol0 + db * wm::kTcTileN;
-        for (int kc = 0; kc < kchunks; ++kc, ++g) {
-          const int s = g % kStages;
-          const int slot = g % kASlots;
-          if (!(ok = mbar_wait(&full[s], (g / kStages) & 1, p.err, 4))) break;
-          if (!(ok = mbar_wait(&afull[slot], (g / kASlots) & 1, p.err, 5))) break;
-          tc_fence_after();
-          const uint64_t b0 = bdesc_sw128(smem_u32(sB + s * kBStageBytes));
+        const uint32_t d_addr = tmem + C::kDCol0 + db * C::kNMax;
+        for (int kc = 0; kc < kstages && ok; ++kc, ++g) {
+          const int s = g % S;
+          if (!(ok = mbar_wait(&full[s], (g / S) & 1, p.err, 4))) break;
+          const uint32_t b_base = smem_u32(sB + s * C::kBStageBytes);
+          for (int q = 0; q < SUBS; ++q, ++h) {
+            const int slot = h % SLOTS;
+            if (!(ok = mbar_wait(&afull[slot], (h / SLOTS) & 1, p.err, 5))) break;
+            tc_fence_after();
+            const uint64_t b0 = bdesc_sw128(b_base + q * C::kBSubBytes);
 #pragma unroll
-          for (int kk = 0; kk < kKC / 16; ++kk) {
-            const uint32_t a_addr = tmem + kACol0 + slot * kACols + kk * 8;
-            tc_mma_ts(d_addr, a_addr, b0 + static_cast<uint64_t>(kk * 2), idesc, (kc | kk) != 0);
+            for (int kk = 0; kk < kSub / 16; ++kk) {
+              const uint32_t a_addr = tmem + C::kACol0 + slot * kACols + kk * 8;
+              tc_mma_ts(d_addr, a_addr, b0 + static_cast<uint64_t>(kk * 2), idesc, (kc | q | kk) != 0);
+            }
+            tc_commit(&aempty[slot]);
           }
           tc_commit(&empty[s]);
-          tc_commit(&aempty[slot]);
         }
         if (ok) tc_commit(&dfull[db]);
       }
     }
-  } else if (warp >= 4 && warp < 8) {
+  } else if (warp >= 4 && warp < kEpiWarp0) {
     // ----------------------------------------------------------- dequant
-    const int t = threadIdx.x - 128;                 // TMEM lane == tile row
+    // kDqGroups warpgroups take alternate sub-chunks (A slots), so several
+    // tcgen05.st -> wait::st chains overlap on every SM sub-partition.  Within
+    // a group the loop is software-pipelined: sub-chunk h+kDqGroups is
+    // converted while the TMEM store of h completes.
+    const int wg = (warp - 4) >> 2;
+    const int t = (threadIdx.x - 128) & 127;          // TMEM lane == tile row
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    uint32_t g = 0;
+    uint32_t g = 0, h0 = 0;
     bool ok = true, bad = false;
+    uint32_t r[32];
+    bool pending = false;                             // a store waiting for wait::st + arrive
+    int pend_slot = 0;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const int4 tile = p.tiles[item / p.m_tiles];
       const int m = item % p.m_tiles;
@@ -337,29 +376,79 @@ __global__ void __launch_bounds__(kThreads, 1)
         srow = t;
         grow = m * kM + t;
       }
-      const uint8_t *sc = p.scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * (p.K / 32);
-      for (int kc = 0; kc < kchunks; ++kc, ++g) {
-        const int s = g % kStages;
-        const int slot = g % kASlots;
-        const uint32_t s0 = sc[2 * kc], s1 = sc[2 * kc + 1];
-        const uint32_t f0 = scale_f16x2(s0, bad), f1 = scale_f16x2(s1, bad);
-        if (!(ok = mbar_wait(&full[s], (g / kStages) & 1, p.err, 6))) break;
-        const uint4 *src = reinterpret_cast<const uint4 *>(sA + s * kAStageBytes + srow * (kKC / 2));
-        const uint4 v0 = src[0], v1 = src[1];
-        uint32_t r[32];
-        dequant16(v0, f0, r);
-        dequant16(v1, f1, r + 16);
-        if (!(ok = mbar_wait(&aempty[slot], ((g / kASlots) & 1) ^ 1, p.err, 7))) break;
-        WM_TMEM_ST32(tmem + lane_base + kACol0 + slot * kACols, r);
-        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-        tc_fence_before();
-        mbar_arrive(&afull[slot]);
+      // This row's E8M0 scales as 8-byte words (256 K values each), prefetched
+      // four words ahead through a register shift queue so the global-load
+      // latency never sits on the per-stage critical path.
+      const uint2 *scw =
+          reinterpret_cast<const uint2 *>(p.scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * (p.K / 32));
+      const int nwords = p.K / 256;
+      auto ldw = [&](int w) { return w < nwords ? __ldg(scw + w) : make_uint2(0u, 0u); };
+      uint2 q0 = ldw(0), q1 = ldw(1), q2 = ldw(2), q3 = ldw(3);
+      int wcur = 0;
+      const uint32_t a_row = (srow >> 6) * (C::kAStageBytes / 2) + (srow & 63) * (C::kKC / 2);
+      for (int kc = 0; kc < kstages && ok; ++kc, ++g, h0 += SUBS) {
+        const int s = g % S;
+        const int wneed = (kc * C::kKC) >> 8;
+        while (wcur < wneed) {
+          q0 = q1; q1 = q2; q2 = q3; q3 = ldw(wcur + 4);
+          ++wcur;
+        }
+        // does this group own a sub-chunk of this stage?
+        const int first = static_cast<int>((wg - static_cast<int>(h0 % kDqGroups) + kDqGroups) % kDqGroups);
+        if (first >= SUBS) continue;
+        uint32_t sbytes[SUBS * 2];
+        {
+          const int boff = ((kc * C::kKC) >> 5) & 7;  // first scale byte of this stage within q0
+#pragma unroll
+          for (int q = 0; q < SUBS * 2; ++q) {
+            const int b = boff + q;
+            const uint32_t word = b < 4 ? q0.x : q0.y;
+            sbytes[q] = (word >> (8 * (b & 3))) & 0xffu;
+          }
+        }
+        if (!(ok = mbar_wait(&full[s], (g / S) & 1, p.err, 6))) break;
+        const uint8_t *arow = sA + s * C::kAStageBytes + a_row;
+#pragma unroll
+        for (int q = 0; q < SUBS; ++q) {
+          const uint32_t h = h0 + q;
+          if (static_cast<int>(h % kDqGroups) != wg) continue;
+          uint4 v0, v1;
+          if (C::kSwizzleA) {
+            const int sw = srow & 7;
+            v0 = *reinterpret_cast<const uint4 *>(arow + (((2 * q) ^ sw) << 4));
+            v1 = *reinterpret_cast<const uint4 *>(arow + (((2 * q + 1) ^ sw) << 4));
+          } else {
+            v0 = reinterpret_cast<const uint4 *>(arow)[2 * q];
+            v1 = reinterpret_cast<const uint4 *>(arow)[2 * q + 1];
+          }
+          uint32_t nr[32];
+          dequant16(v0, scale_f16x2(sbytes[2 * q], bad), nr);
+          dequant16(v1, scale_f16x2(sbytes[2 * q + 1], bad), nr + 16);
+          if (pending) {
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
+            mbar_arrive(&afull[pend_slot]);
+            pending = false;
+          }
+          const int slot = h % SLOTS;
+          if (!(ok = mbar_wait(&aempty[slot], ((h / SLOTS) & 1) ^ 1, p.err, 7))) break;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = nr[i];
+          WM_TMEM_ST32(tmem + lane_base + C::kACol0 + slot * kACols, r);
+          pending = true;
+          pend_slot = slot;
+        }
       }
     }
+    if (pending && ok) {
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(&afull[pend_slot]);
+    }
     if (bad) atomicCAS(p.err, 0, 100);
-  } else if (warp >= 8) {
+  } else if (warp >= kEpiWarp0) {
     // ---------------------------------------------------------- epilogue
-    const int t = threadIdx.x - 256;
+    const int t = threadIdx.x - 32 * kEpiWarp0;
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t it = 0;
     bool ok = true;
@@ -372,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n = tile.z;
       for (int c0 = 0; c0 < n; c0 += 16) {
         uint32_t r[16];
-        WM_TMEM_LD16(tmem + lane_base + kDCol0 + db * wm::kTcTileN + c0, r);
+        WM_TMEM_LD16(tmem + lane_base + C::kDCol0 + db * C::kNMax + c0, r);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
         if (p.mode == 0) {
           const int j = m * 64 + (t >> 1);
@@ -458,16 +547,16 @@ int make_map(CUtensorMap *map, CUtensorMapDataType dt, const void *base, uint64_
   return WM_OK;
 }
 
-constexpr size_t kSmemBytes = 1024 + kStages * (kBStageBytes + kAStageBytes) + (2 * kStages + 2 * kASlots + 4) * 8 + 16;
-
-int launch_tc(int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K, const __half *bmat, int S_rows,
-              int I, int H, int order, float limit, const int4 *tiles, const int32_t *n_tiles, __half *h_out,
-              float *y_out, int32_t *err, cudaStream_t stream) {
+template <class C>
+int launch_tc_cfg(int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K, const __half *bmat,
+                  int S_rows, int I, int H, int order, float limit, const int4 *tiles, const int32_t *n_tiles,
+                  __half *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
+  if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert tc: K must be a multiple of the stage depth");
   CUtensorMap tmA, tmB;
-  if (int rc = make_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K / 2, static_cast<uint64_t>(E) * rows, K / 2, kKC / 2,
-                        64, CU_TENSOR_MAP_SWIZZLE_NONE))
+  if (int rc = make_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K / 2, static_cast<uint64_t>(E) * rows, K / 2,
+                        C::kKC / 2, 64, C::kSwizzleA ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE))
     return rc;
-  if (int rc = make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, bmat, K, S_rows, static_cast<uint64_t>(K) * 2, kKC, 16,
+  if (int rc = make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, bmat, K, S_rows, static_cast<uint64_t>(K) * 2, kSub, 16,
                         CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
   static std::mutex mu;
@@ -477,8 +566,8 @@ int launch_tc(int mode, const uint8_t *w, const uint8_t *scales, int E, int rows
   {
     std::lock_guard<std::mutex> lock(mu);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(k_expert_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(kSmemBytes));
+      cudaError_t e = cudaFuncSetAttribute(k_expert_tc<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(C::kSmem));
       if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("tc smem attribute: ") + cudaGetErrorString(e));
       attr_set[dev] = true;
     }
@@ -498,15 +587,27 @@ int launch_tc(int mode, const uint8_t *w, const uint8_t *scales, int E, int rows
   p.h_out = h_out;
   p.y_out = y_out;
   p.err = err;
-  k_expert_tc<<<wm::sm_count(), kThreads, kSmemBytes, stream>>>(tmA, tmB, p);
+  k_expert_tc<C><<<wm::sm_count(), kThreads, C::kSmem, stream>>>(tmA, tmB, p);
   return wm::check_launch("expert tc");
+}
+
+int launch_tc(bool decode, int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K,
+              const __half *bmat, int S_rows, int I, int H, int order, float limit, const int4 *tiles,
+              const int32_t *n_tiles, __half *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
+  if (decode)
+    return launch_tc_cfg<DecodeCfg>(mode, w, scales, E, rows, K, bmat, S_rows, I, H, order, limit, tiles, n_tiles,
+                                    h_out, y_out, err, stream);
+  return launch_tc_cfg<PrefillCfg>(mode, w, scales, E, rows, K, bmat, S_rows, I, H, order, limit, tiles, n_tiles,
+                                   h_out, y_out, err, stream);
 }
 
 }  // namespace
 
 namespace wm {
 
-bool tc_supported(int H, int I) { return H % 128 == 0 && I % 128 == 0 && H >= 128 && I >= 128; }
+bool tc_supported(int H, int I) { return H % 256 == 0 && I % 256 == 0; }
+
+int tc_tile_n(int T) { return T <= DecodeCfg::kNMax ? DecodeCfg::kNMax : PrefillCfg::kNMax; }
 
 int launch_gather_f16(const uint16_t *x, const int32_t *perm, int S, int kk, int H, void *x16, cudaStream_t stream) {
   const int64_t work = static_cast<int64_t>(S) * (H / 8);
@@ -516,14 +617,15 @@ int launch_gather_f16(const uint16_t *x, const int32_t *perm, int S, int kk, int
 }
 
 int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
-                 float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, cudaStream_t stream) {
-  return launch_tc(0, w13, s13, E, 2 * I, H, static_cast<const __half *>(x16), S_rows, I, H, order, limit, tiles,
+                 float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, int tile_n,
+                 cudaStream_t stream) {
+  return launch_tc(tile_n == DecodeCfg::kNMax, 0, w13, s13, E, 2 * I, H, static_cast<const __half *>(x16), S_rows, I, H, order, limit, tiles,
                    n_tiles, static_cast<__half *>(h16), nullptr, err, stream);
 }
 
 int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
-                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, cudaStream_t stream) {
-  return launch_tc(1, w2, s2, E, H, I, static_cast<const __half *>(h16), S_rows, I, H, WM_UP_GATE, 0.0f, tiles,
+                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, int tile_n, cudaStream_t stream) {
+  return launch_tc(tile_n == DecodeCfg::kNMax, 1, w2, s2, E, H, I, static_cast<const __half *>(h16), S_rows, I, H, WM_UP_GATE, 0.0f, tiles,
                    n_tiles, nullptr, y, err, stream);
 }
 

@@ -60,30 +60,58 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
     }
     return;
   }
-  // totals per expert, then exclusive scan (E <= 4096: a serial scan per thread chunk)
+  // totals per expert, then a block-wide exclusive scan of (tokens, active
+  // experts, tiles): thread i owns the contiguous experts [i*cpt, (i+1)*cpt)
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int c = 0;
     for (int w = 0; w < nw; ++w) c += hist[w * E + e];
     tot[e] = c;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, na = 0, nt = 0;
-    for (int e = 0; e < E; ++e) {
-      int c = tot[e];
+  {
+    __shared__ int3 wsum[32];
+    const int cpt = (E + blockDim.x - 1) / blockDim.x;
+    const int e0 = min(E, static_cast<int>(threadIdx.x) * cpt), e1 = min(E, e0 + cpt);
+    int3 mine = make_int3(0, 0, 0);
+    for (int e = e0; e < e1; ++e) {
+      const int c = tot[e];
+      mine.x += c;
+      mine.y += c > 0 ? 1 : 0;
+      mine.z += tiles ? (c + tile_n - 1) / tile_n : 0;
+    }
+    int3 inc = mine;  // inclusive warp scan
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int ax = __shfl_up_sync(0xffffffffu, inc.x, d);
+      const int ay = __shfl_up_sync(0xffffffffu, inc.y, d);
+      const int az = __shfl_up_sync(0xffffffffu, inc.z, d);
+      if (lane >= d) { inc.x += ax; inc.y += ay; inc.z += az; }
+    }
+    if (lane == 31) wsum[warp] = inc;
+    __syncthreads();
+    int3 base = make_int3(0, 0, 0);
+    for (int w = 0; w < warp; ++w) { base.x += wsum[w].x; base.y += wsum[w].y; base.z += wsum[w].z; }
+    int run = base.x + inc.x - mine.x, na = base.y + inc.y - mine.y, nt = base.z + inc.z - mine.z;
+    __syncthreads();  // every thread has read tot[] for its experts before it is overwritten below
+    for (int e = e0; e < e1; ++e) {
+      const int c = tot[e];
       offsets[e] = run;
       tot[e] = run;
-      if (c > 0 && active) active[na] = e;
-      na += c > 0 ? 1 : 0;
+      if (c > 0) {
+        if (active) active[na] = e;
+        ++na;
+      }
       if (tiles)
         for (int q = 0; q < c; q += tile_n) tiles[nt++] = make_int4(e, run + q, min(tile_n, c - q), 0);
       run += c;
     }
-    if (n_tiles) *n_tiles = nt;
-    offsets[E] = run;
-    tot[E] = run;
-    if (n_active) *n_active = na;
-    if (error_flag) *error_flag = 0;
+    if (threadIdx.x == blockDim.x - 1) {
+      offsets[E] = run;
+      tot[E] = run;
+      if (n_active) *n_active = na;
+      if (n_tiles) *n_tiles = nt;
+      if (error_flag) *error_flag = 0;
+    }
   }
   __syncthreads();
   // per-warp cursors: base of expert e for warp w = tot[e] + sum_{w'<w} hist[w'][e]

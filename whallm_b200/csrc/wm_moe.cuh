@@ -8,9 +8,6 @@
 
 namespace wm {
 
-// Tokens per tensor-core tile (the MMA's N); experts with more tokens get several tiles.
-constexpr int kTcTileN = 128;
-
 // permute.cu.  With tiles != nullptr it also emits the tensor-core work list:
 // {expert, first slot, tokens (<= tile_n), 0} per tile, count in *n_tiles.
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
@@ -19,11 +16,13 @@ int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, i
 
 // moe_tc.cu
 bool tc_supported(int H, int I);
+int tc_tile_n(int T);  // tokens per tile: 64 for decode batches (T <= 64), else 128
 int launch_gather_f16(const uint16_t *x, const int32_t *perm, int S, int kk, int H, void *x16, cudaStream_t stream);
 int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
-                 float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, cudaStream_t stream);
+                 float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, int tile_n,
+                 cudaStream_t stream);
 int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
-                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, cudaStream_t stream);
+                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, int tile_n, cudaStream_t stream);
 
 // Workspace carved out of the caller's buffer for one expert-forward call.
 // S = T * (k + has_shared) assignments.
@@ -33,7 +32,7 @@ struct MoeWorkspace {
   int32_t *inv;        // [S] flat assignment -> sorted slot
   int32_t *active;     // [E] active expert ids, ascending
   int32_t *counters;   // [4]: n_active, permute error flag, n_tiles, tensor-core error code
-  int4 *tiles;         // [E + S/kTcTileN + 1] tensor-core work list
+  int4 *tiles;         // [E + S/64 + 2] tensor-core work list
   uint16_t *h;         // [S_pad, I] SwiGLU output in sorted-slot order (bf16 GEMV path, f16 tensor path)
   uint16_t *x16;       // [S_pad, H] f16 tokens in sorted-slot order (tensor path)
   float *y;            // [S, H] f32 expert outputs in sorted-slot order
@@ -58,7 +57,7 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
   size_t o_act = take(E * sizeof(int32_t));
   size_t o_cnt = take(4 * sizeof(int32_t));
   const size_t S_pad = S < 16 ? 16 : S;
-  size_t o_tiles = take((E + S / kTcTileN + 2) * sizeof(int4));
+  size_t o_tiles = take((E + S / 64 + 2) * sizeof(int4));
   size_t o_h = take(S_pad * I * sizeof(uint16_t));
   size_t o_x16 = take(S_pad * H * sizeof(uint16_t));
   size_t o_y = take(S * H * sizeof(float));
