@@ -10,10 +10,13 @@ never come from L2 between steps; inputs are already in HBM.
   value  tokens/s over the whole job (sum over ranks / max rank time)
   e2e    the same through the public API with pinned host buffers: H2D of the
          step's tokens and D2H of the layer outputs inside the timed region
-  roofline  the expert FFN call (wmoe_mxfp4_moe_forward: permute, fused
-         up-projection + SwiGLU, down-projection, combine): algorithmic bytes
-         (distinct experts x 23,396,352 B + activations) / its CUDA-event
-         time, against the measured HBM copy bandwidth
+  roofline  the expert FFN call (wmoe_mxfp4_moe_forward: permute, token
+         gather, tcgen05 up-projection + SwiGLU, tcgen05 down-projection,
+         combine; the two tcgen05 launches carry ~90% of its device time):
+         algorithmic bytes (distinct experts x 23,396,352 B + activations) /
+         its CUDA-event time, against the measured HBM copy bandwidth
+Decode batches are replayed as CUDA graphs (one per layer and batch size),
+prefill runs eagerly.
   cpu_baseline  the oracle's C restatement (OpenMP, all host threads) on a
          bounded sample of the same sweep
 
@@ -124,6 +127,7 @@ def run_ours(args, rank, world, dev):
     import whallm_b200 as W
     from whallm_b200 import experts as X
     from whallm_b200 import synthetic as S
+    from whallm_b200.graphs import CapturedLayer
 
     torch.cuda.set_device(dev)
     hbm, tc, peak_src = _peaks()
@@ -158,18 +162,44 @@ def run_ours(args, rank, world, dev):
         act_bytes = [x.numel() * 2 * 2 for x in xs]          # x in + out (bf16)
         alg_bytes = [d * expert_bytes + a for d, a in zip(distinct, act_bytes)]
 
-        def step(i):
-            lay = layers[i % n_layers]
-            for x in xs:
-                lay.layer(x)
+        limit = 10.0 if name == "ds" else 0.0
+        shared_id = cfg["E"] if cfg["shared"] else -1
 
-        def experts_only(i):
-            lay = layers[i % n_layers]
-            for b, x in enumerate(xs):
-                w, idx, sw = routes[i % n_layers][b]
-                X.experts_forward(x, idx, lay.experts, weights=w,
-                                  shared_expert=cfg["E"] if cfg["shared"] else -1, shared_w=sw,
-                                  swiglu_limit=10.0 if name == "ds" else 0.0)
+        def experts_call(li, b, x):
+            w, idx, sw = routes[li][b]
+            return X.experts_forward(x, idx, layers[li].experts, weights=w, shared_expert=shared_id, shared_w=sw,
+                                     swiglu_limit=limit)
+
+        graphed = wl in ("ds_decode", "qn_decode")
+        if graphed:
+            # decode: one CUDA graph per (layer, batch) for the whole layer and for
+            # the expert call alone (launch overhead exceeds the work at B = 1)
+            caps = [[CapturedLayer(lay.layer, x) for x in xs] for lay in layers]
+            ecaps = [[CapturedLayer(lambda xx, li=li, b=b: experts_call(li, b, xx), x) for b, x in enumerate(xs)]
+                     for li in range(n_layers)]
+
+            def step(i):
+                for c in caps[i % n_layers]:
+                    c()
+
+            def experts_only(i):
+                for c in ecaps[i % n_layers]:
+                    c()
+
+            def one(i, b):
+                caps[i % n_layers][b]()
+        else:
+            def step(i):
+                lay = layers[i % n_layers]
+                for x in xs:
+                    lay.layer(x)
+
+            def experts_only(i):
+                for b, x in enumerate(xs):
+                    experts_call(i % n_layers, b, x)
+
+            def one(i, b):
+                layers[i % n_layers].layer(xs[b])
 
         for i in range(args.warmup):
             step(i)
@@ -205,10 +235,9 @@ def run_ours(args, rank, world, dev):
         for b, x in enumerate(xs):
             ts = []
             for i in range(min(args.steps, 2 * n_layers)):
-                lay = layers[i % n_layers]
                 s3, e3 = _events(torch)
                 s3.record()
-                lay.layer(x)
+                one(i, b)
                 e3.record()
                 torch.cuda.synchronize()
                 ts.append(s3.elapsed_time(e3))
@@ -226,8 +255,10 @@ def run_ours(args, rank, world, dev):
         for i in range(args.steps):
             lay = layers[i % n_layers]
             for b in range(len(xs)):
-                xd = hx[b].to(dev, non_blocking=True)
-                y = lay.layer(xd)
+                if graphed:
+                    y = caps[i % n_layers][b](hx[b].to(dev, non_blocking=True))
+                else:
+                    y = lay.layer(hx[b].to(dev, non_blocking=True))
                 houts[b].copy_(y, non_blocking=True)
         e4.record()
         torch.cuda.synchronize()
@@ -236,7 +267,8 @@ def run_ours(args, rank, world, dev):
         res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=tokens_per_step, alg_bytes=sum(alg_bytes),
                         per_b=per_b, clocks=clocks, h2d=h2d, d2h=h2d, cfg=cfg, batches=batches,
                         distinct=distinct, hbm=hbm, peak_src=peak_src,
-                        launches=len(xs) * (2 + 4)))
+                        launches=len(xs) * (2 + 5) if name != "tiny" else len(xs) * (2 + 4),
+                        graphed=graphed))
         return res
     if wl == "kv":
         D, rows_total = 576, 32768 * 8 * 61
@@ -423,6 +455,7 @@ def main():
                        "tokens_per_step": r["tokens"], "layers_cycled": args.layers,
                        "l2": "8 resident layers (48 GB) cycled per step: weights larger than L2",
                        "parallelism": "replicas" if world > 1 else "single GPU",
+                       "launch": "CUDA graph per (layer, batch)" if r.get("graphed") else "eager",
                        "per_batch": r["per_b"]},
             "e2e": None if ms_e2e is None else {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2),
                                                  "unit": unit, "h2d_bytes_per_step": r["h2d"],

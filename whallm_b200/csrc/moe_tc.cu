@@ -24,11 +24,11 @@
 // 2^-25 kept exactly), B holds x * 2^-4, so D = 2^8 * (x . w); the epilogue
 // multiplies by 2^-8.
 //
-// Warp roles (512 threads, one CTA per SM, persistent over work items):
+// Warp roles (640 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMA producer              warp 1   MMA issuer (one thread)
-//   warp 2      TMEM allocator            warp 3   idle
-//   warps 4-11  two dequant warpgroups on alternate A slots (TMEM lanes 0-127)
-//   warps 12-15 epilogue (TMEM lanes 0-127): fused ClampedSwiGLU for the
+//   warp 2      TMEM allocator            warp 3   second MMA issuer (decode)
+//   warps 4-15  three dequant warpgroups, round-robin over A slots (TMEM lanes 0-127)
+//   warps 16-19 epilogue (TMEM lanes 0-127): fused ClampedSwiGLU for the
 //               up projection (lanes 2j / 2j+1 hold up_j / gate_j), f32 rows
 //               of y for the down projection.
 // Every mbarrier wait gives up after 2 s, records an error code and skips the
@@ -47,7 +47,7 @@ constexpr int kM = 128;
 constexpr int kSub = 64;                      // K per A slot / MMA group (4 x K16)
 constexpr int kACols = 32;                    // TMEM columns per A slot (64 f16)
 constexpr int kTmemCols = 512;
-constexpr int kDqGroups = 2;                  // dequant warpgroups, alternating A slots
+constexpr int kDqGroups = 3;                  // dequant warpgroups, round-robin over A slots
 constexpr int kEpiWarp0 = 4 + 4 * kDqGroups;  // first epilogue warp
 constexpr int kThreads = 32 * (kEpiWarp0 + 4);
 constexpr unsigned long long kWaitNs = 2000000000ull;
@@ -55,26 +55,28 @@ constexpr unsigned long long kWaitNs = 2000000000ull;
 // Pipeline shapes.  KC: K per TMA stage; NMAX: tokens per tile (MMA N);
 // decode streams long row segments (KC 256 = 128 B of e2m1 per row, 64 KB of
 // weights in flight per SM), prefill keeps small stages and wide N.
-template <int KC, int NMAX, int STAGES>
+template <int KC, int NMAX, int STAGES, int ISSUERS>
 struct Cfg {
   static constexpr int kKC = KC;
   static constexpr int kNMax = NMAX;
   static constexpr int kStages = STAGES;
+  static constexpr int kIssuers = ISSUERS;                         // MMA-issuing threads, one accumulator each
   static constexpr int kSubs = KC / kSub;                          // A slots per stage
   static constexpr int kAStageBytes = kM * KC / 2;
   static constexpr int kBSubBytes = NMAX * kSub * 2;               // one 64-wide K sub-tile of B
   static constexpr int kBStageBytes = kBSubBytes * kSubs;
-  static constexpr int kDCol0 = 0;
-  static constexpr int kACol0 = 2 * NMAX;
-  static constexpr int kASlots = (kTmemCols - 2 * NMAX) / kACols;
+  static constexpr int kDCol0 = 0;                                 // D[issuer][buffer]: NMAX columns each
+  static constexpr int kACol0 = 2 * ISSUERS * NMAX;
+  static constexpr int kASlots = (kTmemCols - kACol0) / kACols;
   static constexpr bool kSwizzleA = (KC / 2) == 128;               // 128-byte rows: 128B swizzle
   static constexpr size_t kSmem =
       1024 + static_cast<size_t>(STAGES) * (kAStageBytes + kBStageBytes) + (2 * STAGES + 2 * kASlots + 4) * 8 + 16;
   static_assert(kAStageBytes % 1024 == 0 && kBSubBytes % 1024 == 0, "stage buffers must stay 1024-aligned");
   static_assert(kASlots >= 4, "too few A slots");
+  static_assert(ISSUERS == 1 || (ISSUERS == 2 && (KC / 64) % 2 == 0), "two issuers need an even number of A slots per stage");
 };
-using DecodeCfg = Cfg<256, 64, 4>;
-using PrefillCfg = Cfg<64, 128, 6>;
+using DecodeCfg = Cfg<256, 64, 4, 2>;
+using PrefillCfg = Cfg<64, 128, 6, 1>;
 
 struct TcParams {
   int mode;              // 0: up projection (+SwiGLU -> h), 1: down projection (-> y)
@@ -111,14 +113,17 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete
+// sleeps (up to the hint, in ns) until the phase flips instead of spinning,
+// so waiting roles do not take issue slots from the dequant warps.
 __device__ __forceinline__ bool mbar_try(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
       : "memory");
   return ok != 0;
 }
@@ -134,7 +139,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int32_
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = gtimer();
   while (true) {
-    for (int i = 0; i < 64; ++i)
+    for (int i = 0; i < 8; ++i)
       if (mbar_try(bar, parity)) return true;
     if (gtimer() - t0 > kWaitNs) {
       atomicCAS(err, 0, code);
@@ -148,6 +153,18 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
       ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
+}
+
+// One lane of a converged warp (the issuing lane for TMA / MMA); the loops
+// around it stay warp-uniform so their values live in uniform registers.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred;
+  asm volatile(
+      "{\n\t.reg .b32 r;\n\t.reg .pred p;\n\t"
+      "elect.sync r|p, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -262,9 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1); mbar_init(&empty[i], C::kIssuers); }
     for (int i = 0; i < SLOTS; ++i) { mbar_init(&afull[i], 128); mbar_init(&aempty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], C::kIssuers); mbar_init(&dempty[i], 128); }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -285,21 +302,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
-    if (lane == 0) {
-      uint32_t g = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const int4 tile = p.tiles[item / p.m_tiles];
-        const int m = item % p.m_tiles;
-        const int nb = (tile.z + 15) >> 4;
-        int r_lo, r_hi;
-        if (p.mode == 0) { r_lo = ub + m * 64; r_hi = gb + m * 64; }
-        else { r_lo = m * kM; r_hi = m * kM + 64; }
-        const int ebase = tile.x * p.rows;
-        for (int kc = 0; kc < kstages; ++kc, ++g) {
-          const int s = g % S;
-          const uint32_t u = g / S;
-          if (!(ok = mbar_wait(&empty[s], (u & 1) ^ 1, p.err, 1))) break;
+    // The whole warp runs the loop; one elected lane issues the TMA copies.
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const int4 tile = p.tiles[item / p.m_tiles];
+      const int m = item % p.m_tiles;
+      const int nb = (tile.z + 15) >> 4;
+      int r_lo, r_hi;
+      if (p.mode == 0) { r_lo = ub + m * 64; r_hi = gb + m * 64; }
+      else { r_lo = m * kM; r_hi = m * kM + 64; }
+      const int ebase = tile.x * p.rows;
+      for (int kc = 0; kc < kstages; ++kc, ++g) {
+        const int s = g % S;
+        const uint32_t u = g / S;
+        if (!(ok = mbar_wait(&empty[s], (u & 1) ^ 1, p.err, 1))) break;
+        if (elect_one()) {
           mbar_expect_tx(&full[s], C::kAStageBytes + SUBS * nb * 16 * kSub * 2);
           uint8_t *a = sA + s * C::kAStageBytes;
           tma_load_2d(a, &tmA, kc * (C::kKC / 2), ebase + r_lo, &full[s]);
@@ -310,45 +328,59 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_2d(b + q * C::kBSubBytes + j * 16 * 128, &tmB, kc * C::kKC + q * kSub, tile.y + 16 * j,
                           &full[s]);
         }
-      }
-      // drain: every issued stage has been consumed (its empty barrier completed)
-      for (uint32_t q = 0; q < S && q < g && ok; ++q) {
-        const uint32_t gg = g - 1 - q;
-        ok = mbar_wait(&empty[gg % S], (gg / S) & 1, p.err, 2);
+        __syncwarp();
       }
     }
-  } else if (warp == 1) {
+    // drain: every issued stage has been consumed (its empty barrier completed)
+    for (uint32_t q = 0; q < S && q < g && ok; ++q) {
+      const uint32_t gg = g - 1 - q;
+      ok = mbar_wait(&empty[gg % S], (gg / S) & 1, p.err, 2);
+    }
+  } else if (warp == 1 || (C::kIssuers == 2 && warp == 3)) {
     // --------------------------------------------------------------- MMA
-    if (lane == 0) {
-      uint32_t g = 0, h = 0, it = 0;
-      bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-        const int4 tile = p.tiles[item / p.m_tiles];
-        const int n_mma = max(16, (tile.z + 15) & ~15);
-        const uint32_t idesc = idesc_f16(n_mma);
-        const int db = it & 1;
-        if (!(ok = mbar_wait(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
-        tc_fence_after();
-        const uint32_t d_addr = tmem + C::kDCol0 + db * C::kNMax;
-        for (int kc = 0; kc < kstages && ok; ++kc, ++g) {
-          const int s = g % S;
-          if (!(ok = mbar_wait(&full[s], (g / S) & 1, p.err, 4))) break;
-          const uint32_t b_base = smem_u32(sB + s * C::kBStageBytes);
-          for (int q = 0; q < SUBS; ++q, ++h) {
-            const int slot = h % SLOTS;
-            if (!(ok = mbar_wait(&afull[slot], (h / SLOTS) & 1, p.err, 5))) break;
-            tc_fence_after();
-            const uint64_t b0 = bdesc_sw128(b_base + q * C::kBSubBytes);
+    // Issuer i (warp 1 -> 0, warp 3 -> 1) takes the A slots h with
+    // h % kIssuers == i and accumulates into its own D; the epilogue adds the
+    // accumulators.  Two issuing threads double the MMA issue rate, which is
+    // what bounds decode (each M128 x N16 x K16 MMA covers 1 KB of weights).
+    const int issuer = warp == 1 ? 0 : 1;
+    uint32_t g = 0, h = 0, it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+      const int4 tile = p.tiles[item / p.m_tiles];
+      const int n_mma = max(16, (tile.z + 15) & ~15);
+      const uint32_t idesc = idesc_f16(n_mma);
+      const int db = it & 1;
+      if (!(ok = mbar_wait(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
+      tc_fence_after();
+      const uint32_t d_addr = tmem + C::kDCol0 + (issuer * 2 + db) * C::kNMax;
+      bool first = true;
+      for (int kc = 0; kc < kstages && ok; ++kc, ++g) {
+        const int s = g % S;
+        if (!(ok = mbar_wait(&full[s], (g / S) & 1, p.err, 4))) break;
+        const uint32_t b_base = smem_u32(sB + s * C::kBStageBytes);
+        for (int q = 0; q < SUBS; ++q, ++h) {
+          if (static_cast<int>(h % C::kIssuers) != issuer) continue;
+          const int slot = h % SLOTS;
+          if (!(ok = mbar_wait(&afull[slot], (h / SLOTS) & 1, p.err, 5))) break;
+          tc_fence_after();
+          const uint64_t b0 = bdesc_sw128(b_base + q * C::kBSubBytes);
+          if (elect_one()) {
 #pragma unroll
             for (int kk = 0; kk < kSub / 16; ++kk) {
               const uint32_t a_addr = tmem + C::kACol0 + slot * kACols + kk * 8;
-              tc_mma_ts(d_addr, a_addr, b0 + static_cast<uint64_t>(kk * 2), idesc, (kc | q | kk) != 0);
+              tc_mma_ts(d_addr, a_addr, b0 + static_cast<uint64_t>(kk * 2), idesc, (first && kk == 0) ? 0u : 1u);
             }
             tc_commit(&aempty[slot]);
           }
-          tc_commit(&empty[s]);
+          __syncwarp();
+          first = false;
         }
-        if (ok) tc_commit(&dfull[db]);
+        if (elect_one()) tc_commit(&empty[s]);
+        __syncwarp();
+      }
+      if (ok) {
+        if (elect_one()) tc_commit(&dfull[db]);
+        __syncwarp();
       }
     }
   } else if (warp >= 4 && warp < kEpiWarp0) {
@@ -362,7 +394,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     uint32_t g = 0, h0 = 0;
     bool ok = true, bad = false;
-    uint32_t r[32];
     bool pending = false;                             // a store waiting for wait::st + arrive
     int pend_slot = 0;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -432,9 +463,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int slot = h % SLOTS;
           if (!(ok = mbar_wait(&aempty[slot], ((h / SLOTS) & 1) ^ 1, p.err, 7))) break;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = nr[i];
-          WM_TMEM_ST32(tmem + lane_base + C::kACol0 + slot * kACols, r);
+          // tcgen05.st reads its source registers at issue; only the TMEM write
+          // is asynchronous (completed by the wait::st above, next round)
+          WM_TMEM_ST32(tmem + lane_base + C::kACol0 + slot * kACols, nr);
           pending = true;
           pend_slot = slot;
         }
@@ -462,7 +493,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c0 = 0; c0 < n; c0 += 16) {
         uint32_t r[16];
         WM_TMEM_LD16(tmem + lane_base + C::kDCol0 + db * C::kNMax + c0, r);
-        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (C::kIssuers == 2) {
+          uint32_t r2[16];
+          WM_TMEM_LD16(tmem + lane_base + C::kDCol0 + (2 + db) * C::kNMax + c0, r2);
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+          for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(__uint_as_float(r[q]) + __uint_as_float(r2[q]));
+        } else {
+          asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        }
         if (p.mode == 0) {
           const int j = m * 64 + (t >> 1);
 #pragma unroll
