@@ -75,7 +75,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -264,7 +264,9 @@ def run_ours(args, rank, world, dev):
         torch.cuda.synchronize()
         ms_e2e = s4.elapsed_time(e4) / args.steps
         h2d = sum(x.numel() * 2 for x in xs)
+        flops = sum(B * (cfg["k"] + (1 if cfg["shared"] else 0)) * 6 * cfg["H"] * cfg["I"] for B in batches)
         res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=tokens_per_step, alg_bytes=sum(alg_bytes),
+                        flops=flops, tc_peak=tc, prefill=wl in ("ds_prefill", "qn_prefill"),
                         per_b=per_b, clocks=clocks, h2d=h2d, d2h=h2d, cfg=cfg, batches=batches,
                         distinct=distinct, hbm=hbm, peak_src=peak_src,
                         launches=len(xs) * (2 + 5) if name != "tiny" else len(xs) * (2 + 4),
@@ -291,7 +293,7 @@ def run_ours(args, rank, world, dev):
         ms = s.elapsed_time(e) / args.steps
         per_entry = 576 + 9 * 4 + 1152
         alg = rows_total * per_entry * 2  # quantize (read bf16, write packed) + dequant (read packed, write bf16)
-        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=None, tokens=rows_total, alg_bytes=alg, per_b={}, clocks=None,
+        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=None, tokens=rows_total, alg_bytes=alg, per_b={}, clocks=None, flops=0,
                         h2d=0, d2h=0, cfg={"D": D}, batches=(), distinct=[], hbm=hbm, peak_src=peak_src,
                         launches=2 * 61))
         return res
@@ -389,7 +391,7 @@ def cpu_reference(args, sample_steps=None):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="ds_decode",
@@ -439,11 +441,20 @@ def main():
     if rank == 0:
         hbm = r["hbm"]
         achieved = r["alg_bytes"] / (ms_exp * 1e-3) / 1e9
+        if r.get("prefill"):
+            # prefill is compute-bound: FLOPs of the expert FFN over the measured dense
+            # 16-bit tensor peak (the MMA runs f16 x f16 -> f32)
+            achieved_tf = r["flops"] / (ms_exp * 1e-3) / 1e12
+        # DRAM bytes per step of the expert calls: per-expert traffic measured by
+        # ncu on a smaller case (profiles/traffic.json), scaled by the distinct
+        # experts this workload streams per step
         traffic = None
         prof = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(prof):
+        if os.path.exists(prof) and r.get("distinct"):
             try:
-                traffic = json.load(open(prof)).get(args.workload)
+                t = json.load(open(prof)).get(args.workload)
+                if t:
+                    traffic = round(t["bytes_per_expert"] * sum(r["distinct"]))
             except Exception:
                 traffic = None
         line = {
@@ -460,9 +471,16 @@ def main():
             "e2e": None if ms_e2e is None else {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2),
                                                  "unit": unit, "h2d_bytes_per_step": r["h2d"],
                                                  "d2h_bytes_per_step": r["d2h"]},
-            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "traffic": traffic,
-                         "kernel": "expert FFN call (wmoe_mxfp4_moe_forward), " + r["peak_src"] + " HBM peak"},
+            "roofline": ({"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                          "frac": round(achieved / hbm, 4), "traffic": traffic,
+                          "algorithmic_bytes_per_step": r["alg_bytes"],
+                          "kernel": "expert FFN call (wmoe_mxfp4_moe_forward), " + r["peak_src"] + " HBM peak"}
+                         if not r.get("prefill") else
+                         {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": r["tc_peak"],
+                          "unit": "TFLOP/s", "frac": round(achieved_tf / r["tc_peak"], 4), "traffic": traffic,
+                          "algorithmic_flops_per_step": r["flops"],
+                          "kernel": "expert FFN call (wmoe_mxfp4_moe_forward), " + r["peak_src"] +
+                                    " dense bf16 peak (f16 MMA)"}),
             "gpu_launches": r["launches"] * args.steps,
             "clocks": r["clocks"],
         }
