@@ -154,6 +154,20 @@ WM_API int wmoe_topk_scores(const float *logits, const float *select_bias, int T
                             int score_fn, float norm_eps, float route_scale, int32_t *idx,
                             float *weights, wm_stream_t stream);
 
+/* wmoe_router_topk without the logits scratch argument, for callers that
+ * cannot allocate device memory where they route (inside a stream capture,
+ * allocation-free serving loops, hosts whose memory belongs to another
+ * allocator).  No counterpart in the reference: MLX allocates its own
+ * temporaries.  The [T,E] logits live in a 1 MiB file-scope device array
+ * (T*E <= 262144, else WM_ERR_INVALID), reserved on every GPU that loads the
+ * library until exit and shared by all calls: calls that overlap on the GPU
+ * race.  The array's address is looked up on the first call per device; make
+ * that call outside any stream capture.  Results equal wmoe_router_topk's. */
+WM_API int wmoe_router_topk_static(const wm_bf16 *x, const wm_bf16 *wg, const float *logit_bias,
+                                   const float *select_bias, const wm_bf16 *wg_shared, int T, int H,
+                                   int E, int k, int score_fn, float norm_eps, float route_scale,
+                                   int32_t *idx, float *weights, float *shared_w, wm_stream_t stream);
+
 /* -------------------------------------------------------------- permute --- */
 
 /* Stable sort of the T*k assignments by expert (mlx-lm _gather_sort, called at

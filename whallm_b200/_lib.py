@@ -45,6 +45,7 @@ SIGNATURES = {
     "wkv_gather_dequantize": [_P, _P, _I64, _P, _I64, _I, _I, _P, _P],
     "wmoe_router_topk": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P, _P, _P],
     "wmoe_topk_scores": [_P, _P, _I, _I, _I, _I, _F, _F, _P, _P, _P],
+    "wmoe_router_topk_static": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P, _P],
     "wmoe_permute": [_P, _I, _I, _I, _P, _P, _P, _P],
     "wmoe_workspace_size": [_I, _I, _I, _I, _I, _I],
     "wmoe_mxfp4_experts": [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _F, _P, _P, _SZ, _P],

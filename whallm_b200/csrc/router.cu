@@ -16,6 +16,8 @@
 //   tokens); each warp streams a quarter of the row with 16-byte loads.
 // Kernel 2 (top-k): one CTA per token; scores are computed by all threads,
 //   then k rounds of a warp arg-max with ties to the lower expert id.
+#include <mutex>
+
 #include "wm_common.cuh"
 #include "wm_detmath.cuh"
 
@@ -213,4 +215,79 @@ extern "C" int wmoe_topk_scores(const float *logits, const float *select_bias, i
   k_router_topk<<<T, 256, 0, stream>>>(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights,
                                        nullptr);
   return wm::check_launch("wmoe_topk_scores");
+}
+
+// ------------------------------------------------------------------------
+// Allocation-free variant of wmoe_router_topk.
+//
+// Some callers cannot allocate device memory at the point where they route:
+// code running inside a CUDA stream capture (cudaMalloc is not capturable),
+// serving loops that must never take the device-synchronising allocation path,
+// and hosts whose memory is owned by another framework's allocator with no
+// hook to borrow scratch.  This entry point takes the same inputs and outputs
+// as wmoe_router_topk but keeps the [T, E] logits scratch in a fixed
+// file-scope device array instead of a caller buffer.
+//
+// Limits and contract:
+//   * the array holds kStaticLogits = 262,144 floats (1 MiB); every GPU that
+//     loads this library reserves it until the process exits; T * E beyond it
+//     is rejected with WM_ERR_INVALID;
+//   * the array's device address is looked up once per device, on the first
+//     call made with that device current (cudaGetSymbolAddress); make that
+//     first call outside any stream capture;
+//   * all calls share the one array and it keeps the last call's contents:
+//     every element the kernels read is written earlier in the same call, so
+//     nothing has to be cleared, but calls whose kernels overlap on the GPU
+//     (different streams, no ordering between them) race on it.
+// ------------------------------------------------------------------------
+namespace {
+
+constexpr int64_t kStaticLogits = 262144;
+__device__ __align__(256) float g_router_logits_scratch[kStaticLogits];
+
+std::mutex g_scratch_mu;
+float *g_scratch_ptr[64] = {nullptr};
+
+}  // namespace
+
+extern "C" int wmoe_router_topk_static(const wm_bf16 *x, const wm_bf16 *wg, const float *logit_bias,
+                                       const float *select_bias, const wm_bf16 *wg_shared, int T, int H, int E, int k,
+                                       int score_fn, float norm_eps, float route_scale, int32_t *idx, float *weights,
+                                       float *shared_w, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "router needs H % 8 == 0");
+  WM_REQUIRE(E >= 1 && E <= kMaxE, "router supports 1 <= E <= 1024 experts");
+  WM_REQUIRE(k >= 1 && k <= kMaxK && k <= E, "router needs 1 <= k <= min(32, E)");
+  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_NONE, "unknown score function");
+  WM_REQUIRE(static_cast<int64_t>(T) * E <= kStaticLogits,
+             "wmoe_router_topk_static: T*E exceeds the 262144-float (1 MiB) static scratch; use wmoe_router_topk");
+  if (T == 0) return WM_OK;
+  WM_REQUIRE(x && wg && idx && weights, "router: null buffer");
+  WM_REQUIRE(!wg_shared || shared_w, "router: wg_shared needs a shared_w output");
+  WM_REQUIRE(wm::aligned(x, 16) && wm::aligned(wg, 16) && (!wg_shared || wm::aligned(wg_shared, 16)),
+             "router inputs must be 16-byte aligned");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return wm::fail(WM_ERR_CUDA, "wmoe_router_topk_static: no current CUDA device");
+  float *scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (!g_scratch_ptr[dev]) {
+      void *p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_router_logits_scratch);
+      if (e != cudaSuccess || !p)
+        return wm::fail(WM_ERR_CUDA, std::string("wmoe_router_topk_static: cudaGetSymbolAddress failed: ") +
+                                         cudaGetErrorString(e));
+      g_scratch_ptr[dev] = static_cast<float *>(p);
+    }
+    scratch = g_scratch_ptr[dev];
+  }
+  const int rows = E + (wg_shared ? 1 : 0);
+  const int64_t ctas = static_cast<int64_t>(rows) * ((T + kTokChunk - 1) / kTokChunk);
+  k_router_logits<<<static_cast<int>(ctas), 128, 0, stream>>>(x, wg, wg_shared, logit_bias, T, H, E, scratch,
+                                                              shared_w);
+  if (int rc = wm::check_launch("wmoe_router_topk_static(logits)")) return rc;
+  k_router_topk<<<T, 256, 0, stream>>>(scratch, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights,
+                                       shared_w);
+  return wm::check_launch("wmoe_router_topk_static(topk)");
 }
