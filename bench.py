@@ -28,9 +28,11 @@ dequantize of 32768 x 8 x 61 rows of 576).
 oracle port; the MLX CPU backend the reference would use is not installable
 here) on the same workload and prints the same JSON line with "impl".
 
-Multi-GPU (torchrun): each rank runs the workload on its own GPU with its own
-weights (independent replicas, weak scaling); value = all ranks' tokens /
-max rank time.
+Multi-GPU (torchrun): the MoE workloads run expert-parallel (`whallm_b200.ep`):
+each rank routes its own tokens (weak scaling), the routed experts are sharded
+evenly over the ranks, token rows go to the owning rank and back through NCCL
+all-to-all, the shared expert is replicated; value = all ranks' tokens / max
+rank time.  Other workloads run as independent replicas.
 """
 from __future__ import annotations
 
@@ -300,6 +302,89 @@ def run_ours(args, rank, world, dev):
     raise SystemExit(f"unknown workload {wl}")
 
 
+def run_ep(args, rank, world, dev):
+    """Expert-parallel layer over NCCL: every rank routes its own tokens, the
+    routed experts are sharded evenly (E/W per rank), the shared expert is
+    replicated; dispatch and combine are variable-split all-to-alls."""
+    import torch
+    import whallm_b200 as W
+    from whallm_b200 import ep as EP
+    from whallm_b200 import synthetic as S
+
+    torch.cuda.set_device(dev)
+    hbm, tc, peak_src = _peaks()
+    wl = args.workload
+    name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn"}[wl]
+    batches = {"ds_decode": SWEEP, "ds_prefill": (4096,), "qn_decode": (1, 32), "qn_prefill": (16384,)}[wl]
+    n_layers = args.layers
+    moes = []
+    cfg = None
+    for i in range(n_layers):
+        lay = S.make_layer(name, dev, seed=17 * i)          # identical weights on every rank
+        cfg = lay.cfg
+        E = cfg["E"]
+        local = EP.shard_experts(lay.experts, rank, world, E, cfg["shared"])
+        per = E // world
+        limit = 10.0 if name == "ds" else 0.0
+        if name == "ds":
+            router = lay.layer.gate
+            gate_fn = None
+        else:
+            state = {}
+
+            def router(x, lay=lay, state=state):
+                w, idx, sw = W.qwen_route(x, lay.gate_weight, cfg["k"], True, shared_gate=lay.shared_gate,
+                                          logit_bias=lay.logit_bias)
+                state["sw"] = sw
+                return w, idx
+
+            def gate_fn(x, state=state):
+                return state["sw"]
+        moes.append(EP.ExpertParallelMoE(router, EP.gpu_local_experts(local, limit), E,
+                                         shared=EP.gpu_shared_expert(local, per, limit, gate=gate_fn)))
+        del lay
+        torch.cuda.empty_cache()
+    H = cfg["H"]
+    xs = [S.make_tokens(B, H, 100 + rank, dev) for B in batches]
+
+    def step(i):
+        for x in xs:
+            moes[i % n_layers](x)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    clk = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clk:
+        clk.start()
+    torch.distributed.barrier()
+    torch.cuda.synchronize()
+    s, e = _events(torch)
+    s.record()
+    for i in range(args.steps):
+        step(i)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    clocks = clk.stop() if clk else None
+    torch.distributed.barrier()
+    hx = [x.cpu().pin_memory() for x in xs]
+    houts = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in xs]
+    torch.cuda.synchronize()
+    s4, e4 = _events(torch)
+    s4.record()
+    for i in range(args.steps):
+        for b in range(len(xs)):
+            houts[b].copy_(moes[i % n_layers](hx[b].to(dev, non_blocking=True)), non_blocking=True)
+    e4.record()
+    torch.cuda.synchronize()
+    ms_e2e = s4.elapsed_time(e4) / args.steps
+    h2d = sum(x.numel() * 2 for x in xs)
+    return dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=0, per_b={}, clocks=clocks,
+                h2d=h2d, d2h=h2d, cfg=cfg, batches=batches, distinct=[], hbm=hbm, peak_src=peak_src,
+                launches=len(xs) * 9, flops=0, ep=True)
+
+
 # --------------------------------------------------------------------------
 # reference arm: the oracle port on the host cores
 # --------------------------------------------------------------------------
@@ -429,7 +514,8 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
-    r = run_ours(args, rank, world, dev)
+    use_ep = world > 1 and args.workload in ("ds_decode", "ds_prefill", "qn_decode", "qn_prefill")
+    r = run_ep(args, rank, world, dev) if use_ep else run_ours(args, rank, world, dev)
     ms = r["ms"]
     if world > 1:
         t = torch.tensor([ms, r["ms_e2e"] or 0.0, r["ms_exp"]], device=dev)
@@ -457,6 +543,23 @@ def main():
                     traffic = round(t["bytes_per_expert"] * sum(r["distinct"]))
             except Exception:
                 traffic = None
+        if r.get("ep"):
+            line_ep = {
+                "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "mxfp4 weights, bf16 activations, fp32 accumulate",
+                "data": "synthetic (seeded N(0,0.02) MXFP4 experts, N(0,1) bf16 tokens, Zipf-skewed router)",
+                "config": {"workload": args.workload, "batches": list(r["batches"]), "tokens_per_rank": r["tokens"],
+                           "layers_cycled": args.layers, "parallelism": f"ep{world}",
+                           "experts_per_rank": r["cfg"]["E"] // world, "launch": "eager (NCCL all-to-all)"},
+                "e2e": {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2), "unit": unit,
+                        "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
+                "roofline": None, "gpu_launches": r["launches"] * args.steps, "clocks": r["clocks"],
+            }
+            print(json.dumps(line_ep), flush=True)
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+            return
         line = {
             "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",

@@ -1,0 +1,155 @@
+"""Expert-parallel exchange logic on CPU ranks (gloo, world size 2).
+
+The dispatch plan, the two variable-split all-to-alls and the combine of
+``whallm_b200.ep.ExpertParallelMoE`` run for real over gloo; the router and the
+local expert math are the CPU oracle, so the result must match the
+single-process oracle layer on each rank's tokens.  A second test makes one
+rank leave before the exchange: the other rank's collective must fail within
+the process-group timeout instead of hanging (failure detection on the host,
+no GPU involved).
+"""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _layer(seed=5, E=8, H=64, I=64, k=3):
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import formats as F
+    from oracle import moe as M
+    rng = np.random.default_rng(seed)
+    n = E + 1
+    w13 = np.zeros((n, 2 * I, H // 2), np.uint8)
+    s13 = np.zeros((n, 2 * I, H // 32), np.uint8)
+    w2 = np.zeros((n, H, I // 2), np.uint8)
+    s2 = np.zeros((n, H, I // 32), np.uint8)
+    for e in range(n):
+        w13[e], s13[e] = F.mxfp4_quantize_bf16(F.f32_to_bf16_bits(rng.normal(0, 0.1, (2 * I, H)).astype(np.float32)))
+        w2[e], s2[e] = F.mxfp4_quantize_bf16(F.f32_to_bf16_bits(rng.normal(0, 0.1, (H, I)).astype(np.float32)))
+    ex = M.MXFP4Experts(w13, s13, w2, s2, M.UP_GATE, 10.0)
+    wg = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    return ex, wg, dict(E=E, H=H, I=I, k=k)
+
+
+def _tokens(rank, T, H):
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import formats as F
+    rng = np.random.default_rng(100 + rank)
+    return F.round_bf16(rng.normal(0, 1, (T, H)).astype(np.float32))
+
+
+def _worker(rank, world, port, result_q):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from oracle import formats as F
+        from oracle import moe as M
+        from oracle import router as R
+        from whallm_b200.ep import ExpertParallelMoE, shard_bounds
+        ex, wg, c = _layer()
+        E, H, k = c["E"], c["H"], c["k"]
+        T = 7 + 5 * rank
+        x = _tokens(rank, T, H)
+
+        def router(xt):
+            xb = F.f32_to_bf16_bits(xt.float().numpy())
+            _, idx, w, _ = R.route(xb, wg, k, R.SCORE_SQRTSOFTPLUS, norm_eps=1e-20, route_scale=1.5)
+            return torch.from_numpy(w), torch.from_numpy(idx)
+
+        e0, per = shard_bounds(E, world, rank)
+
+        def local(rows, ids):
+            rows_np = rows.float().numpy()
+            out = np.zeros_like(rows_np)
+            for le in np.unique(ids.numpy()):
+                sel = np.flatnonzero(ids.numpy() == le)
+                out[sel] = ex.ffn(e0 + int(le), rows_np[sel])
+            return torch.from_numpy(F.round_bf16(out)).to(torch.bfloat16)
+
+        def shared(xt):
+            return torch.from_numpy(ex.ffn(E, xt.float().numpy()))
+
+        moe = ExpertParallelMoE(router, local, E, shared=shared)
+        got = moe(torch.from_numpy(x).to(torch.bfloat16)).float().numpy()
+        _, idx, w, _ = R.route(F.f32_to_bf16_bits(x), wg, k, R.SCORE_SQRTSOFTPLUS, norm_eps=1e-20, route_scale=1.5)
+        ref = M.moe_forward(x, idx, w, ex, shared_expert=E)
+        result_q.put((rank, M.max_rel_err(got, ref), int(idx.max()), int(idx.min())))
+    finally:
+        dist.destroy_process_group()
+
+
+def _dying_worker(rank, world, port, result_q):
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        # leave between steps: no collective of this rank is in flight
+        result_q.put((rank, "left"))
+        result_q.close()
+        result_q.join_thread()  # flush the queue's feeder thread before exiting
+        os._exit(0)
+    from whallm_b200.ep import plan_dispatch
+    try:
+        plan_dispatch(torch.zeros((4, 2), dtype=torch.int32), 8, world)
+        result_q.put((rank, "no error"))
+    except Exception as exc:  # the survivor must see an error, not hang
+        result_q.put((rank, "error: " + type(exc).__name__))
+
+
+def _spawn(fn, world=2, timeout=120):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=fn, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = []
+    for _ in range(world):
+        out.append(q.get(timeout=timeout))
+    for p in procs:
+        p.join(timeout=timeout)
+        if p.is_alive():
+            p.kill()
+    return sorted(out, key=lambda r: r[0])
+
+
+def test_ep_exchange_matches_single_process_layer():
+    res = _spawn(_worker)
+    for rank, err, hi, lo in res:
+        assert err < 2e-2, (rank, err)
+        assert 0 <= lo <= hi < 8
+
+
+def test_rank_leaving_surfaces_as_collective_error():
+    res = _spawn(_dying_worker, timeout=90)
+    assert res[1][1] == "left"
+    assert res[0][1].startswith("error"), res
+
+
+def test_uneven_sharding_rejected():
+    from whallm_b200.ep import shard_bounds
+    with pytest.raises(ValueError):
+        shard_bounds(10, 4, 0)
