@@ -303,19 +303,23 @@ def run_ours(args, rank, world, dev):
 
 
 def run_ep(args, rank, world, dev):
-    """Expert-parallel layer over NCCL: every rank routes its own tokens, the
-    routed experts are sharded evenly (E/W per rank), the shared expert is
-    replicated; dispatch and combine are variable-split all-to-alls."""
+    """Expert-parallel layer over NCCL: the routed experts are sharded evenly
+    (E/W per rank), the router and the shared expert are replicated.  Decode
+    uses the gathered form (all-gather tokens and routes, partial sums of the
+    rank's experts, reduce-scatter; fixed-size collectives, one CUDA graph per
+    (layer, batch)); prefill uses the variable-split all-to-all form, eager."""
     import torch
     import whallm_b200 as W
     from whallm_b200 import ep as EP
     from whallm_b200 import synthetic as S
+    from whallm_b200.graphs import CapturedLayer
 
     torch.cuda.set_device(dev)
     hbm, tc, peak_src = _peaks()
     wl = args.workload
     name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn"}[wl]
     batches = {"ds_decode": SWEEP, "ds_prefill": (4096,), "qn_decode": (1, 32), "qn_prefill": (16384,)}[wl]
+    decode = wl in ("ds_decode", "qn_decode")
     n_layers = args.layers
     moes = []
     cfg = None
@@ -324,7 +328,7 @@ def run_ep(args, rank, world, dev):
         cfg = lay.cfg
         E = cfg["E"]
         local = EP.shard_experts(lay.experts, rank, world, E, cfg["shared"])
-        per = E // world
+        e0, per = EP.shard_bounds(E, world, rank)
         limit = 10.0 if name == "ds" else 0.0
         if name == "ds":
             router = lay.layer.gate
@@ -336,20 +340,49 @@ def run_ep(args, rank, world, dev):
                 w, idx, sw = W.qwen_route(x, lay.gate_weight, cfg["k"], True, shared_gate=lay.shared_gate,
                                           logit_bias=lay.logit_bias)
                 state["sw"] = sw
-                return w, idx
+                return (w, idx, sw) if decode else (w, idx)
 
             def gate_fn(x, state=state):
                 return state["sw"]
-        moes.append(EP.ExpertParallelMoE(router, EP.gpu_local_experts(local, limit), E,
-                                         shared=EP.gpu_shared_expert(local, per, limit, gate=gate_fn)))
+        if decode:
+            moes.append(EP.GatheredExpertParallelMoE(
+                router, EP.gpu_partial_experts(local, e0, per, E, limit, cfg["shared"]), E))
+        else:
+            moes.append(EP.ExpertParallelMoE(router, EP.gpu_local_experts(local, limit), E,
+                                             shared=EP.gpu_shared_expert(local, per, limit, gate=gate_fn)))
+        moes[-1].route_fn = router
         del lay
         torch.cuda.empty_cache()
     H = cfg["H"]
+    E = cfg["E"]
+    e0, per = EP.shard_bounds(E, world, rank)
     xs = [S.make_tokens(B, H, 100 + rank, dev) for B in batches]
+    # algorithmic bytes: the distinct local experts each (layer, batch) touches
+    # over all ranks' tokens, plus the shared expert, plus activations
+    expert_bytes = DS_EXPERT_BYTES if name == "ds" else QN_EXPERT_BYTES
+    distinct = [0.0] * len(xs)
+    for m in moes:
+        for b, x in enumerate(xs):
+            idx = m.route_fn(x)[1].to(torch.int32).contiguous()
+            allidx = torch.empty((world * idx.shape[0], idx.shape[1]), dtype=idx.dtype, device=dev)
+            torch.distributed.all_gather_into_tensor(allidx, idx)
+            ids = set(allidx.flatten().tolist())
+            distinct[b] += (sum(1 for e in ids if e0 <= e < e0 + per) + (1 if cfg["shared"] else 0)) / n_layers
+    act_bytes = sum(world * B * H * (2 + 4 + 4) for B in batches) if decode else 0
+    alg_bytes = sum(distinct) * expert_bytes + act_bytes
+
+    if decode:
+        caps = [[CapturedLayer(m, x) for x in xs] for m in moes]
+
+        def call(li, b, x=None):
+            return caps[li][b](x)
+    else:
+        def call(li, b, x=None):
+            return moes[li](xs[b] if x is None else x)
 
     def step(i):
-        for x in xs:
-            moes[i % n_layers](x)
+        for b in range(len(xs)):
+            call(i % n_layers, b)
 
     for i in range(args.warmup):
         step(i)
@@ -375,14 +408,17 @@ def run_ep(args, rank, world, dev):
     s4.record()
     for i in range(args.steps):
         for b in range(len(xs)):
-            houts[b].copy_(moes[i % n_layers](hx[b].to(dev, non_blocking=True)), non_blocking=True)
+            houts[b].copy_(call(i % n_layers, b, hx[b].to(dev, non_blocking=True)), non_blocking=True)
     e4.record()
     torch.cuda.synchronize()
     ms_e2e = s4.elapsed_time(e4) / args.steps
+    if decode:
+        del caps           # graphs holding NCCL work go before the process group
+        torch.cuda.synchronize()
     h2d = sum(x.numel() * 2 for x in xs)
-    return dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=0, per_b={}, clocks=clocks,
-                h2d=h2d, d2h=h2d, cfg=cfg, batches=batches, distinct=[], hbm=hbm, peak_src=peak_src,
-                launches=len(xs) * 9, flops=0, ep=True)
+    return dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=alg_bytes, per_b={}, clocks=clocks,
+                h2d=h2d, d2h=h2d, cfg=cfg, batches=batches, distinct=distinct, hbm=hbm, peak_src=peak_src,
+                launches=len(xs) * (7 if decode else 9), flops=0, ep=True, decode=decode)
 
 
 # --------------------------------------------------------------------------
@@ -551,10 +587,17 @@ def main():
                 "data": "synthetic (seeded N(0,0.02) MXFP4 experts, N(0,1) bf16 tokens, Zipf-skewed router)",
                 "config": {"workload": args.workload, "batches": list(r["batches"]), "tokens_per_rank": r["tokens"],
                            "layers_cycled": args.layers, "parallelism": f"ep{world}",
-                           "experts_per_rank": r["cfg"]["E"] // world, "launch": "eager (NCCL all-to-all)"},
+                           "experts_per_rank": r["cfg"]["E"] // world,
+                           "launch": ("CUDA graph per (layer, batch): NCCL all-gather, partial experts, "
+                                      "reduce-scatter") if r.get("decode") else "eager (NCCL all-to-all)"},
                 "e2e": {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2), "unit": unit,
                         "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
-                "roofline": None, "gpu_launches": r["launches"] * args.steps, "clocks": r["clocks"],
+                "roofline": ({"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                              "frac": round(achieved / hbm, 4), "traffic": traffic,
+                              "algorithmic_bytes_per_step": round(r["alg_bytes"]),
+                              "kernel": "whole layer per rank (router, collectives, expert share), "
+                                        + r["peak_src"] + " HBM peak"} if r.get("decode") else None),
+                "gpu_launches": r["launches"] * args.steps, "clocks": r["clocks"],
             }
             print(json.dumps(line_ep), flush=True)
             torch.distributed.barrier()

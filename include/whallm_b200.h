@@ -205,6 +205,26 @@ WM_API int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const fl
                            float swiglu_limit, int shared_expert, const float *shared_w,
                            wm_bf16 *out, void *workspace, size_t ws_bytes, wm_stream_t stream);
 
+/* One expert-parallel rank's share of wmoe_mxfp4_moe_forward, for decode
+ * after an all-gather of every rank's tokens (T = all ranks' tokens):
+ * out [T,H] float32 = sum over j with idx[t,j] in [route_base,
+ * route_base + route_count) of weights[t,j] * FFN_{idx[t,j] - route_base}(x[t])
+ * + (shared_lo <= t < shared_hi ? shared_w[t] * FFN_{shared}(x[t]) : 0).
+ * The weight tensors hold E_local experts: the rank's route_count routed
+ * experts, then (optionally) the shared expert at index shared_expert.  Ids in
+ * [0, n_routed) owned by other ranks are skipped; ids outside [0, n_routed)
+ * set the error path (zeros).  Summing `out` over the ranks (a reduce-scatter
+ * over the token blocks) gives the layer output.  The reference has no
+ * multi-device MoE (_streaming_moe raises on a sharding group,
+ * model.py:485-486); this is the sharded form of the same layer.  Workspace:
+ * wmoe_workspace_size(T, k, H, I, E_local, shared_expert >= 0). */
+WM_API int wmoe_mxfp4_moe_forward_ep(const wm_bf16 *x, const int32_t *idx, const float *weights, int T, int k,
+                              int H, int I, int E_local, int n_routed, int route_base, int route_count,
+                              const uint8_t *w13, const uint8_t *s13, const uint8_t *w2, const uint8_t *s2,
+                              int gate_up_order, float swiglu_limit, int shared_expert, const float *shared_w,
+                              int shared_lo, int shared_hi, float *out, void *workspace, size_t ws_bytes,
+                              wm_stream_t stream);
+
 /* Affine 4-bit experts (group `group`): w13 uint32 [E, 2I, H/8] with bf16
  * sc13/bi13 [E, 2I, H/group]; w2 uint32 [E, H, I/8] with sc2/bi2 [E, H, I/group]. */
 WM_API int wmoe_affine4_experts(const wm_bf16 *x, const int32_t *idx, int T, int k, int H, int I, int E,

@@ -99,6 +99,51 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
+def _gathered_worker(rank, world, port, result_q):
+    """Decode form: all-gather tokens + routes, partial sums, reduce-scatter."""
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from oracle import formats as F
+        from oracle import moe as M
+        from oracle import router as R
+        from whallm_b200.ep import GatheredExpertParallelMoE, shard_bounds
+        ex, wg, c = _layer()
+        E, H, k = c["E"], c["H"], c["k"]
+        B = 6                                   # same batch on every rank
+        x = _tokens(rank, B, H)
+        e0, per = shard_bounds(E, world, rank)
+
+        def router(xt):
+            _, idx, w, _ = R.route(F.f32_to_bf16_bits(xt.float().numpy()), wg, k, R.SCORE_SQRTSOFTPLUS,
+                                   norm_eps=1e-20, route_scale=1.5)
+            sw = np.full((xt.shape[0],), 0.75, np.float32)   # a per-token shared-expert weight
+            return torch.from_numpy(w), torch.from_numpy(idx), torch.from_numpy(sw)
+
+        def partial(xg, idxg, wgt, swg, rows):
+            xs = xg.float().numpy()
+            ids, ws, sws = idxg.numpy(), wgt.numpy(), swg.numpy()
+            out = np.zeros_like(xs)
+            for t in range(xs.shape[0]):
+                for j in range(k):
+                    if e0 <= ids[t, j] < e0 + per:
+                        out[t] += ws[t, j] * ex.ffn(int(ids[t, j]), xs[t:t + 1])[0]
+                if rows[0] <= t < rows[1]:
+                    out[t] += sws[t] * ex.ffn(E, xs[t:t + 1])[0]
+            return torch.from_numpy(out)
+
+        moe = GatheredExpertParallelMoE(router, partial, E)
+        got = moe(torch.from_numpy(x).to(torch.bfloat16)).float().numpy()
+        _, idx, w, _ = R.route(F.f32_to_bf16_bits(x), wg, k, R.SCORE_SQRTSOFTPLUS, norm_eps=1e-20, route_scale=1.5)
+        ref = M.moe_forward(x, idx, w, ex, shared_expert=E, shared_weight=np.full((B,), 0.75, np.float32))
+        result_q.put((rank, M.max_rel_err(got, ref), int(idx.max()), int(idx.min())))
+    finally:
+        dist.destroy_process_group()
+
+
 def _dying_worker(rank, world, port, result_q):
     import sys
     sys.path.insert(0, ROOT)
@@ -138,6 +183,13 @@ def _spawn(fn, world=2, timeout=120):
 
 def test_ep_exchange_matches_single_process_layer():
     res = _spawn(_worker)
+    for rank, err, hi, lo in res:
+        assert err < 2e-2, (rank, err)
+        assert 0 <= lo <= hi < 8
+
+
+def test_gathered_ep_matches_single_process_layer():
+    res = _spawn(_gathered_worker)
     for rank, err, hi, lo in res:
         assert err < 2e-2, (rank, err)
         assert 0 <= lo <= hi < 8

@@ -1,9 +1,17 @@
-"""Expert parallelism on 2 GPUs over NCCL vs the single-GPU layer.
+"""Expert parallelism vs the single-GPU layer.
 
-Each rank holds half of the routed experts plus the shared expert, routes its
-own tokens, exchanges rows with all-to-all and combines; the result must match
-the full layer run on one GPU with the same weights and tokens (2e-2
-max-relative, bf16 output).  Skipped when fewer than two GPUs are visible.
+* One GPU, W ranks emulated: each rank's share through
+  ``wmoe_mxfp4_moe_forward_ep`` (its routed experts only, the shared expert on
+  its own token block, float32 partials); the sum over the ranks must match
+  the full layer (``wmoe_mxfp4_moe_forward``) and the oracle, on the
+  tensor-core and the CUDA-core expert paths; edge cases: a rank that owns no
+  assigned expert, an id outside the layer (error path: zeros).
+* Two GPUs over NCCL: the all-to-all layer (each rank routes its own tokens,
+  exchanges rows, combines) and the gathered decode layer (all-gather,
+  partial sums, reduce-scatter), eager and replayed from a CUDA graph; each
+  must match the full layer on one GPU with the same weights and tokens
+  (2e-2 max-relative, bf16 output).  Skipped when fewer than two GPUs are
+  visible.
 """
 import datetime
 import os
@@ -23,6 +31,64 @@ def _free_port():
     p = s.getsockname()[1]
     s.close()
     return p
+
+
+def _partials(lay, x, world, idx=None, w=None):
+    """Sum over emulated ranks of the f32 partial outputs, bf16-rounded."""
+    from whallm_b200 import ep as EP
+    from whallm_b200 import experts as X
+    E = lay.cfg["E"]
+    T = x.shape[0]
+    if idx is None:
+        w, idx = lay.layer.gate(x)
+    B = T // world
+    acc = torch.zeros((T, x.shape[1]), dtype=torch.float32, device=x.device)
+    for r in range(world):
+        e0, per = EP.shard_bounds(E, world, r)
+        local = EP.shard_experts(lay.experts, r, world, E, True)
+        rows = (r * B, T if r == world - 1 else (r + 1) * B)
+        acc += X.experts_forward(x, idx, local, weights=w, shared_expert=per, swiglu_limit=10.0,
+                                 expert_range=(e0, per, E), shared_rows=rows)
+    return acc.to(torch.bfloat16), w, idx
+
+
+@pytest.mark.parametrize("world,T,H,I", [(2, 6, 1024, 256), (4, 72, 1024, 256), (8, 24, 512, 96)])
+def test_partial_sums_over_ranks_equal_full_layer(dev, world, T, H, I):
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import moe as M
+    from whallm_b200 import synthetic as S
+    lay = S.make_layer("ds", dev, seed=11 + world, E=16, H=H, I=I)
+    x = S.make_tokens(T, H, 60 + world, dev)
+    got, w, idx = _partials(lay, x, world)
+    full = lay.layer(x)
+    assert M.max_rel_err(got.float().cpu().numpy(), full.float().cpu().numpy()) < 1e-2
+    ex = M.MXFP4Experts(*(t.cpu().numpy() for t in (lay.experts.w13, lay.experts.w13_scales, lay.experts.w2,
+                                                     lay.experts.w2_scales)), M.UP_GATE, 10.0)
+    ref = M.moe_forward(x.float().cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), ex, shared_expert=16)
+    assert M.max_rel_err(got.float().cpu().numpy(), ref) < 2e-2
+
+
+def test_partial_rank_without_assignments_and_bad_ids(dev):
+    from whallm_b200 import ep as EP
+    from whallm_b200 import experts as X
+    from whallm_b200 import synthetic as S
+    lay = S.make_layer("ds", dev, seed=4, E=8, H=512, I=256)
+    x = S.make_tokens(4, 512, 9, dev)
+    idx = torch.tensor([[0, 1, 2, 3, 0, 1, 2, 3]] * 4, dtype=torch.int32, device=dev)   # all on rank 0 of 2
+    w = torch.full((4, 8), 0.125, device=dev)
+    local1 = EP.shard_experts(lay.experts, 1, 2, 8, True)
+    part = X.experts_forward(x, idx, local1, weights=w, shared_expert=4, swiglu_limit=10.0,
+                             expert_range=(4, 4, 8), shared_rows=(2, 4))
+    shared_only = X.experts_forward(x, torch.full((4, 1), 8, dtype=torch.int32, device=dev), lay.experts,
+                                    swiglu_limit=10.0).view(4, -1).float()
+    assert torch.count_nonzero(part[:2]) == 0
+    assert (part[2:].to(torch.bfloat16).float() - shared_only[2:]).abs().max().item() < 1e-2 * shared_only.abs().max().item()
+    bad = idx.clone()
+    bad[1, 5] = 8                                           # not a routed expert of the layer
+    part = X.experts_forward(x, bad, local1, weights=w, shared_expert=4, swiglu_limit=10.0,
+                             expert_range=(4, 4, 8), shared_rows=(0, 4))
+    assert torch.count_nonzero(part) == 0
 
 
 def _worker(rank, world, port, q):
@@ -46,7 +112,21 @@ def _worker(rank, world, port, q):
                                    shared=EP.gpu_shared_expert(local, 8 // world, 10.0))
         got = moe(x)
         torch.cuda.synchronize()
-        q.put((rank, M.max_rel_err(got.float().cpu().numpy(), full.float().cpu().numpy())))
+        errs = [M.max_rel_err(got.float().cpu().numpy(), full.float().cpu().numpy())]
+        # gathered decode form: same B on every rank
+        from whallm_b200.graphs import CapturedLayer
+        xb = S.make_tokens(9, 1024, 70 + rank, dev)
+        full_b = lay.layer(xb)
+        e0, per = EP.shard_bounds(8, world, rank)
+        gmoe = EP.GatheredExpertParallelMoE(lay.layer.gate, EP.gpu_partial_experts(local, e0, per, 8, 10.0), 8)
+        errs.append(M.max_rel_err(gmoe(xb).float().cpu().numpy(), full_b.float().cpu().numpy()))
+        cap = CapturedLayer(gmoe, xb)
+        y = cap(xb)
+        torch.cuda.synchronize()
+        errs.append(M.max_rel_err(y.float().cpu().numpy(), full_b.float().cpu().numpy()))
+        del cap
+        torch.cuda.synchronize()
+        q.put((rank, errs))
     finally:
         dist.destroy_process_group()
 
@@ -62,5 +142,5 @@ def test_ep_two_gpus_matches_single_gpu_layer():
     res = sorted([q.get(timeout=300) for _ in range(2)])
     for p in procs:
         p.join(timeout=120)
-    for rank, err in res:
-        assert err < 2e-2, (rank, err)
+    for rank, errs in res:
+        assert len(errs) == 3 and max(errs) < 2e-2, (rank, errs)

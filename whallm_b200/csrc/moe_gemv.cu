@@ -189,11 +189,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   }
 }
 
-// out[t, :] = sum_j w[t,j] * y[inv[t*kk+j], :] (+ shared_w[t] * y[inv[t*kk+k], :]), fixed order
-// A set error flag (expert id out of range) yields zeros; slots are bounds-checked.
+// out[t, :] = sum_j w[t,j] * y[inv[t*kk+j], :] (+ shared_w[t] * y[inv[t*kk+k], :]), fixed order,
+// rounded once to bf16 (F32_OUT false) or kept in f32 (an expert-parallel partial sum).
+// A set error flag (expert id out of range) yields zeros; slots are bounds-checked and
+// dropped assignments (slot -1) contribute nothing.
+template <bool F32_OUT>
 __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict__ inv, const float *__restrict__ w,
                           const float *__restrict__ shared_w, const int32_t *__restrict__ err, int T, int k, int kk,
-                          int H, uint16_t *__restrict__ out) {
+                          int H, void *__restrict__ out_v) {
   const int per_row = H / 8;
   const int S = T * kk;
   const bool bad = *err != 0;
@@ -212,12 +215,18 @@ __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict
       acc[4] = fmaf(wt, b.x, acc[4]); acc[5] = fmaf(wt, b.y, acc[5]);
       acc[6] = fmaf(wt, b.z, acc[6]); acc[7] = fmaf(wt, b.w, acc[7]);
     }
-    uint4 o;
-    o.x = wm_f32_to_bf16(acc[0]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16);
-    o.y = wm_f32_to_bf16(acc[2]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16);
-    o.z = wm_f32_to_bf16(acc[4]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[5])) << 16);
-    o.w = wm_f32_to_bf16(acc[6]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[7])) << 16);
-    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(t) * H + c8) = o;
+    if constexpr (F32_OUT) {
+      float4 *op = reinterpret_cast<float4 *>(static_cast<float *>(out_v) + static_cast<int64_t>(t) * H + c8);
+      op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+      op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+    } else {
+      uint4 o;
+      o.x = wm_f32_to_bf16(acc[0]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16);
+      o.y = wm_f32_to_bf16(acc[2]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16);
+      o.z = wm_f32_to_bf16(acc[4]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[5])) << 16);
+      o.w = wm_f32_to_bf16(acc[6]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[7])) << 16);
+      *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out_v) + static_cast<int64_t>(t) * H + c8) = o;
+    }
   }
 }
 
@@ -260,6 +269,8 @@ struct Args {
   void *ws;
   size_t ws_bytes;
   cudaStream_t stream;
+  wm::RouteFilter rf{};      // expert-parallel share (count 0: the whole layer)
+  float *out_f32 = nullptr;  // f32 partial output instead of bf16 `out`
 };
 
 int check_common(const Args &a) {
@@ -268,9 +279,10 @@ int check_common(const Args &a) {
   WM_REQUIRE(a.I % 16 == 0 && a.H % 32 == 0, "experts: I % 16 == 0 and H % 32 == 0 required");
   WM_REQUIRE(a.order == WM_UP_GATE || a.order == WM_GATE_UP, "experts: gate_up_order must be WM_UP_GATE or WM_GATE_UP");
   WM_REQUIRE(a.shared_expert < a.E, "experts: shared_expert must be < E");
-  WM_REQUIRE(a.x && a.idx && a.out && a.w13.w && a.w2.w, "experts: null buffer");
+  WM_REQUIRE(a.x && a.idx && (a.out || a.out_f32) && a.w13.w && a.w2.w, "experts: null buffer");
   WM_REQUIRE(!a.reduce || a.weights, "moe_forward: null weights");
-  WM_REQUIRE(wm::aligned(a.x, 16) && wm::aligned(a.out, 16) && wm::aligned(a.w13.w, 16) && wm::aligned(a.w2.w, 16),
+  WM_REQUIRE(wm::aligned(a.x, 16) && wm::aligned(a.out, 16) && wm::aligned(a.out_f32, 16) &&
+                 wm::aligned(a.w13.w, 16) && wm::aligned(a.w2.w, 16),
              "experts: x, out and packed weights must be 16-byte aligned");
   WM_REQUIRE(wm::aligned(a.ws, 256), "experts: workspace must be 256-byte aligned");
   return WM_OK;
@@ -295,13 +307,13 @@ int run(const Args &a, int fmt) {
   const int tile_n = wm::tc_tile_n(a.T);
   if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
                                   ws.counters, ws.counters + 1, tc ? ws.tiles : nullptr, ws.counters + 2, tile_n,
-                                  a.stream))
+                                  a.stream, a.rf))
     return rc;
   const int grid = wm::sm_count() * 2;
   if (tc) {
     if (cudaMemsetAsync(ws.counters + 3, 0, sizeof(int32_t), a.stream) != cudaSuccess)
       return wm::fail(WM_ERR_CUDA, "experts: memset failed");
-    if (int rc = wm::launch_gather_f16(a.x, ws.perm, S, kk, a.H, ws.x16, a.stream)) return rc;
+    if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream)) return rc;
     if (int rc = wm::launch_tc_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x16, ws.s_pad, a.order, a.limit, ws.tiles,
                                   ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream))
       return rc;
@@ -325,9 +337,12 @@ int run(const Args &a, int fmt) {
   }
   if (int rc = wm::check_launch("expert gemv")) return rc;
   const int cgrid = wm::sm_count() * 8;
-  if (a.reduce)
-    k_combine<<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk, a.H,
-                                           a.out);
+  if (a.reduce && a.out_f32)
+    k_combine<true><<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk,
+                                                 a.H, a.out_f32);
+  else if (a.reduce)
+    k_combine<false><<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk,
+                                                  a.H, a.out);
   else
     k_unsort<<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, ws.counters + 1, S, a.H, a.out);
   return wm::check_launch("expert combine");
@@ -370,6 +385,25 @@ int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const float *we
   wm::clear_error();
   Args a{x, idx, weights, T, k, H, I, E, mx_view(w13, s13, 2 * I, H), mx_view(w2, s2, H, I), gate_up_order,
          swiglu_limit, shared_expert, shared_w, out, true, workspace, ws_bytes, stream};
+  return run(a, kFmtMxfp4);
+}
+
+int wmoe_mxfp4_moe_forward_ep(const wm_bf16 *x, const int32_t *idx, const float *weights, int T, int k, int H, int I,
+                              int E_local, int n_routed, int route_base, int route_count, const uint8_t *w13,
+                              const uint8_t *s13, const uint8_t *w2, const uint8_t *s2, int gate_up_order,
+                              float swiglu_limit, int shared_expert, const float *shared_w, int shared_lo,
+                              int shared_hi, float *out, void *workspace, size_t ws_bytes, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(route_count >= 1 && route_base >= 0 && route_base + route_count <= n_routed,
+             "moe_forward_ep: need 1 <= route_count and [route_base, route_base + route_count) inside [0, n_routed)");
+  WM_REQUIRE(route_count <= E_local && (shared_expert < 0 || shared_expert >= route_count),
+             "moe_forward_ep: local experts are [0, route_count) routed, then the shared expert");
+  WM_REQUIRE(shared_lo >= 0 && shared_lo <= shared_hi && shared_hi <= T, "moe_forward_ep: need 0 <= shared_lo <= shared_hi <= T");
+  WM_REQUIRE(out != nullptr, "moe_forward_ep: null output");
+  Args a{x, idx, weights, T, k, H, I, E_local, mx_view(w13, s13, 2 * I, H), mx_view(w2, s2, H, I), gate_up_order,
+         swiglu_limit, shared_expert, shared_w, nullptr, true, workspace, ws_bytes, stream};
+  a.rf = wm::RouteFilter{route_base, route_count, n_routed, shared_lo, shared_hi};
+  a.out_f32 = out;
   return run(a, kFmtMxfp4);
 }
 

@@ -537,10 +537,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // x16[p, :] = f16(x[perm[p] / kk, :] * 2^-4): the up projection's B operand in expert order
-__global__ void k_gather_f16(const uint16_t *__restrict__ x, const int32_t *__restrict__ perm, int S, int kk, int H,
-                             __half *__restrict__ x16) {
+__global__ void k_gather_f16(const uint16_t *__restrict__ x, const int32_t *__restrict__ perm,
+                             const int32_t *__restrict__ count, int S, int kk, int H, __half *__restrict__ x16) {
   const int per = H / 8;
-  const int64_t total = static_cast<int64_t>(S) * per;
+  const int rows = min(S, max(0, *count));   // kept assignments (all of them unless an expert range drops some)
+  const int64_t total = static_cast<int64_t>(rows) * per;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int pidx = static_cast<int>(i / per), c = static_cast<int>(i % per) * 8;
     const int tok = perm[pidx] / kk;
@@ -648,10 +649,11 @@ bool tc_supported(int H, int I) { return H % 256 == 0 && I % 256 == 0; }
 
 int tc_tile_n(int T) { return T <= DecodeCfg::kNMax ? DecodeCfg::kNMax : PrefillCfg::kNMax; }
 
-int launch_gather_f16(const uint16_t *x, const int32_t *perm, int S, int kk, int H, void *x16, cudaStream_t stream) {
+int launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *count, int S, int kk, int H, void *x16,
+                      cudaStream_t stream) {
   const int64_t work = static_cast<int64_t>(S) * (H / 8);
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
-  if (grid > 0) k_gather_f16<<<grid, 256, 0, stream>>>(x, perm, S, kk, H, static_cast<__half *>(x16));
+  if (grid > 0) k_gather_f16<<<grid, 256, 0, stream>>>(x, perm, count, S, kk, H, static_cast<__half *>(x16));
   return check_launch("gather f16");
 }
 

@@ -19,7 +19,7 @@
 namespace {
 
 __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ idx, int T, int k, int shared_expert,
-                                                  int E, int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
+                                                  wm::RouteFilter rf, int E, int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
                                                   int32_t *__restrict__ inv, int32_t *__restrict__ active,
                                                   int32_t *__restrict__ n_active, int32_t *__restrict__ error_flag,
                                                   int4 *__restrict__ tiles, int32_t *__restrict__ n_tiles, int tile_n) {
@@ -36,14 +36,26 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
   __syncthreads();
   const int seg = (S + nw - 1) / nw;
   const int s0 = warp * seg, s1 = min(S, s0 + seg);
+  // expert of assignment a, kBad for an id outside the layer's experts.  With
+  // a route filter (rf.count > 0, an expert-parallel rank's share) routed ids
+  // in [rf.base, rf.base + rf.count) are kept as id - rf.base; other ids in
+  // [0, rf.n_global), and shared slots of tokens outside
+  // [rf.shared_lo, rf.shared_hi), are kDropped.
+  constexpr int kBad = -1, kDropped = -2;
   auto expert_of = [&](int a) -> int {
     int t = a / kk, j = a - t * kk;
-    int e = j < k ? idx[static_cast<int64_t>(t) * k + j] : shared_expert;
-    return e;
+    if (j >= k) return (rf.count > 0 && (t < rf.shared_lo || t >= rf.shared_hi)) ? kDropped : shared_expert;
+    int e = idx[static_cast<int64_t>(t) * k + j];
+    if (rf.count > 0) {
+      if (e < 0 || e >= rf.n_global) return kBad;
+      return (e >= rf.base && e < rf.base + rf.count) ? e - rf.base : kDropped;
+    }
+    return (e < 0 || e >= E) ? kBad : e;
   };
   for (int a = s0 + lane; a < s1; a += 32) {
     int e = expert_of(a);
-    if (e < 0 || e >= E) {
+    if (e == kDropped) continue;
+    if (e == kBad) {
       bad = 1;
       continue;
     }
@@ -127,8 +139,9 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
   const unsigned lt_mask = (1u << lane) - 1u;
   for (int a0 = s0; a0 < s1; a0 += 32) {
     int a = a0 + lane;
-    bool valid = a < s1;
-    int e = valid ? expert_of(a) : -1;
+    int e = a < s1 ? expert_of(a) : -1;
+    if (a < s1 && e == kDropped) inv[a] = -1;
+    const bool valid = a < s1 && e >= 0;
     unsigned peers = __match_any_sync(0xffffffffu, e);
     int rank = __popc(peers & lt_mask);
     int base = valid ? hist[warp * E + e] : 0;
@@ -158,15 +171,15 @@ int permute_warps(int E) {
 
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
                    int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
-                   int32_t *n_tiles, int tile_n, cudaStream_t stream) {
+                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf) {
   const int nw = permute_warps(E);
   const size_t smem = permute_smem_bytes(E, nw);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("permute smem: ") + cudaGetErrorString(e));
   }
-  k_permute<<<1, nw * 32, smem, stream>>>(idx, T, k, shared_expert, E, offsets, perm, inv, active, n_active, error_flag,
-                                          tiles, n_tiles, tile_n);
+  k_permute<<<1, nw * 32, smem, stream>>>(idx, T, k, shared_expert, rf, E, offsets, perm, inv,
+                                          active, n_active, error_flag, tiles, n_tiles, tile_n);
   return check_launch("permute");
 }
 

@@ -8,16 +8,26 @@
 
 namespace wm {
 
+// Expert-parallel share of one rank: routed ids in [base, base + count) are
+// this rank's local experts 0..count-1, other ids in [0, n_global) are
+// dropped, and only tokens in [shared_lo, shared_hi) get a shared-expert
+// slot.  count == 0 means no filter (the whole layer on one device).
+struct RouteFilter {
+  int base = 0, count = 0, n_global = 0, shared_lo = 0, shared_hi = 0;
+};
+
 // permute.cu.  With tiles != nullptr it also emits the tensor-core work list:
 // {expert, first slot, tokens (<= tile_n), 0} per tile, count in *n_tiles.
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
                    int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
-                   int32_t *n_tiles, int tile_n, cudaStream_t stream);
+                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf = RouteFilter{});
 
 // moe_tc.cu
 bool tc_supported(int H, int I);
 int tc_tile_n(int T);  // tokens per tile: 64 for decode batches (T <= 64), else 128
-int launch_gather_f16(const uint16_t *x, const int32_t *perm, int S, int kk, int H, void *x16, cudaStream_t stream);
+// rows [0, *count) of the expert-ordered token matrix (count = offsets[E] on the device)
+int launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *count, int S, int kk, int H, void *x16,
+                      cudaStream_t stream);
 int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
                  float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, int tile_n,
                  cudaStream_t stream);

@@ -20,6 +20,15 @@ replicated.  One forward on each rank's own tokens:
 Remote rows always land in local HBM through the collective before a kernel
 reads them: no kernel touches another GPU's memory.  The local expert compute
 is a callable so the same exchange logic runs on CPU ranks (gloo) in tests.
+
+``GatheredExpertParallelMoE`` is the decode form: with a few tokens per rank
+the all-to-all's data-dependent splits (a device-to-host read of the counts)
+cost more than the rows they move, so every rank all-gathers all ranks' tokens
+and routes, runs its expert share over all of them with float32 partial sums
+(``wmoe_mxfp4_moe_forward_ep``: other ranks' experts skipped, the shared
+expert only for its own tokens) and a reduce-scatter adds the partials back
+onto the owning rank.  Every collective has a fixed size, so one decode step
+of the layer is capturable as a CUDA graph.
 """
 from __future__ import annotations
 
@@ -100,6 +109,73 @@ class ExpertParallelMoE:
         if self.shared is not None:
             out = out + self.shared(x).float()
         return out.to(torch.bfloat16)
+
+
+def _all_gather(t: torch.Tensor, world: int, group=None) -> torch.Tensor:
+    out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_gather_into_tensor(out, t.contiguous(), group=group)
+    return out
+
+
+def _reduce_scatter(t: torch.Tensor, world: int, rank: int, group=None) -> torch.Tensor:
+    """Sum of ``t`` [world*B, ...] over the ranks, rows [rank*B, (rank+1)*B) kept."""
+    B = t.shape[0] // world
+    if dist.get_backend(group) == "nccl":
+        out = torch.empty((B,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+        dist.reduce_scatter_tensor(out, t.contiguous(), group=group)
+        return out
+    s = t.clone()   # backends without reduce-scatter (gloo on CPU ranks)
+    dist.all_reduce(s, group=group)
+    return s[rank * B:(rank + 1) * B]
+
+
+class GatheredExpertParallelMoE:
+    """Decode form of the expert-parallel layer (fixed-size collectives only).
+
+    ``router(x) -> (weights f32 [B, k], idx int32 [B, k][, shared_w f32 [B]])``
+    with global expert ids; ``partial(xg, idxg, wg, swg, rows) -> f32 [W*B, H]``
+    is this rank's share over all ranks' tokens (``gpu_partial_experts``),
+    with the shared expert applied to rows [lo, hi) only.  Every rank must
+    call with the same B."""
+
+    def __init__(self, router, partial, n_routed: int, group=None):
+        self.router = router
+        self.partial = partial
+        self.n_routed = n_routed
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.e0, self.per = shard_bounds(n_routed, self.world, self.rank)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        B, H = x.shape
+        r = self.router(x)
+        w, idx = r[0], r[1]
+        sw = r[2] if len(r) > 2 else None
+        k = idx.shape[-1]
+        cols = [idx.reshape(B, k).to(torch.int32), w.reshape(B, k).float().contiguous().view(torch.int32)]
+        if sw is not None:
+            cols.append(sw.reshape(B, 1).float().contiguous().view(torch.int32))
+        routes = _all_gather(torch.cat(cols, 1), self.world, self.group)
+        xg = _all_gather(x, self.world, self.group)
+        idxg = routes[:, :k].contiguous()
+        wg = routes[:, k:2 * k].contiguous().view(torch.float32)
+        swg = routes[:, 2 * k].contiguous().view(torch.float32) if sw is not None else None
+        part = self.partial(xg, idxg, wg, swg, (self.rank * B, (self.rank + 1) * B))
+        return _reduce_scatter(part, self.world, self.rank, self.group).to(torch.bfloat16)
+
+
+def gpu_partial_experts(experts, e0: int, per: int, n_routed: int, swiglu_limit: float = 0.0,
+                        has_shared: bool = True):
+    """This rank's share on the device: ``experts`` from ``shard_experts``
+    (routed [e0, e0+per) as 0..per-1, then the shared expert)."""
+    from . import experts as X
+
+    def run(xg, idxg, wg, swg, rows):
+        return X.experts_forward(xg, idxg, experts, weights=wg, shared_expert=per if has_shared else -1,
+                                 shared_w=swg, swiglu_limit=swiglu_limit, expert_range=(e0, per, n_routed),
+                                 shared_rows=rows)
+    return run
 
 
 def gpu_local_experts(experts, swiglu_limit: float = 0.0):

@@ -205,12 +205,20 @@ def _mx_args(w13, s13, w2, s2):
 
 
 def experts_forward(x, indices, experts, *, order=None, swiglu_limit: float = 0.0, weights=None,
-                    shared_expert: int = -1, shared_w=None, out=None, workspace=None):
+                    shared_expert: int = -1, shared_w=None, out=None, workspace=None, expert_range=None,
+                    shared_rows=None):
     """Grouped expert FFN on the device.
 
     ``weights is None``  -> un-reduced [..., k, H] (switch_mlp semantics);
     otherwise            -> [..., H] = sum_j w_j FFN_{idx_j}(x) (+ shared).
     ``experts``: BatchedExperts / QwenBatchedExperts (MXFP4) or Affine4BatchedExperts.
+
+    ``expert_range=(base, count, n_routed)`` (MXFP4, with weights): one
+    expert-parallel rank's share -- ``experts`` holds global routed experts
+    [base, base+count) as local 0..count-1 (then the shared expert), other
+    global ids are skipped, the shared expert runs only for rows in
+    ``shared_rows=(lo, hi)`` (default all), and the result is the float32
+    partial sum [..., H] that a reduce over the ranks completes.
     """
     if x.dtype != torch.bfloat16:
         raise ValueError("expert input must be bf16")
@@ -245,11 +253,23 @@ def experts_forward(x, indices, experts, *, order=None, swiglu_limit: float = 0.
     has_shared = shared_expert is not None and shared_expert >= 0
     nbytes = workspace_size(T, k, H, I, E, has_shared)
     ws = workspace if workspace is not None else _WS.get(dev, nbytes)
-    if out is None:
-        out = torch.empty((T, H) if reduce else (T, k, H), dtype=torch.bfloat16, device=dev)
     wts = weights.reshape(-1, k).float().contiguous() if reduce else None
     sw = shared_w.reshape(-1).float().contiguous() if shared_w is not None else None
     st = L.stream_of(xf)
+    if expert_range is not None:
+        if fmt != "mxfp4" or not reduce:
+            raise ValueError("expert_range needs MXFP4 experts and routing weights")
+        base, count, n_routed = (int(v) for v in expert_range)
+        lo, hi = (0, T) if shared_rows is None else (int(shared_rows[0]), int(shared_rows[1]))
+        if out is None:
+            out = torch.empty((T, H), dtype=torch.float32, device=dev)
+        L.require_cuda(xf, idx, w13, s13, w2, s2, out, wts, sw)
+        L.call("wmoe_mxfp4_moe_forward_ep", L.ptr(xf), L.ptr(idx), L.ptr(wts), T, k, H, I, E, n_routed, base, count,
+               L.ptr(w13), L.ptr(s13), L.ptr(w2), L.ptr(s2), order, float(swiglu_limit),
+               shared_expert if has_shared else -1, L.ptr(sw), lo, hi, L.ptr(out), L.ptr(ws), ws.numel(), st)
+        return out.reshape(*x.shape[:-1], H)
+    if out is None:
+        out = torch.empty((T, H) if reduce else (T, k, H), dtype=torch.bfloat16, device=dev)
     if fmt == "mxfp4":
         L.require_cuda(xf, idx, w13, s13, w2, s2, out, wts, sw)
         if reduce:
