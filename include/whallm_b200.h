@@ -89,6 +89,17 @@ WM_API int wmxfp4_quantize(const wm_bf16 *src, int64_t rows, int64_t cols, uint8
 WM_API int wmxfp4_dequantize(const uint8_t *packed, const uint8_t *scales, int64_t rows, int64_t cols,
                       int out_dtype, void *out, wm_stream_t stream);
 
+/* Exact two-term e4m3 form of bf16 rows, the token operand of the
+ * block-scaled expert kernels: for each 32-value block, scale byte
+ * s = clamp(exponent(block max) - 7, -122) + 127 (E8M0), hi = e4m3(x / 2^(s-127))
+ * and lo = e4m3((x / 2^(s-127) - hi) * 2^5), both round-to-nearest-even, so
+ * x = 2^(s-127) * (hi + 2^-5 * lo) exactly for every element within 2^-14 of
+ * its block maximum.  hi, lo [rows, cols] u8, scales [rows, cols/32] u8.
+ * No reference counterpart (an internal operand format); exported so the
+ * decomposition can be checked bit for bit. */
+WM_API int wmx_split_e4m3(const wm_bf16 *x, int rows, int cols, uint8_t *hi, uint8_t *lo, uint8_t *scales,
+                   wm_stream_t stream);
+
 /* ------------------------------------------------------ affine 4-bit ------ */
 
 /* MLX-style affine 4-bit quantize, group `group` (64 or 32) along cols:

@@ -426,3 +426,42 @@ def fake_quant(x_f32: np.ndarray, kind: str) -> np.ndarray:
 
 
 PACKED_KIND_TO_FMT = {"fp8_ue8m0": KV_FP8_UE8M0_B32, "fp4_e4m3": KV_FP4_E4M3_B16, "fp4_ue8m0": KV_FP4_UE8M0_B32}
+
+
+# --------------------------------------------------------------------------
+# two-term e4m3 operand form (block-scaled expert kernels)
+# --------------------------------------------------------------------------
+
+LO_SHIFT = 5
+
+
+def split_e4m3(x_bits):
+    """bf16 bits [rows, cols] -> (hi, lo, scales) u8, the token operand of the
+    block-scaled expert path (not a reference format: the decomposition that
+    lets MXFP4 weights meet bf16 activations on e4m3 tensor-core inputs).
+
+    Per 32 values: sh = max(exponent(block max) - 7, -122) so that
+    block max / 2^sh lies in [128, 256); hi = e4m3(x / 2^sh) and
+    lo = e4m3((x / 2^sh - hi) * 2^5), round to nearest even; scale = sh + 127."""
+    b = np.asarray(x_bits, np.uint16)
+    rows, cols = b.shape
+    x = bf16_bits_to_f32(b).reshape(rows, cols // 32, 32)
+    amax = (x.view(np.uint32) & np.uint32(0x7FFFFFFF)).max(axis=-1)
+    ebits = np.minimum(amax >> np.uint32(23), np.uint32(255)).astype(np.int64)
+    sh = np.maximum(ebits - 134, -122)
+    inv = ((127 - sh).astype(np.uint32) << np.uint32(23)).view(np.float32)
+    xs = (x * inv[..., None]).astype(np.float32)
+    hi = f32_to_e4m3(xs)
+    r = ((xs - e4m3_to_f32(hi)) * np.float32(2.0 ** LO_SHIFT)).astype(np.float32)
+    lo = f32_to_e4m3(r)
+    return hi.reshape(rows, cols), lo.reshape(rows, cols), (sh + 127).astype(np.uint8)
+
+
+def join_e4m3(hi, lo, scales):
+    """Inverse of ``split_e4m3``: float32 values 2^(s-127) * (hi + 2^-5 * lo)."""
+    hi = np.asarray(hi, np.uint8)
+    rows, cols = hi.shape
+    s = np.asarray(scales, np.int64).repeat(32, axis=1)
+    v = e4m3_to_f32(hi).astype(np.float64) + e4m3_to_f32(lo).astype(np.float64) * 2.0 ** -LO_SHIFT
+    return (v * np.exp2((s - 127).astype(np.float64))).astype(np.float32)
+

@@ -38,6 +38,7 @@ SIGNATURES = {
     "w_abi_version": [],
     "wmxfp4_quantize": [_P, _I64, _I64, _P, _P, _P],
     "wmxfp4_dequantize": [_P, _P, _I64, _I64, _I, _P, _P],
+    "wmx_split_e4m3": [_P, _I, _I, _P, _P, _P, _P],
     "waffine4_quantize": [_P, _I64, _I64, _I, _P, _P, _P, _P],
     "waffine4_dequantize": [_P, _P, _P, _I64, _I64, _I, _I, _P, _P],
     "wkv_quantize": [_P, _I64, _I, _I, _P, _P, _P],

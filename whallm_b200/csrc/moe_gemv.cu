@@ -288,10 +288,15 @@ int check_common(const Args &a) {
   return WM_OK;
 }
 
-// WM_EXPERT_PATH=simt forces the CUDA-core GEMV for MXFP4 experts (A/B checks).
-bool force_simt() {
+// WM_EXPERT_PATH selects the MXFP4 expert path for A/B checks: "simt" (CUDA
+// cores), "f16" (tcgen05 kind::f16 with in-kernel dequantization); default:
+// the block-scaled tcgen05 path.
+enum class MxPath { kBlockScaled, kF16, kSimt };
+MxPath mx_path() {
   const char *v = getenv("WM_EXPERT_PATH");
-  return v && v[0] == 's';
+  if (v && v[0] == 's') return MxPath::kSimt;
+  if (v && v[0] == 'f') return MxPath::kF16;
+  return MxPath::kBlockScaled;
 }
 
 int run(const Args &a, int fmt) {
@@ -303,14 +308,30 @@ int run(const Args &a, int fmt) {
   if (a.T == 0) return WM_OK;
   const int kk = a.k + has_shared;
   const int S = a.T * kk;
-  const bool tc = fmt == kFmtMxfp4 && wm::tc_supported(a.H, a.I) && !force_simt();
-  const int tile_n = wm::tc_tile_n(a.T);
+  const MxPath path = mx_path();
+  const bool mx = fmt == kFmtMxfp4 && path == MxPath::kBlockScaled && wm::mx_supported(a.H, a.I);
+  const bool tc = fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I);
+  const int tile_n = mx ? wm::mx_tile_n(a.T) : wm::tc_tile_n(a.T);
   if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
-                                  ws.counters, ws.counters + 1, tc ? ws.tiles : nullptr, ws.counters + 2, tile_n,
-                                  a.stream, a.rf))
+                                  ws.counters, ws.counters + 1, (tc || mx) ? ws.tiles : nullptr, ws.counters + 2,
+                                  tile_n, a.stream, a.rf))
     return rc;
   const int grid = wm::sm_count() * 2;
-  if (tc) {
+  if (mx) {
+    if (cudaMemsetAsync(ws.counters + 3, 0, sizeof(int32_t), a.stream) != cudaSuccess)
+      return wm::fail(WM_ERR_CUDA, "experts: memset failed");
+    const int32_t *count = ws.offsets + a.E;
+    if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
+      return rc;
+    if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, ws.s_pad, a.order,
+                                  a.limit, ws.tiles, ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream))
+      return rc;
+    if (int rc = wm::launch_split_e4m3(ws.h, nullptr, count, S, 1, a.I, ws.h_hi, ws.h_lo, ws.h_sc, a.stream))
+      return rc;
+    if (int rc = wm::launch_mx_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h_hi, ws.h_lo, ws.h_sc, ws.s_pad, ws.tiles,
+                                    ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream))
+      return rc;
+  } else if (tc) {
     if (cudaMemsetAsync(ws.counters + 3, 0, sizeof(int32_t), a.stream) != cudaSuccess)
       return wm::fail(WM_ERR_CUDA, "experts: memset failed");
     if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream)) return rc;

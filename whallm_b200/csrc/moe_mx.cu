@@ -1,0 +1,588 @@
+// Grouped MXFP4 expert GEMM on block-scaled tcgen05 tensor cores.
+//
+// Reference: the MLX gather_qmm / quantized_matmul expert math
+// (model.py:393-481, qwen4_exp.py:588-678): y = x @ dequant(W)^T per routed
+// (token, expert) pair, W in MXFP4 (e2m1 + E8M0 per 32 along K).
+//
+// The weights go to the tensor core as they are stored: TMA expands each
+// 128-value e2m1 row segment into the padded shared-memory form the MMA reads
+// (CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B) and the MXFP4 E8M0 bytes become the
+// MMA's A scale factors, so nothing dequantizes the weights in software.
+//
+//   tcgen05.mma.kind::mxf8f6f4.block_scale  D[f32, TMEM] += (A * sa) x (B * sb)
+//   A  e2m1 weights, 128 rows x 32 K per instruction, scale sa per 32 K (the
+//      weight's own E8M0 byte)
+//   B  the tokens as two e4m3 terms, x = sb_hi * hi + sb_hi * 2^-5 * lo, with
+//      one E8M0 scale per (token, 32 K) chosen so the block maximum lands in
+//      [128, 256).  For bf16 inputs the two terms are exact for every element
+//      within 2^-14 of its block maximum (8 significant bits = 4 + 4) and off
+//      by at most 2^-22 of the block maximum below that, so the product is the
+//      bf16 x MXFP4 product of the reference up to f32 accumulation order.
+//      Each K-block issues two MMAs (hi, lo) into the same accumulator; the
+//      8-bit kind runs at twice the 16-bit rate, so this costs the tensor time
+//      of one f16 MMA.
+//
+// Orientation ("swap AB"): M = 128 weight rows, N = the tokens routed to one
+// expert (16..NMAX per tile), K = reduction.  The up projection's 128 rows
+// are 64 up and 64 gate rows interleaved in groups of 8 by a 4-D tensor map,
+// so lanes m and m ^ 8 of one warp hold up_j and gate_j for the fused
+// ClampedSwiGLU epilogue; its bf16 output is split into e4m3 terms again for
+// the down projection.
+//
+// Warp roles (384 threads, one CTA per SM, persistent over (tile, 128-row)
+// work items):
+//   warp 0      TMA producer (weights, token terms)
+//   warp 1      MMA issuer: tcgen05.cp of the stage's scale factors into
+//               TMEM, then 2 x KC/32 MMAs (the copy and the MMAs of one
+//               thread execute in issue order)
+//   warp 2      TMEM allocator
+//   warps 4-7   scale warps: per stage they read the rows' E8M0 bytes from
+//               global memory (prefetched four stages ahead) and write them in
+//               the 32 x 16-byte layout that tcgen05.cp.32x128b.warpx4 takes
+//   warps 8-11  epilogue (TMEM lanes 0-127)
+// Every mbarrier wait is bounded and records an error code instead of hanging.
+#include "wm_common.cuh"
+#include "wm_moe.cuh"
+#include "wm_tc.cuh"
+
+namespace {
+
+using namespace wm_tc;
+
+constexpr int kM = 128;
+constexpr int kKH = 128;                 // K values per TMA box row and per scale-factor group
+constexpr int kMxThreads = 384;
+constexpr int kLoShift = 5;              // lo term scale = hi scale * 2^-5
+constexpr uint32_t kLoSub = 0x01010101u * kLoShift;   // E8M0 bytes of the lo term, four at a time
+
+template <int KC, int NMAX, int STAGES>
+struct MxCfg {
+  static constexpr int kKC = KC;
+  static constexpr int kNMax = NMAX;
+  static constexpr int kStages = STAGES;
+  static constexpr int kHalves = KC / kKH;                   // 128-K groups per stage
+  static constexpr int kABox = kM * kKH;                     // 16 KB: 128 rows x 128 padded bytes
+  static constexpr int kAStage = kHalves * kABox;
+  static constexpr int kBBox = NMAX * kKH;                   // NMAX rows x 128 B, one (term, group)
+  static constexpr int kBStage = 2 * kHalves * kBBox;
+  static constexpr int kSFStage = ((3 * kHalves * 512 + 1023) / 1024) * 1024;  // A, B hi, B lo atoms
+  static constexpr int kSfCol0 = 2 * NMAX;                   // after the two accumulators
+  static constexpr int kSfCols = 3 * kHalves * 4;
+  static constexpr int kColsUsed = kSfCol0 + kSfCols;
+  static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
+                                 : kColsUsed <= 256 ? 256 : 512;
+  static constexpr size_t kSmem =
+      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 4) * 8 + 16;
+  static_assert(KC % kKH == 0, "stage depth must be a multiple of 128");
+  static_assert(NMAX % 16 == 0 && NMAX <= 128, "tile width");
+  static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
+  static_assert(kSmem <= 232448, "shared memory");
+  static_assert(kColsUsed <= 512, "TMEM columns");
+};
+using MxDecode = MxCfg<256, 32, 4>;
+using MxPrefill = MxCfg<128, 128, 4>;
+
+struct MxParams {
+  int mode;                  // 0: up projection (+ClampedSwiGLU -> h bf16), 1: down projection (-> y f32)
+  int K;                     // reduction length
+  int rows;                  // weight rows per expert
+  int I, H;
+  int order;                 // WM_UP_GATE / WM_GATE_UP
+  float limit;
+  int m_tiles;               // 128-row work items per tile
+  const uint8_t *a_scales;   // [E * rows, K/32] E8M0 (the MXFP4 scales)
+  const uint8_t *b_scales;   // [S_pad, K/32] hi-term E8M0 in slot order
+  const int4 *tiles;         // {expert, first slot, tokens, 0}
+  const int32_t *n_tiles;
+  uint16_t *h_out;           // up: [S_pad, I] bf16
+  float *y_out;              // down: [S, H] f32
+  int32_t *err;
+};
+
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
+                                            uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Block-scaled instruction descriptor: A e2m1, B e4m3, E8M0 scales, f32 D,
+// K-major A and B, M = 128, N = n, scale-factor byte ids for A and B = j.
+__device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t j) {
+  return (j << 4) | (5u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) |
+         (static_cast<uint32_t>(kM >> 4) << 24) | (j << 29);
+}
+
+__device__ __forceinline__ void tc_mma_mx(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
+                                          uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+
+// 512-byte scale-factor atom (32 rows of 16 bytes, no swizzle) as the source
+// descriptor of tcgen05.cp: 8-row core matrices 128 B apart.
+__device__ __forceinline__ uint64_t sdesc_atom(uint32_t saddr) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (static_cast<uint64_t>(128 >> 4) << 32) |
+         (1ull << 46);
+}
+
+// Atom -> TMEM: source row i (16 bytes) goes to lane i of every 32-lane
+// quadrant, columns +0..+3; column a then holds the 4 K-block scales of
+// matrix row 32a + i.
+__device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+__device__ __forceinline__ float silu_mx(float g) { return g / (1.0f + expf(-g)); }
+
+template <class C>
+__global__ void __launch_bounds__(kMxThreads, 1)
+    k_expert_mx(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
+                const __grid_constant__ CUtensorMap tmBl, MxParams p) {
+  constexpr int S = C::kStages;
+  constexpr int HV = C::kHalves;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = smem;                                   // S x kAStage
+  uint8_t *sB = sA + S * C::kAStage;                    // S x kBStage: [term][group] boxes
+  uint8_t *sF = sB + S * C::kBStage;                    // S x kSFStage: [A | B hi | B lo][group] atoms
+  uint64_t *bars = reinterpret_cast<uint64_t *>(sF + S * C::kSFStage);
+  uint64_t *full = bars;                                // [S]: TMA bytes + 128 scale-thread arrivals
+  uint64_t *empty = full + S;                           // [S]: MMA commit
+  uint64_t *dfull = empty + S;                          // [2]
+  uint64_t *dempty = dfull + 2;                         // [2]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dempty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128); }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(C::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int n_items = (*p.n_tiles) * p.m_tiles;
+  const int kstages = p.K / C::kKC;
+  const int ks32 = p.K / 32;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      const int4 tile = p.tiles[item / p.m_tiles];
+      const int m = item % p.m_tiles;
+      const int nb = (tile.z + 15) >> 4;                // 16-row token boxes
+      for (int kc = 0; kc < kstages; ++kc, ++g) {
+        const int s = g % S;
+        if (!(ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 1))) break;
+        if (elect_one()) {
+          // transaction bytes count the packed global bytes of the weights
+          mbar_expect_tx(&full[s], HV * (kM * kKH / 2) + 2 * HV * nb * 16 * kKH);
+          for (int q = 0; q < HV; ++q) {
+            const int x = kc * C::kKC + q * kKH;
+            uint8_t *a = sA + s * C::kAStage + q * C::kABox;
+            if (p.mode == 0)
+              tma_load_4d(a, &tmA, x, 0, 0, tile.x * (p.I / 4) + m * 8, &full[s]);
+            else
+              tma_load_2d(a, &tmA, x, tile.x * p.rows + m * kM, &full[s]);
+            for (int j = 0; j < nb; ++j) {
+              tma_load_2d(sB + s * C::kBStage + q * C::kBBox + j * 16 * kKH, &tmBh, x, tile.y + 16 * j, &full[s]);
+              tma_load_2d(sB + s * C::kBStage + (HV + q) * C::kBBox + j * 16 * kKH, &tmBl, x, tile.y + 16 * j,
+                          &full[s]);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+    for (uint32_t q = 0; q < S && q < g && ok; ++q) {
+      const uint32_t gg = g - 1 - q;
+      ok = mbar_wait(&empty[gg % S], (gg / S) & 1, p.err, 2);
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------- MMA
+    const uint32_t sfa = tmem + C::kSfCol0;
+    const uint32_t sfbh = sfa + HV * 4;
+    const uint32_t sfbl = sfbh + HV * 4;
+    uint32_t g = 0, it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+      const int4 tile = p.tiles[item / p.m_tiles];
+      const int n_mma = max(16, (tile.z + 15) & ~15);
+      const int db = it & 1;
+      if (!(ok = mbar_wait(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
+      tc_fence_after();
+      const uint32_t d_addr = tmem + db * C::kNMax;
+      for (int kc = 0; kc < kstages && ok; ++kc, ++g) {
+        const int s = g % S;
+        if (!(ok = mbar_wait(&full[s], (g / S) & 1, p.err, 4))) break;
+        tc_fence_after();
+        if (elect_one()) {
+          const uint32_t f0 = smem_u32(sF + s * C::kSFStage);
+#pragma unroll
+          for (int q = 0; q < HV; ++q) {
+            tc_cp_sf(sfa + 4 * q, sdesc_atom(f0 + q * 512));
+            tc_cp_sf(sfbh + 4 * q, sdesc_atom(f0 + (HV + q) * 512));
+            tc_cp_sf(sfbl + 4 * q, sdesc_atom(f0 + (2 * HV + q) * 512));
+          }
+          const uint32_t a0 = smem_u32(sA + s * C::kAStage);
+          const uint32_t bh0 = smem_u32(sB + s * C::kBStage);
+          const uint32_t bl0 = bh0 + HV * C::kBBox;
+#pragma unroll
+          for (int kb = 0; kb < C::kKC / 32; ++kb) {
+            const int q = kb >> 2;
+            const uint32_t j = kb & 3;
+            const uint64_t ad = bdesc_sw128(a0 + q * C::kABox) + 2 * j;
+            const uint64_t bhd = bdesc_sw128(bh0 + q * C::kBBox) + 2 * j;
+            const uint64_t bld = bdesc_sw128(bl0 + q * C::kBBox) + 2 * j;
+            const uint32_t idesc = idesc_mx(n_mma, j);
+            const uint32_t sa = (j << 30) | (sfa + 4 * q);
+            tc_mma_mx(d_addr, ad, bhd, idesc, sa, (j << 30) | (sfbh + 4 * q), (kc == 0 && kb == 0) ? 0u : 1u);
+            tc_mma_mx(d_addr, ad, bld, idesc, sa, (j << 30) | (sfbl + 4 * q), 1u);
+          }
+          tc_commit(&empty[s]);
+        }
+        __syncwarp();
+      }
+      if (ok) {
+        if (elect_one()) tc_commit(&dfull[db]);
+        __syncwarp();
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ------------------------------------------------------- scale warps
+    // Thread t owns row t of the A atom (weight row of the work item) and row
+    // t of the B atoms (token t of the tile; zero past the tile's tokens).
+    const int t = threadIdx.x - 128;
+    const int o = (t & 31) * 4 + (t >> 5);              // 32-bit word of row t inside an atom
+    struct Ent {
+      uint32_t a[HV];
+      uint32_t b[HV];
+    };
+    int c_item = blockIdx.x, c_kc = 0;                  // prefetch cursor
+    auto fetch = [&](Ent &e) {
+#pragma unroll
+      for (int q = 0; q < HV; ++q) { e.a[q] = 0u; e.b[q] = 0u; }
+      if (c_item >= n_items) return;
+      const int4 tile = p.tiles[c_item / p.m_tiles];
+      const int m = c_item % p.m_tiles;
+      const int grow = p.mode == 0 ? ((t >> 3) & 1) * p.I + m * 64 + (t >> 4) * 8 + (t & 7) : m * kM + t;
+      const uint32_t *ap = reinterpret_cast<const uint32_t *>(
+          p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_kc * (C::kKC / 32));
+#pragma unroll
+      for (int q = 0; q < HV; ++q) e.a[q] = __ldg(ap + q);
+      if (t < tile.z) {
+        const uint32_t *bp = reinterpret_cast<const uint32_t *>(
+            p.b_scales + static_cast<int64_t>(tile.y + t) * ks32 + c_kc * (C::kKC / 32));
+#pragma unroll
+        for (int q = 0; q < HV; ++q) e.b[q] = __ldg(bp + q);
+      }
+      if (++c_kc == kstages) {
+        c_kc = 0;
+        c_item += gridDim.x;
+      }
+    };
+    Ent e0, e1, e2, e3;
+    fetch(e0);
+    fetch(e1);
+    fetch(e2);
+    fetch(e3);
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      for (int kc = 0; kc < kstages; ++kc, ++g) {
+        const Ent cur = e0;
+        e0 = e1;
+        e1 = e2;
+        e2 = e3;
+        fetch(e3);
+        const int s = g % S;
+        if (!(ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 9))) break;
+        uint32_t *f = reinterpret_cast<uint32_t *>(sF + s * C::kSFStage);
+#pragma unroll
+        for (int q = 0; q < HV; ++q) {
+          f[q * 128 + o] = cur.a[q];
+          f[(HV + q) * 128 + o] = cur.b[q];
+          f[(2 * HV + q) * 128 + o] = cur.b[q] ? cur.b[q] - kLoSub : 0u;
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(&full[s]);
+      }
+    }
+  } else if (warp >= 8) {
+    // ---------------------------------------------------------- epilogue
+    const int t = threadIdx.x - 256;                    // TMEM lane = tile row
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const int up_half = p.order == WM_UP_GATE ? 0 : 1;
+    const bool is_up = ((t >> 3) & 1) == up_half;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
+      const int4 tile = p.tiles[item / p.m_tiles];
+      const int m = item % p.m_tiles;
+      const int db = it & 1;
+      if (!(ok = mbar_wait(&dfull[db], (it >> 1) & 1, p.err, 8))) break;
+      tc_fence_after();
+      const int n = tile.z;
+      for (int c0 = 0; c0 < n; c0 += 16) {
+        uint32_t r[16];
+        WM_TMEM_LD16(tmem + lane_base + db * C::kNMax + c0, r);
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (p.mode == 0) {
+          const int jj = m * 64 + (t >> 4) * 8 + (t & 7);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float v = __uint_as_float(r[q]);
+            const float o = __shfl_xor_sync(0xffffffffu, v, 8);
+            if (is_up && c0 + q < n) {
+              float up = v, gate = o;
+              if (p.limit > 0.0f) {
+                up = fminf(fmaxf(up, -p.limit), p.limit);
+                gate = fminf(gate, p.limit);
+              }
+              p.h_out[static_cast<int64_t>(tile.y + c0 + q) * p.I + jj] = wm_f32_to_bf16(silu_mx(gate) * up);
+            }
+          }
+        } else {
+          const int row = m * kM + t;
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            if (c0 + q < n) p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = __uint_as_float(r[q]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&dempty[db]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+  }
+}
+
+// --------------------------------------------------------- two-term split
+
+__device__ __forceinline__ uint32_t e4m3x2(float first, float second) {  // first -> low byte
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(second), "f"(first));
+  return r;
+}
+
+__device__ __forceinline__ float2 e4m3x2_to_f32(uint32_t v) {  // .x <- low byte
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(v)));
+  return __half22float2(*reinterpret_cast<__half2 *>(&h2));
+}
+
+// Rows [0, rows) of a bf16 matrix (GATHER: row p is x[perm[p] / kk]) ->
+// hi, lo e4m3 bytes and the hi term's E8M0 scale per 32 columns.  Four
+// threads per 32-value block, eight values each.
+template <bool GATHER>
+__global__ void k_split_e4m3(const uint16_t *__restrict__ src, const int32_t *__restrict__ perm,
+                             const int32_t *__restrict__ count, int S, int kk, int K, uint8_t *__restrict__ hi,
+                             uint8_t *__restrict__ lo, uint8_t *__restrict__ sc) {
+  const int rows = count ? min(S, max(0, *count)) : S;
+  const int per_row = K / 8;
+  const int64_t total = static_cast<int64_t>(rows) * per_row;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;   // a multiple of 32
+  const int64_t span = (total + 31) / 32 * 32;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < span; i += stride) {
+    const bool live = i < total;
+    const int p = live ? static_cast<int>(i / per_row) : 0;
+    const int c = live ? static_cast<int>(i % per_row) : 0;
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (live) {
+      const int64_t srow = GATHER ? perm[p] / kk : p;
+      u = *reinterpret_cast<const uint4 *>(src + srow * K + c * 8);
+    }
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[2 * q] = wm_bf16lo(w[q]);
+      v[2 * q + 1] = wm_bf16hi(w[q]);
+    }
+    uint32_t amax = 0u;                                   // |v| bit patterns compare like the values
+#pragma unroll
+    for (int q = 0; q < 8; ++q) amax = max(amax, __float_as_uint(v[q]) & 0x7fffffffu);
+    amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+    amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+    const int ebits = static_cast<int>(min(amax >> 23, 255u));
+    const int sh = max(ebits - 134, -122);               // block max / 2^sh in [128, 256)
+    const float inv = __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+    uint32_t hb[4], lb[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float x0 = v[2 * q] * inv, x1 = v[2 * q + 1] * inv;
+      hb[q] = e4m3x2(x0, x1);
+      const float2 hf = e4m3x2_to_f32(hb[q]);
+      lb[q] = e4m3x2((x0 - hf.x) * static_cast<float>(1 << kLoShift), (x1 - hf.y) * static_cast<float>(1 << kLoShift));
+    }
+    if (live) {
+      const int64_t off = static_cast<int64_t>(p) * K + c * 8;
+      *reinterpret_cast<uint2 *>(hi + off) = make_uint2(hb[0] | (hb[1] << 16), hb[2] | (hb[3] << 16));
+      *reinterpret_cast<uint2 *>(lo + off) = make_uint2(lb[0] | (lb[1] << 16), lb[2] | (lb[3] << 16));
+      if ((c & 3) == 0) sc[static_cast<int64_t>(p) * (K / 32) + (c >> 2)] = static_cast<uint8_t>(sh + 127);
+    }
+  }
+}
+
+// ------------------------------------------------------------ host side
+
+int make_map_nd(CUtensorMap *map, CUtensorMapDataType dt, int rank, const void *base, const cuuint64_t *dims,
+                const cuuint64_t *strides, const cuuint32_t *box, CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return wm::fail(WM_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = fn(map, dt, rank, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return wm::fail(WM_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(r) + ")");
+  return WM_OK;
+}
+
+template <class C>
+int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K, const uint8_t *b_hi,
+                  const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
+                  const int4 *tiles, const int32_t *n_tiles, uint16_t *h_out, float *y_out, int32_t *err,
+                  cudaStream_t stream) {
+  if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
+  if (!wm::aligned(w, 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed weights must be 32-byte aligned");
+  CUtensorMap tmA, tmBh, tmBl;
+  const cuuint64_t rb = static_cast<cuuint64_t>(K) / 2;   // packed bytes per weight row
+  if (mode == 0) {
+    // (K, row in group of 8, half [first I rows | second I rows], group of 8 rows over all experts):
+    // one box = 8 groups x (8 rows of each half) = 64 up + 64 gate rows, interleaved by 8
+    const cuuint64_t dims[4] = {static_cast<cuuint64_t>(K), 8, 2, static_cast<cuuint64_t>(E) * (I / 4)};
+    const cuuint64_t strides[3] = {rb, rb * I, rb * 8};
+    const cuuint32_t box[4] = {kKH, 8, 2, 8};
+    if (int rc = make_map_nd(&tmA, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 4, w, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(E) * rows};
+    const cuuint64_t strides[1] = {rb};
+    const cuuint32_t box[2] = {kKH, kM};
+    if (int rc = make_map_nd(&tmA, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 2, w, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  {
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(S_rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+    const cuuint32_t box[2] = {kKH, 16};
+    if (int rc = make_map_nd(&tmBh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, b_hi, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+    if (int rc = make_map_nd(&tmBl, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, b_lo, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  }
+  static std::mutex mu;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(k_expert_mx<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(C::kSmem));
+      if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("mx smem attribute: ") + cudaGetErrorString(e));
+      attr_set[dev] = true;
+    }
+  }
+  MxParams p{};
+  p.mode = mode;
+  p.K = K;
+  p.rows = rows;
+  p.I = I;
+  p.H = H;
+  p.order = order;
+  p.limit = limit;
+  p.m_tiles = mode == 0 ? I / 64 : rows / kM;
+  p.a_scales = a_scales;
+  p.b_scales = b_sc;
+  p.tiles = tiles;
+  p.n_tiles = n_tiles;
+  p.h_out = h_out;
+  p.y_out = y_out;
+  p.err = err;
+  k_expert_mx<C><<<wm::sm_count(), kMxThreads, C::kSmem, stream>>>(tmA, tmBh, tmBl, p);
+  return wm::check_launch("expert mx");
+}
+
+int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
+              const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
+              float limit, const int4 *tiles, const int32_t *n_tiles, uint16_t *h_out, float *y_out, int32_t *err,
+              cudaStream_t stream) {
+  if (decode)
+    return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
+                                   n_tiles, h_out, y_out, err, stream);
+  return launch_mx_cfg<MxPrefill>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
+                                  n_tiles, h_out, y_out, err, stream);
+}
+
+}  // namespace
+
+namespace wm {
+
+bool mx_supported(int H, int I) { return H % 256 == 0 && I % 256 == 0; }
+
+int mx_tile_n(int T) { return T <= 64 ? MxDecode::kNMax : MxPrefill::kNMax; }
+
+int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream) {
+  const int64_t work = static_cast<int64_t>(S) * (K / 8);
+  const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
+  if (grid > 0) {
+    if (perm)
+      k_split_e4m3<true><<<grid, 256, 0, stream>>>(src, perm, count, S, kk, K, hi, lo, sc);
+    else
+      k_split_e4m3<false><<<grid, 256, 0, stream>>>(src, nullptr, count, S, 1, K, hi, lo, sc);
+  }
+  return check_launch("split e4m3");
+}
+
+int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
+                 const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
+                 const int32_t *n_tiles, uint16_t *h, int32_t *err, int tile_n, cudaStream_t stream) {
+  return launch_mx(tile_n == MxDecode::kNMax, 0, w13, s13, E, 2 * I, H, x_hi, x_lo, x_sc, S_rows, I, H, order, limit,
+                   tiles, n_tiles, h, nullptr, err, stream);
+}
+
+int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
+                   const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
+                   float *y, int32_t *err, int tile_n, cudaStream_t stream) {
+  return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, I, H, WM_UP_GATE, 0.0f,
+                   tiles, n_tiles, nullptr, y, err, stream);
+}
+
+}  // namespace wm
+
+extern "C" int wmx_split_e4m3(const wm_bf16 *x, int rows, int cols, uint8_t *hi, uint8_t *lo, uint8_t *scales,
+                              wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(rows >= 0 && cols > 0 && cols % 32 == 0, "split_e4m3: need rows >= 0 and cols a multiple of 32");
+  if (rows == 0) return WM_OK;
+  WM_REQUIRE(x && hi && lo && scales, "split_e4m3: null buffer");
+  WM_REQUIRE(wm::aligned(x, 16) && wm::aligned(hi, 8) && wm::aligned(lo, 8), "split_e4m3: misaligned buffer");
+  return wm::launch_split_e4m3(reinterpret_cast<const uint16_t *>(x), nullptr, nullptr, rows, 1, cols, hi, lo, scales,
+                               static_cast<cudaStream_t>(stream));
+}

@@ -34,6 +34,19 @@ int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, co
 int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
                    const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, int tile_n, cudaStream_t stream);
 
+// moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
+bool mx_supported(int H, int I);
+int mx_tile_n(int T);  // tokens per tile: 32 for decode batches (T <= 64), else 128
+// rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk]
+int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream);
+int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
+                 const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
+                 const int32_t *n_tiles, uint16_t *h, int32_t *err, int tile_n, cudaStream_t stream);
+int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
+                   const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
+                   float *y, int32_t *err, int tile_n, cudaStream_t stream);
+
 // Workspace carved out of the caller's buffer for one expert-forward call.
 // S = T * (k + has_shared) assignments.
 struct MoeWorkspace {
@@ -42,9 +55,13 @@ struct MoeWorkspace {
   int32_t *inv;        // [S] flat assignment -> sorted slot
   int32_t *active;     // [E] active expert ids, ascending
   int32_t *counters;   // [4]: n_active, permute error flag, n_tiles, tensor-core error code
-  int4 *tiles;         // [E + S/64 + 2] tensor-core work list
-  uint16_t *h;         // [S_pad, I] SwiGLU output in sorted-slot order (bf16 GEMV path, f16 tensor path)
-  uint16_t *x16;       // [S_pad, H] f16 tokens in sorted-slot order (tensor path)
+  int4 *tiles;         // [E + S/16 + 2] tensor-core work list
+  uint16_t *h;         // [S_pad, I] SwiGLU output in sorted-slot order (bf16; f16 on the f16 tensor path)
+  uint16_t *x16;       // [S_pad, H] f16 tokens in sorted-slot order (f16 tensor path)
+  uint8_t *x_hi, *x_lo;  // [S_pad, H] e4m3 token terms (block-scaled path; same bytes as x16)
+  uint8_t *x_sc;       // [S_pad, H/32] E8M0 scale of x_hi
+  uint8_t *h_hi, *h_lo;  // [S_pad, I] e4m3 terms of h
+  uint8_t *h_sc;       // [S_pad, I/32]
   float *y;            // [S, H] f32 expert outputs in sorted-slot order
   int s_pad;           // S rounded up to at least 16 rows (TMA box height)
   size_t bytes;
@@ -67,9 +84,12 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
   size_t o_act = take(E * sizeof(int32_t));
   size_t o_cnt = take(4 * sizeof(int32_t));
   const size_t S_pad = S < 16 ? 16 : S;
-  size_t o_tiles = take((E + S / 64 + 2) * sizeof(int4));
+  size_t o_tiles = take((E + S / 16 + 2) * sizeof(int4));
   size_t o_h = take(S_pad * I * sizeof(uint16_t));
   size_t o_x16 = take(S_pad * H * sizeof(uint16_t));
+  size_t o_xsc = take(S_pad * (H / 32));
+  size_t o_h8 = take(S_pad * I * 2);
+  size_t o_hsc = take(S_pad * (I / 32));
   size_t o_y = take(S * H * sizeof(float));
   w.s_pad = static_cast<int>(S_pad);
   w.bytes = off;
@@ -83,6 +103,12 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
     w.tiles = reinterpret_cast<int4 *>(b + o_tiles);
     w.h = reinterpret_cast<uint16_t *>(b + o_h);
     w.x16 = reinterpret_cast<uint16_t *>(b + o_x16);
+    w.x_hi = reinterpret_cast<uint8_t *>(b + o_x16);
+    w.x_lo = w.x_hi + S_pad * H;
+    w.x_sc = reinterpret_cast<uint8_t *>(b + o_xsc);
+    w.h_hi = reinterpret_cast<uint8_t *>(b + o_h8);
+    w.h_lo = w.h_hi + S_pad * I;
+    w.h_sc = reinterpret_cast<uint8_t *>(b + o_hsc);
     w.y = reinterpret_cast<float *>(b + o_y);
   }
   return w;

@@ -62,6 +62,21 @@ def mxfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor, dtype=torch.bfl
     return out
 
 
+def split_e4m3(x: torch.Tensor):
+    """bf16 [rows, cols] -> (hi u8, lo u8 [rows, cols], scales u8 [rows, cols/32]):
+    the exact two-term e4m3 operand form of the block-scaled expert kernels."""
+    if x.dtype != torch.bfloat16 or x.dim() != 2:
+        raise ValueError("split_e4m3 takes a 2-D bf16 tensor")
+    x = x.contiguous()
+    rows, cols = x.shape
+    hi = torch.empty((rows, cols), dtype=torch.uint8, device=x.device)
+    lo = torch.empty_like(hi)
+    sc = torch.empty((rows, cols // 32), dtype=torch.uint8, device=x.device)
+    L.require_cuda(x, hi, lo, sc)
+    L.call("wmx_split_e4m3", L.ptr(x), rows, cols, L.ptr(hi), L.ptr(lo), L.ptr(sc), L.stream_of(x))
+    return hi, lo, sc
+
+
 def affine4_quantize(w: torch.Tensor, group: int = 64):
     """bf16 [..., rows, cols] -> (packed uint32 [..., cols/8] as int32 storage, scales bf16, biases bf16)."""
     if w.dtype != torch.bfloat16:
