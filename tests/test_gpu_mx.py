@@ -62,7 +62,7 @@ def _oracle_layer(lay, x):
         w, idx, sw = W.qwen_route(x, lay.gate_weight, lay.cfg["k"], True, shared_gate=lay.shared_gate,
                                   logit_bias=lay.logit_bias)
         return M.moe_forward(x.float().cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), o,
-                             shared_expert=lay.cfg["E"], shared_weight=sw.cpu().numpy())
+                             shared_expert=lay.cfg["E"], shared_weight=sw.reshape(-1).cpu().numpy())
     o = M.MXFP4Experts(*(t.cpu().numpy() for t in (ex.w13, ex.w13_scales, ex.w2, ex.w2_scales)), M.UP_GATE, 10.0)
     w, idx = lay.layer.gate(x)
     return M.moe_forward(x.float().cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), o, shared_expert=lay.cfg["E"])
