@@ -18,9 +18,11 @@
 //      within 2^-14 of its block maximum (8 significant bits = 4 + 4) and off
 //      by at most 2^-22 of the block maximum below that, so the product is the
 //      bf16 x MXFP4 product of the reference up to f32 accumulation order.
-//      Each K-block issues two MMAs (hi, lo) into the same accumulator; the
-//      8-bit kind runs at twice the 16-bit rate, so this costs the tensor time
-//      of one f16 MMA.
+//      The terms are stacked along N (hi rows [0, n16), lo rows [n16, 2 n16),
+//      n16 = tokens rounded up to 16, each row with its own scale), so one
+//      MMA per K-block reads the weight tile once and D = [D_hi | D_lo]; the
+//      epilogue adds the halves.  Shared-memory traffic, not the tensor core,
+//      bounds a skinny MMA: the padded e2m1 tile is 4 KB per 32 K, read once.
 //
 // Orientation ("swap AB"): M = 128 weight rows, N = the tokens routed to one
 // expert (16..NMAX per tile), K = reduction.  The up projection's 128 rows
@@ -33,8 +35,8 @@
 // work items):
 //   warp 0      TMA producer (weights, token terms)
 //   warp 1      MMA issuer: tcgen05.cp of the stage's scale factors into
-//               TMEM, then 2 x KC/32 MMAs (the copy and the MMAs of one
-//               thread execute in issue order)
+//               TMEM, then KC/32 MMAs (the copies and the MMAs of one thread
+//               execute in issue order)
 //   warp 2      TMEM allocator
 //   warps 4-7   scale warps: per stage they read the rows' E8M0 bytes from
 //               global memory (prefetched four stages ahead) and write them in
@@ -63,24 +65,25 @@ struct MxCfg {
   static constexpr int kHalves = KC / kKH;                   // 128-K groups per stage
   static constexpr int kABox = kM * kKH;                     // 16 KB: 128 rows x 128 padded bytes
   static constexpr int kAStage = kHalves * kABox;
-  static constexpr int kBBox = NMAX * kKH;                   // NMAX rows x 128 B, one (term, group)
-  static constexpr int kBStage = 2 * kHalves * kBBox;
-  static constexpr int kSFStage = ((3 * kHalves * 512 + 1023) / 1024) * 1024;  // A, B hi, B lo atoms
-  static constexpr int kSfCol0 = 2 * NMAX;                   // after the two accumulators
-  static constexpr int kSfCols = 3 * kHalves * 4;
+  static constexpr int kBBox = 2 * NMAX * kKH;               // hi + lo rows x 128 B, one K group
+  static constexpr int kBStage = kHalves * kBBox;
+  static constexpr int kSFStage = ((2 * kHalves * 512 + 1023) / 1024) * 1024;  // A and B atoms
+  static constexpr int kDCols = 2 * NMAX;                    // one accumulator: [D_hi | D_lo]
+  static constexpr int kSfCol0 = 2 * kDCols;                 // after the two accumulators
+  static constexpr int kSfCols = 2 * kHalves * 4;
   static constexpr int kColsUsed = kSfCol0 + kSfCols;
   static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
                                  : kColsUsed <= 256 ? 256 : 512;
   static constexpr size_t kSmem =
       1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 4) * 8 + 16;
   static_assert(KC % kKH == 0, "stage depth must be a multiple of 128");
-  static_assert(NMAX % 16 == 0 && NMAX <= 128, "tile width");
+  static_assert(NMAX % 16 == 0 && NMAX <= 64, "tile width (2 NMAX rows share one 128-row scale atom)");
   static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
   static_assert(kSmem <= 232448, "shared memory");
   static_assert(kColsUsed <= 512, "TMEM columns");
 };
 using MxDecode = MxCfg<256, 32, 4>;
-using MxPrefill = MxCfg<128, 128, 4>;
+using MxPrefill = MxCfg<128, 64, 6>;
 
 struct MxParams {
   int mode;                  // 0: up projection (+ClampedSwiGLU -> h bf16), 1: down projection (-> y f32)
@@ -150,8 +153,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sA = smem;                                   // S x kAStage
-  uint8_t *sB = sA + S * C::kAStage;                    // S x kBStage: [term][group] boxes
-  uint8_t *sF = sB + S * C::kBStage;                    // S x kSFStage: [A | B hi | B lo][group] atoms
+  uint8_t *sB = sA + S * C::kAStage;                    // S x kBStage: [group][hi rows | lo rows]
+  uint8_t *sF = sB + S * C::kBStage;                    // S x kSFStage: [A | B][group] atoms
   uint64_t *bars = reinterpret_cast<uint64_t *>(sF + S * C::kSFStage);
   uint64_t *full = bars;                                // [S]: TMA bytes + 128 scale-thread arrivals
   uint64_t *empty = full + S;                           // [S]: MMA commit
@@ -187,7 +190,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const int4 tile = p.tiles[item / p.m_tiles];
       const int m = item % p.m_tiles;
-      const int nb = (tile.z + 15) >> 4;                // 16-row token boxes
+      const int nb = (tile.z + 15) >> 4;                // 16-row token boxes per term
       for (int kc = 0; kc < kstages; ++kc, ++g) {
         const int s = g % S;
         if (!(ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 1))) break;
@@ -201,10 +204,10 @@ __global__ void __launch_bounds__(kMxThreads, 1)
               tma_load_4d(a, &tmA, x, 0, 0, tile.x * (p.I / 4) + m * 8, &full[s]);
             else
               tma_load_2d(a, &tmA, x, tile.x * p.rows + m * kM, &full[s]);
+            uint8_t *b = sB + s * C::kBStage + q * C::kBBox;
             for (int j = 0; j < nb; ++j) {
-              tma_load_2d(sB + s * C::kBStage + q * C::kBBox + j * 16 * kKH, &tmBh, x, tile.y + 16 * j, &full[s]);
-              tma_load_2d(sB + s * C::kBStage + (HV + q) * C::kBBox + j * 16 * kKH, &tmBl, x, tile.y + 16 * j,
-                          &full[s]);
+              tma_load_2d(b + j * 16 * kKH, &tmBh, x, tile.y + 16 * j, &full[s]);
+              tma_load_2d(b + (nb + j) * 16 * kKH, &tmBl, x, tile.y + 16 * j, &full[s]);
             }
           }
         }
@@ -218,17 +221,16 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
     const uint32_t sfa = tmem + C::kSfCol0;
-    const uint32_t sfbh = sfa + HV * 4;
-    const uint32_t sfbl = sfbh + HV * 4;
+    const uint32_t sfb = sfa + HV * 4;
     uint32_t g = 0, it = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
       const int4 tile = p.tiles[item / p.m_tiles];
-      const int n_mma = max(16, (tile.z + 15) & ~15);
+      const int n_mma = 2 * max(16, (tile.z + 15) & ~15);   // hi and lo rows
       const int db = it & 1;
       if (!(ok = mbar_wait(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
       tc_fence_after();
-      const uint32_t d_addr = tmem + db * C::kNMax;
+      const uint32_t d_addr = tmem + db * C::kDCols;
       for (int kc = 0; kc < kstages && ok; ++kc, ++g) {
         const int s = g % S;
         if (!(ok = mbar_wait(&full[s], (g / S) & 1, p.err, 4))) break;
@@ -238,23 +240,17 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 #pragma unroll
           for (int q = 0; q < HV; ++q) {
             tc_cp_sf(sfa + 4 * q, sdesc_atom(f0 + q * 512));
-            tc_cp_sf(sfbh + 4 * q, sdesc_atom(f0 + (HV + q) * 512));
-            tc_cp_sf(sfbl + 4 * q, sdesc_atom(f0 + (2 * HV + q) * 512));
+            tc_cp_sf(sfb + 4 * q, sdesc_atom(f0 + (HV + q) * 512));
           }
           const uint32_t a0 = smem_u32(sA + s * C::kAStage);
-          const uint32_t bh0 = smem_u32(sB + s * C::kBStage);
-          const uint32_t bl0 = bh0 + HV * C::kBBox;
+          const uint32_t b0 = smem_u32(sB + s * C::kBStage);
 #pragma unroll
           for (int kb = 0; kb < C::kKC / 32; ++kb) {
             const int q = kb >> 2;
             const uint32_t j = kb & 3;
-            const uint64_t ad = bdesc_sw128(a0 + q * C::kABox) + 2 * j;
-            const uint64_t bhd = bdesc_sw128(bh0 + q * C::kBBox) + 2 * j;
-            const uint64_t bld = bdesc_sw128(bl0 + q * C::kBBox) + 2 * j;
-            const uint32_t idesc = idesc_mx(n_mma, j);
-            const uint32_t sa = (j << 30) | (sfa + 4 * q);
-            tc_mma_mx(d_addr, ad, bhd, idesc, sa, (j << 30) | (sfbh + 4 * q), (kc == 0 && kb == 0) ? 0u : 1u);
-            tc_mma_mx(d_addr, ad, bld, idesc, sa, (j << 30) | (sfbl + 4 * q), 1u);
+            tc_mma_mx(d_addr, bdesc_sw128(a0 + q * C::kABox) + 2 * j, bdesc_sw128(b0 + q * C::kBBox) + 2 * j,
+                      idesc_mx(n_mma, j), (j << 30) | (sfa + 4 * q), (j << 30) | (sfb + 4 * q),
+                      (kc == 0 && kb == 0) ? 0u : 1u);
           }
           tc_commit(&empty[s]);
         }
@@ -268,7 +264,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------- scale warps
     // Thread t owns row t of the A atom (weight row of the work item) and row
-    // t of the B atoms (token t of the tile; zero past the tile's tokens).
+    // t of the B atom: the hi scale of token t for t < n16, the lo scale of
+    // token t - n16 for n16 <= t < 2 n16, zero past the tile's tokens.
     const int t = threadIdx.x - 128;
     const int o = (t & 31) * 4 + (t >> 5);              // 32-bit word of row t inside an atom
     struct Ent {
@@ -287,11 +284,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_kc * (C::kKC / 32));
 #pragma unroll
       for (int q = 0; q < HV; ++q) e.a[q] = __ldg(ap + q);
-      if (t < tile.z) {
+      const int n16 = max(16, (tile.z + 15) & ~15);
+      const bool lo_row = t >= n16;
+      const int tok = lo_row ? t - n16 : t;
+      if (tok < tile.z && t < 2 * n16) {
         const uint32_t *bp = reinterpret_cast<const uint32_t *>(
-            p.b_scales + static_cast<int64_t>(tile.y + t) * ks32 + c_kc * (C::kKC / 32));
+            p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_kc * (C::kKC / 32));
 #pragma unroll
-        for (int q = 0; q < HV; ++q) e.b[q] = __ldg(bp + q);
+        for (int q = 0; q < HV; ++q) e.b[q] = __ldg(bp + q) - (lo_row ? kLoSub : 0u);
       }
       if (++c_kc == kstages) {
         c_kc = 0;
@@ -319,7 +319,6 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         for (int q = 0; q < HV; ++q) {
           f[q * 128 + o] = cur.a[q];
           f[(HV + q) * 128 + o] = cur.b[q];
-          f[(2 * HV + q) * 128 + o] = cur.b[q] ? cur.b[q] - kLoSub : 0u;
         }
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         mbar_arrive(&full[s]);
@@ -340,10 +339,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       if (!(ok = mbar_wait(&dfull[db], (it >> 1) & 1, p.err, 8))) break;
       tc_fence_after();
       const int n = tile.z;
+      const int n16 = max(16, (n + 15) & ~15);
       for (int c0 = 0; c0 < n; c0 += 16) {
-        uint32_t r[16];
-        WM_TMEM_LD16(tmem + lane_base + db * C::kNMax + c0, r);
+        uint32_t r[16], rl[16];
+        WM_TMEM_LD16(tmem + lane_base + db * C::kDCols + c0, r);
+        WM_TMEM_LD16(tmem + lane_base + db * C::kDCols + n16 + c0, rl);
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+        for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(__uint_as_float(r[q]) + __uint_as_float(rl[q]));
         if (p.mode == 0) {
           const int jj = m * 64 + (t >> 4) * 8 + (t & 7);
 #pragma unroll
