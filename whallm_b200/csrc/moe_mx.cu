@@ -144,6 +144,29 @@ __device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
 
 __device__ __forceinline__ float silu_mx(float g) { return g / (1.0f + expf(-g)); }
 
+// Work items blockIdx.x, +gridDim.x, ... with the tile of the next item loaded
+// one item ahead, so no role waits on a tile-list load between items.
+struct TileCursor {
+  const int4 *tiles;
+  int m_tiles, n_items, item;
+  int4 cur, nxt;
+  __device__ __forceinline__ int4 load(int i) const {
+    return i < n_items ? tiles[i / m_tiles] : make_int4(0, 0, 0, 0);
+  }
+  __device__ __forceinline__ TileCursor(const int4 *t, int mt, int n) : tiles(t), m_tiles(mt), n_items(n) {
+    item = blockIdx.x;
+    cur = load(item);
+    nxt = load(item + gridDim.x);
+  }
+  __device__ __forceinline__ bool valid() const { return item < n_items; }
+  __device__ __forceinline__ int m() const { return item % m_tiles; }
+  __device__ __forceinline__ void advance() {
+    item += gridDim.x;
+    cur = nxt;
+    nxt = load(item + gridDim.x);
+  }
+};
+
 template <class C>
 __global__ void __launch_bounds__(kMxThreads, 1)
     k_expert_mx(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
@@ -187,9 +210,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     // ---------------------------------------------------------- producer
     uint32_t g = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      const int4 tile = p.tiles[item / p.m_tiles];
-      const int m = item % p.m_tiles;
+    for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance()) {
+      const int4 tile = tc.cur;
+      const int m = tc.m();
       const int nb = (tile.z + 15) >> 4;                // 16-row token boxes per term
       for (int kc = 0; kc < kstages; ++kc, ++g) {
         const int s = g % S;
@@ -224,8 +247,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const uint32_t sfb = sfa + HV * 4;
     uint32_t g = 0, it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-      const int4 tile = p.tiles[item / p.m_tiles];
+    for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance(), ++it) {
+      const int4 tile = tc.cur;
       const int n_mma = 2 * max(16, (tile.z + 15) & ~15);   // hi and lo rows
       const int db = it & 1;
       if (!(ok = mbar_wait(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
@@ -266,19 +289,27 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     // Thread t owns row t of the A atom (weight row of the work item) and row
     // t of the B atom: the hi scale of token t for t < n16, the lo scale of
     // token t - n16 for n16 <= t < 2 n16, zero past the tile's tokens.
+    // The loads of stage g + kPf are issued while stage g is written, into a
+    // ring of kPf register sets indexed at compile time: a loaded register is
+    // first read kPf stages later, so the load latency is off the per-stage
+    // path (a register shift queue would wait on every load one stage on).
     const int t = threadIdx.x - 128;
     const int o = (t & 31) * 4 + (t >> 5);              // 32-bit word of row t inside an atom
+    constexpr int kPf = 4;
     struct Ent {
       uint32_t a[HV];
       uint32_t b[HV];
+      uint32_t sub;                                     // kLoSub for a lo-term row, else 0
     };
-    int c_item = blockIdx.x, c_kc = 0;                  // prefetch cursor
+    TileCursor cur(p.tiles, p.m_tiles, n_items);       // prefetch cursor
+    int c_kc = 0;
     auto fetch = [&](Ent &e) {
 #pragma unroll
       for (int q = 0; q < HV; ++q) { e.a[q] = 0u; e.b[q] = 0u; }
-      if (c_item >= n_items) return;
-      const int4 tile = p.tiles[c_item / p.m_tiles];
-      const int m = c_item % p.m_tiles;
+      e.sub = 0u;
+      if (!cur.valid()) return;
+      const int4 tile = cur.cur;
+      const int m = cur.m();
       const int grow = p.mode == 0 ? ((t >> 3) & 1) * p.I + m * 64 + (t >> 4) * 8 + (t & 7) : m * kM + t;
       const uint32_t *ap = reinterpret_cast<const uint32_t *>(
           p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_kc * (C::kKC / 32));
@@ -291,37 +322,39 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const uint32_t *bp = reinterpret_cast<const uint32_t *>(
             p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_kc * (C::kKC / 32));
 #pragma unroll
-        for (int q = 0; q < HV; ++q) e.b[q] = __ldg(bp + q) - (lo_row ? kLoSub : 0u);
+        for (int q = 0; q < HV; ++q) e.b[q] = __ldg(bp + q);
+        e.sub = lo_row ? kLoSub : 0u;
       }
       if (++c_kc == kstages) {
         c_kc = 0;
-        c_item += gridDim.x;
+        cur.advance();
       }
     };
-    Ent e0, e1, e2, e3;
-    fetch(e0);
-    fetch(e1);
-    fetch(e2);
-    fetch(e3);
-    uint32_t g = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-      for (int kc = 0; kc < kstages; ++kc, ++g) {
-        const Ent cur = e0;
-        e0 = e1;
-        e1 = e2;
-        e2 = e3;
-        fetch(e3);
-        const int s = g % S;
-        if (!(ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 9))) break;
-        uint32_t *f = reinterpret_cast<uint32_t *>(sF + s * C::kSFStage);
+    const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const uint32_t total = static_cast<uint32_t>(my_items) * kstages;
+    Ent ring[kPf];
 #pragma unroll
-        for (int q = 0; q < HV; ++q) {
-          f[q * 128 + o] = cur.a[q];
-          f[(HV + q) * 128 + o] = cur.b[q];
+    for (int u = 0; u < kPf; ++u) fetch(ring[u]);
+    bool ok = true;
+    for (uint32_t g0 = 0; g0 < total && ok; g0 += kPf) {
+#pragma unroll
+      for (int u = 0; u < kPf; ++u) {
+        const uint32_t g = g0 + u;
+        if (g < total && ok) {
+          const int s = g % S;
+          ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 9);
+          if (ok) {
+            uint32_t *f = reinterpret_cast<uint32_t *>(sF + s * C::kSFStage);
+#pragma unroll
+            for (int q = 0; q < HV; ++q) {
+              f[q * 128 + o] = ring[u].a[q];
+              f[(HV + q) * 128 + o] = ring[u].b[q] - ring[u].sub;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            mbar_arrive(&full[s]);
+            fetch(ring[u]);
+          }
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        mbar_arrive(&full[s]);
       }
     }
   } else if (warp >= 8) {
@@ -332,9 +365,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const bool is_up = ((t >> 3) & 1) == up_half;
     uint32_t it = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++it) {
-      const int4 tile = p.tiles[item / p.m_tiles];
-      const int m = item % p.m_tiles;
+    for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance(), ++it) {
+      const int4 tile = tc.cur;
+      const int m = tc.m();
       const int db = it & 1;
       if (!(ok = mbar_wait(&dfull[db], (it >> 1) & 1, p.err, 8))) break;
       tc_fence_after();

@@ -12,8 +12,8 @@
 //   denominator uses the same butterfly over lane partials of experts
 //   l, l+32, l+64, ...  Compiled with -fmad=false.
 //
-// Kernel 1 (logits): one 4-warp CTA per (expert row, chunk of up to 8
-//   tokens); each warp streams a quarter of the row with 16-byte loads.
+// Kernel 1 (logits): one 4-warp CTA per (expert-row group, token group);
+//   each warp streams a quarter of the rows with 16-byte loads.
 // Kernel 2 (top-k): one CTA per token; scores are computed by all threads,
 //   then k rounds of a warp arg-max with ties to the lower expert id.
 #include <mutex>
@@ -23,66 +23,100 @@
 
 namespace {
 
-constexpr int kTokChunk = 8;
 constexpr int kMaxE = 1024;
 constexpr int kMaxK = 32;
 constexpr int kSegs = 4;          // warps per expert row
 
-// One CTA (4 warps) per (expert row, chunk of up to 8 tokens).  Warp s takes
-// the column blocks [s*n/4, (s+1)*n/4) of the row (n = ceil(H/256)), lanes
-// stride the blocks in 8-element pieces; partials meet in shared memory.
+// One CTA (4 warps) per (group of ET expert rows, group of TT tokens).  Warp
+// s takes the column blocks [s*n/4, (s+1)*n/4) (n = ceil(H/256)); lane l
+// keeps one fmaf chain per (expert, token) pair of the tile over its 8-element
+// pieces 256*i + 8*l .. +7, so every weight and token load feeds ET or TT
+// chains.  Partials meet in shared memory; warp w reduces the pairs
+// p = w, w+4, ... in the canonical order.
+template <int ET, int TT>
 __global__ void __launch_bounds__(128) k_router_logits(const uint16_t *__restrict__ x, const uint16_t *__restrict__ wg,
                                                        const uint16_t *__restrict__ wg_shared,
                                                        const float *__restrict__ logit_bias, int T, int H, int E,
                                                        float *__restrict__ logits, float *__restrict__ shared_raw) {
-  __shared__ float part[kSegs][kTokChunk][32];
+  __shared__ float part[kSegs][ET * TT][32];
   const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
   const int rows = E + (wg_shared ? 1 : 0);
-  const int e = blockIdx.x % rows;
-  const int t0 = (blockIdx.x / rows) * kTokChunk;
-  const int nt = min(kTokChunk, T - t0);
-  const uint16_t *w = (e < E) ? wg + static_cast<int64_t>(e) * H : wg_shared;
+  const int egroups = (rows + ET - 1) / ET;
+  const int e0 = (blockIdx.x % egroups) * ET;
+  const int t0 = (blockIdx.x / egroups) * TT;
+  const uint16_t *wrow[ET];
+#pragma unroll
+  for (int a = 0; a < ET; ++a) {
+    const int e = min(e0 + a, rows - 1);              // clamped rows compute a discarded duplicate
+    wrow[a] = e < E ? wg + static_cast<int64_t>(e) * H : wg_shared;
+  }
+  const uint16_t *xrow[TT];
+#pragma unroll
+  for (int b = 0; b < TT; ++b) xrow[b] = x + static_cast<int64_t>(min(t0 + b, T - 1)) * H;
   const int n = (H + 255) / 256;
   const int i0 = (seg * n) / kSegs, i1 = ((seg + 1) * n) / kSegs;
-  float acc[kTokChunk];
+  float acc[ET][TT];
 #pragma unroll
-  for (int t = 0; t < kTokChunk; ++t) acc[t] = 0.0f;
-#pragma unroll 8
+  for (int a = 0; a < ET; ++a)
+#pragma unroll
+    for (int b = 0; b < TT; ++b) acc[a][b] = 0.0f;
+#pragma unroll 2
   for (int i = i0; i < i1; ++i) {
     const int base = 256 * i + 8 * lane;
     if (base < H) {
-      uint4 wu = __ldg(reinterpret_cast<const uint4 *>(w + base));
-      float wv[8] = {wm_bf16lo(wu.x), wm_bf16hi(wu.x), wm_bf16lo(wu.y), wm_bf16hi(wu.y),
-                     wm_bf16lo(wu.z), wm_bf16hi(wu.z), wm_bf16lo(wu.w), wm_bf16hi(wu.w)};
+      uint4 wu[ET], xu[TT];
 #pragma unroll
-      for (int t = 0; t < kTokChunk; ++t) {
-        if (t < nt) {
-          uint4 xu = __ldg(reinterpret_cast<const uint4 *>(x + static_cast<int64_t>(t0 + t) * H + base));
-          float xv[8] = {wm_bf16lo(xu.x), wm_bf16hi(xu.x), wm_bf16lo(xu.y), wm_bf16hi(xu.y),
-                         wm_bf16lo(xu.z), wm_bf16hi(xu.z), wm_bf16lo(xu.w), wm_bf16hi(xu.w)};
-          float a = acc[t];
+      for (int a = 0; a < ET; ++a) wu[a] = __ldg(reinterpret_cast<const uint4 *>(wrow[a] + base));
 #pragma unroll
-          for (int j = 0; j < 8; ++j) a = fmaf(xv[j], wv[j], a);
-          acc[t] = a;
+      for (int b = 0; b < TT; ++b) xu[b] = __ldg(reinterpret_cast<const uint4 *>(xrow[b] + base));
+#pragma unroll
+      for (int a = 0; a < ET; ++a) {
+        const float wv[8] = {wm_bf16lo(wu[a].x), wm_bf16hi(wu[a].x), wm_bf16lo(wu[a].y), wm_bf16hi(wu[a].y),
+                             wm_bf16lo(wu[a].z), wm_bf16hi(wu[a].z), wm_bf16lo(wu[a].w), wm_bf16hi(wu[a].w)};
+#pragma unroll
+        for (int b = 0; b < TT; ++b) {
+          const float xv[8] = {wm_bf16lo(xu[b].x), wm_bf16hi(xu[b].x), wm_bf16lo(xu[b].y), wm_bf16hi(xu[b].y),
+                               wm_bf16lo(xu[b].z), wm_bf16hi(xu[b].z), wm_bf16lo(xu[b].w), wm_bf16hi(xu[b].w)};
+          float v = acc[a][b];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v = fmaf(xv[j], wv[j], v);
+          acc[a][b] = v;
         }
       }
     }
   }
 #pragma unroll
-  for (int t = 0; t < kTokChunk; ++t) part[seg][t][lane] = acc[t];
+  for (int a = 0; a < ET; ++a)
+#pragma unroll
+    for (int b = 0; b < TT; ++b) part[seg][a * TT + b][lane] = acc[a][b];
   __syncthreads();
-  if (seg == 0) {
+  for (int pidx = seg; pidx < ET * TT; pidx += kSegs) {
+    float v = ((part[0][pidx][lane] + part[1][pidx][lane]) + part[2][pidx][lane]) + part[3][pidx][lane];
 #pragma unroll
-    for (int t = 0; t < kTokChunk; ++t) {
-      float v = ((part[0][t][lane] + part[1][t][lane]) + part[2][t][lane]) + part[3][t][lane];
-#pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) v = v + __shfl_xor_sync(0xffffffffu, v, m);
-      if (lane == 0 && t < nt) {
-        if (e < E) logits[static_cast<int64_t>(t0 + t) * E + e] = logit_bias ? v + logit_bias[e] : v;
-        else shared_raw[t0 + t] = v;
-      }
+    for (int m = 16; m >= 1; m >>= 1) v = v + __shfl_xor_sync(0xffffffffu, v, m);
+    const int e = e0 + pidx / TT, t = t0 + pidx % TT;
+    if (lane == 0 && e < rows && t < T) {
+      if (e < E) logits[static_cast<int64_t>(t) * E + e] = logit_bias ? v + logit_bias[e] : v;
+      else shared_raw[t] = v;
     }
   }
+}
+
+// Tile shape by batch: enough CTAs to stream the gate matrix at small T, and
+// register-resident reuse of every load (ET x TT chains) at large T.
+int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *wg_shared, const float *logit_bias,
+                         int T, int H, int E, float *logits, float *shared_raw, cudaStream_t stream) {
+  const int rows = E + (wg_shared ? 1 : 0);
+  auto go = [&](auto kern, int et, int tt) {
+    const int64_t ctas = static_cast<int64_t>((rows + et - 1) / et) * ((T + tt - 1) / tt);
+    if (ctas >= (1LL << 31)) return wm::fail(WM_ERR_INVALID, "router: too many tokens");
+    kern<<<static_cast<int>(ctas), 128, 0, stream>>>(x, wg, wg_shared, logit_bias, T, H, E, logits, shared_raw);
+    return wm::check_launch("router logits");
+  };
+  if (T <= 1) return go(k_router_logits<2, 1>, 2, 1);
+  if (T <= 4) return go(k_router_logits<2, 4>, 2, 4);
+  if (T <= 16) return go(k_router_logits<4, 8>, 4, 8);
+  return go(k_router_logits<8, 8>, 8, 8);
 }
 
 // One CTA (256 threads) per token: the score function runs on all threads,
@@ -193,11 +227,10 @@ extern "C" int wmoe_router_topk(const wm_bf16 *x, const wm_bf16 *wg, const float
   WM_REQUIRE(!wg_shared || shared_w, "router: wg_shared needs a shared_w output");
   WM_REQUIRE(wm::aligned(x, 16) && wm::aligned(wg, 16) && (!wg_shared || wm::aligned(wg_shared, 16)),
              "router inputs must be 16-byte aligned");
-  const int rows = E + (wg_shared ? 1 : 0);
-  const int64_t ctas = static_cast<int64_t>(rows) * ((T + kTokChunk - 1) / kTokChunk);
-  WM_REQUIRE(ctas < (1LL << 31), "router: too many tokens");
-  k_router_logits<<<static_cast<int>(ctas), 128, 0, stream>>>(x, wg, wg_shared, logit_bias, T, H, E, logits, shared_w);
-  if (int rc = wm::check_launch("wmoe_router_topk(logits)")) return rc;
+  if (int rc = launch_router_logits(reinterpret_cast<const uint16_t *>(x), reinterpret_cast<const uint16_t *>(wg),
+                                    reinterpret_cast<const uint16_t *>(wg_shared), logit_bias, T, H, E, logits,
+                                    shared_w, stream))
+    return rc;
   k_router_topk<<<T, 256, 0, stream>>>(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights,
                                        shared_w);
   return wm::check_launch("wmoe_router_topk(topk)");
@@ -282,11 +315,10 @@ extern "C" int wmoe_router_topk_static(const wm_bf16 *x, const wm_bf16 *wg, cons
     }
     scratch = g_scratch_ptr[dev];
   }
-  const int rows = E + (wg_shared ? 1 : 0);
-  const int64_t ctas = static_cast<int64_t>(rows) * ((T + kTokChunk - 1) / kTokChunk);
-  k_router_logits<<<static_cast<int>(ctas), 128, 0, stream>>>(x, wg, wg_shared, logit_bias, T, H, E, scratch,
-                                                              shared_w);
-  if (int rc = wm::check_launch("wmoe_router_topk_static(logits)")) return rc;
+  if (int rc = launch_router_logits(reinterpret_cast<const uint16_t *>(x), reinterpret_cast<const uint16_t *>(wg),
+                                    reinterpret_cast<const uint16_t *>(wg_shared), logit_bias, T, H, E, scratch,
+                                    shared_w, stream))
+    return rc;
   k_router_topk<<<T, 256, 0, stream>>>(scratch, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights,
                                        shared_w);
   return wm::check_launch("wmoe_router_topk_static(topk)");
