@@ -204,16 +204,38 @@ __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int t = static_cast<int>(i / per_row), c8 = static_cast<int>(i % per_row) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < kk && !bad; ++j) {
-      const float wt = j < k ? w[static_cast<int64_t>(t) * k + j] : (shared_w ? shared_w[t] : 1.0f);
-      const int slot = inv[static_cast<int64_t>(t) * kk + j];
-      if (slot < 0 || slot >= S) continue;
-      const float4 *yp = reinterpret_cast<const float4 *>(y + static_cast<int64_t>(slot) * H + c8);
-      float4 a = yp[0], b = yp[1];
-      acc[0] = fmaf(wt, a.x, acc[0]); acc[1] = fmaf(wt, a.y, acc[1]);
-      acc[2] = fmaf(wt, a.z, acc[2]); acc[3] = fmaf(wt, a.w, acc[3]);
-      acc[4] = fmaf(wt, b.x, acc[4]); acc[5] = fmaf(wt, b.y, acc[5]);
-      acc[6] = fmaf(wt, b.z, acc[6]); acc[7] = fmaf(wt, b.w, acc[7]);
+    // slots and weights of 8 assignments, then their 8 rows in flight together,
+    // then the fmaf chain in slot order
+    for (int j0 = 0; j0 < kk && !bad; j0 += 8) {
+      int sl[8];
+      float wt[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        sl[u] = j < kk ? inv[static_cast<int64_t>(t) * kk + j] : -1;
+        wt[u] = j < k ? w[static_cast<int64_t>(t) * k + j] : (j < kk && shared_w ? shared_w[t] : 1.0f);
+      }
+      float4 a[8], b[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (sl[u] >= 0 && sl[u] < S) {
+          const float4 *yp = reinterpret_cast<const float4 *>(y + static_cast<int64_t>(sl[u]) * H + c8);
+          a[u] = yp[0];
+          b[u] = yp[1];
+        } else {
+          a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          b[u] = a[u];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (sl[u] < 0 || sl[u] >= S) continue;
+        const float wv = wt[u];
+        acc[0] = fmaf(wv, a[u].x, acc[0]); acc[1] = fmaf(wv, a[u].y, acc[1]);
+        acc[2] = fmaf(wv, a[u].z, acc[2]); acc[3] = fmaf(wv, a[u].w, acc[3]);
+        acc[4] = fmaf(wv, b[u].x, acc[4]); acc[5] = fmaf(wv, b[u].y, acc[5]);
+        acc[6] = fmaf(wv, b[u].z, acc[6]); acc[7] = fmaf(wv, b[u].w, acc[7]);
+      }
     }
     if constexpr (F32_OUT) {
       float4 *op = reinterpret_cast<float4 *>(static_cast<float *>(out_v) + static_cast<int64_t>(t) * H + c8);
@@ -357,7 +379,8 @@ int run(const Args &a, int fmt) {
                                                                               a.limit, nullptr, ws.y);
   }
   if (int rc = wm::check_launch("expert gemv")) return rc;
-  const int cgrid = wm::sm_count() * 8;
+  const int64_t cwork = static_cast<int64_t>(a.reduce ? a.T : S) * (a.H / 8);
+  const int cgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((cwork + 255) / 256, wm::sm_count() * 8)));
   if (a.reduce && a.out_f32)
     k_combine<true><<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk,
                                                  a.H, a.out_f32);

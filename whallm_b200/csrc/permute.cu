@@ -172,7 +172,12 @@ int permute_warps(int E) {
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
                    int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
                    int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf) {
-  const int nw = permute_warps(E);
+  // warps: one per 32 assignments (at least 4, for the per-expert loops), up
+  // to what the per-warp histograms leave room for
+  const int64_t S = static_cast<int64_t>(T) * (k + (shared_expert >= 0 ? 1 : 0));
+  int nw = 4;
+  while (nw < 32 && nw * 32 < S) nw <<= 1;
+  nw = std::min(nw, permute_warps(E));
   const size_t smem = permute_smem_bytes(E, nw);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));

@@ -14,8 +14,8 @@
 //
 // Kernel 1 (logits): one 4-warp CTA per (expert-row group, token group);
 //   each warp streams a quarter of the rows with 16-byte loads.
-// Kernel 2 (top-k): one CTA per token; scores are computed by all threads,
-//   then k rounds of a warp arg-max with ties to the lower expert id.
+// Kernel 2 (top-k): one warp per token; scores in registers, then k rounds
+//   of a warp arg-max with ties to the lower expert id.
 #include <mutex>
 
 #include "wm_common.cuh"
@@ -119,96 +119,116 @@ int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *
   return go(k_router_logits<8, 8>, 8, 8);
 }
 
-// One CTA (256 threads) per token: the score function runs on all threads,
-// then warp 0 selects the top-k (ties to the lower id) and renormalises.
-__global__ void __launch_bounds__(256) k_router_topk(const float *__restrict__ logits, const float *__restrict__ select_bias,
-                                                     int T, int E, int k, int score_fn, float norm_eps,
-                                                     float route_scale, int32_t *__restrict__ idx,
-                                                     float *__restrict__ weights, float *__restrict__ shared_w) {
-  __shared__ float sc[kMaxE];
-  __shared__ float red[8];
-  __shared__ float bcast;
-  const int t = blockIdx.x;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// One warp per token (4 tokens per CTA): lane l holds the scores of experts
+// l, l+32, ...; the softmax denominator sums them in that order and then
+// across lanes with the butterfly; k rounds of a warp arg-max (ties to the
+// lower expert id, NaN keys last) carry the winner's score along, and lane r
+// keeps the r-th selection.  The renormalising sum runs over r in order.
+template <int PER>
+__global__ void __launch_bounds__(128) k_router_topk(const float *__restrict__ logits,
+                                                     const float *__restrict__ select_bias, int T, int E, int k,
+                                                     int score_fn, float norm_eps, float route_scale,
+                                                     int32_t *__restrict__ idx, float *__restrict__ weights,
+                                                     float *__restrict__ shared_w) {
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (t >= T) return;
   const float kNegInf = -__int_as_float(0x7f800000);
   const float *lt = logits + static_cast<int64_t>(t) * E;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) sc[e] = lt[e];
-  __syncthreads();
+  float sc[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const int e = lane + 32 * j;
+    sc[j] = e < E ? lt[e] : kNegInf;
+  }
   if (score_fn == WM_SCORE_SOFTMAX) {
     float mx = kNegInf;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) mx = fmaxf(mx, sc[e]);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) mx = fmaxf(mx, sc[j]);
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red[i]);
-    for (int e = threadIdx.x; e < E; e += blockDim.x) sc[e] = wm_exp(sc[e] - mx);
-    __syncthreads();
-    if (warp == 0) {
-      float part = 0.0f;
-      for (int e = lane; e < E; e += 32) part = part + sc[e];
+    float part = 0.0f;
 #pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) part = part + __shfl_xor_sync(0xffffffffu, part, m);
-      if (lane == 0) bcast = part;
+    for (int j = 0; j < PER; ++j) {
+      if (lane + 32 * j < E) {
+        sc[j] = wm_exp(sc[j] - mx);
+        part = part + sc[j];
+      }
     }
-    __syncthreads();
-    const float sum = bcast;
-    for (int e = threadIdx.x; e < E; e += blockDim.x) sc[e] = __fdiv_rn(sc[e], sum);
-  } else if (score_fn == WM_SCORE_SIGMOID) {
-    for (int e = threadIdx.x; e < E; e += blockDim.x) sc[e] = wm_sigmoid(sc[e]);
-  } else if (score_fn == WM_SCORE_SQRTSOFTPLUS) {
-    for (int e = threadIdx.x; e < E; e += blockDim.x) sc[e] = __fsqrt_rn(wm_softplus(sc[e]));
-  }
-  __syncthreads();
-  if (warp != 0) return;
-  const int per = (E + 31) / 32;
-  float key[kMaxE / 32];
 #pragma unroll
-  for (int j = 0; j < kMaxE / 32; ++j) {
+    for (int m = 16; m >= 1; m >>= 1) part = part + __shfl_xor_sync(0xffffffffu, part, m);
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = __fdiv_rn(sc[j], part);
+  } else if (score_fn == WM_SCORE_SIGMOID) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = wm_sigmoid(sc[j]);
+  } else if (score_fn == WM_SCORE_SQRTSOFTPLUS) {
+#pragma unroll
+    for (int j = 0; j < PER; ++j) sc[j] = __fsqrt_rn(wm_softplus(sc[j]));
+  }
+  float key[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
     float kv = kNegInf;
-    if (j < per && e < E) kv = select_bias ? sc[e] + select_bias[e] : sc[e];
+    if (e < E) kv = select_bias ? sc[j] + select_bias[e] : sc[j];
     key[j] = (kv != kv) ? kNegInf : kv;
   }
-  uint32_t taken = 0u;  // bit j: expert lane + 32 j selected
-  float wsel[kMaxK];
-  int32_t isel[kMaxK];
+  uint32_t taken = 0u;                                // bit j: expert lane + 32 j selected
+  float my_w = 0.0f;
+  int32_t my_i = 0;
   for (int r = 0; r < k; ++r) {
-    float bk = kNegInf;
+    float bk = kNegInf, bs = 0.0f;
     int be = 0x7fffffff;
 #pragma unroll
-    for (int j = 0; j < kMaxE / 32; ++j) {
+    for (int j = 0; j < PER; ++j) {
       const int e = lane + 32 * j;
-      if (j < per && e < E && !((taken >> j) & 1u)) {
-        if (key[j] > bk || (key[j] == bk && e < be)) { bk = key[j]; be = e; }
+      if (e < E && !((taken >> j) & 1u) && (key[j] > bk || (key[j] == bk && e < be))) {
+        bk = key[j];
+        be = e;
+        bs = sc[j];
       }
     }
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) {
       const float ok = __shfl_xor_sync(0xffffffffu, bk, m);
       const int oe = __shfl_xor_sync(0xffffffffu, be, m);
-      if (ok > bk || (ok == bk && oe < be)) { bk = ok; be = oe; }
+      const float os = __shfl_xor_sync(0xffffffffu, bs, m);
+      if (ok > bk || (ok == bk && oe < be)) { bk = ok; be = oe; bs = os; }
     }
     if ((be & 31) == lane) taken |= 1u << (be >> 5);
-    wsel[r] = sc[be];
-    isel[r] = be;
+    if (lane == r) { my_w = bs; my_i = be; }
   }
-  if (lane == 0) {
-    float denom = 1.0f;
-    const bool norm = norm_eps >= 0.0f;
-    if (norm) {
-      float sum = 0.0f;
-      for (int r = 0; r < k; ++r) sum = sum + wsel[r];
-      denom = sum + norm_eps;
-    }
-    for (int r = 0; r < k; ++r) {
-      const float w = norm ? __fdiv_rn(wsel[r], denom) : wsel[r];
-      idx[static_cast<int64_t>(t) * k + r] = isel[r];
-      weights[static_cast<int64_t>(t) * k + r] = w * route_scale;
-    }
-    if (shared_w) shared_w[t] = wm_sigmoid(shared_w[t]);
+  const bool norm = norm_eps >= 0.0f;
+  float denom = 1.0f;
+  if (norm) {
+    float sum = 0.0f;
+    for (int r = 0; r < k; ++r) sum = sum + __shfl_sync(0xffffffffu, my_w, r);
+    denom = sum + norm_eps;
   }
+  if (lane < k) {
+    const float w = norm ? __fdiv_rn(my_w, denom) : my_w;
+    idx[static_cast<int64_t>(t) * k + lane] = my_i;
+    weights[static_cast<int64_t>(t) * k + lane] = w * route_scale;
+  }
+  if (lane == 0 && shared_w) shared_w[t] = wm_sigmoid(shared_w[t]);
+}
+
+int launch_router_topk(const float *logits, const float *select_bias, int T, int E, int k, int score_fn,
+                       float norm_eps, float route_scale, int32_t *idx, float *weights, float *shared_w,
+                       cudaStream_t stream) {
+  const int grid = (T + 3) / 4;
+  const int per = (E + 31) / 32;
+#define WM_TOPK(P) k_router_topk<P><<<grid, 128, 0, stream>>>(logits, select_bias, T, E, k, score_fn, norm_eps, \
+                                                              route_scale, idx, weights, shared_w)
+  if (per <= 1) WM_TOPK(1);
+  else if (per <= 2) WM_TOPK(2);
+  else if (per <= 4) WM_TOPK(4);
+  else if (per <= 8) WM_TOPK(8);
+  else if (per <= 16) WM_TOPK(16);
+  else WM_TOPK(32);
+#undef WM_TOPK
+  return wm::check_launch("router topk");
 }
 
 }  // namespace
@@ -231,9 +251,8 @@ extern "C" int wmoe_router_topk(const wm_bf16 *x, const wm_bf16 *wg, const float
                                     reinterpret_cast<const uint16_t *>(wg_shared), logit_bias, T, H, E, logits,
                                     shared_w, stream))
     return rc;
-  k_router_topk<<<T, 256, 0, stream>>>(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights,
-                                       shared_w);
-  return wm::check_launch("wmoe_router_topk(topk)");
+  return launch_router_topk(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights, shared_w,
+                            stream);
 }
 
 extern "C" int wmoe_topk_scores(const float *logits, const float *select_bias, int T, int E, int k, int score_fn,
@@ -245,9 +264,8 @@ extern "C" int wmoe_topk_scores(const float *logits, const float *select_bias, i
   WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_NONE, "unknown score function");
   if (T == 0) return WM_OK;
   WM_REQUIRE(logits && idx && weights, "topk: null buffer");
-  k_router_topk<<<T, 256, 0, stream>>>(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights,
-                                       nullptr);
-  return wm::check_launch("wmoe_topk_scores");
+  return launch_router_topk(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights, nullptr,
+                            stream);
 }
 
 // ------------------------------------------------------------------------
@@ -319,7 +337,6 @@ extern "C" int wmoe_router_topk_static(const wm_bf16 *x, const wm_bf16 *wg, cons
                                     reinterpret_cast<const uint16_t *>(wg_shared), logit_bias, T, H, E, scratch,
                                     shared_w, stream))
     return rc;
-  k_router_topk<<<T, 256, 0, stream>>>(scratch, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights,
-                                       shared_w);
-  return wm::check_launch("wmoe_router_topk_static(topk)");
+  return launch_router_topk(scratch, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights, shared_w,
+                            stream);
 }
