@@ -336,12 +336,10 @@ int run(const Args &a, int fmt) {
   const int tile_n = mx ? wm::mx_tile_n(a.T) : wm::tc_tile_n(a.T);
   if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
                                   ws.counters, ws.counters + 1, (tc || mx) ? ws.tiles : nullptr, ws.counters + 2,
-                                  tile_n, a.stream, a.rf))
+                                  tile_n, a.stream, a.rf, ws.counters + 3))
     return rc;
   const int grid = wm::sm_count() * 2;
   if (mx) {
-    if (cudaMemsetAsync(ws.counters + 3, 0, sizeof(int32_t), a.stream) != cudaSuccess)
-      return wm::fail(WM_ERR_CUDA, "experts: memset failed");
     const int32_t *count = ws.offsets + a.E;
     if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
       return rc;
@@ -354,8 +352,6 @@ int run(const Args &a, int fmt) {
                                     ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream))
       return rc;
   } else if (tc) {
-    if (cudaMemsetAsync(ws.counters + 3, 0, sizeof(int32_t), a.stream) != cudaSuccess)
-      return wm::fail(WM_ERR_CUDA, "experts: memset failed");
     if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream)) return rc;
     if (int rc = wm::launch_tc_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x16, ws.s_pad, a.order, a.limit, ws.tiles,
                                   ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream))

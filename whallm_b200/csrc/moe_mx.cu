@@ -67,23 +67,25 @@ struct MxCfg {
   static constexpr int kAStage = kHalves * kABox;
   static constexpr int kBBox = 2 * NMAX * kKH;               // hi + lo rows x 128 B, one K group
   static constexpr int kBStage = kHalves * kBBox;
-  static constexpr int kSFStage = ((2 * kHalves * 512 + 1023) / 1024) * 1024;  // A and B atoms
+  static constexpr int kBAtoms = (2 * NMAX + 127) / 128;     // 128-row scale atoms of B per K group
+  static constexpr int kSFStage = (((1 + kBAtoms) * kHalves * 512 + 1023) / 1024) * 1024;  // A and B atoms
   static constexpr int kDCols = 2 * NMAX;                    // one accumulator: [D_hi | D_lo]
   static constexpr int kSfCol0 = 2 * kDCols;                 // after the two accumulators
-  static constexpr int kSfCols = 2 * kHalves * 4;
+  static constexpr int kSfbCols = 4 * kBAtoms;               // TMEM columns of B scales per K group
+  static constexpr int kSfCols = kHalves * (4 + kSfbCols);
   static constexpr int kColsUsed = kSfCol0 + kSfCols;
   static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
                                  : kColsUsed <= 256 ? 256 : 512;
   static constexpr size_t kSmem =
       1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 4) * 8 + 16;
   static_assert(KC % kKH == 0, "stage depth must be a multiple of 128");
-  static_assert(NMAX % 16 == 0 && NMAX <= 64, "tile width (2 NMAX rows share one 128-row scale atom)");
+  static_assert(NMAX % 16 == 0 && 2 * NMAX <= 256, "tile width: MMA N = 2 x tokens <= 256");
   static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
   static_assert(kSmem <= 232448, "shared memory");
   static_assert(kColsUsed <= 512, "TMEM columns");
 };
 using MxDecode = MxCfg<256, 32, 4>;
-using MxPrefill = MxCfg<128, 64, 6>;
+using MxPrefill = MxCfg<128, 112, 4>;
 
 struct MxParams {
   int mode;                  // 0: up projection (+ClampedSwiGLU -> h bf16), 1: down projection (-> y f32)
@@ -263,7 +265,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 #pragma unroll
           for (int q = 0; q < HV; ++q) {
             tc_cp_sf(sfa + 4 * q, sdesc_atom(f0 + q * 512));
-            tc_cp_sf(sfb + 4 * q, sdesc_atom(f0 + (HV + q) * 512));
+#pragma unroll
+            for (int a = 0; a < C::kBAtoms; ++a)
+              tc_cp_sf(sfb + C::kSfbCols * q + 4 * a, sdesc_atom(f0 + (HV + q * C::kBAtoms + a) * 512));
           }
           const uint32_t a0 = smem_u32(sA + s * C::kAStage);
           const uint32_t b0 = smem_u32(sB + s * C::kBStage);
@@ -272,7 +276,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             const int q = kb >> 2;
             const uint32_t j = kb & 3;
             tc_mma_mx(d_addr, bdesc_sw128(a0 + q * C::kABox) + 2 * j, bdesc_sw128(b0 + q * C::kBBox) + 2 * j,
-                      idesc_mx(n_mma, j), (j << 30) | (sfa + 4 * q), (j << 30) | (sfb + 4 * q),
+                      idesc_mx(n_mma, j), (j << 30) | (sfa + 4 * q), (j << 30) | (sfb + C::kSfbCols * q),
                       (kc == 0 && kb == 0) ? 0u : 1u);
           }
           tc_commit(&empty[s]);
@@ -296,17 +300,23 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const int t = threadIdx.x - 128;
     const int o = (t & 31) * 4 + (t >> 5);              // 32-bit word of row t inside an atom
     constexpr int kPf = 4;
+    constexpr int BA = C::kBAtoms;
     struct Ent {
       uint32_t a[HV];
-      uint32_t b[HV];
-      uint32_t sub;                                     // kLoSub for a lo-term row, else 0
+      uint32_t b[BA][HV];                               // B atom rows t + 128 * atom
+      uint32_t sub[BA];                                 // kLoSub for a lo-term row, else 0
     };
     TileCursor cur(p.tiles, p.m_tiles, n_items);       // prefetch cursor
     int c_kc = 0;
     auto fetch = [&](Ent &e) {
 #pragma unroll
-      for (int q = 0; q < HV; ++q) { e.a[q] = 0u; e.b[q] = 0u; }
-      e.sub = 0u;
+      for (int q = 0; q < HV; ++q) e.a[q] = 0u;
+#pragma unroll
+      for (int a = 0; a < BA; ++a) {
+        e.sub[a] = 0u;
+#pragma unroll
+        for (int q = 0; q < HV; ++q) e.b[a][q] = 0u;
+      }
       if (!cur.valid()) return;
       const int4 tile = cur.cur;
       const int m = cur.m();
@@ -316,14 +326,18 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 #pragma unroll
       for (int q = 0; q < HV; ++q) e.a[q] = __ldg(ap + q);
       const int n16 = max(16, (tile.z + 15) & ~15);
-      const bool lo_row = t >= n16;
-      const int tok = lo_row ? t - n16 : t;
-      if (tok < tile.z && t < 2 * n16) {
-        const uint32_t *bp = reinterpret_cast<const uint32_t *>(
-            p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_kc * (C::kKC / 32));
 #pragma unroll
-        for (int q = 0; q < HV; ++q) e.b[q] = __ldg(bp + q);
-        e.sub = lo_row ? kLoSub : 0u;
+      for (int a = 0; a < BA; ++a) {
+        const int r = t + 128 * a;                      // B atom row: hi term of token r, or lo of r - n16
+        const bool lo_row = r >= n16;
+        const int tok = lo_row ? r - n16 : r;
+        if (tok < tile.z && r < 2 * n16) {
+          const uint32_t *bp = reinterpret_cast<const uint32_t *>(
+              p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_kc * (C::kKC / 32));
+#pragma unroll
+          for (int q = 0; q < HV; ++q) e.b[a][q] = __ldg(bp + q);
+          e.sub[a] = lo_row ? kLoSub : 0u;
+        }
       }
       if (++c_kc == kstages) {
         c_kc = 0;
@@ -348,7 +362,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 #pragma unroll
             for (int q = 0; q < HV; ++q) {
               f[q * 128 + o] = ring[u].a[q];
-              f[(HV + q) * 128 + o] = ring[u].b[q] - ring[u].sub;
+#pragma unroll
+              for (int a = 0; a < BA; ++a) f[(HV + q * BA + a) * 128 + o] = ring[u].b[a][q] - ring[u].sub[a];
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             mbar_arrive(&full[s]);

@@ -22,7 +22,8 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
                                                   wm::RouteFilter rf, int E, int32_t *__restrict__ offsets, int32_t *__restrict__ perm,
                                                   int32_t *__restrict__ inv, int32_t *__restrict__ active,
                                                   int32_t *__restrict__ n_active, int32_t *__restrict__ error_flag,
-                                                  int4 *__restrict__ tiles, int32_t *__restrict__ n_tiles, int tile_n) {
+                                                  int4 *__restrict__ tiles, int32_t *__restrict__ n_tiles, int tile_n,
+                                                  int32_t *__restrict__ clear) {
   extern __shared__ int32_t sm[];
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -31,7 +32,10 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
   int32_t *hist = sm;                 // [nw][E]
   int32_t *tot = sm + nw * E;         // [E+1]
   __shared__ int32_t bad;
-  if (threadIdx.x == 0) bad = 0;
+  if (threadIdx.x == 0) {
+    bad = 0;
+    if (clear) *clear = 0;
+  }
   for (int i = threadIdx.x; i < nw * E; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   const int seg = (S + nw - 1) / nw;
@@ -171,7 +175,7 @@ int permute_warps(int E) {
 
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
                    int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
-                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf) {
+                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf, int32_t *clear) {
   // warps: one per 32 assignments (at least 4, for the per-expert loops), up
   // to what the per-warp histograms leave room for
   const int64_t S = static_cast<int64_t>(T) * (k + (shared_expert >= 0 ? 1 : 0));
@@ -184,7 +188,7 @@ int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, i
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("permute smem: ") + cudaGetErrorString(e));
   }
   k_permute<<<1, nw * 32, smem, stream>>>(idx, T, k, shared_expert, rf, E, offsets, perm, inv,
-                                          active, n_active, error_flag, tiles, n_tiles, tile_n);
+                                          active, n_active, error_flag, tiles, n_tiles, tile_n, clear);
   return check_launch("permute");
 }
 

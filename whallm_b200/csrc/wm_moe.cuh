@@ -20,7 +20,8 @@ struct RouteFilter {
 // {expert, first slot, tokens (<= tile_n), 0} per tile, count in *n_tiles.
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
                    int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
-                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf = RouteFilter{});
+                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf = RouteFilter{},
+                   int32_t *clear = nullptr);  // clear: a flag the permute sets to 0 (the expert kernels' error code)
 
 // moe_tc.cu
 bool tc_supported(int H, int I);
@@ -36,7 +37,7 @@ int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
 
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
-int mx_tile_n(int T);  // tokens per tile: 32 for decode batches (T <= 64), else 128
+int mx_tile_n(int T);  // tokens per tile: 32 for decode batches (T <= 64), else 112
 // rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk]
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
                       uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream);
