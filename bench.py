@@ -138,7 +138,7 @@ def run_ours(args, rank, world, dev):
     res = {}
     if wl in ("ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny"):
         name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn", "tiny": "tiny"}[wl]
-        layers = [S.make_layer(name, dev, seed=1000 * rank + 17 * i) for i in range(n_layers)]
+        layers = [S.make_layer(name, dev, seed=1000 * rank + 17 * i, E=args.experts) for i in range(n_layers)]
         cfg = layers[0].cfg
         H = cfg["H"]
         batches = {"ds_decode": SWEEP, "ds_prefill": (4096,), "qn_decode": (1, 32), "qn_prefill": (16384,),
@@ -518,6 +518,8 @@ def main():
     ap.add_argument("--workload", default="ds_decode",
                     choices=["ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny", "kv"])
     ap.add_argument("--layers", type=int, default=8, help="resident layers cycled per step (no L2 reuse)")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="routed experts per layer (default: the configuration's); smaller layers for ncu captures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
