@@ -38,9 +38,10 @@
 //               TMEM, then KC/32 MMAs (the copies and the MMAs of one thread
 //               execute in issue order)
 //   warp 2      TMEM allocator
-//   warps 4-7   scale warps: per stage they read the rows' E8M0 bytes from
-//               global memory (prefetched four stages ahead) and write them in
-//               the 32 x 16-byte layout that tcgen05.cp.32x128b.warpx4 takes
+//   warps 4-7   scale warps: they read the rows' E8M0 bytes from global
+//               memory a chunk (up to 32 bytes per row) ahead and write each
+//               stage's bytes in the 32 x 16-byte layout that
+//               tcgen05.cp.32x128b.warpx4 takes
 //   warps 8-11  epilogue (TMEM lanes 0-127)
 // Every mbarrier wait is bounded and records an error code instead of hanging.
 #include "wm_common.cuh"
@@ -291,40 +292,53 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   } else if (warp >= 4 && warp < 8) {
     // ------------------------------------------------------- scale warps
     // Thread t owns row t of the A atom (weight row of the work item) and row
-    // t of the B atom: the hi scale of token t for t < n16, the lo scale of
-    // token t - n16 for n16 <= t < 2 n16, zero past the tile's tokens.
-    // The loads of stage g + kPf are issued while stage g is written, into a
-    // ring of kPf register sets indexed at compile time: a loaded register is
-    // first read kPf stages later, so the load latency is off the per-stage
-    // path (a register shift queue would wait on every load one stage on).
+    // t (+128) of the B atoms: the hi scale of token r for r < n16, the lo
+    // scale of token r - n16 for n16 <= r < 2 n16, zero past the tile's
+    // tokens.  Scales are read in chunks of CW 32-bit words per row (up to 32
+    // bytes, one vector load, covering CW / HV stages) into a two-chunk
+    // register ring, so the loads need no L1 reuse (the shared-memory
+    // carve-out leaves L1 small) and run a chunk ahead of their use.
     const int t = threadIdx.x - 128;
     const int o = (t & 31) * 4 + (t >> 5);              // 32-bit word of row t inside an atom
-    constexpr int kPf = 4;
     constexpr int BA = C::kBAtoms;
-    struct Ent {
-      uint32_t a[HV];
-      uint32_t b[BA][HV];                               // B atom rows t + 128 * atom
+    const int CW = (ks32 % 32 == 0) ? 8 : (ks32 % 16 == 0) ? 4 : 2;   // words per row per chunk
+    const int SPC = CW / HV;                            // stages per chunk (K % 256 == 0: ks32 % 8 == 0)
+    const int n_ch = ks32 / (4 * CW);                   // chunks per work item
+    struct Chunk {
+      uint32_t a[8];
+      uint32_t b[BA][8];
       uint32_t sub[BA];                                 // kLoSub for a lo-term row, else 0
     };
     TileCursor cur(p.tiles, p.m_tiles, n_items);       // prefetch cursor
-    int c_kc = 0;
-    auto fetch = [&](Ent &e) {
+    int c_ch = 0;
+    auto load_words = [&](const uint8_t *src, uint32_t *dst) {
+      if (CW == 8) {
+        const uint4 u0 = __ldg(reinterpret_cast<const uint4 *>(src));
+        const uint4 u1 = __ldg(reinterpret_cast<const uint4 *>(src) + 1);
+        dst[0] = u0.x; dst[1] = u0.y; dst[2] = u0.z; dst[3] = u0.w;
+        dst[4] = u1.x; dst[5] = u1.y; dst[6] = u1.z; dst[7] = u1.w;
+      } else if (CW == 4) {
+        const uint4 u0 = __ldg(reinterpret_cast<const uint4 *>(src));
+        dst[0] = u0.x; dst[1] = u0.y; dst[2] = u0.z; dst[3] = u0.w;
+      } else {
+        const uint2 u0 = __ldg(reinterpret_cast<const uint2 *>(src));
+        dst[0] = u0.x; dst[1] = u0.y;
+      }
+    };
+    auto fetch = [&](Chunk &e) {
 #pragma unroll
-      for (int q = 0; q < HV; ++q) e.a[q] = 0u;
+      for (int w = 0; w < 8; ++w) e.a[w] = 0u;
 #pragma unroll
       for (int a = 0; a < BA; ++a) {
         e.sub[a] = 0u;
 #pragma unroll
-        for (int q = 0; q < HV; ++q) e.b[a][q] = 0u;
+        for (int w = 0; w < 8; ++w) e.b[a][w] = 0u;
       }
       if (!cur.valid()) return;
       const int4 tile = cur.cur;
       const int m = cur.m();
       const int grow = p.mode == 0 ? ((t >> 3) & 1) * p.I + m * 64 + (t >> 4) * 8 + (t & 7) : m * kM + t;
-      const uint32_t *ap = reinterpret_cast<const uint32_t *>(
-          p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_kc * (C::kKC / 32));
-#pragma unroll
-      for (int q = 0; q < HV; ++q) e.a[q] = __ldg(ap + q);
+      load_words(p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_ch * 4 * CW, e.a);
       const int n16 = max(16, (tile.z + 15) & ~15);
 #pragma unroll
       for (int a = 0; a < BA; ++a) {
@@ -332,44 +346,53 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const bool lo_row = r >= n16;
         const int tok = lo_row ? r - n16 : r;
         if (tok < tile.z && r < 2 * n16) {
-          const uint32_t *bp = reinterpret_cast<const uint32_t *>(
-              p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_kc * (C::kKC / 32));
-#pragma unroll
-          for (int q = 0; q < HV; ++q) e.b[a][q] = __ldg(bp + q);
+          load_words(p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_ch * 4 * CW, e.b[a]);
           e.sub[a] = lo_row ? kLoSub : 0u;
         }
       }
-      if (++c_kc == kstages) {
-        c_kc = 0;
+      if (++c_ch == n_ch) {
+        c_ch = 0;
         cur.advance();
       }
     };
     const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     const uint32_t total = static_cast<uint32_t>(my_items) * kstages;
-    Ent ring[kPf];
-#pragma unroll
-    for (int u = 0; u < kPf; ++u) fetch(ring[u]);
+    Chunk ring[2];
+    fetch(ring[0]);
+    fetch(ring[1]);
     bool ok = true;
-    for (uint32_t g0 = 0; g0 < total && ok; g0 += kPf) {
+    uint32_t g = 0;
+    while (g < total && ok) {
 #pragma unroll
-      for (int u = 0; u < kPf; ++u) {
-        const uint32_t g = g0 + u;
-        if (g < total && ok) {
+      for (int u = 0; u < 2; ++u) {
+        for (int si = 0; si < SPC && g < total && ok; ++si, ++g) {
           const int s = g % S;
           ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 9);
-          if (ok) {
-            uint32_t *f = reinterpret_cast<uint32_t *>(sF + s * C::kSFStage);
+          if (!ok) break;
+          uint32_t *f = reinterpret_cast<uint32_t *>(sF + s * C::kSFStage);
 #pragma unroll
-            for (int q = 0; q < HV; ++q) {
-              f[q * 128 + o] = ring[u].a[q];
+          for (int q = 0; q < HV; ++q) {
+            const int want = si * HV + q;                 // word of this stage within the chunk
+            uint32_t va = 0u, vb[BA];
 #pragma unroll
-              for (int a = 0; a < BA; ++a) f[(HV + q * BA + a) * 128 + o] = ring[u].b[a][q] - ring[u].sub[a];
+            for (int a = 0; a < BA; ++a) vb[a] = 0u;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) {
+              if (w == want) {
+                va = ring[u].a[w];
+#pragma unroll
+                for (int a = 0; a < BA; ++a) vb[a] = ring[u].b[a][w];
+              }
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            mbar_arrive(&full[s]);
-            fetch(ring[u]);
+            f[q * 128 + o] = va;
+#pragma unroll
+            for (int a = 0; a < BA; ++a) f[(HV + q * BA + a) * 128 + o] = vb[a] - ring[u].sub[a];
           }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive(&full[s]);
         }
+        if (!ok || g >= total) break;
+        fetch(ring[u]);
       }
     }
   } else if (warp >= 8) {
@@ -516,6 +539,8 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
                   cudaStream_t stream) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
   if (!wm::aligned(w, 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed weights must be 32-byte aligned");
+  if (!wm::aligned(a_scales, 16) || !wm::aligned(b_sc, 16))
+    return wm::fail(WM_ERR_INVALID, "expert mx: scales must be 16-byte aligned");
   CUtensorMap tmA, tmBh, tmBl;
   const cuuint64_t rb = static_cast<cuuint64_t>(K) / 2;   // packed bytes per weight row
   if (mode == 0) {
