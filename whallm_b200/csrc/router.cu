@@ -69,17 +69,23 @@ __global__ void __launch_bounds__(128) k_router_logits(const uint16_t *__restric
       for (int a = 0; a < ET; ++a) wu[a] = __ldg(reinterpret_cast<const uint4 *>(wrow[a] + base));
 #pragma unroll
       for (int b = 0; b < TT; ++b) xu[b] = __ldg(reinterpret_cast<const uint4 *>(xrow[b] + base));
+      float xv[TT][8];                                  // each token piece converted once per block
+#pragma unroll
+      for (int b = 0; b < TT; ++b) {
+        xv[b][0] = wm_bf16lo(xu[b].x); xv[b][1] = wm_bf16hi(xu[b].x);
+        xv[b][2] = wm_bf16lo(xu[b].y); xv[b][3] = wm_bf16hi(xu[b].y);
+        xv[b][4] = wm_bf16lo(xu[b].z); xv[b][5] = wm_bf16hi(xu[b].z);
+        xv[b][6] = wm_bf16lo(xu[b].w); xv[b][7] = wm_bf16hi(xu[b].w);
+      }
 #pragma unroll
       for (int a = 0; a < ET; ++a) {
         const float wv[8] = {wm_bf16lo(wu[a].x), wm_bf16hi(wu[a].x), wm_bf16lo(wu[a].y), wm_bf16hi(wu[a].y),
                              wm_bf16lo(wu[a].z), wm_bf16hi(wu[a].z), wm_bf16lo(wu[a].w), wm_bf16hi(wu[a].w)};
 #pragma unroll
         for (int b = 0; b < TT; ++b) {
-          const float xv[8] = {wm_bf16lo(xu[b].x), wm_bf16hi(xu[b].x), wm_bf16lo(xu[b].y), wm_bf16hi(xu[b].y),
-                               wm_bf16lo(xu[b].z), wm_bf16hi(xu[b].z), wm_bf16lo(xu[b].w), wm_bf16hi(xu[b].w)};
           float v = acc[a][b];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) v = fmaf(xv[j], wv[j], v);
+          for (int j = 0; j < 8; ++j) v = fmaf(xv[b][j], wv[j], v);
           acc[a][b] = v;
         }
       }
@@ -115,8 +121,8 @@ int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *
   };
   if (T <= 1) return go(k_router_logits<2, 1>, 2, 1);
   if (T <= 4) return go(k_router_logits<2, 4>, 2, 4);
-  if (T <= 16) return go(k_router_logits<4, 8>, 4, 8);
-  return go(k_router_logits<8, 8>, 8, 8);
+  if (T <= 16) return go(k_router_logits<2, 8>, 2, 8);
+  return go(k_router_logits<4, 8>, 4, 8);
 }
 
 // One warp per token (4 tokens per CTA): lane l holds the scores of experts
