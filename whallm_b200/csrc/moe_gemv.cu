@@ -333,7 +333,8 @@ int run(const Args &a, int fmt) {
   const MxPath path = mx_path();
   const bool mx = fmt == kFmtMxfp4 && path == MxPath::kBlockScaled && wm::mx_supported(a.H, a.I);
   const bool tc = fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I);
-  const int tile_n = mx ? wm::mx_tile_n(a.T) : wm::tc_tile_n(a.T);
+  const int n_routed = a.rf.count > 0 ? a.rf.n_global : a.E - has_shared;
+  const int tile_n = mx ? wm::mx_tile_n(a.T, a.k, n_routed) : wm::tc_tile_n(a.T);
   if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
                                   ws.counters, ws.counters + 1, (tc || mx) ? ws.tiles : nullptr, ws.counters + 2,
                                   tile_n, a.stream, a.rf, ws.counters + 3))
@@ -344,9 +345,8 @@ int run(const Args &a, int fmt) {
     if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
       return rc;
     if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, ws.s_pad, a.order,
-                                  a.limit, ws.tiles, ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream))
-      return rc;
-    if (int rc = wm::launch_split_e4m3(ws.h, nullptr, count, S, 1, a.I, ws.h_hi, ws.h_lo, ws.h_sc, a.stream))
+                                  a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.counters + 3,
+                                  tile_n, a.stream))
       return rc;
     if (int rc = wm::launch_mx_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h_hi, ws.h_lo, ws.h_sc, ws.s_pad, ws.tiles,
                                     ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream))

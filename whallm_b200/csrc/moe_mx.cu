@@ -28,8 +28,8 @@
 // expert (16..NMAX per tile), K = reduction.  The up projection's 128 rows
 // are 64 up and 64 gate rows interleaved in groups of 8 by a 4-D tensor map,
 // so lanes m and m ^ 8 of one warp hold up_j and gate_j for the fused
-// ClampedSwiGLU epilogue; its bf16 output is split into e4m3 terms again for
-// the down projection.
+// ClampedSwiGLU epilogue, which rounds h to bf16 and writes its two e4m3
+// terms and scales (the down projection's token operand) directly.
 //
 // Warp roles (384 threads, one CTA per SM, persistent over (tile, 128-row)
 // work items):
@@ -78,7 +78,7 @@ struct MxCfg {
   static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
                                  : kColsUsed <= 256 ? 256 : 512;
   static constexpr size_t kSmem =
-      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 4) * 8 + 16;
+      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 8) * 8 + 16;
   static_assert(KC % kKH == 0, "stage depth must be a multiple of 128");
   static_assert(NMAX % 16 == 0 && 2 * NMAX <= 256, "tile width: MMA N = 2 x tokens <= 256");
   static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
@@ -100,7 +100,8 @@ struct MxParams {
   const uint8_t *b_scales;   // [S_pad, K/32] hi-term E8M0 in slot order
   const int4 *tiles;         // {expert, first slot, tokens, 0}
   const int32_t *n_tiles;
-  uint16_t *h_out;           // up: [S_pad, I] bf16
+  uint8_t *h_hi, *h_lo;     // up: [S_pad, I] e4m3 terms of the bf16 SwiGLU output
+  uint8_t *h_sc;             // up: [S_pad, I/32] E8M0 scale of h_hi
   float *y_out;              // down: [S, H] f32
   int32_t *err;
 };
@@ -145,6 +146,18 @@ __device__ __forceinline__ void tc_cp_sf(uint32_t taddr, uint64_t sdesc) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
+__device__ __forceinline__ uint32_t e4m3x2(float first, float second) {  // first -> low byte
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(second), "f"(first));
+  return r;
+}
+
+__device__ __forceinline__ float2 e4m3x2_to_f32(uint32_t v) {  // .x <- low byte
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(v)));
+  return __half22float2(*reinterpret_cast<__half2 *>(&h2));
+}
+
 __device__ __forceinline__ float silu_mx(float g) { return g / (1.0f + expf(-g)); }
 
 // Work items blockIdx.x, +gridDim.x, ... with the tile of the next item loaded
@@ -186,12 +199,14 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   uint64_t *empty = full + S;                           // [S]: MMA commit
   uint64_t *dfull = empty + S;                          // [2]
   uint64_t *dempty = dfull + 2;                         // [2]
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(dempty + 2);
+  uint64_t *xbar = dempty + 2;                          // [2 warp pairs][2 buffers]: epilogue column-max exchange
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
 
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128); }
+    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 64);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -401,6 +416,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int up_half = p.order == WM_UP_GATE ? 0 : 1;
     const bool is_up = ((t >> 3) & 1) == up_half;
+    const int lane = threadIdx.x & 31;
+    __shared__ uint32_t xchg[2][4][16];                 // per-warp column maxima, double buffered
+    uint32_t xchg_n = 0;
     uint32_t it = 0;
     bool ok = true;
     for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance(), ++it) {
@@ -419,19 +437,48 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 #pragma unroll
         for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(__uint_as_float(r[q]) + __uint_as_float(rl[q]));
         if (p.mode == 0) {
+          // h = ClampedSwiGLU(up, gate) rounded to bf16, then its two e4m3
+          // terms: the item's 64 intermediate columns are two whole 32-column
+          // scale blocks, block b held by the up lanes of warps 2b and 2b+1
           const int jj = m * 64 + (t >> 4) * 8 + (t & 7);
+          uint32_t hb[16];                                // h as f32 bits of its bf16 value (0: not this lane's)
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
             const float v = __uint_as_float(r[q]);
             const float o = __shfl_xor_sync(0xffffffffu, v, 8);
+            hb[q] = 0u;
             if (is_up && c0 + q < n) {
               float up = v, gate = o;
               if (p.limit > 0.0f) {
                 up = fminf(fmaxf(up, -p.limit), p.limit);
                 gate = fminf(gate, p.limit);
               }
-              p.h_out[static_cast<int64_t>(tile.y + c0 + q) * p.I + jj] = wm_f32_to_bf16(silu_mx(gate) * up);
+              hb[q] = static_cast<uint32_t>(wm_f32_to_bf16(silu_mx(gate) * up)) << 16;
             }
+          }
+          const int wq = warp & 3, buf = xchg_n & 1;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const uint32_t am = __reduce_max_sync(0xffffffffu, hb[q] & 0x7fffffffu);
+            if (lane == 0) xchg[buf][wq][q] = am;
+          }
+          mbar_arrive(&xbar[(wq >> 1) * 2 + buf]);
+          if (!(ok = mbar_wait(&xbar[(wq >> 1) * 2 + buf], (xchg_n >> 1) & 1, p.err, 10))) break;
+          ++xchg_n;
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            if (!(is_up && c0 + q < n)) continue;
+            const uint32_t am = max(xchg[buf][wq][q], xchg[buf][wq ^ 1][q]);
+            const int sh = max(static_cast<int>(min(am >> 23, 255u)) - 134, -122);
+            const float xs = __uint_as_float(hb[q]) * __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
+            const uint32_t hi = e4m3x2(xs, 0.0f) & 0xffu;
+            const float hf = e4m3x2_to_f32(hi).x;
+            const uint32_t lo = e4m3x2((xs - hf) * static_cast<float>(1 << kLoShift), 0.0f) & 0xffu;
+            const int64_t off = static_cast<int64_t>(tile.y + c0 + q) * p.I + jj;
+            p.h_hi[off] = static_cast<uint8_t>(hi);
+            p.h_lo[off] = static_cast<uint8_t>(lo);
+            if (!(wq & 1) && (t & 7) == 0 && ((t >> 4) & 1) == 0)  // first up lane of the block
+              p.h_sc[static_cast<int64_t>(tile.y + c0 + q) * (p.I / 32) + (jj >> 5)] = static_cast<uint8_t>(sh + 127);
           }
         } else {
           const int row = m * kM + t;
@@ -453,18 +500,6 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 }
 
 // --------------------------------------------------------- two-term split
-
-__device__ __forceinline__ uint32_t e4m3x2(float first, float second) {  // first -> low byte
-  uint16_t r;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(second), "f"(first));
-  return r;
-}
-
-__device__ __forceinline__ float2 e4m3x2_to_f32(uint32_t v) {  // .x <- low byte
-  uint32_t h2;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(v)));
-  return __half22float2(*reinterpret_cast<__half2 *>(&h2));
-}
 
 // Rows [0, rows) of a bf16 matrix (GATHER: row p is x[perm[p] / kk]) ->
 // hi, lo e4m3 bytes and the hi term's E8M0 scale per 32 columns.  Four
@@ -535,8 +570,8 @@ int make_map_nd(CUtensorMap *map, CUtensorMapDataType dt, int rank, const void *
 template <class C>
 int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K, const uint8_t *b_hi,
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
-                  const int4 *tiles, const int32_t *n_tiles, uint16_t *h_out, float *y_out, int32_t *err,
-                  cudaStream_t stream) {
+                  const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
+                  float *y_out, int32_t *err, cudaStream_t stream) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
   if (!wm::aligned(w, 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed weights must be 32-byte aligned");
   if (!wm::aligned(a_scales, 16) || !wm::aligned(b_sc, 16))
@@ -597,7 +632,9 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.b_scales = b_sc;
   p.tiles = tiles;
   p.n_tiles = n_tiles;
-  p.h_out = h_out;
+  p.h_hi = h_hi;
+  p.h_lo = h_lo;
+  p.h_sc = h_sc;
   p.y_out = y_out;
   p.err = err;
   k_expert_mx<C><<<wm::sm_count(), kMxThreads, C::kSmem, stream>>>(tmA, tmBh, tmBl, p);
@@ -606,13 +643,13 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
 
 int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
               const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
-              float limit, const int4 *tiles, const int32_t *n_tiles, uint16_t *h_out, float *y_out, int32_t *err,
-              cudaStream_t stream) {
+              float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
+              float *y_out, int32_t *err, cudaStream_t stream) {
   if (decode)
     return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
-                                   n_tiles, h_out, y_out, err, stream);
+                                   n_tiles, h_hi, h_lo, h_sc, y_out, err, stream);
   return launch_mx_cfg<MxPrefill>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
-                                  n_tiles, h_out, y_out, err, stream);
+                                  n_tiles, h_hi, h_lo, h_sc, y_out, err, stream);
 }
 
 }  // namespace
@@ -621,7 +658,11 @@ namespace wm {
 
 bool mx_supported(int H, int I) { return H % 256 == 0 && I % 256 == 0; }
 
-int mx_tile_n(int T) { return T <= 64 ? MxDecode::kNMax : MxPrefill::kNMax; }
+int mx_tile_n(int T, int k, int n_routed) {
+  // expected tokens per routed expert under uniform routing
+  const int64_t per_expert = static_cast<int64_t>(T) * k / std::max(1, n_routed);
+  return per_expert <= MxDecode::kNMax ? MxDecode::kNMax : MxPrefill::kNMax;
+}
 
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
                       uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream) {
@@ -638,16 +679,17 @@ int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *c
 
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
-                 const int32_t *n_tiles, uint16_t *h, int32_t *err, int tile_n, cudaStream_t stream) {
+                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, int32_t *err, int tile_n,
+                 cudaStream_t stream) {
   return launch_mx(tile_n == MxDecode::kNMax, 0, w13, s13, E, 2 * I, H, x_hi, x_lo, x_sc, S_rows, I, H, order, limit,
-                   tiles, n_tiles, h, nullptr, err, stream);
+                   tiles, n_tiles, h_hi, h_lo, h_sc, nullptr, err, stream);
 }
 
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
                    float *y, int32_t *err, int tile_n, cudaStream_t stream) {
   return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, I, H, WM_UP_GATE, 0.0f,
-                   tiles, n_tiles, nullptr, y, err, stream);
+                   tiles, n_tiles, nullptr, nullptr, nullptr, y, err, stream);
 }
 
 }  // namespace wm

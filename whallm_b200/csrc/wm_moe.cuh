@@ -37,13 +37,15 @@ int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
 
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
-int mx_tile_n(int T);  // tokens per tile: 32 for decode batches (T <= 64), else 112
+// tokens per tile: 32 (decode configuration) while T * k / n_routed <= 32, else 112
+int mx_tile_n(int T, int k, int n_routed);
 // rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk]
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
                       uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream);
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
-                 const int32_t *n_tiles, uint16_t *h, int32_t *err, int tile_n, cudaStream_t stream);
+                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, int32_t *err, int tile_n,
+                 cudaStream_t stream);
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
                    float *y, int32_t *err, int tile_n, cudaStream_t stream);
