@@ -345,9 +345,12 @@ int run(const Args &a, int fmt) {
     if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
       return rc;
     if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, ws.s_pad, a.order,
-                                  a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.counters + 3,
-                                  tile_n, a.stream))
+                                  a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.h,
+                                  ws.counters + 3, tile_n, a.stream))
       return rc;
+    if (!wm::mx_fused_split(tile_n))
+      if (int rc = wm::launch_split_e4m3(ws.h, nullptr, count, S, 1, a.I, ws.h_hi, ws.h_lo, ws.h_sc, a.stream))
+        return rc;
     if (int rc = wm::launch_mx_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h_hi, ws.h_lo, ws.h_sc, ws.s_pad, ws.tiles,
                                     ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream))
       return rc;

@@ -28,8 +28,9 @@
 // expert (16..NMAX per tile), K = reduction.  The up projection's 128 rows
 // are 64 up and 64 gate rows interleaved in groups of 8 by a 4-D tensor map,
 // so lanes m and m ^ 8 of one warp hold up_j and gate_j for the fused
-// ClampedSwiGLU epilogue, which rounds h to bf16 and writes its two e4m3
-// terms and scales (the down projection's token operand) directly.
+// ClampedSwiGLU epilogue, which rounds h to bf16 and (decode configuration)
+// writes its two e4m3 terms and scales, the down projection's token operand,
+// directly; the prefill configuration writes bf16 h for a split kernel.
 //
 // Warp roles (384 threads, one CTA per SM, persistent over (tile, 128-row)
 // work items):
@@ -58,8 +59,12 @@ constexpr int kMxThreads = 384;
 constexpr int kLoShift = 5;              // lo term scale = hi scale * 2^-5
 constexpr uint32_t kLoSub = 0x01010101u * kLoShift;   // E8M0 bytes of the lo term, four at a time
 
-template <int KC, int NMAX, int STAGES>
+template <int KC, int NMAX, int STAGES, bool FUSE_SPLIT>
 struct MxCfg {
+  // FUSE_SPLIT: the up projection's epilogue writes the e4m3 terms of h
+  // (decode: at most two 16-column chunks per item, hidden behind the
+  // mainloop); otherwise it writes bf16 h and a split kernel follows.
+  static constexpr bool kFuseSplit = FUSE_SPLIT;
   static constexpr int kKC = KC;
   static constexpr int kNMax = NMAX;
   static constexpr int kStages = STAGES;
@@ -85,8 +90,8 @@ struct MxCfg {
   static_assert(kSmem <= 232448, "shared memory");
   static_assert(kColsUsed <= 512, "TMEM columns");
 };
-using MxDecode = MxCfg<256, 32, 4>;
-using MxPrefill = MxCfg<128, 112, 4>;
+using MxDecode = MxCfg<256, 32, 4, true>;
+using MxPrefill = MxCfg<128, 112, 4, false>;
 
 struct MxParams {
   int mode;                  // 0: up projection (+ClampedSwiGLU -> h bf16), 1: down projection (-> y f32)
@@ -100,8 +105,9 @@ struct MxParams {
   const uint8_t *b_scales;   // [S_pad, K/32] hi-term E8M0 in slot order
   const int4 *tiles;         // {expert, first slot, tokens, 0}
   const int32_t *n_tiles;
-  uint8_t *h_hi, *h_lo;     // up: [S_pad, I] e4m3 terms of the bf16 SwiGLU output
-  uint8_t *h_sc;             // up: [S_pad, I/32] E8M0 scale of h_hi
+  uint8_t *h_hi, *h_lo;     // up, fused split: [S_pad, I] e4m3 terms of the bf16 SwiGLU output
+  uint8_t *h_sc;             // up, fused split: [S_pad, I/32] E8M0 scale of h_hi
+  uint16_t *h_out;           // up, separate split: [S_pad, I] bf16
   float *y_out;              // down: [S, H] f32
   int32_t *err;
 };
@@ -436,7 +442,22 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
         for (int q = 0; q < 16; ++q) r[q] = __float_as_uint(__uint_as_float(r[q]) + __uint_as_float(rl[q]));
-        if (p.mode == 0) {
+        if (p.mode == 0 && !C::kFuseSplit) {
+          const int jj = m * 64 + (t >> 4) * 8 + (t & 7);
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float v = __uint_as_float(r[q]);
+            const float o = __shfl_xor_sync(0xffffffffu, v, 8);
+            if (is_up && c0 + q < n) {
+              float up = v, gate = o;
+              if (p.limit > 0.0f) {
+                up = fminf(fmaxf(up, -p.limit), p.limit);
+                gate = fminf(gate, p.limit);
+              }
+              p.h_out[static_cast<int64_t>(tile.y + c0 + q) * p.I + jj] = wm_f32_to_bf16(silu_mx(gate) * up);
+            }
+          }
+        } else if (p.mode == 0) {
           // h = ClampedSwiGLU(up, gate) rounded to bf16, then its two e4m3
           // terms: the item's 64 intermediate columns are two whole 32-column
           // scale blocks, block b held by the up lanes of warps 2b and 2b+1
@@ -571,7 +592,7 @@ template <class C>
 int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K, const uint8_t *b_hi,
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-                  float *y_out, int32_t *err, cudaStream_t stream) {
+                  uint16_t *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
   if (!wm::aligned(w, 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed weights must be 32-byte aligned");
   if (!wm::aligned(a_scales, 16) || !wm::aligned(b_sc, 16))
@@ -635,6 +656,7 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.h_hi = h_hi;
   p.h_lo = h_lo;
   p.h_sc = h_sc;
+  p.h_out = h_out;
   p.y_out = y_out;
   p.err = err;
   k_expert_mx<C><<<wm::sm_count(), kMxThreads, C::kSmem, stream>>>(tmA, tmBh, tmBl, p);
@@ -644,12 +666,12 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
 int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
               const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
               float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-              float *y_out, int32_t *err, cudaStream_t stream) {
+              uint16_t *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
   if (decode)
     return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
-                                   n_tiles, h_hi, h_lo, h_sc, y_out, err, stream);
+                                   n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
   return launch_mx_cfg<MxPrefill>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
-                                  n_tiles, h_hi, h_lo, h_sc, y_out, err, stream);
+                                  n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
 }
 
 }  // namespace
@@ -677,19 +699,21 @@ int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *c
   return check_launch("split e4m3");
 }
 
+bool mx_fused_split(int tile_n) { return tile_n == MxDecode::kNMax ? MxDecode::kFuseSplit : MxPrefill::kFuseSplit; }
+
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
-                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, int32_t *err, int tile_n,
-                 cudaStream_t stream) {
+                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
+                 int tile_n, cudaStream_t stream) {
   return launch_mx(tile_n == MxDecode::kNMax, 0, w13, s13, E, 2 * I, H, x_hi, x_lo, x_sc, S_rows, I, H, order, limit,
-                   tiles, n_tiles, h_hi, h_lo, h_sc, nullptr, err, stream);
+                   tiles, n_tiles, h_hi, h_lo, h_sc, h, nullptr, err, stream);
 }
 
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
                    float *y, int32_t *err, int tile_n, cudaStream_t stream) {
   return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, I, H, WM_UP_GATE, 0.0f,
-                   tiles, n_tiles, nullptr, nullptr, nullptr, y, err, stream);
+                   tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream);
 }
 
 }  // namespace wm

@@ -42,10 +42,12 @@ int mx_tile_n(int T, int k, int n_routed);
 // rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk]
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
                       uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream);
+// the up projection writes h's e4m3 terms itself (true) or bf16 h for launch_split_e4m3 (false)
+bool mx_fused_split(int tile_n);
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
-                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, int32_t *err, int tile_n,
-                 cudaStream_t stream);
+                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
+                 int tile_n, cudaStream_t stream);
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
                    float *y, int32_t *err, int tile_n, cudaStream_t stream);
