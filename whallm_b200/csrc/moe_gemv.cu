@@ -55,6 +55,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
                   const int32_t *__restrict__ perm, const int32_t *__restrict__ active,
                   const int32_t *__restrict__ counters, Weights W, int I, int order, float limit,
                   uint16_t *__restrict__ h_out, float *__restrict__ y_out) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int K = W.K;
   const int rows_per_item = kWarps * kRowsPerWarp;  // 32
@@ -197,6 +199,8 @@ template <bool F32_OUT>
 __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict__ inv, const float *__restrict__ w,
                           const float *__restrict__ shared_w, const int32_t *__restrict__ err, int T, int k, int kk,
                           int H, void *__restrict__ out_v) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
   const int per_row = H / 8;
   const int S = T * kk;
   const bool bad = *err != 0;
@@ -255,6 +259,8 @@ __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict
 // out[t, j, :] = bf16(y[inv[t*k+j], :])  (un-reduced switch_mlp output)
 __global__ void k_unsort(const float *__restrict__ y, const int32_t *__restrict__ inv, const int32_t *__restrict__ err,
                          int S, int H, uint16_t *__restrict__ out) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
   const int per_row = H / 8;
   const bool bad = *err != 0;
   const int64_t total = static_cast<int64_t>(S) * per_row;
@@ -362,32 +368,38 @@ int run(const Args &a, int fmt) {
     if (int rc = wm::launch_tc_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h, ws.s_pad, ws.tiles, ws.counters + 2, ws.y,
                                     ws.counters + 3, tile_n, a.stream))
       return rc;
-  } else if (fmt == kFmtMxfp4) {
-    k_expert_gemv<kFmtMxfp4, kModeUp><<<grid, kWarps * 32, 0, a.stream>>>(a.x, kk, ws.offsets, ws.perm, ws.active,
-                                                                          ws.counters, a.w13, a.I, a.order, a.limit,
-                                                                          ws.h, nullptr);
-    k_expert_gemv<kFmtMxfp4, kModeDown><<<grid, kWarps * 32, 0, a.stream>>>(ws.h, kk, ws.offsets, ws.perm, ws.active,
-                                                                            ws.counters, a.w2, a.I, a.order, a.limit,
-                                                                            nullptr, ws.y);
   } else {
-    k_expert_gemv<kFmtAffine4, kModeUp><<<grid, kWarps * 32, 0, a.stream>>>(a.x, kk, ws.offsets, ws.perm, ws.active,
-                                                                            ws.counters, a.w13, a.I, a.order, a.limit,
-                                                                            ws.h, nullptr);
-    k_expert_gemv<kFmtAffine4, kModeDown><<<grid, kWarps * 32, 0, a.stream>>>(ws.h, kk, ws.offsets, ws.perm, ws.active,
-                                                                              ws.counters, a.w2, a.I, a.order,
-                                                                              a.limit, nullptr, ws.y);
+    const uint16_t *x = a.x;
+    const auto up = fmt == kFmtMxfp4 ? k_expert_gemv<kFmtMxfp4, kModeUp> : k_expert_gemv<kFmtAffine4, kModeUp>;
+    const auto down = fmt == kFmtMxfp4 ? k_expert_gemv<kFmtMxfp4, kModeDown> : k_expert_gemv<kFmtAffine4, kModeDown>;
+    cudaError_t e = wm::launch_pdl(up, dim3(grid), dim3(kWarps * 32), 0, a.stream, x, kk,
+                                   static_cast<const int32_t *>(ws.offsets), static_cast<const int32_t *>(ws.perm),
+                                   static_cast<const int32_t *>(ws.active), static_cast<const int32_t *>(ws.counters),
+                                   a.w13, a.I, a.order, a.limit, ws.h, static_cast<float *>(nullptr));
+    if (e == cudaSuccess)
+      e = wm::launch_pdl(down, dim3(grid), dim3(kWarps * 32), 0, a.stream, static_cast<const uint16_t *>(ws.h), kk,
+                         static_cast<const int32_t *>(ws.offsets), static_cast<const int32_t *>(ws.perm),
+                         static_cast<const int32_t *>(ws.active), static_cast<const int32_t *>(ws.counters), a.w2,
+                         a.I, a.order, a.limit, static_cast<uint16_t *>(nullptr), ws.y);
+    if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("expert gemv: ") + cudaGetErrorString(e));
   }
   if (int rc = wm::check_launch("expert gemv")) return rc;
   const int64_t cwork = static_cast<int64_t>(a.reduce ? a.T : S) * (a.H / 8);
   const int cgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((cwork + 255) / 256, wm::sm_count() * 8)));
+  cudaError_t e;
   if (a.reduce && a.out_f32)
-    k_combine<true><<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk,
-                                                 a.H, a.out_f32);
+    e = wm::launch_pdl(k_combine<true>, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const float *>(ws.y),
+                       static_cast<const int32_t *>(ws.inv), a.weights, a.shared_w,
+                       static_cast<const int32_t *>(ws.counters + 1), a.T, a.k, kk, a.H, static_cast<void *>(a.out_f32));
   else if (a.reduce)
-    k_combine<false><<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk,
-                                                  a.H, a.out);
+    e = wm::launch_pdl(k_combine<false>, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const float *>(ws.y),
+                       static_cast<const int32_t *>(ws.inv), a.weights, a.shared_w,
+                       static_cast<const int32_t *>(ws.counters + 1), a.T, a.k, kk, a.H, static_cast<void *>(a.out));
   else
-    k_unsort<<<cgrid, 256, 0, a.stream>>>(ws.y, ws.inv, ws.counters + 1, S, a.H, a.out);
+    e = wm::launch_pdl(k_unsort, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const float *>(ws.y),
+                       static_cast<const int32_t *>(ws.inv), static_cast<const int32_t *>(ws.counters + 1), S, a.H,
+                       a.out);
+  if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("expert combine: ") + cudaGetErrorString(e));
   return wm::check_launch("expert combine");
 }
 

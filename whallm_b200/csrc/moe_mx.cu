@@ -225,6 +225,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // set-up above overlaps the previous kernel's tail; its results are read below
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
 
   const int n_items = (*p.n_tiles) * p.m_tiles;
   const int kstages = p.K / C::kKC;
@@ -529,6 +532,8 @@ template <bool GATHER>
 __global__ void k_split_e4m3(const uint16_t *__restrict__ src, const int32_t *__restrict__ perm,
                              const int32_t *__restrict__ count, int S, int kk, int K, uint8_t *__restrict__ hi,
                              uint8_t *__restrict__ lo, uint8_t *__restrict__ sc) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
   const int rows = count ? min(S, max(0, *count)) : S;
   const int per_row = K / 8;
   const int64_t total = static_cast<int64_t>(rows) * per_row;
@@ -659,7 +664,9 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.h_out = h_out;
   p.y_out = y_out;
   p.err = err;
-  k_expert_mx<C><<<wm::sm_count(), kMxThreads, C::kSmem, stream>>>(tmA, tmBh, tmBl, p);
+  if (cudaError_t e = wm::launch_pdl(k_expert_mx<C>, dim3(wm::sm_count()), dim3(kMxThreads), C::kSmem, stream, tmA,
+                                     tmBh, tmBl, p))
+    return wm::fail(WM_ERR_CUDA, std::string("expert mx: ") + cudaGetErrorString(e));
   return wm::check_launch("expert mx");
 }
 
@@ -691,10 +698,11 @@ int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *c
   const int64_t work = static_cast<int64_t>(S) * (K / 8);
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
   if (grid > 0) {
-    if (perm)
-      k_split_e4m3<true><<<grid, 256, 0, stream>>>(src, perm, count, S, kk, K, hi, lo, sc);
-    else
-      k_split_e4m3<false><<<grid, 256, 0, stream>>>(src, nullptr, count, S, 1, K, hi, lo, sc);
+    const cudaError_t e =
+        perm ? launch_pdl(k_split_e4m3<true>, dim3(grid), dim3(256), 0, stream, src, perm, count, S, kk, K, hi, lo, sc)
+             : launch_pdl(k_split_e4m3<false>, dim3(grid), dim3(256), 0, stream, src, static_cast<const int32_t *>(nullptr),
+                          count, S, 1, K, hi, lo, sc);
+    if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("split e4m3: ") + cudaGetErrorString(e));
   }
   return check_launch("split e4m3");
 }

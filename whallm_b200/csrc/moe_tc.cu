@@ -186,6 +186,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
 
   const int n_items = (*p.n_tiles) * p.m_tiles;
   const int kstages = p.K / C::kKC;
@@ -431,6 +433,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // x16[p, :] = f16(x[perm[p] / kk, :] * 2^-4): the up projection's B operand in expert order
 __global__ void k_gather_f16(const uint16_t *__restrict__ x, const int32_t *__restrict__ perm,
                              const int32_t *__restrict__ count, int S, int kk, int H, __half *__restrict__ x16) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
   const int per = H / 8;
   const int rows = min(S, max(0, *count));   // kept assignments (all of them unless an expert range drops some)
   const int64_t total = static_cast<int64_t>(rows) * per;

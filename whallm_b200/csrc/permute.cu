@@ -25,6 +25,9 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
                                                   int4 *__restrict__ tiles, int32_t *__restrict__ n_tiles, int tile_n,
                                                   int32_t *__restrict__ clear) {
   extern __shared__ int32_t sm[];
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
+
   const int nw = blockDim.x >> 5;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kk = k + (shared_expert >= 0 ? 1 : 0);
@@ -187,8 +190,9 @@ int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, i
     cudaError_t e = cudaFuncSetAttribute(k_permute, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("permute smem: ") + cudaGetErrorString(e));
   }
-  k_permute<<<1, nw * 32, smem, stream>>>(idx, T, k, shared_expert, rf, E, offsets, perm, inv,
-                                          active, n_active, error_flag, tiles, n_tiles, tile_n, clear);
+  if (cudaError_t e = launch_pdl(k_permute, dim3(1), dim3(nw * 32), smem, stream, idx, T, k, shared_expert, rf, E,
+                                 offsets, perm, inv, active, n_active, error_flag, tiles, n_tiles, tile_n, clear))
+    return fail(WM_ERR_CUDA, std::string("permute: ") + cudaGetErrorString(e));
   return check_launch("permute");
 }
 

@@ -39,6 +39,8 @@ __global__ void __launch_bounds__(128) k_router_logits(const uint16_t *__restric
                                                        const float *__restrict__ logit_bias, int T, int H, int E,
                                                        float *__restrict__ logits, float *__restrict__ shared_raw) {
   __shared__ float part[kSegs][ET * TT][32];
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
   const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
   const int rows = E + (wg_shared ? 1 : 0);
   const int egroups = (rows + ET - 1) / ET;
@@ -116,7 +118,9 @@ int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *
   auto go = [&](auto kern, int et, int tt) {
     const int64_t ctas = static_cast<int64_t>((rows + et - 1) / et) * ((T + tt - 1) / tt);
     if (ctas >= (1LL << 31)) return wm::fail(WM_ERR_INVALID, "router: too many tokens");
-    kern<<<static_cast<int>(ctas), 128, 0, stream>>>(x, wg, wg_shared, logit_bias, T, H, E, logits, shared_raw);
+    if (cudaError_t e = wm::launch_pdl(kern, dim3(static_cast<unsigned>(ctas)), dim3(128), 0, stream, x, wg, wg_shared,
+                                       logit_bias, T, H, E, logits, shared_raw))
+      return wm::fail(WM_ERR_CUDA, std::string("router logits: ") + cudaGetErrorString(e));
     return wm::check_launch("router logits");
   };
   if (T <= 1) return go(k_router_logits<2, 1>, 2, 1);
@@ -136,6 +140,8 @@ __global__ void __launch_bounds__(128) k_router_topk(const float *__restrict__ l
                                                      int score_fn, float norm_eps, float route_scale,
                                                      int32_t *__restrict__ idx, float *__restrict__ weights,
                                                      float *__restrict__ shared_w) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * 4 + (threadIdx.x >> 5);
   if (t >= T) return;
@@ -225,8 +231,10 @@ int launch_router_topk(const float *logits, const float *select_bias, int T, int
                        cudaStream_t stream) {
   const int grid = (T + 3) / 4;
   const int per = (E + 31) / 32;
-#define WM_TOPK(P) k_router_topk<P><<<grid, 128, 0, stream>>>(logits, select_bias, T, E, k, score_fn, norm_eps, \
-                                                              route_scale, idx, weights, shared_w)
+#define WM_TOPK(P)                                                                                              \
+  err = wm::launch_pdl(k_router_topk<P>, dim3(grid), dim3(128), 0, stream, logits, select_bias, T, E, k, score_fn, \
+                       norm_eps, route_scale, idx, weights, shared_w)
+  cudaError_t err = cudaSuccess;
   if (per <= 1) WM_TOPK(1);
   else if (per <= 2) WM_TOPK(2);
   else if (per <= 4) WM_TOPK(4);
@@ -234,6 +242,7 @@ int launch_router_topk(const float *logits, const float *select_bias, int T, int
   else if (per <= 16) WM_TOPK(16);
   else WM_TOPK(32);
 #undef WM_TOPK
+  if (err != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("router topk: ") + cudaGetErrorString(err));
   return wm::check_launch("router topk");
 }
 

@@ -32,6 +32,33 @@ inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_
 // Grid size helper: a multiple of the SM count (148 on B200), capped by work.
 int sm_count();
 
+
+// Programmatic dependent launch for the kernels of the MoE path: they are
+// launched with programmatic stream serialization, so a kernel's CTAs may be
+// scheduled (and run their set-up) while the previous kernel on the stream is
+// still finishing.  Each kernel executes WM_PDL_WAIT() before it reads what
+// earlier kernels wrote (it returns once those grids have completed and their
+// memory is visible; a no-op for an ordinary launch) and WM_PDL_LAUNCH() to
+// let its own successor be scheduled.
+#define WM_PDL_WAIT() asm volatile("griddepcontrol.wait;" ::: "memory")
+#define WM_PDL_LAUNCH() asm volatile("griddepcontrol.launch_dependents;" ::: "memory")
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 }  // namespace wm
 
 #define WM_REQUIRE(cond, msg)                                   \
