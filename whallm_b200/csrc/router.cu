@@ -62,27 +62,39 @@ __global__ void __launch_bounds__(128) k_router_logits(const uint16_t *__restric
   for (int a = 0; a < ET; ++a)
 #pragma unroll
     for (int b = 0; b < TT; ++b) acc[a][b] = 0.0f;
-#pragma unroll 2
-  for (int i = i0; i < i1; ++i) {
-    const int base = 256 * i + 8 * lane;
-    if (base < H) {
-      uint4 wu[ET], xu[TT];
+  // loads of D column blocks are issued before any of them is consumed: small
+  // tiles (decode) keep a whole segment in flight, large tiles two blocks
+  constexpr int D = (ET + TT <= 4) ? 8 : 2;
+  for (int i0c = i0; i0c < i1; i0c += D) {
+    uint4 wu[D][ET], xu[D][TT];
 #pragma unroll
-      for (int a = 0; a < ET; ++a) wu[a] = __ldg(reinterpret_cast<const uint4 *>(wrow[a] + base));
+    for (int d = 0; d < D; ++d) {
+      const int base = 256 * (i0c + d) + 8 * lane;
+      const bool live = i0c + d < i1 && base < H;
 #pragma unroll
-      for (int b = 0; b < TT; ++b) xu[b] = __ldg(reinterpret_cast<const uint4 *>(xrow[b] + base));
+      for (int a = 0; a < ET; ++a)
+        wu[d][a] = live ? __ldg(reinterpret_cast<const uint4 *>(wrow[a] + base)) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int b = 0; b < TT; ++b)
+        xu[d][b] = live ? __ldg(reinterpret_cast<const uint4 *>(xrow[b] + base)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int d = 0; d < D; ++d) {
+      const int base = 256 * (i0c + d) + 8 * lane;
+      if (!(i0c + d < i1 && base < H)) continue;        // the chain skips absent pieces exactly as before
       float xv[TT][8];                                  // each token piece converted once per block
 #pragma unroll
       for (int b = 0; b < TT; ++b) {
-        xv[b][0] = wm_bf16lo(xu[b].x); xv[b][1] = wm_bf16hi(xu[b].x);
-        xv[b][2] = wm_bf16lo(xu[b].y); xv[b][3] = wm_bf16hi(xu[b].y);
-        xv[b][4] = wm_bf16lo(xu[b].z); xv[b][5] = wm_bf16hi(xu[b].z);
-        xv[b][6] = wm_bf16lo(xu[b].w); xv[b][7] = wm_bf16hi(xu[b].w);
+        xv[b][0] = wm_bf16lo(xu[d][b].x); xv[b][1] = wm_bf16hi(xu[d][b].x);
+        xv[b][2] = wm_bf16lo(xu[d][b].y); xv[b][3] = wm_bf16hi(xu[d][b].y);
+        xv[b][4] = wm_bf16lo(xu[d][b].z); xv[b][5] = wm_bf16hi(xu[d][b].z);
+        xv[b][6] = wm_bf16lo(xu[d][b].w); xv[b][7] = wm_bf16hi(xu[d][b].w);
       }
 #pragma unroll
       for (int a = 0; a < ET; ++a) {
-        const float wv[8] = {wm_bf16lo(wu[a].x), wm_bf16hi(wu[a].x), wm_bf16lo(wu[a].y), wm_bf16hi(wu[a].y),
-                             wm_bf16lo(wu[a].z), wm_bf16hi(wu[a].z), wm_bf16lo(wu[a].w), wm_bf16hi(wu[a].w)};
+        const float wv[8] = {wm_bf16lo(wu[d][a].x), wm_bf16hi(wu[d][a].x), wm_bf16lo(wu[d][a].y),
+                             wm_bf16hi(wu[d][a].y), wm_bf16lo(wu[d][a].z), wm_bf16hi(wu[d][a].z),
+                             wm_bf16lo(wu[d][a].w), wm_bf16hi(wu[d][a].w)};
 #pragma unroll
         for (int b = 0; b < TT; ++b) {
           float v = acc[a][b];
@@ -186,28 +198,36 @@ __global__ void __launch_bounds__(128) k_router_topk(const float *__restrict__ l
     if (e < E) kv = select_bias ? sc[j] + select_bias[e] : sc[j];
     key[j] = (kv != kv) ? kNegInf : kv;
   }
+  // Keys as order-preserving unsigned bits (-0 folded into +0, so equal
+  // floats stay equal); each round takes the warp maximum of the lanes' best
+  // untaken keys, then the lowest expert id among the lanes holding it.
+  uint32_t kb[PER];
+#pragma unroll
+  for (int j = 0; j < PER; ++j) {
+    const uint32_t b = __float_as_uint(key[j] == 0.0f ? 0.0f : key[j]);
+    kb[j] = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  }
   uint32_t taken = 0u;                                // bit j: expert lane + 32 j selected
   float my_w = 0.0f;
   int32_t my_i = 0;
   for (int r = 0; r < k; ++r) {
-    float bk = kNegInf, bs = 0.0f;
-    int be = 0x7fffffff;
+    uint32_t best = 0u;                               // below every key (-inf maps to 0x007fffff)
+    int bj = -1;
 #pragma unroll
     for (int j = 0; j < PER; ++j) {
-      const int e = lane + 32 * j;
-      if (e < E && !((taken >> j) & 1u) && (key[j] > bk || (key[j] == bk && e < be))) {
-        bk = key[j];
-        be = e;
-        bs = sc[j];
+      if (lane + 32 * j < E && !((taken >> j) & 1u) && (bj < 0 || kb[j] > best)) {
+        best = kb[j];
+        bj = j;
       }
     }
+    const uint32_t wbest = __reduce_max_sync(0xffffffffu, bj < 0 ? 0u : best);
+    const int cand = (bj >= 0 && best == wbest) ? lane + 32 * bj : 0x7fffffff;
+    const int be = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
+    float bs = 0.0f;
 #pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) {
-      const float ok = __shfl_xor_sync(0xffffffffu, bk, m);
-      const int oe = __shfl_xor_sync(0xffffffffu, be, m);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, m);
-      if (ok > bk || (ok == bk && oe < be)) { bk = ok; be = oe; bs = os; }
-    }
+    for (int j = 0; j < PER; ++j)
+      if (lane + 32 * j == be) bs = sc[j];
+    bs = __shfl_sync(0xffffffffu, bs, be & 31);
     if ((be & 31) == lane) taken |= 1u << (be >> 5);
     if (lane == r) { my_w = bs; my_i = be; }
   }
