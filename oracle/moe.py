@@ -116,7 +116,8 @@ def switch_mlp(x_f32, idx, experts):
 
 
 def moe_forward(x_f32, idx, weights, experts, shared_expert=None, shared_weight=None):
-    """Routed combine plus optional shared expert, float32 accumulation, bf16 result.
+    """Routed combine plus optional shared expert over bf16 expert outputs (the
+    dtype switch_mlp and shared_experts return), float32 accumulation, bf16 result.
 
     ``shared_expert`` is an expert id of ``experts`` run for every token with
     weight ``shared_weight[t]`` (1.0 when None), following
@@ -132,12 +133,12 @@ def moe_forward(x_f32, idx, weights, experts, shared_expert=None, shared_weight=
         if len(pos) == 0:
             continue
         e = int(flat[pos[0]])
-        y = experts.ffn(e, x[pos // k])
+        y = F.round_bf16(experts.ffn(e, x[pos // k]))      # switch_mlp returns bf16 rows
         if out is None:
             out = np.zeros((T, y.shape[-1]), np.float32)
         np.add.at(out, pos // k, y * w[pos][:, None])
     if shared_expert is not None:
-        y = experts.ffn(int(shared_expert), x)
+        y = F.round_bf16(experts.ffn(int(shared_expert), x))
         sw = np.ones((T,), np.float32) if shared_weight is None else np.asarray(shared_weight, np.float32)
         out = y * sw[:, None] if out is None else out + y * sw[:, None]
     return F.round_bf16(out)

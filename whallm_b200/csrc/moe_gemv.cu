@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
     k_expert_gemv(const uint16_t *__restrict__ in, int kk, const int32_t *__restrict__ offsets,
                   const int32_t *__restrict__ perm, const int32_t *__restrict__ active,
                   const int32_t *__restrict__ counters, Weights W, int I, int order, float limit,
-                  uint16_t *__restrict__ h_out, float *__restrict__ y_out) {
+                  uint16_t *__restrict__ h_out, uint16_t *__restrict__ y_out) {
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 #pragma unroll
               for (int tt = 0; tt < kNT; ++tt)
                 if (rr == r && tt == t) v = acc[rr][tt];
-            y_out[static_cast<int64_t>(p0 + c + t) * W.rows + row[r]] = v;
+            y_out[static_cast<int64_t>(p0 + c + t) * W.rows + row[r]] = wm_f32_to_bf16(v);
           }
         }
       }
@@ -191,12 +191,13 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
   }
 }
 
-// out[t, :] = sum_j w[t,j] * y[inv[t*kk+j], :] (+ shared_w[t] * y[inv[t*kk+k], :]), fixed order,
-// rounded once to bf16 (F32_OUT false) or kept in f32 (an expert-parallel partial sum).
+// out[t, :] = sum_j w[t,j] * y[inv[t*kk+j], :] (+ shared_w[t] * y[inv[t*kk+k], :]) over the bf16
+// expert outputs y, accumulated in f32 in a fixed order and rounded once to bf16 (F32_OUT false)
+// or kept in f32 (an expert-parallel partial sum).
 // A set error flag (expert id out of range) yields zeros; slots are bounds-checked and
 // dropped assignments (slot -1) contribute nothing.
 template <bool F32_OUT>
-__global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict__ inv, const float *__restrict__ w,
+__global__ void k_combine(const uint16_t *__restrict__ y, const int32_t *__restrict__ inv, const float *__restrict__ w,
                           const float *__restrict__ shared_w, const int32_t *__restrict__ err, int T, int k, int kk,
                           int H, void *__restrict__ out_v) {
   WM_PDL_WAIT();
@@ -208,8 +209,9 @@ __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int t = static_cast<int>(i / per_row), c8 = static_cast<int>(i % per_row) * 8;
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    // slots and weights of 8 assignments, then their 8 rows in flight together,
-    // then the fmaf chain in slot order
+    // slots and weights of 8 assignments, then their 8 rows (bf16, as the
+    // reference's switch_mlp returns them) in flight together, then the fmaf
+    // chain in slot order
     for (int j0 = 0; j0 < kk && !bad; j0 += 8) {
       int sl[8];
       float wt[8];
@@ -219,26 +221,19 @@ __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict
         sl[u] = j < kk ? inv[static_cast<int64_t>(t) * kk + j] : -1;
         wt[u] = j < k ? w[static_cast<int64_t>(t) * k + j] : (j < kk && shared_w ? shared_w[t] : 1.0f);
       }
-      float4 a[8], b[8];
+      uint4 a[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (sl[u] >= 0 && sl[u] < S) {
-          const float4 *yp = reinterpret_cast<const float4 *>(y + static_cast<int64_t>(sl[u]) * H + c8);
-          a[u] = yp[0];
-          b[u] = yp[1];
-        } else {
-          a[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-          b[u] = a[u];
-        }
-      }
+      for (int u = 0; u < 8; ++u)
+        a[u] = (sl[u] >= 0 && sl[u] < S) ? *reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(sl[u]) * H + c8)
+                                         : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
         if (sl[u] < 0 || sl[u] >= S) continue;
         const float wv = wt[u];
-        acc[0] = fmaf(wv, a[u].x, acc[0]); acc[1] = fmaf(wv, a[u].y, acc[1]);
-        acc[2] = fmaf(wv, a[u].z, acc[2]); acc[3] = fmaf(wv, a[u].w, acc[3]);
-        acc[4] = fmaf(wv, b[u].x, acc[4]); acc[5] = fmaf(wv, b[u].y, acc[5]);
-        acc[6] = fmaf(wv, b[u].z, acc[6]); acc[7] = fmaf(wv, b[u].w, acc[7]);
+        acc[0] = fmaf(wv, wm_bf16lo(a[u].x), acc[0]); acc[1] = fmaf(wv, wm_bf16hi(a[u].x), acc[1]);
+        acc[2] = fmaf(wv, wm_bf16lo(a[u].y), acc[2]); acc[3] = fmaf(wv, wm_bf16hi(a[u].y), acc[3]);
+        acc[4] = fmaf(wv, wm_bf16lo(a[u].z), acc[4]); acc[5] = fmaf(wv, wm_bf16hi(a[u].z), acc[5]);
+        acc[6] = fmaf(wv, wm_bf16lo(a[u].w), acc[6]); acc[7] = fmaf(wv, wm_bf16hi(a[u].w), acc[7]);
       }
     }
     if constexpr (F32_OUT) {
@@ -256,9 +251,9 @@ __global__ void k_combine(const float *__restrict__ y, const int32_t *__restrict
   }
 }
 
-// out[t, j, :] = bf16(y[inv[t*k+j], :])  (un-reduced switch_mlp output)
-__global__ void k_unsort(const float *__restrict__ y, const int32_t *__restrict__ inv, const int32_t *__restrict__ err,
-                         int S, int H, uint16_t *__restrict__ out) {
+// out[t, j, :] = y[inv[t*k+j], :]  (un-reduced switch_mlp output, bf16)
+__global__ void k_unsort(const uint16_t *__restrict__ y, const int32_t *__restrict__ inv,
+                         const int32_t *__restrict__ err, int S, int H, uint16_t *__restrict__ out) {
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
   const int per_row = H / 8;
@@ -267,18 +262,9 @@ __global__ void k_unsort(const float *__restrict__ y, const int32_t *__restrict_
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int a = static_cast<int>(i / per_row), c8 = static_cast<int>(i % per_row) * 8;
     const int slot = inv[a];
-    float4 p = make_float4(0.f, 0.f, 0.f, 0.f), q = p;
-    if (!bad && slot >= 0 && slot < S) {
-      const float4 *yp = reinterpret_cast<const float4 *>(y + static_cast<int64_t>(slot) * H + c8);
-      p = yp[0];
-      q = yp[1];
-    }
-    uint4 o;
-    o.x = wm_f32_to_bf16(p.x) | (static_cast<uint32_t>(wm_f32_to_bf16(p.y)) << 16);
-    o.y = wm_f32_to_bf16(p.z) | (static_cast<uint32_t>(wm_f32_to_bf16(p.w)) << 16);
-    o.z = wm_f32_to_bf16(q.x) | (static_cast<uint32_t>(wm_f32_to_bf16(q.y)) << 16);
-    o.w = wm_f32_to_bf16(q.z) | (static_cast<uint32_t>(wm_f32_to_bf16(q.w)) << 16);
-    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(a) * H + c8) = o;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (!bad && slot >= 0 && slot < S) v = *reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(slot) * H + c8);
+    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(a) * H + c8) = v;
   }
 }
 
@@ -375,7 +361,7 @@ int run(const Args &a, int fmt) {
     cudaError_t e = wm::launch_pdl(up, dim3(grid), dim3(kWarps * 32), 0, a.stream, x, kk,
                                    static_cast<const int32_t *>(ws.offsets), static_cast<const int32_t *>(ws.perm),
                                    static_cast<const int32_t *>(ws.active), static_cast<const int32_t *>(ws.counters),
-                                   a.w13, a.I, a.order, a.limit, ws.h, static_cast<float *>(nullptr));
+                                   a.w13, a.I, a.order, a.limit, ws.h, static_cast<uint16_t *>(nullptr));
     if (e == cudaSuccess)
       e = wm::launch_pdl(down, dim3(grid), dim3(kWarps * 32), 0, a.stream, static_cast<const uint16_t *>(ws.h), kk,
                          static_cast<const int32_t *>(ws.offsets), static_cast<const int32_t *>(ws.perm),
@@ -388,15 +374,15 @@ int run(const Args &a, int fmt) {
   const int cgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((cwork + 255) / 256, wm::sm_count() * 8)));
   cudaError_t e;
   if (a.reduce && a.out_f32)
-    e = wm::launch_pdl(k_combine<true>, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const float *>(ws.y),
+    e = wm::launch_pdl(k_combine<true>, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const uint16_t *>(ws.y),
                        static_cast<const int32_t *>(ws.inv), a.weights, a.shared_w,
                        static_cast<const int32_t *>(ws.counters + 1), a.T, a.k, kk, a.H, static_cast<void *>(a.out_f32));
   else if (a.reduce)
-    e = wm::launch_pdl(k_combine<false>, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const float *>(ws.y),
+    e = wm::launch_pdl(k_combine<false>, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const uint16_t *>(ws.y),
                        static_cast<const int32_t *>(ws.inv), a.weights, a.shared_w,
                        static_cast<const int32_t *>(ws.counters + 1), a.T, a.k, kk, a.H, static_cast<void *>(a.out));
   else
-    e = wm::launch_pdl(k_unsort, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const float *>(ws.y),
+    e = wm::launch_pdl(k_unsort, dim3(cgrid), dim3(256), 0, a.stream, static_cast<const uint16_t *>(ws.y),
                        static_cast<const int32_t *>(ws.inv), static_cast<const int32_t *>(ws.counters + 1), S, a.H,
                        a.out);
   if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("expert combine: ") + cudaGetErrorString(e));

@@ -108,7 +108,7 @@ struct MxParams {
   uint8_t *h_hi, *h_lo;     // up, fused split: [S_pad, I] e4m3 terms of the bf16 SwiGLU output
   uint8_t *h_sc;             // up, fused split: [S_pad, I/32] E8M0 scale of h_hi
   uint16_t *h_out;           // up, separate split: [S_pad, I] bf16
-  float *y_out;              // down: [S, H] f32
+  uint16_t *y_out;           // down: [S, H] bf16
   int32_t *err;
 };
 
@@ -508,7 +508,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const int row = m * kM + t;
 #pragma unroll
           for (int q = 0; q < 16; ++q)
-            if (c0 + q < n) p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = __uint_as_float(r[q]);
+            if (c0 + q < n)
+              p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = wm_f32_to_bf16(__uint_as_float(r[q]));
         }
       }
       tc_fence_before();
@@ -597,7 +598,7 @@ template <class C>
 int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K, const uint8_t *b_hi,
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-                  uint16_t *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
+                  uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
   if (!wm::aligned(w, 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed weights must be 32-byte aligned");
   if (!wm::aligned(a_scales, 16) || !wm::aligned(b_sc, 16))
@@ -673,7 +674,7 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
 int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
               const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
               float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-              uint16_t *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
+              uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
   if (decode)
     return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
                                    n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
@@ -719,7 +720,7 @@ int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, co
 
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
-                   float *y, int32_t *err, int tile_n, cudaStream_t stream) {
+                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream) {
   return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, I, H, WM_UP_GATE, 0.0f,
                    tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream);
 }

@@ -93,7 +93,7 @@ struct TcParams {
   const int4 *tiles;     // {expert, first slot, tokens, 0}
   const int32_t *n_tiles;
   __half *h_out;         // up: [S, I] f16, h * 2^-4
-  float *y_out;          // down: [S, H] f32
+  uint16_t *y_out;       // down: [S, H] bf16
   int32_t *err;
 };
 
@@ -415,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int row = m * kM + t;
 #pragma unroll
           for (int q = 0; q < 16; ++q)
-            if (c0 + q < n) p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = __uint_as_float(r[q]) * 0x1p-8f;
+            if (c0 + q < n)
+              p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = wm_f32_to_bf16(__uint_as_float(r[q]) * 0x1p-8f);
         }
       }
       tc_fence_before();
@@ -458,7 +459,7 @@ __global__ void k_gather_f16(const uint16_t *__restrict__ x, const int32_t *__re
 template <class C>
 int launch_tc_cfg(int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K, const __half *bmat,
                   int S_rows, int I, int H, int order, float limit, const int4 *tiles, const int32_t *n_tiles,
-                  __half *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
+                  __half *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert tc: K must be a multiple of the stage depth");
   CUtensorMap tmA, tmB;
   if (int rc = make_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K / 2, static_cast<uint64_t>(E) * rows, K / 2,
@@ -501,7 +502,7 @@ int launch_tc_cfg(int mode, const uint8_t *w, const uint8_t *scales, int E, int 
 
 int launch_tc(bool decode, int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K,
               const __half *bmat, int S_rows, int I, int H, int order, float limit, const int4 *tiles,
-              const int32_t *n_tiles, __half *h_out, float *y_out, int32_t *err, cudaStream_t stream) {
+              const int32_t *n_tiles, __half *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
   if (decode)
     return launch_tc_cfg<DecodeCfg>(mode, w, scales, E, rows, K, bmat, S_rows, I, H, order, limit, tiles, n_tiles,
                                     h_out, y_out, err, stream);
@@ -533,7 +534,7 @@ int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, co
 }
 
 int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
-                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, int tile_n, cudaStream_t stream) {
+                   const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream) {
   return launch_tc(tile_n == DecodeCfg::kNMax, 1, w2, s2, E, H, I, static_cast<const __half *>(h16), S_rows, I, H, WM_UP_GATE, 0.0f, tiles,
                    n_tiles, nullptr, y, err, stream);
 }

@@ -33,7 +33,7 @@ int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, co
                  float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, int tile_n,
                  cudaStream_t stream);
 int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
-                   const int4 *tiles, const int32_t *n_tiles, float *y, int32_t *err, int tile_n, cudaStream_t stream);
+                   const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream);
 
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
@@ -50,7 +50,7 @@ int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, co
                  int tile_n, cudaStream_t stream);
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
-                   float *y, int32_t *err, int tile_n, cudaStream_t stream);
+                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream);
 
 // Workspace carved out of the caller's buffer for one expert-forward call.
 // S = T * (k + has_shared) assignments.
@@ -67,7 +67,7 @@ struct MoeWorkspace {
   uint8_t *x_sc;       // [S_pad, H/32] E8M0 scale of x_hi
   uint8_t *h_hi, *h_lo;  // [S_pad, I] e4m3 terms of h
   uint8_t *h_sc;       // [S_pad, I/32]
-  float *y;            // [S, H] f32 expert outputs in sorted-slot order
+  uint16_t *y;         // [S, H] bf16 expert outputs in sorted-slot order (the reference switch_mlp dtype)
   int s_pad;           // S rounded up to at least 16 rows (TMA box height)
   size_t bytes;
 };
@@ -95,7 +95,7 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
   size_t o_xsc = take(S_pad * (H / 32));
   size_t o_h8 = take(S_pad * I * 2);
   size_t o_hsc = take(S_pad * (I / 32));
-  size_t o_y = take(S * H * sizeof(float));
+  size_t o_y = take(S * H * sizeof(uint16_t));
   w.s_pad = static_cast<int>(S_pad);
   w.bytes = off;
   if (base) {
@@ -114,7 +114,7 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
     w.h_hi = reinterpret_cast<uint8_t *>(b + o_h8);
     w.h_lo = w.h_hi + S_pad * I;
     w.h_sc = reinterpret_cast<uint8_t *>(b + o_hsc);
-    w.y = reinterpret_cast<float *>(b + o_y);
+    w.y = reinterpret_cast<uint16_t *>(b + o_y);
   }
   return w;
 }
