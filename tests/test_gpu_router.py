@@ -61,7 +61,8 @@ def test_router_golden(dev, case):
 
 
 @pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SIGMOID, R.SCORE_SQRTSOFTPLUS])
-@pytest.mark.parametrize("shape", [(1, 7168, 256, 8), (37, 2048, 512, 10), (5, 1024, 16, 4), (9, 264, 100, 1)])
+@pytest.mark.parametrize("shape", [(1, 7168, 256, 8), (37, 2048, 512, 10), (5, 1024, 16, 4), (9, 264, 100, 1),
+                                   (300, 7168, 256, 8), (129, 2056, 33, 3)])
 def test_router_random_vs_oracle(dev, fn, shape):
     T, H, E, k = shape
     rng = np.random.default_rng(T * 131 + E + fn)

@@ -122,6 +122,103 @@ __global__ void __launch_bounds__(128) k_router_logits(const uint16_t *__restric
   }
 }
 
+// Large-T variant: the same chains for an (ET experts x TT tokens) tile, with
+// each lane's 8-element pieces of the next column block copied with cp.async
+// into its own slots of a double-buffered shared-memory stage while the
+// current block is computed (no registers held by loads in flight), so the
+// tile can be large enough for the FMAs, not the loads, to set the pace.
+template <int ET, int TT>
+__global__ void __launch_bounds__(128) k_router_logits_staged(const uint16_t *__restrict__ x,
+                                                              const uint16_t *__restrict__ wg,
+                                                              const uint16_t *__restrict__ wg_shared,
+                                                              const float *__restrict__ logit_bias, int T, int H,
+                                                              int E, float *__restrict__ logits,
+                                                              float *__restrict__ shared_raw) {
+  extern __shared__ __align__(16) uint4 stage[];        // [4 warps][2 buffers][ET + TT rows][32 lanes]
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
+  const int lane = threadIdx.x & 31, seg = threadIdx.x >> 5;
+  const int rows = E + (wg_shared ? 1 : 0);
+  const int egroups = (rows + ET - 1) / ET;
+  const int e0 = (blockIdx.x % egroups) * ET;
+  const int t0 = (blockIdx.x / egroups) * TT;
+  const uint16_t *src[ET + TT];
+#pragma unroll
+  for (int a = 0; a < ET; ++a) {
+    const int e = min(e0 + a, rows - 1);
+    src[a] = e < E ? wg + static_cast<int64_t>(e) * H : wg_shared;
+  }
+#pragma unroll
+  for (int b = 0; b < TT; ++b) src[ET + b] = x + static_cast<int64_t>(min(t0 + b, T - 1)) * H;
+  const int n = (H + 255) / 256;
+  const int i0 = (seg * n) / kSegs, i1 = ((seg + 1) * n) / kSegs;
+  uint4 *mine = stage + seg * 2 * (ET + TT) * 32;
+  auto issue = [&](int i, int buf) {
+    const int base = 256 * i + 8 * lane;
+    if (i < i1 && base < H) {
+#pragma unroll
+      for (int r = 0; r < ET + TT; ++r) {
+        const uint32_t dst = static_cast<uint32_t>(__cvta_generic_to_shared(mine + (buf * (ET + TT) + r) * 32 + lane));
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src[r] + base) : "memory");
+      }
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  float acc[ET][TT];
+#pragma unroll
+  for (int a = 0; a < ET; ++a)
+#pragma unroll
+    for (int b = 0; b < TT; ++b) acc[a][b] = 0.0f;
+  issue(i0, 0);
+  for (int i = i0; i < i1; ++i) {
+    const int buf = (i - i0) & 1;
+    issue(i + 1, buf ^ 1);
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    if (256 * i + 8 * lane >= H) continue;            // the chain skips absent pieces exactly as before
+    const uint4 *row = mine + buf * (ET + TT) * 32 + lane;
+    float wv[ET][8];
+#pragma unroll
+    for (int a = 0; a < ET; ++a) {
+      const uint4 u = row[a * 32];
+      wv[a][0] = wm_bf16lo(u.x); wv[a][1] = wm_bf16hi(u.x); wv[a][2] = wm_bf16lo(u.y); wv[a][3] = wm_bf16hi(u.y);
+      wv[a][4] = wm_bf16lo(u.z); wv[a][5] = wm_bf16hi(u.z); wv[a][6] = wm_bf16lo(u.w); wv[a][7] = wm_bf16hi(u.w);
+    }
+#pragma unroll
+    for (int b = 0; b < TT; ++b) {
+      const uint4 u = row[(ET + b) * 32];
+      const float xv[8] = {wm_bf16lo(u.x), wm_bf16hi(u.x), wm_bf16lo(u.y), wm_bf16hi(u.y),
+                           wm_bf16lo(u.z), wm_bf16hi(u.z), wm_bf16lo(u.w), wm_bf16hi(u.w)};
+#pragma unroll
+      for (int a = 0; a < ET; ++a) {
+        float v = acc[a][b];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v = fmaf(xv[j], wv[a][j], v);
+        acc[a][b] = v;
+      }
+    }
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();                                      // the stage is reused for the partials below
+  float *part = reinterpret_cast<float *>(stage);       // [kSegs][ET * TT][32]
+#pragma unroll
+  for (int a = 0; a < ET; ++a)
+#pragma unroll
+    for (int b = 0; b < TT; ++b) part[(seg * ET * TT + a * TT + b) * 32 + lane] = acc[a][b];
+  __syncthreads();
+  for (int pidx = seg; pidx < ET * TT; pidx += kSegs) {
+    float v = ((part[(0 * ET * TT + pidx) * 32 + lane] + part[(1 * ET * TT + pidx) * 32 + lane]) +
+               part[(2 * ET * TT + pidx) * 32 + lane]) +
+              part[(3 * ET * TT + pidx) * 32 + lane];
+#pragma unroll
+    for (int m = 16; m >= 1; m >>= 1) v = v + __shfl_xor_sync(0xffffffffu, v, m);
+    const int e = e0 + pidx / TT, t = t0 + pidx % TT;
+    if (lane == 0 && e < rows && t < T) {
+      if (e < E) logits[static_cast<int64_t>(t) * E + e] = logit_bias ? v + logit_bias[e] : v;
+      else shared_raw[t] = v;
+    }
+  }
+}
+
 // Tile shape by batch: enough CTAs to stream the gate matrix at small T, and
 // register-resident reuse of every load (ET x TT chains) at large T.
 int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *wg_shared, const float *logit_bias,
@@ -138,7 +235,31 @@ int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *
   if (T <= 1) return go(k_router_logits<2, 1>, 2, 1);
   if (T <= 4) return go(k_router_logits<2, 4>, 2, 4);
   if (T <= 16) return go(k_router_logits<2, 8>, 2, 8);
-  return go(k_router_logits<4, 8>, 4, 8);
+  if (T <= 64) return go(k_router_logits<4, 8>, 4, 8);
+  // large T: staged 8 x 16 tiles; stage = 4 warps x 2 buffers x 24 rows x 512 B = 96 KB, which also holds the
+  // 4 x 128 x 32 partial sums (64 KB) afterwards
+  constexpr int ET = 8, TT = 16;
+  constexpr size_t smem = static_cast<size_t>(kSegs) * 2 * (ET + TT) * 32 * sizeof(uint4);
+  static_assert(smem >= static_cast<size_t>(kSegs) * ET * TT * 32 * sizeof(float), "stage must hold the partials");
+  static std::mutex mu;
+  static bool attr_set[64] = {false};                    // per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return wm::fail(WM_ERR_CUDA, "router: no device");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_set[dev]) {
+      if (cudaError_t e = cudaFuncSetAttribute(k_router_logits_staged<ET, TT>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)))
+        return wm::fail(WM_ERR_CUDA, std::string("router logits smem: ") + cudaGetErrorString(e));
+      attr_set[dev] = true;
+    }
+  }
+  const int64_t ctas = static_cast<int64_t>((rows + ET - 1) / ET) * ((T + TT - 1) / TT);
+  if (ctas >= (1LL << 31)) return wm::fail(WM_ERR_INVALID, "router: too many tokens");
+  if (cudaError_t e = wm::launch_pdl(k_router_logits_staged<ET, TT>, dim3(static_cast<unsigned>(ctas)), dim3(128),
+                                     smem, stream, x, wg, wg_shared, logit_bias, T, H, E, logits, shared_raw))
+    return wm::fail(WM_ERR_CUDA, std::string("router logits: ") + cudaGetErrorString(e));
+  return wm::check_launch("router logits");
 }
 
 // One warp per token (4 tokens per CTA): lane l holds the scores of experts
