@@ -334,11 +334,10 @@ int run(const Args &a, int fmt) {
   const int grid = wm::sm_count() * 2;
   if (mx) {
     const int32_t *count = ws.offsets + a.E;
-    // each token's two e4m3 terms once; the up projection gathers them by token
-    if (int rc = wm::launch_split_e4m3(a.x, nullptr, nullptr, a.T, 1, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
+    if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
       return rc;
-    if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, a.T, ws.perm, kk,
-                                  a.order, a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.h,
+    if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, ws.s_pad, a.order,
+                                  a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.h,
                                   ws.counters + 3, tile_n, a.stream))
       return rc;
     if (!wm::mx_fused_split(tile_n))

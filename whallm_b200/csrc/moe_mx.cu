@@ -102,9 +102,7 @@ struct MxParams {
   float limit;
   int m_tiles;               // 128-row work items per tile
   const uint8_t *a_scales;   // [E * rows, K/32] E8M0 (the MXFP4 scales)
-  const uint8_t *b_scales;   // up: [T, K/32] per token; down: [S_pad, K/32] per slot (hi-term E8M0)
-  const int32_t *perm;       // up: sorted slot -> flat assignment (token = perm / kk), for gathered token rows
-  int kk;
+  const uint8_t *b_scales;   // [S_pad, K/32] hi-term E8M0 in slot order
   const int4 *tiles;         // {expert, first slot, tokens, 0}
   const int32_t *n_tiles;
   uint8_t *h_hi, *h_lo;     // up, fused split: [S_pad, I] e4m3 terms of the bf16 SwiGLU output
@@ -113,17 +111,6 @@ struct MxParams {
   uint16_t *y_out;           // down: [S, H] bf16
   int32_t *err;
 };
-
-// Four rows (r0..r3) of a 2-D map whose box is one row high, written as four
-// consecutive rows of the destination (TMA gather; no multicast).
-__device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, int x, int r0, int r1, int r2, int r3,
-                                            uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-      "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
                                             uint64_t *bar) {
@@ -248,41 +235,12 @@ __global__ void __launch_bounds__(kMxThreads, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
-    // Up projection: the token rows of a tile are gathered by token id
-    // (4 rows per TMA instruction) from the per-token e4m3 terms; the ids of
-    // the next item are loaded one item ahead into registers (lane r holds
-    // rows r, r+32, ...) and published to shared memory at the item switch.
-    // Down projection: the SwiGLU rows are in slot order, loaded as boxes.
-    __shared__ int32_t s_tok[C::kNMax];
-    constexpr int kTokRegs = (C::kNMax + 31) / 32;
-    const int lane = threadIdx.x & 31;
-    int tok_next[kTokRegs];
-    auto load_toks = [&](const int4 &tl, int *dst) {   // raw perm entries: the loads are first used an item later
-#pragma unroll
-      for (int u = 0; u < kTokRegs; ++u) {
-        const int r = lane + 32 * u;
-        dst[u] = (p.mode == 0 && tl.z > 0 && r < C::kNMax) ? p.perm[tl.y + min(r, tl.z - 1)] : 0;
-      }
-    };
     uint32_t g = 0;
     bool ok = true;
-    TileCursor tc(p.tiles, p.m_tiles, n_items);
-    if (tc.valid()) load_toks(tc.cur, tok_next);
-    int4 toks_for = make_int4(-1, -1, -1, -1);         // tile whose ids are in s_tok
-    for (; tc.valid() && ok; tc.advance()) {
+    for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance()) {
       const int4 tile = tc.cur;
       const int m = tc.m();
       const int nb = (tile.z + 15) >> 4;                // 16-row token boxes per term
-      if (p.mode == 0) {
-        if (tile.x != toks_for.x || tile.y != toks_for.y) {
-#pragma unroll
-          for (int u = 0; u < kTokRegs; ++u)
-            if (lane + 32 * u < C::kNMax) s_tok[lane + 32 * u] = tok_next[u] / p.kk;
-          __syncwarp();
-          toks_for = tile;
-        }
-        load_toks(tc.nxt, tok_next);                    // every item: tok_next always holds the next item's tile
-      }
       for (int kc = 0; kc < kstages; ++kc, ++g) {
         const int s = g % S;
         if (!(ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 1))) break;
@@ -297,17 +255,9 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             else
               tma_load_2d(a, &tmA, x, tile.x * p.rows + m * kM, &full[s]);
             uint8_t *b = sB + s * C::kBStage + q * C::kBBox;
-            if (p.mode == 0) {
-              for (int j = 0; j < 4 * nb; ++j) {
-                const int r0 = s_tok[4 * j], r1 = s_tok[4 * j + 1], r2 = s_tok[4 * j + 2], r3 = s_tok[4 * j + 3];
-                tma_gather4(b + j * 4 * kKH, &tmBh, x, r0, r1, r2, r3, &full[s]);
-                tma_gather4(b + (4 * nb + j) * 4 * kKH, &tmBl, x, r0, r1, r2, r3, &full[s]);
-              }
-            } else {
-              for (int j = 0; j < nb; ++j) {
-                tma_load_2d(b + j * 16 * kKH, &tmBh, x, tile.y + 16 * j, &full[s]);
-                tma_load_2d(b + (nb + j) * 16 * kKH, &tmBl, x, tile.y + 16 * j, &full[s]);
-              }
+            for (int j = 0; j < nb; ++j) {
+              tma_load_2d(b + j * 16 * kKH, &tmBh, x, tile.y + 16 * j, &full[s]);
+              tma_load_2d(b + (nb + j) * 16 * kKH, &tmBl, x, tile.y + 16 * j, &full[s]);
             }
           }
         }
@@ -385,20 +335,6 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     };
     TileCursor cur(p.tiles, p.m_tiles, n_items);       // prefetch cursor
     int c_ch = 0;
-    // up projection: the B rows' scales are per token; the perm entries of this
-    // thread's rows are loaded one item ahead (-1: no token in the row)
-    int perm_cur[BA], perm_next[BA];
-    auto load_perm = [&](const int4 &tl, int *dst) {
-      const int n16 = max(16, (tl.z + 15) & ~15);
-#pragma unroll
-      for (int a = 0; a < BA; ++a) {
-        const int r = t + 128 * a;
-        const int ts = r >= n16 ? r - n16 : r;
-        dst[a] = (p.mode == 0 && tl.z > 0 && ts < tl.z && r < 2 * n16) ? p.perm[tl.y + ts] : -1;
-      }
-    };
-    load_perm(cur.cur, perm_cur);
-    load_perm(cur.nxt, perm_next);
     auto load_words = [&](const uint8_t *src, uint32_t *dst) {
       if (CW == 8) {
         const uint4 u0 = __ldg(reinterpret_cast<const uint4 *>(src));
@@ -434,17 +370,13 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         const bool lo_row = r >= n16;
         const int tok = lo_row ? r - n16 : r;
         if (tok < tile.z && r < 2 * n16) {
-          const int64_t brow = p.mode == 0 ? perm_cur[a] / p.kk : tile.y + tok;
-          load_words(p.b_scales + brow * ks32 + c_ch * 4 * CW, e.b[a]);
+          load_words(p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_ch * 4 * CW, e.b[a]);
           e.sub[a] = lo_row ? kLoSub : 0u;
         }
       }
       if (++c_ch == n_ch) {
         c_ch = 0;
         cur.advance();
-#pragma unroll
-        for (int a = 0; a < BA; ++a) perm_cur[a] = perm_next[a];
-        load_perm(cur.nxt, perm_next);
       }
     };
     const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -664,8 +596,7 @@ int make_map_nd(CUtensorMap *map, CUtensorMapDataType dt, int rank, const void *
 
 template <class C>
 int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K, const uint8_t *b_hi,
-                  const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, const int32_t *perm, int kk, int I, int H,
-                  int order, float limit,
+                  const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
                   uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
@@ -692,10 +623,9 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
       return rc;
   }
   {
-    // up: per-token rows gathered four at a time (box one row high); down: slot-ordered boxes of 16 rows
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(S_rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
-    const cuuint32_t box[2] = {kKH, mode == 0 ? 1u : 16u};
+    const cuuint32_t box[2] = {kKH, 16};
     if (int rc = make_map_nd(&tmBh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, b_hi, dims, strides, box,
                              CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
@@ -727,8 +657,6 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.m_tiles = mode == 0 ? I / 64 : rows / kM;
   p.a_scales = a_scales;
   p.b_scales = b_sc;
-  p.perm = perm;
-  p.kk = kk;
   p.tiles = tiles;
   p.n_tiles = n_tiles;
   p.h_hi = h_hi;
@@ -744,16 +672,13 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
 }
 
 int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
-              const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, const int32_t *perm, int kk,
-              int I, int H, int order,
+              const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
               float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
               uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
   if (decode)
-    return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, perm, kk, I, H, order,
-                                   limit, tiles,
+    return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
                                    n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
-  return launch_mx_cfg<MxPrefill>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, perm, kk, I, H, order,
-                                  limit, tiles,
+  return launch_mx_cfg<MxPrefill>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
                                   n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
 }
 
@@ -786,18 +711,18 @@ int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *c
 bool mx_fused_split(int tile_n) { return tile_n == MxDecode::kNMax ? MxDecode::kFuseSplit : MxPrefill::kFuseSplit; }
 
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
-                 const uint8_t *x_lo, const uint8_t *x_sc, int T, const int32_t *perm, int kk, int order, float limit,
-                 const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h,
-                 int32_t *err, int tile_n, cudaStream_t stream) {
-  return launch_mx(tile_n == MxDecode::kNMax, 0, w13, s13, E, 2 * I, H, x_hi, x_lo, x_sc, T, perm, kk, I, H, order,
-                   limit, tiles, n_tiles, h_hi, h_lo, h_sc, h, nullptr, err, stream);
+                 const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
+                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
+                 int tile_n, cudaStream_t stream) {
+  return launch_mx(tile_n == MxDecode::kNMax, 0, w13, s13, E, 2 * I, H, x_hi, x_lo, x_sc, S_rows, I, H, order, limit,
+                   tiles, n_tiles, h_hi, h_lo, h_sc, h, nullptr, err, stream);
 }
 
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
                    uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream) {
-  return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, nullptr, 1, I, H,
-                   WM_UP_GATE, 0.0f, tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream);
+  return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, I, H, WM_UP_GATE, 0.0f,
+                   tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream);
 }
 
 }  // namespace wm

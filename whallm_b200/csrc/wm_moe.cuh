@@ -44,11 +44,10 @@ int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *c
                       uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream);
 // the up projection writes h's e4m3 terms itself (true) or bf16 h for launch_split_e4m3 (false)
 bool mx_fused_split(int tile_n);
-// x_hi/x_lo/x_sc: per-token terms [T, H]; the tile's rows are gathered through perm (token = perm / kk)
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
-                 const uint8_t *x_lo, const uint8_t *x_sc, int T, const int32_t *perm, int kk, int order, float limit,
-                 const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h,
-                 int32_t *err, int tile_n, cudaStream_t stream);
+                 const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
+                 const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
+                 int tile_n, cudaStream_t stream);
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
                    uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream);
@@ -64,8 +63,8 @@ struct MoeWorkspace {
   int4 *tiles;         // [E + S/16 + 2] tensor-core work list
   uint16_t *h;         // [S_pad, I] SwiGLU output in sorted-slot order (bf16; f16 on the f16 tensor path)
   uint16_t *x16;       // [S_pad, H] f16 tokens in sorted-slot order (f16 tensor path)
-  uint8_t *x_hi, *x_lo;  // [T, H] e4m3 token terms, per token (block-scaled path; within the x16 bytes)
-  uint8_t *x_sc;       // [T, H/32] E8M0 scale of x_hi
+  uint8_t *x_hi, *x_lo;  // [S_pad, H] e4m3 token terms (block-scaled path; same bytes as x16)
+  uint8_t *x_sc;       // [S_pad, H/32] E8M0 scale of x_hi
   uint8_t *h_hi, *h_lo;  // [S_pad, I] e4m3 terms of h
   uint8_t *h_sc;       // [S_pad, I/32]
   uint16_t *y;         // [S, H] bf16 expert outputs in sorted-slot order (the reference switch_mlp dtype)
