@@ -320,9 +320,12 @@ def run_ep(args, rank, world, dev):
     name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn"}[wl]
     batches = {"ds_decode": SWEEP, "ds_prefill": (4096,), "qn_decode": (1, 32), "qn_prefill": (16384,)}[wl]
     decode = wl in ("ds_decode", "qn_decode")
+    # decode exchanges over peer memory (CUDA IPC + flags) unless WM_EP_EXCHANGE=nccl
+    peer = decode and os.environ.get("WM_EP_EXCHANGE", "peer") != "nccl"
     n_layers = args.layers
     moes = []
     cfg = None
+    bufs = None
     for i in range(n_layers):
         lay = S.make_layer(name, dev, seed=17 * i)          # identical weights on every rank
         cfg = lay.cfg
@@ -344,13 +347,19 @@ def run_ep(args, rank, world, dev):
 
             def gate_fn(x, state=state):
                 return state["sw"]
-        if decode:
+        if peer:
+            if bufs is None:
+                bufs = EP.PeerBuffers(max(batches), cfg["H"], cfg["k"], device=dev)
+            moes.append([EP.PeerGatheredMoE(router, local, E, B, bufs, limit, cfg["shared"], shared_gated=name != "ds")
+                         for B in batches])
+        elif decode:
             moes.append(EP.GatheredExpertParallelMoE(
                 router, EP.gpu_partial_experts(local, e0, per, E, limit, cfg["shared"]), E))
         else:
             moes.append(EP.ExpertParallelMoE(router, EP.gpu_local_experts(local, limit), E,
                                              shared=EP.gpu_shared_expert(local, per, limit, gate=gate_fn)))
-        moes[-1].route_fn = router
+        if not peer:
+            moes[-1].route_fn = router
         del lay
         torch.cuda.empty_cache()
     H = cfg["H"]
@@ -363,7 +372,8 @@ def run_ep(args, rank, world, dev):
     distinct = [0.0] * len(xs)
     for m in moes:
         for b, x in enumerate(xs):
-            idx = m.route_fn(x)[1].to(torch.int32).contiguous()
+            route_fn = m[b].router if isinstance(m, list) else m.route_fn
+            idx = route_fn(x)[1].to(torch.int32).contiguous()
             allidx = torch.empty((world * idx.shape[0], idx.shape[1]), dtype=idx.dtype, device=dev)
             torch.distributed.all_gather_into_tensor(allidx, idx)
             ids = set(allidx.flatten().tolist())
@@ -372,7 +382,7 @@ def run_ep(args, rank, world, dev):
     alg_bytes = sum(distinct) * expert_bytes + act_bytes
 
     if decode:
-        caps = [[CapturedLayer(m, x) for x in xs] for m in moes]
+        caps = [[CapturedLayer(m[b] if isinstance(m, list) else m, x) for b, x in enumerate(xs)] for m in moes]
 
         def call(li, b, x=None):
             return caps[li][b](x)
@@ -415,10 +425,17 @@ def run_ep(args, rank, world, dev):
     if decode:
         del caps           # graphs holding NCCL work go before the process group
         torch.cuda.synchronize()
+    if bufs is not None:
+        bufs.check()
+        del moes
+        bufs.close()
     h2d = sum(x.numel() * 2 for x in xs)
     return dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=alg_bytes, per_b={}, clocks=clocks,
                 h2d=h2d, d2h=h2d, cfg=cfg, batches=batches, distinct=distinct, hbm=hbm, peak_src=peak_src,
-                launches=len(xs) * (7 if decode else 9), flops=0, ep=True, decode=decode)
+                launches=len(xs) * ((11 if peer else 7) if decode else 9), flops=0, ep=True, decode=decode,
+                launch=("CUDA graph per (layer, batch): peer-memory exchange (CUDA IPC, flags), partial experts"
+                        if peer else "CUDA graph per (layer, batch): NCCL all-gather, partial experts, "
+                        "reduce-scatter") if decode else "eager (NCCL all-to-all)")
 
 
 # --------------------------------------------------------------------------
@@ -590,8 +607,7 @@ def main():
                 "config": {"workload": args.workload, "batches": list(r["batches"]), "tokens_per_rank": r["tokens"],
                            "layers_cycled": args.layers, "parallelism": f"ep{world}",
                            "experts_per_rank": r["cfg"]["E"] // world,
-                           "launch": ("CUDA graph per (layer, batch): NCCL all-gather, partial experts, "
-                                      "reduce-scatter") if r.get("decode") else "eager (NCCL all-to-all)"},
+                           "launch": r.get("launch", "eager (NCCL all-to-all)")},
                 "e2e": {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2), "unit": unit,
                         "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
                 "roofline": ({"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",

@@ -100,6 +100,42 @@ WM_API int wmxfp4_dequantize(const uint8_t *packed, const uint8_t *scales, int64
 WM_API int wmx_split_e4m3(const wm_bf16 *x, int rows, int cols, uint8_t *hi, uint8_t *lo, uint8_t *scales,
                    wm_stream_t stream);
 
+/* ------------------------------------ expert-parallel peer exchange ------ */
+
+/* No reference counterpart (the reference is single-device).  The decode form
+ * of the expert-parallel layer exchanges a few rows per rank per call over
+ * NVLink without a collective library: buffers are shared with CUDA IPC,
+ * rows are written straight into every rank's buffer and a per-rank flag is
+ * raised there afterwards.  Epoch counters live in device memory (the calls
+ * replay from CUDA graphs); all ranks make the same sequence of calls. */
+
+/* cudaMalloc'd, zeroed buffer and its 64-byte IPC handle. */
+WM_API int wep_ipc_alloc(size_t bytes, void **ptr, unsigned char *handle);
+/* Map a peer's buffer from its handle / unmap / free. */
+WM_API int wep_ipc_open(const unsigned char *handle, void **ptr);
+WM_API int wep_ipc_close(void *ptr);
+WM_API int wep_ipc_free(void *ptr);
+
+/* For each of n_regions (<= 4) regions: rows x row_bytes from srcs[r]
+ * (+ q * src_peer_stride[r] for peer q; src_peer_stride NULL: 0) to byte
+ * dst_offsets[r] + rank * rows * row_bytes[r] of peer_dst[q], for every peer
+ * q < world (<= 8, this rank included; row bytes, offsets and sources
+ * 4-byte aligned, copied 16 bytes at a time where everything is 16-aligned);
+ * then *epoch += 1 and
+ * peer_flags[q][rank] = *epoch on every peer (release, system scope).
+ * counter: a device int32 that starts at 0 and is left at 0. */
+WM_API int wep_put_rows(int n_regions, const void *const *srcs, const size_t *row_bytes,
+                 const size_t *src_peer_stride, const size_t *dst_offsets, int rows, void *const *peer_dst,
+                 int rank, int world, uint32_t *const *peer_flags, uint32_t *epoch, int32_t *counter,
+                 wm_stream_t stream);
+/* Block the stream until flags[q] >= *epoch for all q < world (acquire,
+ * system scope); after 2 s, *err = 1 and the wait ends. */
+WM_API int wep_wait(const uint32_t *flags, int world, const uint32_t *epoch, int32_t *err, wm_stream_t stream);
+/* out [rows, H] bf16 = sum over q < world of part[q] [rows, H] f32, in q
+ * order; zeros when err != NULL and *err != 0. */
+WM_API int wep_sum_rows(const float *part, int world, int rows, int H, const int32_t *err, wm_bf16 *out,
+                 wm_stream_t stream);
+
 /* ------------------------------------------------------ affine 4-bit ------ */
 
 /* MLX-style affine 4-bit quantize, group `group` (64 or 32) along cols:

@@ -6,9 +6,10 @@
   the full layer (``wmoe_mxfp4_moe_forward``) and the oracle, on the
   tensor-core and the CUDA-core expert paths; edge cases: a rank that owns no
   assigned expert, an id outside the layer (error path: zeros).
-* Two GPUs over NCCL: the all-to-all layer (each rank routes its own tokens,
-  exchanges rows, combines) and the gathered decode layer (all-gather,
-  partial sums, reduce-scatter), eager and replayed from a CUDA graph; each
+* Two GPUs: the all-to-all layer over NCCL (each rank routes its own tokens,
+  exchanges rows, combines), the gathered decode layer over NCCL (all-gather,
+  partial sums, reduce-scatter) and over peer memory (CUDA IPC rows + flags),
+  eager and replayed from a CUDA graph; each
   must match the full layer on one GPU with the same weights and tokens
   (2e-2 max-relative, bf16 output).  Skipped when fewer than two GPUs are
   visible.
@@ -126,6 +127,18 @@ def _worker(rank, world, port, q):
         errs.append(M.max_rel_err(y.float().cpu().numpy(), full_b.float().cpu().numpy()))
         del cap
         torch.cuda.synchronize()
+        # the same layer with both exchanges over peer memory (CUDA IPC + flags), eager and from a graph
+        bufs = EP.PeerBuffers(16, 1024, 8, device=dev)
+        pmoe = EP.PeerGatheredMoE(lay.layer.gate, local, 8, 9, bufs, 10.0, True)
+        errs.append(M.max_rel_err(pmoe(xb).float().cpu().numpy(), full_b.float().cpu().numpy()))
+        cap = CapturedLayer(pmoe, xb)
+        for _ in range(3):
+            y = cap(xb)
+        torch.cuda.synchronize()
+        errs.append(M.max_rel_err(y.float().cpu().numpy(), full_b.float().cpu().numpy()))
+        bufs.check()
+        del cap
+        bufs.close()
         q.put((rank, errs))
     finally:
         dist.destroy_process_group()
@@ -143,4 +156,4 @@ def test_ep_two_gpus_matches_single_gpu_layer():
     for p in procs:
         p.join(timeout=120)
     for rank, errs in res:
-        assert len(errs) == 3 and max(errs) < 2e-2, (rank, errs)
+        assert len(errs) == 5 and max(errs) < 2e-2, (rank, errs)

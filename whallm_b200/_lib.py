@@ -39,6 +39,13 @@ SIGNATURES = {
     "wmxfp4_quantize": [_P, _I64, _I64, _P, _P, _P],
     "wmxfp4_dequantize": [_P, _P, _I64, _I64, _I, _P, _P],
     "wmx_split_e4m3": [_P, _I, _I, _P, _P, _P, _P],
+    "wep_ipc_alloc": [_SZ, _P, _P],
+    "wep_ipc_open": [_P, _P],
+    "wep_ipc_close": [_P],
+    "wep_ipc_free": [_P],
+    "wep_put_rows": [_I, _P, _P, _P, _P, _I, _P, _I, _I, _P, _P, _P, _P],
+    "wep_wait": [_P, _I, _P, _P, _P],
+    "wep_sum_rows": [_P, _I, _I, _I, _P, _P, _P],
     "waffine4_quantize": [_P, _I64, _I64, _I, _P, _P, _P, _P],
     "waffine4_dequantize": [_P, _P, _P, _I64, _I64, _I, _I, _P, _P],
     "wkv_quantize": [_P, _I64, _I, _I, _P, _P, _P],

@@ -165,6 +165,177 @@ class GatheredExpertParallelMoE:
         return _reduce_scatter(part, self.world, self.rank, self.group).to(torch.bfloat16)
 
 
+class _DeviceArray:
+    """A raw device pointer as a CUDA array-interface object (viewed by torch.as_tensor)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+def _view(ptr: int, shape, dtype):
+    typestr = {torch.int16: "<i2", torch.int32: "<i4", torch.float32: "<f4", torch.uint8: "|u1"}
+    if dtype == torch.bfloat16:
+        return torch.as_tensor(_DeviceArray(ptr, shape, "<i2"), device="cuda").view(torch.bfloat16)
+    return torch.as_tensor(_DeviceArray(ptr, shape, typestr[dtype]), device="cuda")
+
+
+def _align(n: int, a: int = 256) -> int:
+    return (n + a - 1) // a * a
+
+
+class PeerBuffers:
+    """One CUDA-IPC buffer per rank for the peer exchanges of the gathered
+    decode layer, mapped by every rank: the gathered tokens and routes of all
+    ranks (W * B_max rows), the returned partial sums ([W][B_max] rows), two
+    flag arrays with their epochs and arrival counters, and an error word.
+    The exchanges are lock-step, so every layer and batch size of a process
+    group can share one set (calls are stream-ordered on every rank)."""
+
+    def __init__(self, B_max: int, H: int, k: int, group=None, device=None):
+        import ctypes
+        from . import _lib as L
+        self.L = L
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > 8:
+            raise ValueError("peer exchange supports up to 8 ranks")
+        self.B_max, self.H, self.k = B_max, H, k
+        self.device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        W, R = self.world, self.world * B_max
+        off = 0
+        layout = {}
+        for name, nbytes in (("x", R * H * 2), ("idx", R * k * 4), ("w", R * k * 4), ("sw", R * 4),
+                             ("ret", R * H * 4), ("flags", 2 * 64 * 4), ("ctrl", 256)):
+            layout[name] = off
+            off = _align(off + nbytes)
+        self.layout, self.nbytes = layout, off
+        base = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        L.call("wep_ipc_alloc", off, ctypes.byref(base), handle)
+        self.base = base.value
+        handles = [None] * W
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peers = []
+        for q in range(W):
+            if q == self.rank:
+                self.peers.append(self.base)
+            else:
+                p = ctypes.c_void_p()
+                L.call("wep_ipc_open", (ctypes.c_ubyte * 64).from_buffer_copy(handles[q]), ctypes.byref(p))
+                self.peers.append(p.value)
+        ctrl = self.base + layout["ctrl"]
+        self.epoch = [ctrl, ctrl + 4]                  # uint32 epochs of the two exchanges
+        self.counter = [ctrl + 8, ctrl + 12]           # CTA-arrival counters
+        self.err_ptr = ctrl + 16
+        self.err = _view(self.err_ptr, (1,), torch.int32)
+        self.flags_local = [self.base + layout["flags"], self.base + layout["flags"] + 256]
+        self.flags_peer = [[p + layout["flags"] + 256 * c for p in self.peers] for c in range(2)]
+        dist.barrier(group=group)                      # every peer mapped before any write
+
+    def views(self, B: int):
+        """Gathered tokens / ids / weights / shared weights ([W*B] rows) and returned partials ([W, B, H])."""
+        if B > self.B_max:
+            raise ValueError(f"batch {B} exceeds the buffers' {self.B_max}")
+        b, lay, R, H, k = self.base, self.layout, self.world * B, self.H, self.k
+        return (_view(b + lay["x"], (R, H), torch.bfloat16), _view(b + lay["idx"], (R, k), torch.int32),
+                _view(b + lay["w"], (R, k), torch.float32), _view(b + lay["sw"], (R,), torch.float32),
+                _view(b + lay["ret"], (self.world, B, H), torch.float32))
+
+    def put(self, ch: int, regions, rows: int, stream):
+        """wep_put_rows of (src ptr, row bytes, per-peer src stride, dst offset) regions, then wep_wait."""
+        import ctypes
+        L = self.L
+        n = len(regions)
+        arr = lambda ty, vals: ctypes.cast((ty * len(vals))(*vals), ctypes.c_void_p)
+        L.call("wep_put_rows", n, arr(ctypes.c_void_p, [r[0] for r in regions]),
+               arr(ctypes.c_size_t, [r[1] for r in regions]), arr(ctypes.c_size_t, [r[2] for r in regions]),
+               arr(ctypes.c_size_t, [r[3] for r in regions]), rows, arr(ctypes.c_void_p, self.peers), self.rank,
+               self.world, arr(ctypes.c_void_p, self.flags_peer[ch]), ctypes.c_void_p(self.epoch[ch]),
+               ctypes.c_void_p(self.counter[ch]), stream)
+        L.call("wep_wait", ctypes.c_void_p(self.flags_local[ch]), self.world, ctypes.c_void_p(self.epoch[ch]),
+               ctypes.c_void_p(self.err_ptr), stream)
+
+    def check(self):
+        """Raise if an exchange wait timed out (a rank stopped participating)."""
+        if int(self.err.item()) != 0:
+            raise RuntimeError("expert-parallel peer exchange timed out waiting for a rank")
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's, once every rank is done with them."""
+        if getattr(self, "base", None) is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for q, p in enumerate(self.peers):
+            if q != self.rank:
+                self.L.call("wep_ipc_close", ctypes_ptr(p))
+        dist.barrier(group=self.group)
+        self.L.call("wep_ipc_free", ctypes_ptr(self.base))
+        self.base = None
+
+
+class PeerGatheredMoE:
+    """The gathered decode layer with both exchanges over peer memory
+    (``wep_put_rows`` / ``wep_wait`` / ``wep_sum_rows``) instead of
+    collectives.  A call: route own B tokens -> write tokens + routes into
+    every rank's buffer -> wait for all ranks' flags -> this rank's expert
+    share over all W*B tokens (float32 partials) -> write each rank's block of
+    partials into its buffer -> wait -> out = bf16(sum of the W partials in
+    rank order).  ``router(x) -> (weights f32 [B, k], idx int32 [B, k][,
+    shared_w f32 [B]])``; ``experts``: this rank's slice from
+    ``shard_experts``; ``bufs``: a ``PeerBuffers`` of the group.  Every rank
+    calls with the same B in the same order."""
+
+    def __init__(self, router, experts, n_routed: int, B: int, bufs: PeerBuffers, swiglu_limit: float = 0.0,
+                 has_shared: bool = True, shared_gated: bool = False):
+        self.router = router
+        self.experts = experts
+        self.n_routed = n_routed
+        self.B = B
+        self.bufs = bufs
+        self.limit = float(swiglu_limit)
+        self.has_shared = has_shared
+        self.shared_gated = shared_gated
+        self.e0, self.per = shard_bounds(n_routed, bufs.world, bufs.rank)
+        self.rx_x, self.rx_idx, self.rx_w, self.rx_sw, self.ret = bufs.views(B)
+        self.part = torch.empty((bufs.world * B, bufs.H), dtype=torch.float32, device=bufs.device)
+        self.out = torch.empty((B, bufs.H), dtype=torch.bfloat16, device=bufs.device)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        from . import experts as X
+        bufs, L = self.bufs, self.bufs.L
+        B, H, k = self.B, bufs.H, bufs.k
+        if tuple(x.shape) != (B, H):
+            raise ValueError(f"peer layer expects [{B}, {H}] tokens")
+        r = self.router(x)
+        w = r[0].reshape(B, k).float().contiguous()
+        idx = r[1].reshape(B, k).to(torch.int32).contiguous()
+        sw = r[2].reshape(B).float().contiguous() if (self.shared_gated and len(r) > 2) else None
+        lay = bufs.layout
+        xc = x.contiguous()
+        regions = [(xc.data_ptr(), 2 * H, 0, lay["x"]), (idx.data_ptr(), 4 * k, 0, lay["idx"]),
+                   (w.data_ptr(), 4 * k, 0, lay["w"])]
+        if sw is not None:
+            regions.append((sw.data_ptr(), 4, 0, lay["sw"]))
+        stream = L.stream_of(self.out)
+        bufs.put(0, regions, B, stream)
+        X.experts_forward(self.rx_x, self.rx_idx, self.experts, weights=self.rx_w,
+                          shared_expert=self.per if self.has_shared else -1,
+                          shared_w=self.rx_sw if sw is not None else None, swiglu_limit=self.limit,
+                          expert_range=(self.e0, self.per, self.n_routed),
+                          shared_rows=(bufs.rank * B, (bufs.rank + 1) * B), out=self.part)
+        bufs.put(1, [(self.part.data_ptr(), 4 * H, B * 4 * H, lay["ret"])], B, stream)
+        L.call("wep_sum_rows", L.ptr(self.ret), bufs.world, B, H, ctypes_ptr(bufs.err_ptr), L.ptr(self.out), stream)
+        return self.out
+
+
+def ctypes_ptr(v: int):
+    import ctypes
+    return ctypes.c_void_p(v)
+
+
 def gpu_partial_experts(experts, e0: int, per: int, n_routed: int, swiglu_limit: float = 0.0,
                         has_shared: bool = True):
     """This rank's share on the device: ``experts`` from ``shard_experts``
