@@ -157,3 +157,75 @@ def test_ep_two_gpus_matches_single_gpu_layer():
         p.join(timeout=120)
     for rank, errs in res:
         assert len(errs) == 5 and max(errs) < 2e-2, (rank, errs)
+
+
+def _ptr(t):
+    import ctypes
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def test_peer_put_wait_sum_single_rank(dev):
+    """World size 1: rows land at the rank's offset, the flag is raised to the
+    epoch, the wait passes and the rank-ordered sum is the rows themselves."""
+    import ctypes
+    import sys
+    sys.path.insert(0, ROOT)
+    from whallm_b200 import _lib as L
+    base = ctypes.c_void_p()
+    handle = (ctypes.c_ubyte * 64)()
+    L.call("wep_ipc_alloc", 1 << 20, ctypes.byref(base), handle)
+    try:
+        buf = torch.as_tensor(_Arr(base.value, (1 << 18,), "<f4"), device=dev)      # zeroed by wep_ipc_alloc
+        rows = torch.randn((5, 64), device=dev)
+        ids = torch.arange(15, dtype=torch.int32, device=dev).view(5, 3)           # 12-byte rows: 4-byte copies
+        flags = base.value + 4096 * 4
+        ctrl = base.value + 8192 * 4
+        arr = lambda ty, vals: ctypes.cast((ty * len(vals))(*vals), ctypes.c_void_p)
+        st = L.stream_of(rows)
+        L.call("wep_put_rows", 2, arr(ctypes.c_void_p, [rows.data_ptr(), ids.data_ptr()]),
+               arr(ctypes.c_size_t, [256, 12]), None, arr(ctypes.c_size_t, [0, 2048 * 4]), 5,
+               arr(ctypes.c_void_p, [base.value]), 0, 1, arr(ctypes.c_void_p, [flags]), ctypes.c_void_p(ctrl),
+               ctypes.c_void_p(ctrl + 4), st)
+        L.call("wep_wait", ctypes.c_void_p(flags), 1, ctypes.c_void_p(ctrl), ctypes.c_void_p(ctrl + 8), st)
+        out = torch.empty((5, 64), dtype=torch.bfloat16, device=dev)
+        L.call("wep_sum_rows", ctypes.c_void_p(base.value), 1, 5, 64, ctypes.c_void_p(ctrl + 8), _ptr(out), st)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(buf[:320].view(5, 64), rows, rtol=0, atol=0)
+        assert torch.equal(buf[2048:2063].view(torch.int32).view(5, 3), ids)
+        ctl = buf[8192:8195].view(torch.int32).cpu().tolist()
+        assert ctl == [1, 0, 0]                                                    # epoch 1, counter 0, no error
+        assert int(buf[4096].view(torch.int32).item()) == 1                        # flag raised to the epoch
+        torch.testing.assert_close(out, rows.to(torch.bfloat16), rtol=0, atol=0)
+    finally:
+        L.call("wep_ipc_free", base)
+
+
+def test_peer_wait_times_out_and_reports(dev):
+    """A wait on flags that nothing raises gives up after its bound (2 s), sets
+    the error word and returns; the sum then writes zeros.  No fault, no hang."""
+    import ctypes
+    import sys
+    import time
+    sys.path.insert(0, ROOT)
+    from whallm_b200 import _lib as L
+    flags = torch.zeros(8, dtype=torch.int32, device=dev)
+    epoch = torch.ones(1, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    part = torch.ones((2, 3, 16), dtype=torch.float32, device=dev)
+    out = torch.full((3, 16), 7.0, dtype=torch.bfloat16, device=dev)
+    st = L.stream_of(flags)
+    torch.cuda.synchronize()
+    t0 = time.time()
+    L.call("wep_wait", _ptr(flags), 2, _ptr(epoch), _ptr(err), st)
+    L.call("wep_sum_rows", _ptr(part), 2, 3, 16, _ptr(err), _ptr(out), st)
+    torch.cuda.synchronize()
+    dt = time.time() - t0
+    assert int(err.item()) == 1
+    assert 1.5 < dt < 30, dt
+    assert torch.count_nonzero(out) == 0
+
+
+class _Arr:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None}
