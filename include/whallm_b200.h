@@ -100,6 +100,19 @@ WM_API int wmxfp4_dequantize(const uint8_t *packed, const uint8_t *scales, int64
 WM_API int wmx_split_e4m3(const wm_bf16 *x, int rows, int cols, uint8_t *hi, uint8_t *lo, uint8_t *scales,
                    wm_stream_t stream);
 
+/* Scores of queries against a quantized KV cache on block-scaled tensor cores:
+ * scores[b, q, l] = bf16(query[b, q, :] . dequant(K)[b, l, :]) for a cache
+ * stored as fmt = WKV_MXFP8_B32 (payload [B*L, D] e4m3, scales [B*L, D/32]
+ * E8M0) or WKV_MXFP4_B32 (payload [B*L, D/2] e2m1, same scales).  query bf16
+ * [B, Lq, D], scores bf16 [B, Lq, L]; D % 256 == 0.  Replaces
+ * MXFP8PoolingCache.quantized_matmul / index_matmul over the completed chunks
+ * (runtime/deepseek_v4_ssd/fp8_cache.py:119-159: mx.quantized_matmul,
+ * transpose=True, group 32, mode mxfp8 / mxfp4).  Workspace:
+ * wkv_scores_workspace_size(B, Lq, D). */
+WM_API size_t wkv_scores_workspace_size(int B, int Lq, int D);
+WM_API int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const uint8_t *payload, const uint8_t *scales,
+                  int L, int fmt, wm_bf16 *scores, void *workspace, size_t ws_bytes, wm_stream_t stream);
+
 /* ------------------------------------ expert-parallel peer exchange ------ */
 
 /* No reference counterpart (the reference is single-device).  The decode form

@@ -465,3 +465,15 @@ def join_e4m3(hi, lo, scales):
     v = e4m3_to_f32(hi).astype(np.float64) + e4m3_to_f32(lo).astype(np.float64) * 2.0 ** -LO_SHIFT
     return (v * np.exp2((s - 127).astype(np.float64))).astype(np.float32)
 
+
+def kv_scores(query_f32, payload, scales, fmt: int, D: int) -> np.ndarray:
+    """MXFP8PoolingCache.quantized_matmul / index_matmul over completed chunks
+    (fp8_cache.py:119-159): query [B, Lq, D] @ dequant(K)^T for K [B, L, D]
+    stored as MXFP8 / MXFP4 rows, accumulated in float64, rounded to bf16 (the
+    query dtype mx.quantized_matmul returns)."""
+    q = np.asarray(query_f32, np.float64)
+    B, L = payload.shape[0], payload.shape[1]
+    k = kv_dequantize(np.asarray(payload).reshape(B * L, -1), np.asarray(scales).reshape(B * L, -1), fmt, D)
+    k = k.reshape(B, L, D).astype(np.float64)
+    return round_bf16(np.einsum("bqd,bld->bql", q, k).astype(np.float32))
+

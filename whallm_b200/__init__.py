@@ -12,7 +12,7 @@ from .experts import (Affine4BatchedExperts, BatchedExperts, ClampedSwiGLU, Expe
                       QwenBatchedExperts, QwenExpertWeights, ResidentExpertStore, StreamingExperts,
                       StreamingSwitchGLU, experts_forward, permute)
 from .formats import (affine4_dequantize, affine4_quantize, kv_dequantize, kv_gather_dequantize,  # noqa: F401
-                      kv_quantize, mxfp4_dequantize, mxfp4_quantize, split_e4m3)
+                      kv_quantize, kv_scores, mxfp4_dequantize, mxfp4_quantize, split_e4m3)
 from .moe import MoE, SparseMoE, TinyMoE, route_reduce, streaming_moe  # noqa: F401
 from .router import Gate, qwen_route, route, stable_topk_indices, topk_scores  # noqa: F401
 

@@ -39,6 +39,8 @@ SIGNATURES = {
     "wmxfp4_quantize": [_P, _I64, _I64, _P, _P, _P],
     "wmxfp4_dequantize": [_P, _P, _I64, _I64, _I, _P, _P],
     "wmx_split_e4m3": [_P, _I, _I, _P, _P, _P, _P],
+    "wkv_scores_workspace_size": [_I, _I, _I],
+    "wkv_mx_scores": [_P, _I, _I, _I, _P, _P, _I, _I, _P, _P, _SZ, _P],
     "wep_ipc_alloc": [_SZ, _P, _P],
     "wep_ipc_open": [_P, _P],
     "wep_ipc_close": [_P],
@@ -64,7 +66,8 @@ SIGNATURES = {
     "wmoe_affine4_moe_forward": [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _F, _I, _P, _P, _P,
                                  _SZ, _P],
 }
-_RESTYPE = {"w_last_error": ctypes.c_char_p, "wmoe_workspace_size": ctypes.c_size_t}
+_RESTYPE = {"w_last_error": ctypes.c_char_p, "wmoe_workspace_size": ctypes.c_size_t,
+            "wkv_scores_workspace_size": ctypes.c_size_t}
 
 _lib = None
 _lock = threading.Lock()

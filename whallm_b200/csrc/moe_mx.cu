@@ -101,6 +101,7 @@ struct MxParams {
   int order;                 // WM_UP_GATE / WM_GATE_UP
   float limit;
   int m_tiles;               // 128-row work items per tile
+  int a_fp8;                 // A operand e4m3 (MXFP8: one byte per value) instead of e2m1
   const uint8_t *a_scales;   // [E * rows, K/32] E8M0 (the MXFP4 scales)
   const uint8_t *b_scales;   // [S_pad, K/32] hi-term E8M0 in slot order
   const int4 *tiles;         // {expert, first slot, tokens, 0}
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
         if (!(ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 1))) break;
         if (elect_one()) {
           // transaction bytes count the packed global bytes of the weights
-          mbar_expect_tx(&full[s], HV * (kM * kKH / 2) + 2 * HV * nb * 16 * kKH);
+          mbar_expect_tx(&full[s], HV * (p.a_fp8 ? kM * kKH : kM * kKH / 2) + 2 * HV * nb * 16 * kKH);
           for (int q = 0; q < HV; ++q) {
             const int x = kc * C::kKC + q * kKH;
             uint8_t *a = sA + s * C::kAStage + q * C::kABox;
@@ -272,6 +273,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     // --------------------------------------------------------------- MMA
     const uint32_t sfa = tmem + C::kSfCol0;
     const uint32_t sfb = sfa + HV * 4;
+    const uint32_t a_fmt_mask = p.a_fp8 ? ~(7u << 7) : ~0u;   // A format field: e2m1 (5) or e4m3 (0)
     uint32_t g = 0, it = 0;
     bool ok = true;
     for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance(), ++it) {
@@ -301,7 +303,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
             const int q = kb >> 2;
             const uint32_t j = kb & 3;
             tc_mma_mx(d_addr, bdesc_sw128(a0 + q * C::kABox) + 2 * j, bdesc_sw128(b0 + q * C::kBBox) + 2 * j,
-                      idesc_mx(n_mma, j), (j << 30) | (sfa + 4 * q), (j << 30) | (sfb + C::kSfbCols * q),
+                      idesc_mx(n_mma, j) & a_fmt_mask, (j << 30) | (sfa + 4 * q), (j << 30) | (sfb + C::kSfbCols * q),
                       (kc == 0 && kb == 0) ? 0u : 1u);
           }
           tc_commit(&empty[s]);
@@ -362,7 +364,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       const int4 tile = cur.cur;
       const int m = cur.m();
       const int grow = p.mode == 0 ? ((t >> 3) & 1) * p.I + m * 64 + (t >> 4) * 8 + (t & 7) : m * kM + t;
-      load_words(p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_ch * 4 * CW, e.a);
+      if (grow < p.rows)                                // a last partial 128-row tile (score rows): zero scales
+        load_words(p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_ch * 4 * CW, e.a);
       const int n16 = max(16, (tile.z + 15) & ~15);
 #pragma unroll
       for (int a = 0; a < BA; ++a) {
@@ -508,7 +511,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
           const int row = m * kM + t;
 #pragma unroll
           for (int q = 0; q < 16; ++q)
-            if (c0 + q < n)
+            if (c0 + q < n && row < p.rows)
               p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = wm_f32_to_bf16(__uint_as_float(r[q]));
         }
       }
@@ -598,9 +601,9 @@ template <class C>
 int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K, const uint8_t *b_hi,
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-                  uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
+                  uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool a_fp8 = false) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
-  if (!wm::aligned(w, 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed weights must be 32-byte aligned");
+  if (!wm::aligned(w, a_fp8 ? 16 : 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed A operand misaligned");
   if (!wm::aligned(a_scales, 16) || !wm::aligned(b_sc, 16))
     return wm::fail(WM_ERR_INVALID, "expert mx: scales must be 16-byte aligned");
   CUtensorMap tmA, tmBh, tmBl;
@@ -613,6 +616,13 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
     const cuuint32_t box[4] = {kKH, 8, 2, 8};
     if (int rc = make_map_nd(&tmA, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, 4, w, dims, strides, box,
                              CU_TENSOR_MAP_SWIZZLE_128B))
+      return rc;
+  } else if (a_fp8) {
+    // e4m3 rows, one byte per value: plain byte boxes of 128 rows x 128 values
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(E) * rows};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K)};
+    const cuuint32_t box[2] = {kKH, kM};
+    if (int rc = make_map_nd(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B))
       return rc;
   } else {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(E) * rows};
@@ -654,7 +664,8 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.H = H;
   p.order = order;
   p.limit = limit;
-  p.m_tiles = mode == 0 ? I / 64 : rows / kM;
+  p.m_tiles = mode == 0 ? I / 64 : (rows + kM - 1) / kM;
+  p.a_fp8 = a_fp8 ? 1 : 0;
   p.a_scales = a_scales;
   p.b_scales = b_sc;
   p.tiles = tiles;
@@ -726,6 +737,93 @@ int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
 }
 
 }  // namespace wm
+
+namespace {
+
+// tiles {batch, first query row, queries, 0}: ceil(Lq / nmax) per batch
+__global__ void k_score_tiles(int B, int Lq, int nmax, int4 *tiles, int32_t *n_tiles) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
+  const int per = (Lq + nmax - 1) / nmax;
+  for (int i = threadIdx.x + blockIdx.x * blockDim.x; i < B * per; i += blockDim.x * gridDim.x) {
+    const int b = i / per, j = i % per;
+    tiles[i] = make_int4(b, b * Lq + j * nmax, min(nmax, Lq - j * nmax), 0);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    n_tiles[0] = B * per;
+    n_tiles[1] = 0;                                       // the tensor-core kernel's error code
+  }
+}
+
+struct ScoreWorkspace {
+  uint8_t *q_hi, *q_lo, *q_sc;
+  int4 *tiles;
+  int32_t *counters;  // [0] n_tiles, [1] error code
+  size_t bytes;
+};
+
+ScoreWorkspace carve_scores(void *base, int B, int Lq, int D) {
+  ScoreWorkspace w{};
+  const size_t rows = static_cast<size_t>(std::max(B * Lq, 16));
+  size_t off = 0;
+  auto take = [&](size_t n) {
+    const size_t o = off;
+    off = wm::align_up(off + n, 256);
+    return o;
+  };
+  const size_t o_hi = take(rows * D), o_lo = take(rows * D), o_sc = take(rows * (D / 32));
+  const size_t o_t = take((static_cast<size_t>(B) * (Lq + 15) / 16 + 2) * sizeof(int4)), o_c = take(16);
+  w.bytes = off;
+  if (base) {
+    char *b = static_cast<char *>(base);
+    w.q_hi = reinterpret_cast<uint8_t *>(b + o_hi);
+    w.q_lo = reinterpret_cast<uint8_t *>(b + o_lo);
+    w.q_sc = reinterpret_cast<uint8_t *>(b + o_sc);
+    w.tiles = reinterpret_cast<int4 *>(b + o_t);
+    w.counters = reinterpret_cast<int32_t *>(b + o_c);
+  }
+  return w;
+}
+
+}  // namespace
+
+extern "C" size_t wkv_scores_workspace_size(int B, int Lq, int D) {
+  if (B < 1 || Lq < 1 || D < 32) return 0;
+  return carve_scores(nullptr, B, Lq, D).bytes;
+}
+
+extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const uint8_t *payload,
+                             const uint8_t *scales, int L, int fmt, wm_bf16 *scores, void *workspace,
+                             size_t ws_bytes, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(B >= 1 && Lq >= 1 && L >= 1, "kv scores: need B, Lq, L >= 1");
+  WM_REQUIRE(fmt == WKV_MXFP8_B32 || fmt == WKV_MXFP4_B32, "kv scores: fmt must be WKV_MXFP8_B32 or WKV_MXFP4_B32");
+  WM_REQUIRE(D % 256 == 0, "kv scores: the tensor-core path needs D % 256 == 0");
+  WM_REQUIRE(query && payload && scales && scores && workspace, "kv scores: null buffer");
+  WM_REQUIRE(wm::aligned(query, 16) && wm::aligned(scores, 16) && wm::aligned(workspace, 256),
+             "kv scores: query/scores 16-byte, workspace 256-byte aligned");
+  ScoreWorkspace ws = carve_scores(workspace, B, Lq, D);
+  if (ws_bytes < ws.bytes) return wm::fail(WM_ERR_WORKSPACE, "kv scores: workspace too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nmax = Lq <= 32 ? MxDecode::kNMax : MxPrefill::kNMax;
+  const int per = (Lq + nmax - 1) / nmax;
+  if (cudaError_t e = wm::launch_pdl(k_score_tiles, dim3((B * per + 255) / 256), dim3(256), 0, st, B, Lq, nmax,
+                                     ws.tiles, ws.counters))
+    return wm::fail(WM_ERR_CUDA, std::string("kv scores tiles: ") + cudaGetErrorString(e));
+  if (int rc = wm::launch_split_e4m3(reinterpret_cast<const uint16_t *>(query), nullptr, nullptr, B * Lq, 1, D,
+                                     ws.q_hi, ws.q_lo, ws.q_sc, st))
+    return rc;
+  // scores[b, q, l] = D[l, q] of the "down projection" form: rows = L cache rows of batch b, output row stride L
+  const int s_rows = std::max(B * Lq, 16);
+  if (nmax == MxDecode::kNMax)
+    return launch_mx_cfg<MxDecode>(1, payload, scales, B, L, D, ws.q_hi, ws.q_lo, ws.q_sc, s_rows, 0, L, WM_UP_GATE,
+                                   0.0f, ws.tiles, ws.counters, nullptr, nullptr, nullptr, nullptr,
+                                   reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st,
+                                   fmt == WKV_MXFP8_B32);
+  return launch_mx_cfg<MxPrefill>(1, payload, scales, B, L, D, ws.q_hi, ws.q_lo, ws.q_sc, s_rows, 0, L, WM_UP_GATE,
+                                  0.0f, ws.tiles, ws.counters, nullptr, nullptr, nullptr, nullptr,
+                                  reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st, fmt == WKV_MXFP8_B32);
+}
 
 extern "C" int wmx_split_e4m3(const wm_bf16 *x, int rows, int cols, uint8_t *hi, uint8_t *lo, uint8_t *scales,
                               wm_stream_t stream) {

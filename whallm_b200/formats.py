@@ -62,6 +62,34 @@ def mxfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor, dtype=torch.bfl
     return out
 
 
+def kv_scores(query: torch.Tensor, payload: torch.Tensor, scales: torch.Tensor, fmt, out=None) -> torch.Tensor:
+    """MXFP8PoolingCache.quantized_matmul / index_matmul over completed chunks
+    (fp8_cache.py:119-159): bf16 [B, Lq, L] = query [B, Lq, D] @ dequant(K)^T,
+    K [B, L, D] stored as "mxfp8" (payload u8 [B, L, D]) or "mxfp4" (payload
+    u8 [B, L, D/2]) with E8M0 scales u8 [B, L, D/32]."""
+    f = _fmt(fmt)
+    if f not in (L.WKV_MXFP8_B32, L.WKV_MXFP4_B32):
+        raise ValueError("kv_scores takes an mxfp8 or mxfp4 cache")
+    if query.dtype != torch.bfloat16 or query.dim() != 3:
+        raise ValueError("query must be bf16 [B, Lq, D]")
+    B, Lq, D = query.shape
+    if scales.dim() != 3 or scales.shape[0] != B or scales.shape[2] != D // 32:
+        raise ValueError("scales must be [B, L, D/32]")
+    Lc = scales.shape[1]
+    want = D if f == L.WKV_MXFP8_B32 else D // 2
+    if tuple(payload.shape) != (B, Lc, want) or payload.dtype != torch.uint8:
+        raise ValueError(f"payload must be uint8 [B, L, {want}]")
+    q = query.contiguous()
+    if out is None:
+        out = torch.empty((B, Lq, Lc), dtype=torch.bfloat16, device=q.device)
+    nbytes = int(L.lib().wkv_scores_workspace_size(B, Lq, D))
+    ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
+    L.require_cuda(q, payload, scales, out)
+    L.call("wkv_mx_scores", L.ptr(q), B, Lq, D, L.ptr(payload.contiguous()), L.ptr(scales.contiguous()), Lc, f,
+           L.ptr(out), L.ptr(ws), ws.numel(), L.stream_of(q))
+    return out
+
+
 def split_e4m3(x: torch.Tensor):
     """bf16 [rows, cols] -> (hi u8, lo u8 [rows, cols], scales u8 [rows, cols/32]):
     the exact two-term e4m3 operand form of the block-scaled expert kernels."""
