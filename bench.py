@@ -274,6 +274,47 @@ def run_ours(args, rank, world, dev):
                         launches=len(xs) * (2 + 5) if name != "tiny" else len(xs) * (2 + 4),
                         graphed=graphed))
         return res
+    if wl == "kv_scores":
+        # decode scores of one query per sequence against an MXFP8 latent cache:
+        # 8 sequences x 32768 cached tokens x 512 dims per layer, 61 layers (each its own cache)
+        Bq, Lc, D, n_layer = 8, 32768, 512, 61
+        caches = []
+        for li in range(n_layer):
+            kvr = torch.randn(Bq * Lc, D, device=dev, generator=torch.Generator(device=dev).manual_seed(li))
+            pl, sc = W.kv_quantize(kvr.to(torch.bfloat16), "mxfp8")
+            caches.append((pl.view(Bq, Lc, D), sc.view(Bq, Lc, D // 32)))
+            del kvr
+        q = torch.randn(Bq, 1, D, device=dev).to(torch.bfloat16)
+        out = torch.empty(Bq, 1, Lc, dtype=torch.bfloat16, device=dev)
+        for i in range(args.warmup):
+            W.kv_scores(q, *caches[i % n_layer], "mxfp8", out=out)
+        torch.cuda.synchronize()
+        s, e = _events(torch)
+        s.record()
+        for _ in range(args.steps):
+            for li in range(n_layer):
+                W.kv_scores(q, *caches[li], "mxfp8", out=out)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / args.steps
+        per_layer = Bq * Lc * (D + D // 32) + Bq * D * 2 + Bq * Lc * 2
+        hq = q.cpu().pin_memory()
+        hout = torch.empty(out.shape, dtype=torch.bfloat16).pin_memory()
+        torch.cuda.synchronize()
+        s4, e4 = _events(torch)
+        s4.record()
+        for _ in range(args.steps):
+            for li in range(n_layer):
+                hout.copy_(W.kv_scores(hq.to(dev, non_blocking=True), *caches[li], "mxfp8", out=out),
+                           non_blocking=True)
+        e4.record()
+        torch.cuda.synchronize()
+        ms_e2e = s4.elapsed_time(e4) / args.steps
+        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=Bq * Lc * n_layer, alg_bytes=per_layer * n_layer,
+                        per_b={}, clocks=None, flops=0, h2d=Bq * D * 2 * n_layer, d2h=Bq * Lc * 2 * n_layer,
+                        cfg={"B": Bq, "L": Lc, "D": D, "layers": n_layer}, batches=(), distinct=[], hbm=hbm,
+                        peak_src=peak_src, launches=3 * n_layer))
+        return res
     if wl == "kv":
         D, rows_total = 576, 32768 * 8 * 61
         chunk = 32768 * 8          # one layer of the 8 x 32768-token context per call
@@ -533,7 +574,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="ds_decode",
-                    choices=["ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny", "kv"])
+                    choices=["ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny", "kv", "kv_scores"])
     ap.add_argument("--layers", type=int, default=8, help="resident layers cycled per step (no L2 reuse)")
     ap.add_argument("--experts", type=int, default=None,
                     help="routed experts per layer (default: the configuration's); smaller layers for ncu captures")
@@ -545,9 +586,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    unit = "tokens/s" if args.workload != "kv" else "KV rows/s"
-    metric = ("MoE layer tok/s, DeepSeek-class MXFP4 decode sweep B=1,4,16,64" if args.workload == "ds_decode"
-              else f"MoE layer tok/s ({args.workload})" if args.workload != "kv" else "FP8 KV quantize+dequantize rows/s")
+    unit = {"kv": "KV rows/s", "kv_scores": "cached rows scored/s"}.get(args.workload, "tokens/s")
+    metric = {"ds_decode": "MoE layer tok/s, DeepSeek-class MXFP4 decode sweep B=1,4,16,64",
+              "kv": "FP8 KV quantize+dequantize rows/s",
+              "kv_scores": "MXFP8 KV-cache score rows/s (decode, 8 seq x 32768 x 512, 61 layers)"}.get(
+                  args.workload, f"MoE layer tok/s ({args.workload})")
 
     if args.impl == "reference":
         if rank != 0:
