@@ -508,6 +508,17 @@ def cpu_reference(args, sample_steps=None):
             F.kv_dequantize(p, s, F.KV_FP8_F32_B64, D)
 
         tokens, sample = n, "kv: 32768 rows of 576 (one sequence, one layer), numpy oracle"
+    elif wl == "kv_scores":
+        D, n = 512, 32768
+        rng = np.random.default_rng(0)
+        x = F.round_bf16(rng.normal(0, 1, (n, D)).astype(np.float32))
+        p, s = F.kv_quantize(x, F.KV_MXFP8_B32)
+        q = F.round_bf16(rng.normal(0, 1, (1, 1, D)).astype(np.float32))
+
+        def step():
+            F.kv_scores(q, p.reshape(1, n, -1), s.reshape(1, n, -1), F.KV_MXFP8_B32, D)
+
+        tokens, sample = n, "kv_scores: one query against 32768 MXFP8 rows of 512 (one sequence, one layer), numpy oracle"
     else:
         name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn", "tiny": "tiny"}[wl]
         batches = {"ds_decode": SWEEP, "ds_prefill": (256,), "qn_decode": (1, 32), "qn_prefill": (1024,),
