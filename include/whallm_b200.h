@@ -113,6 +113,17 @@ WM_API size_t wkv_scores_workspace_size(int B, int Lq, int D);
 WM_API int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const uint8_t *payload, const uint8_t *scales,
                   int L, int fmt, wm_bf16 *scores, void *workspace, size_t ws_bytes, wm_stream_t stream);
 
+/* Dense block-scaled linear y [T, N] bf16 = x [T, K] bf16 @ dequant(w)^T for
+ * w stored as fmt = WKV_MXFP8_B32 (u8 e4m3 [N, K]) or WKV_MXFP4_B32 (u8 e2m1
+ * [N, K/2]) with E8M0 scales [N, K/32]; K % 256 == 0.  Replaces the MXFP8
+ * QuantizedLinear layers nn.quantize(mode="mxfp8") installs over native FP8
+ * weights (runtime/deepseek_v4_ssd/deepseek_v41_ssd.py:232-261, 353-360:
+ * mx.quantized_matmul, transpose=True, group 32).  Workspace:
+ * wmx_linear_workspace_size(T, K). */
+WM_API size_t wmx_linear_workspace_size(int T, int K);
+WM_API int wmx_linear(const wm_bf16 *x, int T, int K, const uint8_t *w, const uint8_t *scales, int N, int fmt,
+               wm_bf16 *y, void *workspace, size_t ws_bytes, wm_stream_t stream);
+
 /* ------------------------------------ expert-parallel peer exchange ------ */
 
 /* No reference counterpart (the reference is single-device).  The decode form

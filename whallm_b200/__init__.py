@@ -16,4 +16,6 @@ from .formats import (affine4_dequantize, affine4_quantize, kv_dequantize, kv_ga
 from .moe import MoE, SparseMoE, TinyMoE, route_reduce, streaming_moe  # noqa: F401
 from .router import Gate, qwen_route, route, stable_topk_indices, topk_scores  # noqa: F401
 
+from .linear import MXFP8Linear, expand_block_scales, mx_linear  # noqa: F401
+
 __version__ = "0.1.0"

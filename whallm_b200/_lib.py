@@ -40,6 +40,8 @@ SIGNATURES = {
     "wmxfp4_dequantize": [_P, _P, _I64, _I64, _I, _P, _P],
     "wmx_split_e4m3": [_P, _I, _I, _P, _P, _P, _P],
     "wkv_scores_workspace_size": [_I, _I, _I],
+    "wmx_linear_workspace_size": [_I, _I],
+    "wmx_linear": [_P, _I, _I, _P, _P, _I, _I, _P, _P, _SZ, _P],
     "wkv_mx_scores": [_P, _I, _I, _I, _P, _P, _I, _I, _P, _P, _SZ, _P],
     "wep_ipc_alloc": [_SZ, _P, _P],
     "wep_ipc_open": [_P, _P],
@@ -67,7 +69,7 @@ SIGNATURES = {
                                  _SZ, _P],
 }
 _RESTYPE = {"w_last_error": ctypes.c_char_p, "wmoe_workspace_size": ctypes.c_size_t,
-            "wkv_scores_workspace_size": ctypes.c_size_t}
+            "wkv_scores_workspace_size": ctypes.c_size_t, "wmx_linear_workspace_size": ctypes.c_size_t}
 
 _lib = None
 _lock = threading.Lock()

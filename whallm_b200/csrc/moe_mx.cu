@@ -825,6 +825,17 @@ extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const u
                                   reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st, fmt == WKV_MXFP8_B32);
 }
 
+extern "C" size_t wmx_linear_workspace_size(int T, int K) { return wkv_scores_workspace_size(1, T, K); }
+
+// A dense block-scaled linear is the score kernel with one "sequence" whose N
+// cached rows are the weight rows and whose T queries are the tokens.
+extern "C" int wmx_linear(const wm_bf16 *x, int T, int K, const uint8_t *w, const uint8_t *scales, int N, int fmt,
+                          wm_bf16 *y, void *workspace, size_t ws_bytes, wm_stream_t stream) {
+  wm::clear_error();
+  if (T == 0) return WM_OK;
+  return wkv_mx_scores(x, 1, T, K, w, scales, N, fmt, y, workspace, ws_bytes, stream);
+}
+
 extern "C" int wmx_split_e4m3(const wm_bf16 *x, int rows, int cols, uint8_t *hi, uint8_t *lo, uint8_t *scales,
                               wm_stream_t stream) {
   wm::clear_error();
