@@ -22,7 +22,9 @@ prefill runs eagerly.
 
 Other workloads: --workload ds_prefill (4096 tokens), qn_decode (B 1 and 32),
 qn_prefill (16384 tokens), tiny (64 tokens, affine-4), kv (FP8 KV quantize +
-dequantize of 32768 x 8 x 61 rows of 576).
+dequantize of 32768 x 8 x 61 rows of 576), kv_scores (MXFP8 cache scores),
+qsa (Qwen QSA affine KV caches: one decode update_and_fetch of 8 sequences at
+a 32768-token context over the 12 full-attention layers).
 
 `--impl reference` times the reference's algorithm on the host cores (the
 oracle port; the MLX CPU backend the reference would use is not installable
@@ -315,6 +317,94 @@ def run_ours(args, rank, world, dev):
                         cfg={"B": Bq, "L": Lc, "D": D, "layers": n_layer}, batches=(), distinct=[], hbm=hbm,
                         peak_src=peak_src, launches=3 * n_layer))
         return res
+    if wl == "qsa":
+        # Qwen QSA caches in decode: 12 full-attention layers, each an 8-bit K/V cache of
+        # 2 kv heads x 256 and a 4-bit indexer cache of 1 head x 128; 8 sequences at a
+        # 32768-token context; one step appends one token per sequence and fetches the
+        # whole dequantized history of every cache (update_and_fetch)
+        from whallm_b200.kvcache import QSAQuantizedCache
+        Bq, Lc, n_layer = 8, 32768, 12
+        shapes = ((8, 2, 256), (4, 1, 128))      # (bits, kv heads, head dim)
+        cap = Lc + args.warmup + 2 * args.steps     # warm-up, timed and end-to-end steps each append a row
+        caches = []
+        for li in range(n_layer):
+            pair = []
+            for bits, hk, hd in shapes:
+                c = QSAQuantizedCache(bits, hd, capacity=cap)
+                g = torch.Generator(device=dev).manual_seed(li * 2 + bits)
+                kx = torch.randn(Bq, hk, Lc - 1, hd, device=dev, generator=g).to(torch.bfloat16)
+                c.update_and_fetch(kx, kx)
+                pair.append(c)
+            caches.append(pair)
+            del kx
+        torch.cuda.empty_cache()
+        news = [torch.randn(Bq, hk, 1, hd, device=dev).to(torch.bfloat16) for _, hk, hd in shapes]
+
+        def step(news_):
+            outs = []
+            for pair in caches:
+                for c, x in zip(pair, news_):
+                    outs.append(c.update_and_fetch(x, x))
+            return outs
+
+        for _ in range(args.warmup):
+            step(news)
+        torch.cuda.synchronize()
+        clk = ClockSampler(dev.index if dev.index is not None else 0)
+        clk.start()
+        s, e = _events(torch)
+        s.record()
+        for _ in range(args.steps):
+            step(news)
+        e.record()
+        torch.cuda.synchronize()
+        clocks = clk.stop()
+        ms = s.elapsed_time(e) / args.steps
+        # the dominant kernel alone: the history fetch of every cache
+        s2, e2 = _events(torch)
+        s2.record()
+        for _ in range(args.steps):
+            for pair in caches:
+                for c in pair:
+                    c.fetch()
+        e2.record()
+        torch.cuda.synchronize()
+        ms_exp = s2.elapsed_time(e2) / args.steps
+        L_now = caches[0][0].offset
+        alg = 0
+        for bits, hk, hd in shapes:   # per layer: K and V, packed + bf16 scale/bias read, bf16 written
+            alg += 2 * Bq * hk * L_now * (hd * bits // 8 + 4 * (hd // 32) + 2 * hd)
+        alg *= n_layer
+        # end to end: the new rows come from pinned host memory, the newest dequantized
+        # row of every cache goes back
+        hnews = [x.cpu().pin_memory() for x in news]
+        hlast = [torch.empty((Bq, hk, hd), dtype=torch.bfloat16).pin_memory() for _, hk, hd in shapes]
+        torch.cuda.synchronize()
+        s4, e4 = _events(torch)
+        s4.record()
+        for _ in range(args.steps):
+            dn = [x.to(dev, non_blocking=True) for x in hnews]
+            outs = step(dn)
+            for i, (ko, _vo) in enumerate(outs):
+                hlast[i % 2].copy_(ko[:, :, -1], non_blocking=True)
+        e4.record()
+        torch.cuda.synchronize()
+        ms_e2e = s4.elapsed_time(e4) / args.steps
+        h2d = sum(x.numel() * 2 for x in hnews)
+        d2h = n_layer * sum(Bq * hk * hd * 2 for _, hk, hd in shapes)
+        res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=Bq * Lc * n_layer, alg_bytes=alg, per_b={},
+                        clocks=clocks, flops=0, h2d=h2d, d2h=d2h,
+                        cfg={"B": Bq, "L": Lc, "layers": n_layer, "caches": [list(x) for x in shapes]}, batches=(),
+                        distinct=[], hbm=hbm, peak_src=peak_src, launches=4 * n_layer,
+                        kernel="history fetch of every QSA cache (k_affine_kv_fetch, K and V in one launch)",
+                        dtype="u32 packed affine 8/4-bit, bf16 scales/biases, bf16 out",
+                        data="synthetic (seeded N(0,1) bf16 keys/values)",
+                        config={"sequences": Bq, "context": Lc, "full_attention_layers": n_layer,
+                                "caches": "K/V 8-bit 2 heads x 256, index 4-bit 1 head x 128, group 32",
+                                "step": "append one row per sequence + fetch the whole history, every cache",
+                                "l2": "4.1 GB of packed history read and 8.1 GB of bf16 written per step: larger than L2",
+                                "launch": "eager"}))
+        return res
     if wl == "kv":
         D, rows_total = 576, 32768 * 8 * 61
         chunk = 32768 * 8          # one layer of the 8 x 32768-token context per call
@@ -519,6 +609,23 @@ def cpu_reference(args, sample_steps=None):
             F.kv_scores(q, p.reshape(1, n, -1), s.reshape(1, n, -1), F.KV_MXFP8_B32, D)
 
         tokens, sample = n, "kv_scores: one query against 32768 MXFP8 rows of 512 (one sequence, one layer), numpy oracle"
+    elif wl == "qsa":
+        n = 32768
+        rng = np.random.default_rng(0)
+        caches = []
+        for bits, hk, hd in ((8, 2, 256), (4, 1, 128)):
+            c = F.QSACache(bits, hd)
+            x = F.f32_to_bf16_bits(rng.normal(0, 1, (hk, n - 1, hd)).astype(np.float32))
+            c.update_and_fetch(x, x)
+            caches.append((c, F.f32_to_bf16_bits(rng.normal(0, 1, (hk, 1, hd)).astype(np.float32))))
+
+        def step():
+            for c, x in caches:
+                c.update_and_fetch(x, x)
+
+        tokens = n
+        sample = ("qsa: one decode update_and_fetch of one sequence at a 32768-token context, one layer's two QSA "
+                  "caches (8-bit 2x256 K/V, 4-bit 1x128 index), numpy oracle")
     else:
         name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn", "tiny": "tiny"}[wl]
         batches = {"ds_decode": SWEEP, "ds_prefill": (256,), "qn_decode": (1, 32), "qn_prefill": (1024,),
@@ -575,7 +682,9 @@ def cpu_reference(args, sample_steps=None):
     for _ in range(steps):
         step()
     dt = (time.perf_counter() - t0) / steps
-    return dict(value=tokens / dt, sec_per_step=dt, tokens=tokens, cores=threads, sample=sample)
+    # the KV restatements are single-threaded numpy; the MoE arm runs the C kernels on every host thread
+    cores = 1 if wl in ("kv", "kv_scores", "qsa") else threads
+    return dict(value=tokens / dt, sec_per_step=dt, tokens=tokens, cores=cores, sample=sample)
 
 
 def main():
@@ -585,7 +694,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="ds_decode",
-                    choices=["ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny", "kv", "kv_scores"])
+                    choices=["ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny", "kv", "kv_scores", "qsa"])
     ap.add_argument("--layers", type=int, default=8, help="resident layers cycled per step (no L2 reuse)")
     ap.add_argument("--experts", type=int, default=None,
                     help="routed experts per layer (default: the configuration's); smaller layers for ncu captures")
@@ -597,10 +706,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    unit = {"kv": "KV rows/s", "kv_scores": "cached rows scored/s"}.get(args.workload, "tokens/s")
+    unit = {"kv": "KV rows/s", "kv_scores": "cached rows scored/s", "qsa": "context rows fetched/s"}.get(
+        args.workload, "tokens/s")
     metric = {"ds_decode": "MoE layer tok/s, DeepSeek-class MXFP4 decode sweep B=1,4,16,64",
               "kv": "FP8 KV quantize+dequantize rows/s",
-              "kv_scores": "MXFP8 KV-cache score rows/s (decode, 8 seq x 32768 x 512, 61 layers)"}.get(
+              "kv_scores": "MXFP8 KV-cache score rows/s (decode, 8 seq x 32768 x 512, 61 layers)",
+              "qsa": "Qwen QSA KV-cache decode update_and_fetch, context rows/s (8 seq x 32768, 12 layers)"}.get(
                   args.workload, f"MoE layer tok/s ({args.workload})")
 
     if args.impl == "reference":
@@ -675,24 +786,29 @@ def main():
             torch.distributed.barrier()
             torch.distributed.destroy_process_group()
             return
+        config = {"workload": args.workload, "batches": list(r["batches"]),
+                  "tokens_per_step": r["tokens"], "layers_cycled": args.layers,
+                  "l2": "8 resident layers (48 GB) cycled per step: weights larger than L2",
+                  "parallelism": "replicas" if world > 1 else "single GPU",
+                  "launch": "CUDA graph per (layer, batch)" if r.get("graphed") else "eager",
+                  "per_batch": r["per_b"]}
+        if r.get("config"):
+            config = dict(r["config"], workload=args.workload,
+                          parallelism="replicas" if world > 1 else "single GPU")
         line = {
             "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "mxfp4 weights, bf16 activations, fp32 accumulate",
-            "data": "synthetic (seeded N(0,0.02) MXFP4 experts, N(0,1) bf16 tokens, Zipf-skewed router)",
-            "config": {"workload": args.workload, "batches": list(r["batches"]),
-                       "tokens_per_step": r["tokens"], "layers_cycled": args.layers,
-                       "l2": "8 resident layers (48 GB) cycled per step: weights larger than L2",
-                       "parallelism": "replicas" if world > 1 else "single GPU",
-                       "launch": "CUDA graph per (layer, batch)" if r.get("graphed") else "eager",
-                       "per_batch": r["per_b"]},
+            "vs_baseline": None, "dtype": r.get("dtype", "mxfp4 weights, bf16 activations, fp32 accumulate"),
+            "data": r.get("data", "synthetic (seeded N(0,0.02) MXFP4 experts, N(0,1) bf16 tokens, Zipf-skewed router)"),
+            "config": config,
             "e2e": None if ms_e2e is None else {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2),
                                                  "unit": unit, "h2d_bytes_per_step": r["h2d"],
                                                  "d2h_bytes_per_step": r["d2h"]},
             "roofline": ({"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                           "frac": round(achieved / hbm, 4), "traffic": traffic,
                           "algorithmic_bytes_per_step": r["alg_bytes"],
-                          "kernel": "expert FFN call (wmoe_mxfp4_moe_forward), " + r["peak_src"] + " HBM peak"}
+                          "kernel": r.get("kernel", "expert FFN call (wmoe_mxfp4_moe_forward)") + ", " +
+                                    r["peak_src"] + " HBM peak"}
                          if not r.get("prefill") else
                          {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": r["tc_peak"],
                           "unit": "TFLOP/s", "frac": round(achieved_tf / r["tc_peak"], 4), "traffic": traffic,

@@ -8,7 +8,10 @@
  *     legacy default stream);
  *   - is asynchronous and stream-ordered, allocates no memory and keeps no
  *     state between calls (the tensor-core path caches a per-device tensor-map
- *     encoder lookup behind a mutex);
+ *     encoder lookup behind a mutex).  Exceptions, stated at each: the
+ *     peer-exchange buffers of wep_ipc_alloc, and the installed-model loader
+ *     wld_load_expert_layer, which is synchronous and keeps pinned host
+ *     staging between calls;
  *   - returns WM_OK (0) or a negative WM_ERR_* code; w_last_error() then
  *     describes the failure for the calling thread.  No C++ exception crosses
  *     this boundary.
@@ -174,6 +177,26 @@ WM_API int waffine4_dequantize(const uint32_t *packed, const wm_bf16 *scales, co
                         int64_t rows, int64_t cols, int group, int out_dtype, void *out,
                         wm_stream_t stream);
 
+/* Qwen QSA affine-quantized KV cache: mlx-lm QuantizedKVCache with group 32
+ * and `bits` 4 or 8 (runtime/deepseek_v4_ssd/qwen_quantized_cache.py:6-20).
+ * One tensor's cache (keys or values) is packed uint32
+ * [n_seq, capacity, D*bits/32] (element 0 in the lowest bits) with bf16
+ * scales and biases [n_seq, capacity, D/32]; n_seq = batch * kv heads.
+ * append: quantize keys (and values, if not NULL) bf16 [n_seq, L, D] into
+ * cache rows [offset, offset + L) of each sequence -- the quantize half of
+ * update_and_fetch (qwen_quantized_cache.py:16).  Both tensors in one launch;
+ * at most 2^34 values (n_seq * L * D) per tensor and call. */
+WM_API int wkv_affine_append(const wm_bf16 *keys, const wm_bf16 *values, int64_t n_seq, int64_t L, int D,
+                             int bits, uint32_t *k_q, wm_bf16 *k_s, wm_bf16 *k_b, uint32_t *v_q, wm_bf16 *v_s,
+                             wm_bf16 *v_b, int64_t capacity, int64_t offset, wm_stream_t stream);
+
+/* fetch: dequantize cache rows [0, L) of each sequence to bf16 [n_seq, L, D],
+ * w = float32(scale) * q + float32(bias) rounded once -- the dequantize half
+ * of update_and_fetch (qwen_quantized_cache.py:19-20).  values_out may be NULL. */
+WM_API int wkv_affine_fetch(const uint32_t *k_q, const wm_bf16 *k_s, const wm_bf16 *k_b, const uint32_t *v_q,
+                            const wm_bf16 *v_s, const wm_bf16 *v_b, int64_t n_seq, int64_t L, int64_t capacity,
+                            int D, int bits, wm_bf16 *keys_out, wm_bf16 *values_out, wm_stream_t stream);
+
 /* ------------------------------------------------------------- KV cache --- */
 
 /* Quantize bf16 rows [rows, D] into payload [rows, D*bits/8] and scales
@@ -310,6 +333,23 @@ WM_API int wmoe_affine4_moe_forward(const wm_bf16 *x, const int32_t *idx, const 
                              const wm_bf16 *bi2, int group, int gate_up_order, float swiglu_limit,
                              int shared_expert, const float *shared_w, wm_bf16 *out,
                              void *workspace, size_t ws_bytes, wm_stream_t stream);
+
+/* Installed-model expert layer -> device tensors.  `path` is an installed
+ * `experts/layer_XX.bin`: n_blobs expert blobs of blob_size bytes (the file
+ * size must equal n_blobs * blob_size; manifest.py:170-175).  For every region
+ * r and blob b, bytes [src_offsets[r], src_offsets[r] + lengths[r]) of blob b
+ * are copied to device memory dst_bases[r] + b * dst_pitches[r].  This
+ * replaces the per-blob slot copies of the expert cache (_SlotPool.store,
+ * expert_cache.py:416-428, into the slot layout of expert_layout.py:8-80): a
+ * caller that points w3 and w1 (or their scales) at the two halves of each
+ * expert's rows in one [E, 2I, ...] tensor gets the fused w13 = [w3; w1].
+ * The file is read in chunks of whole blobs (about chunk_bytes each), by up
+ * to 8 threads, into two pinned buffers that the library keeps (and grows)
+ * across calls until exit; concurrent calls are serialised.  Returns after
+ * every copy on `stream` has completed. */
+WM_API int wld_load_expert_layer(const char *path, size_t blob_size, int n_blobs, int n_regions,
+                                 const size_t *src_offsets, const size_t *lengths, void *const *dst_bases,
+                                 const size_t *dst_pitches, size_t chunk_bytes, wm_stream_t stream);
 
 #ifdef __cplusplus
 }

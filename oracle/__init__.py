@@ -20,6 +20,9 @@ here.  The oracle restates, in numpy and plain C:
   device kernel (via ``oracle/c/router_ref.c``), so indices compare exactly.
 * ``moe``      -- the MoE layer composition (``model.py:393-504``,
   ``deepseek_v41/moe.py:30-112``, ``qwen4_exp.py:588-704``).
+* ``loader``   -- the expert-slot layouts of an installed model and the
+  region-by-region blob store (``expert_layout.py:8-80``,
+  ``expert_cache.py:416-493``).
 
 Pinning: ``formats`` is pinned by the reference's own known-answer tests
 (``Tests/DeepSeekRepackTests/DeepSeekRepackTests.swift:336-411``) and by the

@@ -292,6 +292,85 @@ def affine4_dequantize(packed_u32, scales_bf16_bits, biases_bf16_bits, group: in
     return (qg * s[..., None] + b[..., None]).reshape(rows, -1).astype(np.float32)
 
 
+def affine_quantize(w_bf16_values: np.ndarray, group: int = 32, bits: int = 4):
+    """The affine scheme of ``affine4_quantize`` for 4 or 8 bits
+    (2**bits - 1 steps per group); 32/bits values per uint32, element 0 in the
+    lowest bits.  Same parity status as ``affine4_quantize``: the quantizer
+    is unpinned, the dequant w = scale * q + bias is the pinned part."""
+    if bits not in (4, 8):
+        raise ValueError("affine bits must be 4 or 8")
+    w = np.ascontiguousarray(w_bf16_values, np.float32)
+    rows, cols = w.shape
+    if cols % group or group % 32:
+        raise ValueError("affine needs cols % group == 0")
+    nbins = np.float32(2 ** bits - 1)
+    g = w.reshape(rows, cols // group, group)
+    w_max = g.max(-1)
+    w_min = g.min(-1)
+    mask = np.abs(w_min) > np.abs(w_max)
+    scale = np.maximum((w_max - w_min) / nbins, np.float32(1e-7)).astype(np.float32)
+    scale = np.where(mask, scale, -scale).astype(np.float32)
+    edge = np.where(mask, w_min, w_max).astype(np.float32)
+    q0 = np.rint(edge / scale).astype(np.float32)
+    scale = np.where(q0 != 0, edge / np.where(q0 != 0, q0, 1), scale).astype(np.float32)
+    bias = np.where(q0 == 0, np.float32(0), edge).astype(np.float32)
+    q = np.clip(np.rint((g - bias[..., None]) / scale[..., None]), 0, nbins).astype(np.uint32)
+    per = 32 // bits
+    q = q.reshape(rows, cols // per, per)
+    packed = np.zeros((rows, cols // per), np.uint32)
+    for i in range(per):
+        packed |= q[..., i] << np.uint32(bits * i)
+    return packed, f32_to_bf16_bits(scale), f32_to_bf16_bits(bias)
+
+
+def affine_dequantize(packed_u32, scales_bf16_bits, biases_bf16_bits, group: int = 32, bits: int = 4) -> np.ndarray:
+    """w = float32(scale) * q + float32(bias), float32 [rows, cols]."""
+    p = np.asarray(packed_u32, np.uint32)
+    rows, words = p.shape
+    per = 32 // bits
+    mask = np.uint32(2 ** bits - 1)
+    q = np.empty((rows, words, per), np.float32)
+    for i in range(per):
+        q[..., i] = ((p >> np.uint32(bits * i)) & mask).astype(np.float32)
+    q = q.reshape(rows, -1, group)
+    s = bf16_bits_to_f32(scales_bf16_bits)
+    b = bf16_bits_to_f32(biases_bf16_bits)
+    return (q * s[..., None] + b[..., None]).reshape(rows, -1).astype(np.float32)
+
+
+class QSACache:
+    """The Qwen QSA quantized KV cache (qwen_quantized_cache.py:6-20) on
+    mlx-lm's QuantizedKVCache: every update quantizes the new keys and values
+    (group 32, ``bits``), appends them, and returns the whole history
+    dequantized (bf16 bit patterns [n_seq, offset, D]).  Storage growth is not
+    modelled: it does not change the values."""
+
+    def __init__(self, bits: int, dimension: int):
+        if bits not in (4, 8) or dimension % 32:
+            raise ValueError("QSA quantized cache requires 4 or 8 bits and a width divisible by 32")
+        self.bits, self.dimension = bits, dimension
+        self.parts = None      # [(q, s, b) for keys, values], rows of all sequences as [n_seq, offset, width]
+
+    def update_and_fetch(self, keys_bf16_bits, values_bf16_bits):
+        out = []
+        new_parts = []
+        for i, x in enumerate((keys_bf16_bits, values_bf16_bits)):
+            n_seq, L, D = x.shape
+            if D != self.dimension:
+                raise ValueError("QSA cache width does not match")
+            q, s, b = affine_quantize(bf16_bits_to_f32(x.reshape(-1, D)), 32, self.bits)
+            q, s, b = q.reshape(n_seq, L, -1), s.reshape(n_seq, L, -1), b.reshape(n_seq, L, -1)
+            if self.parts is not None:
+                pq, ps, pb = self.parts[i]
+                q, s, b = (np.concatenate([pq, q], 1), np.concatenate([ps, s], 1), np.concatenate([pb, b], 1))
+            new_parts.append((q, s, b))
+            n, T, _ = q.shape
+            w = affine_dequantize(q.reshape(n * T, -1), s.reshape(n * T, -1), b.reshape(n * T, -1), 32, self.bits)
+            out.append(f32_to_bf16_bits(w).reshape(n, T, D))
+        self.parts = new_parts
+        return tuple(out)
+
+
 # --------------------------------------------------------------------------
 # KV-cache row formats
 # --------------------------------------------------------------------------

@@ -17,5 +17,6 @@ from .moe import MoE, SparseMoE, TinyMoE, route_reduce, streaming_moe  # noqa: F
 from .router import Gate, qwen_route, route, stable_topk_indices, topk_scores  # noqa: F401
 
 from .linear import MXFP8Linear, expand_block_scales, mx_linear  # noqa: F401
+from .loader import load_expert_layer, load_installed_experts, read_layout  # noqa: F401
 
 __version__ = "0.1.0"

@@ -50,8 +50,11 @@ SIGNATURES = {
     "wep_put_rows": [_I, _P, _P, _P, _P, _I, _P, _I, _I, _P, _P, _P, _P],
     "wep_wait": [_P, _I, _P, _P, _P],
     "wep_sum_rows": [_P, _I, _I, _I, _P, _P, _P],
+    "wld_load_expert_layer": [ctypes.c_char_p, _SZ, _I, _I, _P, _P, _P, _P, _SZ, _P],
     "waffine4_quantize": [_P, _I64, _I64, _I, _P, _P, _P, _P],
     "waffine4_dequantize": [_P, _P, _P, _I64, _I64, _I, _I, _P, _P],
+    "wkv_affine_append": [_P, _P, _I64, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _P],
+    "wkv_affine_fetch": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _P, _P],
     "wkv_quantize": [_P, _I64, _I, _I, _P, _P, _P],
     "wkv_dequantize": [_P, _P, _I64, _I, _I, _P, _P],
     "wkv_gather_dequantize": [_P, _P, _I64, _P, _I64, _I, _I, _P, _P],

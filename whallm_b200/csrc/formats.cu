@@ -186,6 +186,155 @@ __global__ void k_affine4_dequantize(const uint32_t *__restrict__ packed, const 
   }
 }
 
+// --------------------------------------------------- affine KV (QSA) ----
+// mlx-lm QuantizedKVCache with group 32 and 4 or 8 bits, as the Qwen QSA
+// cache configures it (qwen_quantized_cache.py:6-20).  The cache of one
+// tensor (keys or values) is packed uint32 [n_seq, capacity, D*BITS/32]
+// (element 0 in the lowest bits) with bf16 scales and biases
+// [n_seq, capacity, D/32]; n_seq = batch * kv heads.  blockIdx.y selects
+// keys (0) or values (1), so one launch serves both.
+// Division of a uint32 n by an invariant d >= 1 with one multiply-high, add
+// and shift (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", PLDI 1994, fig. 4.1): l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (mulhi(n, m) + n) >> l, the sum
+// taken in 64 bits.  Exact for every n < 2^32.
+struct DivU32 {
+  uint32_t m, l, d;
+};
+
+DivU32 make_divu32(uint32_t d) {
+  uint32_t l = 0;
+  while ((uint64_t(1) << l) < d) ++l;
+  uint64_t m = ((uint64_t(1) << 32) * ((uint64_t(1) << l) - d)) / d + 1;
+  return DivU32{static_cast<uint32_t>(m), l, d};
+}
+
+__device__ __forceinline__ uint32_t divu32(uint32_t n, DivU32 q) {
+  return static_cast<uint32_t>((static_cast<uint64_t>(__umulhi(n, q.m)) + n) >> q.l);
+}
+
+struct AffineKV {
+  const uint16_t *src[2];
+  uint32_t *q[2];
+  uint16_t *s[2];
+  uint16_t *b[2];
+  uint16_t *out[2];
+};
+
+// Per-group scale and bias of the affine scheme (the endpoint with the larger
+// magnitude is represented exactly; see k_affine4_quantize).
+__device__ __forceinline__ void affine_params(float wmin, float wmax, float nbins, float &scale, float &bias) {
+  bool mask = fabsf(wmin) > fabsf(wmax);
+  scale = fmaxf(__fdiv_rn(wmax - wmin, nbins), 1e-7f);
+  scale = mask ? scale : -scale;
+  float edge = mask ? wmin : wmax;
+  float q0 = rintf(__fdiv_rn(edge, scale));
+  if (q0 != 0.0f) scale = __fdiv_rn(edge, q0);
+  bias = q0 == 0.0f ? 0.0f : edge;
+}
+
+// Quantize n_seq x L new rows into cache rows [offset, offset + L) of each
+// sequence.  A thread owns 8 consecutive values (one 16-byte load); the four
+// lanes of a 32-value group agree on its min/max by shuffles, and a warp
+// covers 256 consecutive values, so loads and stores are contiguous.  The
+// loop runs per warp (every lane takes the same trip count) so that the
+// shuffles always see the whole warp; lanes past the end compute on zeros
+// and store nothing.
+template <int BITS>
+__global__ void k_affine_kv_append(AffineKV a, uint32_t chunks, DivU32 cpr, DivU32 L, int64_t capacity,
+                                   int64_t offset) {
+  constexpr float kBins = static_cast<float>((1 << BITS) - 1);
+  const int t = blockIdx.y;
+  const int lane = threadIdx.x & 31;
+  const uint16_t *src = a.src[t];
+  const uint32_t stride = gridDim.x * blockDim.x;
+  for (uint32_t base = blockIdx.x * blockDim.x + (threadIdx.x & ~31u); base < chunks; base += stride) {
+    const uint32_t c = base + lane;
+    const bool ok = c < chunks;
+    float v[8];
+    uint4 u = ok ? __ldg(reinterpret_cast<const uint4 *>(src) + c) : make_uint4(0, 0, 0, 0);
+    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[2 * j] = wm_bf16lo(w4[j]);
+      v[2 * j + 1] = wm_bf16hi(w4[j]);
+    }
+    float wmax = v[0], wmin = v[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) { wmax = fmaxf(wmax, v[j]); wmin = fminf(wmin, v[j]); }
+#pragma unroll
+    for (int m = 1; m < 4; m <<= 1) {
+      wmax = fmaxf(wmax, __shfl_xor_sync(0xffffffffu, wmax, m));
+      wmin = fminf(wmin, __shfl_xor_sync(0xffffffffu, wmin, m));
+    }
+    float scale, bias;
+    affine_params(wmin, wmax, kBins, scale, bias);
+    uint32_t q8[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float q = rintf(__fdiv_rn(v[j] - bias, scale));
+      q8[j] = static_cast<uint32_t>(fminf(fmaxf(q, 0.0f), kBins));
+    }
+    if (!ok) continue;
+    const uint32_t r = divu32(c, cpr);
+    const uint32_t col = c - r * cpr.d;                      // 8-value chunk within the row
+    const uint32_t seq = divu32(r, L);
+    const int64_t row = static_cast<int64_t>(seq) * capacity + offset + (r - seq * L.d);
+    uint32_t *dst = a.q[t] + row * (int64_t)cpr.d * (BITS / 4) + col * (BITS / 4);
+    if (BITS == 4) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) word |= q8[j] << (4 * j);
+      *dst = word;
+    } else {
+      uint32_t lo = q8[0] | (q8[1] << 8) | (q8[2] << 16) | (q8[3] << 24);
+      uint32_t hi = q8[4] | (q8[5] << 8) | (q8[6] << 16) | (q8[7] << 24);
+      *reinterpret_cast<uint2 *>(dst) = make_uint2(lo, hi);
+    }
+    if ((col & 3) == 0) {
+      const int64_t gi = row * (cpr.d / 4) + col / 4;
+      a.s[t][gi] = wm_f32_to_bf16(scale);
+      a.b[t][gi] = wm_f32_to_bf16(bias);
+    }
+  }
+}
+
+// Dequantize cache rows [0, L) of each sequence to bf16 [n_seq, L, D]:
+// w = float32(scale) * q + float32(bias), rounded once to bf16.  A thread
+// reads 8 packed bytes (8 values at 8 bits, 16 at 4 bits) and writes them as
+// one or two 16-byte stores; consecutive threads cover consecutive values.
+template <int BITS>
+__global__ void k_affine_kv_fetch(AffineKV a, uint32_t chunks, DivU32 cpr, DivU32 L, int64_t capacity) {
+  constexpr int kVals = 64 / BITS;   // values per thread
+  constexpr int kPer = 32 / BITS;    // values per uint32
+  constexpr int kCpg = 32 / kVals;   // threads per 32-value scale group
+  constexpr uint32_t kMask = (1u << BITS) - 1u;
+  const int t = blockIdx.y;
+  for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c < chunks; c += gridDim.x * blockDim.x) {
+    const uint32_t r = divu32(c, cpr);
+    const uint32_t col = c - r * cpr.d;
+    const uint32_t seq = divu32(r, L);
+    const int64_t row = static_cast<int64_t>(seq) * capacity + (r - seq * L.d);
+    const int64_t gi = row * (cpr.d / kCpg) + col / kCpg;
+    const float s = wm_bf16_to_f32(__ldg(a.s[t] + gi));
+    const float b = wm_bf16_to_f32(__ldg(a.b[t] + gi));
+    // a row holds D*BITS/32 = 2*cpr words
+    const uint2 u = __ldg(reinterpret_cast<const uint2 *>(a.q[t] + row * (int64_t)cpr.d * 2) + col);
+    const uint32_t w[2] = {u.x, u.y};
+    uint32_t o[kVals / 2];
+#pragma unroll
+    for (int j = 0; j < kVals / 2; ++j) {
+      const int e = 2 * j;
+      const float v0 = s * static_cast<float>((w[e / kPer] >> (BITS * (e % kPer))) & kMask) + b;
+      const float v1 = s * static_cast<float>((w[e / kPer] >> (BITS * (e % kPer + 1))) & kMask) + b;
+      o[j] = wm_f32_to_bf16(v0) | (static_cast<uint32_t>(wm_f32_to_bf16(v1)) << 16);
+    }
+    uint4 *dst = reinterpret_cast<uint4 *>(a.out[t]) + static_cast<int64_t>(c) * (kVals / 8);   // values c*kVals..
+#pragma unroll
+    for (int i = 0; i < kVals / 8; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+  }
+}
+
 // ------------------------------------------------------------- KV rows ----
 
 __device__ __forceinline__ int kv_block(int fmt) {
@@ -416,6 +565,75 @@ int waffine4_dequantize(const uint32_t *packed, const wm_bf16 *scales, const wm_
     k_affine4_dequantize<uint16_t><<<grid_for(chunks, 256), 256, 0, stream>>>(packed, scales, biases, chunks, group,
                                                                                static_cast<uint16_t *>(out));
   return wm::check_launch("waffine4_dequantize");
+}
+
+int wkv_affine_append(const wm_bf16 *keys, const wm_bf16 *values, int64_t n_seq, int64_t L, int D, int bits,
+                      uint32_t *k_q, wm_bf16 *k_s, wm_bf16 *k_b, uint32_t *v_q, wm_bf16 *v_s, wm_bf16 *v_b,
+                      int64_t capacity, int64_t offset, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(bits == 4 || bits == 8, "QSA quantized cache requires 4 or 8 bits and a width divisible by 32");
+  WM_REQUIRE(D > 0 && D % 32 == 0, "QSA quantized cache requires 4 or 8 bits and a width divisible by 32");
+  WM_REQUIRE(n_seq >= 0 && L >= 0 && offset >= 0 && offset + L <= capacity, "QSA cache rows exceed its capacity");
+  WM_REQUIRE(keys && k_q && k_s && k_b, "QSA cache append needs keys and their cache");
+  WM_REQUIRE(!values || (v_q && v_s && v_b), "QSA cache append: values given without their cache");
+  WM_REQUIRE(wm::aligned(keys, 16) && wm::aligned(k_q, 16) && (!values || (wm::aligned(values, 16) && wm::aligned(v_q, 16))),
+             "QSA cache buffers must be 16-byte aligned");
+  const int cpr = D / 8;
+  const int64_t chunks = n_seq * L * cpr;
+  WM_REQUIRE(chunks <= (int64_t(1) << 31), "QSA cache append: more than 2^34 values in one call");
+  if (chunks == 0) return WM_OK;
+  AffineKV a{};
+  a.src[0] = keys;
+  a.src[1] = values;
+  a.q[0] = k_q;
+  a.q[1] = v_q;
+  a.s[0] = k_s;
+  a.s[1] = v_s;
+  a.b[0] = k_b;
+  a.b[1] = v_b;
+  dim3 grid(grid_for(chunks, 256), values ? 2 : 1);
+  if (bits == 4)
+    k_affine_kv_append<4><<<grid, 256, 0, stream>>>(a, static_cast<uint32_t>(chunks), make_divu32(cpr),
+                                                    make_divu32(static_cast<uint32_t>(L)), capacity, offset);
+  else
+    k_affine_kv_append<8><<<grid, 256, 0, stream>>>(a, static_cast<uint32_t>(chunks), make_divu32(cpr),
+                                                    make_divu32(static_cast<uint32_t>(L)), capacity, offset);
+  return wm::check_launch("wkv_affine_append");
+}
+
+int wkv_affine_fetch(const uint32_t *k_q, const wm_bf16 *k_s, const wm_bf16 *k_b, const uint32_t *v_q,
+                     const wm_bf16 *v_s, const wm_bf16 *v_b, int64_t n_seq, int64_t L, int64_t capacity, int D,
+                     int bits, wm_bf16 *keys_out, wm_bf16 *values_out, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(bits == 4 || bits == 8, "QSA quantized cache requires 4 or 8 bits and a width divisible by 32");
+  WM_REQUIRE(D > 0 && D % 32 == 0, "QSA quantized cache requires 4 or 8 bits and a width divisible by 32");
+  WM_REQUIRE(n_seq >= 0 && L >= 0 && L <= capacity, "QSA cache rows exceed its capacity");
+  WM_REQUIRE(k_q && k_s && k_b && keys_out, "QSA cache fetch needs the key cache and an output");
+  WM_REQUIRE(!values_out || (v_q && v_s && v_b), "QSA cache fetch: values output without their cache");
+  WM_REQUIRE(wm::aligned(k_q, 16) && wm::aligned(keys_out, 16) &&
+                 (!values_out || (wm::aligned(v_q, 16) && wm::aligned(values_out, 16))),
+             "QSA cache buffers must be 16-byte aligned");
+  const int cpr = D * bits / 64;   // threads per row: 8 packed bytes each
+  const int64_t chunks = n_seq * L * cpr;
+  WM_REQUIRE(chunks <= (int64_t(1) << 31), "QSA cache fetch: more than 2^34 values in one call");
+  if (chunks == 0) return WM_OK;
+  AffineKV a{};
+  a.q[0] = const_cast<uint32_t *>(k_q);
+  a.q[1] = const_cast<uint32_t *>(v_q);
+  a.s[0] = const_cast<uint16_t *>(k_s);
+  a.s[1] = const_cast<uint16_t *>(v_s);
+  a.b[0] = const_cast<uint16_t *>(k_b);
+  a.b[1] = const_cast<uint16_t *>(v_b);
+  a.out[0] = keys_out;
+  a.out[1] = values_out;
+  dim3 grid(grid_for(chunks, 256), values_out ? 2 : 1);
+  if (bits == 4)
+    k_affine_kv_fetch<4><<<grid, 256, 0, stream>>>(a, static_cast<uint32_t>(chunks), make_divu32(cpr),
+                                                   make_divu32(static_cast<uint32_t>(L)), capacity);
+  else
+    k_affine_kv_fetch<8><<<grid, 256, 0, stream>>>(a, static_cast<uint32_t>(chunks), make_divu32(cpr),
+                                                   make_divu32(static_cast<uint32_t>(L)), capacity);
+  return wm::check_launch("wkv_affine_fetch");
 }
 
 int wkv_quantize(const wm_bf16 *x, int64_t rows, int D, int fmt, uint8_t *payload, void *scales, wm_stream_t stream) {
