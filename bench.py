@@ -323,7 +323,7 @@ def run_ours(args, rank, world, dev):
         # 32768-token context; one step appends one token per sequence and fetches the
         # whole dequantized history of every cache (update_and_fetch)
         from whallm_b200.kvcache import QSAQuantizedCache
-        Bq, Lc, n_layer = 8, 32768, 12
+        Bq, Lc, n_layer = 8, args.context, 12
         shapes = ((8, 2, 256), (4, 1, 128))      # (bits, kv heads, head dim)
         cap = Lc + args.warmup + 2 * args.steps     # warm-up, timed and end-to-end steps each append a row
         caches = []
@@ -371,10 +371,11 @@ def run_ours(args, rank, world, dev):
         torch.cuda.synchronize()
         ms_exp = s2.elapsed_time(e2) / args.steps
         L_now = caches[0][0].offset
-        alg = 0
+        rd = wr = 0
         for bits, hk, hd in shapes:   # per layer: K and V, packed + bf16 scale/bias read, bf16 written
-            alg += 2 * Bq * hk * L_now * (hd * bits // 8 + 4 * (hd // 32) + 2 * hd)
-        alg *= n_layer
+            rd += 2 * Bq * hk * L_now * (hd * bits // 8 + 4 * (hd // 32)) * n_layer
+            wr += 2 * Bq * hk * L_now * 2 * hd * n_layer
+        alg = rd + wr
         # end to end: the new rows come from pinned host memory, the newest dequantized
         # row of every cache goes back
         hnews = [x.cpu().pin_memory() for x in news]
@@ -402,7 +403,8 @@ def run_ours(args, rank, world, dev):
                         config={"sequences": Bq, "context": Lc, "full_attention_layers": n_layer,
                                 "caches": "K/V 8-bit 2 heads x 256, index 4-bit 1 head x 128, group 32",
                                 "step": "append one row per sequence + fetch the whole history, every cache",
-                                "l2": "4.1 GB of packed history read and 8.1 GB of bf16 written per step: larger than L2",
+                                "l2": f"{rd / 1e9:.1f} GB of packed history read and {wr / 1e9:.1f} GB of bf16 "
+                                      "written per step: larger than L2",
                                 "launch": "eager"}))
         return res
     if wl == "kv":
@@ -698,6 +700,8 @@ def main():
     ap.add_argument("--layers", type=int, default=8, help="resident layers cycled per step (no L2 reuse)")
     ap.add_argument("--experts", type=int, default=None,
                     help="routed experts per layer (default: the configuration's); smaller layers for ncu captures")
+    ap.add_argument("--context", type=int, default=32768,
+                    help="qsa workload: tokens already cached per sequence (smaller for ncu captures)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

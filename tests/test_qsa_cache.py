@@ -118,6 +118,40 @@ def test_gpu_append_fetch_match_oracle(dev, bits, n_seq, L, D, cap, off):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("bits", [4, 8])
+def test_gpu_append_exact_ties(dev, bits):
+    # groups with min -n/16 and max 0 get scale 1/16 and bias min, so
+    # v = -(2k+1)/32 quantizes from exactly n - k - 1/2: every rounding tie
+    # (and the values one bf16 step either side of it) must match the oracle
+    n = 2 ** bits - 1
+    rng = np.random.default_rng(bits)
+    rows = []
+    for _ in range(64):
+        ks = rng.integers(0, min(n, 128), 32)     # 2k+1 < 256: exact in bf16
+        v = -(2 * ks + 1) / 32.0
+        v[0], v[1] = -n / 16.0, 0.0
+        rows.append(v)
+    x = np.asarray(rows, np.float32)
+    nudged = F.bf16_bits_to_f32(F.f32_to_bf16_bits(x) + np.uint16(1))
+    x = np.concatenate([x, np.where(np.arange(32) < 2, x, nudged)])
+    xb = F.f32_to_bf16_bits(x).reshape(1, -1, 32)
+    D = 32
+    rows_n = xb.shape[1]
+    caches = [(torch.zeros(1, rows_n, bits, dtype=torch.int32, device=dev),
+               torch.zeros(1, rows_n, 1, dtype=torch.bfloat16, device=dev),
+               torch.zeros(1, rows_n, 1, dtype=torch.bfloat16, device=dev))]
+    k = _t(xb, dev)
+    (kq, ks, kb), = caches
+    C.call("wkv_affine_append", C.ptr(k), None, 1, rows_n, D, bits, C.ptr(kq), C.ptr(ks), C.ptr(kb), None, None,
+           None, rows_n, 0, C.stream_of(k))
+    torch.cuda.synchronize()
+    rq, rs, rb = F.affine_quantize(F.bf16_bits_to_f32(xb.reshape(-1, D)), 32, bits)
+    np.testing.assert_array_equal(kq.cpu().numpy().view(np.uint32).reshape(-1, bits), rq)
+    np.testing.assert_array_equal(_bits(ks).reshape(-1, 1), rs)
+    np.testing.assert_array_equal(_bits(kb).reshape(-1, 1), rb)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [4, 8])
 def test_gpu_cache_steps_match_oracle_cache(dev, bits):
     B, H, D = 1, 4, 128
     rng = np.random.default_rng(7 + bits)

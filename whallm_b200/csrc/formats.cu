@@ -269,11 +269,22 @@ __global__ void k_affine_kv_append(AffineKV a, uint32_t chunks, DivU32 cpr, DivU
     }
     float scale, bias;
     affine_params(wmin, wmax, kBins, scale, bias);
+    // q = clamp(rint(RN((v - bias) / scale)), 0, bins).  The quotient is taken
+    // as (v - bias) * RN(1/scale), which differs from the correctly rounded
+    // one by under 2^-14 for |quotient| < 2^9; it can only round to another
+    // integer when it lies within that distance of a half-integer, so there
+    // (a 2^-10 window) the exact IEEE division decides.  Beyond 2^9 both
+    // clamp to the same end.
+    const float rcp = __frcp_rn(scale);
     uint32_t q8[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      float q = rintf(__fdiv_rn(v[j] - bias, scale));
-      q8[j] = static_cast<uint32_t>(fminf(fmaxf(q, 0.0f), kBins));
+      const float x = v[j] - bias;
+      float y = x * rcp;
+      const float f = y - floorf(y);
+      if (fabsf(f - 0.5f) < 0x1p-10f) y = __fdiv_rn(x, scale);
+      const float q = fminf(fmaxf(rintf(y), 0.0f), kBins);
+      q8[j] = __float_as_uint(q + 8388608.0f) & 0xFFu;   // integer q in [0, 255], exactly
     }
     if (!ok) continue;
     const uint32_t r = divu32(c, cpr);
@@ -299,8 +310,24 @@ __global__ void k_affine_kv_append(AffineKV a, uint32_t chunks, DivU32 cpr, DivU
   }
 }
 
+// 0x4B000000 | code i of w: the float 2^23 + code.  For 8 bits one byte
+// permute; for 4 bits a shift and a mask.
+template <int BITS>
+__device__ __forceinline__ uint32_t code_bits(uint32_t w, int i) {
+  if (BITS == 8) return __byte_perm(w, 0x4B000000u, 0x7440u | static_cast<uint32_t>(i));
+  return ((w >> (4 * i)) & 15u) | 0x4B000000u;
+}
+
+// Two floats -> bf16x2 (lo in the low half), round to nearest even, one cvt.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
 // Dequantize cache rows [0, L) of each sequence to bf16 [n_seq, L, D]:
-// w = float32(scale) * q + float32(bias), rounded once to bf16.  A thread
+// w = float32(scale) * q + float32(bias), rounded once to bf16 (scale * q is
+// exact: an 8-bit significand times an integer below 256).  A thread
 // reads 8 packed bytes (8 values at 8 bits, 16 at 4 bits) and writes them as
 // one or two 16-byte stores; consecutive threads cover consecutive values.
 template <int BITS>
@@ -308,7 +335,6 @@ __global__ void k_affine_kv_fetch(AffineKV a, uint32_t chunks, DivU32 cpr, DivU3
   constexpr int kVals = 64 / BITS;   // values per thread
   constexpr int kPer = 32 / BITS;    // values per uint32
   constexpr int kCpg = 32 / kVals;   // threads per 32-value scale group
-  constexpr uint32_t kMask = (1u << BITS) - 1u;
   const int t = blockIdx.y;
   for (uint32_t c = blockIdx.x * blockDim.x + threadIdx.x; c < chunks; c += gridDim.x * blockDim.x) {
     const uint32_t r = divu32(c, cpr);
@@ -325,9 +351,10 @@ __global__ void k_affine_kv_fetch(AffineKV a, uint32_t chunks, DivU32 cpr, DivU3
 #pragma unroll
     for (int j = 0; j < kVals / 2; ++j) {
       const int e = 2 * j;
-      const float v0 = s * static_cast<float>((w[e / kPer] >> (BITS * (e % kPer))) & kMask) + b;
-      const float v1 = s * static_cast<float>((w[e / kPer] >> (BITS * (e % kPer + 1))) & kMask) + b;
-      o[j] = wm_f32_to_bf16(v0) | (static_cast<uint32_t>(wm_f32_to_bf16(v1)) << 16);
+      // q as float, exactly: the code in the low mantissa bits of 2^23, minus 2^23
+      const float q0 = __uint_as_float(code_bits<BITS>(w[e / kPer], e % kPer)) - 8388608.0f;
+      const float q1 = __uint_as_float(code_bits<BITS>(w[e / kPer], e % kPer + 1)) - 8388608.0f;
+      o[j] = pack_bf16x2(s * q0 + b, s * q1 + b);
     }
     uint4 *dst = reinterpret_cast<uint4 *>(a.out[t]) + static_cast<int64_t>(c) * (kVals / 8);   // values c*kVals..
 #pragma unroll
