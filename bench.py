@@ -760,11 +760,14 @@ def main():
         # experts this workload streams per step
         traffic = None
         prof = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(prof) and r.get("distinct"):
+        if os.path.exists(prof) and (r.get("distinct") or args.workload == "qsa"):
             try:
                 t = json.load(open(prof)).get(args.workload)
-                if t:
+                if t and r.get("distinct"):
                     traffic = round(t["bytes_per_expert"] * sum(r["distinct"]))
+                elif t:
+                    # DRAM bytes per algorithmic byte of the fetch, from one capture at a smaller context
+                    traffic = round(t["dram_per_algorithmic_byte"] * r["alg_bytes"])
             except Exception:
                 traffic = None
         if r.get("ep"):
