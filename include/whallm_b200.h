@@ -206,6 +206,18 @@ WM_API int wkv_affine_fetch(const uint32_t *k_q, const wm_bf16 *k_s, const wm_bf
 WM_API int wkv_quantize(const wm_bf16 *x, int64_t rows, int D, int fmt, uint8_t *payload, void *scales,
                  wm_stream_t stream);
 
+/* The e4m3 KV row formats by block and scale format (the forms named for
+ * BASELINE config 5 and packed_cache.py 'fp8_ue8m0'): block 64 with one fp32
+ * scale = amax/448 (WKV_SCALE_F32; WKV_FP8_F32_B64), or block 32 with a ue8m0
+ * scale byte (WKV_SCALE_UE8M0; WKV_FP8_UE8M0_B32).  Other pairs return
+ * WM_ERR_UNSUPPORTED.  Same results as wkv_quantize / wkv_dequantize. */
+#define WKV_SCALE_F32 0
+#define WKV_SCALE_UE8M0 1
+WM_API int wkv_fp8_quantize(const wm_bf16 *x, int rows, int D, int block, int scale_fmt, uint8_t *payload,
+                            void *scales, wm_stream_t stream);
+WM_API int wkv_fp8_dequantize(const uint8_t *payload, const void *scales, int rows, int D, int block,
+                              int scale_fmt, wm_bf16 *out, wm_stream_t stream);
+
 /* Dequantize [rows, D] to bf16.  Replaces PackedRows.__getitem__
  * (packed_cache.py:47-59) and mx.dequantize in MXFP8PoolingCache._fetch
  * (fp8_cache.py:231-240). */

@@ -84,3 +84,12 @@ def test_workspace_size_is_pure_host():
 def test_call_raises_valueerror_on_invalid():
     with pytest.raises(ValueError, match="complete BF16 rows"):
         L.call("wmxfp4_quantize", None, 1, 33, None, None, None)
+
+
+def test_fp8_kv_entry_points_reject_other_formats():
+    # checked before any CUDA call: block 64 goes with fp32 scales, block 32 with ue8m0
+    for block, sf in ((32, 0), (64, 1), (16, 1)):
+        with pytest.raises(L.NativeError, match="fp8 KV"):
+            L.call("wkv_fp8_quantize", None, 4, 64, block, sf, None, None, None)
+        with pytest.raises(L.NativeError, match="fp8 KV"):
+            L.call("wkv_fp8_dequantize", None, None, 4, 64, block, sf, None, None)

@@ -130,3 +130,20 @@ def test_kv_bad_width_raises(dev):
     x = torch.zeros(4, 40, dtype=torch.bfloat16, device=dev)
     with pytest.raises(ValueError):
         W.kv_quantize(x, "fp8_ue8m0")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("block,sf,fmt", [(64, 0, "fp8_f32_b64"), (32, 1, "fp8_ue8m0")])
+def test_fp8_kv_named_entry_points(dev, block, sf, fmt):
+    # wkv_fp8_quantize / wkv_fp8_dequantize give the bytes and values of the generic calls
+    from whallm_b200 import _lib as C
+    x = torch.randn(300, 576 if block == 64 else 512, device=dev).to(torch.bfloat16)
+    p, s = W.kv_quantize(x, fmt)
+    p2, s2 = torch.empty_like(p), torch.empty_like(s)
+    rows, D = x.shape
+    C.call("wkv_fp8_quantize", C.ptr(x), rows, D, block, sf, C.ptr(p2), C.ptr(s2), C.stream_of(x))
+    out = torch.empty_like(x)
+    C.call("wkv_fp8_dequantize", C.ptr(p2), C.ptr(s2), rows, D, block, sf, C.ptr(out), C.stream_of(x))
+    torch.cuda.synchronize()
+    assert torch.equal(p, p2) and torch.equal(s, s2)
+    assert torch.equal(out, W.kv_dequantize(p, s, fmt))

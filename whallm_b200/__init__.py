@@ -18,5 +18,6 @@ from .router import Gate, qwen_route, route, stable_topk_indices, topk_scores  #
 
 from .linear import MXFP8Linear, expand_block_scales, mx_linear  # noqa: F401
 from .loader import load_expert_layer, load_installed_experts, read_layout  # noqa: F401
+from .kvcache import MXFP8PoolingCache, PackedRows, QSAQuantizedCache  # noqa: F401
 
 __version__ = "0.1.0"

@@ -56,6 +56,8 @@ SIGNATURES = {
     "wkv_affine_append": [_P, _P, _I64, _I64, _I, _I, _P, _P, _P, _P, _P, _P, _I64, _I64, _P],
     "wkv_affine_fetch": [_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _P, _P, _P],
     "wkv_quantize": [_P, _I64, _I, _I, _P, _P, _P],
+    "wkv_fp8_quantize": [_P, _I, _I, _I, _I, _P, _P, _P],
+    "wkv_fp8_dequantize": [_P, _P, _I, _I, _I, _I, _P, _P],
     "wkv_dequantize": [_P, _P, _I64, _I, _I, _P, _P],
     "wkv_gather_dequantize": [_P, _P, _I64, _P, _I64, _I, _I, _P, _P],
     "wmoe_router_topk": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P, _P, _P],

@@ -675,6 +675,30 @@ int wkv_quantize(const wm_bf16 *x, int64_t rows, int D, int fmt, uint8_t *payloa
   return wm::check_launch("wkv_quantize");
 }
 
+// e4m3 KV formats by (block, scale format): 64 values with an fp32 scale
+// (amax / 448), or 32 values with a ue8m0 byte.
+static int fp8_kv_format(int block, int scale_fmt) {
+  if (block == 64 && scale_fmt == WKV_SCALE_F32) return WKV_FP8_F32_B64;
+  if (block == 32 && scale_fmt == WKV_SCALE_UE8M0) return WKV_FP8_UE8M0_B32;
+  return -1;
+}
+
+int wkv_fp8_quantize(const wm_bf16 *x, int rows, int D, int block, int scale_fmt, uint8_t *payload, void *scales,
+                     wm_stream_t stream) {
+  wm::clear_error();
+  const int fmt = fp8_kv_format(block, scale_fmt);
+  if (fmt < 0) return wm::fail(WM_ERR_UNSUPPORTED, "fp8 KV: block 64 with fp32 scales or block 32 with ue8m0");
+  return wkv_quantize(x, rows, D, fmt, payload, scales, stream);
+}
+
+int wkv_fp8_dequantize(const uint8_t *payload, const void *scales, int rows, int D, int block, int scale_fmt,
+                       wm_bf16 *out, wm_stream_t stream) {
+  wm::clear_error();
+  const int fmt = fp8_kv_format(block, scale_fmt);
+  if (fmt < 0) return wm::fail(WM_ERR_UNSUPPORTED, "fp8 KV: block 64 with fp32 scales or block 32 with ue8m0");
+  return wkv_dequantize(payload, scales, rows, D, fmt, out, stream);
+}
+
 int wkv_dequantize(const uint8_t *payload, const void *scales, int64_t rows, int D, int fmt, wm_bf16 *out,
                    wm_stream_t stream) {
   wm::clear_error();

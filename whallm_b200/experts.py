@@ -7,6 +7,7 @@ Replaces the reference's SSD expert store and its MLX expert math:
     container of the tiny config;
   * ``ResidentExpertStore`` -- the provisioning interface the MoE layer uses
     (``current_batched`` expert_cache.py:990, ``get_many`` :1126,
+    ``iter_ready`` :1199, ``prefetch_layer`` :1003, ``batched_layer`` :1058,
     ``record_gather_qmm`` :828), backed by tensors that stay in HBM;
   * ``StreamingSwitchGLU`` -- ``_StreamingSwitchGLU`` (model.py:276-459):
     ``switch_mlp(x, indices) -> [..., k, H]``;
@@ -19,6 +20,7 @@ byte-identical to MLX's uint32 view) or int32 words (affine-4).
 from __future__ import annotations
 
 import threading
+from contextlib import contextmanager
 from dataclasses import dataclass, field
 
 import torch
@@ -127,6 +129,37 @@ class ResidentExpertStore:
     def record_gather_qmm(self, calls: int = 3) -> None:
         with self._lock:
             self.metrics.gather_qmm_calls += calls
+
+    def prefetch_layer(self, layer: int, experts=None) -> None:
+        """Nothing to read: every expert is resident (expert_cache.py:1003-1017
+        checks the same arguments before starting its reads)."""
+        if layer not in self._layers:
+            return
+        if experts is not None and not tuple(experts):
+            raise ValueError("batched expert prefetch cannot be empty")
+
+    @contextmanager
+    def batched_layer(self, layer: int, enabled: bool = True, experts=None):
+        """The layer's batched experts for the duration of the block, or None
+        when disabled (expert_cache.py:1058-1067)."""
+        if not enabled:
+            yield None
+            return
+        self.prefetch_layer(layer, experts)
+        yield self.current_batched(layer)
+
+    def iter_ready(self, layer: int, expert_ids: list):
+        """(expert, weights) for each distinct expert, in id order; all are
+        ready at once (expert_cache.py:1199-1213)."""
+        batched = self._layers.get(layer)
+        if batched is None:
+            raise ValueError(f"invalid layer {layer}")
+        unique = sorted(set(int(e) for e in expert_ids))
+        n = _expert_count(batched)
+        if any(not 0 <= e < n for e in unique):
+            raise ValueError("selected experts contain an invalid expert ID")
+        for e in unique:
+            yield e, _individual(batched, e)
 
     def get_many(self, layer: int, expert_ids: list) -> ResidentExperts:
         batched = self._layers.get(layer)
