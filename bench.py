@@ -466,15 +466,22 @@ def run_ep(args, rank, world, dev):
     # decode exchanges over peer memory (CUDA IPC + flags) unless WM_EP_EXCHANGE=nccl
     peer = decode and os.environ.get("WM_EP_EXCHANGE", "peer") != "nccl"
     n_layers = args.layers
+    # experts dealt to the ranks by popularity (the router's per-expert bias),
+    # unless WM_EP_PLACEMENT=contiguous
+    balanced = os.environ.get("WM_EP_PLACEMENT", "balanced") != "contiguous"
     moes = []
+    owned = []                                              # per layer: this rank's routed expert ids
     cfg = None
     bufs = None
     for i in range(n_layers):
         lay = S.make_layer(name, dev, seed=17 * i)          # identical weights on every rank
         cfg = lay.cfg
         E = cfg["E"]
-        local = EP.shard_experts(lay.experts, rank, world, E, cfg["shared"])
         e0, per = EP.shard_bounds(E, world, rank)
+        order = EP.balanced_placement(lay.logit_bias.exp(), world) if balanced and lay.logit_bias is not None else None
+        pos = EP.placement_positions(order, dev) if order is not None else None
+        owned.append(set(order[e0:e0 + per].tolist()) if order is not None else set(range(e0, e0 + per)))
+        local = EP.shard_experts(lay.experts, rank, world, E, cfg["shared"], order=order)
         limit = 10.0 if name == "ds" else 0.0
         if name == "ds":
             router = lay.layer.gate
@@ -493,14 +500,16 @@ def run_ep(args, rank, world, dev):
         if peer:
             if bufs is None:
                 bufs = EP.PeerBuffers(max(batches), cfg["H"], cfg["k"], device=dev)
-            moes.append([EP.PeerGatheredMoE(router, local, E, B, bufs, limit, cfg["shared"], shared_gated=name != "ds")
+            moes.append([EP.PeerGatheredMoE(router, local, E, B, bufs, limit, cfg["shared"], shared_gated=name != "ds",
+                                            positions=pos)
                          for B in batches])
         elif decode:
             moes.append(EP.GatheredExpertParallelMoE(
-                router, EP.gpu_partial_experts(local, e0, per, E, limit, cfg["shared"]), E))
+                router, EP.gpu_partial_experts(local, e0, per, E, limit, cfg["shared"], positions=pos), E))
         else:
             moes.append(EP.ExpertParallelMoE(router, EP.gpu_local_experts(local, limit), E,
-                                             shared=EP.gpu_shared_expert(local, per, limit, gate=gate_fn)))
+                                             shared=EP.gpu_shared_expert(local, per, limit, gate=gate_fn),
+                                             positions=pos))
         if not peer:
             moes[-1].route_fn = router
         del lay
@@ -513,14 +522,14 @@ def run_ep(args, rank, world, dev):
     # over all ranks' tokens, plus the shared expert, plus activations
     expert_bytes = DS_EXPERT_BYTES if name == "ds" else QN_EXPERT_BYTES
     distinct = [0.0] * len(xs)
-    for m in moes:
+    for m, mine in zip(moes, owned):
         for b, x in enumerate(xs):
             route_fn = m[b].router if isinstance(m, list) else m.route_fn
             idx = route_fn(x)[1].to(torch.int32).contiguous()
             allidx = torch.empty((world * idx.shape[0], idx.shape[1]), dtype=idx.dtype, device=dev)
             torch.distributed.all_gather_into_tensor(allidx, idx)
             ids = set(allidx.flatten().tolist())
-            distinct[b] += (sum(1 for e in ids if e0 <= e < e0 + per) + (1 if cfg["shared"] else 0)) / n_layers
+            distinct[b] += (len(ids & mine) + (1 if cfg["shared"] else 0)) / n_layers
     act_bytes = sum(world * B * H * (2 + 4 + 4) for B in batches) if decode else 0
     alg_bytes = sum(distinct) * expert_bytes + act_bytes
 
@@ -576,6 +585,7 @@ def run_ep(args, rank, world, dev):
     return dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=alg_bytes, per_b={}, clocks=clocks,
                 h2d=h2d, d2h=h2d, cfg=cfg, batches=batches, distinct=distinct, hbm=hbm, peak_src=peak_src,
                 launches=len(xs) * ((11 if peer else 7) if decode else 9), flops=0, ep=True, decode=decode,
+                placement="popularity-balanced (snake order by router bias)" if balanced else "contiguous",
                 launch=("CUDA graph per (layer, batch): peer-memory exchange (CUDA IPC, flags), partial experts"
                         if peer else "CUDA graph per (layer, batch): NCCL all-gather, partial experts, "
                         "reduce-scatter") if decode else "eager (NCCL all-to-all)")
@@ -789,6 +799,7 @@ def main():
                 "config": {"workload": args.workload, "batches": list(r["batches"]), "tokens_per_rank": r["tokens"],
                            "layers_cycled": args.layers, "parallelism": f"ep{world}",
                            "experts_per_rank": r["cfg"]["E"] // world,
+                           "placement": r.get("placement", "contiguous"),
                            "launch": r.get("launch", "eager (NCCL all-to-all)")},
                 "e2e": {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2), "unit": unit,
                         "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},

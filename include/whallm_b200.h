@@ -319,14 +319,19 @@ WM_API int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const fl
  * The weight tensors hold E_local experts: the rank's route_count routed
  * experts, then (optionally) the shared expert at index shared_expert.  Ids in
  * [0, n_routed) owned by other ranks are skipped; ids outside [0, n_routed)
- * set the error path (zeros).  Summing `out` over the ranks (a reduce-scatter
+ * set the error path (zeros).  `placement` (NULL, or int32 [n_routed] holding
+ * a permutation of [0, n_routed)) moves routed id e to position
+ * placement[e]: the rank then owns the ids whose positions lie in
+ * [route_base, route_base + route_count), local expert = position -
+ * route_base -- a popularity-balanced assignment of experts to ranks with the
+ * router's ids unchanged.  Summing `out` over the ranks (a reduce-scatter
  * over the token blocks) gives the layer output.  The reference has no
  * multi-device MoE (_streaming_moe raises on a sharding group,
  * model.py:485-486); this is the sharded form of the same layer.  Workspace:
  * wmoe_workspace_size(T, k, H, I, E_local, shared_expert >= 0). */
 WM_API int wmoe_mxfp4_moe_forward_ep(const wm_bf16 *x, const int32_t *idx, const float *weights, int T, int k,
                               int H, int I, int E_local, int n_routed, int route_base, int route_count,
-                              const uint8_t *w13, const uint8_t *s13, const uint8_t *w2, const uint8_t *s2,
+                              const int32_t *placement, const uint8_t *w13, const uint8_t *s13, const uint8_t *w2, const uint8_t *s2,
                               int gate_up_order, float swiglu_limit, int shared_expert, const float *shared_w,
                               int shared_lo, int shared_hi, float *out, void *workspace, size_t ws_bytes,
                               wm_stream_t stream);

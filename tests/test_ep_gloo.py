@@ -99,6 +99,52 @@ def _worker(rank, world, port, result_q):
         dist.destroy_process_group()
 
 
+def _placed_worker(rank, world, port, result_q):
+    """The all-to-all layer with a popularity-balanced placement: experts move
+    between ranks, the layer output must not change."""
+    import sys
+    sys.path.insert(0, ROOT)
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        from oracle import formats as F
+        from oracle import moe as M
+        from oracle import router as R
+        from whallm_b200.ep import ExpertParallelMoE, balanced_placement, placement_positions, shard_bounds
+        ex, wg, c = _layer()
+        E, H, k = c["E"], c["H"], c["k"]
+        T = 9 + 3 * rank
+        x = _tokens(rank, T, H)
+        order = balanced_placement(np.arange(E, 0, -1) ** 2.0, world)   # skewed load: expert 0 hottest
+        pos = placement_positions(order)
+
+        def router(xt):
+            xb = F.f32_to_bf16_bits(xt.float().numpy())
+            _, idx, w, _ = R.route(xb, wg, k, R.SCORE_SQRTSOFTPLUS, norm_eps=1e-20, route_scale=1.5)
+            return torch.from_numpy(w), torch.from_numpy(idx)
+
+        e0, per = shard_bounds(E, world, rank)
+        mine = [int(e) for e in order[e0:e0 + per]]
+
+        def local(rows, ids):
+            rows_np = rows.float().numpy()
+            out = np.zeros_like(rows_np)
+            for le in np.unique(ids.numpy()):
+                sel = np.flatnonzero(ids.numpy() == le)
+                out[sel] = ex.ffn(mine[int(le)], rows_np[sel])
+            return torch.from_numpy(F.round_bf16(out)).to(torch.bfloat16)
+
+        moe = ExpertParallelMoE(router, local, E, shared=lambda xt: torch.from_numpy(ex.ffn(E, xt.float().numpy())),
+                                positions=pos)
+        got = moe(torch.from_numpy(x).to(torch.bfloat16)).float().numpy()
+        _, idx, w, _ = R.route(F.f32_to_bf16_bits(x), wg, k, R.SCORE_SQRTSOFTPLUS, norm_eps=1e-20, route_scale=1.5)
+        ref = M.moe_forward(x, idx, w, ex, shared_expert=E)
+        result_q.put((rank, M.max_rel_err(got, ref), sorted(mine), 0))
+    finally:
+        dist.destroy_process_group()
+
+
 def _gathered_worker(rank, world, port, result_q):
     """Decode form: all-gather tokens + routes, partial sums, reduce-scatter."""
     import sys
@@ -193,6 +239,33 @@ def test_gathered_ep_matches_single_process_layer():
     for rank, err, hi, lo in res:
         assert err < 2e-2, (rank, err)
         assert 0 <= lo <= hi < 8
+
+
+def test_ep_exchange_with_balanced_placement():
+    res = _spawn(_placed_worker)
+    assert sorted(res[0][2] + res[1][2]) == list(range(8))      # every expert on exactly one rank
+    for rank, err, _, _ in res:
+        assert err < 2e-2, (rank, err)
+
+
+def test_balanced_placement_properties():
+    from whallm_b200.ep import balanced_placement, placement_positions
+    rng = np.random.default_rng(0)
+    for E, W in ((256, 8), (512, 8), (16, 4), (8, 2)):
+        load = rng.zipf(1.5, E).astype(np.float64)
+        order = balanced_placement(load, W)
+        assert sorted(order.tolist()) == list(range(E))
+        per = order.view(W, E // W)
+        shares = np.array([load[r.numpy()].sum() for r in per])
+        contiguous = load.reshape(W, -1).sum(1)
+        assert shares.max() <= contiguous.max() + 1e-9          # never worse than contiguous ranges
+        assert all(list(r) == sorted(r.tolist()) for r in per)   # each rank's experts in id order
+        pos = placement_positions(order)
+        assert torch.equal(order[pos.long()], torch.arange(E))
+    with pytest.raises(ValueError, match="evenly"):
+        balanced_placement(np.ones(10), 4)
+    with pytest.raises(ValueError, match="permutation"):
+        placement_positions(torch.tensor([0, 0, 1, 2]))
 
 
 def test_rank_leaving_surfaces_as_collective_error():

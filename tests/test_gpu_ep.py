@@ -34,8 +34,9 @@ def _free_port():
     return p
 
 
-def _partials(lay, x, world, idx=None, w=None):
-    """Sum over emulated ranks of the f32 partial outputs, bf16-rounded."""
+def _partials(lay, x, world, idx=None, w=None, order=None):
+    """Sum over emulated ranks of the f32 partial outputs, bf16-rounded
+    (``order``: a placement order of the routed experts)."""
     from whallm_b200 import ep as EP
     from whallm_b200 import experts as X
     E = lay.cfg["E"]
@@ -43,13 +44,14 @@ def _partials(lay, x, world, idx=None, w=None):
     if idx is None:
         w, idx = lay.layer.gate(x)
     B = T // world
+    pos = EP.placement_positions(order, x.device) if order is not None else None
     acc = torch.zeros((T, x.shape[1]), dtype=torch.float32, device=x.device)
     for r in range(world):
         e0, per = EP.shard_bounds(E, world, r)
-        local = EP.shard_experts(lay.experts, r, world, E, True)
+        local = EP.shard_experts(lay.experts, r, world, E, True, order=order)
         rows = (r * B, T if r == world - 1 else (r + 1) * B)
         acc += X.experts_forward(x, idx, local, weights=w, shared_expert=per, swiglu_limit=10.0,
-                                 expert_range=(e0, per, E), shared_rows=rows)
+                                 expert_range=(e0, per, E), shared_rows=rows, placement=pos)
     return acc.to(torch.bfloat16), w, idx
 
 
@@ -68,6 +70,25 @@ def test_partial_sums_over_ranks_equal_full_layer(dev, world, T, H, I):
                                                      lay.experts.w2_scales)), M.UP_GATE, 10.0)
     ref = M.moe_forward(x.float().cpu().numpy(), idx.cpu().numpy(), w.cpu().numpy(), ex, shared_expert=16)
     assert M.max_rel_err(got.float().cpu().numpy(), ref) < 2e-2
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_partial_sums_with_balanced_placement(dev, world):
+    # the same layer with experts dealt to ranks by popularity: the rank sum is unchanged
+    import sys
+    sys.path.insert(0, ROOT)
+    from oracle import moe as M
+    from whallm_b200 import ep as EP
+    from whallm_b200 import synthetic as S
+    lay = S.make_layer("ds", dev, seed=31 + world, E=16, H=512, I=256)
+    x = S.make_tokens(24, 512, 90 + world, dev)
+    order = EP.balanced_placement(lay.logit_bias.exp(), world)
+    assert not torch.equal(order, torch.arange(16))               # experts really move
+    got, w, idx = _partials(lay, x, world, order=order)
+    plain, _, _ = _partials(lay, x, world, idx=idx, w=w)
+    full = lay.layer(x)
+    assert M.max_rel_err(got.float().cpu().numpy(), full.float().cpu().numpy()) < 1e-2
+    assert M.max_rel_err(got.float().cpu().numpy(), plain.float().cpu().numpy()) < 1e-2
 
 
 def test_partial_rank_without_assignments_and_bad_ids(dev):

@@ -430,7 +430,8 @@ int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const float *we
 }
 
 int wmoe_mxfp4_moe_forward_ep(const wm_bf16 *x, const int32_t *idx, const float *weights, int T, int k, int H, int I,
-                              int E_local, int n_routed, int route_base, int route_count, const uint8_t *w13,
+                              int E_local, int n_routed, int route_base, int route_count, const int32_t *placement,
+                              const uint8_t *w13,
                               const uint8_t *s13, const uint8_t *w2, const uint8_t *s2, int gate_up_order,
                               float swiglu_limit, int shared_expert, const float *shared_w, int shared_lo,
                               int shared_hi, float *out, void *workspace, size_t ws_bytes, wm_stream_t stream) {
@@ -443,7 +444,7 @@ int wmoe_mxfp4_moe_forward_ep(const wm_bf16 *x, const int32_t *idx, const float 
   WM_REQUIRE(out != nullptr, "moe_forward_ep: null output");
   Args a{x, idx, weights, T, k, H, I, E_local, mx_view(w13, s13, 2 * I, H), mx_view(w2, s2, H, I), gate_up_order,
          swiglu_limit, shared_expert, shared_w, nullptr, true, workspace, ws_bytes, stream};
-  a.rf = wm::RouteFilter{route_base, route_count, n_routed, shared_lo, shared_hi};
+  a.rf = wm::RouteFilter{route_base, route_count, n_routed, shared_lo, shared_hi, placement};
   a.out_f32 = out;
   return run(a, kFmtMxfp4);
 }

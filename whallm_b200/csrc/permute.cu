@@ -45,9 +45,10 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
   const int s0 = warp * seg, s1 = min(S, s0 + seg);
   // expert of assignment a, kBad for an id outside the layer's experts.  With
   // a route filter (rf.count > 0, an expert-parallel rank's share) routed ids
-  // in [rf.base, rf.base + rf.count) are kept as id - rf.base; other ids in
-  // [0, rf.n_global), and shared slots of tokens outside
-  // [rf.shared_lo, rf.shared_hi), are kDropped.
+  // whose placement position (rf.remap[id], or id) lies in [rf.base, rf.base +
+  // rf.count) are kept as position - rf.base; other ids in [0, rf.n_global),
+  // and shared slots of tokens outside [rf.shared_lo, rf.shared_hi), are
+  // kDropped.
   constexpr int kBad = -1, kDropped = -2;
   auto expert_of = [&](int a) -> int {
     int t = a / kk, j = a - t * kk;
@@ -55,6 +56,7 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
     int e = idx[static_cast<int64_t>(t) * k + j];
     if (rf.count > 0) {
       if (e < 0 || e >= rf.n_global) return kBad;
+      if (rf.remap) e = rf.remap[e];                 // placement position (any value outside the range is dropped)
       return (e >= rf.base && e < rf.base + rf.count) ? e - rf.base : kDropped;
     }
     return (e < 0 || e >= E) ? kBad : e;

@@ -14,6 +14,9 @@ namespace wm {
 // slot.  count == 0 means no filter (the whole layer on one device).
 struct RouteFilter {
   int base = 0, count = 0, n_global = 0, shared_lo = 0, shared_hi = 0;
+  // expert placement: routed id e belongs to position remap[e] of the ranks'
+  // contiguous ranges (nullptr: position e)
+  const int32_t *remap = nullptr;
 };
 
 // permute.cu.  With tiles != nullptr it also emits the tensor-core work list:

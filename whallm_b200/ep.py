@@ -52,10 +52,44 @@ def shard_bounds(n_routed: int, world: int, rank: int):
     return rank * per, per
 
 
-def plan_dispatch(idx: torch.Tensor, n_routed: int, world: int, group=None) -> EPPlan:
-    """Destination ranks of each (token, slot), stable order and split sizes."""
+def balanced_placement(load, world: int) -> torch.Tensor:
+    """Order of the routed experts for sharding: rank r owns
+    ``order[r*c:(r+1)*c]`` (c = E / world).  The experts are dealt to the ranks
+    hottest first in snake order (0..W-1, W-1..0, ...), so every rank holds c
+    experts and about the same share of the expected load ``load`` (e.g. the
+    routing popularity: exp of the router's per-expert logit bias, or counts
+    from a calibration pass).  Ties go to the lower id; each rank's experts
+    are kept in id order.  int64 [E] on the CPU."""
+    load = torch.as_tensor(load, dtype=torch.float64).detach().cpu().reshape(-1)
+    E = load.numel()
+    if E % world:
+        raise ValueError(f"{E} experts do not shard evenly over {world} ranks")
+    hot = torch.argsort(-load, stable=True).tolist()
+    ranks = [[] for _ in range(world)]
+    for i, e in enumerate(hot):
+        r = i % (2 * world)
+        ranks[r if r < world else 2 * world - 1 - r].append(e)
+    return torch.tensor([e for r in ranks for e in sorted(r)], dtype=torch.int64)
+
+
+def placement_positions(order: torch.Tensor, device=None) -> torch.Tensor:
+    """Inverse of a placement order: position[e] = j where order[j] = e (int32)."""
+    order = torch.as_tensor(order, dtype=torch.int64).cpu()
+    pos = torch.empty_like(order)
+    pos[order] = torch.arange(order.numel(), dtype=torch.int64)
+    if sorted(order.tolist()) != list(range(order.numel())):
+        raise ValueError("placement order must be a permutation of the routed experts")
+    return pos.to(torch.int32).to(device) if device is not None else pos.to(torch.int32)
+
+
+def plan_dispatch(idx: torch.Tensor, n_routed: int, world: int, group=None, positions=None) -> EPPlan:
+    """Destination ranks of each (token, slot), stable order and split sizes.
+    ``positions`` (device int32 [n_routed], ``placement_positions``) places
+    expert e at position positions[e] of the ranks' contiguous ranges."""
     per = n_routed // world
     flat = idx.reshape(-1).to(torch.int64)
+    if positions is not None:
+        flat = positions.to(torch.int64)[flat]
     dest = flat // per
     order = torch.sort(dest, stable=True).indices
     send = torch.bincount(dest, minlength=world).to(torch.int64)
@@ -80,12 +114,13 @@ class ExpertParallelMoE:
     runs this rank's experts, one assignment per row (see ``gpu_local_experts``);
     ``shared(x) -> f32 [T, H]`` (optional) is the replicated shared expert."""
 
-    def __init__(self, router, local_experts, n_routed: int, shared=None, group=None):
+    def __init__(self, router, local_experts, n_routed: int, shared=None, group=None, positions=None):
         self.router = router
         self.local_experts = local_experts
         self.n_routed = n_routed
         self.shared = shared
         self.group = group
+        self.positions = positions          # placement_positions(order) on the device, or None
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.e0, self.per = shard_bounds(n_routed, self.world, self.rank)
@@ -94,10 +129,13 @@ class ExpertParallelMoE:
         T, H = x.shape
         w, idx = self.router(x)
         k = idx.shape[-1]
-        plan = plan_dispatch(idx, self.n_routed, self.world, self.group)
+        plan = plan_dispatch(idx, self.n_routed, self.world, self.group, self.positions)
         src_tok = plan.order // k
         rows = x.index_select(0, src_tok)
-        ids = (idx.reshape(-1).to(torch.int64).index_select(0, plan.order) % self.per).to(torch.int32)
+        gid = idx.reshape(-1).to(torch.int64)
+        if self.positions is not None:
+            gid = self.positions.to(torch.int64)[gid]
+        ids = (gid.index_select(0, plan.order) % self.per).to(torch.int32)
         recv_rows = exchange(rows, plan.send_counts, plan.recv_counts, self.group)
         recv_ids = exchange(ids, plan.send_counts, plan.recv_counts, self.group)
         y = self.local_experts(recv_rows, recv_ids) if recv_rows.shape[0] else recv_rows.new_empty((0, H))
@@ -289,8 +327,9 @@ class PeerGatheredMoE:
     calls with the same B in the same order."""
 
     def __init__(self, router, experts, n_routed: int, B: int, bufs: PeerBuffers, swiglu_limit: float = 0.0,
-                 has_shared: bool = True, shared_gated: bool = False):
+                 has_shared: bool = True, shared_gated: bool = False, positions=None):
         self.router = router
+        self.positions = positions          # placement_positions(order) on the device, or None
         self.experts = experts
         self.n_routed = n_routed
         self.B = B
@@ -324,7 +363,7 @@ class PeerGatheredMoE:
         X.experts_forward(self.rx_x, self.rx_idx, self.experts, weights=self.rx_w,
                           shared_expert=self.per if self.has_shared else -1,
                           shared_w=self.rx_sw if sw is not None else None, swiglu_limit=self.limit,
-                          expert_range=(self.e0, self.per, self.n_routed),
+                          expert_range=(self.e0, self.per, self.n_routed), placement=self.positions,
                           shared_rows=(bufs.rank * B, (bufs.rank + 1) * B), out=self.part)
         bufs.put(1, [(self.part.data_ptr(), 4 * H, B * 4 * H, lay["ret"])], B, stream)
         L.call("wep_sum_rows", L.ptr(self.ret), bufs.world, B, H, ctypes_ptr(bufs.err_ptr), L.ptr(self.out), stream)
@@ -337,15 +376,16 @@ def ctypes_ptr(v: int):
 
 
 def gpu_partial_experts(experts, e0: int, per: int, n_routed: int, swiglu_limit: float = 0.0,
-                        has_shared: bool = True):
+                        has_shared: bool = True, positions=None):
     """This rank's share on the device: ``experts`` from ``shard_experts``
-    (routed [e0, e0+per) as 0..per-1, then the shared expert)."""
+    (the routed experts at placement positions [e0, e0+per) as 0..per-1, then
+    the shared expert)."""
     from . import experts as X
 
     def run(xg, idxg, wg, swg, rows):
         return X.experts_forward(xg, idxg, experts, weights=wg, shared_expert=per if has_shared else -1,
                                  shared_w=swg, swiglu_limit=swiglu_limit, expert_range=(e0, per, n_routed),
-                                 shared_rows=rows)
+                                 shared_rows=rows, placement=positions)
     return run
 
 
@@ -373,12 +413,14 @@ def gpu_shared_expert(experts, shared_index: int, swiglu_limit: float = 0.0, gat
     return run
 
 
-def shard_experts(batched, rank: int, world: int, n_routed: int, has_shared: bool = True):
+def shard_experts(batched, rank: int, world: int, n_routed: int, has_shared: bool = True, order=None):
     """Slice a full BatchedExperts / QwenBatchedExperts into this rank's routed
-    experts plus the shared expert (kept as the last local expert)."""
+    experts (``order[e0:e0+per]`` with a placement order, else [e0, e0+per))
+    plus the shared expert (kept as the last local expert)."""
     from . import experts as X
     e0, per = shard_bounds(n_routed, world, rank)
-    sel = list(range(e0, e0 + per)) + ([n_routed] if has_shared else [])
+    routed = list(range(e0, e0 + per)) if order is None else [int(e) for e in order[e0:e0 + per]]
+    sel = routed + ([n_routed] if has_shared else [])
     ix = torch.tensor(sel, device=(batched.gate_up if isinstance(batched, X.QwenBatchedExperts) else batched.w2).device)
     if isinstance(batched, X.QwenBatchedExperts):
         return X.QwenBatchedExperts(*(t.index_select(0, ix).contiguous()

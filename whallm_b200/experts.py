@@ -239,7 +239,7 @@ def _mx_args(w13, s13, w2, s2):
 
 def experts_forward(x, indices, experts, *, order=None, swiglu_limit: float = 0.0, weights=None,
                     shared_expert: int = -1, shared_w=None, out=None, workspace=None, expert_range=None,
-                    shared_rows=None):
+                    shared_rows=None, placement=None):
     """Grouped expert FFN on the device.
 
     ``weights is None``  -> un-reduced [..., k, H] (switch_mlp semantics);
@@ -251,7 +251,10 @@ def experts_forward(x, indices, experts, *, order=None, swiglu_limit: float = 0.
     [base, base+count) as local 0..count-1 (then the shared expert), other
     global ids are skipped, the shared expert runs only for rows in
     ``shared_rows=(lo, hi)`` (default all), and the result is the float32
-    partial sum [..., H] that a reduce over the ranks completes.
+    partial sum [..., H] that a reduce over the ranks completes.  With
+    ``placement`` (int32 [n_routed] on the device, a permutation) the rank
+    owns the routed ids whose placement positions lie in [base, base+count)
+    instead (``ep.balanced_placement``).
     """
     if x.dtype != torch.bfloat16:
         raise ValueError("expert input must be bf16")
@@ -296,9 +299,11 @@ def experts_forward(x, indices, experts, *, order=None, swiglu_limit: float = 0.
         lo, hi = (0, T) if shared_rows is None else (int(shared_rows[0]), int(shared_rows[1]))
         if out is None:
             out = torch.empty((T, H), dtype=torch.float32, device=dev)
-        L.require_cuda(xf, idx, w13, s13, w2, s2, out, wts, sw)
+        if placement is not None and (placement.dtype != torch.int32 or placement.numel() != n_routed):
+            raise ValueError("placement must be int32 [n_routed]")
+        L.require_cuda(xf, idx, w13, s13, w2, s2, out, wts, sw, placement)
         L.call("wmoe_mxfp4_moe_forward_ep", L.ptr(xf), L.ptr(idx), L.ptr(wts), T, k, H, I, E, n_routed, base, count,
-               L.ptr(w13), L.ptr(s13), L.ptr(w2), L.ptr(s2), order, float(swiglu_limit),
+               L.ptr(placement), L.ptr(w13), L.ptr(s13), L.ptr(w2), L.ptr(s2), order, float(swiglu_limit),
                shared_expert if has_shared else -1, L.ptr(sw), lo, hi, L.ptr(out), L.ptr(ws), ws.numel(), st)
         return out.reshape(*x.shape[:-1], H)
     if out is None:
