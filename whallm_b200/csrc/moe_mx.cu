@@ -32,8 +32,8 @@
 // writes its two e4m3 terms and scales, the down projection's token operand,
 // directly; the prefill configuration writes bf16 h for a split kernel.
 //
-// Warp roles (384 threads, one CTA per SM, persistent over (tile, 128-row)
-// work items):
+// Warp roles (384 threads for decode, 768 for prefill; one CTA per SM,
+// persistent over (tile, 128-row) work items):
 //   warp 0      TMA producer (weights, token terms)
 //   warp 1      MMA issuer: tcgen05.cp of the stage's scale factors into
 //               TMEM, then KC/32 MMAs (the copies and the MMAs of one thread
@@ -43,7 +43,9 @@
 //               memory a chunk (up to 32 bytes per row) ahead and write each
 //               stage's bytes in the 32 x 16-byte layout that
 //               tcgen05.cp.32x128b.warpx4 takes
-//   warps 8-11  epilogue (TMEM lanes 0-127)
+//   warps 8-11  epilogue (TMEM lanes 0-127); prefill adds warps 12-23, four
+//               epilogue groups in all, taking a work item's 16-token chunks
+//               in turn
 // Every mbarrier wait is bounded and records an error code instead of hanging.
 #include "wm_common.cuh"
 #include "wm_moe.cuh"
@@ -55,12 +57,17 @@ using namespace wm_tc;
 
 constexpr int kM = 128;
 constexpr int kKH = 128;                 // K values per TMA box row and per scale-factor group
-constexpr int kMxThreads = 384;
 constexpr int kLoShift = 5;              // lo term scale = hi scale * 2^-5
 constexpr uint32_t kLoSub = 0x01010101u * kLoShift;   // E8M0 bytes of the lo term, four at a time
 
-template <int KC, int NMAX, int STAGES, bool FUSE_SPLIT>
+template <int KC, int NMAX, int STAGES, bool FUSE_SPLIT, int EPI = 1>
 struct MxCfg {
+  // EPI: epilogue warp groups (4 warps each, one per TMEM lane quadrant);
+  // the groups take 16-token chunks of a work item in turn, for short-K items
+  // whose epilogue would otherwise outlast their mainloop (prefill: 4 groups,
+  // 768 threads; Qwen-class prefill 2.86M -> 3.53M tok/s).
+  static constexpr int kEpi = EPI;
+  static constexpr int kThreads = 256 + 128 * EPI;
   // FUSE_SPLIT: the up projection's epilogue writes the e4m3 terms of h
   // (decode: at most two 16-column chunks per item, hidden behind the
   // mainloop); otherwise it writes bf16 h and a split kernel follows.
@@ -89,9 +96,11 @@ struct MxCfg {
   static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
   static_assert(kSmem <= 232448, "shared memory");
   static_assert(kColsUsed <= 512, "TMEM columns");
+  static_assert(EPI >= 1 && EPI <= 4 && (EPI == 1 || !FUSE_SPLIT),
+                "1-4 epilogue groups; the fused split's column-max exchange is one warp group's");
 };
 using MxDecode = MxCfg<256, 32, 4, true>;
-using MxPrefill = MxCfg<128, 112, 4, false>;
+using MxPrefill = MxCfg<128, 112, 4, false, 4>;
 
 struct MxParams {
   int mode;                  // 0: up projection (+ClampedSwiGLU -> h bf16), 1: down projection (-> y f32)
@@ -191,7 +200,7 @@ struct TileCursor {
 };
 
 template <class C>
-__global__ void __launch_bounds__(kMxThreads, 1)
+__global__ void __launch_bounds__(C::kThreads, 1)
     k_expert_mx(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
                 const __grid_constant__ CUtensorMap tmBl, MxParams p) {
   constexpr int S = C::kStages;
@@ -212,7 +221,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128 * C::kEpi); }
     for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 64);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -424,7 +433,8 @@ __global__ void __launch_bounds__(kMxThreads, 1)
     }
   } else if (warp >= 8) {
     // ---------------------------------------------------------- epilogue
-    const int t = threadIdx.x - 256;                    // TMEM lane = tile row
+    const int t = (threadIdx.x - 256) & 127;            // TMEM lane = tile row
+    const int grp = (threadIdx.x - 256) >> 7;           // epilogue group: chunks grp, grp + kEpi, ...
     const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
     const int up_half = p.order == WM_UP_GATE ? 0 : 1;
     const bool is_up = ((t >> 3) & 1) == up_half;
@@ -441,7 +451,7 @@ __global__ void __launch_bounds__(kMxThreads, 1)
       tc_fence_after();
       const int n = tile.z;
       const int n16 = max(16, (n + 15) & ~15);
-      for (int c0 = 0; c0 < n; c0 += 16) {
+      for (int c0 = 16 * grp; c0 < n; c0 += 16 * C::kEpi) {
         uint32_t r[16], rl[16];
         WM_TMEM_LD16(tmem + lane_base + db * C::kDCols + c0, r);
         WM_TMEM_LD16(tmem + lane_base + db * C::kDCols + n16 + c0, rl);
@@ -676,7 +686,7 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.h_out = h_out;
   p.y_out = y_out;
   p.err = err;
-  if (cudaError_t e = wm::launch_pdl(k_expert_mx<C>, dim3(wm::sm_count()), dim3(kMxThreads), C::kSmem, stream, tmA,
+  if (cudaError_t e = wm::launch_pdl(k_expert_mx<C>, dim3(wm::sm_count()), dim3(C::kThreads), C::kSmem, stream, tmA,
                                      tmBh, tmBl, p))
     return wm::fail(WM_ERR_CUDA, std::string("expert mx: ") + cudaGetErrorString(e));
   return wm::check_launch("expert mx");
