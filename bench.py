@@ -31,10 +31,13 @@ oracle port; the MLX CPU backend the reference would use is not installable
 here) on the same workload and prints the same JSON line with "impl".
 
 Multi-GPU (torchrun): the MoE workloads run expert-parallel (`whallm_b200.ep`):
-each rank routes its own tokens (weak scaling), the routed experts are sharded
-evenly over the ranks, token rows go to the owning rank and back through NCCL
-all-to-all, the shared expert is replicated; value = all ranks' tokens / max
-rank time.  Other workloads run as independent replicas.
+each rank routes its own tokens (weak scaling); the routed experts are dealt to
+the ranks by popularity, equal counts per rank (WM_EP_PLACEMENT=contiguous for
+plain ranges); decode gathers every rank's tokens and returns partial sums over
+peer memory (WM_EP_EXCHANGE=nccl for NCCL collectives), prefill moves token rows
+to the owning rank and back through NCCL all-to-all; the shared expert is
+replicated; value = all ranks' tokens / max rank time.  Other workloads run as
+independent replicas.
 """
 from __future__ import annotations
 
@@ -270,7 +273,7 @@ def run_ours(args, rank, world, dev):
             lay = layers[i % n_layers]
             for b in range(len(xs)):
                 if graphed:
-                    y = caps[i % n_layers][b](hx[b].to(dev, non_blocking=True))
+                    y = caps[i % n_layers][b](hx[b])     # one H2D straight into the graph's input
                 else:
                     y = lay.layer(hx[b].to(dev, non_blocking=True))
                 houts[b].copy_(y, non_blocking=True)
@@ -570,7 +573,8 @@ def run_ep(args, rank, world, dev):
     s4.record()
     for i in range(args.steps):
         for b in range(len(xs)):
-            houts[b].copy_(call(i % n_layers, b, hx[b].to(dev, non_blocking=True)), non_blocking=True)
+            houts[b].copy_(call(i % n_layers, b, hx[b] if decode else hx[b].to(dev, non_blocking=True)),
+                           non_blocking=True)
     e4.record()
     torch.cuda.synchronize()
     ms_e2e = s4.elapsed_time(e4) / args.steps
