@@ -24,7 +24,8 @@ Other workloads: --workload ds_prefill (4096 tokens), qn_decode (B 1 and 32),
 qn_prefill (16384 tokens), tiny (64 tokens, affine-4), kv (FP8 KV quantize +
 dequantize of 32768 x 8 x 61 rows of 576), kv_scores (MXFP8 cache scores),
 qsa (Qwen QSA affine KV caches: one decode update_and_fetch of 8 sequences at
-a 32768-token context over the 12 full-attention layers).
+a 32768-token context over the 12 full-attention layers), linear (dense MXFP8
+linear, K = N = 5120: decode rows 1, 4, 16; 4096 in the breakdown).
 
 `--impl reference` times the reference's algorithm on the host cores (the
 oracle port; the MLX CPU backend the reference would use is not installable
@@ -420,6 +421,93 @@ def run_ours(args, rank, world, dev):
                                       "written per step: larger than L2",
                                 "launch": "eager"}))
         return res
+    if wl == "linear":
+        # dense MXFP8 linear (the QuantizedLinear layers V4.1 builds from its
+        # native-FP8 attention and shared-expert weights): K 5120 -> N 5120;
+        # one step = the decode rows T = 1, 4, 16, each call on another of 8
+        # weight matrices (210 MB: weights come from HBM); T = 4096 is reported
+        # in the breakdown against the tensor peak
+        K = N = 5120
+        sweep = (1, 4, 16)
+        mats = []
+        for li in range(8):
+            g = torch.Generator(device=dev).manual_seed(li)
+            w = torch.randn((N, K), generator=g, device=dev).mul_(0.02).to(torch.bfloat16)
+            mats.append(W.MXFP8Linear.quantize(w))
+            del w
+        xs_l = [S.make_tokens(T, K, 7 + T, dev) for T in sweep]
+        outs = [torch.empty((T, N), dtype=torch.bfloat16, device=dev) for T in sweep]
+
+        def lstep(i):
+            for j, x in enumerate(xs_l):
+                m = mats[(3 * i + j) % 8]
+                W.mx_linear(x, m.weight, m.scales, "mxfp8", out=outs[j])
+
+        for i in range(args.warmup):
+            lstep(i)
+        torch.cuda.synchronize()
+        clk = ClockSampler(dev.index if dev.index is not None else 0)
+        clk.start()
+        s, e = _events(torch)
+        s.record()
+        for i in range(args.steps):
+            lstep(i)
+        e.record()
+        torch.cuda.synchronize()
+        clocks = clk.stop()
+        ms = s.elapsed_time(e) / args.steps
+        wbytes = N * K + N * (K // 32)
+        alg = sum(wbytes + T * K * 2 + T * N * 2 for T in sweep)
+        per_b = {}
+        for j, T in enumerate(sweep):
+            torch.cuda.synchronize()
+            s3, e3 = _events(torch)
+            s3.record()
+            for i in range(32):
+                m = mats[i % 8]
+                W.mx_linear(xs_l[j], m.weight, m.scales, "mxfp8", out=outs[j])
+            e3.record()
+            torch.cuda.synchronize()
+            t_ms = s3.elapsed_time(e3) / 32
+            per_b[str(T)] = {"ms": round(t_ms, 4), "hbm_frac": round((wbytes + T * K * 2 + T * N * 2) /
+                                                                      (t_ms * 1e-3) / (hbm * 1e9), 4)}
+        xp = S.make_tokens(4096, K, 11, dev)
+        yp = torch.empty((4096, N), dtype=torch.bfloat16, device=dev)
+        W.mx_linear(xp, mats[0].weight, mats[0].scales, "mxfp8", out=yp)
+        torch.cuda.synchronize()
+        s3, e3 = _events(torch)
+        s3.record()
+        for i in range(8):
+            W.mx_linear(xp, mats[i].weight, mats[i].scales, "mxfp8", out=yp)
+        e3.record()
+        torch.cuda.synchronize()
+        t_ms = s3.elapsed_time(e3) / 8
+        per_b["4096"] = {"ms": round(t_ms, 4), "tflops": round(2 * 4096 * N * K / (t_ms * 1e-3) / 1e12, 1),
+                         "tensor_frac": round(2 * 4096 * N * K / (t_ms * 1e-3) / (tc * 1e12), 4)}
+        # end to end: rows from pinned host memory, outputs back
+        hx = [x.cpu().pin_memory() for x in xs_l]
+        ho = [torch.empty(o.shape, dtype=torch.bfloat16).pin_memory() for o in outs]
+        torch.cuda.synchronize()
+        s4, e4 = _events(torch)
+        s4.record()
+        for i in range(args.steps):
+            for j in range(len(sweep)):
+                m = mats[(3 * i + j) % 8]
+                y = W.mx_linear(hx[j].to(dev, non_blocking=True), m.weight, m.scales, "mxfp8", out=outs[j])
+                ho[j].copy_(y, non_blocking=True)
+        e4.record()
+        torch.cuda.synchronize()
+        ms_e2e = s4.elapsed_time(e4) / args.steps
+        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(sweep), alg_bytes=alg, per_b=per_b,
+                        clocks=clocks, flops=0, h2d=sum(T * K * 2 for T in sweep), d2h=sum(T * N * 2 for T in sweep),
+                        cfg={}, batches=sweep, distinct=[], hbm=hbm, peak_src=peak_src, launches=3 * len(sweep),
+                        kernel="dense MXFP8 linear call (wmx_linear: tile list, token split, tcgen05 block-scaled GEMM)",
+                        dtype="e4m3 weights with E8M0 per 32, bf16 activations, fp32 accumulate",
+                        data="synthetic (seeded N(0,0.02) weights quantized to MXFP8, N(0,1) bf16 rows)",
+                        config={"K": K, "N": N, "rows_per_step": list(sweep), "weight_matrices_cycled": 8,
+                                "l2": "8 x 27 MB of weights cycled: larger than L2", "launch": "eager",
+                                "per_batch": per_b}))
+        return res
     if wl == "kv":
         D, rows_total = 576, 32768 * 8 * 61
         chunk = 32768 * 8          # one layer of the 8 x 32768-token context per call
@@ -635,6 +723,17 @@ def cpu_reference(args, sample_steps=None):
             F.kv_scores(q, p.reshape(1, n, -1), s.reshape(1, n, -1), F.KV_MXFP8_B32, D)
 
         tokens, sample = n, "kv_scores: one query against 32768 MXFP8 rows of 512 (one sequence, one layer), numpy oracle"
+    elif wl == "linear":
+        K = N = 5120
+        rng = np.random.default_rng(0)
+        w = F.round_bf16(rng.normal(0, 0.02, (N, K)).astype(np.float32))
+        p, s = F.kv_quantize(w, F.KV_MXFP8_B32)
+        q = F.round_bf16(rng.normal(0, 1, (1, 16, K)).astype(np.float32))
+
+        def step():
+            F.kv_scores(q, p.reshape(1, N, -1), s.reshape(1, N, -1), F.KV_MXFP8_B32, K)
+
+        tokens, sample = 16, "linear: 16 rows through one MXFP8 [5120 x 5120] weight, numpy oracle (float64 product)"
     elif wl == "qsa":
         n = 32768
         rng = np.random.default_rng(0)
@@ -709,7 +808,7 @@ def cpu_reference(args, sample_steps=None):
         step()
     dt = (time.perf_counter() - t0) / steps
     # the KV restatements are single-threaded numpy; the MoE arm runs the C kernels on every host thread
-    cores = 1 if wl in ("kv", "kv_scores", "qsa") else threads
+    cores = 1 if wl in ("kv", "kv_scores", "qsa", "linear") else threads
     return dict(value=tokens / dt, sec_per_step=dt, tokens=tokens, cores=cores, sample=sample)
 
 
@@ -720,7 +819,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="ds_decode",
-                    choices=["ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny", "kv", "kv_scores", "qsa"])
+                    choices=["ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny", "kv", "kv_scores", "qsa",
+                             "linear"])
     ap.add_argument("--layers", type=int, default=8, help="resident layers cycled per step (no L2 reuse)")
     ap.add_argument("--experts", type=int, default=None,
                     help="routed experts per layer (default: the configuration's); smaller layers for ncu captures")
@@ -734,12 +834,13 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    unit = {"kv": "KV rows/s", "kv_scores": "cached rows scored/s", "qsa": "context rows fetched/s"}.get(
-        args.workload, "tokens/s")
+    unit = {"kv": "KV rows/s", "kv_scores": "cached rows scored/s", "qsa": "context rows fetched/s",
+            "linear": "rows/s"}.get(args.workload, "tokens/s")
     metric = {"ds_decode": "MoE layer tok/s, DeepSeek-class MXFP4 decode sweep B=1,4,16,64",
               "kv": "FP8 KV quantize+dequantize rows/s",
               "kv_scores": "MXFP8 KV-cache score rows/s (decode, 8 seq x 32768 x 512, 61 layers)",
-              "qsa": "Qwen QSA KV-cache decode update_and_fetch, context rows/s (8 seq x 32768, 12 layers)"}.get(
+              "qsa": "Qwen QSA KV-cache decode update_and_fetch, context rows/s (8 seq x 32768, 12 layers)",
+              "linear": "dense MXFP8 linear rows/s (K 5120 -> N 5120, decode rows T = 1, 4, 16)"}.get(
                   args.workload, f"MoE layer tok/s ({args.workload})")
 
     if args.impl == "reference":
