@@ -111,8 +111,9 @@ WM_API int wmx_split_e4m3(const wm_bf16 *x, int rows, int cols, uint8_t *hi, uin
  * MXFP8PoolingCache.quantized_matmul / index_matmul over the completed chunks
  * (runtime/deepseek_v4_ssd/fp8_cache.py:119-159: mx.quantized_matmul,
  * transpose=True, group 32, mode mxfp8 / mxfp4).  Workspace:
- * wkv_scores_workspace_size(B, Lq, D). */
-WM_API size_t wkv_scores_workspace_size(int B, int Lq, int D);
+ * wkv_scores_workspace_size(B, Lq, D, L); it includes room for f32 partial
+ * sums when a decode-size launch (Lq <= 32) splits K to fill the GPU. */
+WM_API size_t wkv_scores_workspace_size(int B, int Lq, int D, int L);
 WM_API int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const uint8_t *payload, const uint8_t *scales,
                   int L, int fmt, wm_bf16 *scores, void *workspace, size_t ws_bytes, wm_stream_t stream);
 
@@ -122,8 +123,8 @@ WM_API int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const uint8
  * QuantizedLinear layers nn.quantize(mode="mxfp8") installs over native FP8
  * weights (runtime/deepseek_v4_ssd/deepseek_v41_ssd.py:232-261, 353-360:
  * mx.quantized_matmul, transpose=True, group 32).  Workspace:
- * wmx_linear_workspace_size(T, K). */
-WM_API size_t wmx_linear_workspace_size(int T, int K);
+ * wmx_linear_workspace_size(T, K, N). */
+WM_API size_t wmx_linear_workspace_size(int T, int K, int N);
 WM_API int wmx_linear(const wm_bf16 *x, int T, int K, const uint8_t *w, const uint8_t *scales, int N, int fmt,
                wm_bf16 *y, void *workspace, size_t ws_bytes, wm_stream_t stream);
 

@@ -81,6 +81,16 @@ def test_workspace_size_is_pure_host():
     assert L.lib().wmoe_workspace_size(-1, 8, 7168, 2048, 257, 1) == 0
 
 
+def test_score_workspace_holds_split_partials():
+    # a decode-size call over 40 row blocks splits K (f32 partials in the
+    # workspace); a prefill-size call fills the GPU without splitting
+    lib = L.lib()
+    base = lib.wmx_linear_workspace_size(16, 5120, 128)
+    assert lib.wmx_linear_workspace_size(16, 5120, 5120) >= base + 2 * 16 * 5120 * 4
+    assert lib.wmx_linear_workspace_size(4096, 5120, 5120) == lib.wmx_linear_workspace_size(4096, 5120, 128)
+    assert lib.wkv_scores_workspace_size(1, 1, 512, 0) == 0
+
+
 def test_call_raises_valueerror_on_invalid():
     with pytest.raises(ValueError, match="complete BF16 rows"):
         L.call("wmxfp4_quantize", None, 1, 33, None, None, None)

@@ -39,8 +39,8 @@ SIGNATURES = {
     "wmxfp4_quantize": [_P, _I64, _I64, _P, _P, _P],
     "wmxfp4_dequantize": [_P, _P, _I64, _I64, _I, _P, _P],
     "wmx_split_e4m3": [_P, _I, _I, _P, _P, _P, _P],
-    "wkv_scores_workspace_size": [_I, _I, _I],
-    "wmx_linear_workspace_size": [_I, _I],
+    "wkv_scores_workspace_size": [_I, _I, _I, _I],
+    "wmx_linear_workspace_size": [_I, _I, _I],
     "wmx_linear": [_P, _I, _I, _P, _P, _I, _I, _P, _P, _SZ, _P],
     "wkv_mx_scores": [_P, _I, _I, _I, _P, _P, _I, _I, _P, _P, _SZ, _P],
     "wep_ipc_alloc": [_SZ, _P, _P],

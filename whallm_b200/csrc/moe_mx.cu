@@ -109,7 +109,8 @@ struct MxParams {
   int I, H;
   int order;                 // WM_UP_GATE / WM_GATE_UP
   float limit;
-  int m_tiles;               // 128-row work items per tile
+  int m_tiles;               // work items per tile: 128-row blocks x k_splits
+  int k_splits;              // K ranges per 128-row block (down form only); > 1: f32 partial sums to y_part
   int a_fp8;                 // A operand e4m3 (MXFP8: one byte per value) instead of e2m1
   const uint8_t *a_scales;   // [E * rows, K/32] E8M0 (the MXFP4 scales)
   const uint8_t *b_scales;   // [S_pad, K/32] hi-term E8M0 in slot order
@@ -119,6 +120,8 @@ struct MxParams {
   uint8_t *h_sc;             // up, fused split: [S_pad, I/32] E8M0 scale of h_hi
   uint16_t *h_out;           // up, separate split: [S_pad, I] bf16
   uint16_t *y_out;           // down: [S, H] bf16
+  float *y_part;             // down, k_splits > 1: [k_splits][part_stride] f32, summed by k_sum_splits
+  int64_t part_stride;
   int32_t *err;
 };
 
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   WM_PDL_LAUNCH();
 
   const int n_items = (*p.n_tiles) * p.m_tiles;
-  const int kstages = p.K / C::kKC;
+  const int kstages = p.K / C::kKC / p.k_splits;      // stages per work item
   const int ks32 = p.K / 32;
 
   if (warp == 0) {
@@ -249,7 +252,8 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     bool ok = true;
     for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance()) {
       const int4 tile = tc.cur;
-      const int m = tc.m();
+      const int m = tc.m() / p.k_splits;
+      const int k0 = (tc.m() - m * p.k_splits) * kstages * C::kKC;   // this item's K range
       const int nb = (tile.z + 15) >> 4;                // 16-row token boxes per term
       for (int kc = 0; kc < kstages; ++kc, ++g) {
         const int s = g % S;
@@ -258,7 +262,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
           // transaction bytes count the packed global bytes of the weights
           mbar_expect_tx(&full[s], HV * (p.a_fp8 ? kM * kKH : kM * kKH / 2) + 2 * HV * nb * 16 * kKH);
           for (int q = 0; q < HV; ++q) {
-            const int x = kc * C::kKC + q * kKH;
+            const int x = k0 + kc * C::kKC + q * kKH;
             uint8_t *a = sA + s * C::kAStage + q * C::kABox;
             if (p.mode == 0)
               tma_load_4d(a, &tmA, x, 0, 0, tile.x * (p.I / 4) + m * 8, &full[s]);
@@ -336,9 +340,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     const int t = threadIdx.x - 128;
     const int o = (t & 31) * 4 + (t >> 5);              // 32-bit word of row t inside an atom
     constexpr int BA = C::kBAtoms;
-    const int CW = (ks32 % 32 == 0) ? 8 : (ks32 % 16 == 0) ? 4 : 2;   // words per row per chunk
-    const int SPC = CW / HV;                            // stages per chunk (K % 256 == 0: ks32 % 8 == 0)
-    const int n_ch = ks32 / (4 * CW);                   // chunks per work item
+    const int kb = ks32 / p.k_splits;                   // scale bytes per row of one work item
+    const int CW = (kb % 32 == 0) ? 8 : (kb % 16 == 0) ? 4 : 2;   // words per row per chunk
+    const int SPC = CW / HV;                            // stages per chunk (K range % 256 == 0: kb % 8 == 0)
+    const int n_ch = kb / (4 * CW);                     // chunks per work item
     struct Chunk {
       uint32_t a[8];
       uint32_t b[BA][8];
@@ -371,10 +376,11 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       }
       if (!cur.valid()) return;
       const int4 tile = cur.cur;
-      const int m = cur.m();
+      const int m = cur.m() / p.k_splits;
+      const int kofs = (cur.m() - m * p.k_splits) * kb + c_ch * 4 * CW;   // first scale byte of the chunk
       const int grow = p.mode == 0 ? ((t >> 3) & 1) * p.I + m * 64 + (t >> 4) * 8 + (t & 7) : m * kM + t;
       if (grow < p.rows)                                // a last partial 128-row tile (score rows): zero scales
-        load_words(p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + c_ch * 4 * CW, e.a);
+        load_words(p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + kofs, e.a);
       const int n16 = max(16, (tile.z + 15) & ~15);
 #pragma unroll
       for (int a = 0; a < BA; ++a) {
@@ -382,7 +388,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
         const bool lo_row = r >= n16;
         const int tok = lo_row ? r - n16 : r;
         if (tok < tile.z && r < 2 * n16) {
-          load_words(p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + c_ch * 4 * CW, e.b[a]);
+          load_words(p.b_scales + static_cast<int64_t>(tile.y + tok) * ks32 + kofs, e.b[a]);
           e.sub[a] = lo_row ? kLoSub : 0u;
         }
       }
@@ -445,7 +451,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     bool ok = true;
     for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance(), ++it) {
       const int4 tile = tc.cur;
-      const int m = tc.m();
+      const int m = tc.m() / p.k_splits;
       const int db = it & 1;
       if (!(ok = mbar_wait(&dfull[db], (it >> 1) & 1, p.err, 8))) break;
       tc_fence_after();
@@ -517,6 +523,13 @@ __global__ void __launch_bounds__(C::kThreads, 1)
             if (!(wq & 1) && (t & 7) == 0 && ((t >> 4) & 1) == 0)  // first up lane of the block
               p.h_sc[static_cast<int64_t>(tile.y + c0 + q) * (p.I / 32) + (jj >> 5)] = static_cast<uint8_t>(sh + 127);
           }
+        } else if (p.k_splits > 1) {
+          const int row = m * kM + t;
+          float *part = p.y_part + static_cast<int64_t>(tc.m() - m * p.k_splits) * p.part_stride;
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            if (c0 + q < n && row < p.rows)
+              part[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = __uint_as_float(r[q]);
         } else {
           const int row = m * kM + t;
 #pragma unroll
@@ -594,6 +607,38 @@ __global__ void k_split_e4m3(const uint16_t *__restrict__ src, const int32_t *__
   }
 }
 
+// out[i] = bf16(part[0][i] + part[1][i] + ... + part[splits-1][i]), added in
+// split order so the result does not depend on which CTA finished first.
+__global__ void k_sum_splits(const float *__restrict__ part, int64_t n, int64_t stride, int splits,
+                             uint16_t *__restrict__ out) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
+  const int64_t groups = (n + 3) / 4;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < groups;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = 4 * i;
+    if (e + 4 <= n) {
+      float4 acc = *reinterpret_cast<const float4 *>(part + e);
+      for (int s = 1; s < splits; ++s) {
+        const float4 v = *reinterpret_cast<const float4 *>(part + s * stride + e);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      *reinterpret_cast<uint2 *>(out + e) =
+          make_uint2(static_cast<uint32_t>(wm_f32_to_bf16(acc.x)) | (static_cast<uint32_t>(wm_f32_to_bf16(acc.y)) << 16),
+                     static_cast<uint32_t>(wm_f32_to_bf16(acc.z)) | (static_cast<uint32_t>(wm_f32_to_bf16(acc.w)) << 16));
+    } else {
+      for (int64_t j = e; j < n; ++j) {
+        float acc = part[j];
+        for (int s = 1; s < splits; ++s) acc += part[s * stride + j];
+        out[j] = wm_f32_to_bf16(acc);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------ host side
 
 int make_map_nd(CUtensorMap *map, CUtensorMapDataType dt, int rank, const void *base, const cuuint64_t *dims,
@@ -611,8 +656,11 @@ template <class C>
 int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K, const uint8_t *b_hi,
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-                  uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool a_fp8 = false) {
+                  uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool a_fp8 = false,
+                  int k_splits = 1, float *y_part = nullptr, int64_t part_stride = 0) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
+  if (k_splits < 1 || (K / C::kKC) % k_splits || (k_splits > 1 && (mode != 1 || !y_part)))
+    return wm::fail(WM_ERR_INVALID, "expert mx: bad K split");
   if (!wm::aligned(w, a_fp8 ? 16 : 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed A operand misaligned");
   if (!wm::aligned(a_scales, 16) || !wm::aligned(b_sc, 16))
     return wm::fail(WM_ERR_INVALID, "expert mx: scales must be 16-byte aligned");
@@ -674,7 +722,10 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.H = H;
   p.order = order;
   p.limit = limit;
-  p.m_tiles = mode == 0 ? I / 64 : (rows + kM - 1) / kM;
+  p.m_tiles = (mode == 0 ? I / 64 : (rows + kM - 1) / kM) * k_splits;
+  p.k_splits = k_splits;
+  p.y_part = y_part;
+  p.part_stride = part_stride;
   p.a_fp8 = a_fp8 ? 1 : 0;
   p.a_scales = a_scales;
   p.b_scales = b_sc;
@@ -769,10 +820,42 @@ struct ScoreWorkspace {
   uint8_t *q_hi, *q_lo, *q_sc;
   int4 *tiles;
   int32_t *counters;  // [0] n_tiles, [1] error code
+  float *part;        // [splits][part_stride] f32 partial scores
+  int64_t part_stride;
   size_t bytes;
 };
 
-ScoreWorkspace carve_scores(void *base, int B, int Lq, int D) {
+constexpr int kB200Sms = 148;
+
+// K ranges per work item for a decode-configuration score launch whose
+// (tile, 128-row) items do not fill the GPU: the divisor s of the stage count
+// that minimises the busiest CTA's stages, counting one stage of per-item
+// overhead, ceil(items * s / sm) * (stages / s + 1).  s = 1 for launches that
+// already fill every SM, and always for the prefill configuration.
+int choose_splits(int64_t items, int stages, int nmax, int sm) {
+  if (nmax != MxDecode::kNMax || items <= 0 || items >= sm) return 1;
+  int best = 1;
+  int64_t best_cost = (items + sm - 1) / sm * (stages + 1);
+  for (int s = 2; s <= stages && s <= 32; ++s) {
+    if (stages % s) continue;
+    const int64_t cost = (items * s + sm - 1) / sm * (stages / s + 1);
+    if (cost < best_cost) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+int score_nmax(int Lq) { return Lq <= 32 ? MxDecode::kNMax : MxPrefill::kNMax; }
+
+int score_splits(int B, int Lq, int D, int L, int sm) {
+  const int nmax = score_nmax(Lq);
+  const int64_t items = static_cast<int64_t>(B) * ((Lq + nmax - 1) / nmax) * ((L + kM - 1) / kM);
+  return choose_splits(items, D / MxDecode::kKC, nmax, sm);
+}
+
+ScoreWorkspace carve_scores(void *base, int B, int Lq, int D, int L, int splits) {
   ScoreWorkspace w{};
   const size_t rows = static_cast<size_t>(std::max(B * Lq, 16));
   size_t off = 0;
@@ -783,6 +866,8 @@ ScoreWorkspace carve_scores(void *base, int B, int Lq, int D) {
   };
   const size_t o_hi = take(rows * D), o_lo = take(rows * D), o_sc = take(rows * (D / 32));
   const size_t o_t = take((static_cast<size_t>(B) * (Lq + 15) / 16 + 2) * sizeof(int4)), o_c = take(16);
+  w.part_stride = splits > 1 ? static_cast<int64_t>(wm::align_up(static_cast<size_t>(B) * Lq * L, 64)) : 0;
+  const size_t o_p = take(static_cast<size_t>(splits > 1 ? splits : 0) * w.part_stride * sizeof(float));
   w.bytes = off;
   if (base) {
     char *b = static_cast<char *>(base);
@@ -791,15 +876,16 @@ ScoreWorkspace carve_scores(void *base, int B, int Lq, int D) {
     w.q_sc = reinterpret_cast<uint8_t *>(b + o_sc);
     w.tiles = reinterpret_cast<int4 *>(b + o_t);
     w.counters = reinterpret_cast<int32_t *>(b + o_c);
+    w.part = reinterpret_cast<float *>(b + o_p);
   }
   return w;
 }
 
 }  // namespace
 
-extern "C" size_t wkv_scores_workspace_size(int B, int Lq, int D) {
-  if (B < 1 || Lq < 1 || D < 32) return 0;
-  return carve_scores(nullptr, B, Lq, D).bytes;
+extern "C" size_t wkv_scores_workspace_size(int B, int Lq, int D, int L) {
+  if (B < 1 || Lq < 1 || D < 32 || L < 1) return 0;
+  return carve_scores(nullptr, B, Lq, D, L, D % 256 ? 1 : score_splits(B, Lq, D, L, kB200Sms)).bytes;
 }
 
 extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const uint8_t *payload,
@@ -812,10 +898,16 @@ extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const u
   WM_REQUIRE(query && payload && scales && scores && workspace, "kv scores: null buffer");
   WM_REQUIRE(wm::aligned(query, 16) && wm::aligned(scores, 16) && wm::aligned(workspace, 256),
              "kv scores: query/scores 16-byte, workspace 256-byte aligned");
-  ScoreWorkspace ws = carve_scores(workspace, B, Lq, D);
+  // K splits for an under-filled launch, fewer if the workspace was sized for fewer
+  int splits = score_splits(B, Lq, D, L, wm::sm_count());
+  ScoreWorkspace ws = carve_scores(workspace, B, Lq, D, L, splits);
+  while (splits > 1 && ws_bytes < ws.bytes) {
+    do --splits; while ((D / MxDecode::kKC) % splits);
+    ws = carve_scores(workspace, B, Lq, D, L, splits);
+  }
   if (ws_bytes < ws.bytes) return wm::fail(WM_ERR_WORKSPACE, "kv scores: workspace too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int nmax = Lq <= 32 ? MxDecode::kNMax : MxPrefill::kNMax;
+  const int nmax = score_nmax(Lq);
   const int per = (Lq + nmax - 1) / nmax;
   if (cudaError_t e = wm::launch_pdl(k_score_tiles, dim3((B * per + 255) / 256), dim3(256), 0, st, B, Lq, nmax,
                                      ws.tiles, ws.counters))
@@ -825,17 +917,26 @@ extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const u
     return rc;
   // scores[b, q, l] = D[l, q] of the "down projection" form: rows = L cache rows of batch b, output row stride L
   const int s_rows = std::max(B * Lq, 16);
-  if (nmax == MxDecode::kNMax)
-    return launch_mx_cfg<MxDecode>(1, payload, scales, B, L, D, ws.q_hi, ws.q_lo, ws.q_sc, s_rows, 0, L, WM_UP_GATE,
-                                   0.0f, ws.tiles, ws.counters, nullptr, nullptr, nullptr, nullptr,
-                                   reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st,
-                                   fmt == WKV_MXFP8_B32);
+  if (nmax == MxDecode::kNMax) {
+    if (int rc = launch_mx_cfg<MxDecode>(1, payload, scales, B, L, D, ws.q_hi, ws.q_lo, ws.q_sc, s_rows, 0, L,
+                                         WM_UP_GATE, 0.0f, ws.tiles, ws.counters, nullptr, nullptr, nullptr, nullptr,
+                                         reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st,
+                                         fmt == WKV_MXFP8_B32, splits, ws.part, ws.part_stride))
+      return rc;
+    if (splits == 1) return WM_OK;
+    const int64_t n = static_cast<int64_t>(B) * Lq * L;
+    const int grid = static_cast<int>(std::min<int64_t>(((n + 3) / 4 + 255) / 256, wm::sm_count() * 8));
+    if (cudaError_t e = wm::launch_pdl(k_sum_splits, dim3(grid), dim3(256), 0, st, static_cast<const float *>(ws.part),
+                                       n, ws.part_stride, splits, reinterpret_cast<uint16_t *>(scores)))
+      return wm::fail(WM_ERR_CUDA, std::string("kv scores split sum: ") + cudaGetErrorString(e));
+    return wm::check_launch("kv scores split sum");
+  }
   return launch_mx_cfg<MxPrefill>(1, payload, scales, B, L, D, ws.q_hi, ws.q_lo, ws.q_sc, s_rows, 0, L, WM_UP_GATE,
                                   0.0f, ws.tiles, ws.counters, nullptr, nullptr, nullptr, nullptr,
                                   reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st, fmt == WKV_MXFP8_B32);
 }
 
-extern "C" size_t wmx_linear_workspace_size(int T, int K) { return wkv_scores_workspace_size(1, T, K); }
+extern "C" size_t wmx_linear_workspace_size(int T, int K, int N) { return wkv_scores_workspace_size(1, T, K, N); }
 
 // A dense block-scaled linear is the score kernel with one "sequence" whose N
 // cached rows are the weight rows and whose T queries are the tokens.

@@ -82,7 +82,7 @@ def kv_scores(query: torch.Tensor, payload: torch.Tensor, scales: torch.Tensor, 
     q = query.contiguous()
     if out is None:
         out = torch.empty((B, Lq, Lc), dtype=torch.bfloat16, device=q.device)
-    nbytes = int(L.lib().wkv_scores_workspace_size(B, Lq, D))
+    nbytes = int(L.lib().wkv_scores_workspace_size(B, Lq, D, Lc))
     ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=q.device)
     L.require_cuda(q, payload, scales, out)
     L.call("wkv_mx_scores", L.ptr(q), B, Lq, D, L.ptr(payload.contiguous()), L.ptr(scales.contiguous()), Lc, f,

@@ -46,7 +46,7 @@ def mx_linear(x: torch.Tensor, weight: torch.Tensor, scales: torch.Tensor, fmt="
     if out is None:
         out = torch.empty((T, N), dtype=torch.bfloat16, device=x.device)
     if T:
-        nbytes = int(L.lib().wmx_linear_workspace_size(T, K))
+        nbytes = int(L.lib().wmx_linear_workspace_size(T, K, N))
         ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=x.device)
         L.require_cuda(xf, weight, scales, out)
         L.call("wmx_linear", L.ptr(xf), T, K, L.ptr(weight.contiguous()), L.ptr(scales.contiguous()), N, f,
