@@ -122,6 +122,10 @@ struct MxParams {
   uint16_t *y_out;           // down: [S, H] bf16
   float *y_part;             // down, k_splits > 1: [k_splits][part_stride] f32, summed by k_sum_splits
   int64_t part_stride;
+  // Dense tiles (score and linear launches): d_tiles > 0 tiles computed from
+  // their index instead of read from `tiles`: tile i = {b, b * d_lq + j * d_nmax,
+  // min(d_nmax, d_lq - j * d_nmax)} for b = i / d_per, j = i % d_per.
+  int d_tiles, d_per, d_lq, d_nmax;
   int32_t *err;
 };
 
@@ -184,11 +188,18 @@ __device__ __forceinline__ float silu_mx(float g) { return g / (1.0f + expf(-g))
 struct TileCursor {
   const int4 *tiles;
   int m_tiles, n_items, item;
+  int d_per, d_lq, d_nmax;                    // dense tiles when d_per > 0
   int4 cur, nxt;
   __device__ __forceinline__ int4 load(int i) const {
-    return i < n_items ? tiles[i / m_tiles] : make_int4(0, 0, 0, 0);
+    if (i >= n_items) return make_int4(0, 0, 0, 0);
+    const int t = i / m_tiles;
+    if (d_per == 0) return tiles[t];
+    const int b = t / d_per, j = t - b * d_per;
+    return make_int4(b, b * d_lq + j * d_nmax, min(d_nmax, d_lq - j * d_nmax), 0);
   }
-  __device__ __forceinline__ TileCursor(const int4 *t, int mt, int n) : tiles(t), m_tiles(mt), n_items(n) {
+  __device__ __forceinline__ TileCursor(const MxParams &p, int n)
+      : tiles(p.tiles), m_tiles(p.m_tiles), n_items(n), d_per(p.d_tiles > 0 ? p.d_per : 0), d_lq(p.d_lq),
+        d_nmax(p.d_nmax) {
     item = blockIdx.x;
     cur = load(item);
     nxt = load(item + gridDim.x);
@@ -205,7 +216,7 @@ struct TileCursor {
 template <class C>
 __global__ void __launch_bounds__(C::kThreads, 1)
     k_expert_mx(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmBh,
-                const __grid_constant__ CUtensorMap tmBl, MxParams p) {
+                const __grid_constant__ CUtensorMap tmBl, const __grid_constant__ MxParams p) {
   constexpr int S = C::kStages;
   constexpr int HV = C::kHalves;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -242,7 +253,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
 
-  const int n_items = (*p.n_tiles) * p.m_tiles;
+  const int n_items = (p.d_tiles > 0 ? p.d_tiles : *p.n_tiles) * p.m_tiles;
   const int kstages = p.K / C::kKC / p.k_splits;      // stages per work item
   const int ks32 = p.K / 32;
 
@@ -250,7 +261,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     // ---------------------------------------------------------- producer
     uint32_t g = 0;
     bool ok = true;
-    for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance()) {
+    for (TileCursor tc(p, n_items); tc.valid() && ok; tc.advance()) {
       const int4 tile = tc.cur;
       const int m = tc.m() / p.k_splits;
       const int k0 = (tc.m() - m * p.k_splits) * kstages * C::kKC;   // this item's K range
@@ -289,7 +300,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     const uint32_t a_fmt_mask = p.a_fp8 ? ~(7u << 7) : ~0u;   // A format field: e2m1 (5) or e4m3 (0)
     uint32_t g = 0, it = 0;
     bool ok = true;
-    for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance(), ++it) {
+    for (TileCursor tc(p, n_items); tc.valid() && ok; tc.advance(), ++it) {
       const int4 tile = tc.cur;
       const int n_mma = 2 * max(16, (tile.z + 15) & ~15);   // hi and lo rows
       const int db = it & 1;
@@ -349,7 +360,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       uint32_t b[BA][8];
       uint32_t sub[BA];                                 // kLoSub for a lo-term row, else 0
     };
-    TileCursor cur(p.tiles, p.m_tiles, n_items);       // prefetch cursor
+    TileCursor cur(p, n_items);       // prefetch cursor
     int c_ch = 0;
     auto load_words = [&](const uint8_t *src, uint32_t *dst) {
       if (CW == 8) {
@@ -449,7 +460,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     uint32_t xchg_n = 0;
     uint32_t it = 0;
     bool ok = true;
-    for (TileCursor tc(p.tiles, p.m_tiles, n_items); tc.valid() && ok; tc.advance(), ++it) {
+    for (TileCursor tc(p, n_items); tc.valid() && ok; tc.advance(), ++it) {
       const int4 tile = tc.cur;
       const int m = tc.m() / p.k_splits;
       const int db = it & 1;
@@ -554,13 +565,15 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 
 // Rows [0, rows) of a bf16 matrix (GATHER: row p is x[perm[p] / kk]) ->
 // hi, lo e4m3 bytes and the hi term's E8M0 scale per 32 columns.  Four
-// threads per 32-value block, eight values each.
+// threads per 32-value block, eight values each.  `zero`, if set, is a word
+// the following tensor-core launch reports errors in, cleared here.
 template <bool GATHER>
 __global__ void k_split_e4m3(const uint16_t *__restrict__ src, const int32_t *__restrict__ perm,
                              const int32_t *__restrict__ count, int S, int kk, int K, uint8_t *__restrict__ hi,
-                             uint8_t *__restrict__ lo, uint8_t *__restrict__ sc) {
+                             uint8_t *__restrict__ lo, uint8_t *__restrict__ sc, int32_t *__restrict__ zero) {
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
+  if (zero && blockIdx.x == 0 && threadIdx.x == 0) *zero = 0;
   const int rows = count ? min(S, max(0, *count)) : S;
   const int per_row = K / 8;
   const int64_t total = static_cast<int64_t>(rows) * per_row;
@@ -619,12 +632,19 @@ __global__ void k_sum_splits(const float *__restrict__ part, int64_t n, int64_t 
     const int64_t e = 4 * i;
     if (e + 4 <= n) {
       float4 acc = *reinterpret_cast<const float4 *>(part + e);
-      for (int s = 1; s < splits; ++s) {
-        const float4 v = *reinterpret_cast<const float4 *>(part + s * stride + e);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
+      for (int s0 = 1; s0 < splits; s0 += 8) {       // eight loads in flight, then the adds in split order
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (s0 + u < splits) v[u] = *reinterpret_cast<const float4 *>(part + (s0 + u) * stride + e);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (s0 + u < splits) {
+            acc.x += v[u].x;
+            acc.y += v[u].y;
+            acc.z += v[u].z;
+            acc.w += v[u].w;
+          }
       }
       *reinterpret_cast<uint2 *>(out + e) =
           make_uint2(static_cast<uint32_t>(wm_f32_to_bf16(acc.x)) | (static_cast<uint32_t>(wm_f32_to_bf16(acc.y)) << 16),
@@ -657,10 +677,12 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
                   uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool a_fp8 = false,
-                  int k_splits = 1, float *y_part = nullptr, int64_t part_stride = 0) {
+                  int k_splits = 1, float *y_part = nullptr, int64_t part_stride = 0, int4 dense = int4{0, 0, 0, 0}) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
   if (k_splits < 1 || (K / C::kKC) % k_splits || (k_splits > 1 && (mode != 1 || !y_part)))
     return wm::fail(WM_ERR_INVALID, "expert mx: bad K split");
+  if (dense.x > 0 && (mode != 1 || dense.y < 1 || dense.w < 1 || dense.w > C::kNMax))
+    return wm::fail(WM_ERR_INVALID, "expert mx: bad dense tiles");
   if (!wm::aligned(w, a_fp8 ? 16 : 32)) return wm::fail(WM_ERR_INVALID, "expert mx: packed A operand misaligned");
   if (!wm::aligned(a_scales, 16) || !wm::aligned(b_sc, 16))
     return wm::fail(WM_ERR_INVALID, "expert mx: scales must be 16-byte aligned");
@@ -726,6 +748,10 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.k_splits = k_splits;
   p.y_part = y_part;
   p.part_stride = part_stride;
+  p.d_tiles = dense.x;                                  // {tiles, tiles per batch, rows per batch, rows per tile}
+  p.d_per = dense.y;
+  p.d_lq = dense.z;
+  p.d_nmax = dense.w;
   p.a_fp8 = a_fp8 ? 1 : 0;
   p.a_scales = a_scales;
   p.b_scales = b_sc;
@@ -767,14 +793,15 @@ int mx_tile_n(int T, int k, int n_routed) {
 }
 
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
-                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream) {
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero) {
   const int64_t work = static_cast<int64_t>(S) * (K / 8);
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
   if (grid > 0) {
     const cudaError_t e =
-        perm ? launch_pdl(k_split_e4m3<true>, dim3(grid), dim3(256), 0, stream, src, perm, count, S, kk, K, hi, lo, sc)
+        perm ? launch_pdl(k_split_e4m3<true>, dim3(grid), dim3(256), 0, stream, src, perm, count, S, kk, K, hi, lo, sc,
+                          zero)
              : launch_pdl(k_split_e4m3<false>, dim3(grid), dim3(256), 0, stream, src, static_cast<const int32_t *>(nullptr),
-                          count, S, 1, K, hi, lo, sc);
+                          count, S, 1, K, hi, lo, sc, zero);
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("split e4m3: ") + cudaGetErrorString(e));
   }
   return check_launch("split e4m3");
@@ -801,25 +828,9 @@ int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
 
 namespace {
 
-// tiles {batch, first query row, queries, 0}: ceil(Lq / nmax) per batch
-__global__ void k_score_tiles(int B, int Lq, int nmax, int4 *tiles, int32_t *n_tiles) {
-  WM_PDL_WAIT();
-  WM_PDL_LAUNCH();
-  const int per = (Lq + nmax - 1) / nmax;
-  for (int i = threadIdx.x + blockIdx.x * blockDim.x; i < B * per; i += blockDim.x * gridDim.x) {
-    const int b = i / per, j = i % per;
-    tiles[i] = make_int4(b, b * Lq + j * nmax, min(nmax, Lq - j * nmax), 0);
-  }
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    n_tiles[0] = B * per;
-    n_tiles[1] = 0;                                       // the tensor-core kernel's error code
-  }
-}
-
 struct ScoreWorkspace {
   uint8_t *q_hi, *q_lo, *q_sc;
-  int4 *tiles;
-  int32_t *counters;  // [0] n_tiles, [1] error code
+  int32_t *counters;  // [1] the tensor-core kernel's error code (cleared by the token split)
   float *part;        // [splits][part_stride] f32 partial scores
   int64_t part_stride;
   size_t bytes;
@@ -865,7 +876,7 @@ ScoreWorkspace carve_scores(void *base, int B, int Lq, int D, int L, int splits)
     return o;
   };
   const size_t o_hi = take(rows * D), o_lo = take(rows * D), o_sc = take(rows * (D / 32));
-  const size_t o_t = take((static_cast<size_t>(B) * (Lq + 15) / 16 + 2) * sizeof(int4)), o_c = take(16);
+  const size_t o_c = take(16);
   w.part_stride = splits > 1 ? static_cast<int64_t>(wm::align_up(static_cast<size_t>(B) * Lq * L, 64)) : 0;
   const size_t o_p = take(static_cast<size_t>(splits > 1 ? splits : 0) * w.part_stride * sizeof(float));
   w.bytes = off;
@@ -874,7 +885,6 @@ ScoreWorkspace carve_scores(void *base, int B, int Lq, int D, int L, int splits)
     w.q_hi = reinterpret_cast<uint8_t *>(b + o_hi);
     w.q_lo = reinterpret_cast<uint8_t *>(b + o_lo);
     w.q_sc = reinterpret_cast<uint8_t *>(b + o_sc);
-    w.tiles = reinterpret_cast<int4 *>(b + o_t);
     w.counters = reinterpret_cast<int32_t *>(b + o_c);
     w.part = reinterpret_cast<float *>(b + o_p);
   }
@@ -909,19 +919,18 @@ extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const u
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int nmax = score_nmax(Lq);
   const int per = (Lq + nmax - 1) / nmax;
-  if (cudaError_t e = wm::launch_pdl(k_score_tiles, dim3((B * per + 255) / 256), dim3(256), 0, st, B, Lq, nmax,
-                                     ws.tiles, ws.counters))
-    return wm::fail(WM_ERR_CUDA, std::string("kv scores tiles: ") + cudaGetErrorString(e));
+  // tiles {batch, first query row, queries}: ceil(Lq / nmax) per batch, computed in the kernel
+  const int4 dense = make_int4(B * per, per, Lq, nmax);
   if (int rc = wm::launch_split_e4m3(reinterpret_cast<const uint16_t *>(query), nullptr, nullptr, B * Lq, 1, D,
-                                     ws.q_hi, ws.q_lo, ws.q_sc, st))
+                                     ws.q_hi, ws.q_lo, ws.q_sc, st, ws.counters + 1))
     return rc;
   // scores[b, q, l] = D[l, q] of the "down projection" form: rows = L cache rows of batch b, output row stride L
   const int s_rows = std::max(B * Lq, 16);
   if (nmax == MxDecode::kNMax) {
     if (int rc = launch_mx_cfg<MxDecode>(1, payload, scales, B, L, D, ws.q_hi, ws.q_lo, ws.q_sc, s_rows, 0, L,
-                                         WM_UP_GATE, 0.0f, ws.tiles, ws.counters, nullptr, nullptr, nullptr, nullptr,
+                                         WM_UP_GATE, 0.0f, nullptr, ws.counters, nullptr, nullptr, nullptr, nullptr,
                                          reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st,
-                                         fmt == WKV_MXFP8_B32, splits, ws.part, ws.part_stride))
+                                         fmt == WKV_MXFP8_B32, splits, ws.part, ws.part_stride, dense))
       return rc;
     if (splits == 1) return WM_OK;
     const int64_t n = static_cast<int64_t>(B) * Lq * L;
@@ -932,8 +941,9 @@ extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const u
     return wm::check_launch("kv scores split sum");
   }
   return launch_mx_cfg<MxPrefill>(1, payload, scales, B, L, D, ws.q_hi, ws.q_lo, ws.q_sc, s_rows, 0, L, WM_UP_GATE,
-                                  0.0f, ws.tiles, ws.counters, nullptr, nullptr, nullptr, nullptr,
-                                  reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st, fmt == WKV_MXFP8_B32);
+                                  0.0f, nullptr, ws.counters, nullptr, nullptr, nullptr, nullptr,
+                                  reinterpret_cast<uint16_t *>(scores), ws.counters + 1, st, fmt == WKV_MXFP8_B32, 1,
+                                  nullptr, 0, dense);
 }
 
 extern "C" size_t wmx_linear_workspace_size(int T, int K, int N) { return wkv_scores_workspace_size(1, T, K, N); }

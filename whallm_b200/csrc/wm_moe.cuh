@@ -42,9 +42,10 @@ int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
 bool mx_supported(int H, int I);
 // tokens per tile: 32 (decode configuration) while T * k / n_routed <= 32, else 112
 int mx_tile_n(int T, int k, int n_routed);
-// rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk]
+// rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk];
+// *zero (if given) is set to 0 once the kernel's dependency wait has returned
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
-                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream);
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero = nullptr);
 // the up projection writes h's e4m3 terms itself (true) or bf16 h for launch_split_e4m3 (false)
 bool mx_fused_split(int tile_n);
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
