@@ -138,6 +138,15 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, i
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d_hint(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
+                                                 uint64_t *bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Block-scaled instruction descriptor: A e2m1, B e4m3, E8M0 scales, f32 D,
 // K-major A and B, M = 128, N = n, scale-factor byte ids for A and B = j.
 __device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t j) {
@@ -261,6 +270,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     // ---------------------------------------------------------- producer
     uint32_t g = 0;
     bool ok = true;
+    // decode: each weight box is read by one tile per launch, so it streams
+    // through L2 evict-first; prefill tiles of one expert share its boxes
+    const uint64_t stream_once = l2_evict_first_policy();
     for (TileCursor tc(p, n_items); tc.valid() && ok; tc.advance()) {
       const int4 tile = tc.cur;
       const int m = tc.m() / p.k_splits;
@@ -275,10 +287,17 @@ __global__ void __launch_bounds__(C::kThreads, 1)
           for (int q = 0; q < HV; ++q) {
             const int x = k0 + kc * C::kKC + q * kKH;
             uint8_t *a = sA + s * C::kAStage + q * C::kABox;
-            if (p.mode == 0)
-              tma_load_4d(a, &tmA, x, 0, 0, tile.x * (p.I / 4) + m * 8, &full[s]);
-            else
-              tma_load_2d(a, &tmA, x, tile.x * p.rows + m * kM, &full[s]);
+            if constexpr (C::kNMax == 32) {
+              if (p.mode == 0)
+                tma_load_4d_hint(a, &tmA, x, 0, 0, tile.x * (p.I / 4) + m * 8, &full[s], stream_once);
+              else
+                tma_load_2d_hint(a, &tmA, x, tile.x * p.rows + m * kM, &full[s], stream_once);
+            } else {
+              if (p.mode == 0)
+                tma_load_4d(a, &tmA, x, 0, 0, tile.x * (p.I / 4) + m * 8, &full[s]);
+              else
+                tma_load_2d(a, &tmA, x, tile.x * p.rows + m * kM, &full[s]);
+            }
             uint8_t *b = sB + s * C::kBStage + q * C::kBBox;
             for (int j = 0; j < nb; ++j) {
               tma_load_2d(b + j * 16 * kKH, &tmBh, x, tile.y + 16 * j, &full[s]);
