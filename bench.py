@@ -455,10 +455,12 @@ def run_ours(args, rank, world, dev):
         clk = ClockSampler(dev.index if dev.index is not None else 0)
         clk.start()
         s, e = _events(torch)
+        torch.cuda.nvtx.range_push("timed")
         s.record()
         for i in range(args.steps):
             lstep(i)
         e.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         clocks = clk.stop()
         ms = s.elapsed_time(e) / args.steps
