@@ -505,9 +505,9 @@ def run_ours(args, rank, world, dev):
         ms_e2e = s4.elapsed_time(e4) / args.steps
         res.update(dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(sweep), alg_bytes=alg, per_b=per_b,
                         clocks=clocks, flops=0, h2d=sum(T * K * 2 for T in sweep), d2h=sum(T * N * 2 for T in sweep),
-                        cfg={}, batches=sweep, distinct=[], hbm=hbm, peak_src=peak_src, launches=4 * len(sweep),
-                        kernel="dense MXFP8 linear call (wmx_linear: tile list, token split, tcgen05 block-scaled "
-                               "GEMM split over K, ordered sum of the K splits)",
+                        cfg={}, batches=sweep, distinct=[], hbm=hbm, peak_src=peak_src, launches=3 * len(sweep),
+                        kernel="dense MXFP8 linear call (wmx_linear: token split, tcgen05 block-scaled GEMM split "
+                               "over K, ordered sum of the K splits)",
                         dtype="e4m3 weights with E8M0 per 32, bf16 activations, fp32 accumulate",
                         data="synthetic (seeded N(0,0.02) weights quantized to MXFP8, N(0,1) bf16 rows)",
                         config={"K": K, "N": N, "rows_per_step": list(sweep), "weight_matrices_cycled": 8,
