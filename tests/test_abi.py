@@ -103,3 +103,12 @@ def test_fp8_kv_entry_points_reject_other_formats():
             L.call("wkv_fp8_quantize", None, 4, 64, block, sf, None, None, None)
         with pytest.raises(L.NativeError, match="fp8 KV"):
             L.call("wkv_fp8_dequantize", None, None, 4, 64, block, sf, None, None)
+
+
+def test_scores_and_linear_reject_bad_shapes():
+    # host-side checks, before any device work: D (K) a multiple of 256, an MX format, B/Lq/L >= 1
+    _expect("wmx_linear", None, 4, 5000, None, None, 64, L.WKV_MXFP8_B32, None, None, 0, None, msg="D % 256")
+    _expect("wmx_linear", None, 4, 512, None, None, 64, L.WKV_FP8_F32_B64, None, None, 0, None, msg="fmt must be")
+    _expect("wkv_mx_scores", None, 0, 1, 512, None, None, 64, L.WKV_MXFP8_B32, None, None, 0, None)
+    _expect("wkv_mx_scores", None, 1, 1, 512, None, None, 64, L.WKV_MXFP4_B32, None, None, 0, None, msg="null buffer")
+    _expect("wmx_linear", None, 0, 512, None, None, 64, L.WKV_MXFP8_B32, None, None, 0, None, code=L.WM_OK)
