@@ -884,19 +884,23 @@ def main():
         hbm = r["hbm"]
         achieved = r["alg_bytes"] / (ms_exp * 1e-3) / 1e9
         if r.get("prefill"):
-            # prefill is compute-bound: FLOPs of the expert FFN over the measured dense
-            # 16-bit tensor peak (the MMA runs f16 x f16 -> f32)
+            # prefill is compute-bound: useful FLOPs of the expert FFN over the measured
+            # dense bf16 tensor peak (the block-scaled MMAs run two e4m3 terms of the
+            # tokens, twice these FLOPs in tensor work)
             achieved_tf = r["flops"] / (ms_exp * 1e-3) / 1e12
         # DRAM bytes per step of the expert calls: per-expert traffic measured by
         # ncu on a smaller case (profiles/traffic.json), scaled by the distinct
         # experts this workload streams per step
         traffic = None
         prof = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(prof) and (r.get("distinct") or args.workload == "qsa"):
+        if os.path.exists(prof) and (r.get("distinct") or args.workload in ("qsa", "linear")):
             try:
                 t = json.load(open(prof)).get(args.workload)
                 if t and r.get("distinct"):
                     traffic = round(t["bytes_per_expert"] * sum(r["distinct"]))
+                elif t and "bytes_per_call" in t:
+                    # DRAM bytes of one call of the dominant kernel, captured at the bench's own size
+                    traffic = round(t["bytes_per_call"] * t.get("calls_per_step", 1))
                 elif t:
                     # DRAM bytes per algorithmic byte of the fetch, from one capture at a smaller context
                     traffic = round(t["dram_per_algorithmic_byte"] * r["alg_bytes"])
