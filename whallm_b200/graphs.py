@@ -34,8 +34,18 @@ class CapturedLayer:
 
     def __call__(self, x: torch.Tensor | None = None) -> torch.Tensor:
         if x is not None:
-            if x.shape != self.x.shape or x.dtype != self.x.dtype:
-                raise ValueError("captured layer expects the capture shape and dtype")
-            self.x.copy_(x, non_blocking=True)
+            self.stage(x)
+        return self.replay()
+
+    def stage(self, x: torch.Tensor) -> None:
+        """Copy ``x`` (e.g. pinned host memory) into the graph's input buffer on the
+        current stream, so that a caller can stage the next input on a copy stream
+        while an earlier replay runs; order the replay after it with an event."""
+        if x.shape != self.x.shape or x.dtype != self.x.dtype:
+            raise ValueError("captured layer expects the capture shape and dtype")
+        self.x.copy_(x, non_blocking=True)
+
+    def replay(self) -> torch.Tensor:
+        """Replay on the current stream with the staged input; returns the static output."""
         self.graph.replay()
         return self.out
