@@ -132,6 +132,48 @@ def _events(torch):
     return torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
 
 
+def _e2e_overlapped(torch, dev, caps, hx, houts, steps):
+    """ms per step of the decode sweep through captured layers with host I/O.
+
+    caps[layer][batch] are CapturedLayer graphs; step i replays layer i % len(caps)
+    for every batch.  The token batches go up from pinned host memory on one copy
+    stream, straight into the graphs' inputs, and the outputs come down on
+    another, so copies overlap the layer replays.  A layer's graphs are reused
+    every len(caps) steps; their buffers are staged and replayed again only
+    after the previous use's output copies are done, and every output copy is
+    inside the timed region."""
+    n_layers = len(caps)
+    main = torch.cuda.current_stream(dev)
+    cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ev_in = [torch.cuda.Event() for _ in hx]
+    ev_g = [torch.cuda.Event() for _ in hx]
+    layer_free = [torch.cuda.Event() for _ in range(n_layers)]
+    for ev in layer_free:
+        ev.record(main)
+    s4, e4 = _events(torch)
+    s4.record()
+    for i in range(steps):
+        li = i % n_layers
+        cs_in.wait_event(layer_free[li])
+        with torch.cuda.stream(cs_in):
+            for b in range(len(hx)):
+                caps[li][b].stage(hx[b])
+                ev_in[b].record(cs_in)
+        main.wait_event(layer_free[li])
+        for b in range(len(hx)):
+            main.wait_event(ev_in[b])
+            y = caps[li][b].replay()
+            ev_g[b].record(main)
+            cs_out.wait_event(ev_g[b])
+            with torch.cuda.stream(cs_out):
+                houts[b].copy_(y, non_blocking=True)
+        layer_free[li].record(cs_out)
+    main.wait_stream(cs_out)
+    e4.record()
+    torch.cuda.synchronize()
+    return s4.elapsed_time(e4) / steps
+
+
 def run_ours(args, rank, world, dev):
     import torch
     import whallm_b200 as W
@@ -270,49 +312,18 @@ def run_ours(args, rank, world, dev):
         hx = [x.cpu().pin_memory() for x in xs]
         houts = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in xs]
         torch.cuda.synchronize()
-        s4, e4 = _events(torch)
-        main = torch.cuda.current_stream(dev)
         if graphed:
-            # the token batches go up on one copy stream, straight into the graphs'
-            # inputs, and the outputs come down on another, so copies overlap the
-            # layer replays; a layer's graphs are reused every n_layers steps, and
-            # their buffers are staged and replayed again only after the previous
-            # use's output copies are done
-            cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-            ev_in = [torch.cuda.Event() for _ in xs]
-            ev_g = [torch.cuda.Event() for _ in xs]
-            layer_free = [torch.cuda.Event() for _ in range(n_layers)]
-            for ev in layer_free:
-                ev.record(main)
-        s4.record()
-        for i in range(args.steps):
-            lay = layers[i % n_layers]
-            if graphed:
-                li = i % n_layers
-                capl = caps[li]
-                cs_in.wait_event(layer_free[li])
-                with torch.cuda.stream(cs_in):
-                    for b in range(len(xs)):
-                        capl[b].stage(hx[b])
-                        ev_in[b].record(cs_in)
-                main.wait_event(layer_free[li])
+            ms_e2e = _e2e_overlapped(torch, dev, caps, hx, houts, args.steps)
+        else:
+            s4, e4 = _events(torch)
+            s4.record()
+            for i in range(args.steps):
+                lay = layers[i % n_layers]
                 for b in range(len(xs)):
-                    main.wait_event(ev_in[b])
-                    y = capl[b].replay()
-                    ev_g[b].record(main)
-                    cs_out.wait_event(ev_g[b])
-                    with torch.cuda.stream(cs_out):
-                        houts[b].copy_(y, non_blocking=True)
-                layer_free[li].record(cs_out)
-                continue
-            for b in range(len(xs)):
-                y = lay.layer(hx[b].to(dev, non_blocking=True))
-                houts[b].copy_(y, non_blocking=True)
-        if graphed:
-            main.wait_stream(cs_out)                     # every output copy is inside the timed region
-        e4.record()
-        torch.cuda.synchronize()
-        ms_e2e = s4.elapsed_time(e4) / args.steps
+                    houts[b].copy_(lay.layer(hx[b].to(dev, non_blocking=True)), non_blocking=True)
+            e4.record()
+            torch.cuda.synchronize()
+            ms_e2e = s4.elapsed_time(e4) / args.steps
         h2d = sum(x.numel() * 2 for x in xs)
         flops = sum(B * (cfg["k"] + (1 if cfg["shared"] else 0)) * 6 * cfg["H"] * cfg["I"] for B in batches)
         res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=tokens_per_step, alg_bytes=sum(alg_bytes),
@@ -696,15 +707,17 @@ def run_ep(args, rank, world, dev):
     hx = [x.cpu().pin_memory() for x in xs]
     houts = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in xs]
     torch.cuda.synchronize()
-    s4, e4 = _events(torch)
-    s4.record()
-    for i in range(args.steps):
-        for b in range(len(xs)):
-            houts[b].copy_(call(i % n_layers, b, hx[b] if decode else hx[b].to(dev, non_blocking=True)),
-                           non_blocking=True)
-    e4.record()
-    torch.cuda.synchronize()
-    ms_e2e = s4.elapsed_time(e4) / args.steps
+    if decode:
+        ms_e2e = _e2e_overlapped(torch, dev, caps, hx, houts, args.steps)
+    else:
+        s4, e4 = _events(torch)
+        s4.record()
+        for i in range(args.steps):
+            for b in range(len(xs)):
+                houts[b].copy_(call(i % n_layers, b, hx[b].to(dev, non_blocking=True)), non_blocking=True)
+        e4.record()
+        torch.cuda.synchronize()
+        ms_e2e = s4.elapsed_time(e4) / args.steps
     if decode:
         del caps           # graphs holding NCCL work go before the process group
         torch.cuda.synchronize()
