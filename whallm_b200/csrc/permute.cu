@@ -113,6 +113,11 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
     int3 base = make_int3(0, 0, 0);
     for (int w = 0; w < warp; ++w) { base.x += wsum[w].x; base.y += wsum[w].y; base.z += wsum[w].z; }
     int run = base.x + inc.x - mine.x, na = base.y + inc.y - mine.y, nt = base.z + inc.z - mine.z;
+    // The shared expert (the last id) has a slot for every token, so its tiles are
+    // the widest: they go first in the work list, where their longer epilogues
+    // overlap other tiles' work instead of ending the launch.  Only the order of
+    // the list changes; every tile is computed the same way wherever it sits.
+    const int sh_tiles = (tiles && shared_expert == E - 1) ? (tot[E - 1] + tile_n - 1) / tile_n : 0;
     __syncthreads();  // every thread has read tot[] for its experts before it is overwritten below
     for (int e = e0; e < e1; ++e) {
       const int c = tot[e];
@@ -122,8 +127,15 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
         if (active) active[na] = e;
         ++na;
       }
-      if (tiles)
-        for (int q = 0; q < c; q += tile_n) tiles[nt++] = make_int4(e, run + q, min(tile_n, c - q), 0);
+      if (tiles) {
+        if (e == shared_expert && sh_tiles > 0) {      // the last expert: nt counts every other tile
+          int at = 0;
+          for (int q = 0; q < c; q += tile_n) tiles[at++] = make_int4(e, run + q, min(tile_n, c - q), 0);
+          nt += sh_tiles;
+        } else {
+          for (int q = 0; q < c; q += tile_n) tiles[sh_tiles + nt++] = make_int4(e, run + q, min(tile_n, c - q), 0);
+        }
+      }
       run += c;
     }
     if (threadIdx.x == blockDim.x - 1) {
