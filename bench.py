@@ -188,6 +188,8 @@ def run_ours(args, rank, world, dev):
     res = {}
     if wl in ("ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny"):
         name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn", "tiny": "tiny"}[wl]
+        if name == "tiny":
+            n_layers = max(n_layers, 12)     # 14.2 MB of experts per layer: 12 layers exceed L2
         layers = [S.make_layer(name, dev, seed=1000 * rank + 17 * i, E=args.experts) for i in range(n_layers)]
         cfg = layers[0].cfg
         H = cfg["H"]
@@ -222,10 +224,11 @@ def run_ours(args, rank, world, dev):
             return X.experts_forward(x, idx, layers[li].experts, weights=w, shared_expert=shared_id, shared_w=sw,
                                      swiglu_limit=limit)
 
-        graphed = wl in ("ds_decode", "qn_decode")
+        graphed = wl in ("ds_decode", "qn_decode", "tiny")
         if graphed:
-            # decode: one CUDA graph per (layer, batch) for the whole layer and for
-            # the expert call alone (launch overhead exceeds the work at B = 1)
+            # decode (and the 64-token tiny layer): one CUDA graph per (layer, batch)
+            # for the whole layer and for the expert call alone (launch overhead
+            # exceeds the work)
             caps = [[CapturedLayer(lay.layer, x) for x in xs] for lay in layers]
             ecaps = [[CapturedLayer(lambda xx, li=li, b=b: experts_call(li, b, xx), x) for b, x in enumerate(xs)]
                      for li in range(n_layers)]
@@ -331,7 +334,8 @@ def run_ours(args, rank, world, dev):
                         per_b=per_b, clocks=clocks, h2d=h2d, d2h=h2d, cfg=cfg, batches=batches,
                         distinct=distinct, hbm=hbm, peak_src=peak_src,
                         launches=len(xs) * (2 + 5) if name != "tiny" else len(xs) * (2 + 4),
-                        graphed=graphed))
+                        graphed=graphed, n_layers=n_layers,
+                        layer_bytes=(cfg["E"] + (1 if cfg["shared"] else 0)) * expert_bytes))
         return res
     if wl == "kv_scores":
         # decode scores of one query per sequence against an MXFP8 latent cache:
@@ -976,8 +980,10 @@ def main():
             torch.distributed.destroy_process_group()
             return
         config = {"workload": args.workload, "batches": list(r["batches"]),
-                  "tokens_per_step": r["tokens"], "layers_cycled": args.layers,
-                  "l2": "8 resident layers (48 GB) cycled per step: weights larger than L2",
+                  "tokens_per_step": r["tokens"], "layers_cycled": r.get("n_layers", args.layers),
+                  "l2": (f"{r.get('n_layers', args.layers)} resident layers "
+                         f"({r.get('n_layers', args.layers) * r.get('layer_bytes', 0) / 1e9:.2f} GB of experts) "
+                         "cycled per step: weights larger than L2"),
                   "parallelism": "replicas" if world > 1 else "single GPU",
                   "launch": "CUDA graph per (layer, batch)" if r.get("graphed") else "eager",
                   "per_batch": r["per_b"]}

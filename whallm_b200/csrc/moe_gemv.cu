@@ -94,12 +94,54 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 #pragma unroll
         for (int t = 0; t < kNT; ++t) acc[r][t] = 0.0f;
       for (int q = lane; q < groups; q += 32) {
-        uint4 wq[kRowsPerWarp];
+        // Eight values at a time: one 16-byte load of x per token, each row's
+        // eight weights decoded once and used by every token of the pass.  Per
+        // (row, token) the products are still added in element order 0..31.
+        float part[kRowsPerWarp][kNT], sx[kNT];
+#pragma unroll
+        for (int t = 0; t < kNT; ++t) {
+          sx[t] = 0.0f;
+#pragma unroll
+          for (int r = 0; r < kRowsPerWarp; ++r) part[r][t] = 0.0f;
+        }
+#pragma unroll
+        for (int i0 = 0; i0 < 4; ++i0) {
+          float xv[kNT][8];
+#pragma unroll
+          for (int t = 0; t < kNT; ++t) {
+            // rows past nt repeat the last token (src clamps), their sums are never stored
+            const uint4 u = __ldg(reinterpret_cast<const uint4 *>(src[t] + q * 32) + i0);
+            xv[t][0] = wm_bf16lo(u.x); xv[t][1] = wm_bf16hi(u.x);
+            xv[t][2] = wm_bf16lo(u.y); xv[t][3] = wm_bf16hi(u.y);
+            xv[t][4] = wm_bf16lo(u.z); xv[t][5] = wm_bf16hi(u.z);
+            xv[t][6] = wm_bf16lo(u.w); xv[t][7] = wm_bf16hi(u.w);
+            if (FMT == kFmtAffine4) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i) sx[t] += xv[t][i];
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < kRowsPerWarp; ++r) {
+            // 4 bytes of the row's 16-byte group per step (the first load brings the group into L1)
+            const uint32_t wd =
+                __ldg(reinterpret_cast<const uint32_t *>(W.w + (erow0 + row[r]) * row_bytes) + q * 4 + i0);
+            float wv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const uint32_t nib = (wd >> (4 * i)) & 15u;
+              if (FMT == kFmtMxfp4) wv[i] = wm_e2m1_scaled(nib);
+              else wv[i] = __uint_as_float(0x4B000000u | nib) - 8388608.0f;
+            }
+#pragma unroll
+            for (int t = 0; t < kNT; ++t)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) part[r][t] = fmaf(xv[t][i], wv[i], part[r][t]);
+          }
+        }
         float sc[kRowsPerWarp], bi[kRowsPerWarp];
 #pragma unroll
         for (int r = 0; r < kRowsPerWarp; ++r) {
           const int64_t gr = erow0 + row[r];
-          wq[r] = __ldg(reinterpret_cast<const uint4 *>(W.w + gr * row_bytes) + q);
           if (FMT == kFmtMxfp4) {
             sc[r] = wm_e8m0(W.s[gr * groups + q]);
             bi[r] = 0.0f;
@@ -113,35 +155,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 #pragma unroll
         for (int t = 0; t < kNT; ++t) {
           if (t < nt) {
-            const uint4 *xp = reinterpret_cast<const uint4 *>(src[t] + q * 32);
-            float xv[32];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              uint4 u = __ldg(xp + i);
-              xv[8 * i + 0] = wm_bf16lo(u.x); xv[8 * i + 1] = wm_bf16hi(u.x);
-              xv[8 * i + 2] = wm_bf16lo(u.y); xv[8 * i + 3] = wm_bf16hi(u.y);
-              xv[8 * i + 4] = wm_bf16lo(u.z); xv[8 * i + 5] = wm_bf16hi(u.z);
-              xv[8 * i + 6] = wm_bf16lo(u.w); xv[8 * i + 7] = wm_bf16hi(u.w);
-            }
-            float sx = 0.0f;
-            if (FMT == kFmtAffine4) {
-#pragma unroll
-              for (int i = 0; i < 32; ++i) sx += xv[i];
-            }
 #pragma unroll
             for (int r = 0; r < kRowsPerWarp; ++r) {
-              const uint32_t wd[4] = {wq[r].x, wq[r].y, wq[r].z, wq[r].w};
-              float part = 0.0f;
-#pragma unroll
-              for (int i = 0; i < 32; ++i) {
-                const uint32_t nib = (wd[i >> 3] >> (4 * (i & 7))) & 15u;
-                float wv;
-                if (FMT == kFmtMxfp4) wv = wm_e2m1_scaled(nib);
-                else wv = __uint_as_float(0x4B000000u | nib) - 8388608.0f;
-                part = fmaf(xv[i], wv, part);
-              }
-              if (FMT == kFmtMxfp4) acc[r][t] = fmaf(part * 0x1p126f, sc[r], acc[r][t]);
-              else acc[r][t] = fmaf(part, sc[r], fmaf(sx, bi[r], acc[r][t]));
+              if (FMT == kFmtMxfp4) acc[r][t] = fmaf(part[r][t] * 0x1p126f, sc[r], acc[r][t]);
+              else acc[r][t] = fmaf(part[r][t], sc[r], fmaf(sx[t], bi[r], acc[r][t]));
             }
           }
         }
