@@ -163,45 +163,45 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
           }
         }
       }
+      // Warp sums of the 16 (row, token) partials by a transposed butterfly:
+      // each xor step halves the values a lane carries (16 shuffles instead of
+      // 80), and every sum is built from the same pairs in the same order as a
+      // full butterfly, so the results are the same bits.  Afterwards lanes l
+      // and l ^ 1 hold the sum for row (l >> 3) & 3, token (l >> 1) & 3.
+      static_assert(kRowsPerWarp * kNT == 16, "transposed reduction of 16 sums");
+      float v[16];
 #pragma unroll
       for (int r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll
-        for (int t = 0; t < kNT; ++t) {
-          float v = acc[r][t];
+        for (int t = 0; t < kNT; ++t) v[r * kNT + t] = acc[r][t];
 #pragma unroll
-          for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
-          acc[r][t] = v;
+      for (int m = 16, h = 8; m >= 2; m >>= 1, h >>= 1) {
+        const bool hi = (lane & m) != 0;
+#pragma unroll
+        for (int i = 0; i < h; ++i) {
+          const float send = hi ? v[i] : v[i + h];
+          const float keep = hi ? v[i + h] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
         }
+      }
+      const float sum = v[0] + __shfl_xor_sync(0xffffffffu, v[0], 1);
+      const int r_l = (lane >> 3) & 3, t_l = (lane >> 1) & 3;
       if (MODE == kModeUp) {
-        // lane (jj * kNT + t) finishes intermediate j0 + jj for token t
-        if (lane < 2 * kNT) {
-          const int jj = lane / kNT, t = lane % kNT;
-          if (t < nt) {
-            float up = 0.f, gate = 0.f;
-#pragma unroll
-            for (int q = 0; q < 2; ++q)
-#pragma unroll
-              for (int tt = 0; tt < kNT; ++tt)
-                if (q == jj && tt == t) { up = acc[2 * q][tt]; gate = acc[2 * q + 1][tt]; }
-            if (limit > 0.0f) {
-              up = fminf(fmaxf(up, -limit), limit);
-              gate = fminf(gate, limit);
-            }
-            h_out[static_cast<int64_t>(p0 + c + t) * I + j0 + jj] = wm_f32_to_bf16(silu_f32(gate) * up);
+        // rows are (up j0, gate j0, up j0+1, gate j0+1): the gate sum is 8 lanes up
+        const float gate_sum = __shfl_xor_sync(0xffffffffu, sum, 8);
+        if ((lane & 9) == 0 && t_l < nt) {
+          const int jj = r_l >> 1;
+          float up = sum, gate = gate_sum;
+          if (limit > 0.0f) {
+            up = fminf(fmaxf(up, -limit), limit);
+            gate = fminf(gate, limit);
           }
+          h_out[static_cast<int64_t>(p0 + c + t_l) * I + j0 + jj] = wm_f32_to_bf16(silu_f32(gate) * up);
         }
       } else {
-        if (lane < kRowsPerWarp * kNT) {
-          const int r = lane / kNT, t = lane % kNT;
-          if (t < nt) {
-            float v = 0.f;
-#pragma unroll
-            for (int rr = 0; rr < kRowsPerWarp; ++rr)
-#pragma unroll
-              for (int tt = 0; tt < kNT; ++tt)
-                if (rr == r && tt == t) v = acc[rr][tt];
-            y_out[static_cast<int64_t>(p0 + c + t) * W.rows + row[r]] = wm_f32_to_bf16(v);
-          }
+        if ((lane & 1) == 0 && t_l < nt) {
+          const int rw = r_l == 0 ? row[0] : r_l == 1 ? row[1] : r_l == 2 ? row[2] : row[3];
+          y_out[static_cast<int64_t>(p0 + c + t_l) * W.rows + rw] = wm_f32_to_bf16(sum);
         }
       }
     }
