@@ -49,6 +49,29 @@ struct Weights {
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
+// Two fp32 lanes per instruction (sm_100 packed FMA / add): each lane is
+// rounded exactly like fmaf / a scalar add, so the results are the same bits.
+__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_of(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_of(r);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_of(r);
+}
+
 template <int FMT, int MODE>
 __global__ void __launch_bounds__(kWarps * 32, 2)
     k_expert_gemv(const uint16_t *__restrict__ in, int kk, const int32_t *__restrict__ offsets,
@@ -97,12 +120,14 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
         // Eight values at a time: one 16-byte load of x per token, each row's
         // eight weights decoded once and used by every token of the pass.  Per
         // (row, token) the products are still added in element order 0..31.
-        float part[kRowsPerWarp][kNT], sx[kNT];
+        // token pairs share one packed instruction: part2[r][tp] = {token 2 tp, token 2 tp + 1}
+        constexpr int kNP = kNT / 2;
+        float2 part2[kRowsPerWarp][kNP], sx2[kNP];
 #pragma unroll
-        for (int t = 0; t < kNT; ++t) {
-          sx[t] = 0.0f;
+        for (int tp = 0; tp < kNP; ++tp) {
+          sx2[tp] = make_float2(0.0f, 0.0f);
 #pragma unroll
-          for (int r = 0; r < kRowsPerWarp; ++r) part[r][t] = 0.0f;
+          for (int r = 0; r < kRowsPerWarp; ++r) part2[r][tp] = make_float2(0.0f, 0.0f);
         }
 #pragma unroll
         for (int i0 = 0; i0 < 4; ++i0) {
@@ -115,10 +140,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
             xv[t][2] = wm_bf16lo(u.y); xv[t][3] = wm_bf16hi(u.y);
             xv[t][4] = wm_bf16lo(u.z); xv[t][5] = wm_bf16hi(u.z);
             xv[t][6] = wm_bf16lo(u.w); xv[t][7] = wm_bf16hi(u.w);
-            if (FMT == kFmtAffine4) {
+          }
+          if (FMT == kFmtAffine4) {
 #pragma unroll
-              for (int i = 0; i < 8; ++i) sx[t] += xv[t][i];
-            }
+            for (int tp = 0; tp < kNP; ++tp)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) sx2[tp] = add2(sx2[tp], make_float2(xv[2 * tp][i], xv[2 * tp + 1][i]));
           }
 #pragma unroll
           for (int r = 0; r < kRowsPerWarp; ++r) {
@@ -133,9 +160,22 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
               else wv[i] = __uint_as_float(0x4B000000u | nib) - 8388608.0f;
             }
 #pragma unroll
-            for (int t = 0; t < kNT; ++t)
+            for (int tp = 0; tp < kNP; ++tp)
 #pragma unroll
-              for (int i = 0; i < 8; ++i) part[r][t] = fmaf(xv[t][i], wv[i], part[r][t]);
+              for (int i = 0; i < 8; ++i)
+                part2[r][tp] = fma2(make_float2(xv[2 * tp][i], xv[2 * tp + 1][i]), make_float2(wv[i], wv[i]),
+                                    part2[r][tp]);
+          }
+        }
+        float part[kRowsPerWarp][kNT], sx[kNT];
+#pragma unroll
+        for (int tp = 0; tp < kNP; ++tp) {
+          sx[2 * tp] = sx2[tp].x;
+          sx[2 * tp + 1] = sx2[tp].y;
+#pragma unroll
+          for (int r = 0; r < kRowsPerWarp; ++r) {
+            part[r][2 * tp] = part2[r][tp].x;
+            part[r][2 * tp + 1] = part2[r][tp].y;
           }
         }
         float sc[kRowsPerWarp], bi[kRowsPerWarp];
