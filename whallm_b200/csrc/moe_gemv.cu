@@ -116,10 +116,16 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       for (int r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll
         for (int t = 0; t < kNT; ++t) acc[r][t] = 0.0f;
-      for (int q = lane; q < groups; q += 32) {
+      // Rows shorter than 32 groups (K < 1024) give each group to lpg lanes,
+      // each taking 32 / lpg of its values, so no lane idles; the partial sums
+      // meet in the warp reduction below.
+      const int lpg = groups >= 32 ? 1 : min(4, 32 / groups);
+      const int nseg = 4 / lpg;                            // 8-value steps per lane
+      for (int qq = lane; qq < groups * lpg; qq += 32) {
+        const int q = qq / lpg, seg = qq - q * lpg;
         // Eight values at a time: one 16-byte load of x per token, each row's
         // eight weights decoded once and used by every token of the pass.  Per
-        // (row, token) the products are still added in element order 0..31.
+        // (row, token) the products are added in element order.
         // token pairs share one packed instruction: part2[r][tp] = {token 2 tp, token 2 tp + 1}
         constexpr int kNP = kNT / 2;
         float2 part2[kRowsPerWarp][kNP], sx2[kNP];
@@ -130,7 +136,9 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
           for (int r = 0; r < kRowsPerWarp; ++r) part2[r][tp] = make_float2(0.0f, 0.0f);
         }
 #pragma unroll
-        for (int i0 = 0; i0 < 4; ++i0) {
+        for (int s8 = 0; s8 < 4; ++s8) {
+          if (s8 >= nseg) break;
+          const int i0 = seg * nseg + s8;
           float xv[kNT][8];
 #pragma unroll
           for (int t = 0; t < kNT; ++t) {
