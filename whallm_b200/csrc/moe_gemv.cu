@@ -13,11 +13,11 @@
 //   * Work item = (active expert, block of rows).  A persistent grid walks the
 //     items; the list of active experts comes from the permute kernel, so
 //     idle experts cost nothing.
-//   * Each warp owns 4 weight rows.  Lane l reads 16 bytes (32 FP4 values =
-//     one scale group) of each row per step, i.e. 128-bit coalesced loads of
-//     512 contiguous bytes per row per warp instruction; the same x chunk is
-//     reused for the 4 rows.
-//   * Per-lane partial sums are reduced with a warp-shuffle butterfly.
+//   * Each warp owns 4 weight rows and takes 4 tokens per pass.  Lane l covers
+//     one 32-value scale group of each row (rows under 1024 values: part of a
+//     group), eight values at a time: the eight weights are decoded once for
+//     the 4 tokens, and token pairs share packed f32x2 FMAs.
+//   * Per-lane partial sums are reduced with a transposed warp butterfly.
 //   * Phase "up": rows are (up_j, gate_j, up_j+1, gate_j+1) of w13, so the
 //     fused ClampedSwiGLU runs in the epilogue and writes h (bf16) directly.
 //   * Phase "down": rows of w2 over h; outputs y (f32) in sorted-slot order.
@@ -124,10 +124,11 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       for (int qq = lane; qq < groups * lpg; qq += 32) {
         const int q = qq / lpg, seg = qq - q * lpg;
         // Eight values at a time: one 16-byte load of x per token, each row's
-        // eight weights decoded once and used by every token of the pass.  Per
-        // (row, token) the products are added in element order.
-        // token pairs share one packed instruction: part2[r][tp] = {token 2 tp, token 2 tp + 1}
+        // eight weights decoded once and used by every token of the pass, two
+        // tokens per packed instruction (part2[r][tp] = {token 2 tp, 2 tp + 1}).
+        // Per (row, token) the products are added in element order.
         constexpr int kNP = kNT / 2;
+        static_assert(kNT % 2 == 0, "tokens go in pairs");
         float2 part2[kRowsPerWarp][kNP], sx2[kNP];
 #pragma unroll
         for (int tp = 0; tp < kNP; ++tp) {
