@@ -80,9 +80,10 @@ def test_block_scaled_layer_vs_oracle(dev, name, T, E, H, I):
     assert err < TOL, err
 
 
-@pytest.mark.parametrize("T", [4, 64, 300])
-def test_block_scaled_agrees_with_f16_and_cuda_core_paths(dev, T):
-    lay = S.make_layer("ds", dev, seed=7, E=16, H=1024, I=512)
+@pytest.mark.parametrize("T,I", [(4, 512), (64, 512), (300, 512), (9, 256)])
+def test_block_scaled_agrees_with_f16_and_cuda_core_paths(dev, T, I):
+    # I = 256: the CUDA-core down projection has 8 scale groups per row, each split over 4 lanes
+    lay = S.make_layer("ds", dev, seed=7, E=16, H=1024, I=I)
     x = S.make_tokens(T, 1024, 3, dev)
     a = _with_path(None, lambda: lay.layer(x)).float().cpu().numpy()
     b = _with_path("f16", lambda: lay.layer(x)).float().cpu().numpy()
