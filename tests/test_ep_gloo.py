@@ -210,7 +210,9 @@ def _dying_worker(rank, world, port, result_q):
         result_q.put((rank, "error: " + type(exc).__name__))
 
 
-def _spawn(fn, world=2, timeout=120):
+def _spawn(fn, world=2, timeout=600):
+    # generous: on a freshly started machine the spawned ranks' first imports of
+    # torch and the library can take minutes; a healthy run returns in seconds
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -269,7 +271,7 @@ def test_balanced_placement_properties():
 
 
 def test_rank_leaving_surfaces_as_collective_error():
-    res = _spawn(_dying_worker, timeout=90)
+    res = _spawn(_dying_worker)
     assert res[1][1] == "left"
     assert res[0][1].startswith("error"), res
 
