@@ -49,29 +49,6 @@ struct Weights {
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
-// Two fp32 lanes per instruction (sm_100 packed FMA / add): each lane is
-// rounded exactly like fmaf / a scalar add, so the results are the same bits.
-__device__ __forceinline__ unsigned long long f2_bits(float2 v) {
-  unsigned long long r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
-  return r;
-}
-__device__ __forceinline__ float2 f2_of(unsigned long long r) {
-  float2 v;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
-  return v;
-}
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-  unsigned long long r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
-  return f2_of(r);
-}
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-  unsigned long long r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(f2_bits(a)), "l"(f2_bits(b)));
-  return f2_of(r);
-}
-
 template <int FMT, int MODE>
 __global__ void __launch_bounds__(kWarps * 32, 2)
     k_expert_gemv(const uint16_t *__restrict__ in, int kk, const int32_t *__restrict__ offsets,
@@ -154,7 +131,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 #pragma unroll
             for (int tp = 0; tp < kNP; ++tp)
 #pragma unroll
-              for (int i = 0; i < 8; ++i) sx2[tp] = add2(sx2[tp], make_float2(xv[2 * tp][i], xv[2 * tp + 1][i]));
+              for (int i = 0; i < 8; ++i) sx2[tp] = wm_add2(sx2[tp], make_float2(xv[2 * tp][i], xv[2 * tp + 1][i]));
           }
 #pragma unroll
           for (int r = 0; r < kRowsPerWarp; ++r) {
@@ -172,7 +149,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
             for (int tp = 0; tp < kNP; ++tp)
 #pragma unroll
               for (int i = 0; i < 8; ++i)
-                part2[r][tp] = fma2(make_float2(xv[2 * tp][i], xv[2 * tp + 1][i]), make_float2(wv[i], wv[i]),
+                part2[r][tp] = wm_fma2(make_float2(xv[2 * tp][i], xv[2 * tp + 1][i]), make_float2(wv[i], wv[i]),
                                     part2[r][tp]);
           }
         }

@@ -81,6 +81,29 @@ __device__ __forceinline__ uint16_t wm_f32_to_bf16(float f) {
 }
 
 // Two bf16 packed in a uint32 (element 0 low) -> floats.
+// Two fp32 lanes per instruction (sm_100 packed FMA / add): each lane is
+// rounded exactly like fmaf / a scalar add, so the results are the same bits.
+__device__ __forceinline__ unsigned long long wm_f2_bits(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 wm_f2_of(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 wm_fma2(float2 a, float2 b, float2 c) {
+  unsigned long long r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(wm_f2_bits(a)), "l"(wm_f2_bits(b)), "l"(wm_f2_bits(c)));
+  return wm_f2_of(r);
+}
+__device__ __forceinline__ float2 wm_add2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(wm_f2_bits(a)), "l"(wm_f2_bits(b)));
+  return wm_f2_of(r);
+}
+
 __device__ __forceinline__ float wm_bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float wm_bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
