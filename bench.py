@@ -847,11 +847,11 @@ def cpu_reference(args, sample_steps=None):
                                            route_scale=1.5)
                     M.moe_forward(x, idx, w, ex, shared_expert=E)
                 elif name == "qn":
-                    _, idx, w, sh = R.route(xb, wg, k, R.SCORE_SOFTMAX, logit_bias=lb, norm_eps=0.0,
+                    _, idx, w, sh = R.route(xb, wg, k, R.SCORE_SOFTMAX_BF16, logit_bias=lb, norm_eps=0.0,
                                             wg_shared_bits=sg)
                     M.moe_forward(x, idx, w, ex, shared_expert=E, shared_weight=sh)
                 else:
-                    _, idx, w, _ = R.route(xb, wg, k, R.SCORE_SOFTMAX, norm_eps=0.0)
+                    _, idx, w, _ = R.route(xb, wg, k, R.SCORE_SOFTMAX_BF16, norm_eps=0.0)
                     M.moe_forward(x, idx, w, ex)
 
         tokens = sum(batches)

@@ -57,6 +57,11 @@ typedef uint16_t wm_bf16;
 #define WM_SCORE_SIGMOID 1
 #define WM_SCORE_SQRTSOFTPLUS 2
 #define WM_SCORE_NONE 3
+/* The Qwen gate in the reference's dtypes (qwen4_exp.py:683, 693-699): logits
+ * rounded to bf16 (a bf16 nn.Linear), softmax(precise=True) in float32 rounded
+ * to bf16, top-k on the bf16 probabilities, renormalised as bf16(p / bf16(sum)),
+ * shared-expert gate bf16(sigmoid(bf16(logit))). */
+#define WM_SCORE_SOFTMAX_BF16 4
 
 /* Order of the fused gate/up projection rows. */
 #define WM_UP_GATE 0 /* DeepSeek w13 = [w3(up); w1(gate)]  (expert_layout.py:43-60, model.py:417) */
@@ -236,7 +241,8 @@ WM_API int wkv_gather_dequantize(const uint8_t *payload, const void *scales, int
 
 /* Gate logits, scores, top-k and weights for T tokens.
  *   logits[t,e] = x[t].wg[e] (float32, fixed order) + logit_bias[e] (if given)
- *   score       = score_fn(logits)           (softmax over E, sigmoid, sqrt(softplus), none)
+ *   score       = score_fn(logits)           (softmax over E, sigmoid, sqrt(softplus), none,
+ *                                             or WM_SCORE_SOFTMAX_BF16: the bf16 gate above)
  *   selection   = top-k of score + select_bias (bias picks, does not scale;
  *                 deepseek_v41/moe.py:67-70), ties to the lower expert id
  *                 (model.py:548-560); idx is in selection order

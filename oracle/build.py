@@ -26,7 +26,7 @@ def build(force: bool = False) -> str:
     os.makedirs(tmp, exist_ok=True)
     objs = []
     flags = {
-        "router_ref.c": ["-O2", "-ffp-contract=off", "-fno-fast-math"],
+        "router_ref.c": ["-O2", "-ffp-contract=off", "-fno-fast-math", "-mfma", "-fopenmp"],
         "moe_ref.c": ["-O3", "-mavx2", "-mfma", "-ffast-math", "-fopenmp"],
     }
     for s in srcs:

@@ -10,6 +10,14 @@
  *   ties resolved by expert position                     model.py:548-560
  *   renormalise by (sum + eps), times route_scale        deepseek_v41/moe.py:71-73
  *   Qwen: renormalise by sum (eps 0), no scale           qwen4_exp.py:693-697
+ *   Qwen gate dtypes (score function SOFTMAX_BF16): the gate is a bf16
+ *     nn.Linear, so its logits are rounded to bf16          qwen4_exp.py:683
+ *     softmax(precise=True): float32 math, bf16 result     qwen4_exp.py:693
+ *     top-k on the bf16 probabilities                      qwen4_exp.py:694-695
+ *     scores / scores.sum(): bf16 sum, bf16 quotient       qwen4_exp.py:696-697
+ *     shared gate sigmoid(bf16 logit) in bf16              qwen4_exp.py:699
+ *     (every rounding to nearest even; the sum is taken in float32 in
+ *     selection order and rounded once)
  *
  * The reference computes these with MLX kernels whose reduction order is not
  * specified.  To compare routing indices exactly, this oracle and the device
@@ -25,7 +33,8 @@
  *     part) with the Taylor series of exp truncated after r^7/7!, and
  *     log(m) = 2 atanh((m-1)/(m+1)) truncated after s^13/13; log1p uses
  *     Goldberg's log(1+y) = log(u) * y / (u-1) with u = 1+y.
- * Compile with -ffp-contract=off so that only the explicit fmaf calls fuse.
+ * Compile with -ffp-contract=off so that only the explicit fmaf calls fuse
+ * (with -mfma they are single fused instructions, the same IEEE operation).
  */
 #include <math.h>
 #include <stdint.h>
@@ -39,6 +48,14 @@
 static inline float bits_f(uint32_t b) { float f; memcpy(&f, &b, 4); return f; }
 static inline uint32_t f_bits(float f) { uint32_t b; memcpy(&b, &f, 4); return b; }
 static inline float bf16f(uint16_t b) { return bits_f(((uint32_t)b) << 16); }
+
+/* float32 -> nearest bf16 (ties to even), returned as float32 */
+static inline float round_bf16(float f) {
+  uint32_t u = f_bits(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return bits_f(0x7fc00000u);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return bits_f(u & 0xffff0000u);
+}
 
 float oracle_exp(float x) {
   if (x != x) return x;
@@ -128,21 +145,23 @@ float oracle_dot_bf16(const uint16_t *x, const uint16_t *w, int H) {
   return butterfly32(part);
 }
 
-enum { SCORE_SOFTMAX = 0, SCORE_SIGMOID = 1, SCORE_SQRTSOFTPLUS = 2, SCORE_NONE = 3 };
+enum { SCORE_SOFTMAX = 0, SCORE_SIGMOID = 1, SCORE_SQRTSOFTPLUS = 2, SCORE_NONE = 3, SCORE_SOFTMAX_BF16 = 4 };
 
 /* Scores and top-k for one token from its E logits (already biased). */
 static void topk_one(const float *logit, int E, int k, int score_fn, const float *select_bias,
                      float norm_eps, float route_scale, float *score, int32_t *idx, float *wout) {
-  if (score_fn == SCORE_SOFTMAX) {
+  const int bf = score_fn == SCORE_SOFTMAX_BF16;
+  if (score_fn == SCORE_SOFTMAX || bf) {
     float mx = -INFINITY;
-    for (int e = 0; e < E; ++e) mx = fmaxf(mx, logit[e]);
+    for (int e = 0; e < E; ++e) score[e] = bf ? round_bf16(logit[e]) : logit[e];
+    for (int e = 0; e < E; ++e) mx = fmaxf(mx, score[e]);
     float part[32];
     for (int l = 0; l < 32; ++l) part[l] = 0.0f;
-    for (int e = 0; e < E; ++e) score[e] = oracle_exp(logit[e] - mx);
+    for (int e = 0; e < E; ++e) score[e] = oracle_exp(score[e] - mx);
     for (int l = 0; l < 32; ++l)
       for (int e = l; e < E; e += 32) part[l] = part[l] + score[e];
     float sum = butterfly32(part);
-    for (int e = 0; e < E; ++e) score[e] = score[e] / sum;
+    for (int e = 0; e < E; ++e) score[e] = bf ? round_bf16(score[e] / sum) : score[e] / sum;
   } else if (score_fn == SCORE_SIGMOID) {
     for (int e = 0; e < E; ++e) score[e] = 1.0f / (1.0f + oracle_exp(-logit[e]));
   } else if (score_fn == SCORE_SQRTSOFTPLUS) {
@@ -169,7 +188,8 @@ static void topk_one(const float *logit, int E, int k, int score_fn, const float
     float s = 0.0f;
     for (int j = 0; j < k; ++j) s = s + wout[j];
     s = s + norm_eps;
-    for (int j = 0; j < k; ++j) wout[j] = wout[j] / s;
+    if (bf) s = round_bf16(s);
+    for (int j = 0; j < k; ++j) wout[j] = bf ? round_bf16(wout[j] / s) : wout[j] / s;
   }
   for (int j = 0; j < k; ++j) wout[j] = wout[j] * route_scale;
 }
@@ -185,8 +205,11 @@ int oracle_router(const uint16_t *x, const uint16_t *wg, const float *logit_bias
                   float norm_eps, float route_scale, const uint16_t *wg_shared,
                   float *logits, int32_t *idx, float *weights, float *shared_w) {
   if (E > 4096 || k > E || k < 1 || H % 8) return -1;
-  float score[4096];
+  /* tokens are independent: split across OpenMP threads (each token's
+   * arithmetic is unchanged) */
+#pragma omp parallel for schedule(dynamic, 4)
   for (int t = 0; t < T; ++t) {
+    float score[4096];
     const uint16_t *xt = x + (size_t)t * H;
     float *lt = logits + (size_t)t * E;
     for (int e = 0; e < E; ++e) {
@@ -197,7 +220,10 @@ int oracle_router(const uint16_t *x, const uint16_t *wg, const float *logit_bias
              idx + (size_t)t * k, weights + (size_t)t * k);
     if (wg_shared && shared_w) {
       float g = oracle_dot_bf16(xt, wg_shared, H);
-      shared_w[t] = 1.0f / (1.0f + oracle_exp(-g));
+      if (score_fn == SCORE_SOFTMAX_BF16)
+        shared_w[t] = round_bf16(1.0f / (1.0f + oracle_exp(-round_bf16(g))));
+      else
+        shared_w[t] = 1.0f / (1.0f + oracle_exp(-g));
     }
   }
   return 0;

@@ -5,7 +5,11 @@ TEST INFRASTRUCTURE ONLY (see ``oracle/__init__.py``).
 Thin ctypes wrapper over ``oracle/c/router_ref.c``, which evaluates the
 reference router (``deepseek_v41/moe.py:58-75``, ``qwen4_exp.py:693-699``,
 tie rule ``model.py:548-560``) in the fixed float32 order shared with the
-device kernel, so routing indices compare exactly.
+device kernel, so routing indices compare exactly.  ``SCORE_SOFTMAX_BF16`` is
+the Qwen gate in the reference's dtypes: bf16 logits (a bf16 ``nn.Linear``,
+``qwen4_exp.py:683``), ``softmax(precise=True)`` in float32 returned as bf16
+(``:693``), top-k on the bf16 probabilities and a bf16 renormalisation
+(``:694-697``), shared gate ``bf16(sigmoid(bf16 logit))`` (``:699``).
 """
 from __future__ import annotations
 
@@ -16,7 +20,7 @@ import numpy as np
 
 from . import build as _build
 
-SCORE_SOFTMAX, SCORE_SIGMOID, SCORE_SQRTSOFTPLUS, SCORE_NONE = 0, 1, 2, 3
+SCORE_SOFTMAX, SCORE_SIGMOID, SCORE_SQRTSOFTPLUS, SCORE_NONE, SCORE_SOFTMAX_BF16 = 0, 1, 2, 3, 4
 NO_RENORM = -1.0
 
 _lib = None

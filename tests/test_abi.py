@@ -112,3 +112,12 @@ def test_scores_and_linear_reject_bad_shapes():
     _expect("wkv_mx_scores", None, 0, 1, 512, None, None, 64, L.WKV_MXFP8_B32, None, None, 0, None)
     _expect("wkv_mx_scores", None, 1, 1, 512, None, None, 64, L.WKV_MXFP4_B32, None, None, 0, None, msg="null buffer")
     _expect("wmx_linear", None, 0, 512, None, None, 64, L.WKV_MXFP8_B32, None, None, 0, None, code=L.WM_OK)
+
+
+def test_peer_sum_rejects_misaligned_rows():
+    # wep_sum_rows reads float4 partials and writes 8-byte bf16 groups: pointers off those boundaries are
+    # rejected on the host (these addresses are never dereferenced)
+    _expect("wep_sum_rows", ctypes.c_void_p(0x10004), 2, 3, 16, None, ctypes.c_void_p(0x20000), None,
+            msg="16-byte")
+    _expect("wep_sum_rows", ctypes.c_void_p(0x10000), 2, 3, 16, None, ctypes.c_void_p(0x20004), None,
+            msg="8-byte")

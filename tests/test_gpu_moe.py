@@ -102,7 +102,7 @@ def test_qwen_sparse_moe_vs_oracle(dev):
     x = S.make_tokens(T, H, 3, dev)
     out = lay.layer(x)
     xb = F.f32_to_bf16_bits(_f32(x))
-    _, ri, rw, rsh = R.route(xb, _np(lay.gate_weight.view(torch.int16)).view(np.uint16), k, R.SCORE_SOFTMAX,
+    _, ri, rw, rsh = R.route(xb, _np(lay.gate_weight.view(torch.int16)).view(np.uint16), k, R.SCORE_SOFTMAX_BF16,
                              logit_bias=_np(lay.logit_bias), norm_eps=0.0, route_scale=1.0,
                              wg_shared_bits=_np(lay.shared_gate.view(torch.int16)).view(np.uint16).reshape(-1))
     ex = _mx_oracle(lay.experts, M.GATE_UP, 0.0)
@@ -116,7 +116,7 @@ def test_tiny_affine4_config_vs_oracle(dev):
     x = S.make_tokens(cfg["tokens"], cfg["H"], 0, dev)
     out = lay.layer(x)
     xb = F.f32_to_bf16_bits(_f32(x))
-    _, ri, rw, _ = R.route(xb, _np(lay.gate_weight.view(torch.int16)).view(np.uint16), cfg["k"], R.SCORE_SOFTMAX,
+    _, ri, rw, _ = R.route(xb, _np(lay.gate_weight.view(torch.int16)).view(np.uint16), cfg["k"], R.SCORE_SOFTMAX_BF16,
                            norm_eps=0.0)
     a = lay.experts
     bits = lambda t: _np(t.view(torch.int16)).view(np.uint16)
@@ -139,3 +139,31 @@ def test_batch_equals_tokens_one_at_a_time(dev):
     # route_reduce of the un-reduced output agrees with the fused combine
     routed_only = W.experts_forward(x, idx, lay.experts, weights=wts, swiglu_limit=10.0)
     assert M.max_rel_err(_f32(W.route_reduce(un, wts)), _f32(routed_only)) < TOL
+
+
+def _affine_oracle(a):
+    bits = lambda t: _np(t.view(torch.int16)).view(np.uint16)
+    return M.Affine4Experts(_np(a.w13).view(np.uint32), bits(a.w13_scales), bits(a.w13_biases),
+                            _np(a.w2).view(np.uint32), bits(a.w2_scales), bits(a.w2_biases), M.GATE_UP, 0.0, a.group)
+
+
+@pytest.mark.parametrize("I", [320, 288, 352])
+def test_cuda_core_rows_of_9_to_11_groups(dev, I):
+    # down rows of I values are 9-11 scale groups of 32: the CUDA-core kernel splits each group over
+    # 2 lanes there; every value of every group must be summed (I is not a multiple of 256, so both
+    # formats take the CUDA-core path)
+    T, E, k, H = 7, 6, 3, 512
+    rng = np.random.default_rng(I)
+    idx = torch.from_numpy(rng.integers(0, E, (T, k)).astype(np.int32)).to(dev)
+    w = torch.from_numpy(rng.uniform(0.1, 1.0, (T, k)).astype(np.float32)).to(dev)
+    x = S.make_tokens(T, H, I, dev)
+    if I % 64 == 0:
+        ex = S.make_affine4_experts(E, H, I, seed=I, device=dev)
+        oracle = _affine_oracle(ex)
+        out = W.experts_forward(x, idx, ex, weights=w)
+    else:
+        ex = S.make_mxfp4_experts(E, H, I, seed=I, device=dev)
+        oracle = _mx_oracle(ex, M.UP_GATE, 10.0)
+        out = W.experts_forward(x, idx, ex, weights=w, swiglu_limit=10.0)
+    ref = M.moe_forward(_f32(x), _np(idx), _np(w), oracle)
+    assert M.max_rel_err(_f32(out), ref) < TOL

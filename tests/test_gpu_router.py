@@ -17,7 +17,8 @@ from oracle import router as R
 
 pytestmark = pytest.mark.gpu
 GOLD = os.path.join(os.path.dirname(__file__), "golden")
-FN = {R.SCORE_SOFTMAX: "softmax", R.SCORE_SIGMOID: "sigmoid", R.SCORE_SQRTSOFTPLUS: "sqrtsoftplus", R.SCORE_NONE: "none"}
+FN = {R.SCORE_SOFTMAX: "softmax", R.SCORE_SIGMOID: "sigmoid", R.SCORE_SQRTSOFTPLUS: "sqrtsoftplus", R.SCORE_NONE: "none",
+      R.SCORE_SOFTMAX_BF16: "softmax_bf16"}
 
 
 def _bf16(bits, dev):
@@ -60,7 +61,7 @@ def test_router_golden(dev, case):
     _check(got, ref)
 
 
-@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SIGMOID, R.SCORE_SQRTSOFTPLUS])
+@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SIGMOID, R.SCORE_SQRTSOFTPLUS, R.SCORE_SOFTMAX_BF16])
 @pytest.mark.parametrize("shape", [(1, 7168, 256, 8), (37, 2048, 512, 10), (5, 1024, 16, 4), (9, 264, 100, 1),
                                    (300, 7168, 256, 8), (129, 2056, 33, 3)])
 def test_router_random_vs_oracle(dev, fn, shape):
@@ -104,3 +105,41 @@ def test_gate_v41_semantics(dev):
     _, ri, rw, _ = R.route(xb, wb, k, R.SCORE_SQRTSOFTPLUS, select_bias=bias, norm_eps=1e-20, route_scale=1.5)
     np.testing.assert_array_equal(idx.cpu().numpy(), ri)
     np.testing.assert_array_equal(wts.cpu().numpy().view(np.uint32), rw.view(np.uint32))
+
+
+@pytest.mark.parametrize("T", [1, 32, 300, 4096])
+def test_qwen_bf16_gate_vs_oracle(dev, T):
+    """The Qwen gate in the reference's dtypes (bf16 logits, bf16 probabilities,
+    bf16 renormalisation, bf16 shared gate) at the Qwen-class shape, E = 512,
+    top-10, Zipf 1.1 logit bias: indices, weights and shared weights bit-exact."""
+    H, E, k = 2048, 512, 10
+    rng = np.random.default_rng(T + 1)
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    sg = F.f32_to_bf16_bits((rng.normal(0, 1, (H,)) / np.sqrt(H)).astype(np.float32))
+    lb = np.log(np.arange(1, E + 1, dtype=np.float64) ** -1.1 / np.sum(np.arange(1, E + 1) ** -1.1)).astype(np.float32)
+    rng.shuffle(lb)
+    ref = R.route(xb, wb, k, R.SCORE_SOFTMAX_BF16, logit_bias=lb, norm_eps=0.0, wg_shared_bits=sg)
+    _check(_run(dev, xb, wb, k, R.SCORE_SOFTMAX_BF16, lb, None, 0.0, 1.0, sg), ref)
+
+
+def test_qwen_route_uses_the_bf16_gate(dev):
+    rng = np.random.default_rng(3)
+    T, H, E, k = 16, 512, 64, 6
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    sg = F.f32_to_bf16_bits((rng.normal(0, 1, (H,)) / np.sqrt(H)).astype(np.float32))
+    w, idx, sh = W.qwen_route(_bf16(xb, dev), _bf16(wb, dev), k, True, shared_gate=_bf16(sg, dev))
+    _, ri, rw, rs = R.route(xb, wb, k, R.SCORE_SOFTMAX_BF16, norm_eps=0.0, wg_shared_bits=sg)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ri)
+    np.testing.assert_array_equal(w.cpu().numpy().view(np.uint32), rw.view(np.uint32))
+    np.testing.assert_array_equal(sh.reshape(-1).cpu().numpy().view(np.uint32), rs.view(np.uint32))
+
+
+def test_bf16_gate_exact_ties_choose_lower_index(dev):
+    xb = np.zeros((3, 256), np.uint16)
+    wb = np.zeros((40, 256), np.uint16)
+    ref = R.route(xb, wb, 5, R.SCORE_SOFTMAX_BF16, norm_eps=0.0)
+    got = _run(dev, xb, wb, 5, R.SCORE_SOFTMAX_BF16, eps=0.0)
+    _check(got, ref)
+    assert got[1].tolist() == [[0, 1, 2, 3, 4]] * 3

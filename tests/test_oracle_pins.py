@@ -200,3 +200,61 @@ def test_golden_fixtures_regenerate(tmp_path):
     assert set(a.files) == set(b.files)
     for n in a.files:
         assert np.array_equal(a[n], b[n], equal_nan=True), n
+
+
+def _bf16_round(a):
+    import ml_dtypes
+    return np.asarray(a, np.float32).astype(ml_dtypes.bfloat16).astype(np.float32)
+
+
+def _butterfly32(part):
+    a = part.astype(np.float32)
+    lanes = np.arange(32)
+    for m in (16, 8, 4, 2, 1):
+        a = (a + a[:, lanes ^ m]).astype(np.float32)
+    return a[:, 0]
+
+
+@pytest.mark.parametrize("T,H,E,k", [(64, 2048, 512, 10), (33, 1024, 16, 4), (7, 512, 100, 3)])
+def test_router_bf16_gate_follows_the_reference_dtypes(T, H, E, k):
+    """SCORE_SOFTMAX_BF16 against a numpy restatement of the Qwen gate's dtypes
+    (qwen4_exp.py:683, 693-699): bf16 logits, float32 softmax rounded to bf16
+    (ml_dtypes, round-to-nearest-even), top-k of the bf16 probabilities with
+    ties to the lower id, weights bf16(p / bf16(sum)), shared gate
+    bf16(sigmoid(bf16 logit)).  The float32 steps use the oracle's own exp and
+    summation order, so the comparison is exact."""
+    rng = np.random.default_rng(T + E)
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    sg = F.f32_to_bf16_bits((rng.normal(0, 1, (H,)) / np.sqrt(H)).astype(np.float32))
+    lb = rng.normal(0, 1, E).astype(np.float32)
+    logits, idx, w, sh = R.route(xb, wb, k, R.SCORE_SOFTMAX_BF16, logit_bias=lb, norm_eps=0.0, wg_shared_bits=sg)
+    l32, _, _, sh32 = R.route(xb, wb, k, R.SCORE_SOFTMAX, logit_bias=lb, norm_eps=0.0, wg_shared_bits=sg)
+    assert np.array_equal(logits.view(np.uint32), l32.view(np.uint32))     # the float32 gate output, biased
+    z = _bf16_round(logits)
+    e = R.exp_f32(z - z.max(1, keepdims=True)).reshape(T, E)
+    part = np.zeros((T, 32), np.float32)
+    for j in range(0, E, 32):
+        blk = np.zeros((T, 32), np.float32)
+        blk[:, :min(32, E - j)] = e[:, j:j + 32]
+        part = (part + blk).astype(np.float32)
+    p = _bf16_round(e / _butterfly32(part)[:, None])
+    order = np.lexsort((np.broadcast_to(np.arange(E), p.shape), -p), axis=-1)[:, :k]
+    np.testing.assert_array_equal(idx, order)
+    sel = np.take_along_axis(p, idx, 1)
+    s = np.zeros(T, np.float32)
+    for j in range(k):
+        s = (s + sel[:, j]).astype(np.float32)
+    np.testing.assert_array_equal(w.view(np.uint32), _bf16_round(sel / _bf16_round(s)[:, None]).view(np.uint32))
+    assert not np.any(w.view(np.uint32) & 0xffff)                          # bf16 values
+    g = _bf16_round(np.log(sh32 / (1 - sh32)))                               # the float32 shared logit, rounded
+    assert np.max(np.abs(sh - _bf16_round(1 / (1 + np.exp(-g.astype(np.float64)))))) <= 2.0 ** -8
+
+
+def test_router_bf16_gate_ties_go_to_the_lower_id():
+    # 40 equal logits: equal bf16 probabilities, the first k ids win; weights 1/k in bf16
+    xb = np.zeros((2, 256), np.uint16)
+    wb = np.zeros((40, 256), np.uint16)
+    _, idx, w, _ = R.route(xb, wb, 5, R.SCORE_SOFTMAX_BF16, norm_eps=0.0)
+    assert idx.tolist() == [[0, 1, 2, 3, 4]] * 2
+    assert np.all(w == _bf16_round(np.float32(0.2)))

@@ -22,7 +22,7 @@ WM_ERR_CUDA = -3
 WM_ERR_WORKSPACE = -4
 
 WM_OUT_F32, WM_OUT_BF16 = 0, 1
-WM_SCORE_SOFTMAX, WM_SCORE_SIGMOID, WM_SCORE_SQRTSOFTPLUS, WM_SCORE_NONE = 0, 1, 2, 3
+WM_SCORE_SOFTMAX, WM_SCORE_SIGMOID, WM_SCORE_SQRTSOFTPLUS, WM_SCORE_NONE, WM_SCORE_SOFTMAX_BF16 = 0, 1, 2, 3, 4
 WM_UP_GATE, WM_GATE_UP = 0, 1
 WKV_FP8_F32_B64, WKV_FP8_UE8M0_B32, WKV_FP4_E4M3_B16, WKV_FP4_UE8M0_B32, WKV_MXFP8_B32, WKV_MXFP4_B32 = range(6)
 

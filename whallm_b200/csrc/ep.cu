@@ -245,6 +245,9 @@ int wep_wait(const uint32_t *flags, int world, const uint32_t *epoch, int32_t *e
 int wep_sum_rows(const float *part, int world, int rows, int H, const int32_t *err, wm_bf16 *out, wm_stream_t stream) {
   wm::clear_error();
   WM_REQUIRE(part && out && world >= 1 && rows >= 0 && H % 4 == 0, "wep_sum_rows: bad arguments");
+  // the kernel reads part as float4 and writes out as 4 bf16 (8 bytes) at a time
+  WM_REQUIRE(wm::aligned(part, 16) && wm::aligned(out, 8),
+             "wep_sum_rows: part must be 16-byte and out 8-byte aligned");
   if (rows == 0) return WM_OK;
   const int64_t work = static_cast<int64_t>(rows) * (H / 4);
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, wm::sm_count() * 4)));

@@ -93,10 +93,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
       for (int r = 0; r < kRowsPerWarp; ++r)
 #pragma unroll
         for (int t = 0; t < kNT; ++t) acc[r][t] = 0.0f;
-      // Rows shorter than 32 groups (K < 1024) give each group to lpg lanes,
-      // each taking 32 / lpg of its values, so no lane idles; the partial sums
-      // meet in the warp reduction below.
-      const int lpg = groups >= 32 ? 1 : min(4, 32 / groups);
+      // Rows of at most 16 groups (K <= 512) give each group to lpg lanes,
+      // each taking 32 / lpg of its values, so fewer lanes idle; the partial
+      // sums meet in the warp reduction below.  lpg divides 4, so the lpg
+      // segments of nseg 8-value steps cover the 32 values of a group exactly
+      // (9 or 10 groups take 2 lanes each, not 32 / groups = 3).
+      const int lpg = groups > 16 ? 1 : (groups > 8 ? 2 : 4);
       const int nseg = 4 / lpg;                            // 8-value steps per lane
       for (int qq = lane; qq < groups * lpg; qq += 32) {
         const int q = qq / lpg, seg = qq - q * lpg;

@@ -16,6 +16,14 @@
 //   each warp streams a quarter of the rows with 16-byte loads.
 // Kernel 2 (top-k): one warp per token; scores in registers, then k rounds
 //   of a warp arg-max with ties to the lower expert id.
+//
+// WM_SCORE_SOFTMAX_BF16 is the Qwen gate as the reference evaluates it: the
+// bf16 nn.Linear rounds the logits to bf16 (qwen4_exp.py:683), softmax
+// (precise=True) runs in float32 and returns bf16 probabilities
+// (qwen4_exp.py:693), top-k selects on those bf16 values (:694-695), and the
+// renormalisation divides bf16 by a bf16 sum, rounding the quotient to bf16
+// (:696-697); the shared-expert gate is sigmoid of a bf16 logit, rounded to
+// bf16 (:699).  Every rounding is round-to-nearest-even.
 #include <mutex>
 
 #include "wm_common.cuh"
@@ -26,6 +34,8 @@ namespace {
 constexpr int kMaxE = 1024;
 constexpr int kMaxK = 32;
 constexpr int kSegs = 4;          // warps per expert row
+
+__device__ __forceinline__ float round_bf16(float v) { return wm_bf16_to_f32(wm_f32_to_bf16(v)); }
 
 // One CTA (4 warps) per (group of ET expert rows, group of TT tokens).  Warp
 // s takes the column blocks [s*n/4, (s+1)*n/4) (n = ceil(H/256)); lane l
@@ -280,13 +290,14 @@ __global__ void __launch_bounds__(128) k_router_topk(const float *__restrict__ l
   if (t >= T) return;
   const float kNegInf = -__int_as_float(0x7f800000);
   const float *lt = logits + static_cast<int64_t>(t) * E;
+  const bool bf = score_fn == WM_SCORE_SOFTMAX_BF16;
   float sc[PER];
 #pragma unroll
   for (int j = 0; j < PER; ++j) {
     const int e = lane + 32 * j;
-    sc[j] = e < E ? lt[e] : kNegInf;
+    sc[j] = e < E ? (bf ? round_bf16(lt[e]) : lt[e]) : kNegInf;
   }
-  if (score_fn == WM_SCORE_SOFTMAX) {
+  if (score_fn == WM_SCORE_SOFTMAX || bf) {
     float mx = kNegInf;
 #pragma unroll
     for (int j = 0; j < PER; ++j) mx = fmaxf(mx, sc[j]);
@@ -303,7 +314,7 @@ __global__ void __launch_bounds__(128) k_router_topk(const float *__restrict__ l
 #pragma unroll
     for (int m = 16; m >= 1; m >>= 1) part = part + __shfl_xor_sync(0xffffffffu, part, m);
 #pragma unroll
-    for (int j = 0; j < PER; ++j) sc[j] = __fdiv_rn(sc[j], part);
+    for (int j = 0; j < PER; ++j) sc[j] = bf ? round_bf16(__fdiv_rn(sc[j], part)) : __fdiv_rn(sc[j], part);
   } else if (score_fn == WM_SCORE_SIGMOID) {
 #pragma unroll
     for (int j = 0; j < PER; ++j) sc[j] = wm_sigmoid(sc[j]);
@@ -358,13 +369,16 @@ __global__ void __launch_bounds__(128) k_router_topk(const float *__restrict__ l
     float sum = 0.0f;
     for (int r = 0; r < k; ++r) sum = sum + __shfl_sync(0xffffffffu, my_w, r);
     denom = sum + norm_eps;
+    if (bf) denom = round_bf16(denom);
   }
   if (lane < k) {
-    const float w = norm ? __fdiv_rn(my_w, denom) : my_w;
+    float w = norm ? __fdiv_rn(my_w, denom) : my_w;
+    if (bf) w = round_bf16(w);
     idx[static_cast<int64_t>(t) * k + lane] = my_i;
     weights[static_cast<int64_t>(t) * k + lane] = w * route_scale;
   }
-  if (lane == 0 && shared_w) shared_w[t] = wm_sigmoid(shared_w[t]);
+  if (lane == 0 && shared_w)
+    shared_w[t] = bf ? round_bf16(wm_sigmoid(round_bf16(shared_w[t]))) : wm_sigmoid(shared_w[t]);
 }
 
 int launch_router_topk(const float *logits, const float *select_bias, int T, int E, int k, int score_fn,
@@ -397,7 +411,7 @@ extern "C" int wmoe_router_topk(const wm_bf16 *x, const wm_bf16 *wg, const float
   WM_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "router needs H % 8 == 0");
   WM_REQUIRE(E >= 1 && E <= kMaxE, "router supports 1 <= E <= 1024 experts");
   WM_REQUIRE(k >= 1 && k <= kMaxK && k <= E, "router needs 1 <= k <= min(32, E)");
-  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_NONE, "unknown score function");
+  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_SOFTMAX_BF16, "unknown score function");
   if (T == 0) return WM_OK;
   WM_REQUIRE(x && wg && logits && idx && weights, "router: null buffer");
   WM_REQUIRE(!wg_shared || shared_w, "router: wg_shared needs a shared_w output");
@@ -417,7 +431,7 @@ extern "C" int wmoe_topk_scores(const float *logits, const float *select_bias, i
   WM_REQUIRE(T >= 0, "topk: T >= 0");
   WM_REQUIRE(E >= 1 && E <= kMaxE, "topk supports 1 <= E <= 1024");
   WM_REQUIRE(k >= 1 && k <= kMaxK && k <= E, "topk needs 1 <= k <= min(32, E)");
-  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_NONE, "unknown score function");
+  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_SOFTMAX_BF16, "unknown score function");
   if (T == 0) return WM_OK;
   WM_REQUIRE(logits && idx && weights, "topk: null buffer");
   return launch_router_topk(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights, nullptr,
@@ -465,7 +479,7 @@ extern "C" int wmoe_router_topk_static(const wm_bf16 *x, const wm_bf16 *wg, cons
   WM_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "router needs H % 8 == 0");
   WM_REQUIRE(E >= 1 && E <= kMaxE, "router supports 1 <= E <= 1024 experts");
   WM_REQUIRE(k >= 1 && k <= kMaxK && k <= E, "router needs 1 <= k <= min(32, E)");
-  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_NONE, "unknown score function");
+  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_SOFTMAX_BF16, "unknown score function");
   WM_REQUIRE(static_cast<int64_t>(T) * E <= kStaticLogits,
              "wmoe_router_topk_static: T*E exceeds the 262144-float (1 MiB) static scratch; use wmoe_router_topk");
   if (T == 0) return WM_OK;

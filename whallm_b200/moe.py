@@ -9,7 +9,8 @@ Drop-in mirrors of the reference's MoE call sites:
     whole layer is two native calls (router, fused experts + combine).
   * ``SparseMoE`` -- Qwen ``SparseMoE.__call__`` (qwen4_exp.py:680-704),
     shared expert gated by ``sigmoid(x . w_sg)``.
-  * ``TinyMoE`` -- the affine-4 tiny configuration (softmax top-k, no shared).
+  * ``TinyMoE`` -- the affine-4 tiny configuration (the Qwen-style bf16 gate:
+    softmax top-k, renormalised; no shared expert).
 """
 from __future__ import annotations
 
@@ -83,7 +84,9 @@ class SparseMoE:
 
 
 class TinyMoE:
-    """The tiny affine-4 configuration: softmax over E, top-k, renormalised, no shared expert."""
+    """The tiny affine-4 configuration: bf16 gate, softmax over E (float32, bf16
+    result), top-k, renormalised in bf16 (the SparseMoE gate, qwen4_exp.py:692-697);
+    no shared expert."""
 
     def __init__(self, gate_weight: torch.Tensor, experts: X.Affine4BatchedExperts, top_k: int):
         self.gate_weight = gate_weight

@@ -5,8 +5,11 @@ Mirrors the reference's routers:
     sqrtsoftplus, selection bias that picks but does not scale, weights
     normalised by ``sum + 1e-20`` and multiplied by ``route_scale``).
   * ``qwen_route`` -- the routing half of SparseMoE.__call__
-    (qwen4_exp.py:692-699): softmax, top-k, ``scores / sum``, plus the
-    sigmoid shared-expert gate.
+    (qwen4_exp.py:692-699) in the reference's dtypes: the gate is a bf16
+    ``nn.Linear`` (bf16 logits, :683), ``softmax(precise=True)`` computes in
+    float32 and returns bf16 probabilities (:693), top-k selects on those
+    (:694-695), ``scores / scores.sum()`` is bf16 arithmetic (:696-697), and
+    the shared-expert gate is ``sigmoid`` of a bf16 logit in bf16 (:699).
   * ``stable_topk_indices`` -- model.py:548-560 (ties by position).
 
 Ties are resolved towards the lower expert id, and indices come back in
@@ -20,7 +23,8 @@ import torch
 from . import _lib as L
 
 SCORE_FUNCS = {"softmax": L.WM_SCORE_SOFTMAX, "sigmoid": L.WM_SCORE_SIGMOID,
-               "sqrtsoftplus": L.WM_SCORE_SQRTSOFTPLUS, "none": L.WM_SCORE_NONE}
+               "sqrtsoftplus": L.WM_SCORE_SQRTSOFTPLUS, "none": L.WM_SCORE_NONE,
+               "softmax_bf16": L.WM_SCORE_SOFTMAX_BF16}
 
 
 def route(x: torch.Tensor, weight: torch.Tensor, top_k: int, score_func: str = "softmax", *,
@@ -106,6 +110,9 @@ class Gate:
 
 
 def qwen_route(x, gate_weight, top_k: int, norm_topk_prob: bool = True, shared_gate=None, logit_bias=None):
-    """Routing half of SparseMoE.__call__ (qwen4_exp.py:692-699): (scores, indices, shared_w)."""
-    return route(x, gate_weight, top_k, "softmax", logit_bias=logit_bias,
+    """Routing half of SparseMoE.__call__ (qwen4_exp.py:692-699): (scores, indices, shared_w).
+
+    bf16 gate semantics (``softmax_bf16``): selection on bf16 probabilities,
+    scores and shared_w are bf16 values (returned as float32 tensors)."""
+    return route(x, gate_weight, top_k, "softmax_bf16", logit_bias=logit_bias,
                  norm_eps=0.0 if norm_topk_prob else None, route_scale=1.0, shared_gate=shared_gate)
