@@ -340,7 +340,7 @@ def run_ours(args, rank, world, dev):
     if wl == "kv_scores":
         # decode scores of one query per sequence against an MXFP8 latent cache:
         # 8 sequences x 32768 cached tokens x 512 dims per layer, 61 layers (each its own cache)
-        Bq, Lc, D, n_layer = 8, 32768, 512, 61
+        Bq, Lc, D, n_layer = 8, 32768, 512, args.kv_layers
         caches = []
         for li in range(n_layer):
             kvr = torch.randn(Bq * Lc, D, device=dev, generator=torch.Generator(device=dev).manual_seed(li))
@@ -882,6 +882,9 @@ def main():
                     help="routed experts per layer (default: the configuration's); smaller layers for ncu captures")
     ap.add_argument("--context", type=int, default=32768,
                     help="qsa workload: tokens already cached per sequence (smaller for ncu captures)")
+    ap.add_argument("--kv-layers", type=int, default=61,
+                    help="kv and kv_scores workloads: cache layers held on the device (61 in the configuration; "
+                         "a few for ncu captures, which keep each layer's cache resident)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

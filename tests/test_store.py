@@ -44,3 +44,18 @@ def test_provider_rejects(call, msg):
     s, _ = _store()
     with pytest.raises(ValueError, match=msg):
         call(s)
+
+
+def test_unfused_experts_are_fused_once():
+    # a store that supplies w1 and w3 separately gets [w3; w1] built on the first call and reused afterwards
+    w1 = torch.arange(2 * 4 * 8, dtype=torch.uint8).view(2, 4, 8)
+    w3 = w1 + 100
+    s1 = torch.ones(2, 4, 1, dtype=torch.uint8)
+    s3 = s1 * 2
+    b = W.BatchedExperts(w1, s1, w1, s1, w3, s3)
+    a13, a_s, calls = b.fused()
+    b13, b_s, _ = b.fused()
+    assert calls == 3
+    assert a13 is b13 and a_s is b_s
+    assert torch.equal(a13, torch.cat([w3, w1], dim=-2))
+    assert torch.equal(a_s, torch.cat([s3, s1], dim=-2))

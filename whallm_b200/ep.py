@@ -17,9 +17,9 @@ replicated.  One forward on each rank's own tokens:
   6. combine on the source rank: ``sum_j w_j y_j`` in float32 plus the shared
      expert computed locally, rounded once to bf16.
 
-Remote rows always land in local HBM through the collective before a kernel
-reads them: no kernel touches another GPU's memory.  The local expert compute
-is a callable so the same exchange logic runs on CPU ranks (gloo) in tests.
+In this all-to-all form remote rows land in local HBM through the collective
+before a kernel reads them.  The local expert compute is a callable so the
+same exchange logic runs on CPU ranks (gloo) in tests.
 
 ``GatheredExpertParallelMoE`` is the decode form: with a few tokens per rank
 the all-to-all's data-dependent splits (a device-to-host read of the counts)
@@ -28,7 +28,13 @@ and routes, runs its expert share over all of them with float32 partial sums
 (``wmoe_mxfp4_moe_forward_ep``: other ranks' experts skipped, the shared
 expert only for its own tokens) and a reduce-scatter adds the partials back
 onto the owning rank.  Every collective has a fixed size, so one decode step
-of the layer is capturable as a CUDA graph.
+of the layer is capturable as a CUDA graph.  ``PeerGatheredMoE`` does the same
+exchange without a collective library: ``wep_put_rows`` stores this rank's
+rows into every rank's CUDA-IPC-mapped buffer with plain stores over NVLink
+and raises a flag there; ``wep_wait`` spins (bounded) on the local flags, and
+``wep_sum_rows`` adds the partial sums.  Those three kernels are the only ones
+that touch another GPU's memory (plain loads and stores; no TMA, no library
+kernel on peer memory).
 """
 from __future__ import annotations
 

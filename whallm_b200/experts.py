@@ -64,12 +64,19 @@ class BatchedExperts:
     w13_scales: torch.Tensor | None = None
 
     def fused(self):
+        """(w13, w13_scales, gather_qmm calls).  When the store supplied w1 and
+        w3 unfused, the [w3; w1] fusion of _fused_slot_regions
+        (expert_layout.py:43-62) is built once and kept with this object, not
+        rebuilt on every call (a DeepSeek-class layer is ~4 GB of w13)."""
         if self.w13 is not None and self.w13_scales is not None:
             return self.w13, self.w13_scales, 2
-        # same fusion as _fused_slot_regions (expert_layout.py:43-62): [w3; w1]
-        w13 = torch.cat([self.w3, self.w1], dim=-2).contiguous()
-        s13 = torch.cat([self.w3_scales, self.w1_scales], dim=-2).contiguous()
-        return w13, s13, 3
+        cached = self.__dict__.get("_fused13")
+        if cached is None:
+            w13 = torch.cat([self.w3, self.w1], dim=-2).contiguous()
+            s13 = torch.cat([self.w3_scales, self.w1_scales], dim=-2).contiguous()
+            cached = (w13, s13)
+            object.__setattr__(self, "_fused13", cached)     # frozen dataclass: a private cache slot
+        return cached[0], cached[1], 3
 
 
 @dataclass(frozen=True)
