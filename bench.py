@@ -13,14 +13,22 @@ never come from L2 between steps; inputs are already in HBM.
          (decode: on two copy streams, each copy overlapping another batch's
          layer replay)
   roofline  the expert FFN call (wmoe_mxfp4_moe_forward: permute, token
-         gather, tcgen05 up-projection + SwiGLU, tcgen05 down-projection,
+         split, tcgen05 up-projection + SwiGLU, tcgen05 down-projection,
          combine; the two tcgen05 launches carry ~90% of its device time):
          algorithmic bytes (distinct experts x 23,396,352 B + activations) /
          its CUDA-event time, against the measured HBM copy bandwidth
+  breakdown  per batch size (back-to-back calls, layers cycled): layer and
+         expert-call time, distinct experts, HBM fraction; and, on the same
+         resident DeepSeek-class layers or on Qwen-class layers built beside
+         them, ds_prefill_4096 (4096 tokens through the
+         layer; its tensor fraction is against the dense bf16 peak, the rate of
+         the two-term e4m3 token operand the block-scaled MMAs run),
+         qn_decode_1 / qn_decode_32 and qn_prefill_16384.
+         `--no-extras` skips those.
 Decode batches are replayed as CUDA graphs (one per layer and batch size),
 prefill runs eagerly.
   cpu_baseline  the oracle's C restatement (OpenMP, all host threads) on a
-         bounded sample of the same sweep
+         bounded sample of the same sweep, on a layer built on the host
 
 Other workloads: --workload ds_prefill (4096 tokens), qn_decode (B 1 and 32),
 qn_prefill (16384 tokens), tiny (64 tokens, affine-4), kv (FP8 KV quantize +
@@ -29,9 +37,13 @@ qsa (Qwen QSA affine KV caches: one decode update_and_fetch of 8 sequences at
 a 32768-token context over the 12 full-attention layers), linear (dense MXFP8
 linear, K = N = 5120: decode rows 1, 4, 16; 4096 in the breakdown).
 
-`--impl reference` times the reference's algorithm on the host cores (the
-oracle port; the MLX CPU backend the reference would use is not installable
-here) on the same workload and prints the same JSON line with "impl".
+`--impl reference` times the reference's algorithm on the host cores: the
+oracle's restatement (router, grouped expert matmuls that dequantize inside
+the loop, weighted combine, shared expert) on a layer of the same
+configuration built on the host from seeds (``oracle/synthetic.py``); the
+device library is not loaded.  The MLX CPU backend the reference would use is
+not installable here.  It prints the same JSON line with "impl", the same
+`config`, and the number of steps it actually timed.
 
 Multi-GPU (torchrun): the MoE workloads run expert-parallel (`whallm_b200.ep`):
 each rank routes its own tokens (weak scaling); the routed experts are dealt to
@@ -39,8 +51,9 @@ the ranks by popularity, equal counts per rank (WM_EP_PLACEMENT=contiguous for
 plain ranges); decode gathers every rank's tokens and returns partial sums over
 peer memory (WM_EP_EXCHANGE=nccl for NCCL collectives), prefill moves token rows
 to the owning rank and back through NCCL all-to-all; the shared expert is
-replicated; value = all ranks' tokens / max rank time.  Other workloads run as
-independent replicas.
+replicated; value = all ranks' tokens / max rank time.  The default line's
+breakdown adds ep_prefill_4096: 4096 tokens per rank through the all-to-all
+form.  Other workloads run as independent replicas.
 """
 from __future__ import annotations
 
@@ -57,7 +70,27 @@ sys.path.insert(0, ROOT)
 
 DS_EXPERT_BYTES = 3 * 7168 * 2048 // 2 + 3 * 7168 * 2048 // 32   # 23,396,352
 QN_EXPERT_BYTES = 3 * 2048 * 512 // 2 + 3 * 2048 * 512 // 32     # 1,671,168
+TINY_EXPERT_BYTES = 884736
 SWEEP = (1, 4, 16, 64)
+
+MOE_WORKLOADS = {"ds_decode": ("ds", SWEEP), "ds_prefill": ("ds", (4096,)), "qn_decode": ("qn", (1, 32)),
+                 "qn_prefill": ("qn", (16384,)), "tiny": ("tiny", (64,))}
+GRAPHED = ("ds_decode", "qn_decode", "tiny")
+EP_WORKLOADS = ("ds_decode", "ds_prefill", "qn_decode", "qn_prefill")
+SHAPES = {"ds": dict(H=7168, I=2048, E=256, k=8, shared=True),
+          "qn": dict(H=2048, I=512, E=512, k=10, shared=True),
+          "tiny": dict(H=1024, I=512, E=16, k=4, shared=False)}
+EXPERT_BYTES = {"ds": DS_EXPERT_BYTES, "qn": QN_EXPERT_BYTES, "tiny": TINY_EXPERT_BYTES}
+MODEL = {"ds": "DeepSeek-class routed-expert layer: H 7168, I 2048, 256 routed + 1 shared experts, top-8, "
+               "MXFP4 (E2M1, E8M0 per 32), V4.1 gate with a Zipf 1.0 logit bias, ClampedSwiGLU 10",
+         "qn": "Qwen-Next-class sparse MoE layer: H 2048, I 512, 512 routed + 1 shared experts, top-10, MXFP4, "
+               "bf16 gate with a Zipf 1.1 logit bias, sigmoid-gated shared expert",
+         "tiny": "tiny MoE layer: H 1024, I 512, 16 experts, top-4, MLX affine 4-bit group 64, bf16 gate, "
+                 "no shared expert"}
+# bounded host samples of each MoE workload for the CPU restatement
+CPU_SAMPLE = {"ds_decode": SWEEP, "ds_prefill": (256,), "qn_decode": (1, 32), "qn_prefill": (1024,), "tiny": (64,)}
+REF_BUDGET_S = 150.0      # timed seconds of the reference arm (steps beyond it are not run, and not reported)
+BASELINE_BUDGET_S = 25.0  # timed seconds of the cpu_baseline leg of our arm
 
 
 def _peaks():
@@ -67,6 +100,83 @@ def _peaks():
         return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
     except Exception:
         return 6650.0, 1590.0, "fallback"
+
+
+def _n_layers(args, name):
+    return max(args.layers, 12) if name == "tiny" else args.layers     # 14.2 MB per tiny layer: 12 exceed L2
+
+
+def _ep(args, world):
+    return world > 1 and args.workload in EP_WORKLOADS
+
+
+def workload_config(args, world):
+    """The workload's description, printed identically by both arms."""
+    wl = args.workload
+    par = "single GPU" if world == 1 else "replicas"
+    if wl in MOE_WORKLOADS:
+        name, batches = MOE_WORKLOADS[wl]
+        c = SHAPES[name]
+        nl = _n_layers(args, name)
+        n_exp = (args.experts or c["E"]) + (1 if c["shared"] else 0)
+        cfg = {"workload": wl, "model": MODEL[name], "batches": list(batches), "tokens_per_step": sum(batches),
+               "layers_cycled": nl,
+               "l2": f"{nl} resident layers ({nl * n_exp * EXPERT_BYTES[name] / 1e9:.2f} GB of experts) cycled per "
+                     "step: weights larger than L2"}
+        if args.experts:
+            cfg["routed_experts"] = args.experts
+        if _ep(args, world):
+            decode = wl in ("ds_decode", "qn_decode")
+            peer = decode and os.environ.get("WM_EP_EXCHANGE", "peer") != "nccl"
+            balanced = os.environ.get("WM_EP_PLACEMENT", "balanced") != "contiguous"
+            cfg.update(parallelism=f"ep{world}", tokens_per_rank=sum(batches), experts_per_rank=c["E"] // world,
+                       placement="popularity-balanced (snake order by router bias)" if balanced else "contiguous",
+                       launch=("CUDA graph per (layer, batch): peer-memory exchange (CUDA IPC, flags), partial "
+                               "experts" if peer else "CUDA graph per (layer, batch): NCCL all-gather, partial "
+                               "experts, reduce-scatter") if decode else "eager (NCCL all-to-all)")
+        else:
+            cfg.update(parallelism=par, launch="CUDA graph per (layer, batch)" if wl in GRAPHED else "eager")
+        return cfg
+    if wl == "kv":
+        return {"workload": wl, "rows_per_step": 32768 * 8 * args.kv_layers, "D": 576,
+                "format": "e4m3 with one fp32 scale (amax/448) per 64 values", "sequences": 8, "context": 32768,
+                "layers": args.kv_layers, "step": "quantize every row, then dequantize every row, layer by layer",
+                "l2": "each layer's rows (302 MB bf16) exceed L2", "parallelism": par, "launch": "eager"}
+    if wl == "kv_scores":
+        return {"workload": wl, "sequences": 8, "context": 32768, "D": 512, "layers": args.kv_layers,
+                "format": "MXFP8 (e4m3, E8M0 per 32)", "queries_per_sequence": 1,
+                "l2": f"{args.kv_layers} layers of 145 MB caches: larger than L2", "parallelism": par,
+                "launch": "eager"}
+    if wl == "qsa":
+        return {"workload": wl, "sequences": 8, "context": args.context, "full_attention_layers": 12,
+                "caches": "K/V 8-bit 2 heads x 256, index 4-bit 1 head x 128, group 32",
+                "step": "append one row per sequence + fetch the whole history, every cache",
+                "l2": "the packed history read per step exceeds L2", "parallelism": par, "launch": "eager"}
+    if wl == "linear":
+        return {"workload": wl, "K": 5120, "N": 5120, "rows_per_step": [1, 4, 16], "weight_matrices_cycled": 8,
+                "l2": "8 x 27 MB of weights cycled: larger than L2", "parallelism": par,
+                "launch": "CUDA graph per (rows, matrix); the 4096-row calls eager"}
+    raise SystemExit(f"unknown workload {wl}")
+
+
+def workload_dtype(wl):
+    if wl == "tiny":
+        return "affine 4-bit weights (bf16 scale/bias per 64), bf16 activations, fp32 accumulate"
+    if wl in MOE_WORKLOADS:
+        return "mxfp4 weights, bf16 activations, fp32 accumulate"
+    return {"kv": "e4m3 payload with fp32 scales, bf16 rows", "kv_scores": "e4m3 cache with E8M0 per 32, bf16 query",
+            "qsa": "u32 packed affine 8/4-bit, bf16 scales/biases, bf16 out",
+            "linear": "e4m3 weights with E8M0 per 32, bf16 activations, fp32 accumulate"}[wl]
+
+
+def workload_data(wl):
+    if wl in MOE_WORKLOADS:
+        return ("synthetic (seeded N(0,0.02) expert weights quantized to the configuration's format, N(0,1) bf16 "
+                "tokens, Zipf-skewed router)" if wl != "tiny" else
+                "synthetic (seeded N(0,0.02) weights quantized to affine 4-bit, N(0,0.02) router, N(0,1) bf16 tokens)")
+    return {"kv": "synthetic (seeded N(0,1) bf16 rows)", "kv_scores": "synthetic (seeded N(0,1) cache and query)",
+            "qsa": "synthetic (seeded N(0,1) bf16 keys/values)",
+            "linear": "synthetic (seeded N(0,0.02) weights quantized to MXFP8, N(0,1) bf16 rows)"}[wl]
 
 
 class ClockSampler:
@@ -174,35 +284,32 @@ def _e2e_overlapped(torch, dev, caps, hx, houts, steps):
     return s4.elapsed_time(e4) / steps
 
 
-def run_ours(args, rank, world, dev):
-    import torch
-    import whallm_b200 as W
-    from whallm_b200 import experts as X
-    from whallm_b200 import synthetic as S
-    from whallm_b200.graphs import CapturedLayer
+class MoeBench:
+    """One MoE workload on resident synthetic layers: the routes of every
+    (layer, batch), the distinct experts each reads (for the algorithmic byte
+    count), CUDA graphs for decode shapes, and CUDA-event timing helpers.
 
-    torch.cuda.set_device(dev)
-    hbm, tc, peak_src = _peaks()
-    wl = args.workload
-    n_layers = args.layers
-    res = {}
-    if wl in ("ds_decode", "ds_prefill", "qn_decode", "qn_prefill", "tiny"):
-        name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn", "tiny": "tiny"}[wl]
-        if name == "tiny":
-            n_layers = max(n_layers, 12)     # 14.2 MB of experts per layer: 12 layers exceed L2
-        layers = [S.make_layer(name, dev, seed=1000 * rank + 17 * i, E=args.experts) for i in range(n_layers)]
-        cfg = layers[0].cfg
-        H = cfg["H"]
-        batches = {"ds_decode": SWEEP, "ds_prefill": (4096,), "qn_decode": (1, 32), "qn_prefill": (16384,),
-                   "tiny": (64,)}[wl]
-        xs = [S.make_tokens(B, H, 100 + rank, dev) for B in batches]
-        expert_bytes = {"ds": DS_EXPERT_BYTES, "qn": QN_EXPERT_BYTES, "tiny": 884736}[name]
-        # distinct experts each (layer, batch) reads, for the algorithmic byte count
-        distinct = [0.0] * len(xs)
-        routes = []
-        for li, lay in enumerate(layers):
+    `layers` reuses already-built layers (another batch shape on the same
+    weights); otherwise `n_layers` layers are built with per-rank seeds."""
+
+    def __init__(self, torch, name, batches, graphed, dev, rank, n_layers=None, layers=None, experts=None):
+        import whallm_b200 as W
+        from whallm_b200 import experts as X
+        from whallm_b200 import synthetic as S
+        from whallm_b200.graphs import CapturedLayer
+        self.torch, self.X = torch, X
+        self.name, self.batches, self.graphed = name, tuple(batches), graphed
+        self.layers = (layers if layers is not None else
+                       [S.make_layer(name, dev, seed=1000 * rank + 17 * i, E=experts) for i in range(n_layers)])
+        self.n_layers = len(self.layers)
+        cfg = self.layers[0].cfg
+        self.cfg = cfg
+        self.xs = [S.make_tokens(B, cfg["H"], 100 + rank, dev) for B in self.batches]
+        self.distinct = [0.0] * len(self.xs)
+        self.routes = []
+        for lay in self.layers:
             row = []
-            for b, x in enumerate(xs):
+            for b, x in enumerate(self.xs):
                 if name == "ds":
                     w, idx = lay.layer.gate(x)
                     sw = None
@@ -210,54 +317,109 @@ def run_ours(args, rank, world, dev):
                     w, idx, sw = W.qwen_route(x, lay.gate_weight, cfg["k"], True, shared_gate=lay.shared_gate,
                                               logit_bias=lay.logit_bias)
                 row.append((w, idx, sw))
-                distinct[b] += (len(set(idx.flatten().tolist())) + (1 if cfg["shared"] else 0)) / n_layers
-            routes.append(row)
-        tokens_per_step = sum(batches)
-        act_bytes = [x.numel() * 2 * 2 for x in xs]          # x in + out (bf16)
-        alg_bytes = [d * expert_bytes + a for d, a in zip(distinct, act_bytes)]
-
-        limit = 10.0 if name == "ds" else 0.0
-        shared_id = cfg["E"] if cfg["shared"] else -1
-
-        def experts_call(li, b, x):
-            w, idx, sw = routes[li][b]
-            return X.experts_forward(x, idx, layers[li].experts, weights=w, shared_expert=shared_id, shared_w=sw,
-                                     swiglu_limit=limit)
-
-        graphed = wl in ("ds_decode", "qn_decode", "tiny")
+                self.distinct[b] += (len(set(idx.flatten().tolist())) + (1 if cfg["shared"] else 0)) / self.n_layers
+            self.routes.append(row)
+        self.act_bytes = [x.numel() * 2 * 2 for x in self.xs]           # x in + out (bf16)
+        self.alg_bytes = [d * EXPERT_BYTES[name] + a for d, a in zip(self.distinct, self.act_bytes)]
+        kk = cfg["k"] + (1 if cfg["shared"] else 0)
+        self.flops = [B * kk * 6 * cfg["H"] * cfg["I"] for B in self.batches]
+        self.limit = 10.0 if name == "ds" else 0.0
+        self.shared_id = cfg["E"] if cfg["shared"] else -1
         if graphed:
-            # decode (and the 64-token tiny layer): one CUDA graph per (layer, batch)
-            # for the whole layer and for the expert call alone (launch overhead
-            # exceeds the work)
-            caps = [[CapturedLayer(lay.layer, x) for x in xs] for lay in layers]
-            ecaps = [[CapturedLayer(lambda xx, li=li, b=b: experts_call(li, b, xx), x) for b, x in enumerate(xs)]
-                     for li in range(n_layers)]
+            self.caps = [[CapturedLayer(lay.layer, x) for x in self.xs] for lay in self.layers]
+            self.ecaps = [[CapturedLayer(lambda xx, li=li, b=b: self.experts_call(li, b, xx), x)
+                           for b, x in enumerate(self.xs)] for li in range(self.n_layers)]
 
-            def step(i):
-                for c in caps[i % n_layers]:
-                    c()
+    def experts_call(self, li, b, x):
+        w, idx, sw = self.routes[li][b]
+        return self.X.experts_forward(x, idx, self.layers[li].experts, weights=w, shared_expert=self.shared_id,
+                                      shared_w=sw, swiglu_limit=self.limit)
 
-            def experts_only(i):
-                for c in ecaps[i % n_layers]:
-                    c()
+    def layer(self, i, b):
+        if self.graphed:
+            return self.caps[i % self.n_layers][b]()
+        return self.layers[i % self.n_layers].layer(self.xs[b])
 
-            def one(i, b):
-                caps[i % n_layers][b]()
-        else:
-            def step(i):
-                lay = layers[i % n_layers]
-                for x in xs:
-                    lay.layer(x)
+    def experts(self, i, b):
+        if self.graphed:
+            return self.ecaps[i % self.n_layers][b]()
+        return self.experts_call(i % self.n_layers, b, self.xs[b])
 
-            def experts_only(i):
-                for b, x in enumerate(xs):
-                    experts_call(i % n_layers, b, x)
+    def step(self, i):
+        for b in range(len(self.xs)):
+            self.layer(i, b)
 
-            def one(i, b):
-                layers[i % n_layers].layer(xs[b])
+    def experts_step(self, i):
+        for b in range(len(self.xs)):
+            self.experts(i, b)
 
+    def timed(self, fn, reps):
+        torch = self.torch
+        torch.cuda.synchronize()
+        s, e = _events(torch)
+        s.record()
+        for i in range(reps):
+            fn(i)
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / reps
+
+    def breakdown(self, reps, hbm, tc, prefix=""):
+        """Per batch size: the whole layer and the expert call alone, back to back
+        (layers cycled as in the timed step); hbm_frac = the expert call's
+        algorithmic bytes over its time; prefill shapes add the tensor rate."""
+        out = {}
+        for b, B in enumerate(self.batches):
+            t_layer = self.timed(lambda i, b=b: self.layer(i, b), reps)
+            t_exp = self.timed(lambda i, b=b: self.experts(i, b), reps)
+            d = {"ms": round(t_layer, 4), "tok_s": round(B / t_layer * 1e3, 1), "expert_ms": round(t_exp, 4),
+                 "distinct_experts": round(self.distinct[b], 2),
+                 "hbm_frac": round(self.alg_bytes[b] / (t_exp * 1e-3) / (hbm * 1e9), 4)}
+            if B >= 1024:
+                tf = self.flops[b] / (t_exp * 1e-3) / 1e12
+                d["tflops"] = round(tf, 1)
+                d["tensor_frac_bf16"] = round(tf / tc, 4)
+            out[f"{prefix}{B}"] = d
+        return out
+
+
+def _moe_extras(torch, mb, args, dev, rank, hbm, tc, reps):
+    """Breakdown entries of the default line beyond the decode sweep: the
+    DeepSeek-class 4096-token prefill on the same layers, and the Qwen-class
+    decode (B = 1, 32) and 16384-token prefill on Qwen-class layers."""
+    out = {}
+    pf = MoeBench(torch, "ds", (4096,), False, dev, rank, layers=mb.layers)
+    pf.step(0)
+    out.update(pf.breakdown(min(8, mb.n_layers), hbm, tc, prefix="ds_prefill_"))
+    del pf
+    qn = MoeBench(torch, "qn", (1, 32), True, dev, rank, n_layers=args.layers)
+    for i in range(3):
+        qn.step(i)
+    out.update(qn.breakdown(reps, hbm, tc, prefix="qn_decode_"))
+    qp = MoeBench(torch, "qn", (16384,), False, dev, rank, layers=qn.layers)
+    qp.step(0)
+    out.update(qp.breakdown(min(8, qn.n_layers), hbm, tc, prefix="qn_prefill_"))
+    del qp, qn
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(args, rank, world, dev):
+    import torch
+    import whallm_b200 as W
+    from whallm_b200 import synthetic as S
+    from whallm_b200.graphs import CapturedLayer
+
+    torch.cuda.set_device(dev)
+    hbm, tc, peak_src = _peaks()
+    wl = args.workload
+    res = {"hbm": hbm, "tc": tc, "peak_src": peak_src}
+    if wl in MOE_WORKLOADS:
+        name, batches = MOE_WORKLOADS[wl]
+        mb = MoeBench(torch, name, batches, wl in GRAPHED, dev, rank, n_layers=_n_layers(args, name),
+                      experts=args.experts)
         for i in range(args.warmup):
-            step(i)
+            mb.step(i)
         torch.cuda.synchronize()
         # timed region: whole MoE layer (router + experts + combine)
         clk = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
@@ -270,76 +432,46 @@ def run_ours(args, rank, world, dev):
         torch.cuda.nvtx.range_push("timed")
         s.record()
         for i in range(args.steps):
-            step(i)
+            mb.step(i)
         e.record()
         torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         ms = s.elapsed_time(e) / args.steps
-        # expert-call roofline: time the expert calls alone, same stream
-        torch.cuda.synchronize()
-        s2, e2 = _events(torch)
-        s2.record()
-        for i in range(args.steps):
-            experts_only(i)
-        e2.record()
-        torch.cuda.synchronize()
-        ms_exp = s2.elapsed_time(e2) / args.steps
+        # expert-call roofline: the expert calls alone, same stream
+        ms_exp = mb.timed(mb.experts_step, args.steps)
         clocks = clk.stop() if clk else None
-        # per-batch breakdown: back-to-back calls of one batch size (cycling the
-        # layers, as in the timed step), the whole layer and the expert call alone;
-        # hbm_frac is the expert call's algorithmic bytes over its time
-        def one_expert(i, b):
-            if graphed:
-                ecaps[i % n_layers][b]()
-            else:
-                experts_call(i % n_layers, b, xs[b])
-
-        per_b = {}
-        reps = max(2 * n_layers, min(args.steps, 64))
-        for b, x in enumerate(xs):
-            tb = {}
-            for name_, fn in (("layer", one), ("experts", one_expert)):
-                torch.cuda.synchronize()
-                s3, e3 = _events(torch)
-                s3.record()
-                for i in range(reps):
-                    fn(i, b)
-                e3.record()
-                torch.cuda.synchronize()
-                tb[name_] = s3.elapsed_time(e3) / reps
-            per_b[str(batches[b])] = {"ms": round(tb["layer"], 4), "tok_s": round(batches[b] / tb["layer"] * 1e3, 1),
-                                      "expert_ms": round(tb["experts"], 4),
-                                      "distinct_experts": round(distinct[b], 2),
-                                      "hbm_frac": round(alg_bytes[b] / (tb["experts"] * 1e-3) / (hbm * 1e9), 4)}
+        reps = max(2 * mb.n_layers, min(args.steps, 64))
+        bd = mb.breakdown(reps, hbm, tc)
         # e2e through the public API with host buffers
-        hx = [x.cpu().pin_memory() for x in xs]
-        houts = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in xs]
+        hx = [x.cpu().pin_memory() for x in mb.xs]
+        houts = [torch.empty(x.shape, dtype=torch.bfloat16).pin_memory() for x in mb.xs]
         torch.cuda.synchronize()
-        if graphed:
-            ms_e2e = _e2e_overlapped(torch, dev, caps, hx, houts, args.steps)
+        if mb.graphed:
+            ms_e2e = _e2e_overlapped(torch, dev, mb.caps, hx, houts, args.steps)
         else:
             s4, e4 = _events(torch)
             s4.record()
             for i in range(args.steps):
-                lay = layers[i % n_layers]
-                for b in range(len(xs)):
+                lay = mb.layers[i % mb.n_layers]
+                for b in range(len(hx)):
                     houts[b].copy_(lay.layer(hx[b].to(dev, non_blocking=True)), non_blocking=True)
             e4.record()
             torch.cuda.synchronize()
             ms_e2e = s4.elapsed_time(e4) / args.steps
-        h2d = sum(x.numel() * 2 for x in xs)
-        flops = sum(B * (cfg["k"] + (1 if cfg["shared"] else 0)) * 6 * cfg["H"] * cfg["I"] for B in batches)
-        res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=tokens_per_step, alg_bytes=sum(alg_bytes),
-                        flops=flops, tc_peak=tc, prefill=wl in ("ds_prefill", "qn_prefill"),
-                        per_b=per_b, clocks=clocks, h2d=h2d, d2h=h2d, cfg=cfg, batches=batches,
-                        distinct=distinct, hbm=hbm, peak_src=peak_src,
-                        launches=len(xs) * (2 + 5) if name != "tiny" else len(xs) * (2 + 4),
-                        graphed=graphed, n_layers=n_layers,
-                        layer_bytes=(cfg["E"] + (1 if cfg["shared"] else 0)) * expert_bytes))
+        if wl == "ds_decode" and not args.no_extras and args.experts is None:
+            bd.update(_moe_extras(torch, mb, args, dev, rank, hbm, tc, reps))
+        h2d = sum(x.numel() * 2 for x in mb.xs)
+        prefill = wl in ("ds_prefill", "qn_prefill")
+        res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=sum(mb.alg_bytes),
+                        flops=sum(mb.flops), prefill=prefill, breakdown=bd, clocks=clocks, h2d=h2d, d2h=h2d,
+                        distinct=mb.distinct,
+                        launches=len(mb.xs) * (2 + 5) if name != "tiny" else len(mb.xs) * (2 + 4),
+                        kernel="expert FFN call (wmoe_mxfp4_moe_forward)" if name != "tiny"
+                        else "expert FFN call (wmoe_affine4_moe_forward)"))
         return res
     if wl == "kv_scores":
         # decode scores of one query per sequence against an MXFP8 latent cache:
-        # 8 sequences x 32768 cached tokens x 512 dims per layer, 61 layers (each its own cache)
+        # 8 sequences x 32768 cached tokens x 512 dims per layer, kv_layers layers (each its own cache)
         Bq, Lc, D, n_layer = 8, 32768, 512, args.kv_layers
         caches = []
         for li in range(n_layer):
@@ -352,6 +484,8 @@ def run_ours(args, rank, world, dev):
         for i in range(args.warmup):
             W.kv_scores(q, *caches[i % n_layer], "mxfp8", out=out)
         torch.cuda.synchronize()
+        clk = ClockSampler(dev.index if dev.index is not None else 0)
+        clk.start()
         s, e = _events(torch)
         s.record()
         for _ in range(args.steps):
@@ -359,6 +493,7 @@ def run_ours(args, rank, world, dev):
                 W.kv_scores(q, *caches[li], "mxfp8", out=out)
         e.record()
         torch.cuda.synchronize()
+        clocks = clk.stop()
         ms = s.elapsed_time(e) / args.steps
         per_layer = Bq * Lc * (D + D // 32) + Bq * D * 2 + Bq * Lc * 2
         hq = q.cpu().pin_memory()
@@ -374,9 +509,9 @@ def run_ours(args, rank, world, dev):
         torch.cuda.synchronize()
         ms_e2e = s4.elapsed_time(e4) / args.steps
         res.update(dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=Bq * Lc * n_layer, alg_bytes=per_layer * n_layer,
-                        per_b={}, clocks=None, flops=0, h2d=Bq * D * 2 * n_layer, d2h=Bq * Lc * 2 * n_layer,
-                        cfg={"B": Bq, "L": Lc, "D": D, "layers": n_layer}, batches=(), distinct=[], hbm=hbm,
-                        peak_src=peak_src, launches=3 * n_layer))
+                        breakdown={}, clocks=clocks, flops=0, h2d=Bq * D * 2 * n_layer, d2h=Bq * Lc * 2 * n_layer,
+                        launches=3 * n_layer,
+                        kernel="KV-cache score launch (wkv_mx_scores: query split, tcgen05 block-scaled scores)"))
         return res
     if wl == "qsa":
         # Qwen QSA caches in decode: 12 full-attention layers, each an 8-bit K/V cache of
@@ -454,19 +589,11 @@ def run_ours(args, rank, world, dev):
         ms_e2e = s4.elapsed_time(e4) / args.steps
         h2d = sum(x.numel() * 2 for x in hnews)
         d2h = n_layer * sum(Bq * hk * hd * 2 for _, hk, hd in shapes)
-        res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=Bq * Lc * n_layer, alg_bytes=alg, per_b={},
-                        clocks=clocks, flops=0, h2d=h2d, d2h=d2h,
-                        cfg={"B": Bq, "L": Lc, "layers": n_layer, "caches": [list(x) for x in shapes]}, batches=(),
-                        distinct=[], hbm=hbm, peak_src=peak_src, launches=4 * n_layer,
-                        kernel="history fetch of every QSA cache (k_affine_kv_fetch, K and V in one launch)",
-                        dtype="u32 packed affine 8/4-bit, bf16 scales/biases, bf16 out",
-                        data="synthetic (seeded N(0,1) bf16 keys/values)",
-                        config={"sequences": Bq, "context": Lc, "full_attention_layers": n_layer,
-                                "caches": "K/V 8-bit 2 heads x 256, index 4-bit 1 head x 128, group 32",
-                                "step": "append one row per sequence + fetch the whole history, every cache",
-                                "l2": f"{rd / 1e9:.1f} GB of packed history read and {wr / 1e9:.1f} GB of bf16 "
-                                      "written per step: larger than L2",
-                                "launch": "eager"}))
+        res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=Bq * Lc * n_layer, alg_bytes=alg,
+                        breakdown={"history_read_gb_per_step": round(rd / 1e9, 2),
+                                   "bf16_written_gb_per_step": round(wr / 1e9, 2)},
+                        clocks=clocks, flops=0, h2d=h2d, d2h=d2h, launches=4 * n_layer,
+                        kernel="history fetch of every QSA cache (k_affine_kv_fetch, K and V in one launch)"))
         return res
     if wl == "linear":
         # dense MXFP8 linear (the QuantizedLinear layers V4.1 builds from its
@@ -550,20 +677,14 @@ def run_ours(args, rank, world, dev):
         e4.record()
         torch.cuda.synchronize()
         ms_e2e = s4.elapsed_time(e4) / args.steps
-        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(sweep), alg_bytes=alg, per_b=per_b,
+        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(sweep), alg_bytes=alg, breakdown=per_b,
                         clocks=clocks, flops=0, h2d=sum(T * K * 2 for T in sweep), d2h=sum(T * N * 2 for T in sweep),
-                        cfg={}, batches=sweep, distinct=[], hbm=hbm, peak_src=peak_src, launches=3 * len(sweep),
+                        launches=3 * len(sweep),
                         kernel="dense MXFP8 linear call (wmx_linear: token split, tcgen05 block-scaled GEMM split "
-                               "over K, ordered sum of the K splits)",
-                        dtype="e4m3 weights with E8M0 per 32, bf16 activations, fp32 accumulate",
-                        data="synthetic (seeded N(0,0.02) weights quantized to MXFP8, N(0,1) bf16 rows)",
-                        config={"K": K, "N": N, "rows_per_step": list(sweep), "weight_matrices_cycled": 8,
-                                "l2": "8 x 27 MB of weights cycled: larger than L2",
-                                "launch": "CUDA graph per (rows, matrix); the 4096-row calls eager",
-                                "per_batch": per_b}))
+                               "over K, ordered sum of the K splits)"))
         return res
     if wl == "kv":
-        D, rows_total = 576, 32768 * 8 * 61
+        D, rows_total = 576, 32768 * 8 * args.kv_layers
         chunk = 32768 * 8          # one layer of the 8 x 32768-token context per call
         x = torch.randn(chunk, D, device=dev).to(torch.bfloat16)
         p, sc = W.kv_quantize(x, "fp8_f32_b64")
@@ -575,7 +696,7 @@ def run_ours(args, rank, world, dev):
         s, e = _events(torch)
         s.record()
         for _ in range(args.steps):
-            for _l in range(61):
+            for _l in range(args.kv_layers):
                 W.kv_quantize(x, "fp8_f32_b64", p, sc)
                 W.kv_dequantize(p, sc, "fp8_f32_b64", out)
         e.record()
@@ -583,9 +704,9 @@ def run_ours(args, rank, world, dev):
         ms = s.elapsed_time(e) / args.steps
         per_entry = 576 + 9 * 4 + 1152
         alg = rows_total * per_entry * 2  # quantize (read bf16, write packed) + dequant (read packed, write bf16)
-        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=None, tokens=rows_total, alg_bytes=alg, per_b={}, clocks=None, flops=0,
-                        h2d=0, d2h=0, cfg={"D": D}, batches=(), distinct=[], hbm=hbm, peak_src=peak_src,
-                        launches=2 * 61))
+        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=None, tokens=rows_total, alg_bytes=alg, breakdown={}, clocks=None,
+                        flops=0, h2d=0, d2h=0, launches=2 * args.kv_layers,
+                        kernel="FP8 KV quantize + dequantize (k_kv_quantize, k_kv_dequantize)"))
         return res
     raise SystemExit(f"unknown workload {wl}")
 
@@ -605,8 +726,7 @@ def run_ep(args, rank, world, dev):
     torch.cuda.set_device(dev)
     hbm, tc, peak_src = _peaks()
     wl = args.workload
-    name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn"}[wl]
-    batches = {"ds_decode": SWEEP, "ds_prefill": (4096,), "qn_decode": (1, 32), "qn_prefill": (16384,)}[wl]
+    name, batches = MOE_WORKLOADS[wl]
     decode = wl in ("ds_decode", "qn_decode")
     # decode exchanges over peer memory (CUDA IPC + flags) unless WM_EP_EXCHANGE=nccl
     peer = decode and os.environ.get("WM_EP_EXCHANGE", "peer") != "nccl"
@@ -614,7 +734,9 @@ def run_ep(args, rank, world, dev):
     # experts dealt to the ranks by popularity (the router's per-expert bias),
     # unless WM_EP_PLACEMENT=contiguous
     balanced = os.environ.get("WM_EP_PLACEMENT", "balanced") != "contiguous"
+    extras = wl == "ds_decode" and not args.no_extras
     moes = []
+    prefill_moes = []                                       # the all-to-all form on the same shards (extras)
     owned = []                                              # per layer: this rank's routed expert ids
     cfg = None
     bufs = None
@@ -655,17 +777,18 @@ def run_ep(args, rank, world, dev):
             moes.append(EP.ExpertParallelMoE(router, EP.gpu_local_experts(local, limit), E,
                                              shared=EP.gpu_shared_expert(local, per, limit, gate=gate_fn),
                                              positions=pos))
+        if extras and i < 4:
+            prefill_moes.append(EP.ExpertParallelMoE(router, EP.gpu_local_experts(local, limit), E,
+                                                     shared=EP.gpu_shared_expert(local, per, limit), positions=pos))
         if not peer:
             moes[-1].route_fn = router
         del lay
         torch.cuda.empty_cache()
     H = cfg["H"]
-    E = cfg["E"]
-    e0, per = EP.shard_bounds(E, world, rank)
     xs = [S.make_tokens(B, H, 100 + rank, dev) for B in batches]
     # algorithmic bytes: the distinct local experts each (layer, batch) touches
     # over all ranks' tokens, plus the shared expert, plus activations
-    expert_bytes = DS_EXPERT_BYTES if name == "ds" else QN_EXPERT_BYTES
+    expert_bytes = EXPERT_BYTES[name]
     distinct = [0.0] * len(xs)
     for m, mine in zip(moes, owned):
         for b, x in enumerate(xs):
@@ -725,36 +848,57 @@ def run_ep(args, rank, world, dev):
     if decode:
         del caps           # graphs holding NCCL work go before the process group
         torch.cuda.synchronize()
+    breakdown = {}
+    if prefill_moes:
+        # 4096 tokens per rank through the all-to-all form, max over ranks
+        xp = S.make_tokens(4096, H, 200 + rank, dev)
+        prefill_moes[0](xp)
+        torch.cuda.synchronize()
+        torch.distributed.barrier()
+        s5, e5 = _events(torch)
+        s5.record()
+        reps = 2 * len(prefill_moes)
+        for i in range(reps):
+            prefill_moes[i % len(prefill_moes)](xp)
+        e5.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s5.elapsed_time(e5) / reps], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        pms = float(t.item())
+        breakdown["ep_prefill_4096"] = {"ms": round(pms, 4), "tok_s": round(world * 4096 / pms * 1e3, 1),
+                                        "tokens_per_rank": 4096, "layers_cycled": len(prefill_moes),
+                                        "launch": "eager (NCCL all-to-all)"}
+        del xp
+    prefill_moes.clear()
     if bufs is not None:
         bufs.check()
         del moes
         bufs.close()
     h2d = sum(x.numel() * 2 for x in xs)
-    return dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=alg_bytes, per_b={}, clocks=clocks,
-                h2d=h2d, d2h=h2d, cfg=cfg, batches=batches, distinct=distinct, hbm=hbm, peak_src=peak_src,
+    return dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=alg_bytes, breakdown=breakdown,
+                clocks=clocks, h2d=h2d, d2h=h2d, distinct=distinct, hbm=hbm, tc=tc, peak_src=peak_src,
                 launches=len(xs) * ((11 if peer else 7) if decode else 9), flops=0, ep=True, decode=decode,
-                placement="popularity-balanced (snake order by router bias)" if balanced else "contiguous",
-                launch=("CUDA graph per (layer, batch): peer-memory exchange (CUDA IPC, flags), partial experts"
-                        if peer else "CUDA graph per (layer, batch): NCCL all-gather, partial experts, "
-                        "reduce-scatter") if decode else "eager (NCCL all-to-all)")
+                kernel="whole layer per rank (router, exchange, expert share)")
 
 
 # --------------------------------------------------------------------------
-# reference arm: the oracle port on the host cores
+# reference arm: the oracle restatement on the host cores
 # --------------------------------------------------------------------------
 
-def cpu_reference(args, sample_steps=None):
-    """Times the oracle's restatement of the reference MoE layer (router, grouped
-    expert matmuls that dequantize in the loop, weighted combine, shared expert)
-    on the host cores, on the same synthetic layer the device arm uses (layer 0
-    of rank 0: built with the library's generator on the GPU when one is present,
-    then copied to host memory before timing)."""
+def cpu_reference(args, steps, warmup, budget_s):
+    """Times the oracle's restatement of the reference path on the host cores.
+
+    MoE workloads: the reference MoE layer (router, grouped expert matmuls that
+    dequantize inside the loop, weighted combine, shared expert) on a layer of
+    the workload's configuration built on the host (``oracle/synthetic.py``:
+    seeded weights, the Swift MXFP4 rule; only the experts the sample's tokens
+    are routed to), over a bounded token sample (CPU_SAMPLE).  KV workloads:
+    the numpy restatements of one layer's rows.  No device library is loaded.
+
+    Runs `warmup` untimed steps (fewer if one step is slow), then times `steps`
+    steps, or as many as fit in `budget_s` seconds; returns the counts run."""
     import numpy as np
-    import torch
     from oracle import formats as F
-    from oracle import moe as M
-    from oracle import router as R
-    from whallm_b200 import synthetic as S
 
     threads = os.cpu_count() or 1
     os.environ.setdefault("OMP_NUM_THREADS", str(threads))
@@ -808,64 +952,38 @@ def cpu_reference(args, sample_steps=None):
         sample = ("qsa: one decode update_and_fetch of one sequence at a 32768-token context, one layer's two QSA "
                   "caches (8-bit 2x256 K/V, 4-bit 1x128 index), numpy oracle")
     else:
-        name = {"ds_decode": "ds", "ds_prefill": "ds", "qn_decode": "qn", "qn_prefill": "qn", "tiny": "tiny"}[wl]
-        batches = {"ds_decode": SWEEP, "ds_prefill": (256,), "qn_decode": (1, 32), "qn_prefill": (1024,),
-                   "tiny": (64,)}[wl]
-        dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
-        if dev.type != "cuda":
-            raise RuntimeError("the CPU arm builds its synthetic layer with the device generator")
-        lay = S.make_layer(name, dev, seed=0)
-        cfg = lay.cfg
-        H, E, k = cfg["H"], cfg["E"], cfg["k"]
-        xs_t = [S.make_tokens(B, H, 100, dev) for B in batches]
-        xs = [x.float().cpu().numpy() for x in xs_t]
-        bits = lambda t: t.cpu().view(torch.int16).numpy().view(np.uint16)
-        wg = bits(lay.gate_weight)
-        lb = None if lay.logit_bias is None else lay.logit_bias.cpu().numpy()
-        sg = None if lay.shared_gate is None else bits(lay.shared_gate).reshape(-1)
-        if name == "tiny":
-            a = lay.experts
-            ex = M.Affine4Experts(a.w13.cpu().numpy().view(np.uint32), bits(a.w13_scales), bits(a.w13_biases),
-                                  a.w2.cpu().numpy().view(np.uint32), bits(a.w2_scales), bits(a.w2_biases),
-                                  M.GATE_UP, 0.0, 64)
-        else:
-            g = lay.experts
-            w13 = g.w13 if name == "ds" else g.gate_up
-            s13 = g.w13_scales if name == "ds" else g.gate_up_scales
-            w2 = g.w2 if name == "ds" else g.down
-            s2 = g.w2_scales if name == "ds" else g.down_scales
-            ex = M.MXFP4Experts(w13.cpu().numpy(), s13.cpu().numpy(), w2.cpu().numpy(), s2.cpu().numpy(),
-                                M.UP_GATE if name == "ds" else M.GATE_UP, 10.0 if name == "ds" else 0.0)
-        del lay
-        torch.cuda.empty_cache()
+        from oracle import synthetic as SY
+        name, _ = MOE_WORKLOADS[wl]
+        batches = CPU_SAMPLE[wl]
+        lay = SY.HostLayer(name, seed=0)
+        H = lay.cfg["H"]
+        xs = [SY.tokens(B, H, 100 + j) for j, B in enumerate(batches)]
+        for x in xs:                                   # build the experts the sample is routed to
+            lay.prepare(lay.route(x)[0])
 
         def step():
             for x in xs:
-                xb = F.f32_to_bf16_bits(x)
-                if name == "ds":
-                    _, idx, w, _ = R.route(xb, wg, k, R.SCORE_SQRTSOFTPLUS, logit_bias=lb, norm_eps=1e-20,
-                                           route_scale=1.5)
-                    M.moe_forward(x, idx, w, ex, shared_expert=E)
-                elif name == "qn":
-                    _, idx, w, sh = R.route(xb, wg, k, R.SCORE_SOFTMAX_BF16, logit_bias=lb, norm_eps=0.0,
-                                            wg_shared_bits=sg)
-                    M.moe_forward(x, idx, w, ex, shared_expert=E, shared_weight=sh)
-                else:
-                    _, idx, w, _ = R.route(xb, wg, k, R.SCORE_SOFTMAX_BF16, norm_eps=0.0)
-                    M.moe_forward(x, idx, w, ex)
+                lay.forward(x)                         # router + experts + combine + shared expert
 
         tokens = sum(batches)
-        sample = (f"{wl}: batches {list(batches)} ({tokens} tokens) on the full-size layer; oracle router + "
-                  f"C expert matmuls with in-loop dequant, {threads} threads")
-    step()
-    steps = sample_steps or max(1, args.steps)
+        sample = (f"{wl}: batches {list(batches)} ({tokens} tokens per step) on a full-size layer built on the host "
+                  f"({lay.experts_built} experts materialised); oracle router + C expert matmuls with in-loop "
+                  f"dequant, {threads} threads")
     t0 = time.perf_counter()
-    for _ in range(steps):
+    step()
+    t_step = time.perf_counter() - t0
+    warm = 1
+    while warm < warmup and (warm + 1) * t_step < budget_s / 4:
         step()
-    dt = (time.perf_counter() - t0) / steps
+        warm += 1
+    n = steps if steps * t_step <= budget_s else max(1, int(budget_s / t_step))
+    t0 = time.perf_counter()
+    for _ in range(n):
+        step()
+    dt = (time.perf_counter() - t0) / n
     # the KV restatements are single-threaded numpy; the MoE arm runs the C kernels on every host thread
     cores = 1 if wl in ("kv", "kv_scores", "qsa", "linear") else threads
-    return dict(value=tokens / dt, sec_per_step=dt, tokens=tokens, cores=cores, sample=sample)
+    return dict(value=tokens / dt, sec_per_step=dt, tokens=tokens, cores=cores, sample=sample, steps=n, warmup=warm)
 
 
 def main():
@@ -885,6 +1003,8 @@ def main():
     ap.add_argument("--kv-layers", type=int, default=61,
                     help="kv and kv_scores workloads: cache layers held on the device (61 in the configuration; "
                          "a few for ncu captures, which keep each layer's cache resident)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the breakdown's prefill and Qwen-class entries of the default workload")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
@@ -905,15 +1025,17 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        r = cpu_reference(args, sample_steps=max(1, min(args.steps, 3)))
-        line = {"impl": "reference", "metric": metric, "value": round(r["value"], 3), "unit": unit, "n_gpus": args.gpus,
-                "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(r["sec_per_step"] * 1e3, 3),
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic", "config": {"workload": args.workload},
+        r = cpu_reference(args, steps=args.steps, warmup=args.warmup, budget_s=REF_BUDGET_S)
+        line = {"impl": "reference", "metric": metric, "value": round(r["value"], 3), "unit": unit,
+                "n_gpus": args.gpus, "steps": r["steps"], "warmup": r["warmup"],
+                "ms_per_step": round(r["sec_per_step"] * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": workload_dtype(args.workload), "data": workload_data(args.workload),
+                "config": workload_config(args, args.gpus),
                 "cpu_baseline": {"value": round(r["value"], 3), "unit": unit, "cores": r["cores"], "kind": "port",
                                  "sample": r["sample"]},
                 "e2e": {"value": round(r["value"], 3), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-                "note": "reference MLX CPU backend unavailable (mlx not installable offline); oracle port timed"}
+                "note": ("reference MLX CPU backend unavailable (mlx not installable offline); the oracle's "
+                         "restatement timed on the host cores; steps and warmup are the counts actually run")}
         print(json.dumps(line), flush=True)
         return
 
@@ -922,8 +1044,7 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = torch.device("cuda", local)
-    use_ep = world > 1 and args.workload in ("ds_decode", "ds_prefill", "qn_decode", "qn_prefill")
-    r = run_ep(args, rank, world, dev) if use_ep else run_ours(args, rank, world, dev)
+    r = run_ep(args, rank, world, dev) if _ep(args, world) else run_ours(args, rank, world, dev)
     ms = r["ms"]
     if world > 1:
         t = torch.tensor([ms, r["ms_e2e"] or 0.0, r["ms_exp"]], device=dev)
@@ -935,17 +1056,12 @@ def main():
     if rank == 0:
         hbm = r["hbm"]
         achieved = r["alg_bytes"] / (ms_exp * 1e-3) / 1e9
-        if r.get("prefill"):
-            # prefill is compute-bound: useful FLOPs of the expert FFN over the measured
-            # dense bf16 tensor peak (the block-scaled MMAs run two e4m3 terms of the
-            # tokens, twice these FLOPs in tensor work)
-            achieved_tf = r["flops"] / (ms_exp * 1e-3) / 1e12
-        # DRAM bytes per step of the expert calls: per-expert traffic measured by
+        # DRAM bytes per step of the dominant kernel: per-expert traffic measured by
         # ncu on a smaller case (profiles/traffic.json), scaled by the distinct
         # experts this workload streams per step
         traffic = None
         prof = os.path.join(ROOT, "profiles", "traffic.json")
-        if os.path.exists(prof) and (r.get("distinct") or args.workload in ("qsa", "linear")):
+        if os.path.exists(prof) and (r.get("distinct") or args.workload in ("qsa", "linear", "kv", "kv_scores")):
             try:
                 t = json.load(open(prof)).get(args.workload)
                 if t and r.get("distinct"):
@@ -954,71 +1070,43 @@ def main():
                     # DRAM bytes of one call of the dominant kernel, captured at the bench's own size
                     traffic = round(t["bytes_per_call"] * t.get("calls_per_step", 1))
                 elif t:
-                    # DRAM bytes per algorithmic byte of the fetch, from one capture at a smaller context
+                    # DRAM bytes per algorithmic byte, from one capture at a smaller size
                     traffic = round(t["dram_per_algorithmic_byte"] * r["alg_bytes"])
             except Exception:
                 traffic = None
-        if r.get("ep"):
-            line_ep = {
-                "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "mxfp4 weights, bf16 activations, fp32 accumulate",
-                "data": "synthetic (seeded N(0,0.02) MXFP4 experts, N(0,1) bf16 tokens, Zipf-skewed router)",
-                "config": {"workload": args.workload, "batches": list(r["batches"]), "tokens_per_rank": r["tokens"],
-                           "layers_cycled": args.layers, "parallelism": f"ep{world}",
-                           "experts_per_rank": r["cfg"]["E"] // world,
-                           "placement": r.get("placement", "contiguous"),
-                           "launch": r.get("launch", "eager (NCCL all-to-all)")},
-                "e2e": {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2), "unit": unit,
-                        "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"]},
-                "roofline": ({"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                              "frac": round(achieved / hbm, 4), "traffic": traffic,
-                              "algorithmic_bytes_per_step": round(r["alg_bytes"]),
-                              "kernel": "whole layer per rank (router, collectives, expert share), "
-                                        + r["peak_src"] + " HBM peak"} if r.get("decode") else None),
-                "gpu_launches": r["launches"] * args.steps, "clocks": r["clocks"],
-            }
-            print(json.dumps(line_ep), flush=True)
-            torch.distributed.barrier()
-            torch.distributed.destroy_process_group()
-            return
-        config = {"workload": args.workload, "batches": list(r["batches"]),
-                  "tokens_per_step": r["tokens"], "layers_cycled": r.get("n_layers", args.layers),
-                  "l2": (f"{r.get('n_layers', args.layers)} resident layers "
-                         f"({r.get('n_layers', args.layers) * r.get('layer_bytes', 0) / 1e9:.2f} GB of experts) "
-                         "cycled per step: weights larger than L2"),
-                  "parallelism": "replicas" if world > 1 else "single GPU",
-                  "launch": "CUDA graph per (layer, batch)" if r.get("graphed") else "eager",
-                  "per_batch": r["per_b"]}
-        if r.get("config"):
-            config = dict(r["config"], workload=args.workload,
-                          parallelism="replicas" if world > 1 else "single GPU")
+        if r.get("prefill"):
+            # prefill is compute-bound: useful FLOPs of the expert FFN over the measured
+            # dense bf16 tensor peak (the block-scaled MMAs run two e4m3 terms of the
+            # tokens, twice these FLOPs in 8-bit tensor work at twice the 16-bit rate)
+            achieved_tf = r["flops"] / (ms_exp * 1e-3) / 1e12
+            roof = {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": r["tc"], "unit": "TFLOP/s",
+                    "frac": round(achieved_tf / r["tc"], 4), "traffic": traffic,
+                    "algorithmic_flops_per_step": r["flops"],
+                    "kernel": r["kernel"] + ", " + r["peak_src"] + " dense bf16 peak (the rate of the two-term "
+                              "e4m3 token operand)"}
+        elif r.get("ep") and not r.get("decode"):
+            roof = None
+        else:
+            roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                    "frac": round(achieved / hbm, 4), "traffic": traffic,
+                    "algorithmic_bytes_per_step": round(r["alg_bytes"]),
+                    "kernel": r["kernel"] + ", " + r["peak_src"] + " HBM peak"}
         line = {
             "metric": metric, "value": round(value, 2), "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": r.get("dtype", "mxfp4 weights, bf16 activations, fp32 accumulate"),
-            "data": r.get("data", "synthetic (seeded N(0,0.02) MXFP4 experts, N(0,1) bf16 tokens, Zipf-skewed router)"),
-            "config": config,
+            "vs_baseline": None, "dtype": workload_dtype(args.workload), "data": workload_data(args.workload),
+            "config": workload_config(args, world),
             "e2e": None if ms_e2e is None else {"value": round(r["tokens"] * world / (ms_e2e * 1e-3), 2),
                                                  "unit": unit, "h2d_bytes_per_step": r["h2d"],
                                                  "d2h_bytes_per_step": r["d2h"]},
-            "roofline": ({"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                          "frac": round(achieved / hbm, 4), "traffic": traffic,
-                          "algorithmic_bytes_per_step": r["alg_bytes"],
-                          "kernel": r.get("kernel", "expert FFN call (wmoe_mxfp4_moe_forward)") + ", " +
-                                    r["peak_src"] + " HBM peak"}
-                         if not r.get("prefill") else
-                         {"bound": "tensor", "achieved": round(achieved_tf, 1), "peak": r["tc_peak"],
-                          "unit": "TFLOP/s", "frac": round(achieved_tf / r["tc_peak"], 4), "traffic": traffic,
-                          "algorithmic_flops_per_step": r["flops"],
-                          "kernel": "expert FFN call (wmoe_mxfp4_moe_forward), " + r["peak_src"] +
-                                    " dense bf16 peak (f16 MMA)"}),
+            "roofline": roof,
             "gpu_launches": r["launches"] * args.steps,
             "clocks": r["clocks"],
+            "breakdown": r.get("breakdown", {}),
         }
         if not args.no_cpu_baseline and world == 1:
             try:
-                cb = cpu_reference(args, sample_steps=1)
+                cb = cpu_reference(args, steps=3, warmup=1, budget_s=BASELINE_BUDGET_S)
                 line["cpu_baseline"] = {"value": round(cb["value"], 3), "unit": unit, "cores": cb["cores"],
                                         "kind": "port", "sample": cb["sample"]}
             except Exception as exc:  # pragma: no cover

@@ -19,7 +19,7 @@ LIB = os.path.join(HERE, "liboracle.so")
 
 
 def build(force: bool = False) -> str:
-    srcs = [os.path.join(HERE, "c", n) for n in ("router_ref.c", "moe_ref.c")]
+    srcs = [os.path.join(HERE, "c", n) for n in ("router_ref.c", "moe_ref.c", "synth_ref.c")]
     if not force and os.path.exists(LIB) and all(os.path.getmtime(LIB) >= os.path.getmtime(s) for s in srcs):
         return LIB
     tmp = os.path.join(HERE, "_build")
@@ -28,6 +28,7 @@ def build(force: bool = False) -> str:
     flags = {
         "router_ref.c": ["-O2", "-ffp-contract=off", "-fno-fast-math", "-mfma", "-fopenmp"],
         "moe_ref.c": ["-O3", "-mavx2", "-mfma", "-ffast-math", "-fopenmp"],
+        "synth_ref.c": ["-O3", "-ffp-contract=off", "-fno-fast-math", "-fopenmp"],
     }
     for s in srcs:
         o = os.path.join(tmp, os.path.basename(s) + ".o")

@@ -258,3 +258,29 @@ def test_router_bf16_gate_ties_go_to_the_lower_id():
     _, idx, w, _ = R.route(xb, wb, 5, R.SCORE_SOFTMAX_BF16, norm_eps=0.0)
     assert idx.tolist() == [[0, 1, 2, 3, 4]] * 2
     assert np.all(w == _bf16_round(np.float32(0.2)))
+
+
+def test_host_mxfp4_quantizer_equals_the_numpy_restatement():
+    # the C quantizer the CPU baseline builds its layers with gives the bytes of formats.mxfp4_quantize_values
+    from oracle import synthetic as SY
+    rng = np.random.default_rng(12)
+    v = F.round_bf16(rng.normal(0, 0.02, (64, 512)).astype(np.float32))
+    v[0, :32] = 0.0                                                  # all-zero group
+    v[1, :32] *= np.float32(1e-30)                                   # tiny scales (clamped exponent)
+    v[2, :32] = np.float32(6.0) * np.float32(2.0 ** 100)             # huge values
+    v[3, 32:64] = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0, -0.25] * 4, np.float32)   # e2m1 ties
+    v[4, :32] = -0.0
+    p, s = SY.mxfp4_quantize(v)
+    rp, rs = F.mxfp4_quantize_values(v)
+    np.testing.assert_array_equal(p, rp)
+    np.testing.assert_array_equal(s, rs)
+
+
+def test_host_normal_generator_is_seeded_bf16_normal():
+    from oracle import synthetic as SY
+    a = SY.normal_bf16(3, 5, (1000, 1001), 0.02)
+    b = SY.normal_bf16(3, 5, (1000, 1001), 0.02)
+    c = SY.normal_bf16(3, 6, (1000, 1001), 0.02)
+    assert np.array_equal(a, b) and not np.array_equal(a, c)
+    assert np.array_equal(a, F.round_bf16(a))
+    assert abs(float(a.mean())) < 1e-4 and abs(float(a.std()) - 0.02) < 1e-4
