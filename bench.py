@@ -684,6 +684,8 @@ def run_ours(args, rank, world, dev):
                                "over K, ordered sum of the K splits)"))
         return res
     if wl == "kv":
+        # quantize every row of a 8 x 32768-token MLA cache (576 = 512 latent + 64 rope,
+        # e4m3 with an fp32 scale per 64), then dequantize it, layer by layer
         D, rows_total = 576, 32768 * 8 * args.kv_layers
         chunk = 32768 * 8          # one layer of the 8 x 32768-token context per call
         x = torch.randn(chunk, D, device=dev).to(torch.bfloat16)
@@ -693,6 +695,8 @@ def run_ours(args, rank, world, dev):
             W.kv_quantize(x, "fp8_f32_b64", p, sc)
             W.kv_dequantize(p, sc, "fp8_f32_b64", out)
         torch.cuda.synchronize()
+        clk = ClockSampler(dev.index if dev.index is not None else 0)
+        clk.start()
         s, e = _events(torch)
         s.record()
         for _ in range(args.steps):
@@ -701,12 +705,70 @@ def run_ours(args, rank, world, dev):
                 W.kv_dequantize(p, sc, "fp8_f32_b64", out)
         e.record()
         torch.cuda.synchronize()
+        clocks = clk.stop()
         ms = s.elapsed_time(e) / args.steps
         per_entry = 576 + 9 * 4 + 1152
         alg = rows_total * per_entry * 2  # quantize (read bf16, write packed) + dequant (read packed, write bf16)
-        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=None, tokens=rows_total, alg_bytes=alg, breakdown={}, clocks=None,
-                        flops=0, h2d=0, d2h=0, launches=2 * args.kv_layers,
-                        kernel="FP8 KV quantize + dequantize (k_kv_quantize, k_kv_dequantize)"))
+        # the two kernels alone, for the breakdown
+        tq = _events(torch)
+        td = _events(torch)
+        tq[0].record()
+        for _l in range(args.kv_layers):
+            W.kv_quantize(x, "fp8_f32_b64", p, sc)
+        tq[1].record()
+        td[0].record()
+        for _l in range(args.kv_layers):
+            W.kv_dequantize(p, sc, "fp8_f32_b64", out)
+        td[1].record()
+        torch.cuda.synchronize()
+        half = chunk * per_entry * args.kv_layers
+        bd = {"quantize": {"ms_per_layer": round(tq[0].elapsed_time(tq[1]) / args.kv_layers, 4),
+                           "hbm_frac": round(half / (tq[0].elapsed_time(tq[1]) * 1e-3) / (hbm * 1e9), 4)},
+              "dequantize": {"ms_per_layer": round(td[0].elapsed_time(td[1]) / args.kv_layers, 4),
+                             "hbm_frac": round(half / (td[0].elapsed_time(td[1]) * 1e-3) / (hbm * 1e9), 4)}}
+        # e2e: every layer's rows come up from pinned host memory and its dequantized rows go back, on two
+        # copy streams overlapping the kernels of the neighbouring layers (double-buffered device rows)
+        hx = x.cpu().pin_memory()
+        hout = torch.empty_like(hx).pin_memory()
+        dx = [torch.empty_like(x) for _ in range(2)]
+        dout = [torch.empty_like(x) for _ in range(2)]
+        main = torch.cuda.current_stream(dev)
+        cs_in, cs_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        ev_in = [torch.cuda.Event() for _ in range(2)]
+        ev_q = [torch.cuda.Event() for _ in range(2)]
+        ev_c = [torch.cuda.Event() for _ in range(2)]
+        ev_out = [torch.cuda.Event() for _ in range(2)]
+        for ev in ev_q + ev_out:
+            ev.record(main)
+        n_e2e = min(args.steps, 2)
+        torch.cuda.synchronize()
+        s4, e4 = _events(torch)
+        s4.record()
+        for j in range(n_e2e * args.kv_layers):
+            b = j % 2
+            cs_in.wait_event(ev_q[b])
+            with torch.cuda.stream(cs_in):
+                dx[b].copy_(hx, non_blocking=True)
+                ev_in[b].record(cs_in)
+            main.wait_event(ev_in[b])
+            main.wait_event(ev_out[b])
+            W.kv_quantize(dx[b], "fp8_f32_b64", p, sc)
+            ev_q[b].record(main)
+            W.kv_dequantize(p, sc, "fp8_f32_b64", dout[b])
+            ev_c[b].record(main)
+            cs_out.wait_event(ev_c[b])
+            with torch.cuda.stream(cs_out):
+                hout.copy_(dout[b], non_blocking=True)
+                ev_out[b].record(cs_out)
+        main.wait_stream(cs_out)
+        e4.record()
+        torch.cuda.synchronize()
+        ms_e2e = s4.elapsed_time(e4) / n_e2e
+        layer_bytes = chunk * D * 2
+        res.update(dict(ms=ms, ms_exp=ms, ms_e2e=ms_e2e, tokens=rows_total, alg_bytes=alg, breakdown=bd,
+                        clocks=clocks, flops=0, h2d=layer_bytes * args.kv_layers, d2h=layer_bytes * args.kv_layers,
+                        launches=2 * args.kv_layers,
+                        kernel="FP8 KV quantize + dequantize (k_kv_fp8_quantize, k_kv_fp8_dequantize)"))
         return res
     raise SystemExit(f"unknown workload {wl}")
 

@@ -379,7 +379,7 @@ KV_FP8_F32_B64 = 0    # fp32 scale = amax/448 per 64 values
 KV_FP8_UE8M0_B32 = 1  # PackedRows 'fp8_ue8m0' (packed_cache.py:24-45)
 KV_FP4_E4M3_B16 = 2   # PackedRows 'fp4_e4m3'
 KV_FP4_UE8M0_B32 = 3  # PackedRows 'fp4_ue8m0'
-KV_MXFP8_B32 = 4      # MXFP8 (e4m3 + E8M0 per 32), OCP shared-exponent rule
+KV_MXFP8_B32 = 4      # MXFP8 (e4m3 + E8M0 per 32), OCP MX v1.0 conversion rule
 KV_MXFP4_B32 = 5      # MXFP4 index copy (e2m1 + E8M0 per 32), Swift/MLX rule
 
 KV_BLOCK = {0: 64, 1: 32, 2: 16, 3: 32, 4: 32, 5: 32}
@@ -398,9 +398,17 @@ def kv_quantize(x_f32: np.ndarray, fmt: int):
       e4m3 scale (fp4_e4m3): s = from_fp8(to_fp8(max(amax, 6*2^-9)/6)).
     fmt 0 (BASELINE): s = amax/448 in fp32 (amax == 0 -> s = 0, payload 0),
       payload = to_fp8(clip(x/s, +-448)); scales stored as float32.
-    fmt 4 (MXFP8, OCP MX rule by analogy with the pinned MXFP4 rule):
-      e = clamp(floor(log2 amax) - 8, -127, 127), byte e + 127,
-      payload = to_fp8(clip(x*2^-e, +-448)); amax == 0 -> byte 0, payload 0.
+    fmt 4 (MXFP8: mx.quantize(mode="mxfp8"), fp8_cache.py:112): the OCP
+      Microscaling Formats (MX) Specification v1.0 conversion of a 32-value
+      block to MXFP8 E4M3 (section 6.3; E8M0 scale section 5.4; E4M3 element
+      section 5.3): shared exponent X = floor(log2 max|V|) - emax_elem with
+      emax_elem = 8 for E4M3 (largest normal 1.75 * 2^8 = 448), stored as the
+      E8M0 byte X + 127 and clamped to the byte's finite range [-127, 127];
+      elements P_i = V_i / 2^X rounded to nearest even in E4M3 and clamped to
+      +-448 (E4M3 has no infinity, overflows saturate); a block of zeros
+      (log2 0 undefined) stores scale byte 0 and zero elements.  The same rule
+      with emax_elem = 2 (E2M1) is what the Swift MXFP4 quantizer implements
+      (MXFP4.swift:19-37, pinned by its known-answer tests).
     fmt 5 (MXFP4 index copy): the Swift MXFP4 rule (mxfp4_quantize_values)."""
     x = np.ascontiguousarray(x_f32, np.float32)
     D = x.shape[-1]

@@ -147,3 +147,73 @@ def test_fp8_kv_named_entry_points(dev, block, sf, fmt):
     torch.cuda.synchronize()
     assert torch.equal(p, p2) and torch.equal(s, s2)
     assert torch.equal(out, W.kv_dequantize(p, s, fmt))
+
+
+def _all_finite_bf16_rows(D, order):
+    b = np.arange(65536, dtype=np.uint32).astype(np.uint16)
+    b = b[((b.astype(np.uint32) >> 7) & 0xFF) != 0xFF]                  # drop inf / NaN
+    if order == "shuffled":
+        b = np.random.default_rng(5).permutation(b)
+    else:
+        b = b[np.argsort(np.abs(F.bf16_bits_to_f32(b)), kind="stable")]  # blocks of neighbouring magnitudes
+    n = (len(b) // D) * D
+    return b[:n].reshape(-1, D)
+
+
+@pytest.mark.parametrize("fmt", [F.KV_FP8_F32_B64, F.KV_FP8_UE8M0_B32, F.KV_MXFP8_B32])
+@pytest.mark.parametrize("order", ["shuffled", "sorted"])
+def test_e4m3_kv_every_bf16_value_vs_oracle(dev, fmt, order):
+    """Every finite bf16 value through the vectorised e4m3 row kernels: payload,
+    scales and dequantized rows bit-exact against the oracle (sorted blocks
+    put each scale over values of one magnitude, so every e4m3 binade,
+    subnormals and rounding midpoints are reached)."""
+    bits = _all_finite_bf16_rows(576 if fmt == F.KV_FP8_F32_B64 else 512, order)
+    x = F.bf16_bits_to_f32(bits)
+    p, s = W.kv_quantize(_bf16(bits, dev), fmt)
+    rp, rs = F.kv_quantize(x, fmt)
+    np.testing.assert_array_equal(p.cpu().numpy(), rp)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint8), rs.view(np.uint8))
+    d = W.kv_dequantize(p, s, fmt)
+    D = bits.shape[1]
+    np.testing.assert_array_equal(_bits(d), F.f32_to_bf16_bits(F.kv_dequantize(rp, rs, fmt, D)))
+
+
+def test_fp8_f32_scale_quotients_on_e4m3_midpoints(dev):
+    """Blocks whose quotients v / s fall exactly on (and one bf16 step beside)
+    e4m3 rounding midpoints, with scales that are not powers of two: the
+    reciprocal product would round some of them the wrong way, the kernel's
+    exact-division fallback must not."""
+    mids = F.e4m3_to_f32(np.arange(1, 0x7E, dtype=np.uint8))
+    mids = ((mids[:-1] + mids[1:]) / 2).astype(np.float32)            # midpoints between neighbouring codes
+    rows = []
+    for k in (3.0, 5.0, 7.0, 0.6, 1.7, 9.0, 11.0, 13.0):
+        v = F.round_bf16((mids * np.float32(k)).astype(np.float32))
+        v = np.concatenate([v, F.bf16_bits_to_f32(F.f32_to_bf16_bits(v) + 1), F.bf16_bits_to_f32(F.f32_to_bf16_bits(v) - 1)])
+        for c0 in range(0, len(v), 63):
+            blk = np.zeros(64, np.float32)
+            chunk = v[c0:c0 + 63]
+            blk[:len(chunk)] = chunk
+            blk[63] = np.float32(448.0 * k)                              # amax, so s = float32(448 k / 448)
+            rows.append(blk)
+    flat = np.concatenate(rows)                                          # 64-value blocks, 9 per 576-row
+    x = F.round_bf16(flat[: (flat.size // 576) * 576].reshape(-1, 576))
+    bits = F.f32_to_bf16_bits(x)
+    p, s = W.kv_quantize(_bf16(bits, dev), F.KV_FP8_F32_B64)
+    rp, rs = F.kv_quantize(x, F.KV_FP8_F32_B64)
+    np.testing.assert_array_equal(p.cpu().numpy(), rp)
+    np.testing.assert_array_equal(s.cpu().numpy().view(np.uint8), rs.view(np.uint8))
+
+
+def test_fp8_dequantize_nan_codes_and_scales(dev):
+    # NaN payload codes and non-finite scales take the scalar path: NaN is 0x7FC0 as in the oracle
+    rng = np.random.default_rng(9)
+    p = rng.integers(0, 256, (64, 576), dtype=np.uint8)
+    p[0, :8] = 0x7F
+    p[1, 8:16] = 0xFF
+    s = rng.uniform(0.01, 2.0, (64, 9)).astype(np.float32)
+    s[2, 0] = np.inf
+    s[3, 1] = np.nan
+    d = W.kv_dequantize(torch.from_numpy(p).to(dev), torch.from_numpy(s).to(dev), F.KV_FP8_F32_B64)
+    with np.errstate(invalid="ignore"):
+        ref = F.f32_to_bf16_bits(F.kv_dequantize(p, s, F.KV_FP8_F32_B64, 576))
+    np.testing.assert_array_equal(_bits(d), ref)

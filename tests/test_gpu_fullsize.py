@@ -189,7 +189,7 @@ def test_constant_weights_give_the_dequantize_then_matmul_result(dev, path, T):
     for e in (1, 0):
         g, d, u = vals[e]
         gate, up = H * g, H * u
-        h = F.round_bf16(np.float32(gate / (1.0 + np.exp(-gate)) * up))
+        h = float(F.round_bf16(np.float32(gate / (1.0 + np.exp(-gate)) * up))[0])
         exp.append(np.float32(I * h * d))
     ref = np.broadcast_to(np.array(exp, np.float32)[None, :, None], (T, 2, H))
     np.testing.assert_array_equal(_f32(out), F.round_bf16(ref))

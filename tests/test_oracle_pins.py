@@ -284,3 +284,57 @@ def test_host_normal_generator_is_seeded_bf16_normal():
     assert np.array_equal(a, b) and not np.array_equal(a, c)
     assert np.array_equal(a, F.round_bf16(a))
     assert abs(float(a.mean())) < 1e-4 and abs(float(a.std()) - 0.02) < 1e-4
+
+
+# Blocks for the OCP Microscaling Formats (MX) Specification v1.0 conversion to MXFP8 E4M3: shared
+# exponent X = floor(log2 max|V|) - 8, E8M0 byte X + 127, elements V / 2^X rounded to nearest even in
+# E4M3 and saturated at +-448.
+_MX8 = [[448.0], [1.0], [500.0, 1.0], [512.0, -3.0], [0.75, 0.0078125], [6.0, 1.0625], [3.0e-5, -1.0e-6]]
+
+
+def _e4m3(v):
+    return int(F.f32_to_e4m3(np.array([v], np.float32))[0])
+
+
+def test_mxfp8_rule_follows_the_ocp_mx_conversion():
+    from oracle.formats import kv_quantize, KV_MXFP8_B32
+    for vals in _MX8:
+        block = np.zeros(32, np.float32)
+        block[:len(vals)] = vals
+        p, s = kv_quantize(block[None], KV_MXFP8_B32)
+        amax = float(np.max(np.abs(block)))
+        X = int(np.floor(np.log2(amax))) - 8
+        assert int(s[0, 0]) == X + 127
+        for i, v in enumerate(vals):
+            assert int(p[0, i]) == _e4m3(np.clip(v / 2.0 ** X, -448, 448)), (vals, i)
+
+
+def test_mxfp8_rule_hand_checked_codes():
+    # codes written out from the E4M3 layout (sign, 4 exponent bits with bias 7, 3 mantissa bits)
+    cases = [([448.0], 127, {0: 0x7E}), ([1.0], 119, {0: 0x78}), ([500.0, 1.0], 127, {0: 0x7E, 1: 0x38}),
+             ([512.0, -3.0], 128, {0: 0x78, 1: 0xBC}),
+             ([6.0, 1.0625], 121, {0: 0x7C, 1: 0x68}),     # 1.0625 * 2^6: a tie between 1.0 and 1.125 -> 1.0
+             ([0.0] * 32, 0, {0: 0x00, 31: 0x00})]
+    from oracle.formats import kv_quantize, KV_MXFP8_B32
+    for vals, byte, codes in cases:
+        block = np.zeros(32, np.float32)
+        block[:len(vals)] = vals
+        p, s = kv_quantize(block[None], KV_MXFP8_B32)
+        assert int(s[0, 0]) == byte, vals
+        for i, c in codes.items():
+            assert int(p[0, i]) == c, (vals, i, hex(int(p[0, i])))
+
+
+def test_mxfp8_scale_byte_clamps_and_ties_round_to_even():
+    from oracle.formats import kv_quantize, KV_MXFP8_B32
+    # max 2^-130 (a float32 subnormal): floor(log2) - 8 = -138 clamps to the smallest E8M0 exponent -127
+    block = np.zeros(32, np.float32)
+    block[0] = np.float32(2.0 ** -130)
+    _, s = kv_quantize(block[None], KV_MXFP8_B32)
+    assert int(s[0, 0]) == 0
+    # max 256 (X = 0): 1.0625 lies halfway between the E4M3 values 1.0 and 1.125 -> the even code (1.0)
+    block = np.zeros(32, np.float32)
+    block[:3] = [256.0, 1.0625, 1.1875]
+    p, s = kv_quantize(block[None], KV_MXFP8_B32)
+    assert int(s[0, 0]) == 127
+    assert int(p[0, 1]) == 0x38 and int(p[0, 2]) == 0x3A   # 1.1875 halfway between 1.125 and 1.25 -> 1.25

@@ -6,6 +6,8 @@
 // and write contiguous spans.  Results are bit-exact against the CPU
 // restatement: only IEEE-exact float32 operations are used and this file is
 // compiled with -fmad=false.
+#include <cuda_fp16.h>
+
 #include <algorithm>
 
 #include "wm_common.cuh"
@@ -523,10 +525,167 @@ __global__ void k_kv_dequantize(const uint8_t *__restrict__ payload, const void 
   }
 }
 
+// ---------------------------------------------- e4m3 KV rows, vectorised ---
+//
+// The three e4m3 row formats (WKV_FP8_F32_B64: fp32 scale amax/448 per 64;
+// WKV_FP8_UE8M0_B32: PackedRows ue8m0 per 32; WKV_MXFP8_B32: E8M0 per 32) as
+// coalesced streaming passes.  A thread owns 8 consecutive values: one
+// 16-byte bf16 load and one 8-byte e4m3 store (dequantize: the reverse), so a
+// warp moves 512 + 256 contiguous bytes.  The G = block / 8 threads of a
+// scale block are adjacent lanes and take the block maximum with xor
+// shuffles; the block's first lane writes the scale.  Bytes and scales equal
+// kv_quant_block's (the per-block kernel kept for the 4-bit formats):
+//   * the e4m3 encode is cvt.rn.satfinite.e4m3x2.f32 on values already
+//     clamped to +-448, i.e. round to nearest even as wm_f32_to_e4m3;
+//   * for the fp32-scale format the quotient v / s is v * (1/s) except where
+//     that product lies within 8 float32 ulps of an e4m3 rounding midpoint
+//     (or below 2^-6, the e4m3 subnormal range), or where 1/s overflows
+//     (s < 2^-128): there the exact quotient is taken.  The product differs from the quotient by less than 2 ulps, so
+//     away from a midpoint both round to the same e4m3 value;
+//   * the power-of-two scales divide exactly as multiplications by 2^-e.
+// Dequantize decodes pairs with cvt.rn.f16x2.e4m3x2 (exact), multiplies by the
+// scale in float32 and packs bf16 pairs with cvt.rn.bf16x2.f32; a group with
+// a NaN code or a non-finite scale takes the scalar path, whose NaN pattern
+// (0x7FC0) is the oracle's.
+
+template <int FMT>
+struct Fp8Fmt {
+  static constexpr int kG = FMT == WKV_FP8_F32_B64 ? 8 : 4;   // threads per scale block
+};
+
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+__device__ __forceinline__ float clamp448(float q) { return fminf(fmaxf(q, -448.0f), 448.0f); }
+
+template <int FMT>
+__global__ void __launch_bounds__(256) k_kv_fp8_quantize(const uint4 *__restrict__ x, int64_t n8,
+                                                         uint2 *__restrict__ payload, void *__restrict__ scales) {
+  constexpr int G = Fp8Fmt<FMT>::kG;
+  const int lane = threadIdx.x & 31;
+  const unsigned gmask = ((1u << G) - 1u) << (lane & ~(G - 1));
+  // n8 is a multiple of G and G divides 32, so the lanes of a block enter and
+  // leave the loop together (the shuffles below only involve them)
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint4 u = __ldcs(x + i);
+    float v[8] = {wm_bf16lo(u.x), wm_bf16hi(u.x), wm_bf16lo(u.y), wm_bf16hi(u.y),
+                  wm_bf16lo(u.z), wm_bf16hi(u.z), wm_bf16lo(u.w), wm_bf16hi(u.w)};
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int m = 1; m < G; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, m));
+    const bool first = (lane & (G - 1)) == 0;
+    float q[8];
+    if (FMT == WKV_FP8_F32_B64) {
+      const float s = __fdiv_rn(amax, 448.0f);
+      if (first) static_cast<float *>(scales)[i / G] = s;
+      if (!(s > 0.0f)) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = 0.0f;
+      } else {
+        const float r = __frcp_rn(s);
+        const bool recip = r < 3.4028234663852886e38f;   // 1/s finite: s >= 2^-128 (else every quotient is exact)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float t = v[j] * r;
+          const uint32_t a = __float_as_uint(t) & 0x7fffffffu;
+          if (!recip || a < 0x3c800000u || ((a & 0xfffffu) - 0x7fff8u) < 16u) t = __fdiv_rn(v[j], s);
+          q[j] = clamp448(t);
+        }
+      }
+    } else if (FMT == WKV_FP8_UE8M0_B32) {
+      const int e = ceil_log2_bits(fmaxf(amax, kFp8Floor) * kFp8MaxInv);
+      if (first) static_cast<uint8_t *>(scales)[i / G] = static_cast<uint8_t>(e + 127);
+      const float f = pow2i(-e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = clamp448(v[j] * f);
+    } else {
+      const bool zero = amax == 0.0f;
+      const int e = zero ? 0 : max(-127, min(127, floor_log2(amax) - 8));
+      if (first) static_cast<uint8_t *>(scales)[i / G] = zero ? 0 : static_cast<uint8_t>(e + 127);
+      const float f = pow2i(-e);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = zero ? 0.0f : clamp448(v[j] * f);
+    }
+    const uint32_t lo = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
+    const uint32_t hi = e4m3x2(q[4], q[5]) | (e4m3x2(q[6], q[7]) << 16);
+    __stcs(payload + i, make_uint2(lo, hi));
+  }
+}
+
+__device__ __forceinline__ float2 e4m3x2_to_f32x2(uint32_t pair) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(pair)));
+  return __half22float2(*reinterpret_cast<__half2 *>(&h2));
+}
+
+template <int FMT, bool GATHER>
+__global__ void __launch_bounds__(256) k_kv_fp8_dequantize(const uint2 *__restrict__ payload,
+                                                           const void *__restrict__ scales, int64_t rows,
+                                                           const int32_t *__restrict__ row_idx, int64_t n8,
+                                                           int per_row8, uint4 *__restrict__ out) {
+  constexpr int G = Fp8Fmt<FMT>::kG;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t src = i;
+    if (GATHER) {
+      const int64_t r = i / per_row8;
+      const int64_t q = row_idx[r];
+      src = (q < 0 ? 0 : (q >= rows ? rows - 1 : q)) * per_row8 + (i - r * per_row8);
+    }
+    const uint2 p = __ldcs(payload + src);
+    const float s = kv_scale(scales, src / G, FMT);
+    const uint32_t w[2] = {p.x, p.y};
+    const bool nan_code = (__vcmpeq4(w[0] & 0x7f7f7f7fu, 0x7f7f7f7fu) | __vcmpeq4(w[1] & 0x7f7f7f7fu, 0x7f7f7f7fu)) != 0;
+    uint32_t o[4];
+    if (!nan_code && fabsf(s) <= 3.4028234663852886e38f) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = e4m3x2_to_f32x2(w[j >> 1] >> (16 * (j & 1)));
+        o[j] = pack_bf16x2(f.x * s, f.y * s);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t c = w[j >> 1] >> (16 * (j & 1));
+        o[j] = wm_f32_to_bf16(wm_e4m3_to_f32(c & 255u) * s) |
+               (static_cast<uint32_t>(wm_f32_to_bf16(wm_e4m3_to_f32((c >> 8) & 255u) * s)) << 16);
+      }
+    }
+    __stcs(out + i, make_uint4(o[0], o[1], o[2], o[3]));
+  }
+}
+
+bool is_fp8_fmt(int fmt) { return fmt == WKV_FP8_F32_B64 || fmt == WKV_FP8_UE8M0_B32 || fmt == WKV_MXFP8_B32; }
+
 int grid_for(int64_t work, int threads) {
   int64_t blocks = (work + threads - 1) / threads;
   int64_t cap = static_cast<int64_t>(wm::sm_count()) * 16;
   return static_cast<int>(std::max<int64_t>(1, std::min(blocks, cap)));
+}
+
+// rows n of D values from payload rows (row_idx[r] clipped to [0, rows), or r)
+int launch_fp8_dequantize(const uint8_t *payload, const void *scales, int64_t rows, const int32_t *row_idx,
+                          int64_t n, int D, int fmt, wm_bf16 *out, cudaStream_t stream) {
+  const int64_t n8 = n * (D / 8);
+  const auto *pv = reinterpret_cast<const uint2 *>(payload);
+  auto *ov = reinterpret_cast<uint4 *>(out);
+  const int grid = grid_for(n8, 256);
+#define WM_FP8_DQ(F)                                                                                            \
+  do {                                                                                                          \
+    if (row_idx)                                                                                                \
+      k_kv_fp8_dequantize<F, true><<<grid, 256, 0, stream>>>(pv, scales, rows, row_idx, n8, D / 8, ov);        \
+    else                                                                                                        \
+      k_kv_fp8_dequantize<F, false><<<grid, 256, 0, stream>>>(pv, scales, rows, nullptr, n8, D / 8, ov);       \
+  } while (0)
+  if (fmt == WKV_FP8_F32_B64) WM_FP8_DQ(WKV_FP8_F32_B64);
+  else if (fmt == WKV_FP8_UE8M0_B32) WM_FP8_DQ(WKV_FP8_UE8M0_B32);
+  else WM_FP8_DQ(WKV_MXFP8_B32);
+#undef WM_FP8_DQ
+  return wm::check_launch(row_idx ? "wkv_gather_dequantize" : "wkv_dequantize");
 }
 
 int kv_check(int64_t rows, int D, int fmt) {
@@ -671,6 +830,16 @@ int wkv_quantize(const wm_bf16 *x, int64_t rows, int D, int fmt, uint8_t *payloa
   int blk = fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
   int64_t total = rows * (D / blk);
   if (total == 0) return WM_OK;
+  if (is_fp8_fmt(fmt)) {
+    const int64_t n8 = rows * (D / 8);
+    const auto *xv = reinterpret_cast<const uint4 *>(x);
+    auto *pv = reinterpret_cast<uint2 *>(payload);
+    const int grid = grid_for(n8, 256);
+    if (fmt == WKV_FP8_F32_B64) k_kv_fp8_quantize<WKV_FP8_F32_B64><<<grid, 256, 0, stream>>>(xv, n8, pv, scales);
+    else if (fmt == WKV_FP8_UE8M0_B32) k_kv_fp8_quantize<WKV_FP8_UE8M0_B32><<<grid, 256, 0, stream>>>(xv, n8, pv, scales);
+    else k_kv_fp8_quantize<WKV_MXFP8_B32><<<grid, 256, 0, stream>>>(xv, n8, pv, scales);
+    return wm::check_launch("wkv_quantize");
+  }
   k_kv_quantize<<<grid_for(total, 128), 128, 0, stream>>>(x, rows, D, fmt, payload, scales);
   return wm::check_launch("wkv_quantize");
 }
@@ -708,6 +877,7 @@ int wkv_dequantize(const uint8_t *payload, const void *scales, int64_t rows, int
   int blk = fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
   int64_t total = rows * (D / blk);
   if (total == 0) return WM_OK;
+  if (is_fp8_fmt(fmt)) return launch_fp8_dequantize(payload, scales, rows, nullptr, rows, D, fmt, out, stream);
   k_kv_dequantize<<<grid_for(total, 128), 128, 0, stream>>>(payload, scales, rows, nullptr, rows, D, fmt, out);
   return wm::check_launch("wkv_dequantize");
 }
@@ -722,6 +892,7 @@ int wkv_gather_dequantize(const uint8_t *payload, const void *scales, int64_t ro
   int blk = fmt == WKV_FP8_F32_B64 ? 64 : (fmt == WKV_FP4_E4M3_B16 ? 16 : 32);
   int64_t total = n * (D / blk);
   if (total == 0) return WM_OK;
+  if (is_fp8_fmt(fmt)) return launch_fp8_dequantize(payload, scales, rows, row_idx, n, D, fmt, out, stream);
   k_kv_dequantize<<<grid_for(total, 128), 128, 0, stream>>>(payload, scales, rows, row_idx, n, D, fmt, out);
   return wm::check_launch("wkv_gather_dequantize");
 }
