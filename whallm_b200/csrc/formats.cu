@@ -562,58 +562,71 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
 __device__ __forceinline__ float clamp448(float q) { return fminf(fmaxf(q, -448.0f), 448.0f); }
 
 template <int FMT>
+__device__ __forceinline__ void kv_fp8_quant8(const uint4 u, int64_t i, unsigned gmask, int lane,
+                                              uint2 *__restrict__ payload, void *__restrict__ scales) {
+  constexpr int G = Fp8Fmt<FMT>::kG;
+  float v[8] = {wm_bf16lo(u.x), wm_bf16hi(u.x), wm_bf16lo(u.y), wm_bf16hi(u.y),
+                wm_bf16lo(u.z), wm_bf16hi(u.z), wm_bf16lo(u.w), wm_bf16hi(u.w)};
+  float amax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+  for (int m = 1; m < G; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, m));
+  const bool first = (lane & (G - 1)) == 0;
+  float q[8];
+  if (FMT == WKV_FP8_F32_B64) {
+    const float s = __fdiv_rn(amax, 448.0f);
+    if (first) static_cast<float *>(scales)[i / G] = s;
+    if (!(s > 0.0f)) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = 0.0f;
+    } else {
+      const float r = __frcp_rn(s);
+      const bool recip = r < 3.4028234663852886e38f;   // 1/s finite: s >= 2^-128 (else every quotient is exact)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float t = v[j] * r;
+        const uint32_t a = __float_as_uint(t) & 0x7fffffffu;
+        if (!recip || a < 0x3c800000u || ((a & 0xfffffu) - 0x7fff8u) < 16u) t = __fdiv_rn(v[j], s);
+        q[j] = clamp448(t);
+      }
+    }
+  } else if (FMT == WKV_FP8_UE8M0_B32) {
+    const int e = ceil_log2_bits(fmaxf(amax, kFp8Floor) * kFp8MaxInv);
+    if (first) static_cast<uint8_t *>(scales)[i / G] = static_cast<uint8_t>(e + 127);
+    const float f = pow2i(-e);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = clamp448(v[j] * f);
+  } else {
+    const bool zero = amax == 0.0f;
+    const int e = zero ? 0 : max(-127, min(127, floor_log2(amax) - 8));
+    if (first) static_cast<uint8_t *>(scales)[i / G] = zero ? 0 : static_cast<uint8_t>(e + 127);
+    const float f = pow2i(-e);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) q[j] = zero ? 0.0f : clamp448(v[j] * f);
+  }
+  const uint32_t lo = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
+  const uint32_t hi = e4m3x2(q[4], q[5]) | (e4m3x2(q[6], q[7]) << 16);
+  __stcs(payload + i, make_uint2(lo, hi));
+}
+
+// Two 8-value pieces per thread and loop trip, both loads issued first, so
+// each thread keeps 32 bytes of reads in flight.
+template <int FMT>
 __global__ void __launch_bounds__(256) k_kv_fp8_quantize(const uint4 *__restrict__ x, int64_t n8,
                                                          uint2 *__restrict__ payload, void *__restrict__ scales) {
   constexpr int G = Fp8Fmt<FMT>::kG;
   const int lane = threadIdx.x & 31;
   const unsigned gmask = ((1u << G) - 1u) << (lane & ~(G - 1));
-  // n8 is a multiple of G and G divides 32, so the lanes of a block enter and
-  // leave the loop together (the shuffles below only involve them)
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += (int64_t)gridDim.x * blockDim.x) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  // n8 is a multiple of G, G divides 32 and the stride is a multiple of 32, so
+  // the lanes of a block take each branch together (the shuffles only involve them)
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += 2 * stride) {
+    const int64_t i2 = i + stride;
     const uint4 u = __ldcs(x + i);
-    float v[8] = {wm_bf16lo(u.x), wm_bf16hi(u.x), wm_bf16lo(u.y), wm_bf16hi(u.y),
-                  wm_bf16lo(u.z), wm_bf16hi(u.z), wm_bf16lo(u.w), wm_bf16hi(u.w)};
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
-#pragma unroll
-    for (int m = 1; m < G; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, m));
-    const bool first = (lane & (G - 1)) == 0;
-    float q[8];
-    if (FMT == WKV_FP8_F32_B64) {
-      const float s = __fdiv_rn(amax, 448.0f);
-      if (first) static_cast<float *>(scales)[i / G] = s;
-      if (!(s > 0.0f)) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) q[j] = 0.0f;
-      } else {
-        const float r = __frcp_rn(s);
-        const bool recip = r < 3.4028234663852886e38f;   // 1/s finite: s >= 2^-128 (else every quotient is exact)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float t = v[j] * r;
-          const uint32_t a = __float_as_uint(t) & 0x7fffffffu;
-          if (!recip || a < 0x3c800000u || ((a & 0xfffffu) - 0x7fff8u) < 16u) t = __fdiv_rn(v[j], s);
-          q[j] = clamp448(t);
-        }
-      }
-    } else if (FMT == WKV_FP8_UE8M0_B32) {
-      const int e = ceil_log2_bits(fmaxf(amax, kFp8Floor) * kFp8MaxInv);
-      if (first) static_cast<uint8_t *>(scales)[i / G] = static_cast<uint8_t>(e + 127);
-      const float f = pow2i(-e);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = clamp448(v[j] * f);
-    } else {
-      const bool zero = amax == 0.0f;
-      const int e = zero ? 0 : max(-127, min(127, floor_log2(amax) - 8));
-      if (first) static_cast<uint8_t *>(scales)[i / G] = zero ? 0 : static_cast<uint8_t>(e + 127);
-      const float f = pow2i(-e);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = zero ? 0.0f : clamp448(v[j] * f);
-    }
-    const uint32_t lo = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
-    const uint32_t hi = e4m3x2(q[4], q[5]) | (e4m3x2(q[6], q[7]) << 16);
-    __stcs(payload + i, make_uint2(lo, hi));
+    const uint4 u2 = i2 < n8 ? __ldcs(x + i2) : make_uint4(0u, 0u, 0u, 0u);
+    kv_fp8_quant8<FMT>(u, i, gmask, lane, payload, scales);
+    if (i2 < n8) kv_fp8_quant8<FMT>(u2, i2, gmask, lane, payload, scales);
   }
 }
 
