@@ -167,3 +167,29 @@ def test_cuda_core_rows_of_9_to_11_groups(dev, I):
         out = W.experts_forward(x, idx, ex, weights=w, swiglu_limit=10.0)
     ref = M.moe_forward(_f32(x), _np(idx), _np(w), oracle)
     assert M.max_rel_err(_f32(out), ref) < TOL
+
+
+@pytest.mark.parametrize("T", [1, 64, 300])
+def test_affine4_tensor_core_path_vs_cuda_core_and_oracle(dev, T):
+    # the tiny configuration's affine-4 experts (group 64) on the f16 tensor-core kernel (the default for
+    # H, I multiples of 256) against the CUDA-core kernel (WM_EXPERT_PATH=simt) and the oracle; T = 300 takes
+    # the prefill tile shape
+    import os
+    lay = S.make_layer("tiny", dev, seed=T + 1)
+    x = S.make_tokens(T, 1024, T, dev)
+    w, idx, _ = W.qwen_route(x, lay.gate_weight, 4, True)
+    out_tc = W.experts_forward(x, idx, lay.experts, weights=w)
+    old = os.environ.get("WM_EXPERT_PATH")
+    os.environ["WM_EXPERT_PATH"] = "simt"
+    try:
+        out_cc = W.experts_forward(x, idx, lay.experts, weights=w)
+    finally:
+        if old is None:
+            os.environ.pop("WM_EXPERT_PATH", None)
+        else:
+            os.environ["WM_EXPERT_PATH"] = old
+    ref = M.moe_forward(_f32(x), _np(idx), _np(w), _affine_oracle(lay.experts))
+    assert M.max_rel_err(_f32(out_tc), ref) < TOL
+    assert M.max_rel_err(_f32(out_tc), _f32(out_cc)) < TOL
+    un = W.experts_forward(x, idx, lay.experts)                       # un-reduced switch_mlp rows
+    assert M.max_rel_err(_f32(un), M.switch_mlp(_f32(x), _np(idx), _affine_oracle(lay.experts))) < TOL

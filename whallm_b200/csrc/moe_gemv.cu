@@ -369,7 +369,11 @@ int run(const Args &a, int fmt) {
   const int S = a.T * kk;
   const MxPath path = mx_path();
   const bool mx = fmt == kFmtMxfp4 && path == MxPath::kBlockScaled && wm::mx_supported(a.H, a.I);
-  const bool tc = fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I);
+  // affine-4 (group 64) runs on the f16 tensor-core kernel, dequantizing in
+  // software; WM_EXPERT_PATH=simt keeps it on the CUDA-core kernel
+  const bool affine_tc = fmt == kFmtAffine4 && path != MxPath::kSimt && a.w13.group == 64 && a.w2.group == 64 &&
+                         wm::tc_supported(a.H, a.I);
+  const bool tc = (fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I)) || affine_tc;
   const int n_routed = a.rf.count > 0 ? a.rf.n_global : a.E - has_shared;
   const int tile_n = mx ? wm::mx_tile_n(a.T, a.k, n_routed) : wm::tc_tile_n(a.T);
   // decode-configuration block-scaled layers combine the top-k rows in the down
@@ -415,10 +419,12 @@ int run(const Args &a, int fmt) {
   } else if (tc) {
     if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream)) return rc;
     if (int rc = wm::launch_tc_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x16, ws.s_pad, a.order, a.limit, ws.tiles,
-                                  ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream))
+                                  ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream,
+                                  affine_tc ? a.w13.sc : nullptr, affine_tc ? a.w13.bi : nullptr))
       return rc;
     if (int rc = wm::launch_tc_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h, ws.s_pad, ws.tiles, ws.counters + 2, ws.y,
-                                    ws.counters + 3, tile_n, a.stream))
+                                    ws.counters + 3, tile_n, a.stream, affine_tc ? a.w2.sc : nullptr,
+                                    affine_tc ? a.w2.bi : nullptr))
       return rc;
   } else {
     const uint16_t *x = a.x;

@@ -240,7 +240,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   uint64_t *dfull = empty + S;                          // [2]
   uint64_t *dempty = dfull + 2;                         // [2]
   uint64_t *xbar = dempty + 2;                          // [2 warp pairs][2 buffers]: epilogue column-max exchange
-  uint64_t *cbar = xbar + 4;                            // [2 rendezvous][2 buffers]: fused combine
+  uint64_t *cbar = xbar + 4;                            // [2 buffers] (+2 spare): fused combine, y rows written
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(cbar + 4);
 
   const int warp = threadIdx.x >> 5;
@@ -575,54 +575,64 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       mbar_arrive(&dempty[db]);
       if (C::kFuseSplit && p.mode == 1 && p.comb.out != nullptr) {
         // Fused top-k combine (_route_reduce, model.py:502-504).  Every token of
-        // this item has one slot here (a token's experts are distinct); after the
-        // item's y rows are written, the token's arrival counter for this 128-row
-        // block goes up by one, and the epilogue that brings it to kk sums the
-        // token's kk bf16 rows of the block in slot order j = 0..kk-1 (fmaf
-        // chain in float32, rounded once), as k_combine does.  Which CTA arrives
-        // last does not change the arithmetic.  The two rendezvous are bounded
-        // mbarrier waits over the 128 epilogue threads.
+        // this item has one slot here (a token's experts are distinct).  Warps
+        // 1-3 only arrive on cbar after their y stores; warp 0 waits for them,
+        // makes the item's rows visible device-wide (one fence), and raises the
+        // arrival counter of (token, this 128-row block) for each token.  The
+        // item that brings a counter to kk sums the token's kk bf16 rows of the
+        // block in slot order j = 0..kk-1 (fmaf chain in float32, rounded once),
+        // exactly as k_combine does, so which CTA arrives last does not change
+        // the result.  The wait is bounded like every other.
         const int cb = it & 1;
-        const uint32_t cph = (it >> 1) & 1;
-        __shared__ int32_t cdone[2][32];
-        __threadfence();                                  // this thread's y stores, device-wide
         mbar_arrive(&cbar[cb]);
-        if (!(ok = mbar_wait(&cbar[cb], cph, p.err, 11))) break;
-        const int mb = p.H / kM;
-        if (t < tile.z) {
-          const int tok = p.comb.perm[tile.y + t] / p.comb.kk;
-          const int old = atomicAdd(&p.comb.arrive[static_cast<int64_t>(tok) * mb + m], 1);
-          cdone[cb][t] = old == p.comb.kk - 1 ? tok : -1;
-        }
-        mbar_arrive(&cbar[2 + cb]);
-        if (!(ok = mbar_wait(&cbar[2 + cb], cph, p.err, 12))) break;
-        const int row = m * kM + t;
-        for (int q = 0; q < tile.z; ++q) {
-          const int tok = cdone[cb][q];
-          if (tok < 0) continue;
-          __threadfence();                                // after the last arrival: the other CTAs' rows
-          const int32_t *iv = p.comb.inv + static_cast<int64_t>(tok) * p.comb.kk;
-          float acc = 0.0f;
-          for (int j0 = 0; j0 < p.comb.kk; j0 += 8) {
-            int sl[8];
-            float wt[8], yv[8];
-#pragma unroll
-            for (int u = 0; u < 8; ++u) {
-              const int j = j0 + u;
-              sl[u] = j < p.comb.kk ? iv[j] : -1;
-              wt[u] = j < p.comb.k ? p.comb.w[static_cast<int64_t>(tok) * p.comb.k + j]
-                                   : (p.comb.shared_w ? p.comb.shared_w[tok] : 1.0f);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              yv[u] = (sl[u] >= 0 && sl[u] < p.comb.S)
-                          ? wm_bf16_to_f32(__ldcg(p.y_out + static_cast<int64_t>(sl[u]) * p.H + row))
-                          : 0.0f;
-#pragma unroll
-            for (int u = 0; u < 8; ++u)
-              if (sl[u] >= 0 && sl[u] < p.comb.S) acc = fmaf(wt[u], yv[u], acc);
+        if ((warp & 3) == 0) {
+          if (!(ok = mbar_wait(&cbar[cb], (it >> 1) & 1, p.err, 11))) break;
+          __threadfence();
+          const int mb = p.H / kM;
+          int tok = -1;
+          bool last = false;
+          if (lane < tile.z) {
+            tok = p.comb.perm[tile.y + lane] / p.comb.kk;
+            last = atomicAdd(&p.comb.arrive[static_cast<int64_t>(tok) * mb + m], 1) == p.comb.kk - 1;
           }
-          p.comb.out[static_cast<int64_t>(tok) * p.H + row] = wm_f32_to_bf16(acc);
+          uint32_t done = __ballot_sync(0xffffffffu, last);
+          if (done) __threadfence();                      // after the last arrival: the other CTAs' rows
+          while (done) {
+            const int src = __ffs(done) - 1;
+            done &= done - 1;
+            const int tk = __shfl_sync(0xffffffffu, tok, src);
+            const int32_t *iv = p.comb.inv + static_cast<int64_t>(tk) * p.comb.kk;
+            const int row0 = m * kM + 4 * lane;             // this lane's 4 rows of the block
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            for (int j0 = 0; j0 < p.comb.kk; j0 += 8) {
+              int sl[8];
+              float wt[8];
+              uint2 yv[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                const int j = j0 + u;
+                sl[u] = j < p.comb.kk ? iv[j] : -1;
+                wt[u] = j < p.comb.k ? p.comb.w[static_cast<int64_t>(tk) * p.comb.k + j]
+                                     : (p.comb.shared_w ? p.comb.shared_w[tk] : 1.0f);
+              }
+#pragma unroll
+              for (int u = 0; u < 8; ++u)
+                yv[u] = (sl[u] >= 0 && sl[u] < p.comb.S)
+                            ? __ldcg(reinterpret_cast<const uint2 *>(p.y_out + static_cast<int64_t>(sl[u]) * p.H + row0))
+                            : make_uint2(0u, 0u);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) {
+                if (!(sl[u] >= 0 && sl[u] < p.comb.S)) continue;
+                acc[0] = fmaf(wt[u], wm_bf16lo(yv[u].x), acc[0]);
+                acc[1] = fmaf(wt[u], wm_bf16hi(yv[u].x), acc[1]);
+                acc[2] = fmaf(wt[u], wm_bf16lo(yv[u].y), acc[2]);
+                acc[3] = fmaf(wt[u], wm_bf16hi(yv[u].y), acc[3]);
+              }
+            }
+            *reinterpret_cast<uint2 *>(p.comb.out + static_cast<int64_t>(tk) * p.H + row0) =
+                make_uint2(static_cast<uint32_t>(wm_f32_to_bf16(acc[0])) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16),
+                           static_cast<uint32_t>(wm_f32_to_bf16(acc[2])) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16));
+          }
         }
       }
     }

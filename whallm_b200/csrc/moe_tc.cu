@@ -24,6 +24,16 @@
 // 2^-25 kept exactly), B holds x * 2^-4, so D = 2^8 * (x . w); the epilogue
 // multiplies by 2^-8.
 //
+// MLX affine 4-bit weights (the tiny configuration; deepseek_v41/engram.py:
+// 207-221 shapes) use the same packed layout -- eight 4-bit codes per uint32,
+// element 0 in the low bits, i.e. two codes per byte, low nibble first -- so
+// the same TMA tiles carry them.  Their dequant is w = scale * q + bias with
+// one bf16 (scale, bias) per 64 values of a row: each code becomes the exact
+// f16 (1024 + q) - 1024 and one fma.rn.f16x2 applies the group's f16 scale
+// and bias (one rounding to f16, relative error <= 2^-11).  A holds w
+// unscaled, so D = 2^-4 * (x . w) and the epilogue multiplies by 2^4; a scale
+// or bias beyond +-32768 (outside what f16 carries safely) sets the error code.
+//
 // Warp roles (640 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMA producer              warp 1   MMA issuer (one thread)
 //   warp 2      TMEM allocator            warp 3   second MMA issuer (decode)
@@ -95,7 +105,36 @@ struct TcParams {
   __half *h_out;         // up: [S, I] f16, h * 2^-4
   uint16_t *y_out;       // down: [S, H] bf16
   int32_t *err;
+  const uint16_t *af_sc; // affine: bf16 scales [E*rows, K/64]
+  const uint16_t *af_bi; // affine: bf16 biases [E*rows, K/64]
+  float d_scale;         // D -> x . w: 2^-8 (MXFP4, A = w * 2^12) or 2^4 (affine, A = w)
 };
+
+// 16 packed bytes (32 affine codes, element 0 in the low nibble) -> 16 f16x2
+// words scale * q + bias (scale2, bias2: f16x2 with both halves equal)
+__device__ __forceinline__ void dequant16_affine(uint4 v, uint32_t scale2, uint32_t bias2, uint32_t *out) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t x = w[i] >> (8 * j);              // codes 2j (bits 0-3) and 2j+1 (bits 4-7) of this word
+      uint32_t q = (x & 0xFu) | ((x & 0xF0u) << 12) | 0x64006400u;   // f16x2 (1024 + lo, 1024 + hi)
+      asm("sub.rn.f16x2 %0, %0, %1;" : "+r"(q) : "r"(0x64006400u));
+      asm("fma.rn.f16x2 %0, %0, %1, %2;" : "+r"(q) : "r"(scale2), "r"(bias2));
+      out[4 * i + j] = q;
+    }
+  }
+}
+
+// bf16 bits -> f16x2 (both halves); |v| > 32768 or NaN sets `bad`
+__device__ __forceinline__ uint32_t affine_f16x2(uint16_t b, bool &bad) {
+  const float f = wm_bf16_to_f32(b);
+  if (!(fabsf(f) <= 32768.0f)) bad = true;
+  const __half h = __float2half_rn(f);
+  const uint32_t u = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&h));
+  return u | (u << 16);
+}
 
 #define WM_TMEM_ST32(taddr, r)                                                                                        \
   asm volatile(                                                                                                       \
@@ -150,7 +189,7 @@ __device__ __forceinline__ void dequant16(uint4 v, uint32_t sf, uint32_t *out) {
 
 __device__ __forceinline__ float silu_f32(float g) { return g / (1.0f + expf(-g)); }
 
-template <class C>
+template <class C, bool AFFINE>
 __global__ void __launch_bounds__(kThreads, 1)
     k_expert_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, TcParams p) {
   constexpr int S = C::kStages;
@@ -304,11 +343,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       // This row's E8M0 scales as 8-byte words (256 K values each), prefetched
       // four words ahead through a register shift queue so the global-load
       // latency never sits on the per-stage critical path.
-      const uint2 *scw =
+      const uint2 *scw = AFFINE ? nullptr :
           reinterpret_cast<const uint2 *>(p.scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * (p.K / 32));
-      const int nwords = p.K / 256;
+      const int nwords = AFFINE ? 0 : p.K / 256;
       auto ldw = [&](int w) { return w < nwords ? __ldg(scw + w) : make_uint2(0u, 0u); };
       uint2 q0 = ldw(0), q1 = ldw(1), q2 = ldw(2), q3 = ldw(3);
+      // affine: this row's (scale, bias) per 64 values, one pair per A slot
+      const int64_t af_row = (static_cast<int64_t>(tile.x) * p.rows + grow) * (p.K / kSub);
       int wcur = 0;
       const uint32_t a_row = (srow >> 6) * (C::kAStageBytes / 2) + (srow & 63) * (C::kKC / 2);
       for (int kc = 0; kc < kstages && ok; ++kc, ++g, h0 += SUBS) {
@@ -322,7 +363,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int first = static_cast<int>((wg - static_cast<int>(h0 % kDqGroups) + kDqGroups) % kDqGroups);
         if (first >= SUBS) continue;
         uint32_t sbytes[SUBS * 2];
-        {
+        uint16_t af_s[SUBS], af_b[SUBS];
+        if constexpr (AFFINE) {
+#pragma unroll
+          for (int q = 0; q < SUBS; ++q) {
+            af_s[q] = __ldg(p.af_sc + af_row + kc * SUBS + q);
+            af_b[q] = __ldg(p.af_bi + af_row + kc * SUBS + q);
+          }
+        } else {
           const int boff = ((kc * C::kKC) >> 5) & 7;  // first scale byte of this stage within q0
 #pragma unroll
           for (int q = 0; q < SUBS * 2; ++q) {
@@ -347,8 +395,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             v1 = reinterpret_cast<const uint4 *>(arow)[2 * q + 1];
           }
           uint32_t nr[32];
-          dequant16(v0, scale_f16x2(sbytes[2 * q], bad), nr);
-          dequant16(v1, scale_f16x2(sbytes[2 * q + 1], bad), nr + 16);
+          if constexpr (AFFINE) {
+            const uint32_t s2 = affine_f16x2(af_s[q], bad), b2 = affine_f16x2(af_b[q], bad);
+            dequant16_affine(v0, s2, b2, nr);
+            dequant16_affine(v1, s2, b2, nr + 16);
+          } else {
+            dequant16(v0, scale_f16x2(sbytes[2 * q], bad), nr);
+            dequant16(v1, scale_f16x2(sbytes[2 * q + 1], bad), nr + 16);
+          }
           if (pending) {
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
@@ -400,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int j = m * 64 + (t >> 1);
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const float v = __uint_as_float(r[q]) * 0x1p-8f;
+            const float v = __uint_as_float(r[q]) * p.d_scale;
             const float o = __shfl_xor_sync(0xffffffffu, v, 1);
             if (!(t & 1) && c0 + q < n) {
               float up = v, gate = o;
@@ -416,7 +470,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < 16; ++q)
             if (c0 + q < n)
-              p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = wm_f32_to_bf16(__uint_as_float(r[q]) * 0x1p-8f);
+              p.y_out[static_cast<int64_t>(tile.y + c0 + q) * p.H + row] = wm_f32_to_bf16(__uint_as_float(r[q]) * p.d_scale);
         }
       }
       tc_fence_before();
@@ -459,7 +513,8 @@ __global__ void k_gather_f16(const uint16_t *__restrict__ x, const int32_t *__re
 template <class C>
 int launch_tc_cfg(int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K, const __half *bmat,
                   int S_rows, int I, int H, int order, float limit, const int4 *tiles, const int32_t *n_tiles,
-                  __half *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
+                  __half *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream,
+                  const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert tc: K must be a multiple of the stage depth");
   CUtensorMap tmA, tmB;
   if (int rc = make_map(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, w, K / 2, static_cast<uint64_t>(E) * rows, K / 2,
@@ -468,17 +523,19 @@ int launch_tc_cfg(int mode, const uint8_t *w, const uint8_t *scales, int E, int 
   if (int rc = make_map(&tmB, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, bmat, K, S_rows, static_cast<uint64_t>(K) * 2, kSub, 16,
                         CU_TENSOR_MAP_SWIZZLE_128B))
     return rc;
+  const bool affine = af_sc != nullptr;
+  const auto kern = affine ? k_expert_tc<C, true> : k_expert_tc<C, false>;
   static std::mutex mu;
-  static bool attr_set[64] = {false};
+  static bool attr_set[2][64] = {{false}, {false}};
   int dev = 0;
   cudaGetDevice(&dev);
   {
     std::lock_guard<std::mutex> lock(mu);
-    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(k_expert_tc<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (dev >= 0 && dev < 64 && !attr_set[affine][dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(C::kSmem));
       if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("tc smem attribute: ") + cudaGetErrorString(e));
-      attr_set[dev] = true;
+      attr_set[affine][dev] = true;
     }
   }
   TcParams p{};
@@ -496,18 +553,23 @@ int launch_tc_cfg(int mode, const uint8_t *w, const uint8_t *scales, int E, int 
   p.h_out = h_out;
   p.y_out = y_out;
   p.err = err;
-  k_expert_tc<C><<<wm::sm_count(), kThreads, C::kSmem, stream>>>(tmA, tmB, p);
+  p.af_sc = af_sc;
+  p.af_bi = af_bi;
+  p.d_scale = affine ? 0x1p4f : 0x1p-8f;
+  if (cudaError_t e = wm::launch_pdl(kern, dim3(wm::sm_count()), dim3(kThreads), C::kSmem, stream, tmA, tmB, p))
+    return wm::fail(WM_ERR_CUDA, std::string("expert tc: ") + cudaGetErrorString(e));
   return wm::check_launch("expert tc");
 }
 
 int launch_tc(bool decode, int mode, const uint8_t *w, const uint8_t *scales, int E, int rows, int K,
               const __half *bmat, int S_rows, int I, int H, int order, float limit, const int4 *tiles,
-              const int32_t *n_tiles, __half *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
+              const int32_t *n_tiles, __half *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream,
+              const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr) {
   if (decode)
     return launch_tc_cfg<DecodeCfg>(mode, w, scales, E, rows, K, bmat, S_rows, I, H, order, limit, tiles, n_tiles,
-                                    h_out, y_out, err, stream);
+                                    h_out, y_out, err, stream, af_sc, af_bi);
   return launch_tc_cfg<PrefillCfg>(mode, w, scales, E, rows, K, bmat, S_rows, I, H, order, limit, tiles, n_tiles,
-                                   h_out, y_out, err, stream);
+                                   h_out, y_out, err, stream, af_sc, af_bi);
 }
 
 }  // namespace
@@ -522,21 +584,25 @@ int launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *cou
                       cudaStream_t stream) {
   const int64_t work = static_cast<int64_t>(S) * (H / 8);
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
-  if (grid > 0) k_gather_f16<<<grid, 256, 0, stream>>>(x, perm, count, S, kk, H, static_cast<__half *>(x16));
+  if (grid > 0)
+    if (cudaError_t e = launch_pdl(k_gather_f16, dim3(grid), dim3(256), 0, stream, x, perm, count, S, kk, H,
+                                   static_cast<__half *>(x16)))
+      return fail(WM_ERR_CUDA, std::string("gather f16: ") + cudaGetErrorString(e));
   return check_launch("gather f16");
 }
 
 int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
                  float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, int tile_n,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const uint16_t *af_sc, const uint16_t *af_bi) {
   return launch_tc(tile_n == DecodeCfg::kNMax, 0, w13, s13, E, 2 * I, H, static_cast<const __half *>(x16), S_rows, I, H, order, limit, tiles,
-                   n_tiles, static_cast<__half *>(h16), nullptr, err, stream);
+                   n_tiles, static_cast<__half *>(h16), nullptr, err, stream, af_sc, af_bi);
 }
 
 int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
-                   const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream) {
+                   const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream,
+                   const uint16_t *af_sc, const uint16_t *af_bi) {
   return launch_tc(tile_n == DecodeCfg::kNMax, 1, w2, s2, E, H, I, static_cast<const __half *>(h16), S_rows, I, H, WM_UP_GATE, 0.0f, tiles,
-                   n_tiles, nullptr, y, err, stream);
+                   n_tiles, nullptr, y, err, stream, af_sc, af_bi);
 }
 
 }  // namespace wm

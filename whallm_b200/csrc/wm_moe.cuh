@@ -33,11 +33,13 @@ int tc_tile_n(int T);  // tokens per tile: 64 for decode batches (T <= 64), else
 // rows [0, *count) of the expert-ordered token matrix (count = offsets[E] on the device)
 int launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *count, int S, int kk, int H, void *x16,
                       cudaStream_t stream);
+// af_sc / af_bi (bf16 [E * rows, K / 64]): MLX affine 4-bit weights (group 64) instead of MXFP4 (s13 / s2 unused)
 int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
                  float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, int tile_n,
-                 cudaStream_t stream);
+                 cudaStream_t stream, const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr);
 int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const void *h16, int S_rows,
-                   const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream);
+                   const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream,
+                   const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr);
 
 // The top-k combine fused into the decode-configuration down projection:
 // out[t] = bf16(sum_j w[t, j] * y[inv[t * kk + j]]) (j = k: the shared expert,
