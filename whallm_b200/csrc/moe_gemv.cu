@@ -376,21 +376,14 @@ int run(const Args &a, int fmt) {
   const bool tc = (fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I)) || affine_tc;
   const int n_routed = a.rf.count > 0 ? a.rf.n_global : a.E - has_shared;
   const int tile_n = mx ? wm::mx_tile_n(a.T, a.k, n_routed) : wm::tc_tile_n(a.T);
-  // decode-configuration block-scaled layers combine the top-k rows in the down
-  // projection's epilogue (a bf16 layer output; expert-parallel partial sums and
-  // the un-reduced output keep their own kernels)
-  const bool fused_combine = mx && a.reduce && !a.out_f32 && wm::mx_fused_split(tile_n) && a.H % 128 == 0;
-  const int n_arrive = fused_combine ? a.T * (a.H / 128) : 0;
   if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
                                   ws.counters, ws.counters + 1, (tc || mx) ? ws.tiles : nullptr, ws.counters + 2,
-                                  tile_n, a.stream, a.rf, ws.counters + 3, fused_combine ? ws.arrive : nullptr,
-                                  n_arrive))
+                                  tile_n, a.stream, a.rf, ws.counters + 3))
     return rc;
   const int grid = wm::sm_count() * 2;
   if (mx) {
     const int32_t *count = ws.offsets + a.E;
-    if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream, nullptr,
-                                       fused_combine ? a.out : nullptr, static_cast<int64_t>(a.T) * a.H))
+    if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
       return rc;
     if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, ws.s_pad, a.order,
                                   a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.h,
@@ -399,23 +392,9 @@ int run(const Args &a, int fmt) {
     if (!wm::mx_fused_split(tile_n))
       if (int rc = wm::launch_split_e4m3(ws.h, nullptr, count, S, 1, a.I, ws.h_hi, ws.h_lo, ws.h_sc, a.stream))
         return rc;
-    wm::MxCombine comb{};
-    if (fused_combine) {
-      comb.out = a.out;
-      comb.perm = ws.perm;
-      comb.inv = ws.inv;
-      comb.w = a.weights;
-      comb.shared_w = a.shared_w;
-      comb.arrive = ws.arrive;
-      comb.k = a.k;
-      comb.kk = kk;
-      comb.S = S;
-    }
     if (int rc = wm::launch_mx_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h_hi, ws.h_lo, ws.h_sc, ws.s_pad, ws.tiles,
-                                    ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream,
-                                    fused_combine ? &comb : nullptr))
+                                    ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream))
       return rc;
-    if (fused_combine) return WM_OK;
   } else if (tc) {
     if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream)) return rc;
     if (int rc = wm::launch_tc_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x16, ws.s_pad, a.order, a.limit, ws.tiles,

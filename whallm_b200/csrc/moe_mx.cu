@@ -90,7 +90,7 @@ struct MxCfg {
   static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
                                  : kColsUsed <= 256 ? 256 : 512;
   static constexpr size_t kSmem =
-      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 12) * 8 + 16;
+      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 8) * 8 + 16;
   static_assert(KC % kKH == 0, "stage depth must be a multiple of 128");
   static_assert(NMAX % 16 == 0 && 2 * NMAX <= 256, "tile width: MMA N = 2 x tokens <= 256");
   static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
@@ -127,7 +127,6 @@ struct MxParams {
   // min(d_nmax, d_lq - j * d_nmax)} for b = i / d_per, j = i % d_per.
   int d_tiles, d_per, d_lq, d_nmax;
   int32_t *err;
-  wm::MxCombine comb;        // down, decode configuration: the top-k combine fused into the epilogue (comb.out)
 };
 
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
@@ -240,15 +239,13 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   uint64_t *dfull = empty + S;                          // [2]
   uint64_t *dempty = dfull + 2;                         // [2]
   uint64_t *xbar = dempty + 2;                          // [2 warp pairs][2 buffers]: epilogue column-max exchange
-  uint64_t *cbar = xbar + 4;                            // [2 buffers] (+2 spare): fused combine, y rows written
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(cbar + 4);
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
 
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128 * C::kEpi); }
     for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 64);
-    for (int i = 0; i < 4; ++i) mbar_init(&cbar[i], 128);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -573,68 +570,6 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       }
       tc_fence_before();
       mbar_arrive(&dempty[db]);
-      if (C::kFuseSplit && p.mode == 1 && p.comb.out != nullptr) {
-        // Fused top-k combine (_route_reduce, model.py:502-504).  Every token of
-        // this item has one slot here (a token's experts are distinct).  Warps
-        // 1-3 only arrive on cbar after their y stores; warp 0 waits for them,
-        // makes the item's rows visible device-wide (one fence), and raises the
-        // arrival counter of (token, this 128-row block) for each token.  The
-        // item that brings a counter to kk sums the token's kk bf16 rows of the
-        // block in slot order j = 0..kk-1 (fmaf chain in float32, rounded once),
-        // exactly as k_combine does, so which CTA arrives last does not change
-        // the result.  The wait is bounded like every other.
-        const int cb = it & 1;
-        mbar_arrive(&cbar[cb]);
-        if ((warp & 3) == 0) {
-          if (!(ok = mbar_wait(&cbar[cb], (it >> 1) & 1, p.err, 11))) break;
-          __threadfence();
-          const int mb = p.H / kM;
-          int tok = -1;
-          bool last = false;
-          if (lane < tile.z) {
-            tok = p.comb.perm[tile.y + lane] / p.comb.kk;
-            last = atomicAdd(&p.comb.arrive[static_cast<int64_t>(tok) * mb + m], 1) == p.comb.kk - 1;
-          }
-          uint32_t done = __ballot_sync(0xffffffffu, last);
-          if (done) __threadfence();                      // after the last arrival: the other CTAs' rows
-          while (done) {
-            const int src = __ffs(done) - 1;
-            done &= done - 1;
-            const int tk = __shfl_sync(0xffffffffu, tok, src);
-            const int32_t *iv = p.comb.inv + static_cast<int64_t>(tk) * p.comb.kk;
-            const int row0 = m * kM + 4 * lane;             // this lane's 4 rows of the block
-            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            for (int j0 = 0; j0 < p.comb.kk; j0 += 8) {
-              int sl[8];
-              float wt[8];
-              uint2 yv[8];
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                const int j = j0 + u;
-                sl[u] = j < p.comb.kk ? iv[j] : -1;
-                wt[u] = j < p.comb.k ? p.comb.w[static_cast<int64_t>(tk) * p.comb.k + j]
-                                     : (p.comb.shared_w ? p.comb.shared_w[tk] : 1.0f);
-              }
-#pragma unroll
-              for (int u = 0; u < 8; ++u)
-                yv[u] = (sl[u] >= 0 && sl[u] < p.comb.S)
-                            ? __ldcg(reinterpret_cast<const uint2 *>(p.y_out + static_cast<int64_t>(sl[u]) * p.H + row0))
-                            : make_uint2(0u, 0u);
-#pragma unroll
-              for (int u = 0; u < 8; ++u) {
-                if (!(sl[u] >= 0 && sl[u] < p.comb.S)) continue;
-                acc[0] = fmaf(wt[u], wm_bf16lo(yv[u].x), acc[0]);
-                acc[1] = fmaf(wt[u], wm_bf16hi(yv[u].x), acc[1]);
-                acc[2] = fmaf(wt[u], wm_bf16lo(yv[u].y), acc[2]);
-                acc[3] = fmaf(wt[u], wm_bf16hi(yv[u].y), acc[3]);
-              }
-            }
-            *reinterpret_cast<uint2 *>(p.comb.out + static_cast<int64_t>(tk) * p.H + row0) =
-                make_uint2(static_cast<uint32_t>(wm_f32_to_bf16(acc[0])) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16),
-                           static_cast<uint32_t>(wm_f32_to_bf16(acc[2])) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16));
-          }
-        }
-      }
     }
   }
   tc_fence_before();
@@ -654,18 +589,10 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 template <bool GATHER>
 __global__ void k_split_e4m3(const uint16_t *__restrict__ src, const int32_t *__restrict__ perm,
                              const int32_t *__restrict__ count, int S, int kk, int K, uint8_t *__restrict__ hi,
-                             uint8_t *__restrict__ lo, uint8_t *__restrict__ sc, int32_t *__restrict__ zero,
-                             uint16_t *__restrict__ zero_out, int64_t zero_n) {
+                             uint8_t *__restrict__ lo, uint8_t *__restrict__ sc, int32_t *__restrict__ zero) {
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
   if (zero && blockIdx.x == 0 && threadIdx.x == 0) *zero = 0;
-  if (zero_out && count && *count < 0) {
-    // an expert id outside the layer: no expert work follows, the layer output is zeros
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < zero_n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-      zero_out[i] = 0;
-    return;
-  }
   const int rows = count ? min(S, max(0, *count)) : S;
   const int per_row = K / 8;
   const int64_t total = static_cast<int64_t>(rows) * per_row;
@@ -769,8 +696,7 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
                   uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool a_fp8 = false,
-                  int k_splits = 1, float *y_part = nullptr, int64_t part_stride = 0, int4 dense = int4{0, 0, 0, 0},
-                  const wm::MxCombine *comb = nullptr) {
+                  int k_splits = 1, float *y_part = nullptr, int64_t part_stride = 0, int4 dense = int4{0, 0, 0, 0}) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
   if (k_splits < 1 || (K / C::kKC) % k_splits || (k_splits > 1 && (mode != 1 || !y_part)))
     return wm::fail(WM_ERR_INVALID, "expert mx: bad K split");
@@ -856,11 +782,6 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.h_out = h_out;
   p.y_out = y_out;
   p.err = err;
-  if (comb) {
-    if (!C::kFuseSplit || mode != 1 || k_splits != 1 || H % kM || comb->kk > 64 || comb->kk < 1)
-      return wm::fail(WM_ERR_INVALID, "expert mx: fused combine needs the decode down projection");
-    p.comb = *comb;
-  }
   if (cudaError_t e = wm::launch_pdl(k_expert_mx<C>, dim3(wm::sm_count()), dim3(C::kThreads), C::kSmem, stream, tmA,
                                      tmBh, tmBl, p))
     return wm::fail(WM_ERR_CUDA, std::string("expert mx: ") + cudaGetErrorString(e));
@@ -870,12 +791,10 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
 int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
               const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
               float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-              uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, const wm::MxCombine *comb = nullptr) {
+              uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
   if (decode)
     return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
-                                   n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream, false, 1, nullptr, 0,
-                                   int4{0, 0, 0, 0}, comb);
-  if (comb) return wm::fail(WM_ERR_INVALID, "expert mx: the fused combine is a decode-configuration epilogue");
+                                   n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
   return launch_mx_cfg<MxPrefill>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
                                   n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
 }
@@ -893,16 +812,15 @@ int mx_tile_n(int T, int k, int n_routed) {
 }
 
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
-                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero, uint16_t *zero_out,
-                      int64_t zero_n) {
-  const int64_t work = std::max<int64_t>(static_cast<int64_t>(S) * (K / 8), zero_out ? zero_n / 8 : 0);
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero) {
+  const int64_t work = static_cast<int64_t>(S) * (K / 8);
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
   if (grid > 0) {
     const cudaError_t e =
         perm ? launch_pdl(k_split_e4m3<true>, dim3(grid), dim3(256), 0, stream, src, perm, count, S, kk, K, hi, lo, sc,
-                          zero, zero_out, zero_n)
+                          zero)
              : launch_pdl(k_split_e4m3<false>, dim3(grid), dim3(256), 0, stream, src, static_cast<const int32_t *>(nullptr),
-                          count, S, 1, K, hi, lo, sc, zero, zero_out, zero_n);
+                          count, S, 1, K, hi, lo, sc, zero);
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("split e4m3: ") + cudaGetErrorString(e));
   }
   return check_launch("split e4m3");
@@ -920,9 +838,9 @@ int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, co
 
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
-                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream, const MxCombine *comb) {
+                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream) {
   return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, I, H, WM_UP_GATE, 0.0f,
-                   tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream, comb);
+                   tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream);
 }
 
 }  // namespace wm

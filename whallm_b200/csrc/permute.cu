@@ -23,8 +23,7 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
                                                   int32_t *__restrict__ inv, int32_t *__restrict__ active,
                                                   int32_t *__restrict__ n_active, int32_t *__restrict__ error_flag,
                                                   int4 *__restrict__ tiles, int32_t *__restrict__ n_tiles, int tile_n,
-                                                  int32_t *__restrict__ clear, int32_t *__restrict__ zero_words,
-                                                  int n_zero) {
+                                                  int32_t *__restrict__ clear) {
   extern __shared__ int32_t sm[];
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
@@ -41,7 +40,6 @@ __global__ void __launch_bounds__(1024) k_permute(const int32_t *__restrict__ id
     if (clear) *clear = 0;
   }
   for (int i = threadIdx.x; i < nw * E; i += blockDim.x) hist[i] = 0;
-  for (int i = threadIdx.x; i < n_zero; i += blockDim.x) zero_words[i] = 0;
   __syncthreads();
   const int seg = (S + nw - 1) / nw;
   const int s0 = warp * seg, s1 = min(S, s0 + seg);
@@ -194,8 +192,7 @@ int permute_warps(int E) {
 
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
                    int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
-                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf, int32_t *clear,
-                   int32_t *zero_words, int n_zero) {
+                   int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf, int32_t *clear) {
   // warps: one per 32 assignments (at least 4, for the per-expert loops), up
   // to what the per-warp histograms leave room for
   const int64_t S = static_cast<int64_t>(T) * (k + (shared_expert >= 0 ? 1 : 0));
@@ -208,8 +205,7 @@ int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, i
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("permute smem: ") + cudaGetErrorString(e));
   }
   if (cudaError_t e = launch_pdl(k_permute, dim3(1), dim3(nw * 32), smem, stream, idx, T, k, shared_expert, rf, E,
-                                 offsets, perm, inv, active, n_active, error_flag, tiles, n_tiles, tile_n, clear,
-                                 zero_words, zero_words ? n_zero : 0))
+                                 offsets, perm, inv, active, n_active, error_flag, tiles, n_tiles, tile_n, clear))
     return fail(WM_ERR_CUDA, std::string("permute: ") + cudaGetErrorString(e));
   return check_launch("permute");
 }

@@ -24,8 +24,7 @@ struct RouteFilter {
 int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, int32_t *offsets, int32_t *perm,
                    int32_t *inv, int32_t *active, int32_t *n_active, int32_t *error_flag, int4 *tiles,
                    int32_t *n_tiles, int tile_n, cudaStream_t stream, RouteFilter rf = RouteFilter{},
-                   int32_t *clear = nullptr,  // clear: a flag the permute sets to 0 (the expert kernels' error code)
-                   int32_t *zero_words = nullptr, int n_zero = 0);  // words the permute sets to 0 (combine counters)
+                   int32_t *clear = nullptr);  // clear: a flag the permute sets to 0 (the expert kernels' error code)
 
 // moe_tc.cu
 bool tc_supported(int H, int I);
@@ -41,41 +40,23 @@ int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
                    const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream,
                    const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr);
 
-// The top-k combine fused into the decode-configuration down projection:
-// out[t] = bf16(sum_j w[t, j] * y[inv[t * kk + j]]) (j = k: the shared expert,
-// weight shared_w[t] or 1), added in slot order j.  arrive: [T, H / 128]
-// counters, zero on entry (launch_permute's zero_words clears them).
-struct MxCombine {
-  uint16_t *out = nullptr;       // [T, H] bf16
-  const int32_t *perm = nullptr; // [S] sorted slot -> flat assignment t * kk + j
-  const int32_t *inv = nullptr;  // [S] flat assignment -> sorted slot
-  const float *w = nullptr;      // [T, k]
-  const float *shared_w = nullptr;
-  int32_t *arrive = nullptr;
-  int k = 0, kk = 0, S = 0;
-};
-
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
 // tokens per tile: 32 (decode configuration) while T * k / n_routed <= 32, else 112
 int mx_tile_n(int T, int k, int n_routed);
 // rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk];
 // *zero (if given) is set to 0 once the kernel's dependency wait has returned
-// zero_out (if given, zero_n bf16 values): written with zeros when *count < 0 (an invalid expert id), for a
-// caller whose output is otherwise written by the fused combine
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
-                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero = nullptr,
-                      uint16_t *zero_out = nullptr, int64_t zero_n = 0);
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero = nullptr);
 // the up projection writes h's e4m3 terms itself (true) or bf16 h for launch_split_e4m3 (false)
 bool mx_fused_split(int tile_n);
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
                  const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
                  int tile_n, cudaStream_t stream);
-// comb (decode configuration only): the top-k combine in the epilogue
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
-                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream, const MxCombine *comb = nullptr);
+                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream);
 
 // Workspace carved out of the caller's buffer for one expert-forward call.
 // S = T * (k + has_shared) assignments.
@@ -93,7 +74,6 @@ struct MoeWorkspace {
   uint8_t *h_hi, *h_lo;  // [S_pad, I] e4m3 terms of h
   uint8_t *h_sc;       // [S_pad, I/32]
   uint16_t *y;         // [S, H] bf16 expert outputs in sorted-slot order (the reference switch_mlp dtype)
-  int32_t *arrive;     // [T, H/128] arrival counters of the fused combine
   int s_pad;           // S rounded up to at least 16 rows (TMA box height)
   size_t bytes;
 };
@@ -122,7 +102,6 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
   size_t o_h8 = take(S_pad * I * 2);
   size_t o_hsc = take(S_pad * (I / 32));
   size_t o_y = take(S * H * sizeof(uint16_t));
-  size_t o_arr = take(static_cast<size_t>(T) * ((H + 127) / 128) * sizeof(int32_t));
   w.s_pad = static_cast<int>(S_pad);
   w.bytes = off;
   if (base) {
@@ -142,7 +121,6 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
     w.h_lo = w.h_hi + S_pad * I;
     w.h_sc = reinterpret_cast<uint8_t *>(b + o_hsc);
     w.y = reinterpret_cast<uint16_t *>(b + o_y);
-    w.arrive = reinterpret_cast<int32_t *>(b + o_arr);
   }
   return w;
 }
