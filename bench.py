@@ -698,12 +698,14 @@ def run_ours(args, rank, world, dev):
         clk = ClockSampler(dev.index if dev.index is not None else 0)
         clk.start()
         s, e = _events(torch)
+        torch.cuda.nvtx.range_push("timed")
         s.record()
         for _ in range(args.steps):
             for _l in range(args.kv_layers):
                 W.kv_quantize(x, "fp8_f32_b64", p, sc)
                 W.kv_dequantize(p, sc, "fp8_f32_b64", out)
         e.record()
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
         clocks = clk.stop()
         ms = s.elapsed_time(e) / args.steps
