@@ -537,10 +537,9 @@ __global__ void k_kv_dequantize(const uint8_t *__restrict__ payload, const void 
 // kv_quant_block's (the per-block kernel kept for the 4-bit formats):
 //   * the e4m3 encode is cvt.rn.satfinite.e4m3x2.f32 on values already
 //     clamped to +-448, i.e. round to nearest even as wm_f32_to_e4m3;
-//   * for the fp32-scale format the quotient v / s is v * (1/s) except where
-//     that product lies within 8 float32 ulps of an e4m3 rounding midpoint
-//     (or below 2^-6, the e4m3 subnormal range), or where 1/s overflows
-//     (s < 2^-128): there the exact quotient is taken.  The product differs from the quotient by less than 2 ulps, so
+//   * for the fp32-scale format the scale amax / 448 and the quotients v / s
+//     are correctly rounded divisions done as a product and one fma
+//     correction (Markstein), exact division for blocks below 2^-80;  The product differs from the quotient by less than 2 ulps, so
 //     away from a midpoint both round to the same e4m3 value;
 //   * the power-of-two scales divide exactly as multiplications by 2^-e.
 // Dequantize decodes pairs with cvt.rn.f16x2.e4m3x2 (exact), multiplies by the
@@ -575,21 +574,29 @@ __device__ __forceinline__ void kv_fp8_quant8(const uint4 u, int64_t i, unsigned
   const bool first = (lane & (G - 1)) == 0;
   float q[8];
   if (FMT == WKV_FP8_F32_B64) {
-    const float s = __fdiv_rn(amax, 448.0f);
-    if (first) static_cast<float *>(scales)[i / G] = s;
-    if (!(s > 0.0f)) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = 0.0f;
-    } else {
+    // Quotients by Markstein's correction: with y = RN(1/b) and q0 = RN(a * y)
+    // within an ulp of a / b, the remainder a - q0 * b is exact in one fma and
+    // RN(q0 + rem * y) is the correctly rounded a / b, as long as the remainder
+    // does not underflow -- true for blocks whose maximum is at least 2^-80
+    // (quotients below 2^-10, the only ones whose remainders could, encode to
+    // a signed zero either way).  Smaller blocks divide exactly.  The sign is
+    // the value's (for +-0); .satfinite saturates as the clamp to +-448 did.
+    if (amax >= 0x1p-80f) {
+      const float s0 = amax * kFp8MaxInv;
+      const float s = fmaf(fmaf(-s0, 448.0f, amax), kFp8MaxInv, s0);     // RN(amax / 448)
+      if (first) static_cast<float *>(scales)[i / G] = s;
       const float r = __frcp_rn(s);
-      const bool recip = r < 3.4028234663852886e38f;   // 1/s finite: s >= 2^-128 (else every quotient is exact)
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        float t = v[j] * r;
-        const uint32_t a = __float_as_uint(t) & 0x7fffffffu;
-        if (!recip || a < 0x3c800000u || ((a & 0xfffffu) - 0x7fff8u) < 16u) t = __fdiv_rn(v[j], s);
-        q[j] = clamp448(t);
+        const float q0 = v[j] * r;
+        const float qq = fmaf(fmaf(-q0, s, v[j]), r, q0);
+        q[j] = __uint_as_float((__float_as_uint(qq) & 0x7fffffffu) | (__float_as_uint(v[j]) & 0x80000000u));
       }
+    } else {
+      const float s = __fdiv_rn(amax, 448.0f);
+      if (first) static_cast<float *>(scales)[i / G] = s;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = s > 0.0f ? clamp448(__fdiv_rn(v[j], s)) : 0.0f;
     }
   } else if (FMT == WKV_FP8_UE8M0_B32) {
     const int e = ceil_log2_bits(fmaxf(amax, kFp8Floor) * kFp8MaxInv);
