@@ -143,3 +143,28 @@ def test_bf16_gate_exact_ties_choose_lower_index(dev):
     got = _run(dev, xb, wb, 5, R.SCORE_SOFTMAX_BF16, eps=0.0)
     _check(got, ref)
     assert got[1].tolist() == [[0, 1, 2, 3, 4]] * 3
+
+
+@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SOFTMAX_BF16, R.SCORE_SIGMOID, R.SCORE_SQRTSOFTPLUS, R.SCORE_NONE])
+@pytest.mark.parametrize("shape", [(3, 1024, 200, 20), (5, 512, 1000, 32), (2, 256, 129, 1), (64, 2048, 513, 10)])
+def test_wide_router_cta_kernel_vs_oracle(dev, fn, shape):
+    # E > 128 runs one CTA per token: ragged E, k up to 32, every score function, bit-exact
+    T, H, E, k = shape
+    rng = np.random.default_rng(T * 7 + E + fn)
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    sb = rng.normal(0, 0.1, E).astype(np.float32)
+    eps = -1.0 if fn == R.SCORE_NONE else 1e-20
+    ref = R.route(xb, wb, k, fn, select_bias=sb, norm_eps=eps, route_scale=1.5)
+    _check(_run(dev, xb, wb, k, fn, None, sb, eps, 1.5), ref)
+
+
+def test_wide_router_exact_ties_choose_lower_index(dev):
+    # 300 equal logits: every warp's list and the merge must take ids 0..k-1
+    xb = np.zeros((2, 256), np.uint16)
+    wb = np.zeros((300, 256), np.uint16)
+    for fn in (R.SCORE_SOFTMAX, R.SCORE_SOFTMAX_BF16):
+        ref = R.route(xb, wb, 12, fn, norm_eps=0.0)
+        got = _run(dev, xb, wb, 12, fn, eps=0.0)
+        _check(got, ref)
+        assert got[1].tolist() == [list(range(12))] * 2
