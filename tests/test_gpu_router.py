@@ -168,3 +168,18 @@ def test_wide_router_exact_ties_choose_lower_index(dev):
         got = _run(dev, xb, wb, 12, fn, eps=0.0)
         _check(got, ref)
         assert got[1].tolist() == [list(range(12))] * 2
+
+
+@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SOFTMAX_BF16, R.SCORE_SQRTSOFTPLUS])
+@pytest.mark.parametrize("shape", [(65, 2048, 513, 10), (200, 264, 40, 4), (1000, 4096, 256, 8), (77, 1032, 129, 6)])
+def test_many_token_short_row_logits_vs_oracle(dev, fn, shape):
+    # T > 64 with H <= 4096 takes the bit-reversed tree kernel: logits, routes and weights bit-exact,
+    # including rows that end inside a 256-column block and tiles past E and T
+    T, H, E, k = shape
+    rng = np.random.default_rng(T + H + E)
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    sg = F.f32_to_bf16_bits((rng.normal(0, 1, (H,)) / np.sqrt(H)).astype(np.float32))
+    lb = rng.normal(0, 1, E).astype(np.float32)
+    ref = R.route(xb, wb, k, fn, logit_bias=lb, norm_eps=0.0, wg_shared_bits=sg)
+    _check(_run(dev, xb, wb, k, fn, lb, None, 0.0, 1.0, sg), ref)
