@@ -343,6 +343,17 @@ WM_API int wmoe_mxfp4_moe_forward_ep(const wm_bf16 *x, const int32_t *idx, const
                               int shared_lo, int shared_hi, float *out, void *workspace, size_t ws_bytes,
                               wm_stream_t stream);
 
+/* Top-k weighted reduce of expert rows: out [T, H] bf16 =
+ *   sum_j weights[t, j] * y[slots[t, j], :]  (+ add[t, :] if add != NULL)
+ * accumulated in float32 in j order (fmaf), the addend last, rounded once.
+ * y: [rows, H] bf16; slots [T, k] int32 (a slot outside [0, rows) is
+ * skipped); add: float32 [T, H] (e.g. a gated shared expert) or NULL.
+ * Replaces _route_reduce (runtime/deepseek_v4_ssd/model.py:502-504, with
+ * slots t * k + j over the un-reduced switch_mlp rows) and the combine of an
+ * expert-parallel layer whose rows came back through an all-to-all. */
+WM_API int wmoe_route_reduce(const wm_bf16 *y, int64_t rows, const int32_t *slots, const float *weights, int T,
+                             int k, int H, const float *add, wm_bf16 *out, wm_stream_t stream);
+
 /* Affine 4-bit experts (group `group`): w13 uint32 [E, 2I, H/8] with bf16
  * sc13/bi13 [E, 2I, H/group]; w2 uint32 [E, H, I/8] with sc2/bi2 [E, H, I/group]. */
 WM_API int wmoe_affine4_experts(const wm_bf16 *x, const int32_t *idx, int T, int k, int H, int I, int E,

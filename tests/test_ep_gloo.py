@@ -21,6 +21,17 @@ import torch.multiprocessing as mp
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
+def _host_reduce(back, slots, weights, add=None):
+    """The all-to-all layer's combine for host-tensor ranks (the device kernel's
+    arithmetic: float32 sum over j, then the addend)."""
+    T, k = slots.shape
+    rows = back.float()[slots.reshape(-1).long()].view(T, k, -1)
+    out = (rows * weights.view(T, k, 1)).sum(1)
+    if add is not None:
+        out = out + add
+    return out.to(torch.bfloat16)
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
@@ -90,7 +101,7 @@ def _worker(rank, world, port, result_q):
         def shared(xt):
             return torch.from_numpy(ex.ffn(E, xt.float().numpy()))
 
-        moe = ExpertParallelMoE(router, local, E, shared=shared)
+        moe = ExpertParallelMoE(router, local, E, shared=shared, reduce=_host_reduce)
         got = moe(torch.from_numpy(x).to(torch.bfloat16)).float().numpy()
         _, idx, w, _ = R.route(F.f32_to_bf16_bits(x), wg, k, R.SCORE_SQRTSOFTPLUS, norm_eps=1e-20, route_scale=1.5)
         ref = M.moe_forward(x, idx, w, ex, shared_expert=E)
@@ -136,7 +147,7 @@ def _placed_worker(rank, world, port, result_q):
             return torch.from_numpy(F.round_bf16(out)).to(torch.bfloat16)
 
         moe = ExpertParallelMoE(router, local, E, shared=lambda xt: torch.from_numpy(ex.ffn(E, xt.float().numpy())),
-                                positions=pos)
+                                positions=pos, reduce=_host_reduce)
         got = moe(torch.from_numpy(x).to(torch.bfloat16)).float().numpy()
         _, idx, w, _ = R.route(F.f32_to_bf16_bits(x), wg, k, R.SCORE_SQRTSOFTPLUS, norm_eps=1e-20, route_scale=1.5)
         ref = M.moe_forward(x, idx, w, ex, shared_expert=E)

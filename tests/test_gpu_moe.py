@@ -193,3 +193,25 @@ def test_affine4_tensor_core_path_vs_cuda_core_and_oracle(dev, T):
     assert M.max_rel_err(_f32(out_tc), _f32(out_cc)) < TOL
     un = W.experts_forward(x, idx, lay.experts)                       # un-reduced switch_mlp rows
     assert M.max_rel_err(_f32(un), M.switch_mlp(_f32(x), _np(idx), _affine_oracle(lay.experts))) < TOL
+
+
+def test_route_reduce_and_rows_reduce_vs_float64(dev):
+    # _route_reduce (model.py:502-504) on the device, and the slot-indexed form the expert-parallel
+    # all-to-all layer uses: skipped slots, a float32 addend, float32 accumulation in j order
+    rng = np.random.default_rng(31)
+    T, k, H = 37, 9, 1024
+    routed = torch.from_numpy(rng.normal(0, 1, (T, k, H)).astype(np.float32)).to(dev).to(torch.bfloat16)
+    scores = torch.from_numpy(rng.uniform(0, 1, (T, k)).astype(np.float32)).to(dev)
+    got = W.route_reduce(routed, scores)
+    ref = (routed.double() * scores.double()[..., None]).sum(1)
+    assert M.max_rel_err(_f32(got), ref.cpu().numpy()) < 1e-2
+    R = 500
+    y = torch.from_numpy(rng.normal(0, 1, (R, H)).astype(np.float32)).to(dev).to(torch.bfloat16)
+    slots = torch.from_numpy(rng.integers(-2, R, (T, k)).astype(np.int32)).to(dev)
+    add = torch.from_numpy(rng.normal(0, 1, (T, H)).astype(np.float32)).to(dev)
+    from whallm_b200.moe import rows_reduce
+    out = rows_reduce(y, slots, scores, add)
+    s = slots.long().cpu()
+    rows = torch.where((s >= 0)[..., None], y.double().cpu()[s.clamp(min=0)], torch.zeros((), dtype=torch.float64))
+    ref2 = (rows * scores.double().cpu()[..., None]).sum(1) + add.double().cpu()
+    assert M.max_rel_err(_f32(out), ref2.numpy()) < 1e-2

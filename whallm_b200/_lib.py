@@ -65,6 +65,7 @@ SIGNATURES = {
     "wmoe_router_topk_static": [_P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _F, _F, _P, _P, _P, _P],
     "wmoe_permute": [_P, _I, _I, _I, _P, _P, _P, _P],
     "wmoe_workspace_size": [_I, _I, _I, _I, _I, _I],
+    "wmoe_route_reduce": [_P, _I64, _P, _P, _I, _I, _I, _P, _P, _P],
     "wmoe_mxfp4_experts": [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _F, _P, _P, _SZ, _P],
     "wmoe_mxfp4_moe_forward": [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _F, _I, _P, _P, _P, _SZ, _P],
     "wmoe_mxfp4_moe_forward_ep": [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _F, _I, _P, _I,

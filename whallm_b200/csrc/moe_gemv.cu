@@ -296,6 +296,58 @@ __global__ void k_combine(const uint16_t *__restrict__ y, const int32_t *__restr
   }
 }
 
+// out[t, :] = bf16(sum_j w[t, j] * y[slots[t, j], :] (+ add[t, :])): the fmaf
+// chain of k_combine over caller-given row indices (slot < 0 or >= R: skipped),
+// then the optional float32 addend, rounded once.
+__global__ void k_route_reduce(const uint16_t *__restrict__ y, int64_t R, const int32_t *__restrict__ slots,
+                               const float *__restrict__ w, int T, int k, int H, const float *__restrict__ add,
+                               uint16_t *__restrict__ out) {
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
+  const int per_row = H / 8;
+  const int64_t total = static_cast<int64_t>(T) * per_row;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int t = static_cast<int>(i / per_row), c8 = static_cast<int>(i % per_row) * 8;
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j0 = 0; j0 < k; j0 += 8) {
+      int64_t sl[8];
+      float wt[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        sl[u] = j < k ? slots[static_cast<int64_t>(t) * k + j] : -1;
+        wt[u] = j < k ? w[static_cast<int64_t>(t) * k + j] : 0.0f;
+      }
+      uint4 a[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        a[u] = (sl[u] >= 0 && sl[u] < R) ? *reinterpret_cast<const uint4 *>(y + sl[u] * H + c8)
+                                         : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (sl[u] < 0 || sl[u] >= R) continue;
+        const float wv = wt[u];
+        acc[0] = fmaf(wv, wm_bf16lo(a[u].x), acc[0]); acc[1] = fmaf(wv, wm_bf16hi(a[u].x), acc[1]);
+        acc[2] = fmaf(wv, wm_bf16lo(a[u].y), acc[2]); acc[3] = fmaf(wv, wm_bf16hi(a[u].y), acc[3]);
+        acc[4] = fmaf(wv, wm_bf16lo(a[u].z), acc[4]); acc[5] = fmaf(wv, wm_bf16hi(a[u].z), acc[5]);
+        acc[6] = fmaf(wv, wm_bf16lo(a[u].w), acc[6]); acc[7] = fmaf(wv, wm_bf16hi(a[u].w), acc[7]);
+      }
+    }
+    if (add) {
+      const float4 *ap = reinterpret_cast<const float4 *>(add + static_cast<int64_t>(t) * H + c8);
+      const float4 p0 = ap[0], p1 = ap[1];
+      acc[0] = acc[0] + p0.x; acc[1] = acc[1] + p0.y; acc[2] = acc[2] + p0.z; acc[3] = acc[3] + p0.w;
+      acc[4] = acc[4] + p1.x; acc[5] = acc[5] + p1.y; acc[6] = acc[6] + p1.z; acc[7] = acc[7] + p1.w;
+    }
+    uint4 o;
+    o.x = wm_f32_to_bf16(acc[0]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16);
+    o.y = wm_f32_to_bf16(acc[2]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16);
+    o.z = wm_f32_to_bf16(acc[4]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[5])) << 16);
+    o.w = wm_f32_to_bf16(acc[6]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[7])) << 16);
+    *reinterpret_cast<uint4 *>(out + static_cast<int64_t>(t) * H + c8) = o;
+  }
+}
+
 // out[t, j, :] = y[inv[t*k+j], :]  (un-reduced switch_mlp output, bf16)
 __global__ void k_unsort(const uint16_t *__restrict__ y, const int32_t *__restrict__ inv,
                          const int32_t *__restrict__ err, int S, int H, uint16_t *__restrict__ out) {
@@ -455,6 +507,23 @@ Weights af_view(const uint32_t *w, const uint16_t *sc, const uint16_t *bi, int g
 }  // namespace
 
 extern "C" {
+
+int wmoe_route_reduce(const wm_bf16 *y, int64_t rows, const int32_t *slots, const float *weights, int T, int k,
+                      int H, const float *add, wm_bf16 *out, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(T >= 0 && k >= 1 && H > 0 && H % 8 == 0 && rows >= 0, "route_reduce: need T >= 0, k >= 1, H % 8 == 0");
+  if (T == 0) return WM_OK;
+  WM_REQUIRE(y && slots && weights && out, "route_reduce: null buffer");
+  WM_REQUIRE(wm::aligned(y, 16) && wm::aligned(out, 16) && wm::aligned(add, 16),
+             "route_reduce: y, out and add must be 16-byte aligned");
+  const int64_t work = static_cast<int64_t>(T) * (H / 8);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, wm::sm_count() * 8)));
+  if (cudaError_t e = wm::launch_pdl(k_route_reduce, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                                     reinterpret_cast<const uint16_t *>(y), rows, slots, weights, T, k, H, add,
+                                     reinterpret_cast<uint16_t *>(out)))
+    return wm::fail(WM_ERR_CUDA, std::string("route_reduce: ") + cudaGetErrorString(e));
+  return wm::check_launch("route_reduce");
+}
 
 size_t wmoe_workspace_size(int T, int k, int H, int I, int E, int has_shared) {
   if (T < 0 || k < 1 || H <= 0 || I <= 0 || E < 1) return 0;

@@ -120,9 +120,13 @@ class ExpertParallelMoE:
     runs this rank's experts, one assignment per row (see ``gpu_local_experts``);
     ``shared(x) -> f32 [T, H]`` (optional) is the replicated shared expert."""
 
-    def __init__(self, router, local_experts, n_routed: int, shared=None, group=None, positions=None):
+    def __init__(self, router, local_experts, n_routed: int, shared=None, group=None, positions=None,
+                 reduce=None):
         self.router = router
         self.local_experts = local_experts
+        # reduce(back bf16 [T*k, H], slots int32 [T, k], weights f32 [T, k], add f32 [T, H] or None) -> bf16 [T, H]:
+        # the device combine by default; host-tensor ranks (gloo tests) pass their own
+        self.reduce = reduce if reduce is not None else gpu_rows_reduce
         self.n_routed = n_routed
         self.shared = shared
         self.group = group
@@ -146,13 +150,11 @@ class ExpertParallelMoE:
         recv_ids = exchange(ids, plan.send_counts, plan.recv_counts, self.group)
         y = self.local_experts(recv_rows, recv_ids) if recv_rows.shape[0] else recv_rows.new_empty((0, H))
         back = exchange(y, plan.recv_counts, plan.send_counts, self.group)
-        # back[i] is the output of assignment plan.order[i]
-        per_assign = torch.empty((T * k, H), dtype=torch.float32, device=x.device)
-        per_assign.index_copy_(0, plan.order, back.float())
-        out = (per_assign.view(T, k, H) * w.reshape(T, k, 1).float()).sum(1)
-        if self.shared is not None:
-            out = out + self.shared(x).float()
-        return out.to(torch.bfloat16)
+        # back[i] is the output of assignment plan.order[i]: slot of assignment (t, j) in back
+        slots = torch.empty(T * k, dtype=torch.int32, device=x.device)
+        slots[plan.order] = torch.arange(T * k, dtype=torch.int32, device=x.device)
+        add = self.shared(x).float().contiguous() if self.shared is not None else None
+        return self.reduce(back.contiguous(), slots.view(T, k), w.reshape(T, k).float().contiguous(), add)
 
 
 def _all_gather(t: torch.Tensor, world: int, group=None) -> torch.Tensor:
@@ -393,6 +395,12 @@ def gpu_partial_experts(experts, e0: int, per: int, n_routed: int, swiglu_limit:
                                  shared_w=swg, swiglu_limit=swiglu_limit, expert_range=(e0, per, n_routed),
                                  shared_rows=rows, placement=positions)
     return run
+
+
+def gpu_rows_reduce(back, slots, weights, add=None):
+    """The all-to-all layer's combine on the device (``wmoe_route_reduce``)."""
+    from .moe import rows_reduce
+    return rows_reduce(back, slots, weights, add)
 
 
 def gpu_local_experts(experts, swiglu_limit: float = 0.0):

@@ -21,8 +21,36 @@ from .router import Gate, qwen_route
 
 
 def route_reduce(routed: torch.Tensor, scores: torch.Tensor) -> torch.Tensor:
-    """_route_reduce (model.py:502-504): sum_k routed * scores, in float32, bf16 result."""
-    return (routed.float() * scores[..., None].float()).sum(-2).to(routed.dtype)
+    """_route_reduce (model.py:502-504): sum_k routed * scores over the
+    un-reduced expert rows [..., k, H] (bf16), accumulated in float32 in k order
+    on the device (``wmoe_route_reduce``), bf16 result."""
+    if routed.dtype != torch.bfloat16:
+        raise ValueError("route_reduce takes the bf16 switch_mlp rows")
+    k, H = routed.shape[-2], routed.shape[-1]
+    y = routed.reshape(-1, H).contiguous()
+    T = y.shape[0] // k
+    slots = torch.arange(T * k, dtype=torch.int32, device=routed.device).view(T, k)
+    w = scores.reshape(T, k).float().contiguous()
+    return rows_reduce(y, slots, w).reshape(*routed.shape[:-2], H)
+
+
+def rows_reduce(y: torch.Tensor, slots: torch.Tensor, weights: torch.Tensor, add: torch.Tensor | None = None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """out [T, H] bf16 = sum_j weights[t, j] * y[slots[t, j]] (+ add[t]) on the device
+    (``wmoe_route_reduce``): y bf16 [R, H], slots int32 [T, k] (negative: skipped),
+    weights f32 [T, k], add f32 [T, H] or None."""
+    from . import _lib as L
+    if y.dtype != torch.bfloat16 or slots.dtype != torch.int32 or weights.dtype != torch.float32:
+        raise ValueError("rows_reduce: y bf16, slots int32, weights float32")
+    T, k = slots.shape
+    H = y.shape[-1]
+    if add is not None and (add.dtype != torch.float32 or tuple(add.shape) != (T, H)):
+        raise ValueError("rows_reduce: add must be float32 [T, H]")
+    L.require_cuda(y, slots, weights, add)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=y.device) if out is None else out
+    L.call("wmoe_route_reduce", L.ptr(y), y.shape[0], L.ptr(slots), L.ptr(weights), T, k, H, L.ptr(add), L.ptr(out),
+           L.stream_of(y))
+    return out
 
 
 def streaming_moe(moe, x: torch.Tensor, input_ids=None) -> torch.Tensor:
