@@ -90,16 +90,20 @@ struct MxCfg {
   static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
                                  : kColsUsed <= 256 ? 256 : 512;
   static constexpr size_t kSmem =
-      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 8) * 8 + 16;
+      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 4 + 4 * EPI) * 8 + 16;
   static_assert(KC % kKH == 0, "stage depth must be a multiple of 128");
   static_assert(NMAX % 16 == 0 && 2 * NMAX <= 256, "tile width: MMA N = 2 x tokens <= 256");
   static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
   static_assert(kSmem <= 232448, "shared memory");
   static_assert(kColsUsed <= 512, "TMEM columns");
-  static_assert(EPI >= 1 && EPI <= 4 && (EPI == 1 || !FUSE_SPLIT),
-                "1-4 epilogue groups; the fused split's column-max exchange is one warp group's");
+  static_assert(EPI >= 1 && EPI <= 4 && (EPI <= 2 || !FUSE_SPLIT),
+                "1-4 epilogue groups; the fused split's column-max exchange buffers are for two");
 };
 using MxDecode = MxCfg<256, 32, 4, true>;
+// The decode up projection has two epilogue groups: a 32-token tile's two
+// 16-token chunks (ClampedSwiGLU, the e4m3 split of h) run side by side, so a
+// short-K item (Qwen-class: K = 2048, 8 stages) is not held up by its epilogue.
+using MxDecodeUp = MxCfg<256, 32, 4, true, 2>;
 using MxPrefill = MxCfg<128, 112, 4, false, 4>;
 
 struct MxParams {
@@ -238,14 +242,14 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   uint64_t *empty = full + S;                           // [S]: MMA commit
   uint64_t *dfull = empty + S;                          // [2]
   uint64_t *dempty = dfull + 2;                         // [2]
-  uint64_t *xbar = dempty + 2;                          // [2 warp pairs][2 buffers]: epilogue column-max exchange
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4);
+  uint64_t *xbar = dempty + 2;                          // [group][2 warp pairs][2 buffers]: column-max exchange
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4 * C::kEpi);
 
   const int warp = threadIdx.x >> 5;
   if (threadIdx.x == 0) {
     for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
     for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128 * C::kEpi); }
-    for (int i = 0; i < 4; ++i) mbar_init(&xbar[i], 64);
+    for (int i = 0; i < 4 * C::kEpi; ++i) mbar_init(&xbar[i], 64);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -475,7 +479,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     const int up_half = p.order == WM_UP_GATE ? 0 : 1;
     const bool is_up = ((t >> 3) & 1) == up_half;
     const int lane = threadIdx.x & 31;
-    __shared__ uint32_t xchg[2][4][16];                 // per-warp column maxima, double buffered
+    __shared__ uint32_t xchg[2][2][4][16];              // [group][buffer][warp] column maxima
     uint32_t xchg_n = 0;
     uint32_t it = 0;
     bool ok = true;
@@ -533,15 +537,15 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
             const uint32_t am = __reduce_max_sync(0xffffffffu, hb[q] & 0x7fffffffu);
-            if (lane == 0) xchg[buf][wq][q] = am;
+            if (lane == 0) xchg[grp & 1][buf][wq][q] = am;
           }
-          mbar_arrive(&xbar[(wq >> 1) * 2 + buf]);
-          if (!(ok = mbar_wait(&xbar[(wq >> 1) * 2 + buf], (xchg_n >> 1) & 1, p.err, 10))) break;
+          mbar_arrive(&xbar[grp * 4 + (wq >> 1) * 2 + buf]);
+          if (!(ok = mbar_wait(&xbar[grp * 4 + (wq >> 1) * 2 + buf], (xchg_n >> 1) & 1, p.err, 10))) break;
           ++xchg_n;
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
             if (!(is_up && c0 + q < n)) continue;
-            const uint32_t am = max(xchg[buf][wq][q], xchg[buf][wq ^ 1][q]);
+            const uint32_t am = max(xchg[grp & 1][buf][wq][q], xchg[grp & 1][buf][wq ^ 1][q]);
             const int sh = max(static_cast<int>(min(am >> 23, 255u)) - 134, -122);
             const float xs = __uint_as_float(hb[q]) * __uint_as_float(static_cast<uint32_t>(127 - sh) << 23);
             const uint32_t hi = e4m3x2(xs, 0.0f) & 0xffu;
@@ -792,6 +796,9 @@ int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, 
               const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
               float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
               uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
+  if (decode && mode == 0)
+    return launch_mx_cfg<MxDecodeUp>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit,
+                                     tiles, n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
   if (decode)
     return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
                                    n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
