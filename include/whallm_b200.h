@@ -268,14 +268,17 @@ WM_API int wmoe_topk_scores(const float *logits, const float *select_bias, int T
                             float *weights, wm_stream_t stream);
 
 /* wmoe_router_topk without the logits scratch argument, for callers that
- * cannot allocate device memory where they route (inside a stream capture,
- * allocation-free serving loops, hosts whose memory belongs to another
+ * cannot call cudaMalloc where they route (serving loops that must stay free
+ * of device allocations, hosts whose device memory belongs to another
  * allocator).  No counterpart in the reference: MLX allocates its own
  * temporaries.  The [T,E] logits live in a 1 MiB file-scope device array
  * (T*E <= 262144, else WM_ERR_INVALID), reserved on every GPU that loads the
  * library until exit and shared by all calls: calls that overlap on the GPU
- * race.  The array's address is looked up on the first call per device; make
- * that call outside any stream capture.  Results equal wmoe_router_topk's. */
+ * race.  The array's address is looked up on the first call per device and
+ * kept; make that first call before any stream capture.  The kept address
+ * belongs to the device's context at that time: after cudaDeviceReset (a new
+ * context) the address is stale, so do not use this entry point after a
+ * reset.  Results equal wmoe_router_topk's. */
 WM_API int wmoe_router_topk_static(const wm_bf16 *x, const wm_bf16 *wg, const float *logit_bias,
                                    const float *select_bias, const wm_bf16 *wg_shared, int T, int H,
                                    int E, int k, int score_fn, float norm_eps, float route_scale,

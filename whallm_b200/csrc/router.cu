@@ -782,10 +782,9 @@ extern "C" int wmoe_topk_scores(const float *logits, const float *select_bias, i
 // ------------------------------------------------------------------------
 // Allocation-free variant of wmoe_router_topk.
 //
-// Some callers cannot allocate device memory at the point where they route:
-// code running inside a CUDA stream capture (cudaMalloc is not capturable),
-// serving loops that must never take the device-synchronising allocation path,
-// and hosts whose memory is owned by another framework's allocator with no
+// Some callers cannot call cudaMalloc at the point where they route: serving
+// loops that must never take the device-synchronising allocation path, and
+// hosts whose device memory is owned by another framework's allocator with no
 // hook to borrow scratch.  This entry point takes the same inputs and outputs
 // as wmoe_router_topk but keeps the [T, E] logits scratch in a fixed
 // file-scope device array instead of a caller buffer.
@@ -795,8 +794,10 @@ extern "C" int wmoe_topk_scores(const float *logits, const float *select_bias, i
 //     loads this library reserves it until the process exits; T * E beyond it
 //     is rejected with WM_ERR_INVALID;
 //   * the array's device address is looked up once per device, on the first
-//     call made with that device current (cudaGetSymbolAddress); make that
-//     first call outside any stream capture;
+//     call made with that device current (cudaGetSymbolAddress), and kept;
+//     make that first call before any stream capture.  The kept address is
+//     the one of the context current then: it does not survive
+//     cudaDeviceReset;
 //   * all calls share the one array and it keeps the last call's contents:
 //     every element the kernels read is written earlier in the same call, so
 //     nothing has to be cleared, but calls whose kernels overlap on the GPU
