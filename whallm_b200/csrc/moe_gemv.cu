@@ -439,7 +439,7 @@ int run(const Args &a, int fmt) {
       return rc;
     if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, ws.s_pad, a.order,
                                   a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.h,
-                                  ws.counters + 3, tile_n, a.stream))
+                                  ws.counters + 3, tile_n, a.stream, a.T))
       return rc;
     if (!wm::mx_fused_split(tile_n))
       if (int rc = wm::launch_split_e4m3(ws.h, nullptr, count, S, 1, a.I, ws.h_hi, ws.h_lo, ws.h_sc, a.stream))

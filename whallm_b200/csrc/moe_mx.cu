@@ -100,9 +100,13 @@ struct MxCfg {
                 "1-4 epilogue groups; the fused split's column-max exchange buffers are for two");
 };
 using MxDecode = MxCfg<256, 32, 4, true>;
-// The decode up projection has two epilogue groups: a 32-token tile's two
-// 16-token chunks (ClampedSwiGLU, the e4m3 split of h) run side by side, so a
-// short-K item (Qwen-class: K = 2048, 8 stages) is not held up by its epilogue.
+// A decode up projection whose tiles can hold more than 16 tokens (T > 16: the
+// shared expert's tile holds every token) has two epilogue groups, so a
+// 32-token tile's two 16-token chunks (ClampedSwiGLU, the e4m3 split of h) run
+// side by side and a short-K item (Qwen-class: K = 2048, 8 stages) is not held
+// up by its epilogue (Qwen-class B = 32 expert call 59.5 -> 56.5 us).  With at
+// most 16 tokens per tile the second group would idle (DeepSeek-class B = 1:
+// 63.2 -> 64.9 us), so smaller batches keep one.
 using MxDecodeUp = MxCfg<256, 32, 4, true, 2>;
 using MxPrefill = MxCfg<128, 112, 4, false, 4>;
 
@@ -795,8 +799,8 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
 int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
               const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
               float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-              uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream) {
-  if (decode && mode == 0)
+              uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool wide_up = false) {
+  if (decode && mode == 0 && wide_up)
     return launch_mx_cfg<MxDecodeUp>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit,
                                      tiles, n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
   if (decode)
@@ -838,9 +842,9 @@ bool mx_fused_split(int tile_n) { return tile_n == MxDecode::kNMax ? MxDecode::k
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
                  const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
-                 int tile_n, cudaStream_t stream) {
+                 int tile_n, cudaStream_t stream, int T) {
   return launch_mx(tile_n == MxDecode::kNMax, 0, w13, s13, E, 2 * I, H, x_hi, x_lo, x_sc, S_rows, I, H, order, limit,
-                   tiles, n_tiles, h_hi, h_lo, h_sc, h, nullptr, err, stream);
+                   tiles, n_tiles, h_hi, h_lo, h_sc, h, nullptr, err, stream, T > 16);
 }
 
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,

@@ -53,7 +53,7 @@ bool mx_fused_split(int tile_n);
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
                  const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
-                 int tile_n, cudaStream_t stream);
+                 int tile_n, cudaStream_t stream, int T);  // T: tokens of the call (tiles of more than 16 use two epilogue groups)
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
                    uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream);
