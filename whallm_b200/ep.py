@@ -139,6 +139,18 @@ class ExpertParallelMoE:
         T, H = x.shape
         w, idx = self.router(x)
         k = idx.shape[-1]
+        add = None
+        side = None
+        if self.shared is not None and x.is_cuda:
+            # the replicated shared expert needs no exchange: it runs on a side
+            # stream while the rows travel (the router has run on the main stream)
+            main = torch.cuda.current_stream(x.device)
+            side = torch.cuda.Stream(device=x.device)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                add = self.shared(x).float().contiguous()
+        elif self.shared is not None:
+            add = self.shared(x).float().contiguous()
         plan = plan_dispatch(idx, self.n_routed, self.world, self.group, self.positions)
         src_tok = plan.order // k
         rows = x.index_select(0, src_tok)
@@ -153,7 +165,9 @@ class ExpertParallelMoE:
         # back[i] is the output of assignment plan.order[i]: slot of assignment (t, j) in back
         slots = torch.empty(T * k, dtype=torch.int32, device=x.device)
         slots[plan.order] = torch.arange(T * k, dtype=torch.int32, device=x.device)
-        add = self.shared(x).float().contiguous() if self.shared is not None else None
+        if side is not None:
+            torch.cuda.current_stream(x.device).wait_stream(side)
+            add.record_stream(torch.cuda.current_stream(x.device))
         return self.reduce(back.contiguous(), slots.view(T, k), w.reshape(T, k).float().contiguous(), add)
 
 
