@@ -149,13 +149,14 @@ def _constant_mxfp4(rows, cols, value, dev):
     return W.mxfp4_quantize(torch.full((rows, cols), value, dtype=torch.bfloat16, device=dev))
 
 
-@pytest.mark.parametrize("path", [None, "f16", "simt"])
+@pytest.mark.parametrize("path", [None, "mma", "stream", "f16", "simt"])
 @pytest.mark.parametrize("T", [1, 2, 40])
 def test_constant_weights_give_the_dequantize_then_matmul_result(dev, path, T):
     """test_runtime.py:2466-2528 restated: experts with constant weights that
     MXFP4 represents exactly (0.125 ... 0.5) give exactly x @ W13^T -> SwiGLU
     -> @ W2^T, per token and expert, in the selected order.  H = I = 256 so
-    every expert path (block-scaled, f16 tensor-core, CUDA-core) can run it;
+    every expert path (block-scaled, CUDA-core weight stream, f16 tensor-core,
+    general CUDA-core) can run it;
     the gate rows are 256 * 0.125 = 32, where silu(32) = 32 in float32, so the
     whole chain is exact."""
     import os

@@ -8,7 +8,8 @@
   ClampedSwiGLU 10), Qwen (gate_up = [gate; up], sigmoid-gated shared) and the
   affine-4 tiny configuration.
 * grouping invariance: a batch gives bit-identical rows to the same tokens run
-  one at a time (test_qwen_grouped_experts.py:23-45 asks the same of MLX).
+  one at a time on the same expert path (test_qwen_grouped_experts.py:23-45
+  asks the same of MLX).
 """
 import numpy as np
 import pytest
@@ -126,7 +127,10 @@ def test_tiny_affine4_config_vs_oracle(dev):
     assert M.max_rel_err(_f32(out), ref) < TOL
 
 
-def test_batch_equals_tokens_one_at_a_time(dev):
+def test_batch_equals_tokens_one_at_a_time(dev, monkeypatch):
+    # within one expert path: single tokens would otherwise take the CUDA-core weight
+    # stream (its own two-token check is in test_gpu_stream.py)
+    monkeypatch.setenv("WM_EXPERT_PATH", "mma")
     lay, x = _ds_case(dev, 12, 16, 1024, 256, seed=9)
     wts, idx = lay.layer.gate(x)
     full = W.experts_forward(x, idx, lay.experts, weights=wts, shared_expert=16, swiglu_limit=10.0)

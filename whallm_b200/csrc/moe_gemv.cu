@@ -399,15 +399,21 @@ int check_common(const Args &a) {
   return WM_OK;
 }
 
-// WM_EXPERT_PATH selects the MXFP4 expert path for A/B checks: "simt" (CUDA
-// cores), "f16" (tcgen05 kind::f16 with in-kernel dequantization); default:
-// the block-scaled tcgen05 path.
-enum class MxPath { kBlockScaled, kF16, kSimt };
+// WM_EXPERT_PATH selects the MXFP4 expert path for A/B checks: "simt" (the
+// general CUDA-core kernel), "f16" (tcgen05 kind::f16 with in-kernel
+// dequantization), "mma" (block-scaled tcgen05 at every call size), "stream"
+// (the CUDA-core weight stream at every call size whose staged rows fit);
+// default: the weight stream for calls of at most kStreamMaxTokens tokens on
+// Qwen-class experts (H <= kStreamMaxH, I <= kStreamMaxI), the block-scaled
+// tcgen05 path otherwise.
+enum class MxPath { kAuto, kMma, kStream, kF16, kSimt };
 MxPath mx_path() {
   const char *v = getenv("WM_EXPERT_PATH");
-  if (v && v[0] == 's') return MxPath::kSimt;
+  if (v && v[0] == 's' && v[1] == 'i') return MxPath::kSimt;
+  if (v && v[0] == 's' && v[1] == 't') return MxPath::kStream;
   if (v && v[0] == 'f') return MxPath::kF16;
-  return MxPath::kBlockScaled;
+  if (v && v[0] == 'm') return MxPath::kMma;
+  return MxPath::kAuto;
 }
 
 int run(const Args &a, int fmt) {
@@ -420,7 +426,12 @@ int run(const Args &a, int fmt) {
   const int kk = a.k + has_shared;
   const int S = a.T * kk;
   const MxPath path = mx_path();
-  const bool mx = fmt == kFmtMxfp4 && path == MxPath::kBlockScaled && wm::mx_supported(a.H, a.I);
+  const bool small_call = a.T <= wm::kStreamMaxTokens && a.H <= wm::kStreamMaxH && a.I <= wm::kStreamMaxI;
+  const bool stream = fmt == kFmtMxfp4 && (path == MxPath::kStream || (path == MxPath::kAuto && small_call)) &&
+                      wm::stream_supported(a.T, a.k, has_shared, a.H, a.I) && wm::aligned(a.w13.s, 8) &&
+                      wm::aligned(a.w2.s, 8);
+  const bool mx = !stream && fmt == kFmtMxfp4 && (path == MxPath::kAuto || path == MxPath::kMma || path == MxPath::kStream) &&
+                  wm::mx_supported(a.H, a.I);
   // affine-4 (group 64) runs on the f16 tensor-core kernel, dequantizing in
   // software; WM_EXPERT_PATH=simt keeps it on the CUDA-core kernel
   const bool affine_tc = fmt == kFmtAffine4 && path != MxPath::kSimt && a.w13.group == 64 && a.w2.group == 64 &&
@@ -433,7 +444,14 @@ int run(const Args &a, int fmt) {
                                   tile_n, a.stream, a.rf, ws.counters + 3))
     return rc;
   const int grid = wm::sm_count() * 2;
-  if (mx) {
+  if (stream) {
+    if (int rc = wm::launch_stream_up(a.w13.w, a.w13.s, a.T, kk, a.H, a.I, a.order, a.limit, a.x, ws.offsets, ws.perm,
+                                      ws.active, ws.counters, ws.h, a.stream))
+      return rc;
+    if (int rc = wm::launch_stream_down(a.w2.w, a.w2.s, S, a.H, a.I, ws.h, ws.offsets, ws.active, ws.counters, ws.y,
+                                        a.stream))
+      return rc;
+  } else if (mx) {
     const int32_t *count = ws.offsets + a.E;
     if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
       return rc;

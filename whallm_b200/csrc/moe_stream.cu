@@ -1,0 +1,529 @@
+// Decode-size MXFP4 expert FFN on CUDA cores: calls of one or two tokens.
+//
+// Reference: the MLX gather_qmm decode path (model.py:393-481,
+// qwen4_exp.py:613-678): y = x @ dequant(W)^T per routed (token, expert)
+// pair, ClampedSwiGLU (deepseek_v41/moe.py:30-43) between the projections.
+//
+// At one or two tokens a layer is a weight stream and each weight byte meets
+// at most two token values, so for Qwen-class experts (1.6 MB each, 17 MB per
+// token) the tensor-core kernels' fixed cost (TMEM and barrier set-up,
+// pipeline fill, a split launch) is most of the call.  Here the weights go
+// from HBM through shared memory straight to CUDA-core arithmetic:
+//
+//   * A chunk is 8 weight rows of one active expert (up projection: up_j..j+3
+//     and gate_j..j+3, so the SwiGLU runs in the epilogue).  The chunks of
+//     all active experts are cut into one contiguous range per CTA and one
+//     per warp, so every SM streams the same number of bytes.
+//   * Lane l takes piece l + 32 s of each row: 16 bytes (one whole 32-value
+//     scale group), or 8 bytes (half a group) for rows of fewer than 1024
+//     values, so each row's step is one coalesced 512-byte (256-byte) read.
+//     The pieces travel by cp.async through a 3-stage ring per warp in shared
+//     memory, two steps ahead of the arithmetic (12 warps x 2 x 4 KB, about
+//     96 KB in flight per SM, none of it in registers; a register double
+//     buffer stalled on loads at 28 % of the HBM peak).
+//   * cvt.rn.f16x2.e2m1x2 turns each weight byte into two exact f16 values;
+//     fma.rn.f32.f16 multiplies them by the token values exactly and rounds
+//     once into an f32 sum.  The token operand is held as f16 with a power of
+//     two per 32-value group, chosen so the group's largest magnitude lies in
+//     [2^14, 2^15): every bf16 value within 2^-32 of its group maximum is then
+//     exact in f16, and smaller ones are off by less than 2^-39 of it.  The
+//     operand rows (up: the call's tokens; down: the SwiGLU rows of the
+//     CTA's experts, bf16 as the reference rounds them) are converted into
+//     shared memory once per CTA.
+//   * Per (row, token): two f32 chains (even and odd values) per piece, their
+//     sum times the group's token scale, then fmaf with the row's E8M0 scale
+//     into the lane's sum; the 32 lane sums meet in a butterfly whose tree
+//     does not depend on how many (row, token) sums it carries, so a token's
+//     result is the same alone or beside another.
+//
+// Measured (one B200, expert call with permute and combine, eager launches):
+// Qwen-class one token 23.3 us against 28.4 us on the block-scaled tensor
+// cores, two tokens 32.7 against 33.1 us; DeepSeek-class one token 67 us
+// against 59 us -- about 2.3 issued instructions per weight value (the
+// conversion and one FMA per value and token) keep a 23 MB expert below the
+// HBM rate, so the dispatch sends only small experts here.
+//
+// Outputs match the other expert paths' buffers: h (bf16, slot order) and y
+// (bf16, slot order), combined by the same k_combine.
+#include "wm_common.cuh"
+#include "wm_moe.cuh"
+#include "wm_tc.cuh"
+
+namespace {
+
+constexpr int kWarps = 12;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRows = 8;    // weight rows per chunk (up: 4 up/gate pairs)
+constexpr int kNT = 2;      // tokens per pass over a chunk
+
+struct StreamParams {
+  const uint8_t *w;          // packed e2m1 rows [E * rows, K / 2]
+  const uint8_t *sc;         // E8M0 [E * rows, K / 32]
+  const uint16_t *src;       // up: tokens [T, K] bf16; down: h [S, K] bf16 in slot order
+  const int32_t *offsets;    // [E + 1] first slot of each expert
+  const int32_t *perm;       // [S] slot -> flat assignment t * kk + j
+  const int32_t *active;     // active expert ids, ascending
+  const int32_t *counters;   // [0] active experts, [1] error flag (an expert id out of range)
+  int kk;                    // slots per token
+  int K;                     // row length (values)
+  int rows;                  // weight rows per expert (up: 2 I, down: H)
+  int I;
+  int up_base, gate_base;    // up projection: first up row, first gate row
+  float limit;
+  int stage_rows;            // rows the shared-memory operand buffer holds
+  int ring_offset;           // shared-memory offset of the warps' copy rings
+  uint16_t *out;             // up: h [S, I]; down: y [S, H] (bf16, slot order)
+};
+
+__device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
+  asm("{.reg .b8 b0, b1, b2, b3;\n\t"
+      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %3, b3;}"
+      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
+      : "r"(w));
+}
+
+// lo += a.lo * b.lo, hi += a.hi * b.hi: exact f16 products, one f32 rounding each
+__device__ __forceinline__ void fma_f16x2_f32(uint32_t a, uint32_t b, float &lo, float &hi) {
+  asm("{.reg .b16 a0, a1, b0, b1;\n\t"
+      "mov.b32 {a0, a1}, %2;\n\t"
+      "mov.b32 {b0, b1}, %3;\n\t"
+      "fma.rn.f32.f16 %0, a0, b0, %0;\n\t"
+      "fma.rn.f32.f16 %1, a1, b1, %1;}"
+      : "+f"(lo), "+f"(hi)
+      : "r"(a), "r"(b));
+}
+
+__device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+__device__ __forceinline__ float pow2f(int e) {  // 2^e for e in [-126, 127]
+  return __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+}
+
+// Each warp streams its weight pieces through a ring of kDepth stages in
+// shared memory (cp.async: the bytes in flight are not held in registers);
+// a stage holds every lane's piece of the chunk's 4 rows and the rows' E8M0
+// bytes of the step (8-byte copies by the first 16 lanes).
+constexpr int kDepth = 3;
+template <int PB>
+struct Ring {
+  static constexpr int kW = kRows * 32 * PB;      // weight bytes per stage
+  static constexpr int kS = kRows * 32;           // scale bytes per stage (2 PB per row used)
+  static constexpr int kStage = kW + kS;
+  static constexpr int kWarpBytes = kDepth * kStage;
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src, uint64_t pol) {
+  asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 8, %2;" ::"r"(dst), "l"(src), "l"(pol)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Sums of V lane-held values over the warp.  Each xor step halves the values
+// a lane carries (a transposed butterfly); every sum is built from the same
+// pairs as a full butterfly of that value alone.  Afterwards lane l holds
+// value (l >> (5 - log2 V)) & (V - 1), as do all lanes equal to it in the low
+// bits.
+template <int V>
+__device__ __forceinline__ float warp_sums(float (&v)[V], int lane) {
+#pragma unroll
+  for (int m = 16, h = V / 2; h >= 1; m >>= 1, h >>= 1) {
+    const bool hi = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < h; ++i) {
+      const float send = hi ? v[i] : v[i + h];
+      const float keep = hi ? v[i + h] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+    }
+  }
+  constexpr int kLow = 32 / V;               // lanes still holding partial sums of one value
+  float s = v[0];
+#pragma unroll
+  for (int m = kLow / 2; m >= 1; m >>= 1) s += __shfl_xor_sync(0xffffffffu, s, m);
+  return s;
+}
+
+constexpr int kMaxCtaExperts = 32;   // experts one CTA's chunk range can span: at most E / grid + 2
+
+template <int MODE, int PB>
+__global__ void __launch_bounds__(kThreads, 1) k_expert_stream(const __grid_constant__ StreamParams p) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  __shared__ int m_e[kMaxCtaExperts], m_p0[kMaxCtaExperts], m_n[kMaxCtaExperts];
+  constexpr int VPP = 2 * PB;                 // values per piece
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
+  if (p.counters[1] != 0) return;             // bad expert id: the combine writes zeros
+  const int n_active = p.counters[0];
+  const int cpe = p.rows / kRows;
+  const int64_t n_chunks = static_cast<int64_t>(n_active) * cpe;
+  const int64_t c0 = n_chunks * blockIdx.x / gridDim.x, c1 = n_chunks * (blockIdx.x + 1) / gridDim.x;
+  if (c0 >= c1) return;
+  const int K = p.K, G = K / 32;
+  const int a_first = static_cast<int>(c0 / cpe), a_last = static_cast<int>((c1 - 1) / cpe);
+
+  // ------------------------------ the CTA's experts, operand rows -> f16
+  for (int i = threadIdx.x; i <= a_last - a_first && i < kMaxCtaExperts; i += kThreads) {
+    const int e = p.active[a_first + i];
+    const int o = p.offsets[e];
+    m_e[i] = e; m_p0[i] = o; m_n[i] = p.offsets[e + 1] - o;
+  }
+  const int p_lo = p.offsets[p.active[a_first]];
+  const int p_hi = p.offsets[p.active[a_last] + 1];
+  int base_row = 0, n_rows;
+  if (MODE == 0) {
+    n_rows = p.stage_rows;                    // every token of the call
+  } else {
+    base_row = p_lo;                          // the slots of the CTA's experts
+    n_rows = p_hi - p_lo;
+  }
+  uint16_t *xs = reinterpret_cast<uint16_t *>(smem);                                        // [n_rows][K]
+  float *xk = reinterpret_cast<float *>(smem + static_cast<size_t>(p.stage_rows) * K * 2);  // [n_rows][G]
+  int *tok = reinterpret_cast<int *>(xk + static_cast<size_t>(p.stage_rows) * G);           // up: slot -> token
+  if (MODE == 0)
+    for (int i = threadIdx.x; i < p_hi - p_lo; i += kThreads) tok[i] = p.perm[p_lo + i] / p.kk;
+  for (int g = threadIdx.x; g < n_rows * G; g += kThreads) {
+    const int r = g / G, q = g - r * G;
+    const uint4 *s = reinterpret_cast<const uint4 *>(p.src + static_cast<int64_t>(base_row + r) * K + q * 32);
+    uint4 v[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __ldcg(s + i);
+    uint32_t mx = 0u;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      mx = __vmaxu2(mx, v[i].x & 0x7fff7fffu);
+      mx = __vmaxu2(mx, v[i].y & 0x7fff7fffu);
+      mx = __vmaxu2(mx, v[i].z & 0x7fff7fffu);
+      mx = __vmaxu2(mx, v[i].w & 0x7fff7fffu);
+    }
+    mx = max(mx & 0xffffu, mx >> 16);
+    // the group maximum's exponent e (bf16 bits >> 7); values scale by 2^-k, k = e - 127 - 14
+    const int k = max(static_cast<int>(mx >> 7) - 141, -100);
+    const float down = pow2f(-k);
+    uint4 *d = reinterpret_cast<uint4 *>(xs + static_cast<int64_t>(r) * K + q * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 o;
+      o.x = f32x2_to_f16x2(wm_bf16lo(v[i].x) * down, wm_bf16hi(v[i].x) * down);
+      o.y = f32x2_to_f16x2(wm_bf16lo(v[i].y) * down, wm_bf16hi(v[i].y) * down);
+      o.z = f32x2_to_f16x2(wm_bf16lo(v[i].z) * down, wm_bf16hi(v[i].z) * down);
+      o.w = f32x2_to_f16x2(wm_bf16lo(v[i].w) * down, wm_bf16hi(v[i].w) * down);
+      d[i] = o;
+    }
+    xk[r * G + q] = mx == 0u ? 0.0f : pow2f(k);
+  }
+  __syncthreads();
+
+  // ------------------------------------------------------------ stream
+  // Each warp walks its chunks as one stream of (chunk, pass, step) with the
+  // loads one step ahead of the arithmetic, across chunk boundaries too.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t nc = c1 - c0;
+  const int64_t w0 = c0 + nc * warp / kWarps, w1 = c0 + nc * (warp + 1) / kWarps;
+  if (w0 >= w1) return;
+  const int pieces = K / VPP;
+  const int steps = (pieces + 31) / 32;
+  const int64_t row_bytes = K / 2;
+  const int rstep = MODE == 0 ? 1 : 2;        // row distance between rows r and r + 2
+  const uint64_t pol = wm_tc::l2_evict_first_policy();
+  auto meta = [&](int a, int &e, int &p0, int &n) {
+    const int i = a - a_first;
+    if (i < kMaxCtaExperts) {
+      e = m_e[i]; p0 = m_p0[i]; n = m_n[i];
+    } else {
+      e = p.active[a]; p0 = p.offsets[e]; n = p.offsets[e + 1] - p0;
+    }
+  };
+  // first weight rows of chunk m (r = 0, 1); row r is row r & 1 plus (r >> 1) * rstep
+  auto first_rows = [&](int m, int &r0, int &r1) {
+    if (MODE == 0) { r0 = p.up_base + (kRows / 2) * m; r1 = p.gate_base + (kRows / 2) * m; }
+    else { r0 = kRows * m; r1 = kRows * m + 1; }
+  };
+  struct Cursor {
+    int64_t c;        // chunk
+    int a, m;         // active expert, chunk within it
+    int t0, s;        // first slot of the pass, step
+    int n;            // slots of the expert
+  };
+  auto start = [&](Cursor &u) {
+    u.c = w0; u.a = static_cast<int>(w0 / cpe); u.m = static_cast<int>(w0 - static_cast<int64_t>(u.a) * cpe);
+    u.t0 = 0; u.s = 0;
+    int e, p0;
+    meta(u.a, e, p0, u.n);
+  };
+  auto advance = [&](Cursor &u) {
+    if (++u.s < steps) return;
+    u.s = 0;
+    u.t0 += kNT;
+    if (u.t0 < u.n) return;
+    u.t0 = 0;
+    ++u.c;
+    if (++u.m == cpe) {
+      u.m = 0;
+      ++u.a;
+    }
+    if (u.c < w1) {
+      int e, p0;
+      meta(u.a, e, p0, u.n);
+    }
+  };
+
+  // ---- copies (cursor L, kDepth - 1 steps ahead)
+  using RG = Ring<PB>;
+  constexpr int kGps = 2 * PB;                // scale groups per step
+  uint8_t *ring = smem + p.ring_offset + static_cast<size_t>(warp) * RG::kWarpBytes;
+  const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
+  Cursor L;
+  start(L);
+  const uint8_t *wb0 = nullptr, *wb1 = nullptr, *sb0 = nullptr, *sb1 = nullptr;
+  int64_t l_chunk = -1;
+  auto issue = [&](int slot) {
+    if (L.c < w1) {
+      if (L.c != l_chunk) {
+        l_chunk = L.c;
+        int e, p0, n, r0, r1;
+        meta(L.a, e, p0, n);
+        first_rows(L.m, r0, r1);
+        const int64_t e_row = static_cast<int64_t>(e) * p.rows;
+        wb0 = p.w + (e_row + r0) * row_bytes; wb1 = p.w + (e_row + r1) * row_bytes;
+        sb0 = p.sc + (e_row + r0) * G; sb1 = p.sc + (e_row + r1) * G;
+      }
+      const int q = lane + 32 * L.s;
+      const uint32_t st = ring_s + slot * RG::kStage;
+      if (q < pieces) {
+#pragma unroll
+        for (int r = 0; r < kRows; ++r) {
+          const uint8_t *wr = ((r & 1) ? wb1 : wb0) + static_cast<int64_t>((r >> 1) * rstep) * row_bytes;
+          if (PB == 16) cp_async16(st + r * 32 * PB + lane * PB, wr + q * PB, pol);
+          else cp_async8(st + r * 32 * PB + lane * PB, wr + q * PB, pol);
+        }
+      }
+      if (lane < 4 * kRows) {                 // row r = lane / 4, bytes [8 j, 8 j + 8) of the step's groups
+        const int r = lane >> 2, j = lane & 3;
+        const int g0 = L.s * kGps + 8 * j;
+        if (8 * j < kGps && g0 < G) {
+          const uint8_t *sr = ((r & 1) ? sb1 : sb0) + static_cast<int64_t>((r >> 1) * rstep) * G;
+          cp_async8(st + RG::kW + r * 32 + 8 * j, sr + g0, pol);
+        }
+      }
+      advance(L);
+    }
+    cp_async_commit();
+  };
+
+  // ---- arithmetic (cursor C) and the per-pass epilogue
+  Cursor C;
+  start(C);
+  int c_p0 = 0, nt = 1;
+  int xr[kNT];
+  float acc[kRows][kNT];
+  auto begin_pass = [&]() {
+    int e, n;
+    meta(C.a, e, c_p0, n);
+    nt = min(kNT, n - C.t0);
+#pragma unroll
+    for (int t = 0; t < kNT; ++t) {
+      const int pp = c_p0 + C.t0 + min(t, nt - 1);
+      xr[t] = MODE == 0 ? tok[pp - p_lo] : pp - base_row;
+    }
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int t = 0; t < kNT; ++t) acc[r][t] = 0.0f;
+  };
+  auto compute = [&](int slot, auto ntok_c) {
+    constexpr int NTOK = decltype(ntok_c)::value;
+    const int q = lane + 32 * C.s;
+    if (q >= pieces) return;
+    const int grp = (q * VPP) / 32;
+    const uint8_t *st = ring + slot * RG::kStage;
+    uint32_t xv[NTOK][PB];
+    float xsc[NTOK];
+#pragma unroll
+    for (int t = 0; t < NTOK; ++t) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(xs + static_cast<int64_t>(xr[t]) * K + q * VPP);
+#pragma unroll
+      for (int i = 0; i < PB / 4; ++i) {
+        const uint4 u = src[i];
+        xv[t][4 * i] = u.x; xv[t][4 * i + 1] = u.y; xv[t][4 * i + 2] = u.z; xv[t][4 * i + 3] = u.w;
+      }
+      xsc[t] = xk[xr[t] * G + grp];
+    }
+    // two rows at a time: four independent f32 chains per token (each row's
+    // lo and hi chains keep their own order)
+#pragma unroll
+    for (int r = 0; r < kRows; r += 2) {
+      uint32_t h[2][PB];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        uint32_t wv[PB / 4];
+        if constexpr (PB == 16) {
+          const uint4 v = *reinterpret_cast<const uint4 *>(st + (r + u) * 32 * PB + lane * PB);
+          wv[0] = v.x; wv[1] = v.y; wv[2] = v.z; wv[3] = v.w;
+        } else {
+          const uint2 v = *reinterpret_cast<const uint2 *>(st + (r + u) * 32 * PB + lane * PB);
+          wv[0] = v.x; wv[1] = v.y;
+        }
+#pragma unroll
+        for (int i = 0; i < PB / 4; ++i) {
+          uint32_t hh[4];
+          e2m1x8_to_f16x2(wv[i], hh);
+          h[u][4 * i] = hh[0]; h[u][4 * i + 1] = hh[1]; h[u][4 * i + 2] = hh[2]; h[u][4 * i + 3] = hh[3];
+        }
+      }
+      const float sw0 = wm_e8m0(st[RG::kW + r * 32 + grp - C.s * kGps]);
+      const float sw1 = wm_e8m0(st[RG::kW + (r + 1) * 32 + grp - C.s * kGps]);
+#pragma unroll
+      for (int t = 0; t < NTOK; ++t) {
+        float lo0 = 0.0f, hi0 = 0.0f, lo1 = 0.0f, hi1 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PB; ++i) {
+          fma_f16x2_f32(h[0][i], xv[t][i], lo0, hi0);
+          fma_f16x2_f32(h[1][i], xv[t][i], lo1, hi1);
+        }
+        acc[r][t] = fmaf((lo0 + hi0) * xsc[t], sw0, acc[r][t]);
+        acc[r + 1][t] = fmaf((lo1 + hi1) * xsc[t], sw1, acc[r + 1][t]);
+      }
+    }
+  };
+  // warp sums, then the epilogue: value r * NTOK + t is (row r, token t)
+  auto epilogue = [&](auto ntok_c) {
+    constexpr int NTOK = decltype(ntok_c)::value;
+    constexpr int V = kRows * NTOK;
+    constexpr int kShift = V == 16 ? 1 : V == 8 ? 2 : 3;   // lane bits below the value index
+    float v[V];
+#pragma unroll
+    for (int r = 0; r < kRows; ++r)
+#pragma unroll
+      for (int t = 0; t < NTOK; ++t) v[r * NTOK + t] = acc[r][t];
+    const float sum = warp_sums<V>(v, lane);
+    const int vi = (lane >> kShift) & (V - 1);
+    const int r = vi / NTOK, t = vi - r * NTOK;
+    const bool writer = (lane & ((1 << kShift) - 1)) == 0;
+    const int64_t slot = c_p0 + C.t0 + t;
+    if (MODE == 0) {
+      // rows (up, gate, up, gate, ...): the gate sum of row r is value r + 1, 32 / kRows lanes over
+      const float gate_sum = __shfl_xor_sync(0xffffffffu, sum, 32 / kRows);
+      if (writer && (r & 1) == 0) {
+        float up = sum, gate = gate_sum;
+        if (p.limit > 0.0f) {
+          up = fminf(fmaxf(up, -p.limit), p.limit);
+          gate = fminf(gate, p.limit);
+        }
+        const float silu = gate / (1.0f + expf(-gate));
+        p.out[slot * p.I + (kRows / 2) * C.m + (r >> 1)] = wm_f32_to_bf16(silu * up);
+      }
+    } else if (writer) {
+      p.out[slot * p.rows + kRows * C.m + r] = wm_f32_to_bf16(sum);
+    }
+  };
+  // one step of cursor C on piece b; false once the warp's chunks are done
+  auto step = [&](int slot) -> bool {
+    if (nt == 1) compute(slot, std::integral_constant<int, 1>{});
+    else compute(slot, std::integral_constant<int, 2>{});
+    if (C.s == steps - 1) {
+      if (nt == 1) epilogue(std::integral_constant<int, 1>{});
+      else epilogue(std::integral_constant<int, 2>{});
+    }
+    advance(C);
+    if (C.c >= w1) return false;
+    if (C.s == 0) begin_pass();
+    return true;
+  };
+
+  for (int i = 0; i < kDepth - 1; ++i) issue(i);
+  begin_pass();
+  for (int use = 0, fill = kDepth - 1;;) {
+    issue(fill);                              // the slot the previous step used
+    cp_async_wait<kDepth - 1>();              // this lane's copies of this step have landed
+    __syncwarp();                             // and every lane's (the scale bytes)
+    const bool more = step(use);
+    __syncwarp();                             // the slot is read before a later step refills it
+    if (!more) break;
+    fill = use;
+    use = use + 1 == kDepth ? 0 : use + 1;
+  }
+  cp_async_wait<0>();
+}
+
+// operand rows (f16 + one f32 scale per 32 values) and, for the up projection, a token index per slot
+size_t stage_bytes(int rows, int K, int slots = 0) {
+  return static_cast<size_t>(rows) * K * 2 + static_cast<size_t>(rows) * (K / 32) * 4 + static_cast<size_t>(slots) * 4;
+}
+
+// shared memory of a launch over rows of K values: the staged operand rows, then the copy rings
+size_t launch_smem(size_t stage, int K, size_t *ring_offset) {
+  *ring_offset = (stage + 15) / 16 * 16;
+  const size_t ring = static_cast<size_t>(kWarps) * (K >= 1024 ? Ring<16>::kWarpBytes : Ring<8>::kWarpBytes);
+  return *ring_offset + ring;
+}
+
+template <int MODE, int PB>
+cudaError_t launch_one(const StreamParams &p, size_t smem, cudaStream_t stream) {
+  static bool attr_done = false;       // per template instance; the attribute is per function
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(k_expert_stream<MODE, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(wm::kStreamSmemMax));
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  return wm::launch_pdl(k_expert_stream<MODE, PB>, dim3(wm::sm_count()), dim3(kThreads), smem, stream, p);
+}
+
+}  // namespace
+
+namespace wm {
+
+bool stream_supported(int T, int k, int has_shared, int H, int I) {
+  const int S = T * (k + has_shared);
+  size_t o;
+  return T >= 1 && H % 256 == 0 && I % 256 == 0 && launch_smem(stage_bytes(T, H, S), H, &o) <= kStreamSmemMax &&
+         launch_smem(stage_bytes(S, I), I, &o) <= kStreamSmemMax;
+}
+
+int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int H, int I, int order, float limit,
+                     const uint16_t *x, const int32_t *offsets, const int32_t *perm, const int32_t *active,
+                     const int32_t *counters, uint16_t *h, cudaStream_t stream) {
+  StreamParams p{};
+  p.w = w13; p.sc = s13; p.src = x; p.offsets = offsets; p.perm = perm; p.active = active; p.counters = counters;
+  p.kk = kk; p.K = H; p.rows = 2 * I; p.I = I;
+  p.up_base = order == WM_UP_GATE ? 0 : I;
+  p.gate_base = order == WM_UP_GATE ? I : 0;
+  p.limit = limit; p.stage_rows = T; p.out = h;
+  size_t ring_offset;
+  const size_t smem = launch_smem(stage_bytes(T, H, T * kk), H, &ring_offset);
+  p.ring_offset = static_cast<int>(ring_offset);
+  cudaError_t e = H >= 1024 ? launch_one<0, 16>(p, smem, stream) : launch_one<0, 8>(p, smem, stream);
+  if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("expert stream up: ") + cudaGetErrorString(e));
+  return check_launch("expert stream up");
+}
+
+int launch_stream_down(const uint8_t *w2, const uint8_t *s2, int S, int H, int I, const uint16_t *h,
+                       const int32_t *offsets, const int32_t *active, const int32_t *counters, uint16_t *y,
+                       cudaStream_t stream) {
+  StreamParams p{};
+  p.w = w2; p.sc = s2; p.src = h; p.offsets = offsets; p.active = active; p.counters = counters;
+  p.kk = 1; p.K = I; p.rows = H; p.I = I; p.stage_rows = S; p.out = y;
+  size_t ring_offset;
+  const size_t smem = launch_smem(stage_bytes(S, I), I, &ring_offset);
+  p.ring_offset = static_cast<int>(ring_offset);
+  cudaError_t e = I >= 1024 ? launch_one<1, 16>(p, smem, stream) : launch_one<1, 8>(p, smem, stream);
+  if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("expert stream down: ") + cudaGetErrorString(e));
+  return check_launch("expert stream down");
+}
+
+}  // namespace wm

@@ -40,6 +40,19 @@ int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
                    const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream,
                    const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr);
 
+// moe_stream.cu: CUDA-core MXFP4 weight stream for calls of one or two tokens
+constexpr size_t kStreamSmemMax = 225 * 1024;   // shared memory: staged f16 operand rows + copy rings
+constexpr int kStreamMaxTokens = 2;               // calls of at most this many tokens take the stream path
+constexpr int kStreamMaxH = 4096, kStreamMaxI = 1024;   // ... when the experts are this small (Qwen-class)
+// H and I multiples of 256, and the staged rows (T tokens of H, S slots of I) fit in shared memory
+bool stream_supported(int T, int k, int has_shared, int H, int I);
+int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int H, int I, int order, float limit,
+                     const uint16_t *x, const int32_t *offsets, const int32_t *perm, const int32_t *active,
+                     const int32_t *counters, uint16_t *h, cudaStream_t stream);
+int launch_stream_down(const uint8_t *w2, const uint8_t *s2, int S, int H, int I, const uint16_t *h,
+                       const int32_t *offsets, const int32_t *active, const int32_t *counters, uint16_t *y,
+                       cudaStream_t stream);
+
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
 // tokens per tile: 32 (decode configuration) while T * k / n_routed <= 32, else 112
