@@ -284,6 +284,33 @@ def _e2e_overlapped(torch, dev, caps, hx, houts, steps):
     return s4.elapsed_time(e4) / steps
 
 
+def _layer_launches(name, cfg, T):
+    """Kernel launches of one layer forward, following the library's dispatch
+    (csrc/moe_gemv.cu `run`): 2 router launches, then for the MXFP4 experts a
+    permute unless the call has at most 64 (token, expert) slots (the first
+    expert kernel groups them itself), the CUDA-core weight stream (up, down)
+    for one- and two-token calls on experts with H <= 4096 and I <= 1024, else
+    the token split and the two tcgen05 projections (plus the SwiGLU split in
+    the prefill configuration), and the combine unless the call has at most
+    64 slots and 4096 output values (the down projection's last CTA combines).
+    Affine-4 (tiny): permute, f16 gather, two tcgen05 projections, combine."""
+    if name == "tiny":
+        return 2 + 5
+    H, I, k = cfg["H"], cfg["I"], cfg["k"]
+    kk = k + (1 if cfg["shared"] else 0)
+    S = T * kk
+    n_routed = cfg["E"]
+    stream = T <= 2 and H <= 4096 and I <= 1024
+    small = S <= 64
+    n = 2 + (0 if small else 1) + (0 if small and T * H <= 4096 else 1)
+    if stream:
+        n += 2
+    else:
+        decode = (T * k) // n_routed <= 32         # mx_tile_n: the decode configuration fuses the SwiGLU split
+        n += 3 + (0 if decode else 1)
+    return n
+
+
 class MoeBench:
     """One MoE workload on resident synthetic layers: the routes of every
     (layer, batch), the distinct experts each reads (for the algorithmic byte
@@ -465,7 +492,7 @@ def run_ours(args, rank, world, dev):
         res.update(dict(ms=ms, ms_exp=ms_exp, ms_e2e=ms_e2e, tokens=sum(batches), alg_bytes=sum(mb.alg_bytes),
                         flops=sum(mb.flops), prefill=prefill, breakdown=bd, clocks=clocks, h2d=h2d, d2h=h2d,
                         distinct=mb.distinct,
-                        launches=len(mb.xs) * (2 + 5) if name != "tiny" else len(mb.xs) * (2 + 4),
+                        launches=sum(_layer_launches(name, mb.cfg, B) for B in mb.batches),
                         kernel="expert FFN call (wmoe_mxfp4_moe_forward)" if name != "tiny"
                         else "expert FFN call (wmoe_affine4_moe_forward)"))
         return res

@@ -219,3 +219,93 @@ def test_route_reduce_and_rows_reduce_vs_float64(dev):
     rows = torch.where((s >= 0)[..., None], y.double().cpu()[s.clamp(min=0)], torch.zeros((), dtype=torch.float64))
     ref2 = (rows * scores.double().cpu()[..., None]).sum(1) + add.double().cpu()
     assert M.max_rel_err(_f32(out), ref2.numpy()) < 1e-2
+
+
+def _ws_layout(T, k, E, has_shared):
+    """Offsets (bytes) of the grouping regions in the expert workspace (csrc/wm_moe.cuh carve_workspace)."""
+    S = T * (k + has_shared)
+    off, regions = 0, {}
+    for name, nbytes in (("offsets", (E + 1) * 4), ("perm", S * 4), ("inv", S * 4), ("active", E * 4),
+                         ("counters", 32), ("tiles", (E + S // 16 + 2) * 16)):
+        regions[name] = (off, nbytes)
+        off = (off + nbytes + 255) // 256 * 256
+    return regions
+
+
+@pytest.mark.parametrize("T,E,path", [(1, 16, "mma"), (3, 16, "mma"), (7, 257, "mma"), (2, 33, "stream"),
+                                      (1, 513, "stream")])
+def test_in_kernel_grouping_equals_permute(dev, monkeypatch, T, E, path):
+    # calls of at most 64 slots group their assignments inside the first expert kernel; the grouping it
+    # writes to the workspace must be the permute kernel's (offsets, perm, inv, active list, counters and,
+    # on the tensor path, the work list with the shared expert's tiles first)
+    monkeypatch.setenv("WM_EXPERT_PATH", path)
+    k, H, I = 8, 1024, 512
+    ex = S.make_mxfp4_experts(E + 1, H, I, seed=T + E, device=dev)
+    x = S.make_tokens(T, H, T, dev)
+    rng = np.random.default_rng(T * E)
+    ri = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+    ri[0, 0] = ri[0, 1] if T > 1 else ri[0, 0]
+    idx = torch.from_numpy(ri).to(dev)
+    w = torch.full((T, k), 1.0 / k, device=dev)
+    nbytes = W.experts.workspace_size(T, k, H, I, E + 1, True)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    W.experts_forward(x, idx, ex, weights=w, shared_expert=E, swiglu_limit=10.0, workspace=ws)
+    torch.cuda.synchronize()
+    lay = _ws_layout(T, k, E + 1, 1)
+    get = lambda name, n: ws[lay[name][0]:lay[name][0] + 4 * n].view(torch.int32).cpu().numpy()
+    ext = np.concatenate([ri, np.full((T, 1), E, np.int32)], axis=1)        # the shared slot is expert E
+    r_off, r_perm, r_inv = M.permute(ext, E + 1)
+    np.testing.assert_array_equal(get("offsets", E + 2), r_off)
+    np.testing.assert_array_equal(get("perm", ext.size), r_perm)
+    np.testing.assert_array_equal(get("inv", ext.size), r_inv)
+    act = np.flatnonzero(np.diff(r_off) > 0).astype(np.int32)
+    cnt = get("counters", 4)
+    assert cnt[0] == act.size and cnt[1] == 0 and cnt[3] == 0
+    np.testing.assert_array_equal(get("active", act.size), act)
+    if path == "mma":
+        tn = 32
+        want = [(E, r_off[E] + q, min(tn, r_off[E + 1] - r_off[E] - q)) for q in range(0, r_off[E + 1] - r_off[E], tn)]
+        for e in act:
+            if e != E:
+                n = r_off[e + 1] - r_off[e]
+                want += [(e, r_off[e] + q, min(tn, n - q)) for q in range(0, n, tn)]
+        assert cnt[2] == len(want)
+        tiles = get("tiles", 4 * len(want)).reshape(-1, 4)[:, :3]
+        np.testing.assert_array_equal(tiles, np.array(want, np.int32))
+
+
+@pytest.mark.parametrize("path", ["mma", "stream"])
+def test_small_call_invalid_id_gives_zeros(dev, monkeypatch, path):
+    # a two-token call groups its slots in-kernel and combines in the down projection's last CTA:
+    # an out-of-range id must still give zeros (and nothing outside the layer is read)
+    monkeypatch.setenv("WM_EXPERT_PATH", path)
+    E, H, I = 4, 256, 256
+    ex = S.make_mxfp4_experts(E + 1, H, I, seed=3, device=dev)
+    x = S.make_tokens(2, H, 3, dev)
+    idx = torch.tensor([[0, 1, 2], [3, 0, 99]], dtype=torch.int32, device=dev)
+    w = torch.full((2, 3), 0.25, device=dev)
+    out = W.experts_forward(x, idx, ex, weights=w, shared_expert=E, swiglu_limit=10.0)
+    assert torch.count_nonzero(out) == 0
+    # and the next call on the same workspace is whole again (the grouping and the ticket are rewritten)
+    idx_ok = torch.tensor([[0, 1, 2], [3, 0, 1]], dtype=torch.int32, device=dev)
+    out2 = W.experts_forward(x, idx_ok, ex, weights=w, shared_expert=E, swiglu_limit=10.0)
+    ref = M.moe_forward(_f32(x), _np(idx_ok), _np(w), _mx_oracle(ex, M.UP_GATE, 10.0), shared_expert=E)
+    assert M.max_rel_err(_f32(out2), ref) < TOL
+
+
+@pytest.mark.parametrize("path", ["mma", "stream"])
+@pytest.mark.parametrize("T", [1, 2])
+def test_small_call_repeats_bit_for_bit(dev, monkeypatch, path, T):
+    # the fused combine's ticket is re-armed by every call: back-to-back calls give identical bits
+    monkeypatch.setenv("WM_EXPERT_PATH", path)
+    E, H, I, k = 12, 1024, 512, 6
+    ex = S.make_mxfp4_experts(E + 1, H, I, seed=T, device=dev)
+    x = S.make_tokens(T, H, T, dev)
+    rng = np.random.default_rng(T)
+    idx = torch.from_numpy(np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)).to(dev)
+    w = torch.from_numpy(rng.uniform(0.1, 1.0, (T, k)).astype(np.float32)).to(dev)
+    outs = [W.experts_forward(x, idx, ex, weights=w, shared_expert=E, swiglu_limit=10.0) for _ in range(4)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    ref = M.moe_forward(_f32(x), _np(idx), _np(w), _mx_oracle(ex, M.UP_GATE, 10.0), shared_expert=E)
+    assert M.max_rel_err(_f32(outs[0]), ref) < TOL

@@ -101,3 +101,31 @@ def test_block_scaled_unreduced_switch_mlp(dev):
                                                       lay.experts.w2_scales)), M.UP_GATE, 10.0)
     ref = M.switch_mlp(x.float().cpu().numpy(), idx.cpu().numpy(), o)
     assert M.max_rel_err(un.float().cpu().numpy(), ref) < TOL
+
+
+@pytest.mark.parametrize("T,E,H,I,k", [(512, 8, 1024, 512, 4), (300, 6, 2048, 1024, 3), (1024, 16, 1024, 256, 8)])
+def test_prefill_cta_pair_vs_single_cta_and_oracle(dev, monkeypatch, T, E, H, I, k):
+    # prefill-size calls (more than 32 tokens per expert) on the cta_group::2 configuration
+    # (WM_MX_PAIR=1: two CTAs per 256-row MMA, each staging one token term) against the single-CTA
+    # configuration and the oracle, with the shared expert and un-reduced rows
+    import numpy as np
+    from oracle import moe as M
+    ex = S.make_mxfp4_experts(E + 1, H, I, seed=T + I, device=dev)
+    x = S.make_tokens(T, H, T, dev)
+    rng = np.random.default_rng(T)
+    ri = np.stack([rng.choice(E, k, replace=False) for _ in range(T)]).astype(np.int32)
+    rw = rng.uniform(0.05, 1.0, (T, k)).astype(np.float32)
+    idx, w = torch.from_numpy(ri).to(dev), torch.from_numpy(rw).to(dev)
+    monkeypatch.delenv("WM_MX_PAIR", raising=False)
+    single = W.experts_forward(x, idx, ex, weights=w, shared_expert=E, swiglu_limit=10.0)
+    monkeypatch.setenv("WM_MX_PAIR", "1")
+    pair = W.experts_forward(x, idx, ex, weights=w, shared_expert=E, swiglu_limit=10.0)
+    pair_un = W.experts_forward(x, idx, ex, swiglu_limit=10.0)
+    orc = M.MXFP4Experts(ex.w13.cpu().numpy(), ex.w13_scales.cpu().numpy(), ex.w2.cpu().numpy(),
+                         ex.w2_scales.cpu().numpy(), M.UP_GATE, 10.0)
+    xf = x.float().cpu().numpy()
+    ref = M.moe_forward(xf, ri, rw, orc, shared_expert=E)
+    assert M.max_rel_err(pair.float().cpu().numpy(), ref) < 2e-2
+    assert M.max_rel_err(single.float().cpu().numpy(), ref) < 2e-2
+    assert M.max_rel_err(pair.float().cpu().numpy(), single.float().cpu().numpy()) < 2e-2
+    assert M.max_rel_err(pair_un.float().cpu().numpy(), M.switch_mlp(xf, ri, orc)) < 2e-2

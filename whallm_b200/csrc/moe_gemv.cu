@@ -26,6 +26,7 @@
 
 #include "wm_common.cuh"
 #include "wm_moe.cuh"
+#include "wm_combine.cuh"
 
 namespace {
 
@@ -238,7 +239,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2)
 
 // out[t, :] = sum_j w[t,j] * y[inv[t*kk+j], :] (+ shared_w[t] * y[inv[t*kk+k], :]) over the bf16
 // expert outputs y, accumulated in f32 in a fixed order and rounded once to bf16 (F32_OUT false)
-// or kept in f32 (an expert-parallel partial sum).
+// or kept in f32 (an expert-parallel partial sum); the arithmetic is wm::combine_groups.
 // A set error flag (expert id out of range) yields zeros; slots are bounds-checked and
 // dropped assignments (slot -1) contribute nothing.
 template <bool F32_OUT>
@@ -247,53 +248,9 @@ __global__ void k_combine(const uint16_t *__restrict__ y, const int32_t *__restr
                           int H, void *__restrict__ out_v) {
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
-  const int per_row = H / 8;
-  const int S = T * kk;
-  const bool bad = *err != 0;
-  const int64_t total = static_cast<int64_t>(T) * per_row;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int t = static_cast<int>(i / per_row), c8 = static_cast<int>(i % per_row) * 8;
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    // slots and weights of 8 assignments, then their 8 rows (bf16, as the
-    // reference's switch_mlp returns them) in flight together, then the fmaf
-    // chain in slot order
-    for (int j0 = 0; j0 < kk && !bad; j0 += 8) {
-      int sl[8];
-      float wt[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int j = j0 + u;
-        sl[u] = j < kk ? inv[static_cast<int64_t>(t) * kk + j] : -1;
-        wt[u] = j < k ? w[static_cast<int64_t>(t) * k + j] : (j < kk && shared_w ? shared_w[t] : 1.0f);
-      }
-      uint4 a[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        a[u] = (sl[u] >= 0 && sl[u] < S) ? *reinterpret_cast<const uint4 *>(y + static_cast<int64_t>(sl[u]) * H + c8)
-                                         : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        if (sl[u] < 0 || sl[u] >= S) continue;
-        const float wv = wt[u];
-        acc[0] = fmaf(wv, wm_bf16lo(a[u].x), acc[0]); acc[1] = fmaf(wv, wm_bf16hi(a[u].x), acc[1]);
-        acc[2] = fmaf(wv, wm_bf16lo(a[u].y), acc[2]); acc[3] = fmaf(wv, wm_bf16hi(a[u].y), acc[3]);
-        acc[4] = fmaf(wv, wm_bf16lo(a[u].z), acc[4]); acc[5] = fmaf(wv, wm_bf16hi(a[u].z), acc[5]);
-        acc[6] = fmaf(wv, wm_bf16lo(a[u].w), acc[6]); acc[7] = fmaf(wv, wm_bf16hi(a[u].w), acc[7]);
-      }
-    }
-    if constexpr (F32_OUT) {
-      float4 *op = reinterpret_cast<float4 *>(static_cast<float *>(out_v) + static_cast<int64_t>(t) * H + c8);
-      op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-      op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    } else {
-      uint4 o;
-      o.x = wm_f32_to_bf16(acc[0]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16);
-      o.y = wm_f32_to_bf16(acc[2]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16);
-      o.z = wm_f32_to_bf16(acc[4]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[5])) << 16);
-      o.w = wm_f32_to_bf16(acc[6]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[7])) << 16);
-      *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out_v) + static_cast<int64_t>(t) * H + c8) = o;
-    }
-  }
+  const wm::CombineArgs a{y, inv, w, shared_w, err, T, k, kk, H, out_v, F32_OUT};
+  wm::combine_groups<F32_OUT>(a, blockIdx.x * (int64_t)blockDim.x + threadIdx.x, (int64_t)gridDim.x * blockDim.x,
+                              false);
 }
 
 // out[t, :] = bf16(sum_j w[t, j] * y[slots[t, j], :] (+ add[t, :])): the fmaf
@@ -439,21 +396,41 @@ int run(const Args &a, int fmt) {
   const bool tc = (fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I)) || affine_tc;
   const int n_routed = a.rf.count > 0 ? a.rf.n_global : a.E - has_shared;
   const int tile_n = mx ? wm::mx_tile_n(a.T, a.k, n_routed) : wm::tc_tile_n(a.T);
-  if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv, ws.active,
-                                  ws.counters, ws.counters + 1, (tc || mx) ? ws.tiles : nullptr, ws.counters + 2,
-                                  tile_n, a.stream, a.rf, ws.counters + 3))
+  // small calls: the first expert kernel groups the assignments itself (no permute launch), and when
+  // the output is at most 4096 values the last CTA of the down projection combines the rows (no combine
+  // launch; for a 7168-wide DeepSeek-class row the serial passes of one CTA cost more than the launch)
+  wm::RoutePlan plan{};
+  // (WM_FUSE=0 keeps the separate permute and combine launches, for A/B checks)
+  const char *fuse_env = getenv("WM_FUSE");
+  const bool fuse = !(fuse_env && fuse_env[0] == '0');
+  const bool small = fuse && a.rf.count == 0 && S <= wm::kSmallRouteMax && (stream || mx);
+  // one CTA combines the rows in about one pass over its threads (T * H / 8 output groups)
+  const bool fuse_combine = small && a.reduce && a.T * a.H <= 4096;
+  const wm::CombineArgs comb{ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk, a.H,
+                             a.out_f32 ? static_cast<void *>(a.out_f32) : static_cast<void *>(a.out),
+                             a.out_f32 != nullptr};
+  int32_t *done = fuse_combine ? ws.counters + 4 : nullptr;
+  if (small) {
+    plan.idx = a.idx; plan.T = a.T; plan.k = a.k; plan.shared_expert = a.shared_expert; plan.E = a.E;
+    plan.offsets = ws.offsets; plan.perm = ws.perm; plan.inv = ws.inv; plan.active = ws.active;
+    plan.counters = ws.counters; plan.tiles = mx ? ws.tiles : nullptr; plan.tile_n = tile_n; plan.done = done;
+  } else if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv,
+                                         ws.active, ws.counters, ws.counters + 1, (tc || mx) ? ws.tiles : nullptr,
+                                         ws.counters + 2, tile_n, a.stream, a.rf, ws.counters + 3)) {
     return rc;
+  }
   const int grid = wm::sm_count() * 2;
   if (stream) {
     if (int rc = wm::launch_stream_up(a.w13.w, a.w13.s, a.T, kk, a.H, a.I, a.order, a.limit, a.x, ws.offsets, ws.perm,
-                                      ws.active, ws.counters, ws.h, a.stream))
+                                      ws.active, ws.counters, ws.h, a.stream, plan))
       return rc;
     if (int rc = wm::launch_stream_down(a.w2.w, a.w2.s, S, a.H, a.I, ws.h, ws.offsets, ws.active, ws.counters, ws.y,
-                                        a.stream))
+                                        a.stream, &comb, done))
       return rc;
   } else if (mx) {
     const int32_t *count = ws.offsets + a.E;
-    if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream))
+    if (int rc = wm::launch_split_e4m3(a.x, ws.perm, count, S, kk, a.H, ws.x_hi, ws.x_lo, ws.x_sc, a.stream, nullptr,
+                                       plan))
       return rc;
     if (int rc = wm::launch_mx_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x_hi, ws.x_lo, ws.x_sc, ws.s_pad, a.order,
                                   a.limit, ws.tiles, ws.counters + 2, ws.h_hi, ws.h_lo, ws.h_sc, ws.h,
@@ -463,7 +440,7 @@ int run(const Args &a, int fmt) {
       if (int rc = wm::launch_split_e4m3(ws.h, nullptr, count, S, 1, a.I, ws.h_hi, ws.h_lo, ws.h_sc, a.stream))
         return rc;
     if (int rc = wm::launch_mx_down(a.w2.w, a.w2.s, a.E, a.H, a.I, ws.h_hi, ws.h_lo, ws.h_sc, ws.s_pad, ws.tiles,
-                                    ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream))
+                                    ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream, &comb, done))
       return rc;
   } else if (tc) {
     if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream)) return rc;
@@ -491,6 +468,7 @@ int run(const Args &a, int fmt) {
     if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("expert gemv: ") + cudaGetErrorString(e));
   }
   if (int rc = wm::check_launch("expert gemv")) return rc;
+  if (fuse_combine) return WM_OK;                     // the down projection's last CTA combined the rows
   const int64_t cwork = static_cast<int64_t>(a.reduce ? a.T : S) * (a.H / 8);
   const int cgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((cwork + 255) / 256, wm::sm_count() * 8)));
   cudaError_t e;

@@ -48,7 +48,9 @@
 //               in turn
 // Every mbarrier wait is bounded and records an error code instead of hanging.
 #include "wm_common.cuh"
+#include "wm_combine.cuh"
 #include "wm_moe.cuh"
+#include "wm_route.cuh"
 #include "wm_tc.cuh"
 
 namespace {
@@ -60,8 +62,14 @@ constexpr int kKH = 128;                 // K values per TMA box row and per sca
 constexpr int kLoShift = 5;              // lo term scale = hi scale * 2^-5
 constexpr uint32_t kLoSub = 0x01010101u * kLoShift;   // E8M0 bytes of the lo term, four at a time
 
-template <int KC, int NMAX, int STAGES, bool FUSE_SPLIT, int EPI = 1>
+template <int KC, int NMAX, int STAGES, bool FUSE_SPLIT, int EPI = 1, bool PAIR = false>
 struct MxCfg {
+  // PAIR: a cluster of two CTAs on two SMs runs each work item as one
+  // cta_group::2 MMA of M = 256 weight rows: CTA r holds rows [128 r, 128 r +
+  // 128) of A and one token term of B (r = 0: hi rows, r = 1: lo rows), so a
+  // CTA stages half the token tile and the stage count grows; CTA 0 issues
+  // the MMAs into both CTAs' tensor memory.
+  static constexpr bool kPair = PAIR;
   // EPI: epilogue warp groups (4 warps each, one per TMEM lane quadrant);
   // the groups take 16-token chunks of a work item in turn, for short-K items
   // whose epilogue would otherwise outlast their mainloop (prefill: 4 groups,
@@ -78,7 +86,7 @@ struct MxCfg {
   static constexpr int kHalves = KC / kKH;                   // 128-K groups per stage
   static constexpr int kABox = kM * kKH;                     // 16 KB: 128 rows x 128 padded bytes
   static constexpr int kAStage = kHalves * kABox;
-  static constexpr int kBBox = 2 * NMAX * kKH;               // hi + lo rows x 128 B, one K group
+  static constexpr int kBBox = (PAIR ? 1 : 2) * NMAX * kKH;  // hi + lo rows (a pair CTA: its term) x 128 B, one K group
   static constexpr int kBStage = kHalves * kBBox;
   static constexpr int kBAtoms = (2 * NMAX + 127) / 128;     // 128-row scale atoms of B per K group
   static constexpr int kSFStage = (((1 + kBAtoms) * kHalves * 512 + 1023) / 1024) * 1024;  // A and B atoms
@@ -90,7 +98,7 @@ struct MxCfg {
   static constexpr int kTmemCols = kColsUsed <= 32 ? 32 : kColsUsed <= 64 ? 64 : kColsUsed <= 128 ? 128
                                  : kColsUsed <= 256 ? 256 : 512;
   static constexpr size_t kSmem =
-      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (2 * STAGES + 4 + 4 * EPI) * 8 + 16;
+      1024 + static_cast<size_t>(STAGES) * (kAStage + kBStage + kSFStage) + (3 * STAGES + 6 + 4 * EPI) * 8 + 16;
   static_assert(KC % kKH == 0, "stage depth must be a multiple of 128");
   static_assert(NMAX % 16 == 0 && 2 * NMAX <= 256, "tile width: MMA N = 2 x tokens <= 256");
   static_assert(kBBox % 1024 == 0, "B boxes must stay 1024-aligned");
@@ -98,6 +106,7 @@ struct MxCfg {
   static_assert(kColsUsed <= 512, "TMEM columns");
   static_assert(EPI >= 1 && EPI <= 4 && (EPI <= 2 || !FUSE_SPLIT),
                 "1-4 epilogue groups; the fused split's column-max exchange buffers are for two");
+  static_assert(!PAIR || !FUSE_SPLIT, "the CTA pair runs the prefill configuration (bf16 h, separate split)");
 };
 using MxDecode = MxCfg<256, 32, 4, true>;
 // A decode up projection whose tiles can hold more than 16 tokens (T > 16: the
@@ -109,6 +118,14 @@ using MxDecode = MxCfg<256, 32, 4, true>;
 // 63.2 -> 64.9 us), so smaller batches keep one.
 using MxDecodeUp = MxCfg<256, 32, 4, true, 2>;
 using MxPrefill = MxCfg<128, 112, 4, false, 4>;
+// The prefill configuration on CTA pairs: 32 KB stages (16 KB weights, 14 KB
+// of one token term, scale atoms), six of them.  Opt-in (WM_MX_PAIR=1): it
+// matches the single-CTA results within the tolerance but measured 2.2x
+// slower on the 4096-token DeepSeek-class layer (9.1 vs 4.1 ms): per-stage
+// stamps show the stage period doubling (0.45 -> 0.9 us) with ~4.4 us from a
+// stage's copy issue to its ready barrier, unchanged by the wait mode, the
+// stage count, the epilogue width or removing the MMAs altogether.
+using MxPrefillPair = MxCfg<128, 112, 6, false, 4, true>;
 
 struct MxParams {
   int mode;                  // 0: up projection (+ClampedSwiGLU -> h bf16), 1: down projection (-> y f32)
@@ -135,6 +152,9 @@ struct MxParams {
   // min(d_nmax, d_lq - j * d_nmax)} for b = i / d_per, j = i % d_per.
   int d_tiles, d_per, d_lq, d_nmax;
   int32_t *err;
+  // down projection of a small call: with done set, the last CTA to finish combines the rows
+  wm::CombineArgs comb;
+  int32_t *done;
 };
 
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
@@ -155,11 +175,84 @@ __device__ __forceinline__ void tma_load_4d_hint(void *dst, const CUtensorMap *m
       : "memory");
 }
 
+// ------------------------------------------------ CTA-pair (cta_group::2)
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_idx() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of this CTA's shared variable at `saddr` in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t peer_addr(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// arrive on an mbarrier of any CTA of the cluster, releasing this thread's earlier writes at cluster scope
+__device__ __forceinline__ void mbar_arrive_at(uint32_t cl_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cl_addr) : "memory");
+}
+// bounded wait that acquires at cluster scope (arrivals and copies from the peer CTA)
+__device__ __forceinline__ bool mbar_try_cl(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(100000u)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_cl(uint64_t *bar, uint32_t parity, int32_t *err, int code) {
+  if (mbar_try_cl(bar, parity)) return true;
+  const unsigned long long t0 = gtimer();
+  while (true) {
+    for (int i = 0; i < 8; ++i)
+      if (mbar_try_cl(bar, parity)) return true;
+    if (gtimer() - t0 > kWaitNs) {
+      atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+// completion of this thread's earlier tcgen05 operations (both CTAs' tensor
+// memory) signalled on an mbarrier of either CTA
+__device__ __forceinline__ void tc_commit_pair(uint32_t cl_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cl_bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma_mx_pair(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
+                                               uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+// each CTA's scale atom (same shared-memory offset) into its own tensor memory
+__device__ __forceinline__ void tc_cp_sf_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 // Block-scaled instruction descriptor: A e2m1, B e4m3, E8M0 scales, f32 D,
 // K-major A and B, M = 128, N = n, scale-factor byte ids for A and B = j.
-__device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t j) {
+__device__ __forceinline__ uint32_t idesc_mx(int n, uint32_t j, int m = kM) {
   return (j << 4) | (5u << 7) | (0u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (1u << 23) |
-         (static_cast<uint32_t>(kM >> 4) << 24) | (j << 29);
+         (static_cast<uint32_t>(m >> 4) << 24) | (j << 29);
 }
 
 __device__ __forceinline__ void tc_mma_mx(uint32_t d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t sfa,
@@ -214,19 +307,20 @@ struct TileCursor {
     const int b = t / d_per, j = t - b * d_per;
     return make_int4(b, b * d_lq + j * d_nmax, min(d_nmax, d_lq - j * d_nmax), 0);
   }
-  __device__ __forceinline__ TileCursor(const MxParams &p, int n)
+  int step;                                   // CTAs (CTA pairs) walking the items
+  __device__ __forceinline__ TileCursor(const MxParams &p, int n, int first, int stride)
       : tiles(p.tiles), m_tiles(p.m_tiles), n_items(n), d_per(p.d_tiles > 0 ? p.d_per : 0), d_lq(p.d_lq),
-        d_nmax(p.d_nmax) {
-    item = blockIdx.x;
+        d_nmax(p.d_nmax), step(stride) {
+    item = first;
     cur = load(item);
-    nxt = load(item + gridDim.x);
+    nxt = load(item + step);
   }
   __device__ __forceinline__ bool valid() const { return item < n_items; }
   __device__ __forceinline__ int m() const { return item % m_tiles; }
   __device__ __forceinline__ void advance() {
-    item += gridDim.x;
+    item += step;
     cur = nxt;
-    nxt = load(item + gridDim.x);
+    nxt = load(item + step);
   }
 };
 
@@ -247,24 +341,56 @@ __global__ void __launch_bounds__(C::kThreads, 1)
   uint64_t *dfull = empty + S;                          // [2]
   uint64_t *dempty = dfull + 2;                         // [2]
   uint64_t *xbar = dempty + 2;                          // [group][2 warp pairs][2 buffers]: column-max exchange
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 4 * C::kEpi);
+  uint64_t *pfull = xbar + 4 * C::kEpi;                 // [S] pair, rank 1: its scale threads' arrivals
+  uint64_t *pempty = pfull + S;                         // [2] pair, rank 1: its epilogue threads' arrivals
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pempty + 2);
 
   const int warp = threadIdx.x >> 5;
+  // CTA pair: rank 0 issues the MMAs and owns the barriers they wait on (full,
+  // dempty).  Rank 1's scale and epilogue threads arrive on barriers of their
+  // own CTA (pfull, pempty) as cheaply as on a single CTA, and one of its idle
+  // warps forwards each completed phase with a single cluster-scope arrival:
+  // a cluster-scope release from the busy threads themselves would wait for
+  // their outstanding loads and stores (ncu: the pair ran at half speed).
+  const uint32_t rank = C::kPair ? cluster_rank() : 0u;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < S; ++i) { mbar_init(&full[i], 1 + 128); mbar_init(&empty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&dfull[i], 1); mbar_init(&dempty[i], 128 * C::kEpi); }
+    // full: the producer's expect_tx + every scale thread (+ the peer's forwarded arrival);
+    // dempty: every epilogue thread (+ the peer's forwarded arrival)
+    for (int i = 0; i < S; ++i) {
+      mbar_init(&full[i], C::kPair ? 1 + 128 + 1 : 1 + 128);
+      mbar_init(&empty[i], 1);
+      mbar_init(&pfull[i], 128 + 1);                   // rank 1: its scale threads + its producer's expect_tx
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&dfull[i], 1);
+      mbar_init(&dempty[i], C::kPair ? 128 * C::kEpi + 1 : 128 * C::kEpi);
+      mbar_init(&pempty[i], 128 * C::kEpi);
+    }
     for (int i = 0; i < 4 * C::kEpi; ++i) mbar_init(&xbar[i], 64);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
+  if constexpr (C::kPair) cluster_sync();              // the peer's barriers exist before anything reaches them
   if (warp == 2) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(C::kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (C::kPair) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(C::kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                   "r"(C::kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // work items: CTA (pair) c takes items c, c + count, ...; a pair CTA's weight rows are block 2 m + rank
+  const int first_item = C::kPair ? static_cast<int>(cluster_idx()) : static_cast<int>(blockIdx.x);
+  const int item_step = C::kPair ? static_cast<int>(cluster_count()) : static_cast<int>(gridDim.x);
+  // the leader's barriers as shared::cluster addresses (the pair's reports go there)
+  const uint32_t full_l = C::kPair ? peer_addr(smem_u32(full), 0) : 0u;
+  const uint32_t dempty_l = C::kPair ? peer_addr(smem_u32(dempty), 0) : 0u;
   const uint32_t tmem = *tmem_slot;
   // set-up above overlaps the previous kernel's tail; its results are read below
   WM_PDL_WAIT();
@@ -281,15 +407,33 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     // decode: each weight box is read by one tile per launch, so it streams
     // through L2 evict-first; prefill tiles of one expert share its boxes
     const uint64_t stream_once = l2_evict_first_policy();
-    for (TileCursor tc(p, n_items); tc.valid() && ok; tc.advance()) {
+    for (TileCursor tc(p, n_items, first_item, item_step); tc.valid() && ok; tc.advance()) {
       const int4 tile = tc.cur;
-      const int m = tc.m() / p.k_splits;
-      const int k0 = (tc.m() - m * p.k_splits) * kstages * C::kKC;   // this item's K range
+      const int mi = tc.m() / p.k_splits;
+      const int k0 = (tc.m() - mi * p.k_splits) * kstages * C::kKC;   // this item's K range
+      const int m = C::kPair ? 2 * mi + static_cast<int>(rank) : mi;  // this CTA's 128-row block
       const int nb = (tile.z + 15) >> 4;                // 16-row token boxes per term
       for (int kc = 0; kc < kstages; ++kc, ++g) {
         const int s = g % S;
         if (!(ok = mbar_wait(&empty[s], ((g / S) & 1) ^ 1, p.err, 1))) break;
-        if (elect_one()) {
+        if (C::kPair && elect_one()) {
+          // this CTA's 128 weight rows and its own token term (rank 0: hi, rank 1: lo), counted on a
+          // barrier of its own CTA: rank 0's full, rank 1's pfull (which its forwarding warp relays
+          // to rank 0 with the scale rows; copies completing on the other SM's barrier made the
+          // pair slower than one CTA)
+          uint64_t *fb = rank == 0 ? &full[s] : &pfull[s];
+          mbar_expect_tx(fb, HV * kM * kKH / 2 + HV * nb * 16 * kKH);
+          for (int q = 0; q < HV; ++q) {
+            const int x = k0 + kc * C::kKC + q * kKH;
+            uint8_t *a = sA + s * C::kAStage + q * C::kABox;
+            if (p.mode == 0)
+              tma_load_4d(a, &tmA, x, 0, 0, tile.x * (p.I / 4) + m * 8, fb);
+            else
+              tma_load_2d(a, &tmA, x, tile.x * p.rows + m * kM, fb);
+            uint8_t *b = sB + s * C::kBStage + q * C::kBBox;
+            for (int j = 0; j < nb; ++j) tma_load_2d(b + j * 16 * kKH, rank == 0 ? &tmBh : &tmBl, x, tile.y + 16 * j, fb);
+          }
+        } else if (!C::kPair && elect_one()) {
           // transaction bytes count the packed global bytes of the weights
           mbar_expect_tx(&full[s], HV * (p.a_fp8 ? kM * kKH : kM * kKH / 2) + 2 * HV * nb * 16 * kKH);
           for (int q = 0; q < HV; ++q) {
@@ -320,6 +464,81 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       const uint32_t gg = g - 1 - q;
       ok = mbar_wait(&empty[gg % S], (gg / S) & 1, p.err, 2);
     }
+  } else if (C::kPair && rank != 0 && (warp == 1 || warp == 3)) {
+    // ------------------------------------- pair, rank 1: forward to rank 0
+    // warp 1: each stage's copies and scale rows (pfull) -> the leader's full barrier;
+    // warp 3: each work item's released accumulator (pempty) -> its dempty
+    uint32_t g = 0, it = 0;
+    bool ok = true;
+    for (TileCursor tc(p, n_items, first_item, item_step); tc.valid() && ok; tc.advance(), ++it) {
+      if (warp == 1) {
+        for (int kc = 0; kc < kstages && ok; ++kc, ++g) {
+          const int s = g % S;
+          if (!(ok = mbar_wait(&pfull[s], (g / S) & 1, p.err, 11))) break;
+          if ((threadIdx.x & 31) == 0) mbar_arrive_at(full_l + 8u * s);
+          __syncwarp();
+        }
+      } else {
+        const int db = it & 1;
+        if (!(ok = mbar_wait(&pempty[db], (it >> 1) & 1, p.err, 12))) break;
+        if ((threadIdx.x & 31) == 0) mbar_arrive_at(dempty_l + 8u * db);
+        __syncwarp();
+      }
+    }
+  } else if (warp == 1 && C::kPair) {
+    // ------------------------------------------- MMA, CTA pair (rank 0 only)
+    // M = 256: rows [0, 128) from this CTA's A stage, [128, 256) from the
+    // peer's; N = hi rows (this CTA's B stage) then lo rows (the peer's); D
+    // lands in both CTAs' tensor memory, each CTA's scale atoms in its own
+    if (rank == 0) {
+      const uint32_t sfa = tmem + C::kSfCol0;
+      const uint32_t sfb = sfa + HV * 4;
+      uint32_t g = 0, it = 0;
+      bool ok = true;
+      for (TileCursor tc(p, n_items, first_item, item_step); tc.valid() && ok; tc.advance(), ++it) {
+        const int4 tile = tc.cur;
+        const int n_mma = 2 * max(16, (tile.z + 15) & ~15);
+        const int db = it & 1;
+        if (!(ok = mbar_wait_cl(&dempty[db], ((it >> 1) & 1) ^ 1, p.err, 3))) break;
+        tc_fence_after();
+        const uint32_t d_addr = tmem + db * C::kDCols;
+        for (int kc = 0; kc < kstages && ok; ++kc, ++g) {
+          const int s = g % S;
+          if (!(ok = mbar_wait_cl(&full[s], (g / S) & 1, p.err, 4))) break;
+          tc_fence_after();
+          if (elect_one()) {
+            const uint32_t f0 = smem_u32(sF + s * C::kSFStage);
+#pragma unroll
+            for (int q = 0; q < HV; ++q) {
+              tc_cp_sf_pair(sfa + 4 * q, sdesc_atom(f0 + q * 512));
+#pragma unroll
+              for (int a = 0; a < C::kBAtoms; ++a)
+                tc_cp_sf_pair(sfb + C::kSfbCols * q + 4 * a, sdesc_atom(f0 + (HV + q * C::kBAtoms + a) * 512));
+            }
+            const uint32_t a0 = smem_u32(sA + s * C::kAStage);
+            const uint32_t b0 = smem_u32(sB + s * C::kBStage);
+#pragma unroll
+            for (int kb = 0; kb < C::kKC / 32; ++kb) {
+              const int q = kb >> 2;
+              const uint32_t j = kb & 3;
+              tc_mma_mx_pair(d_addr, bdesc_sw128(a0 + q * C::kABox) + 2 * j, bdesc_sw128(b0 + q * C::kBBox) + 2 * j,
+                             idesc_mx(n_mma, j, 2 * kM), (j << 30) | (sfa + 4 * q), (j << 30) | (sfb + C::kSfbCols * q),
+                             (kc == 0 && kb == 0) ? 0u : 1u);
+            }
+            tc_commit_pair(peer_addr(smem_u32(&empty[s]), 0));
+            tc_commit_pair(peer_addr(smem_u32(&empty[s]), 1));
+          }
+          __syncwarp();
+        }
+        if (ok) {
+          if (elect_one()) {
+            tc_commit_pair(peer_addr(smem_u32(&dfull[db]), 0));
+            tc_commit_pair(peer_addr(smem_u32(&dfull[db]), 1));
+          }
+          __syncwarp();
+        }
+      }
+    }
   } else if (warp == 1) {
     // --------------------------------------------------------------- MMA
     const uint32_t sfa = tmem + C::kSfCol0;
@@ -327,7 +546,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     const uint32_t a_fmt_mask = p.a_fp8 ? ~(7u << 7) : ~0u;   // A format field: e2m1 (5) or e4m3 (0)
     uint32_t g = 0, it = 0;
     bool ok = true;
-    for (TileCursor tc(p, n_items); tc.valid() && ok; tc.advance(), ++it) {
+    for (TileCursor tc(p, n_items, first_item, item_step); tc.valid() && ok; tc.advance(), ++it) {
       const int4 tile = tc.cur;
       const int n_mma = 2 * max(16, (tile.z + 15) & ~15);   // hi and lo rows
       const int db = it & 1;
@@ -387,7 +606,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       uint32_t b[BA][8];
       uint32_t sub[BA];                                 // kLoSub for a lo-term row, else 0
     };
-    TileCursor cur(p, n_items);       // prefetch cursor
+    TileCursor cur(p, n_items, first_item, item_step);   // prefetch cursor
     int c_ch = 0;
     auto load_words = [&](const uint8_t *src, uint32_t *dst) {
       if (CW == 8) {
@@ -414,8 +633,9 @@ __global__ void __launch_bounds__(C::kThreads, 1)
       }
       if (!cur.valid()) return;
       const int4 tile = cur.cur;
-      const int m = cur.m() / p.k_splits;
-      const int kofs = (cur.m() - m * p.k_splits) * kb + c_ch * 4 * CW;   // first scale byte of the chunk
+      const int mi = cur.m() / p.k_splits;
+      const int kofs = (cur.m() - mi * p.k_splits) * kb + c_ch * 4 * CW;   // first scale byte of the chunk
+      const int m = C::kPair ? 2 * mi + static_cast<int>(rank) : mi;    // this CTA's 128-row block
       const int grow = p.mode == 0 ? ((t >> 3) & 1) * p.I + m * 64 + (t >> 4) * 8 + (t & 7) : m * kM + t;
       if (grow < p.rows)                                // a last partial 128-row tile (score rows): zero scales
         load_words(p.a_scales + (static_cast<int64_t>(tile.x) * p.rows + grow) * ks32 + kofs, e.a);
@@ -435,7 +655,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
         cur.advance();
       }
     };
-    const int my_items = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int my_items = first_item < n_items ? (n_items - 1 - first_item) / item_step + 1 : 0;
     const uint32_t total = static_cast<uint32_t>(my_items) * kstages;
     Chunk ring[2];
     fetch(ring[0]);
@@ -469,7 +689,7 @@ __global__ void __launch_bounds__(C::kThreads, 1)
             for (int a = 0; a < BA; ++a) f[(HV + q * BA + a) * 128 + o] = vb[a] - ring[u].sub[a];
           }
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          mbar_arrive(&full[s]);
+          mbar_arrive(C::kPair && rank != 0 ? &pfull[s] : &full[s]);
         }
         if (!ok || g >= total) break;
         fetch(ring[u]);
@@ -487,11 +707,13 @@ __global__ void __launch_bounds__(C::kThreads, 1)
     uint32_t xchg_n = 0;
     uint32_t it = 0;
     bool ok = true;
-    for (TileCursor tc(p, n_items); tc.valid() && ok; tc.advance(), ++it) {
+    for (TileCursor tc(p, n_items, first_item, item_step); tc.valid() && ok; tc.advance(), ++it) {
       const int4 tile = tc.cur;
-      const int m = tc.m() / p.k_splits;
+      const int m = C::kPair ? 2 * (tc.m() / p.k_splits) + static_cast<int>(rank) : tc.m() / p.k_splits;
       const int db = it & 1;
-      if (!(ok = mbar_wait(&dfull[db], (it >> 1) & 1, p.err, 8))) break;
+      if (!(ok = C::kPair ? mbar_wait_cl(&dfull[db], (it >> 1) & 1, p.err, 8)
+                          : mbar_wait(&dfull[db], (it >> 1) & 1, p.err, 8)))
+        break;
       tc_fence_after();
       const int n = tile.z;
       const int n16 = max(16, (n + 15) & ~15);
@@ -577,15 +799,20 @@ __global__ void __launch_bounds__(C::kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&dempty[db]);
+      mbar_arrive(C::kPair && rank != 0 ? &pempty[db] : &dempty[db]);
     }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (C::kPair) cluster_sync();              // both CTAs done with the pair's tensor memory and barriers
   if (warp == 2) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+    if constexpr (C::kPair)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols));
   }
+  if (p.done) wm::combine_if_last(p.comb, p.done);
 }
 
 // --------------------------------------------------------- two-term split
@@ -594,14 +821,31 @@ __global__ void __launch_bounds__(C::kThreads, 1)
 // hi, lo e4m3 bytes and the hi term's E8M0 scale per 32 columns.  Four
 // threads per 32-value block, eight values each.  `zero`, if set, is a word
 // the following tensor-core launch reports errors in, cleared here.
+// With plan.idx set (GATHER, calls of at most kSmallRouteMax slots) every CTA
+// groups the call's assignments by expert itself (small_route) and CTA 0
+// writes the grouping for the launches that follow: no permute launch.
 template <bool GATHER>
 __global__ void k_split_e4m3(const uint16_t *__restrict__ src, const int32_t *__restrict__ perm,
                              const int32_t *__restrict__ count, int S, int kk, int K, uint8_t *__restrict__ hi,
-                             uint8_t *__restrict__ lo, uint8_t *__restrict__ sc, int32_t *__restrict__ zero) {
+                             uint8_t *__restrict__ lo, uint8_t *__restrict__ sc, int32_t *__restrict__ zero,
+                             const wm::RoutePlan plan) {
+  __shared__ wm::SmallRoute route;
+  __shared__ int32_t route_key[wm::kSmallRouteMax];
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
-  if (zero && blockIdx.x == 0 && threadIdx.x == 0) *zero = 0;
-  const int rows = count ? min(S, max(0, *count)) : S;
+  int rows;
+  if (GATHER && plan.idx) {
+    if (threadIdx.x < 32) wm::small_route(plan.idx, plan.T, plan.k, plan.shared_expert, plan.E, route, route_key);
+    __syncthreads();
+    if (blockIdx.x == 0)
+      wm::publish_route(route, plan.T, plan.k, plan.shared_expert, plan.E, plan.offsets, plan.perm, plan.inv,
+                        plan.active, plan.counters, plan.tiles, plan.tile_n, plan.done);
+    perm = route.perm;
+    rows = route.bad ? 0 : S;
+  } else {
+    if (zero && blockIdx.x == 0 && threadIdx.x == 0) *zero = 0;
+    rows = count ? min(S, max(0, *count)) : S;
+  }
   const int per_row = K / 8;
   const int64_t total = static_cast<int64_t>(rows) * per_row;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;   // a multiple of 32
@@ -704,7 +948,8 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
                   const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order, float limit,
                   const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
                   uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool a_fp8 = false,
-                  int k_splits = 1, float *y_part = nullptr, int64_t part_stride = 0, int4 dense = int4{0, 0, 0, 0}) {
+                  int k_splits = 1, float *y_part = nullptr, int64_t part_stride = 0, int4 dense = int4{0, 0, 0, 0},
+                  const wm::CombineArgs *comb = nullptr, int32_t *done = nullptr) {
   if (K % C::kKC) return wm::fail(WM_ERR_UNSUPPORTED, "expert mx: K must be a multiple of the stage depth");
   if (k_splits < 1 || (K / C::kKC) % k_splits || (k_splits > 1 && (mode != 1 || !y_part)))
     return wm::fail(WM_ERR_INVALID, "expert mx: bad K split");
@@ -771,7 +1016,9 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.H = H;
   p.order = order;
   p.limit = limit;
-  p.m_tiles = (mode == 0 ? I / 64 : (rows + kM - 1) / kM) * k_splits;
+  p.m_tiles = C::kPair ? (mode == 0 ? I / 128 : rows / (2 * kM)) : (mode == 0 ? I / 64 : (rows + kM - 1) / kM) * k_splits;
+  if (C::kPair && (k_splits != 1 || a_fp8 || dense.x > 0 || (mode == 0 ? I % 128 : rows % (2 * kM)) != 0))
+    return wm::fail(WM_ERR_INVALID, "expert mx: the CTA-pair configuration takes whole 256-row blocks, no K split");
   p.k_splits = k_splits;
   p.y_part = y_part;
   p.part_stride = part_stride;
@@ -790,24 +1037,82 @@ int launch_mx_cfg(int mode, const uint8_t *w, const uint8_t *a_scales, int E, in
   p.h_out = h_out;
   p.y_out = y_out;
   p.err = err;
-  if (cudaError_t e = wm::launch_pdl(k_expert_mx<C>, dim3(wm::sm_count()), dim3(C::kThreads), C::kSmem, stream, tmA,
-                                     tmBh, tmBl, p))
-    return wm::fail(WM_ERR_CUDA, std::string("expert mx: ") + cudaGetErrorString(e));
+  if (comb && done) {
+    p.comb = *comb;
+    p.done = done;
+  }
+  cudaError_t e;
+  if constexpr (C::kPair) {
+    // clusters of two CTAs (the pair), programmatic dependent launch as for every launch of the path
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(wm::sm_count() & ~1);
+    cfg.blockDim = dim3(C::kThreads);
+    // a persistent grid must be resident all at once: clusters of two need both CTAs on one
+    // TPC's pair of SMs, and not every SM can be part of a pair, so the grid is the number of
+    // pairs that fit, not the SM count
+    static int max_clusters[64] = {0};
+    if (dev >= 0 && dev < 64 && max_clusters[dev] == 0) {
+      cudaLaunchConfig_t q = cfg;
+      q.dynamicSmemBytes = C::kSmem;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 2;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, k_expert_mx<C>, &q) != cudaSuccess || n < 1)
+        return wm::fail(WM_ERR_CUDA, "expert mx: no resident CTA pair");
+      max_clusters[dev] = std::min(n, wm::sm_count() / 2);
+      if (getenv("WM_MX_PAIR_VERBOSE")) fprintf(stderr, "expert mx: %d resident CTA pairs\n", max_clusters[dev]);
+    }
+    cfg.gridDim = dim3(2 * max_clusters[dev]);
+    cfg.dynamicSmemBytes = C::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 2;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    e = cudaLaunchKernelEx(&cfg, k_expert_mx<C>, tmA, tmBh, tmBl, p);
+  } else {
+    e = wm::launch_pdl(k_expert_mx<C>, dim3(wm::sm_count()), dim3(C::kThreads), C::kSmem, stream, tmA, tmBh, tmBl, p);
+  }
+  if (e != cudaSuccess) return wm::fail(WM_ERR_CUDA, std::string("expert mx: ") + cudaGetErrorString(e));
   return wm::check_launch("expert mx");
+}
+
+// WM_MX_PAIR=1: the prefill configuration runs on CTA pairs (cta_group::2)
+bool mx_pair_enabled() {
+  const char *v = getenv("WM_MX_PAIR");
+  return v && v[0] == '1';
 }
 
 int launch_mx(bool decode, int mode, const uint8_t *w, const uint8_t *a_scales, int E, int rows, int K,
               const uint8_t *b_hi, const uint8_t *b_lo, const uint8_t *b_sc, int S_rows, int I, int H, int order,
               float limit, const int4 *tiles, const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc,
-              uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool wide_up = false) {
+              uint16_t *h_out, uint16_t *y_out, int32_t *err, cudaStream_t stream, bool wide_up = false,
+              const wm::CombineArgs *comb = nullptr, int32_t *done = nullptr) {
+  const int4 nd{0, 0, 0, 0};
   if (decode && mode == 0 && wide_up)
     return launch_mx_cfg<MxDecodeUp>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit,
                                      tiles, n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
   if (decode)
     return launch_mx_cfg<MxDecode>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
-                                   n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
+                                   n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream, false, 1, nullptr, 0, nd,
+                                   comb, done);
+  if (mx_pair_enabled() && (mode == 0 ? I % 128 : rows % (2 * kM)) == 0)
+    return launch_mx_cfg<MxPrefillPair>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit,
+                                        tiles, n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream, false, 1, nullptr,
+                                        0, nd, comb, done);
   return launch_mx_cfg<MxPrefill>(mode, w, a_scales, E, rows, K, b_hi, b_lo, b_sc, S_rows, I, H, order, limit, tiles,
-                                  n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream);
+                                  n_tiles, h_hi, h_lo, h_sc, h_out, y_out, err, stream, false, 1, nullptr, 0, nd,
+                                  comb, done);
 }
 
 }  // namespace
@@ -823,15 +1128,15 @@ int mx_tile_n(int T, int k, int n_routed) {
 }
 
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
-                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero) {
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero, const RoutePlan &plan) {
   const int64_t work = static_cast<int64_t>(S) * (K / 8);
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
   if (grid > 0) {
     const cudaError_t e =
         perm ? launch_pdl(k_split_e4m3<true>, dim3(grid), dim3(256), 0, stream, src, perm, count, S, kk, K, hi, lo, sc,
-                          zero)
+                          zero, plan)
              : launch_pdl(k_split_e4m3<false>, dim3(grid), dim3(256), 0, stream, src, static_cast<const int32_t *>(nullptr),
-                          count, S, 1, K, hi, lo, sc, zero);
+                          count, S, 1, K, hi, lo, sc, zero, RoutePlan{});
     if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("split e4m3: ") + cudaGetErrorString(e));
   }
   return check_launch("split e4m3");
@@ -849,9 +1154,10 @@ int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, co
 
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
-                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream) {
+                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream, const CombineArgs *comb,
+                   int32_t *done) {
   return launch_mx(tile_n == MxDecode::kNMax, 1, w2, s2, E, H, I, h_hi, h_lo, h_sc, S_rows, I, H, WM_UP_GATE, 0.0f,
-                   tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream);
+                   tiles, n_tiles, nullptr, nullptr, nullptr, nullptr, y, err, stream, false, comb, done);
 }
 
 }  // namespace wm

@@ -46,6 +46,7 @@
 // Outputs match the other expert paths' buffers: h (bf16, slot order) and y
 // (bf16, slot order), combined by the same k_combine.
 #include "wm_common.cuh"
+#include "wm_combine.cuh"
 #include "wm_moe.cuh"
 #include "wm_tc.cuh"
 
@@ -72,6 +73,9 @@ struct StreamParams {
   float limit;
   int stage_rows;            // rows the shared-memory operand buffer holds
   int ring_offset;           // shared-memory offset of the warps' copy rings
+  wm::RoutePlan plan;        // up projection: plan.idx set -> group the assignments in-kernel
+  wm::CombineArgs comb;      // down projection: with `done` set, the last CTA combines the rows
+  int32_t *done;
   uint16_t *out;             // up: h [S, I]; down: y [S, H] (bf16, slot order)
 };
 
@@ -161,14 +165,30 @@ __device__ __forceinline__ float warp_sums(float (&v)[V], int lane) {
 constexpr int kMaxCtaExperts = 32;   // experts one CTA's chunk range can span: at most E / grid + 2
 
 template <int MODE, int PB>
-__global__ void __launch_bounds__(kThreads, 1) k_expert_stream(const __grid_constant__ StreamParams p) {
+__device__ __forceinline__ void stream_body(const StreamParams &p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ int m_e[kMaxCtaExperts], m_p0[kMaxCtaExperts], m_n[kMaxCtaExperts];
+  __shared__ wm::SmallRoute route;
+  __shared__ int32_t route_key[wm::kSmallRouteMax];
   constexpr int VPP = 2 * PB;                 // values per piece
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
-  if (p.counters[1] != 0) return;             // bad expert id: the combine writes zeros
-  const int n_active = p.counters[0];
+  // up projection of a small call: group the assignments here (every CTA), CTA 0 writes the grouping
+  const bool in_kernel = MODE == 0 && p.plan.idx != nullptr;
+  int n_active;
+  if (in_kernel) {
+    if (threadIdx.x < 32)
+      wm::small_route(p.plan.idx, p.plan.T, p.plan.k, p.plan.shared_expert, p.plan.E, route, route_key);
+    __syncthreads();
+    if (blockIdx.x == 0)
+      wm::publish_route(route, p.plan.T, p.plan.k, p.plan.shared_expert, p.plan.E, p.plan.offsets, p.plan.perm,
+                        p.plan.inv, p.plan.active, p.plan.counters, nullptr, 0, p.plan.done);
+    if (route.bad) return;                    // bad expert id: the combine writes zeros
+    n_active = route.n_act;
+  } else {
+    if (p.counters[1] != 0) return;
+    n_active = p.counters[0];
+  }
   const int cpe = p.rows / kRows;
   const int64_t n_chunks = static_cast<int64_t>(n_active) * cpe;
   const int64_t c0 = n_chunks * blockIdx.x / gridDim.x, c1 = n_chunks * (blockIdx.x + 1) / gridDim.x;
@@ -177,13 +197,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_expert_stream(const __grid_cons
   const int a_first = static_cast<int>(c0 / cpe), a_last = static_cast<int>((c1 - 1) / cpe);
 
   // ------------------------------ the CTA's experts, operand rows -> f16
-  for (int i = threadIdx.x; i <= a_last - a_first && i < kMaxCtaExperts; i += kThreads) {
-    const int e = p.active[a_first + i];
-    const int o = p.offsets[e];
-    m_e[i] = e; m_p0[i] = o; m_n[i] = p.offsets[e + 1] - o;
-  }
-  const int p_lo = p.offsets[p.active[a_first]];
-  const int p_hi = p.offsets[p.active[a_last] + 1];
+  if (!in_kernel)
+    for (int i = threadIdx.x; i <= a_last - a_first && i < kMaxCtaExperts; i += kThreads) {
+      const int e = p.active[a_first + i];
+      const int o = p.offsets[e];
+      m_e[i] = e; m_p0[i] = o; m_n[i] = p.offsets[e + 1] - o;
+    }
+  const int p_lo = in_kernel ? route.act_p0[a_first] : p.offsets[p.active[a_first]];
+  const int p_hi = in_kernel ? route.act_p0[a_last] + route.act_n[a_last] : p.offsets[p.active[a_last] + 1];
   int base_row = 0, n_rows;
   if (MODE == 0) {
     n_rows = p.stage_rows;                    // every token of the call
@@ -195,7 +216,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_expert_stream(const __grid_cons
   float *xk = reinterpret_cast<float *>(smem + static_cast<size_t>(p.stage_rows) * K * 2);  // [n_rows][G]
   int *tok = reinterpret_cast<int *>(xk + static_cast<size_t>(p.stage_rows) * G);           // up: slot -> token
   if (MODE == 0)
-    for (int i = threadIdx.x; i < p_hi - p_lo; i += kThreads) tok[i] = p.perm[p_lo + i] / p.kk;
+    for (int i = threadIdx.x; i < p_hi - p_lo; i += kThreads)
+      tok[i] = (in_kernel ? route.perm[p_lo + i] : p.perm[p_lo + i]) / p.kk;
   for (int g = threadIdx.x; g < n_rows * G; g += kThreads) {
     const int r = g / G, q = g - r * G;
     const uint4 *s = reinterpret_cast<const uint4 *>(p.src + static_cast<int64_t>(base_row + r) * K + q * 32);
@@ -242,7 +264,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_expert_stream(const __grid_cons
   const uint64_t pol = wm_tc::l2_evict_first_policy();
   auto meta = [&](int a, int &e, int &p0, int &n) {
     const int i = a - a_first;
-    if (i < kMaxCtaExperts) {
+    if (in_kernel) {
+      e = route.act_e[a]; p0 = route.act_p0[a]; n = route.act_n[a];
+    } else if (i < kMaxCtaExperts) {
       e = m_e[i]; p0 = m_p0[i]; n = m_n[i];
     } else {
       e = p.active[a]; p0 = p.offsets[e]; n = p.offsets[e + 1] - p0;
@@ -460,6 +484,14 @@ __global__ void __launch_bounds__(kThreads, 1) k_expert_stream(const __grid_cons
   cp_async_wait<0>();
 }
 
+// The body may return early (CTAs or warps without chunks); the down
+// projection of a small call then combines the call's rows in its last CTA.
+template <int MODE, int PB>
+__global__ void __launch_bounds__(kThreads, 1) k_expert_stream(const __grid_constant__ StreamParams p) {
+  stream_body<MODE, PB>(p);
+  if (MODE == 1 && p.done) wm::combine_if_last(p.comb, p.done);
+}
+
 // operand rows (f16 + one f32 scale per 32 values) and, for the up projection, a token index per slot
 size_t stage_bytes(int rows, int K, int slots = 0) {
   return static_cast<size_t>(rows) * K * 2 + static_cast<size_t>(rows) * (K / 32) * 4 + static_cast<size_t>(slots) * 4;
@@ -497,8 +529,9 @@ bool stream_supported(int T, int k, int has_shared, int H, int I) {
 
 int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int H, int I, int order, float limit,
                      const uint16_t *x, const int32_t *offsets, const int32_t *perm, const int32_t *active,
-                     const int32_t *counters, uint16_t *h, cudaStream_t stream) {
+                     const int32_t *counters, uint16_t *h, cudaStream_t stream, const RoutePlan &plan) {
   StreamParams p{};
+  p.plan = plan;
   p.w = w13; p.sc = s13; p.src = x; p.offsets = offsets; p.perm = perm; p.active = active; p.counters = counters;
   p.kk = kk; p.K = H; p.rows = 2 * I; p.I = I;
   p.up_base = order == WM_UP_GATE ? 0 : I;
@@ -514,8 +547,12 @@ int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int 
 
 int launch_stream_down(const uint8_t *w2, const uint8_t *s2, int S, int H, int I, const uint16_t *h,
                        const int32_t *offsets, const int32_t *active, const int32_t *counters, uint16_t *y,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const CombineArgs *comb, int32_t *done) {
   StreamParams p{};
+  if (comb && done) {
+    p.comb = *comb;
+    p.done = done;
+  }
   p.w = w2; p.sc = s2; p.src = h; p.offsets = offsets; p.active = active; p.counters = counters;
   p.kk = 1; p.K = I; p.rows = H; p.I = I; p.stage_rows = S; p.out = y;
   size_t ring_offset;

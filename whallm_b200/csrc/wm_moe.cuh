@@ -5,6 +5,8 @@
 #include <stdint.h>
 
 #include "wm_common.cuh"
+#include "wm_combine.cuh"
+#include "wm_route.cuh"
 
 namespace wm {
 
@@ -46,12 +48,14 @@ constexpr int kStreamMaxTokens = 2;               // calls of at most this many 
 constexpr int kStreamMaxH = 4096, kStreamMaxI = 1024;   // ... when the experts are this small (Qwen-class)
 // H and I multiples of 256, and the staged rows (T tokens of H, S slots of I) fit in shared memory
 bool stream_supported(int T, int k, int has_shared, int H, int I);
+// plan.idx set: the kernel groups the call's assignments itself (no permute launch)
 int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int H, int I, int order, float limit,
                      const uint16_t *x, const int32_t *offsets, const int32_t *perm, const int32_t *active,
-                     const int32_t *counters, uint16_t *h, cudaStream_t stream);
+                     const int32_t *counters, uint16_t *h, cudaStream_t stream, const RoutePlan &plan = RoutePlan{});
+// comb + done: the launch's last CTA also combines the rows (done zeroed by the call's first kernel)
 int launch_stream_down(const uint8_t *w2, const uint8_t *s2, int S, int H, int I, const uint16_t *h,
                        const int32_t *offsets, const int32_t *active, const int32_t *counters, uint16_t *y,
-                       cudaStream_t stream);
+                       cudaStream_t stream, const CombineArgs *comb = nullptr, int32_t *done = nullptr);
 
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
@@ -59,17 +63,21 @@ bool mx_supported(int H, int I);
 int mx_tile_n(int T, int k, int n_routed);
 // rows [0, min(S, *count)) (all S when count is null); GATHER when perm != null: row p = src[perm[p] / kk];
 // *zero (if given) is set to 0 once the kernel's dependency wait has returned
+// plan.idx set (GATHER only): the kernel groups the call's assignments itself (no permute launch; perm unused)
 int launch_split_e4m3(const uint16_t *src, const int32_t *perm, const int32_t *count, int S, int kk, int K,
-                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero = nullptr);
+                      uint8_t *hi, uint8_t *lo, uint8_t *sc, cudaStream_t stream, int32_t *zero = nullptr,
+                      const RoutePlan &plan = RoutePlan{});
 // the up projection writes h's e4m3 terms itself (true) or bf16 h for launch_split_e4m3 (false)
 bool mx_fused_split(int tile_n);
 int launch_mx_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const uint8_t *x_hi,
                  const uint8_t *x_lo, const uint8_t *x_sc, int S_rows, int order, float limit, const int4 *tiles,
                  const int32_t *n_tiles, uint8_t *h_hi, uint8_t *h_lo, uint8_t *h_sc, uint16_t *h, int32_t *err,
                  int tile_n, cudaStream_t stream, int T);  // T: tokens of the call (tiles of more than 16 use two epilogue groups)
+// comb + done: the launch's last CTA also combines the rows (done zeroed by the call's first kernel)
 int launch_mx_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, const uint8_t *h_hi,
                    const uint8_t *h_lo, const uint8_t *h_sc, int S_rows, const int4 *tiles, const int32_t *n_tiles,
-                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream);
+                   uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream, const CombineArgs *comb = nullptr,
+                   int32_t *done = nullptr);
 
 // Workspace carved out of the caller's buffer for one expert-forward call.
 // S = T * (k + has_shared) assignments.
@@ -78,7 +86,7 @@ struct MoeWorkspace {
   int32_t *perm;       // [S] sorted slot -> flat assignment
   int32_t *inv;        // [S] flat assignment -> sorted slot
   int32_t *active;     // [E] active expert ids, ascending
-  int32_t *counters;   // [4]: n_active, permute error flag, n_tiles, tensor-core error code
+  int32_t *counters;   // [8]: n_active, permute error flag, n_tiles, tensor-core error code, fused-combine ticket
   int4 *tiles;         // [E + S/16 + 2] tensor-core work list
   uint16_t *h;         // [S_pad, I] SwiGLU output in sorted-slot order (bf16; f16 on the f16 tensor path)
   uint16_t *x16;       // [S_pad, H] f16 tokens in sorted-slot order (f16 tensor path)
@@ -106,7 +114,7 @@ inline MoeWorkspace carve_workspace(void *base, int T, int k, int H, int I, int 
   size_t o_perm = take(S * sizeof(int32_t));
   size_t o_inv = take(S * sizeof(int32_t));
   size_t o_act = take(E * sizeof(int32_t));
-  size_t o_cnt = take(4 * sizeof(int32_t));
+  size_t o_cnt = take(8 * sizeof(int32_t));
   const size_t S_pad = S < 16 ? 16 : S;
   size_t o_tiles = take((E + S / 16 + 2) * sizeof(int4));
   size_t o_h = take(S_pad * I * sizeof(uint16_t));
