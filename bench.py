@@ -293,9 +293,10 @@ def _layer_launches(name, cfg, T):
     the token split and the two tcgen05 projections (plus the SwiGLU split in
     the prefill configuration), and the combine unless the call has at most
     64 slots and 4096 output values (the down projection's last CTA combines).
-    Affine-4 (tiny): permute, f16 gather, two tcgen05 projections, combine."""
+    Affine-4 (tiny): permute (unless at most 64 slots), f16 gather, two
+    tcgen05 projections, combine."""
     if name == "tiny":
-        return 2 + 5
+        return 2 + (4 if T * cfg["k"] <= 64 else 5)       # at most 64 slots: no permute launch
     H, I, k = cfg["H"], cfg["I"], cfg["k"]
     kk = k + (1 if cfg["shared"] else 0)
     S = T * kk

@@ -233,7 +233,7 @@ def _ws_layout(T, k, E, has_shared):
 
 
 @pytest.mark.parametrize("T,E,path", [(1, 16, "mma"), (3, 16, "mma"), (7, 257, "mma"), (2, 33, "stream"),
-                                      (1, 513, "stream")])
+                                      (1, 513, "stream"), (7, 40, "stream")])
 def test_in_kernel_grouping_equals_permute(dev, monkeypatch, T, E, path):
     # calls of at most 64 slots group their assignments inside the first expert kernel; the grouping it
     # writes to the workspace must be the permute kernel's (offsets, perm, inv, active list, counters and,
@@ -309,3 +309,33 @@ def test_small_call_repeats_bit_for_bit(dev, monkeypatch, path, T):
         assert torch.equal(o, outs[0])
     ref = M.moe_forward(_f32(x), _np(idx), _np(w), _mx_oracle(ex, M.UP_GATE, 10.0), shared_expert=E)
     assert M.max_rel_err(_f32(outs[0]), ref) < TOL
+
+
+def test_in_kernel_grouping_affine_tensor_path(dev):
+    # 16 tokens of the tiny configuration (x top-4 = 64 slots) group their slots in the f16 gather kernel;
+    # the grouping and the work list (64-token tiles, no shared expert) equal the permute kernel's
+    lay = S.make_layer("tiny", dev, seed=2)
+    cfg = lay.cfg
+    T, k, E, H, I = 16, cfg["k"], cfg["E"], cfg["H"], cfg["I"]
+    x = S.make_tokens(T, H, 2, dev)
+    w, idx, _ = W.qwen_route(x, lay.gate_weight, k, True)
+    nbytes = W.experts.workspace_size(T, k, H, I, E, False)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    out = W.experts_forward(x, idx, lay.experts, weights=w, workspace=ws)
+    torch.cuda.synchronize()
+    lay_ws = _ws_layout(T, k, E, 0)
+    get = lambda name, n: ws[lay_ws[name][0]:lay_ws[name][0] + 4 * n].view(torch.int32).cpu().numpy()
+    ri = _np(idx)
+    r_off, r_perm, r_inv = M.permute(ri, E)
+    np.testing.assert_array_equal(get("offsets", E + 1), r_off)
+    np.testing.assert_array_equal(get("perm", ri.size), r_perm)
+    np.testing.assert_array_equal(get("inv", ri.size), r_inv)
+    want = []
+    for e in range(E):
+        n = r_off[e + 1] - r_off[e]
+        want += [(e, r_off[e] + q, min(64, n - q)) for q in range(0, n, 64)]
+    cnt = get("counters", 4)
+    assert cnt[2] == len(want)
+    np.testing.assert_array_equal(get("tiles", 4 * len(want)).reshape(-1, 4)[:, :3], np.array(want, np.int32))
+    ref = M.moe_forward(_f32(x), ri, _np(w), _affine_oracle(lay.experts))
+    assert M.max_rel_err(_f32(out), ref) < TOL

@@ -403,9 +403,10 @@ int run(const Args &a, int fmt) {
   // (WM_FUSE=0 keeps the separate permute and combine launches, for A/B checks)
   const char *fuse_env = getenv("WM_FUSE");
   const bool fuse = !(fuse_env && fuse_env[0] == '0');
-  const bool small = fuse && a.rf.count == 0 && S <= wm::kSmallRouteMax && (stream || mx);
+  const bool small = fuse && a.rf.count == 0 && (stream || mx || tc) &&
+                     S <= (stream ? wm::kStreamRouteMax : wm::kSmallRouteMax);
   // one CTA combines the rows in about one pass over its threads (T * H / 8 output groups)
-  const bool fuse_combine = small && a.reduce && a.T * a.H <= 4096;
+  const bool fuse_combine = small && (stream || mx) && a.reduce && a.T * a.H <= 4096;
   const wm::CombineArgs comb{ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk, a.H,
                              a.out_f32 ? static_cast<void *>(a.out_f32) : static_cast<void *>(a.out),
                              a.out_f32 != nullptr};
@@ -413,7 +414,7 @@ int run(const Args &a, int fmt) {
   if (small) {
     plan.idx = a.idx; plan.T = a.T; plan.k = a.k; plan.shared_expert = a.shared_expert; plan.E = a.E;
     plan.offsets = ws.offsets; plan.perm = ws.perm; plan.inv = ws.inv; plan.active = ws.active;
-    plan.counters = ws.counters; plan.tiles = mx ? ws.tiles : nullptr; plan.tile_n = tile_n; plan.done = done;
+    plan.counters = ws.counters; plan.tiles = (mx || tc) ? ws.tiles : nullptr; plan.tile_n = tile_n; plan.done = done;
   } else if (int rc = wm::launch_permute(a.idx, a.T, a.k, a.shared_expert, a.E, ws.offsets, ws.perm, ws.inv,
                                          ws.active, ws.counters, ws.counters + 1, (tc || mx) ? ws.tiles : nullptr,
                                          ws.counters + 2, tile_n, a.stream, a.rf, ws.counters + 3)) {
@@ -443,7 +444,7 @@ int run(const Args &a, int fmt) {
                                     ws.counters + 2, ws.y, ws.counters + 3, tile_n, a.stream, &comb, done))
       return rc;
   } else if (tc) {
-    if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream)) return rc;
+    if (int rc = wm::launch_gather_f16(a.x, ws.perm, ws.offsets + a.E, S, kk, a.H, ws.x16, a.stream, plan)) return rc;
     if (int rc = wm::launch_tc_up(a.w13.w, a.w13.s, a.E, a.H, a.I, ws.x16, ws.s_pad, a.order, a.limit, ws.tiles,
                                   ws.counters + 2, ws.h, ws.counters + 3, tile_n, a.stream,
                                   affine_tc ? a.w13.sc : nullptr, affine_tc ? a.w13.bi : nullptr))

@@ -829,14 +829,13 @@ __global__ void k_split_e4m3(const uint16_t *__restrict__ src, const int32_t *__
                              const int32_t *__restrict__ count, int S, int kk, int K, uint8_t *__restrict__ hi,
                              uint8_t *__restrict__ lo, uint8_t *__restrict__ sc, int32_t *__restrict__ zero,
                              const wm::RoutePlan plan) {
-  __shared__ wm::SmallRoute route;
+  __shared__ wm::SmallRoute<wm::kSmallRouteMax> route;
   __shared__ int32_t route_key[wm::kSmallRouteMax];
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
   int rows;
   if (GATHER && plan.idx) {
-    if (threadIdx.x < 32) wm::small_route(plan.idx, plan.T, plan.k, plan.shared_expert, plan.E, route, route_key);
-    __syncthreads();
+    wm::small_route(plan.idx, plan.T, plan.k, plan.shared_expert, plan.E, route, route_key);
     if (blockIdx.x == 0)
       wm::publish_route(route, plan.T, plan.k, plan.shared_expert, plan.E, plan.offsets, plan.perm, plan.inv,
                         plan.active, plan.counters, plan.tiles, plan.tile_n, plan.done);

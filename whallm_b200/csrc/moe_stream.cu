@@ -168,8 +168,8 @@ template <int MODE, int PB>
 __device__ __forceinline__ void stream_body(const StreamParams &p) {
   extern __shared__ __align__(16) uint8_t smem[];
   __shared__ int m_e[kMaxCtaExperts], m_p0[kMaxCtaExperts], m_n[kMaxCtaExperts];
-  __shared__ wm::SmallRoute route;
-  __shared__ int32_t route_key[wm::kSmallRouteMax];
+  __shared__ wm::SmallRoute<wm::kStreamRouteMax> route;
+  __shared__ int32_t route_key[wm::kStreamRouteMax];
   constexpr int VPP = 2 * PB;                 // values per piece
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
@@ -177,9 +177,7 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   const bool in_kernel = MODE == 0 && p.plan.idx != nullptr;
   int n_active;
   if (in_kernel) {
-    if (threadIdx.x < 32)
-      wm::small_route(p.plan.idx, p.plan.T, p.plan.k, p.plan.shared_expert, p.plan.E, route, route_key);
-    __syncthreads();
+    wm::small_route(p.plan.idx, p.plan.T, p.plan.k, p.plan.shared_expert, p.plan.E, route, route_key);
     if (blockIdx.x == 0)
       wm::publish_route(route, p.plan.T, p.plan.k, p.plan.shared_expert, p.plan.E, p.plan.offsets, p.plan.perm,
                         p.plan.inv, p.plan.active, p.plan.counters, nullptr, 0, p.plan.done);

@@ -486,12 +486,28 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // x16[p, :] = f16(x[perm[p] / kk, :] * 2^-4): the up projection's B operand in expert order
+// With plan.idx set (calls of at most kSmallRouteMax slots) every CTA groups
+// the call's assignments itself and CTA 0 writes the grouping for the
+// launches that follow: no permute launch.
 __global__ void k_gather_f16(const uint16_t *__restrict__ x, const int32_t *__restrict__ perm,
-                             const int32_t *__restrict__ count, int S, int kk, int H, __half *__restrict__ x16) {
+                             const int32_t *__restrict__ count, int S, int kk, int H, __half *__restrict__ x16,
+                             const wm::RoutePlan plan) {
+  __shared__ wm::SmallRoute<wm::kSmallRouteMax> route;
+  __shared__ int32_t route_key[wm::kSmallRouteMax];
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
   const int per = H / 8;
-  const int rows = min(S, max(0, *count));   // kept assignments (all of them unless an expert range drops some)
+  int rows;
+  if (plan.idx) {
+    wm::small_route(plan.idx, plan.T, plan.k, plan.shared_expert, plan.E, route, route_key);
+    if (blockIdx.x == 0)
+      wm::publish_route(route, plan.T, plan.k, plan.shared_expert, plan.E, plan.offsets, plan.perm, plan.inv,
+                        plan.active, plan.counters, plan.tiles, plan.tile_n, plan.done);
+    perm = route.perm;
+    rows = route.bad ? 0 : S;
+  } else {
+    rows = min(S, max(0, *count));             // kept assignments (all of them unless an expert range drops some)
+  }
   const int64_t total = static_cast<int64_t>(rows) * per;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
     const int pidx = static_cast<int>(i / per), c = static_cast<int>(i % per) * 8;
@@ -581,12 +597,12 @@ bool tc_supported(int H, int I) { return H % 256 == 0 && I % 256 == 0; }
 int tc_tile_n(int T) { return T <= DecodeCfg::kNMax ? DecodeCfg::kNMax : PrefillCfg::kNMax; }
 
 int launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *count, int S, int kk, int H, void *x16,
-                      cudaStream_t stream) {
+                      cudaStream_t stream, const RoutePlan &plan) {
   const int64_t work = static_cast<int64_t>(S) * (H / 8);
   const int grid = static_cast<int>(std::min<int64_t>((work + 255) / 256, sm_count() * 8));
   if (grid > 0)
     if (cudaError_t e = launch_pdl(k_gather_f16, dim3(grid), dim3(256), 0, stream, x, perm, count, S, kk, H,
-                                   static_cast<__half *>(x16)))
+                                   static_cast<__half *>(x16), plan))
       return fail(WM_ERR_CUDA, std::string("gather f16: ") + cudaGetErrorString(e));
   return check_launch("gather f16");
 }

@@ -32,8 +32,9 @@ int launch_permute(const int32_t *idx, int T, int k, int shared_expert, int E, i
 bool tc_supported(int H, int I);
 int tc_tile_n(int T);  // tokens per tile: 64 for decode batches (T <= 64), else 128
 // rows [0, *count) of the expert-ordered token matrix (count = offsets[E] on the device)
+// plan.idx set: the kernel groups the call's assignments itself (no permute launch; perm unused)
 int launch_gather_f16(const uint16_t *x, const int32_t *perm, const int32_t *count, int S, int kk, int H, void *x16,
-                      cudaStream_t stream);
+                      cudaStream_t stream, const RoutePlan &plan = RoutePlan{});
 // af_sc / af_bi (bf16 [E * rows, K / 64]): MLX affine 4-bit weights (group 64) instead of MXFP4 (s13 / s2 unused)
 int launch_tc_up(const uint8_t *w13, const uint8_t *s13, int E, int H, int I, const void *x16, int S_rows, int order,
                  float limit, const int4 *tiles, const int32_t *n_tiles, void *h16, int32_t *err, int tile_n,
@@ -43,7 +44,7 @@ int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
                    const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr);
 
 // moe_stream.cu: CUDA-core MXFP4 weight stream for calls of one or two tokens
-constexpr size_t kStreamSmemMax = 225 * 1024;   // shared memory: staged f16 operand rows + copy rings
+constexpr size_t kStreamSmemMax = 216 * 1024;   // shared memory: staged f16 operand rows + copy rings (+ ~7 KB static)
 constexpr int kStreamMaxTokens = 2;               // calls of at most this many tokens take the stream path
 constexpr int kStreamMaxH = 4096, kStreamMaxI = 1024;   // ... when the experts are this small (Qwen-class)
 // H and I multiples of 256, and the staged rows (T tokens of H, S slots of I) fit in shared memory

@@ -9,16 +9,22 @@
 // shared expert's tiles first.
 //
 // For S = T * kk <= kSmallRouteMax every CTA of the kernel builds the grouping
-// in shared memory (warp 0: each lane ranks its assignments against all S
-// keys), so no CTA waits for another; CTA 0 also writes it to the workspace
-// for the launches that follow (offsets, perm, inv, active, counters, tiles).
+// in shared memory (each thread ranks its assignments against all S keys), so
+// no CTA waits for another; CTA 0 also writes it to the workspace for the
+// launches that follow (offsets, perm, inv, active, counters, tiles).
 #pragma once
 
 #include "wm_common.cuh"
 
 namespace wm {
 
+// Every CTA of the first kernel repeats the ranking (S^2 / threads comparisons
+// before its first row): measured, that beats a permute launch at 9-63 slots
+// (DeepSeek-class B = 1: expert call 63.3 -> 60.4 us; B = 4: 106.8 -> 106.4)
+// and loses above (256 slots, the tiny layer: 38.6 -> 41.6 us; 352, Qwen-class
+// B = 32: 74.5 -> 89.1 us).
 constexpr int kSmallRouteMax = 64;
+constexpr int kStreamRouteMax = 64;
 
 // Where a kernel that routes in-kernel finds the call's routing and writes the
 // grouping (idx == nullptr: the grouping is already in the workspace).
@@ -31,61 +37,83 @@ struct RoutePlan {
   int32_t *done = nullptr;         // a counter later launches of the call use, zeroed here
 };
 
+template <int CAP>
 struct SmallRoute {
-  int32_t perm[kSmallRouteMax];    // sorted slot -> flat assignment t * kk + j
-  int32_t inv[kSmallRouteMax];     // flat assignment -> sorted slot
-  int32_t act_e[kSmallRouteMax];   // active experts, ascending
-  int32_t act_p0[kSmallRouteMax];  // their first slot
-  int32_t act_n[kSmallRouteMax];   // their slot count
+  static constexpr int kCap = CAP;
+  int32_t perm[CAP];               // sorted slot -> flat assignment t * kk + j
+  int32_t inv[CAP];                // flat assignment -> sorted slot
+  int32_t act_e[CAP];              // active experts, ascending
+  int32_t act_p0[CAP];             // their first slot
+  int32_t act_n[CAP];              // their slot count
   int32_t n_act;
   int32_t bad;                     // an expert id outside [0, E)
 };
 
-// Warp 0 of the calling CTA runs this (all 32 lanes); the result is in `r`
-// after the caller's next __syncthreads.  `key` is kSmallRouteMax ints of
-// shared scratch.  idx is [T, k]; slot j >= k of a token is the shared expert.
+// Every thread of the calling CTA runs this (blockDim.x >= 64, a multiple of
+// 32; __syncthreads inside); the result is in `r` when it returns.  `key` is
+// kSmallRouteMax ints of shared scratch.  idx is [T, k]; slot j >= k of a
+// token is the shared expert.  Each thread ranks its assignments against all
+// S keys (the stable order of (expert, assignment)), then warp 0 numbers the
+// experts' first slots.  S <= CAP.
+template <int CAP>
 __device__ __forceinline__ void small_route(const int32_t *__restrict__ idx, int T, int k, int shared_expert, int E,
-                                            SmallRoute &r, int32_t *key) {
-  const int lane = threadIdx.x & 31;
+                                            SmallRoute<CAP> &r, int32_t *key) {
+  __shared__ int bad_any;
+  __shared__ uint8_t first[CAP];
   const int kk = k + (shared_expert >= 0 ? 1 : 0);
   const int S = T * kk;
-  int bad = 0;
-  for (int a = lane; a < S; a += 32) {
+  if (threadIdx.x == 0) bad_any = 0;
+  __syncthreads();
+  for (int a = threadIdx.x; a < S; a += blockDim.x) {
     const int t = a / kk, j = a - t * kk;
     const int e = j < k ? idx[t * k + j] : shared_expert;
-    if (e < 0 || e >= E) bad = 1;
-    key[a] = (e < 0 || e >= E ? 0 : e) * kSmallRouteMax + a;   // unique; orders by (expert, assignment)
+    if (e < 0 || e >= E) bad_any = 1;
+    key[a] = (e < 0 || e >= E ? 0 : e) * CAP + a;   // unique; orders by (expert, assignment)
   }
-  bad = __any_sync(0xffffffffu, bad);
-  __syncwarp();
-  for (int a = lane; a < S; a += 32) {
+  __syncthreads();
+  for (int a = threadIdx.x; a < S; a += blockDim.x) {
     const int ka = key[a];
     int rank = 0;
     for (int b = 0; b < S; ++b) rank += key[b] < ka ? 1 : 0;
     r.perm[rank] = a;
     r.inv[a] = rank;
   }
-  __syncwarp();
-  // first slot of each expert: a run start in the sorted keys
-  int n_act = 0;
-  for (int s0 = 0; s0 < S; s0 += 32) {
-    const int s = s0 + lane;
-    const int e = s < S ? key[r.perm[s]] / kSmallRouteMax : -1;
-    const int e_prev = (s < S && s > 0) ? key[r.perm[s - 1]] / kSmallRouteMax : -2;
-    const unsigned first = __ballot_sync(0xffffffffu, s < S && e != e_prev);
-    if (s < S && e != e_prev) {
-      const int ai = n_act + __popc(first & ((1u << lane) - 1u));
-      r.act_e[ai] = e;
-      r.act_p0[ai] = s;
+  __syncthreads();
+  // run starts in the sorted keys: the first slot of each expert
+  for (int sl = threadIdx.x; sl < S; sl += blockDim.x)
+    first[sl] = (sl == 0 || key[r.perm[sl]] / CAP != key[r.perm[sl - 1]] / CAP) ? 1 : 0;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    constexpr int kPer = CAP / 32;                     // slots per lane, in order
+    int cnt = 0;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) cnt += (lane * kPer + u < S) ? first[lane * kPer + u] : 0;
+    int incl = cnt;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += o;
     }
-    n_act += __popc(first);
+    const int n_act = __shfl_sync(0xffffffffu, incl, 31);
+    int ai = incl - cnt;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+      const int sl = lane * kPer + u;
+      if (sl < S && first[sl]) {
+        r.act_e[ai] = key[r.perm[sl]] / CAP;
+        r.act_p0[ai] = sl;
+        ++ai;
+      }
+    }
+    __syncwarp();
+    for (int q = lane; q < n_act; q += 32) r.act_n[q] = (q + 1 < n_act ? r.act_p0[q + 1] : S) - r.act_p0[q];
+    if (lane == 0) {
+      r.n_act = bad_any ? 0 : n_act;
+      r.bad = bad_any;
+    }
   }
-  __syncwarp();
-  for (int ai = lane; ai < n_act; ai += 32) r.act_n[ai] = (ai + 1 < n_act ? r.act_p0[ai + 1] : S) - r.act_p0[ai];
-  if (lane == 0) {
-    r.n_act = bad ? 0 : n_act;
-    r.bad = bad;
-  }
+  __syncthreads();
 }
 
 // CTA 0 writes the grouping where k_permute would have: offsets [E + 1]
@@ -94,8 +122,9 @@ __device__ __forceinline__ void small_route(const int32_t *__restrict__ idx, int
 // counters[3] = 0 (the tensor kernels' error word), *done = 0 (a counter the
 // call's later launches use), and with tiles the tensor-core work list and
 // counters[2].  All threads of the CTA call it after the __syncthreads that
-// follows small_route.
-__device__ __forceinline__ void publish_route(const SmallRoute &r, int T, int k, int shared_expert, int E,
+// ends small_route.
+template <int CAP>
+__device__ __forceinline__ void publish_route(const SmallRoute<CAP> &r, int T, int k, int shared_expert, int E,
                                               int32_t *offsets, int32_t *perm, int32_t *inv, int32_t *active,
                                               int32_t *counters, int4 *tiles, int tile_n, int32_t *done) {
   const int kk = k + (shared_expert >= 0 ? 1 : 0);
