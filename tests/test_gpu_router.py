@@ -170,6 +170,39 @@ def test_wide_router_exact_ties_choose_lower_index(dev):
         assert got[1].tolist() == [list(range(12))] * 2
 
 
+@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SOFTMAX_BF16, R.SCORE_SIGMOID])
+@pytest.mark.parametrize("E,k", [(700, 20), (513, 10), (1024, 32), (257, 8)])
+def test_wide_router_cross_warp_ties(dev, fn, E, k):
+    # gate rows drawn from 6 distinct rows: equal logits spread over every warp of the CTA, so the
+    # per-warp winners tie with each other and the merge alone decides by expert id
+    rng = np.random.default_rng(E + k + fn)
+    base = (rng.normal(0, 1, (6, 512)) / np.sqrt(512)).astype(np.float32)
+    wb = F.f32_to_bf16_bits(base[rng.integers(0, 6, E)])
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (3, 512)).astype(np.float32))
+    ref = R.route(xb, wb, k, fn, norm_eps=1e-20)
+    _check(_run(dev, xb, wb, k, fn, eps=1e-20), ref)
+
+
+@pytest.mark.parametrize("fn", [R.SCORE_SIGMOID, R.SCORE_SQRTSOFTPLUS, R.SCORE_NONE])
+@pytest.mark.parametrize("E", [100, 513])
+def test_router_nan_and_inf_logits(dev, fn, E):
+    # token 0 holds +inf: its logits are +-inf where the gate column is nonzero and NaN where it is zero;
+    # NaN keys sort as -inf (lowest id first among them), on the warp and on the CTA kernel
+    rng = np.random.default_rng(E + fn)
+    x = rng.normal(0, 1, (2, 256)).astype(np.float32)
+    x[0, 5] = np.inf
+    w = (rng.normal(0, 1, (E, 256)) / 16).astype(np.float32)
+    w[::3, 5] = 0.0
+    xb, wb = F.f32_to_bf16_bits(x), F.f32_to_bf16_bits(w)
+    eps = -1.0 if fn == R.SCORE_NONE else 1e-20
+    lg, idx, wt, _ = _run(dev, xb, wb, 6, fn, eps=eps)
+    rl, ri, rw, _ = R.route(xb, wb, 6, fn, norm_eps=eps)
+    assert np.isnan(rl[0]).any() and np.isinf(rl[0]).any()
+    np.testing.assert_array_equal(lg, rl)           # NaN-aware: NaN payloads may differ host to device
+    np.testing.assert_array_equal(idx, ri)
+    np.testing.assert_array_equal(wt, rw)
+
+
 @pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SOFTMAX_BF16, R.SCORE_SQRTSOFTPLUS])
 @pytest.mark.parametrize("shape", [(65, 2048, 513, 10), (200, 264, 40, 4), (1000, 4096, 256, 8), (77, 1032, 129, 6)])
 def test_many_token_short_row_logits_vs_oracle(dev, fn, shape):

@@ -28,6 +28,7 @@
 
 #include "wm_common.cuh"
 #include "wm_detmath.cuh"
+#include "wm_topk.cuh"
 
 namespace {
 
@@ -548,14 +549,10 @@ __global__ void __launch_bounds__(128) k_router_topk(const float *__restrict__ l
     shared_w[t] = bf ? round_bf16(wm_sigmoid(round_bf16(shared_w[t]))) : wm_sigmoid(shared_w[t]);
 }
 
-// Wide routers (E > 128): one 256-thread CTA per token, so no single warp
-// walks hundreds of experts alone.  Thread (w, l) holds experts l + 32 (w + 8 i)
-// for i < PERT.  The scores follow k_router_topk's arithmetic exactly: the
-// softmax sum keeps its order (warp 0 lane l adds experts l, l + 32, l + 64,
-// ... from shared memory in that order, then the same butterfly), and the
-// selection its rule (descending key, ties to the lower expert id): each warp
-// takes its own top k in k rounds, then warp 0 takes the top k of the 8 lists
-// (every expert of the overall top k is in its warp's top k).
+// Wide routers (E > 128): one 256-thread CTA per token (wm::cta_topk_row:
+// per-warp winners, then each candidate's place by counting the candidates
+// ahead of it), so no single warp walks hundreds of experts in k serial
+// rounds.  Same arithmetic and order as k_router_topk.
 template <int PERT>
 __global__ void __launch_bounds__(256) k_router_topk_cta(const float *__restrict__ logits,
                                                          const float *__restrict__ select_bias, int T, int E, int k,
@@ -563,149 +560,21 @@ __global__ void __launch_bounds__(256) k_router_topk_cta(const float *__restrict
                                                          int32_t *__restrict__ idx, float *__restrict__ weights,
                                                          float *__restrict__ shared_w) {
   constexpr int kWarpsCta = 8;
-  __shared__ float s_sc[kWarpsCta * 32 * PERT];          // scores by expert id
-  __shared__ float s_red[kWarpsCta];
-  __shared__ uint32_t c_key[kWarpsCta][kMaxK];            // per-warp top-k lists
-  __shared__ int32_t c_id[kWarpsCta][kMaxK];
+  __shared__ wm::TopkScratch<kWarpsCta> s;
   WM_PDL_WAIT();
   WM_PDL_LAUNCH();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int t = blockIdx.x;
   if (t >= T) return;
-  const float kNegInf = -__int_as_float(0x7f800000);
-  const float *lt = logits + static_cast<int64_t>(t) * E;
-  const bool bf = score_fn == WM_SCORE_SOFTMAX_BF16;
-  float sc[PERT];
-#pragma unroll
-  for (int i = 0; i < PERT; ++i) {
-    const int e = lane + 32 * (warp + kWarpsCta * i);
-    sc[i] = e < E ? (bf ? round_bf16(lt[e]) : lt[e]) : kNegInf;
-  }
-  if (score_fn == WM_SCORE_SOFTMAX || bf) {
-    float mx = kNegInf;
-#pragma unroll
-    for (int i = 0; i < PERT; ++i) mx = fmaxf(mx, sc[i]);
-#pragma unroll
-    for (int m = 16; m >= 1; m >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, m));
-    if (lane == 0) s_red[warp] = mx;
-    __syncthreads();
-    mx = s_red[0];
-#pragma unroll
-    for (int w = 1; w < kWarpsCta; ++w) mx = fmaxf(mx, s_red[w]);
-#pragma unroll
-    for (int i = 0; i < PERT; ++i) {
-      const int e = lane + 32 * (warp + kWarpsCta * i);
-      if (e < E) {
-        sc[i] = wm_exp(sc[i] - mx);
-        s_sc[e] = sc[i];
-      }
-    }
-    __syncthreads();                                      // s_red read by all before warp 0 rewrites it
-    if (warp == 0) {
-      float part = 0.0f;
-      for (int e = lane; e < E; e += 32) part = part + s_sc[e];   // experts l, l+32, ... in order
-#pragma unroll
-      for (int m = 16; m >= 1; m >>= 1) part = part + __shfl_xor_sync(0xffffffffu, part, m);
-      if (lane == 0) s_red[0] = part;
-    }
-    __syncthreads();
-    const float part = s_red[0];
-#pragma unroll
-    for (int i = 0; i < PERT; ++i) sc[i] = bf ? round_bf16(__fdiv_rn(sc[i], part)) : __fdiv_rn(sc[i], part);
-  } else if (score_fn == WM_SCORE_SIGMOID) {
-#pragma unroll
-    for (int i = 0; i < PERT; ++i) sc[i] = wm_sigmoid(sc[i]);
-  } else if (score_fn == WM_SCORE_SQRTSOFTPLUS) {
-#pragma unroll
-    for (int i = 0; i < PERT; ++i) sc[i] = __fsqrt_rn(wm_softplus(sc[i]));
-  }
-  // order-preserving key bits (-0 folded into +0, NaN keys last), as k_router_topk
-  uint32_t kb[PERT];
-#pragma unroll
-  for (int i = 0; i < PERT; ++i) {
-    const int e = lane + 32 * (warp + kWarpsCta * i);
-    float kv = kNegInf;
-    if (e < E) {
-      kv = select_bias ? sc[i] + select_bias[e] : sc[i];
-      s_sc[e] = sc[i];                                     // scores by id, for the weights below
-    }
-    kv = (kv != kv) ? kNegInf : kv;
-    const uint32_t b = __float_as_uint(kv == 0.0f ? 0.0f : kv);
-    kb[i] = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  }
-  // this warp's top k: k rounds of (lane best untaken, then warp max key, then lowest id holding it)
-  const int warp_e = min(E - 32 * warp, 32) > 0 ? 1 : 0;  // the warp holds at least one expert
-  uint32_t taken = 0u;
-  for (int r = 0; r < k; ++r) {
-    uint32_t best = 0u;
-    int bi = -1;
-#pragma unroll
-    for (int i = 0; i < PERT; ++i) {
-      const int e = lane + 32 * (warp + kWarpsCta * i);
-      if (e < E && !((taken >> i) & 1u) && (bi < 0 || kb[i] > best)) {
-        best = kb[i];
-        bi = i;
-      }
-    }
-    const uint32_t wbest = __reduce_max_sync(0xffffffffu, bi < 0 ? 0u : best);
-    const int cand = (bi >= 0 && best == wbest) ? lane + 32 * (warp + kWarpsCta * bi) : 0x7fffffff;
-    const int be = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
-    if (be != 0x7fffffff && lane == (be & 31)) taken |= 1u << ((be >> 5) / kWarpsCta);
-    if (lane == 0) {
-      c_key[warp][r] = be != 0x7fffffff ? wbest : 0u;
-      c_id[warp][r] = be;                                  // 0x7fffffff: this warp ran out of experts
-    }
-  }
-  (void)warp_e;
-  __syncthreads();
-  if (warp != 0) return;
-  // merge: candidate c = w * k + r is held by lane c % 32 (at most 8 per lane)
-  constexpr int kCand = (kWarpsCta * kMaxK + 31) / 32;
-  uint32_t ck[kCand];
-  int32_t ci[kCand];
-#pragma unroll
-  for (int u = 0; u < kCand; ++u) {
-    const int c = lane + 32 * u;
-    const bool live = c < kWarpsCta * k && c_id[c / k][c % k] != 0x7fffffff;
-    ck[u] = live ? c_key[c / k][c % k] : 0u;
-    ci[u] = live ? c_id[c / k][c % k] : 0x7fffffff;
-  }
-  uint32_t mtaken = 0u;
-  float my_w = 0.0f;
-  int32_t my_i = 0;
-  for (int r = 0; r < k; ++r) {
-    uint32_t best = 0u;
-    int bu = -1;
-#pragma unroll
-    for (int u = 0; u < kCand; ++u) {
-      if (ci[u] != 0x7fffffff && !((mtaken >> u) & 1u) &&
-          (bu < 0 || ck[u] > best || (ck[u] == best && ci[u] < ci[bu])))
-        { best = ck[u]; bu = u; }
-    }
-    const uint32_t wbest = __reduce_max_sync(0xffffffffu, bu < 0 ? 0u : best);
-    const int cand = (bu >= 0 && best == wbest) ? ci[bu] : 0x7fffffff;
-    const int be = static_cast<int>(__reduce_min_sync(0xffffffffu, static_cast<uint32_t>(cand)));
-#pragma unroll
-    for (int u = 0; u < kCand; ++u)
-      if (ci[u] == be) mtaken |= 1u << u;
-    if (lane == r) { my_i = be; my_w = s_sc[be]; }
-  }
-  const bool norm = norm_eps >= 0.0f;
   float denom = 1.0f;
-  if (norm) {
-    float sum = 0.0f;
-    for (int r = 0; r < k; ++r) sum = sum + __shfl_sync(0xffffffffu, my_w, r);
-    denom = sum + norm_eps;
-    if (bf) denom = round_bf16(denom);
+  wm::cta_topk_row<kWarpsCta, PERT>(logits + static_cast<int64_t>(t) * E, select_bias, E, k, score_fn, norm_eps, s,
+                                    &denom);
+  const bool bf = score_fn == WM_SCORE_SOFTMAX_BF16;
+  const int r = threadIdx.x;
+  if (r < k) {
+    idx[static_cast<int64_t>(t) * k + r] = s.sel_id[r];
+    weights[static_cast<int64_t>(t) * k + r] = wm::topk_weight(s.sel_w[r], denom, norm_eps >= 0.0f, bf, route_scale);
   }
-  if (lane < k) {
-    float w = norm ? __fdiv_rn(my_w, denom) : my_w;
-    if (bf) w = round_bf16(w);
-    idx[static_cast<int64_t>(t) * k + lane] = my_i;
-    weights[static_cast<int64_t>(t) * k + lane] = w * route_scale;
-  }
-  if (lane == 0 && shared_w)
-    shared_w[t] = bf ? round_bf16(wm_sigmoid(round_bf16(shared_w[t]))) : wm_sigmoid(shared_w[t]);
+  if (r == 0 && shared_w) shared_w[t] = wm::topk_shared_gate(shared_w[t], bf);
 }
 
 int launch_router_topk(const float *logits, const float *select_bias, int T, int E, int k, int score_fn,
