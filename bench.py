@@ -292,7 +292,9 @@ def _layer_launches(name, cfg, T):
     for one- and two-token calls on experts with H <= 4096 and I <= 1024, else
     the token split and the two tcgen05 projections (plus the SwiGLU split in
     the prefill configuration), and the combine unless the call has at most
-    64 slots and 4096 output values (the down projection's last CTA combines).
+    64 slots and either takes the weight stream (each CTA of its down
+    projection combines its own output rows) or has at most 4096 output values
+    (the down projection's last CTA combines).
     Affine-4 (tiny): permute (unless at most 64 slots), f16 gather, two
     tcgen05 projections, combine."""
     if name == "tiny":
@@ -303,7 +305,7 @@ def _layer_launches(name, cfg, T):
     n_routed = cfg["E"]
     stream = T <= 2 and H <= 4096 and I <= 1024
     small = S <= 64
-    n = 2 + (0 if small else 1) + (0 if small and T * H <= 4096 else 1)
+    n = 2 + (0 if small else 1) + (0 if small and (stream or T * H <= 4096) else 1)
     if stream:
         n += 2
     else:

@@ -153,3 +153,22 @@ def test_stream_and_tensor_core_paths_agree(dev, monkeypatch):
     out4 = W.experts_forward(x4, idx4, ex, weights=w4, shared_expert=E, swiglu_limit=10.0)
     ref4 = M.moe_forward(_f32(x4), ri4, rw4, _oracle(ex, M.UP_GATE, 10.0), shared_expert=E)
     assert M.max_rel_err(_f32(out4), ref4) < TOL
+
+
+@pytest.mark.parametrize("T,H,I,E,k", [(1, 2048, 512, 40, 10), (2, 4096, 1024, 20, 8), (2, 1024, 256, 12, 4),
+                                       (1, 256, 256, 6, 3)])
+def test_stream_row_split_combine_equals_combine_launch(dev, monkeypatch, T, H, I, E, k):
+    # small calls: the down projection splits the output rows over its CTAs, groups the call before its
+    # dependency wait and combines its own rows; the same bits as the grouping launch, the row-chunk
+    # split by expert and the separate combine launch (WM_FUSE=0), with a shared-expert weight
+    ex = S.make_mxfp4_experts(E + 1, H, I, seed=T * 7 + H, device=dev)
+    x = S.make_tokens(T, H, T + H, dev)
+    ri, rw, idx, w = _route(T, k, E, T + E + H, dev)
+    sw = torch.rand(T, 1, device=dev) + 0.25
+    fused = W.experts_forward(x, idx, ex, weights=w, shared_expert=E, shared_w=sw, swiglu_limit=10.0)
+    monkeypatch.setenv("WM_FUSE", "0")
+    sep = W.experts_forward(x, idx, ex, weights=w, shared_expert=E, shared_w=sw, swiglu_limit=10.0)
+    assert torch.equal(fused, sep)
+    ref = M.moe_forward(_f32(x), ri, rw, _oracle(ex, M.UP_GATE, 10.0), shared_expert=E,
+                         shared_weight=_f32(sw).reshape(-1))
+    assert M.max_rel_err(_f32(fused), ref) < TOL

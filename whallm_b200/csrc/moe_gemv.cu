@@ -405,12 +405,14 @@ int run(const Args &a, int fmt) {
   const bool fuse = !(fuse_env && fuse_env[0] == '0');
   const bool small = fuse && a.rf.count == 0 && (stream || mx || tc) &&
                      S <= (stream ? wm::kStreamRouteMax : wm::kSmallRouteMax);
-  // one CTA combines the rows in about one pass over its threads (T * H / 8 output groups)
-  const bool fuse_combine = small && (stream || mx) && a.reduce && a.T * a.H <= 4096;
+  // one CTA combines the rows in about one pass over its threads (T * H / 8 output groups); the weight
+  // stream's down projection splits the output rows over its CTAs and each combines its own
+  const bool stream_rows = small && stream && a.reduce && wm::stream_row_split(S, a.H, a.I);
+  const bool fuse_combine = stream_rows || (small && (stream || mx) && a.reduce && a.T * a.H <= 4096);
   const wm::CombineArgs comb{ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk, a.H,
                              a.out_f32 ? static_cast<void *>(a.out_f32) : static_cast<void *>(a.out),
                              a.out_f32 != nullptr};
-  int32_t *done = fuse_combine ? ws.counters + 4 : nullptr;
+  int32_t *done = fuse_combine && !stream_rows ? ws.counters + 4 : nullptr;
   if (small) {
     plan.idx = a.idx; plan.T = a.T; plan.k = a.k; plan.shared_expert = a.shared_expert; plan.E = a.E;
     plan.offsets = ws.offsets; plan.perm = ws.perm; plan.inv = ws.inv; plan.active = ws.active;
@@ -426,7 +428,7 @@ int run(const Args &a, int fmt) {
                                       ws.active, ws.counters, ws.h, a.stream, plan))
       return rc;
     if (int rc = wm::launch_stream_down(a.w2.w, a.w2.s, S, a.H, a.I, ws.h, ws.offsets, ws.active, ws.counters, ws.y,
-                                        a.stream, &comb, done))
+                                        a.stream, &comb, done, stream_rows ? &plan : nullptr))
       return rc;
   } else if (mx) {
     const int32_t *count = ws.offsets + a.E;

@@ -77,6 +77,8 @@ struct StreamParams {
   wm::CombineArgs comb;      // down projection: with `done` set, the last CTA combines the rows
   int32_t *done;
   uint16_t *out;             // up: h [S, I]; down: y [S, H] (bf16, slot order)
+  int row_chunks;            // MODE 2: 8-row chunks of every active expert per CTA
+  int y_offset;              // MODE 2: shared-memory offset of the CTA's y rows [S][row_chunks * 8] (bf16)
 };
 
 __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
@@ -162,7 +164,8 @@ __device__ __forceinline__ float warp_sums(float (&v)[V], int lane) {
   return s;
 }
 
-constexpr int kMaxCtaExperts = 32;   // experts one CTA's chunk range can span: at most E / grid + 2
+constexpr int kMaxCtaExperts = 32;
+constexpr int kRowChunksMax = 8;     // MODE 2: 8-row chunks per CTA (H <= 9472 on 148 SMs)   // experts one CTA's chunk range can span: at most E / grid + 2
 
 template <int MODE, int PB>
 __device__ __forceinline__ void stream_body(const StreamParams &p) {
@@ -170,42 +173,80 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   __shared__ int m_e[kMaxCtaExperts], m_p0[kMaxCtaExperts], m_n[kMaxCtaExperts];
   __shared__ wm::SmallRoute<wm::kStreamRouteMax> route;
   __shared__ int32_t route_key[wm::kStreamRouteMax];
+  __shared__ float comb_w[wm::kStreamRouteMax];   // MODE 2: the weight of flat assignment t * kk + j
   constexpr int VPP = 2 * PB;                 // values per piece
-  WM_PDL_WAIT();
-  WM_PDL_LAUNCH();
-  // up projection of a small call: group the assignments here (every CTA), CTA 0 writes the grouping
-  const bool in_kernel = MODE == 0 && p.plan.idx != nullptr;
+  // MODE 2 reads only what was complete before the previous launch started (the routing, the weights)
+  // until its copies are in flight, then waits for that launch (the up projection's h)
+  if (MODE != 2) {
+    WM_PDL_WAIT();
+    WM_PDL_LAUNCH();
+  }
+  const int K = p.K, G = K / 32;
+  // up projection: this thread's first 32-value group of the token rows is loaded now, so that its latency
+  // overlaps the grouping below (the rows do not depend on it)
+  uint4 pre[4];
+  if (MODE == 0 && static_cast<int>(threadIdx.x) < p.stage_rows * G) {
+    const uint4 *s = reinterpret_cast<const uint4 *>(p.src + static_cast<int64_t>(threadIdx.x / G) * K +
+                                                     (threadIdx.x % G) * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pre[i] = __ldcg(s + i);
+  }
+  if (MODE == 2)                              // the combine's weights (inputs of the call, complete before it)
+    for (int a = threadIdx.x; a < p.comb.T * p.comb.kk; a += kThreads) {
+      const int t = a / p.comb.kk, j = a - t * p.comb.kk;
+      comb_w[a] = j < p.comb.k ? p.comb.w[static_cast<int64_t>(t) * p.comb.k + j]
+                               : (p.comb.shared_w ? p.comb.shared_w[t] : 1.0f);
+    }
+  // small calls: group the assignments here (every CTA); in the up projection CTA 0 writes the grouping
+  const bool in_kernel = (MODE == 0 || MODE == 2) && p.plan.idx != nullptr;
   int n_active;
   if (in_kernel) {
     wm::small_route(p.plan.idx, p.plan.T, p.plan.k, p.plan.shared_expert, p.plan.E, route, route_key);
-    if (blockIdx.x == 0)
+    if (MODE == 0 && blockIdx.x == 0)
       wm::publish_route(route, p.plan.T, p.plan.k, p.plan.shared_expert, p.plan.E, p.plan.offsets, p.plan.perm,
                         p.plan.inv, p.plan.active, p.plan.counters, nullptr, 0, p.plan.done);
-    if (route.bad) return;                    // bad expert id: the combine writes zeros
-    n_active = route.n_act;
+    if (MODE == 0 && route.bad) return;       // bad expert id: the combine writes zeros
+    n_active = route.bad ? 0 : route.n_act;
   } else {
     if (p.counters[1] != 0) return;
     n_active = p.counters[0];
   }
   const int cpe = p.rows / kRows;
-  const int64_t n_chunks = static_cast<int64_t>(n_active) * cpe;
-  const int64_t c0 = n_chunks * blockIdx.x / gridDim.x, c1 = n_chunks * (blockIdx.x + 1) / gridDim.x;
-  if (c0 >= c1) return;
-  const int K = p.K, G = K / 32;
-  const int a_first = static_cast<int>(c0 / cpe), a_last = static_cast<int>((c1 - 1) / cpe);
+  // the CTA's chunks: MODE 0 / 1 a contiguous share of all (expert, row chunk) pairs; MODE 2 the row chunks
+  // [mb, mb + lc) of every active expert, so the CTA holds every slot's rows there and combines them itself
+  int64_t c0, c1;
+  int lc = cpe, mb = 0;
+  if (MODE == 2) {
+    mb = blockIdx.x * p.row_chunks;
+    lc = max(0, min(p.row_chunks, cpe - mb));
+    c0 = 0;
+    c1 = static_cast<int64_t>(n_active) * lc;
+  } else {
+    const int64_t n_chunks = static_cast<int64_t>(n_active) * cpe;
+    c0 = n_chunks * blockIdx.x / gridDim.x;
+    c1 = n_chunks * (blockIdx.x + 1) / gridDim.x;
+    if (c0 >= c1) return;
+  }
+  const int a_first = MODE == 2 ? 0 : static_cast<int>(c0 / cpe);
+  const int a_last = MODE == 2 ? n_active - 1 : static_cast<int>((c1 - 1) / cpe);
 
-  // ------------------------------ the CTA's experts, operand rows -> f16
-  if (!in_kernel)
+  // ------------------------------ the CTA's experts
+  if (!in_kernel) {
     for (int i = threadIdx.x; i <= a_last - a_first && i < kMaxCtaExperts; i += kThreads) {
       const int e = p.active[a_first + i];
       const int o = p.offsets[e];
       m_e[i] = e; m_p0[i] = o; m_n[i] = p.offsets[e + 1] - o;
     }
-  const int p_lo = in_kernel ? route.act_p0[a_first] : p.offsets[p.active[a_first]];
-  const int p_hi = in_kernel ? route.act_p0[a_last] + route.act_n[a_last] : p.offsets[p.active[a_last] + 1];
+    __syncthreads();                          // the warps' copies below read them
+  }
+  int p_lo = 0, p_hi = 0;
+  if (MODE != 2) {
+    p_lo = in_kernel ? route.act_p0[a_first] : p.offsets[p.active[a_first]];
+    p_hi = in_kernel ? route.act_p0[a_last] + route.act_n[a_last] : p.offsets[p.active[a_last] + 1];
+  }
   int base_row = 0, n_rows;
-  if (MODE == 0) {
-    n_rows = p.stage_rows;                    // every token of the call
+  if (MODE != 1) {
+    n_rows = p.stage_rows;                    // every token (up) or every slot (MODE 2) of the call
   } else {
     base_row = p_lo;                          // the slots of the CTA's experts
     n_rows = p_hi - p_lo;
@@ -213,6 +254,11 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   uint16_t *xs = reinterpret_cast<uint16_t *>(smem);                                        // [n_rows][K]
   float *xk = reinterpret_cast<float *>(smem + static_cast<size_t>(p.stage_rows) * K * 2);  // [n_rows][G]
   int *tok = reinterpret_cast<int *>(xk + static_cast<size_t>(p.stage_rows) * G);           // up: slot -> token
+  const int rows_cta = p.row_chunks * kRows;
+  uint16_t *ysm = reinterpret_cast<uint16_t *>(smem + p.y_offset);                            // MODE 2: [S][rows_cta]
+  // operand rows -> f16 with a power-of-two scale per 32 values (all threads; run after the first weight
+  // copies are issued, so the two latencies overlap)
+  auto stage_operands = [&]() {
   if (MODE == 0)
     for (int i = threadIdx.x; i < p_hi - p_lo; i += kThreads)
       tok[i] = (in_kernel ? route.perm[p_lo + i] : p.perm[p_lo + i]) / p.kk;
@@ -221,7 +267,7 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
     const uint4 *s = reinterpret_cast<const uint4 *>(p.src + static_cast<int64_t>(base_row + r) * K + q * 32);
     uint4 v[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) v[i] = __ldcg(s + i);
+    for (int i = 0; i < 4; ++i) v[i] = (MODE == 0 && g == static_cast<int>(threadIdx.x)) ? pre[i] : __ldcg(s + i);
     uint32_t mx = 0u;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -246,7 +292,7 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
     }
     xk[r * G + q] = mx == 0u ? 0.0f : pow2f(k);
   }
-  __syncthreads();
+  };
 
   // ------------------------------------------------------------ stream
   // Each warp walks its chunks as one stream of (chunk, pass, step) with the
@@ -254,7 +300,7 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t nc = c1 - c0;
   const int64_t w0 = c0 + nc * warp / kWarps, w1 = c0 + nc * (warp + 1) / kWarps;
-  if (w0 >= w1) return;
+  const bool has_work = w0 < w1;
   const int pieces = K / VPP;
   const int steps = (pieces + 31) / 32;
   const int64_t row_bytes = K / 2;
@@ -282,7 +328,7 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
     int n;            // slots of the expert
   };
   auto start = [&](Cursor &u) {
-    u.c = w0; u.a = static_cast<int>(w0 / cpe); u.m = static_cast<int>(w0 - static_cast<int64_t>(u.a) * cpe);
+    u.c = w0; u.a = static_cast<int>(w0 / lc); u.m = mb + static_cast<int>(w0 - static_cast<int64_t>(u.a) * lc);
     u.t0 = 0; u.s = 0;
     int e, p0;
     meta(u.a, e, p0, u.n);
@@ -294,8 +340,8 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
     if (u.t0 < u.n) return;
     u.t0 = 0;
     ++u.c;
-    if (++u.m == cpe) {
-      u.m = 0;
+    if (++u.m == mb + lc) {
+      u.m = mb;
       ++u.a;
     }
     if (u.c < w1) {
@@ -309,8 +355,8 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   constexpr int kGps = 2 * PB;                // scale groups per step
   uint8_t *ring = smem + p.ring_offset + static_cast<size_t>(warp) * RG::kWarpBytes;
   const uint32_t ring_s = static_cast<uint32_t>(__cvta_generic_to_shared(ring));
-  Cursor L;
-  start(L);
+  Cursor L{};
+  if (has_work) start(L);
   const uint8_t *wb0 = nullptr, *wb1 = nullptr, *sb0 = nullptr, *sb1 = nullptr;
   int64_t l_chunk = -1;
   auto issue = [&](int slot) {
@@ -348,8 +394,8 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   };
 
   // ---- arithmetic (cursor C) and the per-pass epilogue
-  Cursor C;
-  start(C);
+  Cursor C{};
+  if (has_work) start(C);
   int c_p0 = 0, nt = 1;
   int xr[kNT];
   float acc[kRows][kNT];
@@ -449,6 +495,8 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
         const float silu = gate / (1.0f + expf(-gate));
         p.out[slot * p.I + (kRows / 2) * C.m + (r >> 1)] = wm_f32_to_bf16(silu * up);
       }
+    } else if (MODE == 2) {
+      if (writer) ysm[slot * rows_cta + kRows * (C.m - mb) + r] = wm_f32_to_bf16(sum);
     } else if (writer) {
       p.out[slot * p.rows + kRows * C.m + r] = wm_f32_to_bf16(sum);
     }
@@ -467,19 +515,79 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
     return true;
   };
 
-  for (int i = 0; i < kDepth - 1; ++i) issue(i);
-  begin_pass();
-  for (int use = 0, fill = kDepth - 1;;) {
-    issue(fill);                              // the slot the previous step used
-    cp_async_wait<kDepth - 1>();              // this lane's copies of this step have landed
-    __syncwarp();                             // and every lane's (the scale bytes)
-    const bool more = step(use);
-    __syncwarp();                             // the slot is read before a later step refills it
-    if (!more) break;
-    fill = use;
-    use = use + 1 == kDepth ? 0 : use + 1;
+  if (has_work)
+    for (int i = 0; i < kDepth - 1; ++i) issue(i);
+  if (MODE == 2) {
+    WM_PDL_WAIT();                            // h of the up projection from here on
+    WM_PDL_LAUNCH();
   }
-  cp_async_wait<0>();
+  stage_operands();
+  __syncthreads();
+  if (MODE != 2 && !has_work) return;
+  if (has_work) {
+    begin_pass();
+    for (int use = 0, fill = kDepth - 1;;) {
+      issue(fill);                            // the slot the previous step used
+      cp_async_wait<kDepth - 1>();            // this lane's copies of this step have landed
+      __syncwarp();                           // and every lane's (the scale bytes)
+      const bool more = step(use);
+      __syncwarp();                           // the slot is read before a later step refills it
+      if (!more) break;
+      fill = use;
+      use = use + 1 == kDepth ? 0 : use + 1;
+    }
+    cp_async_wait<0>();
+  }
+  if constexpr (MODE == 2) {
+    // the combine of rows [8 mb, 8 (mb + lc)): out[t, h] = sum_j w[t, j] * y[slot(t, j), h] (+ the shared
+    // expert's row times its weight), f32 fmaf chain in assignment order j, rounded once -- the arithmetic
+    // of wm::combine_groups, on the CTA's own y rows
+    __syncthreads();
+    const wm::CombineArgs &a = p.comb;
+    const int S = a.T * a.kk;
+    const bool bad = route.bad != 0;
+    for (int i = threadIdx.x; i < a.T * lc; i += kThreads) {
+      const int t = i / lc, q = i - t * lc;   // rows 8 (mb + q) .. + 7 of token t
+      float acc[kRows] = {0, 0, 0, 0, 0, 0, 0, 0};
+      // eight assignments at a time: their slots, weights and rows loaded together, then the chain
+      for (int j0 = 0; j0 < a.kk && !bad; j0 += 8) {
+        int sl[8];
+        float wv[8];
+        uint4 y[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int j = j0 + u;
+          sl[u] = j < a.kk ? route.inv[t * a.kk + j] : -1;
+          wv[u] = j < a.kk ? comb_w[t * a.kk + j] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          y[u] = (sl[u] >= 0 && sl[u] < S) ? *reinterpret_cast<const uint4 *>(ysm + sl[u] * rows_cta + kRows * q)
+                                           : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (sl[u] < 0 || sl[u] >= S) continue;
+          acc[0] = fmaf(wv[u], wm_bf16lo(y[u].x), acc[0]); acc[1] = fmaf(wv[u], wm_bf16hi(y[u].x), acc[1]);
+          acc[2] = fmaf(wv[u], wm_bf16lo(y[u].y), acc[2]); acc[3] = fmaf(wv[u], wm_bf16hi(y[u].y), acc[3]);
+          acc[4] = fmaf(wv[u], wm_bf16lo(y[u].z), acc[4]); acc[5] = fmaf(wv[u], wm_bf16hi(y[u].z), acc[5]);
+          acc[6] = fmaf(wv[u], wm_bf16lo(y[u].w), acc[6]); acc[7] = fmaf(wv[u], wm_bf16hi(y[u].w), acc[7]);
+        }
+      }
+      const int64_t o = static_cast<int64_t>(t) * a.H + kRows * (mb + q);
+      if (a.f32_out) {
+        float4 *op = reinterpret_cast<float4 *>(static_cast<float *>(a.out) + o);
+        op[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        op[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+      } else {
+        uint4 ob;
+        ob.x = wm_f32_to_bf16(acc[0]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[1])) << 16);
+        ob.y = wm_f32_to_bf16(acc[2]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[3])) << 16);
+        ob.z = wm_f32_to_bf16(acc[4]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[5])) << 16);
+        ob.w = wm_f32_to_bf16(acc[6]) | (static_cast<uint32_t>(wm_f32_to_bf16(acc[7])) << 16);
+        *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(a.out) + o) = ob;
+      }
+    }
+  }
 }
 
 // The body may return early (CTAs or warps without chunks); the down
@@ -503,7 +611,7 @@ size_t launch_smem(size_t stage, int K, size_t *ring_offset) {
 }
 
 template <int MODE, int PB>
-cudaError_t launch_one(const StreamParams &p, size_t smem, cudaStream_t stream) {
+cudaError_t launch_one(const StreamParams &p, size_t smem, cudaStream_t stream, int grid = 0) {
   static bool attr_done = false;       // per template instance; the attribute is per function
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(k_expert_stream<MODE, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -511,7 +619,8 @@ cudaError_t launch_one(const StreamParams &p, size_t smem, cudaStream_t stream) 
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  return wm::launch_pdl(k_expert_stream<MODE, PB>, dim3(wm::sm_count()), dim3(kThreads), smem, stream, p);
+  return wm::launch_pdl(k_expert_stream<MODE, PB>, dim3(grid > 0 ? grid : wm::sm_count()), dim3(kThreads), smem,
+                        stream, p);
 }
 
 }  // namespace
@@ -523,6 +632,18 @@ bool stream_supported(int T, int k, int has_shared, int H, int I) {
   size_t o;
   return T >= 1 && H % 256 == 0 && I % 256 == 0 && launch_smem(stage_bytes(T, H, S), H, &o) <= kStreamSmemMax &&
          launch_smem(stage_bytes(S, I), I, &o) <= kStreamSmemMax;
+}
+
+int stream_row_chunks(int H) {
+  const int cpe = H / kRows, nsm = sm_count();
+  return (cpe + nsm - 1) / nsm;
+}
+
+bool stream_row_split(int S, int H, int I) {
+  size_t o;
+  const int rc = stream_row_chunks(H);
+  return S <= kStreamRouteMax && rc <= kRowChunksMax &&
+         launch_smem(stage_bytes(S, I), I, &o) + 16 + static_cast<size_t>(S) * rc * kRows * 2 <= kStreamSmemMax;
 }
 
 int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int H, int I, int order, float limit,
@@ -545,18 +666,34 @@ int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int 
 
 int launch_stream_down(const uint8_t *w2, const uint8_t *s2, int S, int H, int I, const uint16_t *h,
                        const int32_t *offsets, const int32_t *active, const int32_t *counters, uint16_t *y,
-                       cudaStream_t stream, const CombineArgs *comb, int32_t *done) {
+                       cudaStream_t stream, const CombineArgs *comb, int32_t *done, const RoutePlan *plan) {
   StreamParams p{};
-  if (comb && done) {
+  const bool rows = plan && plan->idx && comb;
+  if (rows) {
+    p.plan = *plan;
+    p.comb = *comb;
+  } else if (comb && done) {
     p.comb = *comb;
     p.done = done;
   }
   p.w = w2; p.sc = s2; p.src = h; p.offsets = offsets; p.active = active; p.counters = counters;
   p.kk = 1; p.K = I; p.rows = H; p.I = I; p.stage_rows = S; p.out = y;
   size_t ring_offset;
-  const size_t smem = launch_smem(stage_bytes(S, I), I, &ring_offset);
+  size_t smem = launch_smem(stage_bytes(S, I), I, &ring_offset);
   p.ring_offset = static_cast<int>(ring_offset);
-  cudaError_t e = I >= 1024 ? launch_one<1, 16>(p, smem, stream) : launch_one<1, 8>(p, smem, stream);
+  cudaError_t e;
+  if (rows) {
+    // row chunks per CTA: the fewest that cover H / 8 chunks with at most one CTA per SM
+    if (!stream_row_split(S, H, I)) return fail(WM_ERR_INVALID, "expert stream down: no row split for this shape");
+    const int cpe = H / kRows;
+    p.row_chunks = stream_row_chunks(H);
+    const int grid = (cpe + p.row_chunks - 1) / p.row_chunks;
+    p.y_offset = static_cast<int>((smem + 15) / 16 * 16);
+    smem = p.y_offset + static_cast<size_t>(S) * p.row_chunks * kRows * 2;
+    e = I >= 1024 ? launch_one<2, 16>(p, smem, stream, grid) : launch_one<2, 8>(p, smem, stream, grid);
+  } else {
+    e = I >= 1024 ? launch_one<1, 16>(p, smem, stream) : launch_one<1, 8>(p, smem, stream);
+  }
   if (e != cudaSuccess) return fail(WM_ERR_CUDA, std::string("expert stream down: ") + cudaGetErrorString(e));
   return check_launch("expert stream down");
 }

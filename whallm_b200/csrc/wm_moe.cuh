@@ -49,14 +49,19 @@ constexpr int kStreamMaxTokens = 2;               // calls of at most this many 
 constexpr int kStreamMaxH = 4096, kStreamMaxI = 1024;   // ... when the experts are this small (Qwen-class)
 // H and I multiples of 256, and the staged rows (T tokens of H, S slots of I) fit in shared memory
 bool stream_supported(int T, int k, int has_shared, int H, int I);
+// the down projection can split the output rows over its CTAs and combine in each (a small call of S slots)
+bool stream_row_split(int S, int H, int I);
 // plan.idx set: the kernel groups the call's assignments itself (no permute launch)
 int launch_stream_up(const uint8_t *w13, const uint8_t *s13, int T, int kk, int H, int I, int order, float limit,
                      const uint16_t *x, const int32_t *offsets, const int32_t *perm, const int32_t *active,
                      const int32_t *counters, uint16_t *h, cudaStream_t stream, const RoutePlan &plan = RoutePlan{});
-// comb + done: the launch's last CTA also combines the rows (done zeroed by the call's first kernel)
+// comb + done: the launch's last CTA also combines the rows (done zeroed by the call's first kernel);
+// comb + plan (plan->idx set): each CTA takes a range of output rows of every active expert, grouping the
+// call itself before its dependency wait, and combines its own rows (y is not written)
 int launch_stream_down(const uint8_t *w2, const uint8_t *s2, int S, int H, int I, const uint16_t *h,
                        const int32_t *offsets, const int32_t *active, const int32_t *counters, uint16_t *y,
-                       cudaStream_t stream, const CombineArgs *comb = nullptr, int32_t *done = nullptr);
+                       cudaStream_t stream, const CombineArgs *comb = nullptr, int32_t *done = nullptr,
+                       const RoutePlan *plan = nullptr);
 
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
