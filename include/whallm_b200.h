@@ -321,6 +321,26 @@ WM_API int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const fl
                            float swiglu_limit, int shared_expert, const float *shared_w,
                            wm_bf16 *out, void *workspace, size_t ws_bytes, wm_stream_t stream);
 
+/* One whole routed-expert layer: wmoe_router_topk followed by
+ * wmoe_mxfp4_moe_forward on its outputs, in one call and on one stream, with
+ * the same results bit for bit (logits, idx, weights, shared_w and out are
+ * all written).
+ *   router:  gate wg [n_routed, H], logit_bias, select_bias, wg_shared, k,
+ *            score_fn, norm_eps, route_scale as wmoe_router_topk;
+ *   experts: E = n_routed (+1 when shared_expert >= 0, which must then be
+ *            n_routed: the shared expert is the last one), weighted by
+ *            shared_w when wg_shared is given, else by 1.
+ * Workspace: wmoe_workspace_size(T, k, H, I, E, shared_expert >= 0).  Replaces MoE.__call__
+ * (deepseek_v41/moe.py:105-112) and SparseMoE.__call__ (qwen4_exp.py:680-704)
+ * with their gates. */
+WM_API int wmoe_mxfp4_moe_layer(const wm_bf16 *x, int T, int H, int I, const wm_bf16 *wg, const float *logit_bias,
+                                const float *select_bias, const wm_bf16 *wg_shared, int n_routed, int k,
+                                int score_fn, float norm_eps, float route_scale, const uint8_t *w13,
+                                const uint8_t *s13, const uint8_t *w2, const uint8_t *s2, int gate_up_order,
+                                float swiglu_limit, int shared_expert, float *logits, int32_t *idx, float *weights,
+                                float *shared_w, wm_bf16 *out, void *workspace, size_t ws_bytes,
+                                wm_stream_t stream);
+
 /* One expert-parallel rank's share of wmoe_mxfp4_moe_forward, for decode
  * after an all-gather of every rank's tokens (T = all ranks' tokens):
  * out [T,H] float32 = sum over j with idx[t,j] in [route_base,

@@ -46,6 +46,17 @@ def _expect(rc_name, *args, code=L.WM_ERR_INVALID, msg=None):
         assert msg in L.last_error()
 
 
+def test_layer_rejects_bad_router_and_shared_expert_arguments():
+    # checked before any CUDA call: the shared expert must be the last one (expert n_routed)
+    f = "wmoe_mxfp4_moe_layer"
+    _expect(f, None, 1, 256, 256, None, None, None, None, 8, 2, 0, -1.0, 1.0, None, None, None, None, 0, 0.0, 3,
+            None, None, None, None, None, None, 0, None, msg="shared expert must be expert n_routed")
+    _expect(f, None, 1, 256, 256, None, None, None, None, 8, 9, 0, -1.0, 1.0, None, None, None, None, 0, 0.0, -1,
+            None, None, None, None, None, None, 0, None, msg="1 <= k <= min(32, n_routed)")
+    _expect(f, None, 0, 256, 256, None, None, None, None, 8, 2, 0, -1.0, 1.0, None, None, None, None, 0, 0.0, 8,
+            None, None, None, None, None, None, 0, None, code=L.WM_OK)
+
+
 def test_mxfp4_rejects_partial_groups():
     _expect("wmxfp4_quantize", None, 1, 33, None, None, None, msg="complete BF16 rows")
     _expect("wmxfp4_dequantize", None, None, 1, 31, 0, None, None)

@@ -13,7 +13,7 @@ from .experts import (Affine4BatchedExperts, BatchedExperts, ClampedSwiGLU, Expe
                       StreamingSwitchGLU, experts_forward, permute)
 from .formats import (affine4_dequantize, affine4_quantize, kv_dequantize, kv_gather_dequantize,  # noqa: F401
                       kv_quantize, kv_scores, mxfp4_dequantize, mxfp4_quantize, split_e4m3)
-from .moe import MoE, SparseMoE, TinyMoE, route_reduce, streaming_moe  # noqa: F401
+from .moe import MoE, SparseMoE, TinyMoE, moe_layer, route_reduce, streaming_moe  # noqa: F401
 from .router import Gate, qwen_route, route, stable_topk_indices, topk_scores  # noqa: F401
 
 from .linear import MXFP8Linear, expand_block_scales, mx_linear  # noqa: F401

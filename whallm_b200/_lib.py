@@ -68,6 +68,8 @@ SIGNATURES = {
     "wmoe_route_reduce": [_P, _I64, _P, _P, _I, _I, _I, _P, _P, _P],
     "wmoe_mxfp4_experts": [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _F, _P, _P, _SZ, _P],
     "wmoe_mxfp4_moe_forward": [_P, _P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _F, _I, _P, _P, _P, _SZ, _P],
+    "wmoe_mxfp4_moe_layer": [_P, _I, _I, _I, _P, _P, _P, _P, _I, _I, _I, _F, _F, _P, _P, _P, _P, _I, _F, _I, _P, _P, _P,
+                             _P, _P, _P, _SZ, _P],
     "wmoe_mxfp4_moe_forward_ep": [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _I, _F, _I, _P, _I,
                                   _I, _P, _P, _SZ, _P],
     "wmoe_affine4_experts": [_P, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _I, _I, _F, _P, _P, _SZ, _P],

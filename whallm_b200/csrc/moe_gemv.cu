@@ -373,42 +373,58 @@ MxPath mx_path() {
   return MxPath::kAuto;
 }
 
+// The call's path: which kernels run it, whether its first expert kernel
+// groups the slots itself (small) and where the rows are combined.
+struct Choice {
+  bool stream, mx, tc, affine_tc, small, stream_rows, fuse_combine;
+  int tile_n;
+};
+
+Choice choose(const Args &a, int fmt) {
+  Choice c{};
+  const int has_shared = a.shared_expert >= 0 ? 1 : 0;
+  const int S = a.T * (a.k + has_shared);
+  const MxPath path = mx_path();
+  const bool small_call = a.T <= wm::kStreamMaxTokens && a.H <= wm::kStreamMaxH && a.I <= wm::kStreamMaxI;
+  c.stream = fmt == kFmtMxfp4 && (path == MxPath::kStream || (path == MxPath::kAuto && small_call)) &&
+             wm::stream_supported(a.T, a.k, has_shared, a.H, a.I) && wm::aligned(a.w13.s, 8) && wm::aligned(a.w2.s, 8);
+  c.mx = !c.stream && fmt == kFmtMxfp4 && (path == MxPath::kAuto || path == MxPath::kMma || path == MxPath::kStream) &&
+         wm::mx_supported(a.H, a.I);
+  // affine-4 (group 64) runs on the f16 tensor-core kernel, dequantizing in
+  // software; WM_EXPERT_PATH=simt keeps it on the CUDA-core kernel
+  c.affine_tc = fmt == kFmtAffine4 && path != MxPath::kSimt && a.w13.group == 64 && a.w2.group == 64 &&
+                wm::tc_supported(a.H, a.I);
+  c.tc = (fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I)) || c.affine_tc;
+  const int n_routed = a.rf.count > 0 ? a.rf.n_global : a.E - has_shared;
+  c.tile_n = c.mx ? wm::mx_tile_n(a.T, a.k, n_routed) : wm::tc_tile_n(a.T);
+  // small calls: the first expert kernel groups the assignments itself (no permute launch), and when
+  // the output is at most 4096 values the last CTA of the down projection combines the rows (no combine
+  // launch; for a 7168-wide DeepSeek-class row the serial passes of one CTA cost more than the launch)
+  // (WM_FUSE=0 keeps the separate permute and combine launches, for A/B checks)
+  const char *fuse_env = getenv("WM_FUSE");
+  const bool fuse = !(fuse_env && fuse_env[0] == '0');
+  c.small = fuse && a.rf.count == 0 && (c.stream || c.mx || c.tc) &&
+            S <= (c.stream ? wm::kStreamRouteMax : wm::kSmallRouteMax);
+  // one CTA combines the rows in about one pass over its threads (T * H / 8 output groups); the weight
+  // stream's down projection splits the output rows over its CTAs and each combines its own
+  c.stream_rows = c.small && c.stream && a.reduce && wm::stream_row_split(S, a.H, a.I);
+  c.fuse_combine = c.stream_rows || (c.small && (c.stream || c.mx) && a.reduce && a.T * a.H <= 4096);
+  return c;
+}
+
 int run(const Args &a, int fmt) {
   if (a.T == 0) return WM_OK;
   if (int rc = check_common(a)) return rc;
   const int has_shared = a.shared_expert >= 0 ? 1 : 0;
   wm::MoeWorkspace ws = wm::carve_workspace(a.ws, a.T, a.k, a.H, a.I, a.E, has_shared);
   if (a.ws_bytes < ws.bytes) return wm::fail(WM_ERR_WORKSPACE, "experts: workspace too small");
-  if (a.T == 0) return WM_OK;
   const int kk = a.k + has_shared;
   const int S = a.T * kk;
-  const MxPath path = mx_path();
-  const bool small_call = a.T <= wm::kStreamMaxTokens && a.H <= wm::kStreamMaxH && a.I <= wm::kStreamMaxI;
-  const bool stream = fmt == kFmtMxfp4 && (path == MxPath::kStream || (path == MxPath::kAuto && small_call)) &&
-                      wm::stream_supported(a.T, a.k, has_shared, a.H, a.I) && wm::aligned(a.w13.s, 8) &&
-                      wm::aligned(a.w2.s, 8);
-  const bool mx = !stream && fmt == kFmtMxfp4 && (path == MxPath::kAuto || path == MxPath::kMma || path == MxPath::kStream) &&
-                  wm::mx_supported(a.H, a.I);
-  // affine-4 (group 64) runs on the f16 tensor-core kernel, dequantizing in
-  // software; WM_EXPERT_PATH=simt keeps it on the CUDA-core kernel
-  const bool affine_tc = fmt == kFmtAffine4 && path != MxPath::kSimt && a.w13.group == 64 && a.w2.group == 64 &&
-                         wm::tc_supported(a.H, a.I);
-  const bool tc = (fmt == kFmtMxfp4 && path == MxPath::kF16 && wm::tc_supported(a.H, a.I)) || affine_tc;
-  const int n_routed = a.rf.count > 0 ? a.rf.n_global : a.E - has_shared;
-  const int tile_n = mx ? wm::mx_tile_n(a.T, a.k, n_routed) : wm::tc_tile_n(a.T);
-  // small calls: the first expert kernel groups the assignments itself (no permute launch), and when
-  // the output is at most 4096 values the last CTA of the down projection combines the rows (no combine
-  // launch; for a 7168-wide DeepSeek-class row the serial passes of one CTA cost more than the launch)
+  const Choice ch = choose(a, fmt);
+  const bool stream = ch.stream, mx = ch.mx, tc = ch.tc, affine_tc = ch.affine_tc, small = ch.small;
+  const bool stream_rows = ch.stream_rows, fuse_combine = ch.fuse_combine;
+  const int tile_n = ch.tile_n;
   wm::RoutePlan plan{};
-  // (WM_FUSE=0 keeps the separate permute and combine launches, for A/B checks)
-  const char *fuse_env = getenv("WM_FUSE");
-  const bool fuse = !(fuse_env && fuse_env[0] == '0');
-  const bool small = fuse && a.rf.count == 0 && (stream || mx || tc) &&
-                     S <= (stream ? wm::kStreamRouteMax : wm::kSmallRouteMax);
-  // one CTA combines the rows in about one pass over its threads (T * H / 8 output groups); the weight
-  // stream's down projection splits the output rows over its CTAs and each combines its own
-  const bool stream_rows = small && stream && a.reduce && wm::stream_row_split(S, a.H, a.I);
-  const bool fuse_combine = stream_rows || (small && (stream || mx) && a.reduce && a.T * a.H <= 4096);
   const wm::CombineArgs comb{ws.y, ws.inv, a.weights, a.shared_w, ws.counters + 1, a.T, a.k, kk, a.H,
                              a.out_f32 ? static_cast<void *>(a.out_f32) : static_cast<void *>(a.out),
                              a.out_f32 != nullptr};
@@ -545,6 +561,42 @@ int wmoe_mxfp4_moe_forward(const wm_bf16 *x, const int32_t *idx, const float *we
   wm::clear_error();
   Args a{x, idx, weights, T, k, H, I, E, mx_view(w13, s13, 2 * I, H), mx_view(w2, s2, H, I), gate_up_order,
          swiglu_limit, shared_expert, shared_w, out, true, workspace, ws_bytes, stream};
+  return run(a, kFmtMxfp4);
+}
+
+int wmoe_mxfp4_moe_layer(const wm_bf16 *x, int T, int H, int I, const wm_bf16 *wg, const float *logit_bias,
+                         const float *select_bias, const wm_bf16 *wg_shared, int n_routed, int k, int score_fn,
+                         float norm_eps, float route_scale, const uint8_t *w13, const uint8_t *s13, const uint8_t *w2,
+                         const uint8_t *s2, int gate_up_order, float swiglu_limit, int shared_expert, float *logits,
+                         int32_t *idx, float *weights, float *shared_w, wm_bf16 *out, void *workspace,
+                         size_t ws_bytes, wm_stream_t stream) {
+  wm::clear_error();
+  WM_REQUIRE(T >= 0 && H > 0 && H % 8 == 0, "layer: router needs H % 8 == 0");
+  WM_REQUIRE(n_routed >= 1 && n_routed <= 1024, "layer: router supports 1 <= n_routed <= 1024 experts");
+  WM_REQUIRE(k >= 1 && k <= 32 && k <= n_routed, "layer: router needs 1 <= k <= min(32, n_routed)");
+  WM_REQUIRE(score_fn >= WM_SCORE_SOFTMAX && score_fn <= WM_SCORE_SOFTMAX_BF16, "layer: unknown score function");
+  WM_REQUIRE(shared_expert < 0 || shared_expert == n_routed, "layer: the shared expert must be expert n_routed");
+  if (T == 0) return WM_OK;
+  WM_REQUIRE(x && wg && logits && idx && weights, "layer: null buffer");
+  WM_REQUIRE(!wg_shared || shared_w, "layer: wg_shared needs a shared_w output");
+  WM_REQUIRE(wm::aligned(x, 16) && wm::aligned(wg, 16) && (!wg_shared || wm::aligned(wg_shared, 16)),
+             "layer: router inputs must be 16-byte aligned");
+  const int E = n_routed + (shared_expert >= 0 ? 1 : 0);
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Args a{x, idx, weights, T, k, H, I, E, mx_view(w13, s13, 2 * I, H), mx_view(w2, s2, H, I), gate_up_order,
+         swiglu_limit, shared_expert, wg_shared ? shared_w : nullptr, out, true, workspace, ws_bytes, st};
+  if (int rc = check_common(a)) return rc;
+  const wm::MoeWorkspace ws = wm::carve_workspace(workspace, T, k, H, I, E, shared_expert >= 0 ? 1 : 0);
+  if (ws_bytes < ws.bytes) return wm::fail(WM_ERR_WORKSPACE, "layer: workspace too small");
+  // (the router's top-k run inside every CTA of the first expert kernel instead of its own launch was
+  // measured slower: the per-CTA top-k costs more than the launch it saves)
+  if (int rc = wm::router_logits(reinterpret_cast<const uint16_t *>(x), reinterpret_cast<const uint16_t *>(wg),
+                                 reinterpret_cast<const uint16_t *>(wg_shared), logit_bias, T, H, n_routed, logits,
+                                 wg_shared ? shared_w : nullptr, st))
+    return rc;
+  if (int rc = wm::router_topk(logits, select_bias, T, n_routed, k, score_fn, norm_eps, route_scale, idx, weights,
+                               wg_shared ? shared_w : nullptr, st))
+    return rc;
   return run(a, kFmtMxfp4);
 }
 

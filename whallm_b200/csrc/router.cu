@@ -613,6 +613,21 @@ int launch_router_topk(const float *logits, const float *select_bias, int T, int
 
 }  // namespace
 
+namespace wm {
+
+int router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *wg_shared, const float *logit_bias, int T,
+                  int H, int E, float *logits, float *shared_raw, cudaStream_t stream) {
+  return launch_router_logits(x, wg, wg_shared, logit_bias, T, H, E, logits, shared_raw, stream);
+}
+
+int router_topk(const float *logits, const float *select_bias, int T, int E, int k, int score_fn, float norm_eps,
+                float route_scale, int32_t *idx, float *weights, float *shared_w, cudaStream_t stream) {
+  return launch_router_topk(logits, select_bias, T, E, k, score_fn, norm_eps, route_scale, idx, weights, shared_w,
+                            stream);
+}
+
+}  // namespace wm
+
 extern "C" int wmoe_router_topk(const wm_bf16 *x, const wm_bf16 *wg, const float *logit_bias, const float *select_bias,
                                 const wm_bf16 *wg_shared, int T, int H, int E, int k, int score_fn, float norm_eps,
                                 float route_scale, float *logits, int32_t *idx, float *weights, float *shared_w,

@@ -43,6 +43,14 @@ int launch_tc_down(const uint8_t *w2, const uint8_t *s2, int E, int H, int I, co
                    const int4 *tiles, const int32_t *n_tiles, uint16_t *y, int32_t *err, int tile_n, cudaStream_t stream,
                    const uint16_t *af_sc = nullptr, const uint16_t *af_bi = nullptr);
 
+// router.cu: the two router launches of wmoe_router_topk (arguments checked by the caller); the logits
+// launch writes the raw shared-gate logit into shared_raw[t], the top-k launch turns shared_w[t] (the same
+// buffer, when given) into the gate
+int router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *wg_shared, const float *logit_bias, int T,
+                  int H, int E, float *logits, float *shared_raw, cudaStream_t stream);
+int router_topk(const float *logits, const float *select_bias, int T, int E, int k, int score_fn, float norm_eps,
+                float route_scale, int32_t *idx, float *weights, float *shared_w, cudaStream_t stream);
+
 // moe_stream.cu: CUDA-core MXFP4 weight stream for calls of one or two tokens
 constexpr size_t kStreamSmemMax = 216 * 1024;   // shared memory: staged f16 operand rows + copy rings (+ ~7 KB static)
 constexpr int kStreamMaxTokens = 2;               // calls of at most this many tokens take the stream path
