@@ -55,7 +55,8 @@ def _partials(lay, x, world, idx=None, w=None, order=None):
     return acc.to(torch.bfloat16), w, idx
 
 
-@pytest.mark.parametrize("world,T,H,I", [(2, 6, 1024, 256), (4, 72, 1024, 256), (8, 24, 512, 96)])
+@pytest.mark.parametrize("world,T,H,I", [(2, 6, 1024, 256), (4, 72, 1024, 256), (8, 24, 512, 96),
+                                         (2, 2, 1024, 512)])   # two tokens: the weight stream with a route filter
 def test_partial_sums_over_ranks_equal_full_layer(dev, world, T, H, I):
     import sys
     sys.path.insert(0, ROOT)
