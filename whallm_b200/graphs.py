@@ -1,9 +1,9 @@
 """CUDA-graph capture of a whole MoE-layer forward for a fixed decode shape.
 
-A decode step launches eight small kernels per layer (router logits, top-k,
-permute, token gather, up projection, down projection, combine, a flag reset);
-at batch 1 the GPU work is tens of microseconds, comparable to the host cost
-of issuing it.  ``CapturedLayer`` records the launches once and replays them
+A decode step launches four to seven small kernels per layer (router logits
+and top-k, then the expert call: up to a permute, a token split or gather,
+the two projections and a combine, fewer for small calls); at batch 1 the GPU
+work is tens of microseconds, comparable to the host cost of issuing it.  ``CapturedLayer`` records the launches once and replays them
 with a single graph launch; inputs are copied into a static buffer first.
 The captured kernels, streams and workspaces are the same as the eager path.
 """
