@@ -214,21 +214,23 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   const int cpe = p.rows / kRows;
   // the CTA's chunks: MODE 0 / 1 a contiguous share of all (expert, row chunk) pairs; MODE 2 the row chunks
   // [mb, mb + lc) of every active expert, so the CTA holds every slot's rows there and combines them itself
-  int64_t c0, c1;
+  // chunk indices fit 32 bits (at most 4096 experts x 1024 chunks), and 32-bit divisions are a few
+  // instructions where 64-bit ones are a subroutine
+  int c0, c1;
   int lc = cpe, mb = 0;
   if (MODE == 2) {
     mb = blockIdx.x * p.row_chunks;
     lc = max(0, min(p.row_chunks, cpe - mb));
     c0 = 0;
-    c1 = static_cast<int64_t>(n_active) * lc;
+    c1 = n_active * lc;
   } else {
-    const int64_t n_chunks = static_cast<int64_t>(n_active) * cpe;
+    const int n_chunks = n_active * cpe;
     c0 = n_chunks * blockIdx.x / gridDim.x;
     c1 = n_chunks * (blockIdx.x + 1) / gridDim.x;
     if (c0 >= c1) return;
   }
-  const int a_first = MODE == 2 ? 0 : static_cast<int>(c0 / cpe);
-  const int a_last = MODE == 2 ? n_active - 1 : static_cast<int>((c1 - 1) / cpe);
+  const int a_first = MODE == 2 ? 0 : c0 / cpe;
+  const int a_last = MODE == 2 ? n_active - 1 : (c1 - 1) / cpe;
 
   // ------------------------------ the CTA's experts
   if (!in_kernel) {
@@ -298,8 +300,8 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   // Each warp walks its chunks as one stream of (chunk, pass, step) with the
   // loads one step ahead of the arithmetic, across chunk boundaries too.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t nc = c1 - c0;
-  const int64_t w0 = c0 + nc * warp / kWarps, w1 = c0 + nc * (warp + 1) / kWarps;
+  const int nc = c1 - c0;
+  const int w0 = c0 + nc * warp / kWarps, w1 = c0 + nc * (warp + 1) / kWarps;
   const bool has_work = w0 < w1;
   const int pieces = K / VPP;
   const int steps = (pieces + 31) / 32;
@@ -322,13 +324,13 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
     else { r0 = kRows * m; r1 = kRows * m + 1; }
   };
   struct Cursor {
-    int64_t c;        // chunk
+    int c;            // chunk
     int a, m;         // active expert, chunk within it
     int t0, s;        // first slot of the pass, step
     int n;            // slots of the expert
   };
   auto start = [&](Cursor &u) {
-    u.c = w0; u.a = static_cast<int>(w0 / lc); u.m = mb + static_cast<int>(w0 - static_cast<int64_t>(u.a) * lc);
+    u.c = w0; u.a = w0 / lc; u.m = mb + (w0 - u.a * lc);
     u.t0 = 0; u.s = 0;
     int e, p0;
     meta(u.a, e, p0, u.n);
@@ -358,7 +360,7 @@ __device__ __forceinline__ void stream_body(const StreamParams &p) {
   Cursor L{};
   if (has_work) start(L);
   const uint8_t *wb0 = nullptr, *wb1 = nullptr, *sb0 = nullptr, *sb1 = nullptr;
-  int64_t l_chunk = -1;
+  int l_chunk = -1;
   auto issue = [&](int slot) {
     if (L.c < w1) {
       if (L.c != l_chunk) {

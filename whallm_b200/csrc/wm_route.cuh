@@ -50,27 +50,24 @@ struct SmallRoute {
 };
 
 // Every thread of the calling CTA runs this (blockDim.x >= 64, a multiple of
-// 32; __syncthreads inside); the result is in `r` when it returns.  `key` is
-// kSmallRouteMax ints of shared scratch.  idx is [T, k]; slot j >= k of a
-// token is the shared expert.  Each thread ranks its assignments against all
-// S keys (the stable order of (expert, assignment)), then warp 0 numbers the
+// 32; three barriers inside); the result is in `r` when it returns.  `key` is
+// CAP ints of shared scratch.  idx is [T, k]; slot j >= k of a token is the
+// shared expert.  Each thread ranks its assignments against all S keys (the
+// stable order of (expert, assignment)), then warp 0 finds and numbers the
 // experts' first slots.  S <= CAP.
 template <int CAP>
 __device__ __forceinline__ void small_route(const int32_t *__restrict__ idx, int T, int k, int shared_expert, int E,
                                             SmallRoute<CAP> &r, int32_t *key) {
-  __shared__ int bad_any;
-  __shared__ uint8_t first[CAP];
   const int kk = k + (shared_expert >= 0 ? 1 : 0);
   const int S = T * kk;
-  if (threadIdx.x == 0) bad_any = 0;
-  __syncthreads();
+  int bad = 0;
   for (int a = threadIdx.x; a < S; a += blockDim.x) {
     const int t = a / kk, j = a - t * kk;
     const int e = j < k ? idx[t * k + j] : shared_expert;
-    if (e < 0 || e >= E) bad_any = 1;
+    if (e < 0 || e >= E) bad = 1;
     key[a] = (e < 0 || e >= E ? 0 : e) * CAP + a;   // unique; orders by (expert, assignment)
   }
-  __syncthreads();
+  const int bad_any = __syncthreads_or(bad);       // (also the barrier that publishes key[])
   for (int a = threadIdx.x; a < S; a += blockDim.x) {
     const int ka = key[a];
     int rank = 0;
@@ -79,16 +76,18 @@ __device__ __forceinline__ void small_route(const int32_t *__restrict__ idx, int
     r.inv[a] = rank;
   }
   __syncthreads();
-  // run starts in the sorted keys: the first slot of each expert
-  for (int sl = threadIdx.x; sl < S; sl += blockDim.x)
-    first[sl] = (sl == 0 || key[r.perm[sl]] / CAP != key[r.perm[sl - 1]] / CAP) ? 1 : 0;
-  __syncthreads();
   if (threadIdx.x < 32) {
+    // run starts in the sorted keys (the first slot of each expert), numbered by a warp scan
     const int lane = threadIdx.x;
     constexpr int kPer = CAP / 32;                     // slots per lane, in order
+    bool first[kPer];
     int cnt = 0;
 #pragma unroll
-    for (int u = 0; u < kPer; ++u) cnt += (lane * kPer + u < S) ? first[lane * kPer + u] : 0;
+    for (int u = 0; u < kPer; ++u) {
+      const int sl = lane * kPer + u;
+      first[u] = sl < S && (sl == 0 || key[r.perm[sl]] / CAP != key[r.perm[sl - 1]] / CAP);
+      cnt += first[u] ? 1 : 0;
+    }
     int incl = cnt;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
@@ -100,7 +99,7 @@ __device__ __forceinline__ void small_route(const int32_t *__restrict__ idx, int
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
       const int sl = lane * kPer + u;
-      if (sl < S && first[sl]) {
+      if (first[u]) {
         r.act_e[ai] = key[r.perm[sl]] / CAP;
         r.act_p0[ai] = sl;
         ++ai;
