@@ -43,8 +43,15 @@
 // conversion and one FMA per value and token) keep a 23 MB expert below the
 // HBM rate, so the dispatch sends only small experts here.
 //
-// Outputs match the other expert paths' buffers: h (bf16, slot order) and y
-// (bf16, slot order), combined by the same k_combine.
+// Three launch forms (MODE): 0 the up projection (+ ClampedSwiGLU, and for
+// a small call the grouping of its slots, CTA 0 writing it for the later
+// launches); 1 the down projection over a contiguous share of (expert, chunk)
+// pairs per CTA, y (bf16, slot order) combined by k_combine or the last CTA;
+// 2 the down projection of a small call split by output rows: CTA b takes
+// chunks [b n, b n + n) of every active expert, groups the call and issues its
+// first weight copies before its dependency wait (the routing was complete
+// before the up projection's own wait returned), and combines its own rows
+// with k_combine's arithmetic -- y never leaves shared memory.
 #include "wm_common.cuh"
 #include "wm_combine.cuh"
 #include "wm_moe.cuh"
