@@ -216,3 +216,21 @@ def test_many_token_short_row_logits_vs_oracle(dev, fn, shape):
     lb = rng.normal(0, 1, E).astype(np.float32)
     ref = R.route(xb, wb, k, fn, logit_bias=lb, norm_eps=0.0, wg_shared_bits=sg)
     _check(_run(dev, xb, wb, k, fn, lb, None, 0.0, 1.0, sg), ref)
+
+
+@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX, R.SCORE_SIGMOID, R.SCORE_SQRTSOFTPLUS, R.SCORE_NONE,
+                                R.SCORE_SOFTMAX_BF16])
+@pytest.mark.parametrize("shape", [(1, 1024, 8, 2), (3, 264, 32, 5), (70, 512, 31, 4), (64, 1024, 16, 4)])
+def test_small_gates_vs_oracle(dev, fn, shape):
+    # up to 32 gate rows (a shared gate on the 31-expert case fills the 32nd), every score function with
+    # logit and selection biases, token counts not a multiple of the top-k kernel's 4 tokens per CTA
+    T, H, E, k = shape
+    rng = np.random.default_rng(T + E + fn)
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    lb = rng.normal(0, 0.5, E).astype(np.float32)
+    sb = rng.normal(0, 0.1, E).astype(np.float32)
+    sg = F.f32_to_bf16_bits((rng.normal(0, 1, (H,)) / np.sqrt(H)).astype(np.float32)) if E == 31 else None
+    eps = -1.0 if fn == R.SCORE_NONE else 1e-20
+    ref = R.route(xb, wb, k, fn, logit_bias=lb, select_bias=sb, norm_eps=eps, route_scale=1.5, wg_shared_bits=sg)
+    _check(_run(dev, xb, wb, k, fn, lb, sb, eps, 1.5, sg), ref)
