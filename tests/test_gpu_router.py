@@ -234,3 +234,17 @@ def test_small_gates_vs_oracle(dev, fn, shape):
     eps = -1.0 if fn == R.SCORE_NONE else 1e-20
     ref = R.route(xb, wb, k, fn, logit_bias=lb, select_bias=sb, norm_eps=eps, route_scale=1.5, wg_shared_bits=sg)
     _check(_run(dev, xb, wb, k, fn, lb, sb, eps, 1.5, sg), ref)
+
+
+@pytest.mark.parametrize("fn", [R.SCORE_SOFTMAX_BF16, R.SCORE_SQRTSOFTPLUS])
+def test_many_tokens_wide_tree_tiles_vs_oracle(dev, fn):
+    # 5000 tokens x (512 experts + a shared gate) on short rows: two waves of 8 x 4 output tiles per thread;
+    # ragged rows (513 of 128 per CTA), tokens (5000 of 64) and row length (1032 of 256)
+    T, H, E, k = 5000, 1032, 512, 6
+    rng = np.random.default_rng(fn + 5)
+    xb = F.f32_to_bf16_bits(rng.normal(0, 1, (T, H)).astype(np.float32))
+    wb = F.f32_to_bf16_bits((rng.normal(0, 1, (E, H)) / np.sqrt(H)).astype(np.float32))
+    sg = F.f32_to_bf16_bits((rng.normal(0, 1, (H,)) / np.sqrt(H)).astype(np.float32))
+    lb = rng.normal(0, 0.5, E).astype(np.float32)
+    ref = R.route(xb, wb, k, fn, logit_bias=lb, norm_eps=1e-20, wg_shared_bits=sg)
+    _check(_run(dev, xb, wb, k, fn, lb, None, 1e-20, 1.0, sg), ref)

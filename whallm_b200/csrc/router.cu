@@ -232,47 +232,45 @@ __global__ void __launch_bounds__(128) k_router_logits_staged(const uint16_t *__
 
 // Many tokens, short rows (T > 64, H <= 4096): the per-warp segments of the
 // kernels above hold only a few column blocks, so their shared-memory partial
-// reduction outweighs the multiply-adds.  Here one thread owns a 4 x 4 tile of
-// (expert, token) outputs and evaluates each output's whole canonical sum
+// reduction outweighs the multiply-adds.  Here one thread owns a TE x TT tile
+// of (expert, token) outputs and evaluates each output's whole canonical sum
 // itself: the 32 lane partials l (each the four segment chains, added in
 // segment order) are produced in bit-reversed lane order 0, 16, 8, 24, 4, ...,
 // which turns the butterfly (strides 16, 8, 4, 2, 1) into a five-level binary
 // counter of running sums -- the same additions in the same tree, so the
-// bits equal k_router_logits'.  A CTA (256 threads) covers 64 experts x 64
-// tokens; leaf l's 16-byte pieces 256 i + 8 l of its 128 rows are staged with
-// cp.async, double buffered; token pairs share packed f32x2 FMAs.
-constexpr int kTreeTE = 4, kTreeTT = 4;        // outputs per thread
-constexpr int kTreeRows = 16 * (kTreeTE + kTreeTT);
+// bits equal k_router_logits'.  A CTA (256 threads) covers 16 TE experts x
+// 16 TT tokens; leaf l's 16-byte pieces 256 i + 8 l of its rows are staged
+// with cp.async, double buffered; token pairs share packed f32x2 FMAs; the
+// last merge lands in the tree's top level, which then holds the output.
+// 8 x 4 tiles (half the token staging per multiply-add; a few registers
+// spill) measured 10 % faster than 4 x 4 from one and a half waves of CTAs up
+// (512-row gate: 1730 -> 1551 us at 16384 tokens, 492 -> 441 at 4096) and
+// slower below (127 -> 217 us at 1024).
 
 __device__ __forceinline__ int bitrev5(int k) { return static_cast<int>(__brev(static_cast<unsigned>(k)) >> 27); }
 
-__global__ void __launch_bounds__(256, 1) k_router_logits_tree(const uint16_t *__restrict__ x,
-                                                               const uint16_t *__restrict__ wg,
-                                                               const uint16_t *__restrict__ wg_shared,
-                                                               const float *__restrict__ logit_bias, int T, int H,
-                                                               int E, float *__restrict__ logits,
-                                                               float *__restrict__ shared_raw) {
-  extern __shared__ __align__(16) uint4 tstage[];       // [2][kTreeRows][pitch]
-  WM_PDL_WAIT();
-  WM_PDL_LAUNCH();
+// The CTA's tile: rows [e0, e0 + 16 TE) x tokens [t0, t0 + 16 TT).
+template <int TE, int TT>
+__device__ __forceinline__ void tree_tile(const uint16_t *__restrict__ x, const uint16_t *__restrict__ wg,
+                                          const uint16_t *__restrict__ wg_shared,
+                                          const float *__restrict__ logit_bias, int T, int H, int E, int e0, int t0,
+                                          float *__restrict__ logits, float *__restrict__ shared_raw,
+                                          uint4 *tstage) {                // [2][(16 * (TE + TT))][pitch]
   const int n = (H + 255) / 256;
   const int pitch = n + ((9 - n % 8) % 8);               // pitch % 8 == 1: 16 consecutive rows hit distinct banks
   const int rows = E + (wg_shared ? 1 : 0);
-  const int egroups = (rows + 63) / 64;
-  const int e0 = (blockIdx.x % egroups) * 64;
-  const int t0 = (blockIdx.x / egroups) * 64;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-  // staged row r: r < 64 gate row e0 + r (clamped; row E is the shared gate), else token t0 + r - 64 (clamped)
+  // staged row r: r < 16 TE gate row e0 + r (clamped; row E is the shared gate), else token t0 + r - 16 TE
   auto row_ptr = [&](int r) -> const uint16_t * {
-    if (r < 64) {
+    if (r < 16 * TE) {
       const int e = min(e0 + r, rows - 1);
       return e < E ? wg + static_cast<int64_t>(e) * H : wg_shared;
     }
-    return x + static_cast<int64_t>(min(t0 + r - 64, T - 1)) * H;
+    return x + static_cast<int64_t>(min(t0 + r - 16 * TE, T - 1)) * H;
   };
   auto issue = [&](int leaf, int buf) {
-    uint4 *dst = tstage + buf * kTreeRows * pitch;
-    for (int c = threadIdx.x; c < kTreeRows * n; c += 256) {
+    uint4 *dst = tstage + buf * (16 * (TE + TT)) * pitch;
+    for (int c = threadIdx.x; c < (16 * (TE + TT)) * n; c += 256) {
       const int r = c / n, i = c - r * n;
       const int base = 256 * i + 8 * leaf;
       const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(dst + r * pitch + i));
@@ -282,8 +280,7 @@ __global__ void __launch_bounds__(256, 1) k_router_logits_tree(const uint16_t *_
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  float lv[5][kTreeTE][kTreeTT];                         // running sums of the butterfly tree, by level
-  float out[kTreeTE][kTreeTT];
+  float lv[5][TE][TT];                         // running sums of the butterfly tree, by level
   issue(0, 0);
   for (int k = 0; k < 32; ++k) {
     const int leaf = bitrev5(k);
@@ -294,58 +291,58 @@ __global__ void __launch_bounds__(256, 1) k_router_logits_tree(const uint16_t *_
       asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    const uint4 *st = tstage + (k & 1) * kTreeRows * pitch;
-    float ls[kTreeTE][kTreeTT];                          // lane partial of this leaf: segments in order
+    const uint4 *st = tstage + (k & 1) * (16 * (TE + TT)) * pitch;
+    float ls[TE][TT];                          // lane partial of this leaf: segments in order
 #pragma unroll
-    for (int a = 0; a < kTreeTE; ++a)
+    for (int a = 0; a < TE; ++a)
 #pragma unroll
-      for (int b = 0; b < kTreeTT; ++b) ls[a][b] = 0.0f;
+      for (int b = 0; b < TT; ++b) ls[a][b] = 0.0f;
     for (int sg = 0; sg < 4; ++sg) {
       const int i0 = (sg * n) / 4, i1 = ((sg + 1) * n) / 4;
-      float2 acc[kTreeTE][kTreeTT / 2];                  // {token 2 bp, token 2 bp + 1}
+      float2 acc[TE][TT / 2];                  // {token 2 bp, token 2 bp + 1}
 #pragma unroll
-      for (int a = 0; a < kTreeTE; ++a)
+      for (int a = 0; a < TE; ++a)
 #pragma unroll
-        for (int bp = 0; bp < kTreeTT / 2; ++bp) acc[a][bp] = make_float2(0.0f, 0.0f);
+        for (int bp = 0; bp < TT / 2; ++bp) acc[a][bp] = make_float2(0.0f, 0.0f);
       for (int i = i0; i < i1; ++i) {
         if (256 * i + 8 * leaf >= H) continue;           // the chain skips absent pieces, as k_router_logits
-        uint4 wu[kTreeTE], xu[kTreeTT];
+        uint4 wu[TE], xu[TT];
 #pragma unroll
-        for (int a = 0; a < kTreeTE; ++a) wu[a] = st[(ty + 16 * a) * pitch + i];
+        for (int a = 0; a < TE; ++a) wu[a] = st[(ty + 16 * a) * pitch + i];
 #pragma unroll
-        for (int b = 0; b < kTreeTT; ++b) xu[b] = st[(64 + tx + 16 * b) * pitch + i];
+        for (int b = 0; b < TT; ++b) xu[b] = st[(16 * TE + tx + 16 * b) * pitch + i];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int wd = j >> 1;
-          float xv[kTreeTT];
+          float xv[TT];
 #pragma unroll
-          for (int b = 0; b < kTreeTT; ++b) {
+          for (int b = 0; b < TT; ++b) {
             const uint32_t u = wd == 0 ? xu[b].x : wd == 1 ? xu[b].y : wd == 2 ? xu[b].z : xu[b].w;
             xv[b] = (j & 1) ? wm_bf16hi(u) : wm_bf16lo(u);
           }
 #pragma unroll
-          for (int a = 0; a < kTreeTE; ++a) {
+          for (int a = 0; a < TE; ++a) {
             const uint32_t u = wd == 0 ? wu[a].x : wd == 1 ? wu[a].y : wd == 2 ? wu[a].z : wu[a].w;
             const float wv = (j & 1) ? wm_bf16hi(u) : wm_bf16lo(u);
 #pragma unroll
-            for (int bp = 0; bp < kTreeTT / 2; ++bp)
+            for (int bp = 0; bp < TT / 2; ++bp)
               acc[a][bp] = wm_fma2(make_float2(xv[2 * bp], xv[2 * bp + 1]), make_float2(wv, wv), acc[a][bp]);
           }
         }
       }
 #pragma unroll
-      for (int a = 0; a < kTreeTE; ++a)
+      for (int a = 0; a < TE; ++a)
 #pragma unroll
-        for (int bp = 0; bp < kTreeTT / 2; ++bp) {
+        for (int bp = 0; bp < TT / 2; ++bp) {
           ls[a][2 * bp] = ls[a][2 * bp] + acc[a][bp].x;   // ((seg0 + seg1) + seg2) + seg3 (0 + seg0 exact)
           ls[a][2 * bp + 1] = ls[a][2 * bp + 1] + acc[a][bp].y;
         }
     }
     // insert the leaf into the tree: k's trailing ones are the merges
 #pragma unroll
-    for (int a = 0; a < kTreeTE; ++a)
+    for (int a = 0; a < TE; ++a)
 #pragma unroll
-      for (int b = 0; b < kTreeTT; ++b) {
+      for (int b = 0; b < TT; ++b) {
         float v = ls[a][b];
         if (!(k & 1)) { lv[0][a][b] = v; continue; }
         v = lv[0][a][b] + v;
@@ -356,21 +353,50 @@ __global__ void __launch_bounds__(256, 1) k_router_logits_tree(const uint16_t *_
         if (!(k & 8)) { lv[3][a][b] = v; continue; }
         v = lv[3][a][b] + v;
         if (!(k & 16)) { lv[4][a][b] = v; continue; }
-        out[a][b] = lv[4][a][b] + v;
+        lv[4][a][b] = lv[4][a][b] + v;
       }
     __syncthreads();                                     // buffer k & 1 is refilled by the next iteration's issue
   }
 #pragma unroll
-  for (int a = 0; a < kTreeTE; ++a) {
+  for (int a = 0; a < TE; ++a) {
     const int e = e0 + ty + 16 * a;
 #pragma unroll
-    for (int b = 0; b < kTreeTT; ++b) {
+    for (int b = 0; b < TT; ++b) {
       const int t = t0 + tx + 16 * b;
       if (e < rows && t < T) {
-        if (e < E) logits[static_cast<int64_t>(t) * E + e] = logit_bias ? out[a][b] + logit_bias[e] : out[a][b];
-        else shared_raw[t] = out[a][b];
+        if (e < E) logits[static_cast<int64_t>(t) * E + e] = logit_bias ? lv[4][a][b] + logit_bias[e] : lv[4][a][b];
+        else shared_raw[t] = lv[4][a][b];
       }
     }
+  }
+}
+
+
+// Rows [0, main_rows) in TE x TT tiles (main_rows a multiple of 16 TE), then
+// the few rows left over (the shared gate after 512 experts) in TE2 x TT tiles,
+// so that a ragged last row group does not cost a whole wide tile.
+template <int TE, int TT, int TE2>
+__global__ void __launch_bounds__(256, 1) k_router_logits_tree(const uint16_t *__restrict__ x,
+                                                               const uint16_t *__restrict__ wg,
+                                                               const uint16_t *__restrict__ wg_shared,
+                                                               const float *__restrict__ logit_bias, int T, int H,
+                                                               int E, float *__restrict__ logits,
+                                                               float *__restrict__ shared_raw, int main_rows) {
+  extern __shared__ __align__(16) uint4 tstage[];
+  WM_PDL_WAIT();
+  WM_PDL_LAUNCH();
+  const int eg = main_rows / (16 * TE);
+  const int main_ctas = eg * ((T + 16 * TT - 1) / (16 * TT));
+  const int b = static_cast<int>(blockIdx.x);
+  if (b < main_ctas) {
+    tree_tile<TE, TT>(x, wg, wg_shared, logit_bias, T, H, E, (b % eg) * 16 * TE, (b / eg) * 16 * TT, logits,
+                      shared_raw, tstage);
+  } else {
+    const int rows = E + (wg_shared ? 1 : 0);
+    const int eg2 = (rows - main_rows + 16 * TE2 - 1) / (16 * TE2);
+    const int r = b - main_ctas;
+    tree_tile<TE2, TT>(x, wg, wg_shared, logit_bias, T, H, E, main_rows + (r % eg2) * 16 * TE2,
+                       (r / eg2) * 16 * TT, logits, shared_raw, tstage);
   }
 }
 
@@ -417,7 +443,7 @@ int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *
   }
   if (H <= 4096) {
     const int n = (H + 255) / 256;
-    const size_t smem = static_cast<size_t>(2) * kTreeRows * (n + ((9 - n % 8) % 8)) * sizeof(uint4);
+    const size_t pitch = n + ((9 - n % 8) % 8);
     static std::mutex tmu;
     static bool tattr[64] = {false};
     int dev = 0;
@@ -425,18 +451,27 @@ int launch_router_logits(const uint16_t *x, const uint16_t *wg, const uint16_t *
     {
       std::lock_guard<std::mutex> lock(tmu);
       if (!tattr[dev]) {
-        if (cudaError_t e = cudaFuncSetAttribute(k_router_logits_tree, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 static_cast<int>(80 * 1024)))
-          return wm::fail(WM_ERR_CUDA, std::string("router logits smem: ") + cudaGetErrorString(e));
+        // H <= 4096: at most 2 buffers x 192 rows x 17 pieces x 16 B = 104 KB
+        for (auto kern : {k_router_logits_tree<4, 4, 1>, k_router_logits_tree<8, 4, 1>})
+          if (cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   static_cast<int>(112 * 1024)))
+            return wm::fail(WM_ERR_CUDA, std::string("router logits smem: ") + cudaGetErrorString(e));
         tattr[dev] = true;
       }
     }
-    const int64_t ctas = static_cast<int64_t>((rows + 63) / 64) * ((T + 63) / 64);
-    if (ctas >= (1LL << 31)) return wm::fail(WM_ERR_INVALID, "router: too many tokens");
-    if (cudaError_t e = wm::launch_pdl(k_router_logits_tree, dim3(static_cast<unsigned>(ctas)), dim3(256), smem, stream,
-                                       x, wg, wg_shared, logit_bias, T, H, E, logits, shared_raw))
-      return wm::fail(WM_ERR_CUDA, std::string("router logits: ") + cudaGetErrorString(e));
-    return wm::check_launch("router logits");
+    const int tg = (T + 63) / 64;
+    auto tree = [&](auto kern, int te) {
+      const int main_rows = rows / (16 * te) * (16 * te);
+      const int64_t ctas = static_cast<int64_t>(main_rows / (16 * te) + (rows - main_rows + 15) / 16) * tg;
+      const size_t smem = static_cast<size_t>(2) * 16 * (te + 4) * pitch * sizeof(uint4);
+      if (ctas >= (1LL << 31)) return wm::fail(WM_ERR_INVALID, "router: too many tokens");
+      if (cudaError_t e = wm::launch_pdl(kern, dim3(static_cast<unsigned>(ctas)), dim3(256), smem, stream, x, wg,
+                                         wg_shared, logit_bias, T, H, E, logits, shared_raw, main_rows))
+        return wm::fail(WM_ERR_CUDA, std::string("router logits: ") + cudaGetErrorString(e));
+      return wm::check_launch("router logits");
+    };
+    if (2 * static_cast<int64_t>(rows / 128) * tg >= 3LL * wm::sm_count()) return tree(k_router_logits_tree<8, 4, 1>, 8);
+    return tree(k_router_logits_tree<4, 4, 1>, 4);
   }
   // large T: staged 8 x 16 tiles; stage = 4 warps x 2 buffers x 24 rows x 512 B = 96 KB, which also holds the
   // 4 x 128 x 32 partial sums (64 KB) afterwards
