@@ -68,3 +68,59 @@ def test_mxfp8_linear_from_native_fp8_blocks(dev):
     ref = F.kv_scores(x.float().cpu().numpy()[None], wq.cpu().numpy()[None], lin.scales.cpu().numpy()[None],
                       F.KV_MXFP8_B32, K)[0]
     assert M.max_rel_err(y.float().cpu().numpy(), ref) < 1e-2
+
+
+# ---- one- and two-row calls: the CUDA-core weight stream (linear_stream.cu)
+
+def _linear_case(dev, fmt, T, N, K, seed):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = (torch.randn((N, K), generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
+    p, s = W.kv_quantize(w, fmt)
+    f = {"mxfp8": F.KV_MXFP8_B32, "mxfp4": F.KV_MXFP4_B32}[fmt]
+    ref = F.kv_scores(x.float().cpu().numpy()[None], p.cpu().numpy()[None], s.cpu().numpy()[None], f, K)[0]
+    return x, p, s, ref
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "mxfp4"])
+@pytest.mark.parametrize("T", [1, 2])
+@pytest.mark.parametrize("N,K", [(5120, 5120), (333, 512), (7, 7168), (1001, 7168), (7168, 1536), (130, 3072),
+                                 (600, 18432), (4101, 1280)])
+def test_stream_linear_vs_oracle_and_tensor_path(dev, monkeypatch, fmt, T, N, K):
+    """Heights that are not multiples of the 4-row chunk, rows whose last 1024-value step is ragged (1536,
+    3072, 1280), fewer chunks than SMs (a chunk's steps split into parts added in order), and two-row calls
+    too wide to stage (18432 e4m3), which stay on the tensor path."""
+    x, p, s, ref = _linear_case(dev, fmt, T, N, K, 11 * T + N + K)
+    y = W.mx_linear(x, p, s, fmt)
+    assert M.max_rel_err(y.float().cpu().numpy(), ref) < 1e-2
+    assert torch.equal(W.mx_linear(x, p, s, fmt), y)                  # fixed order: repeats bit for bit
+    monkeypatch.setenv("WM_LINEAR_PATH", "tc")
+    y_tc = W.mx_linear(x, p, s, fmt)
+    assert M.max_rel_err(y_tc.float().cpu().numpy(), ref) < 1e-2
+    assert M.max_rel_err(y.float().cpu().numpy(), y_tc.float().cpu().numpy()) < 1e-2
+
+
+@pytest.mark.parametrize("fmt", ["mxfp8", "mxfp4"])
+def test_stream_linear_two_rows_equal_each_row_alone(dev, fmt):
+    """Each (row, token) sum keeps its own chains, butterfly and segment order, so a two-row call gives
+    every row's result bit for bit as a one-row call does."""
+    x, p, s, _ = _linear_case(dev, fmt, 2, 3000, 3072, 7)
+    y2 = W.mx_linear(x, p, s, fmt)
+    for t in range(2):
+        assert torch.equal(W.mx_linear(x[t:t + 1].contiguous(), p, s, fmt)[0], y2[t])
+
+
+@pytest.mark.parametrize("T", [1, 2])
+def test_stream_linear_every_e4m3_code(dev, T):
+    """Random bytes over the whole e4m3 range (subnormals, both zeros, the largest finite values; no NaN
+    codes) with scales far from 1: the stream widens each code to an exact f16 value."""
+    N, K = 300, 2048
+    g = torch.Generator(device=dev).manual_seed(3 + T)
+    wq = torch.randint(0, 256, (N, K), generator=g, device=dev, dtype=torch.uint8)
+    wq[(wq & 0x7F) == 0x7F] = 0
+    sc = torch.randint(100, 150, (N, K // 32), generator=g, device=dev, dtype=torch.uint8)
+    x = torch.randn((T, K), generator=g, device=dev).to(torch.bfloat16)
+    y = W.mx_linear(x, wq, sc, "mxfp8")
+    ref = F.kv_scores(x.float().cpu().numpy()[None], wq.cpu().numpy()[None], sc.cpu().numpy()[None],
+                      F.KV_MXFP8_B32, K)[0]
+    assert M.max_rel_err(y.float().cpu().numpy(), ref) < 1e-2

@@ -1284,11 +1284,19 @@ extern "C" int wkv_mx_scores(const wm_bf16 *query, int B, int Lq, int D, const u
 extern "C" size_t wmx_linear_workspace_size(int T, int K, int N) { return wkv_scores_workspace_size(1, T, K, N); }
 
 // A dense block-scaled linear is the score kernel with one "sequence" whose N
-// cached rows are the weight rows and whose T queries are the tokens.
+// cached rows are the weight rows and whose T queries are the tokens.  Calls
+// of one or two rows stream the weights on CUDA cores instead (one launch,
+// linear_stream.cu); WM_LINEAR_PATH=tc keeps them on the tensor path.
 extern "C" int wmx_linear(const wm_bf16 *x, int T, int K, const uint8_t *w, const uint8_t *scales, int N, int fmt,
                           wm_bf16 *y, void *workspace, size_t ws_bytes, wm_stream_t stream) {
   wm::clear_error();
   if (T == 0) return WM_OK;
+  const char *path = getenv("WM_LINEAR_PATH");
+  const int bits = fmt == WKV_MXFP8_B32 ? 8 : fmt == WKV_MXFP4_B32 ? 4 : 0;
+  if (!(path && path[0] == 't') && T >= 1 && N >= 1 && bits && x && w && scales && y && wm::aligned(x, 16) &&
+      wm::aligned(w, 16) && wm::aligned(scales, 8) && wm::linear_stream_supported(T, K, N, bits))
+    return wm::launch_linear_stream(reinterpret_cast<const uint16_t *>(x), T, K, w, scales, N, bits,
+                                    reinterpret_cast<uint16_t *>(y), static_cast<cudaStream_t>(stream));
   return wkv_mx_scores(x, 1, T, K, w, scales, N, fmt, y, workspace, ws_bytes, stream);
 }
 

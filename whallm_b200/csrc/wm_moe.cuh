@@ -71,6 +71,12 @@ int launch_stream_down(const uint8_t *w2, const uint8_t *s2, int S, int H, int I
                        cudaStream_t stream, const CombineArgs *comb = nullptr, int32_t *done = nullptr,
                        const RoutePlan *plan = nullptr);
 
+// linear_stream.cu: dense block-scaled linear of one or two rows on CUDA cores (fmt 8: e4m3 weights, 4: e2m1)
+constexpr int kLinearStreamMaxT = 2;
+bool linear_stream_supported(int T, int K, int N, int fmt);
+int launch_linear_stream(const uint16_t *x, int T, int K, const uint8_t *w, const uint8_t *sc, int N, int fmt,
+                         uint16_t *y, cudaStream_t stream);
+
 // moe_mx.cu: block-scaled tensor-core path (MXFP4 weights x two e4m3 token terms)
 bool mx_supported(int H, int I);
 // tokens per tile: 32 (decode configuration) while T * k / n_routed <= 32, else 112
