@@ -586,11 +586,15 @@ __device__ __forceinline__ void kv_fp8_quant8(const uint4 u, int64_t i, unsigned
       const float s = fmaf(fmaf(-s0, 448.0f, amax), kFp8MaxInv, s0);     // RN(amax / 448)
       if (first) static_cast<float *>(scales)[i / G] = s;
       const float r = __frcp_rn(s);
+      // value pairs on packed f32x2 arithmetic: each lane rounds as the scalar mul / fma do
+      const float2 r2 = make_float2(r, r), ns2 = make_float2(-s, -s);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float q0 = v[j] * r;
-        const float qq = fmaf(fmaf(-q0, s, v[j]), r, q0);
-        q[j] = __uint_as_float((__float_as_uint(qq) & 0x7fffffffu) | (__float_as_uint(v[j]) & 0x80000000u));
+      for (int j = 0; j < 8; j += 2) {
+        const float2 vv = make_float2(v[j], v[j + 1]);
+        const float2 q0 = wm_mul2(vv, r2);
+        const float2 qq = wm_fma2(wm_fma2(q0, ns2, vv), r2, q0);
+        q[j] = __uint_as_float((__float_as_uint(qq.x) & 0x7fffffffu) | (__float_as_uint(v[j]) & 0x80000000u));
+        q[j + 1] = __uint_as_float((__float_as_uint(qq.y) & 0x7fffffffu) | (__float_as_uint(v[j + 1]) & 0x80000000u));
       }
     } else {
       const float s = __fdiv_rn(amax, 448.0f);
@@ -664,8 +668,8 @@ __global__ void __launch_bounds__(256) k_kv_fp8_dequantize(const uint2 *__restri
     if (!nan_code && fabsf(s) <= 3.4028234663852886e38f) {
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float2 f = e4m3x2_to_f32x2(w[j >> 1] >> (16 * (j & 1)));
-        o[j] = pack_bf16x2(f.x * s, f.y * s);
+        const float2 f = wm_mul2(e4m3x2_to_f32x2(w[j >> 1] >> (16 * (j & 1))), make_float2(s, s));
+        o[j] = pack_bf16x2(f.x, f.y);
       }
     } else {
 #pragma unroll

@@ -98,6 +98,11 @@ __device__ __forceinline__ float2 wm_fma2(float2 a, float2 b, float2 c) {
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(wm_f2_bits(a)), "l"(wm_f2_bits(b)), "l"(wm_f2_bits(c)));
   return wm_f2_of(r);
 }
+__device__ __forceinline__ float2 wm_mul2(float2 a, float2 b) {
+  unsigned long long r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(wm_f2_bits(a)), "l"(wm_f2_bits(b)));
+  return wm_f2_of(r);
+}
 __device__ __forceinline__ float2 wm_add2(float2 a, float2 b) {
   unsigned long long r;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(wm_f2_bits(a)), "l"(wm_f2_bits(b)));
