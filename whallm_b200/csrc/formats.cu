@@ -360,7 +360,7 @@ __global__ void k_affine_kv_fetch(AffineKV a, uint32_t chunks, DivU32 cpr, DivU3
     }
     uint4 *dst = reinterpret_cast<uint4 *>(a.out[t]) + static_cast<int64_t>(c) * (kVals / 8);   // values c*kVals..
 #pragma unroll
-    for (int i = 0; i < kVals / 8; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+    for (int i = 0; i < kVals / 8; ++i) __stcs(dst + i, make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]));
   }
 }
 
