@@ -529,11 +529,11 @@ __global__ void k_kv_dequantize(const uint8_t *__restrict__ payload, const void 
 //
 // The three e4m3 row formats (WKV_FP8_F32_B64: fp32 scale amax/448 per 64;
 // WKV_FP8_UE8M0_B32: PackedRows ue8m0 per 32; WKV_MXFP8_B32: E8M0 per 32) as
-// coalesced streaming passes.  A thread owns 8 consecutive values: one
-// 16-byte bf16 load and one 8-byte e4m3 store (dequantize: the reverse), so a
-// warp moves 512 + 256 contiguous bytes.  The G = block / 8 threads of a
-// scale block are adjacent lanes and take the block maximum with xor
-// shuffles; the block's first lane writes the scale.  Bytes and scales equal
+// coalesced streaming passes.  A quantize thread owns 16 consecutive values
+// (two 16-byte bf16 loads, one 16-byte e4m3 store), a dequantize thread 8 (an
+// 8-byte load, one 16-byte store), so a warp moves contiguous bytes.  The
+// block / 16 quantize threads of a scale block are adjacent lanes and take the
+// block maximum with xor shuffles; the block's first lane writes the scale.  Bytes and scales equal
 // kv_quant_block's (the per-block kernel kept for the 4-bit formats):
 //   * the e4m3 encode is cvt.rn.satfinite.e4m3x2.f32 on values already
 //     clamped to +-448, i.e. round to nearest even as wm_f32_to_e4m3;
@@ -560,19 +560,26 @@ __device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
 
 __device__ __forceinline__ float clamp448(float q) { return fminf(fmaxf(q, -448.0f), 448.0f); }
 
-template <int FMT>
-__device__ __forceinline__ void kv_fp8_quant8(const uint4 u, int64_t i, unsigned gmask, int lane,
-                                              uint2 *__restrict__ payload, void *__restrict__ scales) {
-  constexpr int G = Fp8Fmt<FMT>::kG;
-  float v[8] = {wm_bf16lo(u.x), wm_bf16hi(u.x), wm_bf16lo(u.y), wm_bf16hi(u.y),
-                wm_bf16lo(u.z), wm_bf16hi(u.z), wm_bf16lo(u.w), wm_bf16hi(u.w)};
+// NV (8 or 16) consecutive values of one thread; i indexes NV-value chunks.
+template <int FMT, int NV>
+__device__ __forceinline__ void kv_fp8_quant(const uint4 (&u)[NV / 8], int64_t i, unsigned gmask, int lane,
+                                             uint8_t *__restrict__ payload, void *__restrict__ scales) {
+  constexpr int G = Fp8Fmt<FMT>::kG * 8 / NV;   // threads per scale block
+  float v[NV];
+#pragma unroll
+  for (int k = 0; k < NV / 8; ++k) {
+    v[8 * k + 0] = wm_bf16lo(u[k].x); v[8 * k + 1] = wm_bf16hi(u[k].x);
+    v[8 * k + 2] = wm_bf16lo(u[k].y); v[8 * k + 3] = wm_bf16hi(u[k].y);
+    v[8 * k + 4] = wm_bf16lo(u[k].z); v[8 * k + 5] = wm_bf16hi(u[k].z);
+    v[8 * k + 6] = wm_bf16lo(u[k].w); v[8 * k + 7] = wm_bf16hi(u[k].w);
+  }
   float amax = 0.0f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+  for (int j = 0; j < NV; ++j) amax = fmaxf(amax, fabsf(v[j]));
 #pragma unroll
   for (int m = 1; m < G; m <<= 1) amax = fmaxf(amax, __shfl_xor_sync(gmask, amax, m));
   const bool first = (lane & (G - 1)) == 0;
-  float q[8];
+  float q[NV];
   if (FMT == WKV_FP8_F32_B64) {
     // Quotients by Markstein's correction: with y = RN(1/b) and q0 = RN(a * y)
     // within an ulp of a / b, the remainder a - q0 * b is exact in one fma and
@@ -589,7 +596,7 @@ __device__ __forceinline__ void kv_fp8_quant8(const uint4 u, int64_t i, unsigned
       // value pairs on packed f32x2 arithmetic: each lane rounds as the scalar mul / fma do
       const float2 r2 = make_float2(r, r), ns2 = make_float2(-s, -s);
 #pragma unroll
-      for (int j = 0; j < 8; j += 2) {
+      for (int j = 0; j < NV; j += 2) {
         const float2 vv = make_float2(v[j], v[j + 1]);
         const float2 q0 = wm_mul2(vv, r2);
         const float2 qq = wm_fma2(wm_fma2(q0, ns2, vv), r2, q0);
@@ -600,44 +607,45 @@ __device__ __forceinline__ void kv_fp8_quant8(const uint4 u, int64_t i, unsigned
       const float s = __fdiv_rn(amax, 448.0f);
       if (first) static_cast<float *>(scales)[i / G] = s;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = s > 0.0f ? clamp448(__fdiv_rn(v[j], s)) : 0.0f;
+      for (int j = 0; j < NV; ++j) q[j] = s > 0.0f ? clamp448(__fdiv_rn(v[j], s)) : 0.0f;
     }
   } else if (FMT == WKV_FP8_UE8M0_B32) {
     const int e = ceil_log2_bits(fmaxf(amax, kFp8Floor) * kFp8MaxInv);
     if (first) static_cast<uint8_t *>(scales)[i / G] = static_cast<uint8_t>(e + 127);
     const float f = pow2i(-e);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) q[j] = clamp448(v[j] * f);
+    for (int j = 0; j < NV; ++j) q[j] = clamp448(v[j] * f);
   } else {
     const bool zero = amax == 0.0f;
     const int e = zero ? 0 : max(-127, min(127, floor_log2(amax) - 8));
     if (first) static_cast<uint8_t *>(scales)[i / G] = zero ? 0 : static_cast<uint8_t>(e + 127);
     const float f = pow2i(-e);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) q[j] = zero ? 0.0f : clamp448(v[j] * f);
+    for (int j = 0; j < NV; ++j) q[j] = zero ? 0.0f : clamp448(v[j] * f);
   }
-  const uint32_t lo = e4m3x2(q[0], q[1]) | (e4m3x2(q[2], q[3]) << 16);
-  const uint32_t hi = e4m3x2(q[4], q[5]) | (e4m3x2(q[6], q[7]) << 16);
-  __stcs(payload + i, make_uint2(lo, hi));
+  uint32_t w[NV / 4];
+#pragma unroll
+  for (int k = 0; k < NV / 4; ++k) w[k] = e4m3x2(q[4 * k], q[4 * k + 1]) | (e4m3x2(q[4 * k + 2], q[4 * k + 3]) << 16);
+  if constexpr (NV == 16) __stcs(reinterpret_cast<uint4 *>(payload) + i, make_uint4(w[0], w[1], w[2], w[3]));
+  else __stcs(reinterpret_cast<uint2 *>(payload) + i, make_uint2(w[0], w[1]));
 }
 
-// Two 8-value pieces per thread and loop trip, both loads issued first, so
-// each thread keeps 32 bytes of reads in flight.
+// 16 consecutive values per thread (two 16-byte loads issued together, one
+// 16-byte store): the block maximum's shuffles, the scale and its reciprocal
+// are paid once per 16 values.
 template <int FMT>
-__global__ void __launch_bounds__(256) k_kv_fp8_quantize(const uint4 *__restrict__ x, int64_t n8,
-                                                         uint2 *__restrict__ payload, void *__restrict__ scales) {
-  constexpr int G = Fp8Fmt<FMT>::kG;
+__global__ void __launch_bounds__(256) k_kv_fp8_quantize(const uint4 *__restrict__ x, int64_t n16,
+                                                         uint8_t *__restrict__ payload, void *__restrict__ scales) {
+  constexpr int G = Fp8Fmt<FMT>::kG / 2;
   const int lane = threadIdx.x & 31;
   const unsigned gmask = ((1u << G) - 1u) << (lane & ~(G - 1));
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  // n8 is a multiple of G, G divides 32 and the stride is a multiple of 32, so
+  // n16 is a multiple of G, G divides 32 and the stride is a multiple of 32, so
   // the lanes of a block take each branch together (the shuffles only involve them)
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n8; i += 2 * stride) {
-    const int64_t i2 = i + stride;
-    const uint4 u = __ldcs(x + i);
-    const uint4 u2 = i2 < n8 ? __ldcs(x + i2) : make_uint4(0u, 0u, 0u, 0u);
-    kv_fp8_quant8<FMT>(u, i, gmask, lane, payload, scales);
-    if (i2 < n8) kv_fp8_quant8<FMT>(u2, i2, gmask, lane, payload, scales);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n16; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 u[2];
+    u[0] = __ldcs(x + 2 * i);
+    u[1] = __ldcs(x + 2 * i + 1);
+    kv_fp8_quant<FMT, 16>(u, i, gmask, lane, payload, scales);
   }
 }
 
@@ -855,13 +863,13 @@ int wkv_quantize(const wm_bf16 *x, int64_t rows, int D, int fmt, uint8_t *payloa
   int64_t total = rows * (D / blk);
   if (total == 0) return WM_OK;
   if (is_fp8_fmt(fmt)) {
-    const int64_t n8 = rows * (D / 8);
+    const int64_t n16 = rows * (D / 16);
     const auto *xv = reinterpret_cast<const uint4 *>(x);
-    auto *pv = reinterpret_cast<uint2 *>(payload);
-    const int grid = grid_for(n8, 256);
-    if (fmt == WKV_FP8_F32_B64) k_kv_fp8_quantize<WKV_FP8_F32_B64><<<grid, 256, 0, stream>>>(xv, n8, pv, scales);
-    else if (fmt == WKV_FP8_UE8M0_B32) k_kv_fp8_quantize<WKV_FP8_UE8M0_B32><<<grid, 256, 0, stream>>>(xv, n8, pv, scales);
-    else k_kv_fp8_quantize<WKV_MXFP8_B32><<<grid, 256, 0, stream>>>(xv, n8, pv, scales);
+    const int grid = grid_for(n16, 256);
+    if (fmt == WKV_FP8_F32_B64) k_kv_fp8_quantize<WKV_FP8_F32_B64><<<grid, 256, 0, stream>>>(xv, n16, payload, scales);
+    else if (fmt == WKV_FP8_UE8M0_B32)
+      k_kv_fp8_quantize<WKV_FP8_UE8M0_B32><<<grid, 256, 0, stream>>>(xv, n16, payload, scales);
+    else k_kv_fp8_quantize<WKV_MXFP8_B32><<<grid, 256, 0, stream>>>(xv, n16, payload, scales);
     return wm::check_launch("wkv_quantize");
   }
   k_kv_quantize<<<grid_for(total, 128), 128, 0, stream>>>(x, rows, D, fmt, payload, scales);
