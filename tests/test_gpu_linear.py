@@ -1,4 +1,4 @@
-"""Dense MXFP8 / MXFP4 linears on the block-scaled tensor path vs the oracle.
+"""Dense MXFP8 / MXFP4 linears vs the oracle.
 
 ``MXFP8Linear`` mirrors the QuantizedLinear layers the reference installs over
 native FP8 weights (deepseek_v41_ssd.py:232-261, 353-360): y = x @
@@ -8,7 +8,9 @@ product rounded to bf16 (1e-2 max-relative) for decode- and prefill-sized
 token counts and weight heights that are not multiples of 128.  Decode-sized
 calls that leave SMs idle split K across work items and add the f32 partial
 sums in a fixed order: those results repeat bit for bit, and a workspace sized
-for fewer splits gives the same answer through fewer splits.
+for fewer splits gives the same answer through fewer splits.  One- and two-row
+calls run on the CUDA-core weight stream (``linear_stream.cu``); they are
+checked against the oracle and against the tensor path (``WM_LINEAR_PATH=tc``).
 """
 import numpy as np
 import pytest
