@@ -38,6 +38,8 @@
 //     warps write f32 partial sums into shared memory and the CTA adds a
 //     row's parts in part order.  Results do not depend on which warp ran
 //     what, and a row's result is the same with one token or two.
+#include <mutex>
+
 #include "wm_common.cuh"
 #include "wm_moe.cuh"
 #include "wm_tc.cuh"
@@ -298,12 +300,20 @@ LinearPlan plan_linear(int T, int K, int N, int fmt, int sm) {
 
 template <int FMT, int NT>
 cudaError_t launch_linear(const LinearStreamParams &p, const LinearPlan &lp, cudaStream_t stream) {
-  static bool attr_done = false;       // per template instance; the attribute is per function
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_linear_stream<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(wm::kStreamSmemMax));
-    if (e != cudaSuccess) return e;
-    attr_done = true;
+  // the attribute is per function and device: set once per template instance on each device
+  static std::mutex mu;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(k_linear_stream<FMT, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(wm::kStreamSmemMax));
+      if (e != cudaSuccess) return e;
+      attr_done[dev] = true;
+    }
   }
   return wm::launch_pdl(k_linear_stream<FMT, NT>, dim3(lp.grid), dim3(kLThreads), lp.smem, stream, p);
 }

@@ -52,6 +52,8 @@
 // first weight copies before its dependency wait (the routing was complete
 // before the up projection's own wait returned), and combines its own rows
 // with k_combine's arithmetic -- y never leaves shared memory.
+#include <mutex>
+
 #include "wm_common.cuh"
 #include "wm_combine.cuh"
 #include "wm_moe.cuh"
@@ -532,12 +534,20 @@ size_t launch_smem(size_t stage, int K, size_t *ring_offset) {
 
 template <int MODE, int PB>
 cudaError_t launch_one(const StreamParams &p, size_t smem, cudaStream_t stream, int grid = 0) {
-  static bool attr_done = false;       // per template instance; the attribute is per function
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(k_expert_stream<MODE, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(wm::kStreamSmemMax));
-    if (e != cudaSuccess) return e;
-    attr_done = true;
+  // the attribute is per function and device: set once per template instance on each device
+  static std::mutex mu;
+  static bool attr_done[64] = {false};
+  int dev = 0;
+  if (cudaError_t e = cudaGetDevice(&dev)) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (!attr_done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(k_expert_stream<MODE, PB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(wm::kStreamSmemMax));
+      if (e != cudaSuccess) return e;
+      attr_done[dev] = true;
+    }
   }
   return wm::launch_pdl(k_expert_stream<MODE, PB>, dim3(grid > 0 ? grid : wm::sm_count()), dim3(kThreads), smem,
                         stream, p);
