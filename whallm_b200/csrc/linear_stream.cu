@@ -19,10 +19,10 @@
 //     one contiguous range per warp, so every warp gets a few units.
 //   * Weights and scale bytes travel by cp.async through a 3-stage ring per
 //     warp (two steps in flight, about 100 KB per SM), evict-first in L2.
-//     One 1D bulk copy (cp.async.bulk) per stage streamed at 1.2-3.3 TB/s
-//     here against 5.9 TB/s for these per-lane copies: a bulk copy's bytes
-//     arrive at a limited rate per copy, and a few large ones do not keep HBM
-//     busy.  Each thread loads its token values before its first weight
+//     A copy warp issuing 1D bulk copies (cp.async.bulk) into a deep ring
+//     streamed at 1.2-3.3 TB/s against 5.9 TB/s for these per-lane copies
+//     (one to eight copies per stage): a bulk copy's bytes arrive at a limited
+//     rate per copy, and a few large copies do not keep HBM busy.  Each thread loads its token values before its first weight
 //     copy, so they do not queue behind the weight stream.
 //   * Each weight pair becomes two exact f16 values (cvt.rn.f16x2.e4m3x2 /
 //     e2m1x2) and fma.rn.f32.f16 multiplies them by the token values exactly,
